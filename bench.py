@@ -1,0 +1,338 @@
+#!/usr/bin/env python
+"""Training-throughput benchmark: GENESIS-1B dense (24 layers, d_model 2048,
+16 heads, SwiGLU ffn 5632, vocab 32000, RoPE), seq 4096, bf16, fully sharded
+data parallel with distributed Muon, synthetic uniform token ids, random
+N(0, 0.02) weights.
+
+Weak scaling: every GPU processes 32 sequences per optimizer step (global
+batch 256 at 8 GPUs), as micro-batches accumulated in fp32.
+
+One step = all micro-batches of one optimizer step, including the gradient
+reduce-scatter, clipping, the distributed Muon/AdamW update and the weight
+refresh.  Two timed phases, each bracketed by barrier + synchronize:
+
+* device-timed: inputs staged on the GPU beforehand; CUDA events on the
+  launching stream; the reported ``value`` uses the max over ranks;
+* end-to-end (``e2e``): the public trainer API called with inputs in pinned
+  host memory (copied host->device inside the step) and the step's loss read
+  back to the host every step; host wall clock, max over ranks.
+
+Inputs and activations are far larger than the 126 MB L2 (no flush needed).
+
+``--impl reference`` runs the unmodified reference installation in
+``baseline/_ref`` through its own ``DistributedBootstrapTrainer`` on the same
+configuration and prints the same JSON line with ``"impl": "reference"``.
+
+Usage: ``python bench.py [--gpus N] [--steps K] [--warmup W]``; for N > 1 launch
+one process per GPU with ``torch.distributed.run``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+METRIC = "train tokens/sec/box (device-timed, max over ranks) at 1/2/4/8 B200; exposed comm ms/step"
+MODEL_NAME = "GENESIS-1B dense (HLRT trunk: 24L, d2048, 16H, SwiGLU 5632, vocab 32000, RoPE)"
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--preset", default="genesis-1b")
+    ap.add_argument("--seq-len", type=int, default=4096)
+    ap.add_argument("--per-gpu-seqs", type=int, default=32)
+    ap.add_argument("--micro-batch", type=int, default=8)
+    ap.add_argument("--ref-micro-batch", type=int, default=1)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--count-launches", type=int, default=1)
+    return ap.parse_args(argv)
+
+
+def _max_over_ranks(x: float, dist, device) -> float:
+    import torch
+
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier_sync(dist, torch):
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _count_kernels(step_fn, prefixes=("lrb::",)) -> int:
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    n = 0
+    for ev in prof.events():
+        if getattr(ev, "device_type", None) is not None and str(ev.device_type).endswith("CUDA"):
+            if any(p in ev.name for p in prefixes):
+                n += 1
+    return n
+
+
+def run_ours(args) -> dict:
+    sys.path.insert(0, REPO)
+    import torch
+    import torch.distributed as dist
+
+    from genesis.model.hlrt import HLRT
+    from genesis.training.train_phase1_distributed import DistributedBootstrapTrainer, init_distributed
+    from llm_research_b200.models.presets import build_hlrt_config, count_flops_per_token
+    from llm_research_b200.utils.clocks import ClockSampler
+    from olympus.data.tokenizer import TokenizerWrapper
+    from olympus.distributed.fsdp_wrapper import FSDPConfig
+
+    local_rank, world, rank = init_distributed(timeout_s=900.0)
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    micro = args.micro_batch
+    accum = max(args.per_gpu_seqs // micro, 1)
+    S = args.seq_len
+    cfg = build_hlrt_config(args.preset)
+    torch.manual_seed(args.seed)
+    with torch.device(device):
+        model = HLRT(cfg)
+    trainer = DistributedBootstrapTrainer(
+        model,
+        optimizer_kwargs={"lr_muon": 0.02, "lr_adamw": 3e-4, "weight_decay_adamw": 0.01, "ns_steps": 5},
+        scheduler_kwargs={"base_lr": 3e-4, "min_lr": 2e-5, "warmup_steps": 10, "total_steps": 1000},
+        tokenizer=TokenizerWrapper(backend="char", vocab_size=cfg.vocab_size),
+        config={"gradient_accumulation_steps": accum, "max_grad_norm": 1.0, "sync_metrics": False},
+        fsdp_config=FSDPConfig(sharding_strategy="FULL_SHARD", mixed_precision="bf16", activation_checkpointing=False),
+    )
+    g = torch.Generator().manual_seed(args.seed * 1000 + rank)
+    host = torch.randint(0, cfg.vocab_size, (accum, micro, S), generator=g, dtype=torch.int64).pin_memory()
+    dev_batches = [host[i].to(device) for i in range(accum)]
+
+    def step(batches):
+        out = None
+        for b in batches:
+            out = trainer.train_step({"input_ids": b})
+        return out["loss"]
+
+    for _ in range(args.warmup):
+        step(dev_batches)
+    _barrier_sync(dist, torch)
+
+    sampler = ClockSampler(device_index=local_rank)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        _barrier_sync(dist, torch)
+        e0.record()
+        for _ in range(args.steps):
+            loss = step(dev_batches)
+        e1.record()
+        _barrier_sync(dist, torch)
+    dev_ms = _max_over_ranks(e0.elapsed_time(e1), dist, device)
+    final_loss = float(loss)
+
+    e2e = None
+    if not args.no_e2e:
+        host_batches = [host[i] for i in range(accum)]
+        _barrier_sync(dist, torch)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            l = step(host_batches)
+            lv = float(l)  # device -> host read of the step's result
+        _barrier_sync(dist, torch)
+        e2e_s = _max_over_ranks(time.perf_counter() - t0, dist, device)
+        e2e = {
+            "value": world * accum * micro * S * args.steps / e2e_s,
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": int(host[0].numel() * host.element_size() * accum),
+            "d2h_bytes_per_step": 4,
+            "ms_per_step": e2e_s * 1000.0 / args.steps,
+        }
+
+    launches = None
+    if args.count_launches:
+        per_step = _count_kernels(lambda: step(dev_batches))
+        launches = per_step * args.steps
+
+    tokens_per_step = world * accum * micro * S
+    value = tokens_per_step * args.steps / (dev_ms / 1000.0)
+    flops = count_flops_per_token(cfg, S)
+    res = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dev_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (uniform token ids, seeded); random N(0,0.02) init",
+        "impl": "ours",
+        "config": {
+            "model": MODEL_NAME,
+            "global_batch": world * accum * micro,
+            "seq_len": S,
+            "micro_batch": micro,
+            "grad_accum": accum,
+            "parallelism": f"fsdp{world} (FULL_SHARD, bf16 compute, fp32 master) + distributed Muon",
+            "optimizer": "MuonAdamWHybrid (Muon on 2-D, AdamW on embedding/norms)",
+            "l2": "inputs+activations >> 126 MB L2; no flush",
+            "model_tflops_per_gpu": flops * value / world / 1e12,
+            "exposed_comm_ms_per_step": None,
+            "final_loss": final_loss,
+        },
+        "clocks": sampler.summary(),
+        "e2e": e2e,
+        "gpu_launches": launches,
+    }
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+    return res if rank == 0 else None
+
+
+def run_reference(args) -> dict:
+    """The unmodified reference (installed into baseline/_ref) through its public API."""
+    ref = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "genesis")) or not os.path.isdir(os.path.join(ref, "olympus")):
+        return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+    # Make sure its packages, not this repository's, are imported.
+    sys.path[:] = [p for p in sys.path if os.path.abspath(p or os.getcwd()) != REPO]
+    sys.path.insert(0, ref)
+    for mod in [m for m in list(sys.modules) if m.split(".")[0] in ("genesis", "olympus")]:
+        del sys.modules[mod]
+    import torch
+    import torch.distributed as dist
+
+    import genesis
+    from genesis.model.hlrt import HLRT, HLRTConfig
+    from genesis.training.train_phase1_distributed import DistributedBootstrapTrainer
+    from olympus.data.tokenizer import TokenizerWrapper
+    from olympus.optim.muon_adamw_hybrid import MuonAdamWHybrid
+    from olympus.optim.schedulers import WSDScheduler
+
+    assert os.path.abspath(genesis.__file__).startswith(ref), genesis.__file__
+    sys.path.insert(0, REPO)
+    from llm_research_b200.models.presets import build_hlrt_config  # only for the field values
+    from llm_research_b200.utils.clocks import ClockSampler
+    sys.path.pop(0)
+
+    ours = build_hlrt_config(args.preset)
+    fields = {k: getattr(ours, k) for k in HLRTConfig.__dataclass_fields__ if hasattr(ours, k)}
+    cfg = HLRTConfig(**fields)
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    rank = int(os.environ.get("RANK", 0))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    micro = args.ref_micro_batch
+    accum = max(args.per_gpu_seqs // micro, 1)
+    S = args.seq_len
+    torch.manual_seed(args.seed)
+    model = HLRT(cfg)
+    trainer = DistributedBootstrapTrainer(
+        model=model,
+        optimizer_cls=MuonAdamWHybrid,
+        optimizer_kwargs={"lr_muon": 0.02, "lr_adamw": 3e-4, "weight_decay_adamw": 0.01, "ns_steps": 5},
+        scheduler_cls=WSDScheduler,
+        scheduler_kwargs={"base_lr": 3e-4, "min_lr": 2e-5, "warmup_steps": 10, "total_steps": 1000},
+        tokenizer=TokenizerWrapper(backend="char"),
+        config={"gradient_accumulation_steps": accum, "max_grad_norm": 1.0},
+    )
+    g = torch.Generator().manual_seed(args.seed * 1000 + rank)
+    host = torch.randint(0, cfg.vocab_size, (accum, micro, S), generator=g, dtype=torch.int64).pin_memory()
+    dev_batches = [host[i].to(device) for i in range(accum)]
+
+    def step(batches):
+        m = None
+        for b in batches:
+            m = trainer.train_step({"input_ids": b})
+        return m["loss"]
+
+    for _ in range(args.warmup):
+        step(dev_batches)
+    sampler = ClockSampler(device_index=local_rank)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        _barrier_sync(dist, torch)
+        e0.record()
+        for _ in range(args.steps):
+            loss = step(dev_batches)
+        e1.record()
+        _barrier_sync(dist, torch)
+    dev_ms = _max_over_ranks(e0.elapsed_time(e1), dist, device)
+    e2e = None
+    if not args.no_e2e:
+        host_batches = [host[i] for i in range(accum)]
+        _barrier_sync(dist, torch)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            lv = float(step(host_batches))
+        _barrier_sync(dist, torch)
+        e2e_s = _max_over_ranks(time.perf_counter() - t0, dist, device)
+        e2e = {"value": world * accum * micro * S * args.steps / e2e_s, "unit": "tokens/s",
+               "h2d_bytes_per_step": int(host.numel() * host.element_size()), "d2h_bytes_per_step": 4 * accum,
+               "ms_per_step": e2e_s * 1000.0 / args.steps}
+    tokens_per_step = world * accum * micro * S
+    res = {
+        "metric": METRIC,
+        "value": tokens_per_step * args.steps / (dev_ms / 1000.0),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dev_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32" if world == 1 else "bf16",
+        "data": "synthetic (uniform token ids, seeded); random N(0,0.02) init",
+        "impl": "reference",
+        "config": {"model": MODEL_NAME, "global_batch": world * accum * micro, "seq_len": S, "micro_batch": micro,
+                   "grad_accum": accum,
+                   "parallelism": f"reference stock path: {'FSDP1 FULL_SHARD bf16' if world > 1 else 'single GPU, fp32'}",
+                   "final_loss": float(loss)},
+        "clocks": sampler.summary(),
+        "e2e": e2e,
+    }
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+    return res if rank == 0 else None
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    if args.impl == "reference":
+        try:
+            res = run_reference(args)
+        except Exception as exc:  # report instead of crashing the driver
+            res = {"impl": "reference", "unavailable": f"reference run failed: {type(exc).__name__}: {exc}"[:400]}
+            if int(os.environ.get("RANK", 0)) != 0:
+                res = None
+    else:
+        res = run_ours(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

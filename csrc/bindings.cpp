@@ -1,0 +1,73 @@
+// Python bindings of llm_research_b200._C
+#include <torch/extension.h>
+
+#include <tuple>
+#include <vector>
+
+namespace lrb {
+// norm.cu
+std::tuple<at::Tensor, at::Tensor, c10::optional<at::Tensor>> rmsnorm_fwd(const at::Tensor&, const at::Tensor&, double,
+                                                                          const c10::optional<at::Tensor>&,
+                                                                          at::ScalarType);
+std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                               const at::Tensor&, const c10::optional<at::Tensor>&);
+// elementwise.cu
+at::Tensor swiglu_fwd(const at::Tensor&);
+at::Tensor swiglu_bwd(const at::Tensor&, const at::Tensor&);
+std::tuple<at::Tensor, at::Tensor, at::Tensor> rope_qkv_fwd(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                                            int64_t, int64_t, int64_t, int64_t);
+at::Tensor rope_qkv_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                        int64_t, int64_t, int64_t, int64_t);
+// loss.cu
+std::tuple<at::Tensor, at::Tensor, at::Tensor> ce_fwd(const at::Tensor&, const at::Tensor&, int64_t);
+at::Tensor ce_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t);
+// routing.cu
+std::tuple<at::Tensor, at::Tensor, at::Tensor> softmax_topk_fwd(const at::Tensor&, int64_t);
+at::Tensor chunk_mean_pool_fwd(const at::Tensor&, int64_t);
+std::tuple<at::Tensor, at::Tensor> compact_chunks(const at::Tensor&);
+// optim.cu
+at::Tensor muon_prologue(std::vector<at::Tensor>, std::vector<at::Tensor>, std::vector<at::Tensor>,
+                         std::vector<at::Tensor>, double, double, double);
+void muon_epilogue(std::vector<at::Tensor>, std::vector<at::Tensor>, at::Tensor, double);
+void axpy_list(std::vector<at::Tensor>, std::vector<at::Tensor>, double);
+void adamw_step(std::vector<at::Tensor>, std::vector<at::Tensor>, std::vector<at::Tensor>, std::vector<at::Tensor>,
+                std::vector<double>, std::vector<double>, double, double, double, double, double);
+// ns.cu
+at::Tensor newton_schulz(const at::Tensor&, int64_t, double, double, double);
+// quant.cu
+std::tuple<at::Tensor, at::Tensor> int4_quantize(const at::Tensor&, int64_t);
+at::Tensor int4_dequantize(const at::Tensor&, const at::Tensor&, int64_t);
+std::tuple<at::Tensor, at::Tensor, at::Tensor> nvfp4_quantize(const at::Tensor&, bool, int64_t);
+at::Tensor nvfp4_dequantize(const at::Tensor&, const at::Tensor&, const at::Tensor&, at::ScalarType);
+// attention.cu
+std::tuple<at::Tensor, at::Tensor> attn_fwd(const at::Tensor&, const at::Tensor&, const at::Tensor&, bool, double);
+std::tuple<at::Tensor, at::Tensor, at::Tensor> attn_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                                        const at::Tensor&, const at::Tensor&, const at::Tensor&, bool,
+                                                        double);
+}  // namespace lrb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of the llm_research_b200 framework";
+  m.def("rmsnorm_fwd", &lrb::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &lrb::rmsnorm_bwd);
+  m.def("swiglu_fwd", &lrb::swiglu_fwd);
+  m.def("swiglu_bwd", &lrb::swiglu_bwd);
+  m.def("rope_qkv_fwd", &lrb::rope_qkv_fwd);
+  m.def("rope_qkv_bwd", &lrb::rope_qkv_bwd);
+  m.def("ce_fwd", &lrb::ce_fwd);
+  m.def("ce_bwd", &lrb::ce_bwd);
+  m.def("softmax_topk_fwd", &lrb::softmax_topk_fwd);
+  m.def("chunk_mean_pool_fwd", &lrb::chunk_mean_pool_fwd);
+  m.def("compact_chunks", &lrb::compact_chunks);
+  m.def("muon_prologue", &lrb::muon_prologue);
+  m.def("muon_epilogue", &lrb::muon_epilogue);
+  m.def("adamw_step", &lrb::adamw_step);
+  m.def("axpy_list", &lrb::axpy_list);
+  m.def("newton_schulz", &lrb::newton_schulz);
+  m.def("int4_quantize", &lrb::int4_quantize);
+  m.def("int4_dequantize", &lrb::int4_dequantize);
+  m.def("nvfp4_quantize", &lrb::nvfp4_quantize);
+  m.def("nvfp4_dequantize", &lrb::nvfp4_dequantize);
+  m.def("attn_fwd", &lrb::attn_fwd);
+  m.def("attn_bwd", &lrb::attn_bwd);
+}

@@ -1,0 +1,285 @@
+// RMSNorm forward/backward, optionally fused with the preceding residual add.
+//
+// One warp per row.  Rows whose width is a multiple of 256 keep the row in
+// registers (8 elements per lane per 256 columns, up to 8192 columns) and
+// touch HBM exactly once per direction; other widths take a two-pass scalar
+// loop.  The weight gradient is reduced per block in shared memory and then
+// across blocks by a second tiny kernel, never with per-element atomics.
+#include "../common.cuh"
+
+namespace lrb {
+namespace {
+
+constexpr int kWarps = 8;  // rows per block in flight
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* f) {
+  if constexpr (sizeof(T) == 2) {
+    Vec16<T> v = ld16(p);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = to_f(v.v[i]);
+  } else {
+    Vec16<T> a = ld16(p), b = ld16(p + 4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { f[i] = to_f(a.v[i]); f[4 + i] = to_f(b.v[i]); }
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float* f) {
+  if constexpr (sizeof(T) == 2) {
+    Vec16<T> v;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v.v[i] = from_f<T>(f[i]);
+    st16(p, v);
+  } else {
+    Vec16<T> a, b;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { a.v[i] = from_f<T>(f[i]); b.v[i] = from_f<T>(f[4 + i]); }
+    st16(p, a);
+    st16(p + 4, b);
+  }
+}
+template <typename T>
+__device__ __forceinline__ float round_to(float v) { return to_f(from_f<T>(v)); }
+
+// ---------------------------------------------------------------- forward
+template <typename T, typename W, typename O, int NV>
+__global__ void __launch_bounds__(kWarps * 32) rmsnorm_fwd_reg(
+    const T* __restrict__ x, const T* __restrict__ res, T* __restrict__ s_out, const W* __restrict__ w,
+    O* __restrict__ y, float* __restrict__ rstd_out, int64_t rows, int d, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * d;
+  float v[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    load8(xr + c, v[i]);
+    if (res != nullptr) {
+      float r[8];
+      load8(res + row * d + c, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = round_to<T>(v[i][j] + r[j]);
+      store8(s_out + row * d + c, v[i]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / d + eps);
+  if (lane == 0) rstd_out[row] = r;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    float wf[8], o[8];
+    load8(w + c, wf);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = round_to<T>(v[i][j] * r) * wf[j];
+    store8(y + row * d + c, o);
+  }
+}
+
+template <typename T, typename W, typename O>
+__global__ void __launch_bounds__(kWarps * 32) rmsnorm_fwd_generic(
+    const T* __restrict__ x, const T* __restrict__ res, T* __restrict__ s_out, const W* __restrict__ w,
+    O* __restrict__ y, float* __restrict__ rstd_out, int64_t rows, int d, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float ss = 0.f;
+  for (int c = lane; c < d; c += 32) {
+    float v = to_f(x[row * d + c]);
+    if (res != nullptr) {
+      v = round_to<T>(v + to_f(res[row * d + c]));
+      s_out[row * d + c] = from_f<T>(v);
+    }
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / d + eps);
+  if (lane == 0) rstd_out[row] = r;
+  const T* src = res != nullptr ? s_out : x;
+  __syncwarp();
+  for (int c = lane; c < d; c += 32) {
+    const float v = to_f(src[row * d + c]);
+    y[row * d + c] = from_f<O>(round_to<T>(v * r) * to_f(w[c]));
+  }
+}
+
+// --------------------------------------------------------------- backward
+// dx = r * (dn - xhat * mean(dn * xhat)),  dn = dy * w,  xhat = x * r
+// dw_partial[block, c] = sum over this block's rows of dy * cast_T(xhat)
+template <typename T, typename W, typename O>
+__global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(
+    const O* __restrict__ dy, const T* __restrict__ x, const W* __restrict__ w, const float* __restrict__ rstd,
+    const T* __restrict__ ds, T* __restrict__ dx, float* __restrict__ dw_part, int64_t rows, int d) {
+  extern __shared__ float sh[];  // kWarps * d floats
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float* acc = sh + (size_t)wid * d;
+  for (int c = lane; c < d; c += 32) acc[c] = 0.f;
+  const bool vec = (d % 256) == 0;
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + wid; row < rows; row += (int64_t)gridDim.x * kWarps) {
+    const float r = rstd[row];
+    const T* xr = x + row * d;
+    const O* dyr = dy + row * d;
+    float dot = 0.f;
+    if (vec) {
+      for (int c = lane * 8; c < d; c += 256) {
+        float xf[8], gf[8], wf[8];
+        load8(xr + c, xf);
+        load8(dyr + c, gf);
+        load8(w + c, wf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = xf[j] * r;
+          dot += gf[j] * wf[j] * xh;
+          acc[c + j] += gf[j] * round_to<T>(xh);
+        }
+      }
+    } else {
+      for (int c = lane; c < d; c += 32) {
+        const float xh = to_f(xr[c]) * r;
+        const float g = to_f(dyr[c]);
+        dot += g * to_f(w[c]) * xh;
+        acc[c] += g * round_to<T>(xh);
+      }
+    }
+    dot = warp_sum(dot) / d;
+    if (vec) {
+      for (int c = lane * 8; c < d; c += 256) {
+        float xf[8], gf[8], wf[8], o[8];
+        load8(xr + c, xf);
+        load8(dyr + c, gf);
+        load8(w + c, wf);
+        float dsf[8];
+        if (ds != nullptr) load8(ds + row * d + c, dsf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = xf[j] * r;
+          o[j] = r * (gf[j] * wf[j] - xh * dot) + (ds != nullptr ? dsf[j] : 0.f);
+        }
+        store8(dx + row * d + c, o);
+      }
+    } else {
+      for (int c = lane; c < d; c += 32) {
+        const float xh = to_f(xr[c]) * r;
+        float o = r * (to_f(dyr[c]) * to_f(w[c]) - xh * dot);
+        if (ds != nullptr) o += to_f(ds[row * d + c]);
+        dx[row * d + c] = from_f<T>(o);
+      }
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) s += sh[(size_t)k * d + c];
+    dw_part[(size_t)blockIdx.x * d + c] = s;
+  }
+}
+
+__global__ void reduce_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int nrows, int d) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= d) return;
+  float s = 0.f;
+  for (int r = 0; r < nrows; ++r) s += part[(size_t)r * d + c];
+  out[c] = s;
+}
+
+template <typename T, typename W, typename O>
+void launch_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& res, at::Tensor& s, const at::Tensor& w,
+                at::Tensor& y, at::Tensor& rstd, int64_t rows, int d, float eps) {
+  const T* rp = res ? reinterpret_cast<const T*>(res->data_ptr()) : nullptr;
+  T* sp = res ? reinterpret_cast<T*>(s.data_ptr()) : nullptr;
+  auto xp = reinterpret_cast<const T*>(x.data_ptr());
+  auto wp = reinterpret_cast<const W*>(w.data_ptr());
+  auto yp = reinterpret_cast<O*>(y.data_ptr());
+  auto rs = rstd.data_ptr<float>();
+  const dim3 grid((unsigned)((rows + kWarps - 1) / kWarps)), block(kWarps * 32);
+  auto st = stream();
+  switch (d % 256 == 0 ? d / 256 : 0) {
+#define LRB_NV(n) case n: rmsnorm_fwd_reg<T, W, O, n><<<grid, block, 0, st>>>(xp, rp, sp, wp, yp, rs, rows, d, eps); break;
+    LRB_NV(1) LRB_NV(2) LRB_NV(3) LRB_NV(4) LRB_NV(6) LRB_NV(8) LRB_NV(12) LRB_NV(16)
+#undef LRB_NV
+    default: rmsnorm_fwd_generic<T, W, O><<<grid, block, 0, st>>>(xp, rp, sp, wp, yp, rs, rows, d, eps);
+  }
+  LRB_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+// y = norm(x [+ residual]) * w; returns (y, rstd, s = x + residual or None)
+std::tuple<at::Tensor, at::Tensor, c10::optional<at::Tensor>> rmsnorm_fwd(
+    const at::Tensor& x, const at::Tensor& w, double eps, const c10::optional<at::Tensor>& residual,
+    at::ScalarType out_dtype) {
+  LRB_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "rmsnorm_fwd: x must be contiguous 2-D CUDA");
+  const int64_t rows = x.size(0);
+  const int d = (int)x.size(1);
+  LRB_CHECK(w.numel() == d && w.is_contiguous(), "rmsnorm_fwd: weight size mismatch");
+  c10::cuda::CUDAGuard g(x.device());
+  auto y = at::empty({rows, d}, x.options().dtype(out_dtype));
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  at::Tensor s;
+  if (residual) {
+    LRB_CHECK(residual->sizes() == x.sizes() && residual->scalar_type() == x.scalar_type(), "residual mismatch");
+    s = at::empty_like(x);
+  }
+  if (rows == 0) return {y, rstd, residual ? c10::optional<at::Tensor>(s) : c10::nullopt};
+  const auto xt = x.scalar_type(), wt = w.scalar_type();
+  if (xt == at::kBFloat16 && wt == at::kBFloat16 && out_dtype == at::kBFloat16)
+    launch_fwd<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(x, residual, s, w, y, rstd, rows, d, (float)eps);
+  else if (xt == at::kBFloat16 && wt == at::kFloat && out_dtype == at::kFloat)
+    launch_fwd<__nv_bfloat16, float, float>(x, residual, s, w, y, rstd, rows, d, (float)eps);
+  else if (xt == at::kFloat && wt == at::kFloat && out_dtype == at::kFloat)
+    launch_fwd<float, float, float>(x, residual, s, w, y, rstd, rows, d, (float)eps);
+  else if (xt == at::kHalf && wt == at::kHalf && out_dtype == at::kHalf)
+    launch_fwd<__half, __half, __half>(x, residual, s, w, y, rstd, rows, d, (float)eps);
+  else if (xt == at::kFloat && wt == at::kBFloat16 && out_dtype == at::kFloat)
+    launch_fwd<float, __nv_bfloat16, float>(x, residual, s, w, y, rstd, rows, d, (float)eps);
+  else
+    LRB_CHECK(false, "rmsnorm_fwd: unsupported dtype combination");
+  return {y, rstd, residual ? c10::optional<at::Tensor>(s) : c10::nullopt};
+}
+
+std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                               const at::Tensor& rstd, const c10::optional<at::Tensor>& ds) {
+  LRB_CHECK(dy.is_contiguous() && x.is_contiguous(), "rmsnorm_bwd: contiguous inputs required");
+  const int64_t rows = x.size(0);
+  const int d = (int)x.size(1);
+  c10::cuda::CUDAGuard g(x.device());
+  auto dx = at::empty_like(x);
+  auto dw = at::zeros({d}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {dx, dw};
+  const size_t smem = (size_t)kWarps * d * sizeof(float);
+  LRB_CHECK(smem <= 200 * 1024, "rmsnorm_bwd: row too wide");
+  int blocks = (int)std::min<int64_t>((rows + kWarps - 1) / kWarps, 2 * num_sms());
+  auto part = at::empty({blocks, d}, x.options().dtype(at::kFloat));
+  auto st = stream();
+  auto run = [&](auto tag_t, auto tag_w, auto tag_o) {
+    using T = decltype(tag_t);
+    using W = decltype(tag_w);
+    using O = decltype(tag_o);
+    auto k = rmsnorm_bwd_kernel<T, W, O>;
+    if (smem > 48 * 1024) LRB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k<<<blocks, kWarps * 32, smem, st>>>(
+        reinterpret_cast<const O*>(dy.data_ptr()), reinterpret_cast<const T*>(x.data_ptr()),
+        reinterpret_cast<const W*>(w.data_ptr()), rstd.data_ptr<float>(),
+        ds ? reinterpret_cast<const T*>(ds->data_ptr()) : nullptr, reinterpret_cast<T*>(dx.data_ptr()),
+        part.data_ptr<float>(), rows, d);
+    LRB_LAUNCH_CHECK();
+  };
+  const auto xt = x.scalar_type(), wt = w.scalar_type(), ot = dy.scalar_type();
+  if (xt == at::kBFloat16 && wt == at::kBFloat16 && ot == at::kBFloat16) run(__nv_bfloat16{}, __nv_bfloat16{}, __nv_bfloat16{});
+  else if (xt == at::kBFloat16 && wt == at::kFloat && ot == at::kFloat) run(__nv_bfloat16{}, float{}, float{});
+  else if (xt == at::kFloat && wt == at::kFloat && ot == at::kFloat) run(float{}, float{}, float{});
+  else if (xt == at::kHalf && wt == at::kHalf && ot == at::kHalf) run(__half{}, __half{}, __half{});
+  else if (xt == at::kFloat && wt == at::kBFloat16 && ot == at::kFloat) run(float{}, __nv_bfloat16{}, float{});
+  else LRB_CHECK(false, "rmsnorm_bwd: unsupported dtype combination");
+  reduce_rows_kernel<<<(d + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), dw.data_ptr<float>(), blocks, d);
+  LRB_LAUNCH_CHECK();
+  return {dx, dw};
+}
+
+}  // namespace lrb

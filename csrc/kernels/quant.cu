@@ -1,0 +1,216 @@
+// INT4 absmax (reference-compatible) and NVFP4 (E2M1 + e4m3 block scale +
+// fp32 tensor scale) quantisation kernels.
+#include "../common.cuh"
+
+#include <cuda_fp8.h>
+
+namespace lrb {
+namespace {
+
+// ---------------------------------------------------------------- INT4
+// One warp per (row, group).
+template <typename T>
+__global__ void int4_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scales,
+                                  int64_t M, int D, int G, int ng) {
+  const int lane = threadIdx.x & 31;
+  const int64_t job = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (job >= M * ng) return;
+  const int64_t row = job / ng;
+  const int grp = (int)(job - row * ng);
+  const int c0 = grp * G, c1 = min(c0 + G, D);
+  float amax = 0.f;
+  for (int c = c0 + lane; c < c1; c += 32) amax = fmaxf(amax, fabsf(to_f(x[row * D + c])));
+  amax = warp_max(amax);
+  const float s = fmaxf(amax / 7.f, 1e-10f);
+  if (lane == 0) scales[job] = s;
+  for (int c = c0 + lane; c < c1; c += 32) {
+    float v = rintf(to_f(x[row * D + c]) / s);  // round half to even, like torch.round
+    v = fminf(fmaxf(v, -8.f), 7.f);
+    q[row * D + c] = (int8_t)v;
+  }
+}
+
+__global__ void int4_dequant_kernel(const int8_t* __restrict__ q, const float* __restrict__ scales,
+                                    float* __restrict__ out, int64_t M, int D, int G, int ng) {
+  const int64_t n = M * (int64_t)D;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / D;
+    const int c = (int)(i - row * D);
+    out[i] = (float)q[i] * scales[row * ng + c / G];
+  }
+}
+
+// ---------------------------------------------------------------- NVFP4
+__device__ __forceinline__ uint32_t hash3(uint32_t a, uint32_t b, uint32_t c) {
+  // splitmix-style integer hash (Steele, Lea, Flood 2014) for stochastic rounding.
+  uint64_t z = ((uint64_t)a << 32 | b) + 0x9E3779B97F4A7C15ull * (c + 1);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return (uint32_t)(z ^ (z >> 31));
+}
+
+__device__ __forceinline__ float e2m1_value(int code) {
+  const float grid[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+  return grid[code & 7];
+}
+
+// magnitude -> code 0..7, round to nearest, ties to even code
+__device__ __forceinline__ int e2m1_rne(float a) {
+  a = fminf(a, 6.f);
+  const float grid[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+  int lo = 0;
+#pragma unroll
+  for (int i = 1; i < 8; ++i) lo = (a >= grid[i]) ? i : lo;
+  if (lo == 7) return 7;
+  const float dl = a - grid[lo], dh = grid[lo + 1] - a;
+  if (dh < dl) return lo + 1;
+  if (dh > dl) return lo;
+  return ((lo + 1) % 2 == 0) ? lo + 1 : lo;
+}
+
+__device__ __forceinline__ int e2m1_stochastic(float a, float r) {
+  a = fminf(a, 6.f);
+  const float grid[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+  int lo = 0;
+#pragma unroll
+  for (int i = 1; i < 8; ++i) lo = (a >= grid[i]) ? i : lo;
+  if (lo == 7) return 7;
+  const float p = (a - grid[lo]) / (grid[lo + 1] - grid[lo]);
+  return r < p ? lo + 1 : lo;
+}
+
+template <typename T>
+__global__ void absmax_kernel(const T* __restrict__ x, int64_t n, float* __restrict__ out) {
+  __shared__ float red[32];
+  float m = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(to_f(x[i])));
+  m = block_max(m, red);
+  if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(out), __float_as_int(m));  // m >= 0: int order == float order
+}
+
+// One thread per 16-element block.
+template <typename T>
+__global__ void nvfp4_quant_kernel(const T* __restrict__ x, const float* __restrict__ amax, uint8_t* __restrict__ packed,
+                                   __nv_fp8_e4m3* __restrict__ sb, float* __restrict__ st_out, int64_t nblocks,
+                                   bool stochastic, uint32_t seed) {
+  const float st = fmaxf(amax[0] / (6.f * 448.f), 1e-12f);
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b == 0) st_out[0] = st;
+  if (b >= nblocks) return;
+  const T* xp = x + b * 16;
+  float v[16], bm = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) { v[i] = to_f(xp[i]); bm = fmaxf(bm, fabsf(v[i])); }
+  const __nv_fp8_e4m3 s8(fminf(bm / (6.f * st), 448.f));
+  sb[b] = s8;
+  const float denom = fmaxf(float(s8) * st, 1e-30f);
+  uint8_t out[8];
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    int c[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float y = v[i + j] / denom;
+      const float a = fabsf(y);
+      int code;
+      if (stochastic) {
+        const float r = (hash3(seed, (uint32_t)(b >> 32), (uint32_t)(b * 16 + i + j)) >> 8) * (1.f / 16777216.f);
+        code = e2m1_stochastic(a, r);
+      } else {
+        code = e2m1_rne(a);
+      }
+      if (y < 0.f && code > 0) code |= 8;
+      c[j] = code;
+    }
+    out[i / 2] = (uint8_t)(c[0] | (c[1] << 4));
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) packed[b * 8 + i] = out[i];
+}
+
+template <typename O>
+__global__ void nvfp4_dequant_kernel(const uint8_t* __restrict__ packed, const __nv_fp8_e4m3* __restrict__ sb,
+                                     const float* __restrict__ st, O* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint8_t byte = packed[i >> 1];
+    const int code = (i & 1) ? (byte >> 4) : (byte & 15);
+    float v = e2m1_value(code);
+    if (code & 8) v = -v;
+    out[i] = from_f<O>(v * float(sb[i >> 4]) * st[0]);
+  }
+}
+
+}  // namespace
+
+std::tuple<at::Tensor, at::Tensor> int4_quantize(const at::Tensor& x, int64_t G) {
+  LRB_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "int4_quantize: 2-D contiguous CUDA input");
+  c10::cuda::CUDAGuard g(x.device());
+  const int64_t M = x.size(0);
+  const int D = (int)x.size(1);
+  const int ng = (int)((D + G - 1) / G);
+  auto q = at::empty({M, D}, x.options().dtype(at::kChar));
+  auto s = at::empty({M, ng}, x.options().dtype(at::kFloat));
+  if (M * ng == 0) return {q, s};
+  LRB_DISPATCH_FLOAT(x.scalar_type(), T, [&] {
+    int4_quant_kernel<T><<<(unsigned)((M * ng + 7) / 8), 256, 0, stream()>>>(
+        reinterpret_cast<const T*>(x.data_ptr()), q.data_ptr<int8_t>(), s.data_ptr<float>(), M, D, (int)G, ng);
+  });
+  LRB_LAUNCH_CHECK();
+  return {q, s};
+}
+
+at::Tensor int4_dequantize(const at::Tensor& q, const at::Tensor& s, int64_t G) {
+  c10::cuda::CUDAGuard g(q.device());
+  const int64_t M = q.size(0);
+  const int D = (int)q.size(1);
+  auto out = at::empty({M, D}, q.options().dtype(at::kFloat));
+  const int64_t n = M * D;
+  if (n == 0) return out;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 16);
+  int4_dequant_kernel<<<blocks, 256, 0, stream()>>>(q.data_ptr<int8_t>(), s.data_ptr<float>(), out.data_ptr<float>(),
+                                                    M, D, (int)G, (int)s.size(1));
+  LRB_LAUNCH_CHECK();
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> nvfp4_quantize(const at::Tensor& x, bool stochastic, int64_t seed) {
+  LRB_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous() && x.size(1) % 16 == 0, "nvfp4_quantize: (M, K%16==0)");
+  c10::cuda::CUDAGuard g(x.device());
+  const int64_t M = x.size(0), K = x.size(1);
+  auto packed = at::empty({M, K / 2}, x.options().dtype(at::kByte));
+  auto sb = at::empty({M, K / 16}, x.options().dtype(at::kFloat8_e4m3fn));
+  auto st = at::empty({}, x.options().dtype(at::kFloat));
+  auto amax = at::zeros({1}, x.options().dtype(at::kFloat));
+  const int64_t n = M * K, nb = n / 16;
+  if (n == 0) return {packed, sb, st};
+  LRB_DISPATCH_FLOAT(x.scalar_type(), T, [&] {
+    const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 8);
+    absmax_kernel<T><<<blocks, 256, 0, stream()>>>(reinterpret_cast<const T*>(x.data_ptr()), n, amax.data_ptr<float>());
+    LRB_LAUNCH_CHECK();
+    nvfp4_quant_kernel<T><<<(unsigned)((nb + 255) / 256), 256, 0, stream()>>>(
+        reinterpret_cast<const T*>(x.data_ptr()), amax.data_ptr<float>(), packed.data_ptr<uint8_t>(),
+        reinterpret_cast<__nv_fp8_e4m3*>(sb.data_ptr()), st.data_ptr<float>(), nb, stochastic, (uint32_t)seed);
+  });
+  LRB_LAUNCH_CHECK();
+  return {packed, sb, st};
+}
+
+at::Tensor nvfp4_dequantize(const at::Tensor& packed, const at::Tensor& sb, const at::Tensor& st,
+                            at::ScalarType dtype) {
+  c10::cuda::CUDAGuard g(packed.device());
+  const int64_t M = packed.size(0), K = packed.size(1) * 2;
+  auto out = at::empty({M, K}, packed.options().dtype(dtype));
+  const int64_t n = M * K;
+  if (n == 0) return out;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 16);
+  LRB_DISPATCH_FLOAT(dtype, O, [&] {
+    nvfp4_dequant_kernel<O><<<blocks, 256, 0, stream()>>>(packed.data_ptr<uint8_t>(),
+                                                          reinterpret_cast<const __nv_fp8_e4m3*>(sb.data_ptr()),
+                                                          st.data_ptr<float>(), reinterpret_cast<O*>(out.data_ptr()), n);
+  });
+  LRB_LAUNCH_CHECK();
+  return out;
+}
+
+}  // namespace lrb

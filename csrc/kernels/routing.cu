@@ -1,0 +1,160 @@
+// Router softmax + top-k, chunk mean pooling and escalated-chunk compaction.
+#include "../common.cuh"
+
+namespace lrb {
+namespace {
+
+// One warp per token: softmax over E experts (E <= 1024), iterative top-k
+// (ties -> lower index, as torch.topk on equal values from a stable max),
+// renormalised weights.
+template <typename T>
+__global__ void softmax_topk_kernel(const T* __restrict__ logits, float* __restrict__ w, int64_t* __restrict__ idx,
+                                    float* __restrict__ probs, int64_t N, int E, int K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (tok >= N) return;
+  const T* x = logits + tok * E;
+  float* p = probs + tok * E;
+  float m = -INFINITY;
+  for (int e = lane; e < E; e += 32) m = fmaxf(m, to_f(x[e]));
+  m = warp_max(m);
+  float s = 0.f;
+  for (int e = lane; e < E; e += 32) s += __expf(to_f(x[e]) - m);
+  s = warp_sum(s);
+  const float inv = 1.f / s;
+  for (int e = lane; e < E; e += 32) p[e] = __expf(to_f(x[e]) - m) * inv;
+  __syncwarp();
+  // top-k by repeated arg-max; chosen experts are masked by index.
+  float sel_sum = 0.f;
+  unsigned long long chosen_lo = 0ull;  // experts < 64 tracked in a bitmask, others via re-scan
+  float vals[8];
+  int ids[8];
+  for (int k = 0; k < K; ++k) {
+    float best = -1.f;
+    int bi = 0x7fffffff;
+    for (int e = lane; e < E; e += 32) {
+      bool used = false;
+      if (e < 64) used = (chosen_lo >> e) & 1ull;
+      else
+        for (int j = 0; j < k; ++j) used |= (ids[j] == e);
+      const float v = p[e];
+      if (!used && (v > best || (v == best && e < bi))) { best = v; bi = e; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (b2 > best || (b2 == best && i2 < bi)) { best = b2; bi = i2; }
+    }
+    if (k < 8) { vals[k] = best; ids[k] = bi; }
+    if (bi < 64) chosen_lo |= (1ull << bi);
+    sel_sum += best;
+  }
+  if (lane == 0) {
+    const float denom = sel_sum + 1e-9f;
+    for (int k = 0; k < K && k < 8; ++k) {
+      w[tok * K + k] = vals[k] / denom;
+      idx[tok * K + k] = ids[k];
+    }
+  }
+}
+
+// x (B, S, D) -> out (B, S/c, D); fp32 accumulation.
+template <typename T>
+__global__ void chunk_mean_pool_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t BC, int c, int D) {
+  const int64_t n = BC * D;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t bc = i / D;
+    const int d = (int)(i - bc * D);
+    const T* p = x + bc * c * (int64_t)D + d;
+    float s = 0.f;
+    for (int t = 0; t < c; ++t) s += to_f(p[(int64_t)t * D]);
+    out[i] = from_f<T>(s / c);
+  }
+}
+
+// One block per row: prefix sum over the bool mask, scatter chunk ids to the
+// front.  ids must be pre-filled with C (padding id).
+__global__ void compact_kernel(const bool* __restrict__ mask, int64_t* __restrict__ ids, int64_t* __restrict__ counts,
+                               int C) {
+  __shared__ int warp_tot[32];
+  const int b = blockIdx.x;
+  const bool* m = mask + (int64_t)b * C;
+  int64_t* out = ids + (int64_t)b * C;
+  int base = 0;
+  for (int start = 0; start < C; start += blockDim.x) {
+    const int c = start + threadIdx.x;
+    const int v = (c < C && m[c]) ? 1 : 0;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const unsigned bal = __ballot_sync(0xffffffffu, v);
+    const int in_warp = __popc(bal & ((1u << lane) - 1u));
+    if (lane == 0) warp_tot[wid] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w2 = 0; w2 < (int)(blockDim.x >> 5); ++w2) {
+      if (w2 < wid) before += warp_tot[w2];
+      total += warp_tot[w2];
+    }
+    if (v) out[base + before + in_warp] = c;
+    base += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) counts[b] = base;
+}
+
+}  // namespace
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> softmax_topk_fwd(const at::Tensor& logits, int64_t k) {
+  LRB_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.is_contiguous(), "softmax_topk: 2-D contiguous logits");
+  const int64_t N = logits.size(0);
+  const int E = (int)logits.size(1);
+  LRB_CHECK(k >= 1 && k <= 8 && k <= E, "softmax_topk supports 1 <= k <= min(8, E)");
+  c10::cuda::CUDAGuard g(logits.device());
+  auto f32 = logits.options().dtype(at::kFloat);
+  auto w = at::empty({N, k}, f32);
+  auto idx = at::empty({N, k}, logits.options().dtype(at::kLong));
+  auto probs = at::empty({N, E}, f32);
+  if (N == 0) return {w, idx, probs};
+  const int warps = 8;
+  LRB_DISPATCH_FLOAT(logits.scalar_type(), T, [&] {
+    softmax_topk_kernel<T><<<(unsigned)((N + warps - 1) / warps), warps * 32, 0, stream()>>>(
+        reinterpret_cast<const T*>(logits.data_ptr()), w.data_ptr<float>(), idx.data_ptr<int64_t>(),
+        probs.data_ptr<float>(), N, E, (int)k);
+  });
+  LRB_LAUNCH_CHECK();
+  return {w, idx, probs};
+}
+
+at::Tensor chunk_mean_pool_fwd(const at::Tensor& x, int64_t c) {
+  LRB_CHECK(x.is_cuda() && x.dim() == 3 && x.is_contiguous() && x.size(1) % c == 0, "chunk_mean_pool: bad input");
+  c10::cuda::CUDAGuard g(x.device());
+  const int64_t B = x.size(0), S = x.size(1), D = x.size(2);
+  auto out = at::empty({B, S / c, D}, x.options());
+  const int64_t n = B * (S / c) * D;
+  if (n == 0) return out;
+  LRB_DISPATCH_FLOAT(x.scalar_type(), T, [&] {
+    const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 16);
+    chunk_mean_pool_kernel<T><<<blocks, 256, 0, stream()>>>(reinterpret_cast<const T*>(x.data_ptr()),
+                                                            reinterpret_cast<T*>(out.data_ptr()), B * (S / c), (int)c,
+                                                            (int)D);
+  });
+  LRB_LAUNCH_CHECK();
+  return out;
+}
+
+// mask (B, C) bool -> (ids (B, C) with selected chunk ids packed first, padded with C; counts (B))
+std::tuple<at::Tensor, at::Tensor> compact_chunks(const at::Tensor& mask) {
+  LRB_CHECK(mask.is_cuda() && mask.scalar_type() == at::kBool && mask.dim() == 2 && mask.is_contiguous(),
+            "compact_chunks: bool (B, C) mask");
+  c10::cuda::CUDAGuard g(mask.device());
+  const int64_t B = mask.size(0), C = mask.size(1);
+  auto ids = at::full({B, C}, C, mask.options().dtype(at::kLong));
+  auto counts = at::zeros({B}, mask.options().dtype(at::kLong));
+  if (B == 0 || C == 0) return {ids, counts};
+  compact_kernel<<<(unsigned)B, 256, 0, stream()>>>(mask.data_ptr<bool>(), ids.data_ptr<int64_t>(),
+                                                    counts.data_ptr<int64_t>(), (int)C);
+  LRB_LAUNCH_CHECK();
+  return {ids, counts};
+}
+
+}  // namespace lrb

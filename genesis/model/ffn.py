@@ -1,0 +1,40 @@
+"""SwiGLU feed-forward network (``genesis/model/ffn.py:15-66``).
+
+``FFN(x) = W2( silu(W_gate x) * (W1 x) )``; ``d_ff`` defaults to
+``ceil(8/3 * d_model / 256) * 256``.  On B200 the two up projections are one
+GEMM against ``[W_gate; W1]`` and the gating runs in one fused kernel
+(``llm_research_b200.ops.swiglu``).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from llm_research_b200 import ops
+
+
+def default_ffn_dim(d_model: int) -> int:
+    d_ff = int(8 / 3 * d_model)
+    return ((d_ff + 255) // 256) * 256
+
+
+class SwiGLUFFN(nn.Module):
+    def __init__(self, d_model: int, d_ff: int | None = None, dropout: float = 0.0, bias: bool = False) -> None:
+        super().__init__()
+        d_ff = default_ffn_dim(d_model) if d_ff is None else d_ff
+        self.d_ff = d_ff
+        self.w1 = nn.Linear(d_model, d_ff, bias=bias)
+        self.w_gate = nn.Linear(d_model, d_ff, bias=bias)
+        self.w2 = nn.Linear(d_ff, d_model, bias=bias)
+        self.dropout = nn.Dropout(dropout) if dropout > 0.0 else nn.Identity()
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        w = torch.cat([self.w_gate.weight, self.w1.weight], 0)
+        b = None
+        if self.w1.bias is not None:
+            b = torch.cat([self.w_gate.bias, self.w1.bias], 0)
+        gu = F.linear(x, w, b)  # [..., gate | up]
+        h = ops.swiglu(gu)
+        return self.w2(self.dropout(h))

@@ -1,0 +1,48 @@
+"""Top-k expert router with the Switch load-balance loss (``genesis/model/moe_router.py:16-120``).
+
+Optional multiplicative jitter, gate linear, fp32 softmax, top-k,
+renormalisation (``w / (sum w + 1e-9)``).  The probabilities and a per-token
+expert-count mask are kept for ``E * sum_i f_i * P_i``.  On CUDA softmax,
+top-k and renormalisation are one kernel (``llm_research_b200.ops.softmax_topk``).
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from llm_research_b200 import ops
+
+
+class ExpertRouter(nn.Module):
+    def __init__(self, d_model: int, num_experts: int, top_k: int = 2, jitter_noise: float = 0.0) -> None:
+        super().__init__()
+        self.d_model = d_model
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.jitter_noise = jitter_noise
+        self.gate = nn.Linear(d_model, num_experts, bias=False)
+        self._last_router_probs: Optional[torch.Tensor] = None
+        self._last_expert_mask: Optional[torch.Tensor] = None
+
+    def forward(self, x: torch.Tensor):
+        if self.training and self.jitter_noise > 0.0:
+            x = x * torch.empty_like(x).uniform_(1.0 - self.jitter_noise, 1.0 + self.jitter_noise)
+        logits = self.gate(x)
+        flat = logits.reshape(-1, self.num_experts)
+        w, idx, probs = ops.softmax_topk(flat, self.top_k)
+        w = w.reshape(*logits.shape[:-1], self.top_k).type_as(x)
+        idx = idx.reshape(*logits.shape[:-1], self.top_k)
+        self._last_router_probs = probs
+        self._last_expert_mask = F.one_hot(idx.reshape(-1, self.top_k), self.num_experts).sum(dim=-2).float()
+        return w, idx, logits
+
+    def load_balance_loss(self) -> torch.Tensor:
+        if self._last_router_probs is None or self._last_expert_mask is None:
+            return torch.tensor(0.0)
+        f = self._last_expert_mask.float().mean(dim=0)
+        p = self._last_router_probs.float().mean(dim=0)
+        return self.num_experts * (f * p).sum()

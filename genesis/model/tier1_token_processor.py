@@ -1,0 +1,96 @@
+"""Tier 1: the pre-norm transformer trunk over the full token sequence
+(``genesis/model/tier1_token_processor.py:22-169``).
+
+Block: ``x += attn(RMSNorm(x)); x += ffn(RMSNorm(x))``.  The second residual
+add is fused with the FFN RMSNorm (one kernel reads ``x`` and the attention
+output once and writes both the new residual stream and its norm).
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from genesis.model.attention import MultiHeadAttention
+from genesis.model.ffn import SwiGLUFFN
+from genesis.model.rmsnorm import RMSNorm
+from genesis.model.rotary import RotaryEmbedding
+
+
+class TransformerBlock(nn.Module):
+    def __init__(
+        self,
+        d_model: int,
+        num_heads: int,
+        d_ff: int | None = None,
+        num_kv_heads: int | None = None,
+        dropout: float = 0.0,
+        use_flash_attention: bool = True,
+        norm_eps: float = 1e-6,
+    ) -> None:
+        super().__init__()
+        self.attn_norm = RMSNorm(d_model, eps=norm_eps)
+        self.attn = MultiHeadAttention(
+            d_model=d_model, num_heads=num_heads, num_kv_heads=num_kv_heads,
+            dropout=dropout, use_flash_attention=use_flash_attention,
+        )
+        self.ffn_norm = RMSNorm(d_model, eps=norm_eps)
+        self.ffn = self._make_ffn(d_model, d_ff, dropout)
+
+    def _make_ffn(self, d_model: int, d_ff: int | None, dropout: float) -> nn.Module:
+        return SwiGLUFFN(d_model=d_model, d_ff=d_ff, dropout=dropout)
+
+    def forward(
+        self,
+        x: torch.Tensor,
+        cos: torch.Tensor,
+        sin: torch.Tensor,
+        attention_mask: Optional[torch.Tensor] = None,
+        kv_cache: Optional[object] = None,
+        position_offset: int = 0,
+    ) -> torch.Tensor:
+        h = self.attn(self.attn_norm(x), cos, sin, attention_mask=attention_mask,
+                      kv_cache=kv_cache, position_offset=position_offset)
+        normed, x = self.ffn_norm.forward_residual(h, x)
+        return x + self.ffn(normed)
+
+
+class Tier1TokenProcessor(nn.Module):
+    def __init__(
+        self,
+        num_layers: int,
+        d_model: int,
+        num_heads: int,
+        d_ff: int | None = None,
+        num_kv_heads: int | None = None,
+        dropout: float = 0.0,
+        use_flash_attention: bool = True,
+        max_seq_len: int = 8192,
+        rope_base: float = 10000.0,
+        norm_eps: float = 1e-6,
+    ) -> None:
+        super().__init__()
+        self.rotary_emb = RotaryEmbedding(dim=d_model // num_heads, max_seq_len=max_seq_len, base=rope_base)
+        self.layers = nn.ModuleList([
+            TransformerBlock(
+                d_model=d_model, num_heads=num_heads, d_ff=d_ff, num_kv_heads=num_kv_heads,
+                dropout=dropout, use_flash_attention=use_flash_attention, norm_eps=norm_eps,
+            )
+            for _ in range(num_layers)
+        ])
+
+    def forward(
+        self,
+        x: torch.Tensor,
+        attention_mask: Optional[torch.Tensor] = None,
+        kv_cache: Optional[object] = None,
+        position_offset: int = 0,
+    ) -> torch.Tensor:
+        cos, sin = self.rotary_emb(position_offset + x.size(1))
+        for i, layer in enumerate(self.layers):
+            x = layer(x, cos, sin, attention_mask=attention_mask,
+                      kv_cache=kv_cache[i] if kv_cache is not None else None,
+                      position_offset=position_offset)
+        return x

@@ -1,0 +1,219 @@
+"""Phase 1 with sharded data parallelism (``genesis/training/train_phase1_distributed.py:42-379``).
+
+Launch: ``torchrun --nproc-per-node N -m genesis.training.train_phase1_distributed
+--preset genesis-1b --data-dir packed/``.
+
+:class:`DistributedBootstrapTrainer` reads ``LOCAL_RANK/WORLD_SIZE/RANK``,
+initialises the process group (NCCL on GPUs, gloo on CPU), wraps the model
+with the flat-shard engine (FULL_SHARD, bf16 compute, fp32 master) and uses
+distributed Muon.  An explicitly passed ``fsdp_config`` is honoured on a
+single GPU too (mixed precision through the same engine).
+
+The reference ``main()`` fails while building its config
+(``HLRTConfig(max_seq_len=...)``, ``train_phase1_distributed.py:288-291``);
+this one builds the model from ``--preset`` (or the YAML given with
+``--config``) and runs.
+"""
+
+from __future__ import annotations
+
+import argparse
+import logging
+import math
+import os
+import time
+from datetime import timedelta
+from typing import Any, Dict, Optional
+
+import torch
+import torch.distributed as dist
+from torch.utils.data import DataLoader
+from torch.utils.data.distributed import DistributedSampler
+
+from genesis.model.hlrt import HLRT
+from genesis.training.train_phase1_bootstrap import ntp_objective
+from olympus.core.training_orchestrator import ModelConfig, ObjectiveConfig
+from olympus.data.tokenizer import TokenizerWrapper
+from olympus.distributed.distributed_orchestrator import DistributedTrainingOrchestrator
+from olympus.distributed.fsdp_wrapper import FSDPConfig
+from olympus.optim.muon_adamw_hybrid import MuonAdamWHybrid
+from olympus.optim.schedulers import WSDScheduler
+
+logger = logging.getLogger(__name__)
+
+
+def init_distributed(timeout_s: float = 600.0) -> tuple[int, int, int]:
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    rank = int(os.environ.get("RANK", 0))
+    if world > 1 and not dist.is_initialized():
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s),
+                                    device_id=torch.device("cuda", local_rank))
+        else:
+            dist.init_process_group("gloo", timeout=timedelta(seconds=timeout_s))
+    return local_rank, world, rank
+
+
+class DistributedBootstrapTrainer:
+    def __init__(
+        self,
+        model: HLRT,
+        optimizer_cls=MuonAdamWHybrid,
+        optimizer_kwargs: Optional[dict] = None,
+        scheduler_cls=WSDScheduler,
+        scheduler_kwargs: Optional[dict] = None,
+        tokenizer: Optional[TokenizerWrapper] = None,
+        config: Optional[dict] = None,
+        fsdp_config: Optional[FSDPConfig] = None,
+    ) -> None:
+        config = dict(config or {})
+        self.local_rank, self.world_size, self.global_rank = init_distributed(config.get("dist_timeout_s", 600.0))
+        self.is_distributed = self.world_size > 1
+        if torch.cuda.is_available() and config.get("device", "cuda") != "cpu":
+            self.device = torch.device(f"cuda:{self.local_rank}")
+        else:
+            self.device = torch.device("cpu")
+        explicit = fsdp_config is not None
+        if fsdp_config is None and self.is_distributed:
+            fsdp_config = FSDPConfig(sharding_strategy="FULL_SHARD", mixed_precision="bf16",
+                                     activation_checkpointing=config.get("activation_checkpointing", False))
+        model = model.to(self.device)
+        optimizer = optimizer_cls(model.parameters(), **(optimizer_kwargs or {}))
+        scheduler = scheduler_cls(optimizer, **(scheduler_kwargs or {}))
+        self.tokenizer = tokenizer or TokenizerWrapper(backend="tiktoken")
+        self.orchestrator = DistributedTrainingOrchestrator(
+            fsdp_config=fsdp_config if (self.is_distributed or explicit) else None,
+            local_rank=self.local_rank, world_size=self.world_size,
+            gradient_accumulation_steps=config.get("gradient_accumulation_steps", 4),
+            device=self.device, sync_metrics=config.get("sync_metrics", True),
+        )
+        self.orchestrator.add_model(ModelConfig(
+            name="hlrt", model=model, optimizer=optimizer, scheduler=scheduler,
+            max_grad_norm=config.get("max_grad_norm", 1.0), enabled_phases=["bootstrap"],
+        ))
+        self.orchestrator.add_objective(ObjectiveConfig(name="ntp", compute_fn=ntp_objective, weight=1.0,
+                                                        enabled_phases=["bootstrap"]))
+        self.orchestrator.set_phase("bootstrap")
+        cfg = self.orchestrator._models["hlrt"]
+        self.model, self.optimizer, self.scheduler = cfg.model, cfg.optimizer, cfg.scheduler
+        self.config = config
+        self._tokens_seen = 0
+
+    @property
+    def is_main_rank(self) -> bool:
+        return self.global_rank == 0
+
+    def train_step(self, batch: Dict[str, torch.Tensor]) -> Dict[str, Any]:
+        t0 = time.time()
+        losses = self.orchestrator.step(batch)
+        total = losses.get("total", losses.get("ntp", 0.0))
+        n = batch["input_ids"].numel()
+        self._tokens_seen += n
+        tps = n / max(time.time() - t0, 1e-6) * self.world_size
+        if isinstance(total, torch.Tensor):
+            ppl: Any = torch.where(total < 20, total.exp().clamp(max=1e6), torch.full_like(total, 1e6))
+        else:
+            ppl = min(math.exp(total), 1e6) if total < 20 else 1e6
+        return {"loss": total, "perplexity": ppl, "lr": getattr(self.scheduler, "last_lr", 0.0), "tokens_per_sec": tps}
+
+    def train_epoch(self, dataloader: DataLoader) -> Dict[str, float]:
+        log_every = self.config.get("log_interval", 100)
+        save_every = self.config.get("save_interval", 5000)
+        ckpt_dir = self.config.get("checkpoint_dir", "checkpoints/phase1")
+        tot, tps, steps = 0.0, 0.0, 0
+        start = time.time()
+        for batch in dataloader:
+            m = self.train_step(batch)
+            loss = float(m["loss"])
+            tot += loss
+            tps += m["tokens_per_sec"]
+            steps += 1
+            gs = self.orchestrator.global_step
+            if self.is_main_rank and steps % log_every == 0:
+                logger.info("Step %d | loss=%.4f | lr=%.2e | %.0f tok/s", gs, loss, m["lr"], m["tokens_per_sec"])
+            if save_every > 0 and gs > 0 and gs % save_every == 0 and self.orchestrator._accumulation_step == 0:
+                self.save_checkpoint(os.path.join(ckpt_dir, f"checkpoint_step{gs}.pt"))
+        avg = tot / max(steps, 1)
+        if self.is_main_rank:
+            logger.info("Epoch complete | avg_loss=%.4f | %d steps in %.1fs", avg, steps, time.time() - start)
+        return {"epoch_loss": avg, "epoch_perplexity": min(math.exp(avg), 1e6) if avg < 20 else 1e6,
+                "avg_tokens_per_sec": tps / max(steps, 1), "total_steps": steps}
+
+    def save_checkpoint(self, path: str) -> None:
+        self.orchestrator.save_checkpoint(path)
+
+    def load_checkpoint(self, path: str) -> None:
+        self.orchestrator.load_checkpoint(path)
+
+    def make_dataloader(self, dataset, batch_size: int = 32, num_workers: int = 4) -> DataLoader:
+        sampler = DistributedSampler(dataset, num_replicas=self.world_size, rank=self.global_rank, shuffle=True) \
+            if self.is_distributed else None
+        return DataLoader(dataset, batch_size=batch_size, shuffle=sampler is None, sampler=sampler,
+                          num_workers=num_workers, pin_memory=self.device.type == "cuda", drop_last=True)
+
+
+def main(argv=None) -> None:
+    from llm_research_b200.models.presets import build_hlrt_config
+
+    ap = argparse.ArgumentParser(description="GENESIS phase-1 distributed training")
+    ap.add_argument("--preset", default="genesis-1b")
+    ap.add_argument("--config", default=None, help="YAML in the reference's nested model schema")
+    ap.add_argument("--data-dir", default=None, help="packed data; synthetic tokens when omitted")
+    ap.add_argument("--checkpoint-dir", default="checkpoints/phase1")
+    ap.add_argument("--resume", default=None)
+    ap.add_argument("--max-steps", type=int, default=50000)
+    ap.add_argument("--batch-size", type=int, default=8)
+    ap.add_argument("--grad-accum", type=int, default=4)
+    ap.add_argument("--lr", type=float, default=3e-4)
+    ap.add_argument("--muon-lr", type=float, default=0.02)
+    ap.add_argument("--warmup-steps", type=int, default=2000)
+    ap.add_argument("--log-interval", type=int, default=10)
+    ap.add_argument("--save-interval", type=int, default=1000)
+    ap.add_argument("--seq-len", type=int, default=4096)
+    args = ap.parse_args(argv)
+    logging.basicConfig(level=logging.INFO, format=f"[rank {os.environ.get('RANK', 0)}] %(name)s | %(message)s")
+    if args.config:
+        from olympus.utils.config import hlrt_config_from_yaml
+
+        cfg = hlrt_config_from_yaml(args.config)
+    else:
+        cfg = build_hlrt_config(args.preset)
+    torch.manual_seed(0)
+    model = HLRT(cfg)
+    trainer = DistributedBootstrapTrainer(
+        model,
+        optimizer_kwargs={"lr_muon": args.muon_lr, "lr_adamw": args.lr, "weight_decay_adamw": 0.01, "ns_steps": 5},
+        scheduler_kwargs={"base_lr": args.lr, "min_lr": 2e-5, "warmup_steps": args.warmup_steps,
+                          "total_steps": args.max_steps, "decay_start": int(args.max_steps * 0.9)},
+        tokenizer=TokenizerWrapper(backend="char", vocab_size=cfg.vocab_size),
+        config={"gradient_accumulation_steps": args.grad_accum, "max_grad_norm": 1.0,
+                "log_interval": args.log_interval, "save_interval": args.save_interval,
+                "checkpoint_dir": args.checkpoint_dir},
+    )
+    if args.resume:
+        trainer.load_checkpoint(args.resume)
+    if args.data_dir:
+        from olympus.data.packed_dataset import PackedDataset
+
+        ds = PackedDataset(args.data_dir, split="train")
+    else:
+        from olympus.data.packed_dataset import SyntheticTokenDataset
+
+        ds = SyntheticTokenDataset(max(args.batch_size * trainer.world_size * 64, 64), args.seq_len, cfg.vocab_size)
+    loader = trainer.make_dataloader(ds, batch_size=args.batch_size, num_workers=2)
+    epoch = 0
+    while trainer.orchestrator.global_step < args.max_steps:
+        if isinstance(loader.sampler, DistributedSampler):
+            loader.sampler.set_epoch(epoch)
+        trainer.orchestrator.set_epoch(epoch)
+        trainer.train_epoch(loader)
+        epoch += 1
+    trainer.save_checkpoint(os.path.join(args.checkpoint_dir, "checkpoint_final.pt"))
+    if trainer.is_distributed:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

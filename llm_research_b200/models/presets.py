@@ -1,0 +1,82 @@
+"""Named model configurations.
+
+``genesis-1b``  -- the 24-layer dense trunk (d_model 2048, 16 heads, SwiGLU
+                   ffn 5632, vocab 32000, RoPE) as HLRT Tier 1.  Tiers 2 and 3
+                   carry no transformer layers, so the layer count and the
+                   FLOPs are those of the named dense model; the hierarchy
+                   (gate, latent pooling, plan conditioning, Tier-3
+                   projections and integration) still runs every step.
+``genesis-7b``  -- 32 layers, d_model 4096, 32 query / 8 KV heads, ffn 11008,
+                   vocab 32000, same tier layout.
+``tiny``        -- the CPU plumbing configuration: vocab 32000, d_model 256,
+                   every tier 4 layers / 4 heads / ffn 1024, Tier-3
+                   recurrence 2.
+``toy``         -- a few-hundred-thousand-parameter model for smoke tests.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Dict
+
+from genesis.model.hlrt import HLRTConfig
+
+
+def _trunk(vocab: int, d: int, layers: int, heads: int, kv_heads: int | None, ffn: int, seq: int) -> HLRTConfig:
+    return HLRTConfig(
+        vocab_size=vocab,
+        d_model=d,
+        tier1_num_layers=layers,
+        tier1_num_heads=heads,
+        tier1_num_kv_heads=kv_heads,
+        tier1_d_ff=ffn,
+        tier1_max_seq_len=seq,
+        gate1_chunk_size=32,
+        num_latent_vectors=8,
+        latent_pool_num_heads=heads,
+        tier2_d_model=d,
+        tier2_num_layers=0,
+        tier2_num_heads=heads,
+        tier2_max_seq_len=max(seq // 4, 256),
+        tier3_d_model=d,
+        tier3_num_layers=0,
+        tier3_num_heads=heads,
+        tier3_max_seq_len=max(seq // 4, 256),
+        tier3_recurrence_steps=1,
+    )
+
+
+PRESETS: Dict[str, Callable[[], HLRTConfig]] = {
+    "genesis-1b": lambda: _trunk(32000, 2048, 24, 16, None, 5632, 4096),
+    "genesis-7b": lambda: _trunk(32000, 4096, 32, 32, 8, 11008, 4096),
+    "tiny": lambda: HLRTConfig(
+        vocab_size=32000, d_model=256,
+        tier1_num_layers=4, tier1_num_heads=4, tier1_d_ff=1024,
+        tier2_d_model=256, tier2_num_layers=4, tier2_num_heads=4, tier2_d_ff=1024,
+        tier3_d_model=256, tier3_num_layers=4, tier3_num_heads=4, tier3_d_ff=1024,
+        tier3_recurrence_steps=2, latent_pool_num_heads=4,
+    ),
+    "toy": lambda: HLRTConfig(
+        vocab_size=512, d_model=128, tier1_num_layers=2, tier1_num_heads=2, tier1_d_ff=256,
+        gate1_chunk_size=16, num_latent_vectors=4, latent_pool_num_heads=2,
+        tier2_d_model=128, tier2_num_layers=1, tier2_num_heads=2, tier2_d_ff=256,
+        tier3_d_model=128, tier3_num_layers=1, tier3_num_heads=2, tier3_d_ff=256, tier3_recurrence_steps=2,
+    ),
+}
+
+
+def build_hlrt_config(name: str) -> HLRTConfig:
+    if name not in PRESETS:
+        raise KeyError(f"unknown preset {name!r}; choose from {sorted(PRESETS)}")
+    return PRESETS[name]()
+
+
+def count_flops_per_token(cfg: HLRTConfig, seq_len: int) -> float:
+    """Training FLOPs per token of the Tier-1 trunk + head (6N + causal attention)."""
+    d, L = cfg.d_model, cfg.tier1_num_layers
+    hkv = cfg.tier1_num_kv_heads or cfg.tier1_num_heads
+    hd = d // cfg.tier1_num_heads
+    ffn = cfg.tier1_d_ff or ((int(8 / 3 * d) + 255) // 256) * 256
+    per_layer = d * d * 2 + 2 * d * hkv * hd + 3 * d * ffn
+    matmul_params = L * per_layer + cfg.vocab_size * d
+    attn = L * 2 * 2 * seq_len * d / 2  # QK^T and PV, causal half, per token (fwd)
+    return 6.0 * matmul_params + 3.0 * attn

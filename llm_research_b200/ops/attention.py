@@ -1,0 +1,58 @@
+"""Flash attention with native grouped-query heads.
+
+``q (B, Sq, H, D)``, ``k, v (B, Skv, Hkv, D)`` with ``H % Hkv == 0``; query
+head ``h`` reads K/V head ``h // (H / Hkv)``.  With ``causal`` the mask is
+aligned to the end of the key sequence: query ``i`` sees keys
+``j <= i + (Skv - Sq)`` (prefill and cached decode alike, as in
+``genesis/model/attention.py:176-187``).  Softmax in fp32 with scale
+``1/sqrt(D)``.  Output ``(B, Sq, H, D)`` in the input dtype; the row
+log-sum-exp is kept for the backward pass (and is the hook for
+sequence-parallel merging).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from llm_research_b200._ext import native
+
+
+def _reference(q, k, v, causal: bool, scale: float) -> torch.Tensor:
+    B, Sq, H, D = q.shape
+    Skv, Hkv = k.shape[1], k.shape[2]
+    g = H // Hkv
+    qh = q.transpose(1, 2).float()
+    kh = k.transpose(1, 2).float().repeat_interleave(g, dim=1)
+    vh = v.transpose(1, 2).float().repeat_interleave(g, dim=1)
+    s = torch.matmul(qh, kh.transpose(-1, -2)) * scale
+    if causal:
+        mask = torch.ones(Sq, Skv, dtype=torch.bool, device=q.device).triu(Skv - Sq + 1)
+        s = s.masked_fill(mask, float("-inf"))
+    p = F.softmax(s, dim=-1)
+    return torch.matmul(p, vh).transpose(1, 2).to(q.dtype)
+
+
+class _FlashAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale):
+        out, lse = native().attn_fwd(q, k, v, bool(causal), float(scale))
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.causal = causal
+        ctx.scale = scale
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = native().attn_bwd(dout.contiguous(), q, k, v, out, lse, ctx.causal, ctx.scale)
+        return dq, dk, dv, None, None
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True, scale: float | None = None) -> torch.Tensor:
+    scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
+    if not q.is_cuda:
+        return _reference(q, k, v, causal, scale)
+    return _FlashAttnFn.apply(q, k, v, causal, scale)

@@ -1,0 +1,345 @@
+"""Sharded optimizer for :class:`~llm_research_b200.parallel.fsdp.FlatShardEngine`,
+including distributed Muon.
+
+Each rank updates only its shard of every unit.  AdamW is elementwise and runs
+directly on the shard (one multi-tensor launch).  Muon needs the whole matrix,
+so for every Muon matrix an *owner* rank is chosen (greedy longest-processing-
+time assignment by Newton-Schulz FLOPs, identical on all ranks) and:
+
+1. every rank runs the fused prologue on the pieces it holds (decay,
+   momentum, Nesterov direction in bf16, partial ``||g||^2``);
+2. one ``all_to_all`` gathers the pieces of each matrix on its owner, which
+   stacks equal shapes and runs the batched Newton-Schulz iteration;
+3. the owner scales the result by ``lr * ||g|| / (||o|| + 1e-8)`` and a second
+   ``all_to_all`` scatters the pieces back, where they are subtracted from the
+   fp32 master shard.
+
+So the reduce-scatter of the engine plus two bf16 all-to-alls carry all the
+optimizer traffic, and every rank runs Newton-Schulz on ~1/world of the
+matrices.  ``state_dict`` gathers the full per-parameter state in the layout
+of ``torch.optim.Optimizer.state_dict`` with the reference's state keys
+(``olympus/optim/muon_adamw_hybrid.py:118-170``).
+"""
+
+from __future__ import annotations
+
+from collections import defaultdict
+from dataclasses import dataclass
+from typing import Any, Dict, List, Optional, Tuple, Type
+
+import torch
+import torch.distributed as dist
+
+from llm_research_b200 import ops
+
+
+@dataclass
+class Segment:
+    pid: int            # ParamInfo.index
+    unit: int
+    shard_off: int      # offset inside this rank's shard of the unit
+    param_off: int      # offset inside the flattened parameter
+    length: int
+
+
+def _is_hybrid(cls: type) -> bool:
+    from olympus.optim.muon import Muon
+    from olympus.optim.muon_adamw_hybrid import MuonAdamWHybrid
+
+    return issubclass(cls, (MuonAdamWHybrid, Muon))
+
+
+def _pure_muon(cls: type) -> bool:
+    from olympus.optim.muon import Muon
+
+    return issubclass(cls, Muon)
+
+
+class ShardedHybridOptimizer:
+    """Optimizer facade over the engine's shards (``step``/``zero_grad``/``state_dict``)."""
+
+    def __init__(self, engine, optimizer_cls: Type[torch.optim.Optimizer], defaults: Dict[str, Any]) -> None:
+        self.engine = engine
+        self.optimizer_cls = optimizer_cls
+        self.defaults = dict(defaults)
+        self.param_groups: List[Dict[str, Any]] = [dict(self.defaults, params=[i.param for i in engine.params])]
+        self.hybrid = _is_hybrid(optimizer_cls)
+        self.state: Dict[Any, Any] = {}
+        world, rank = engine.world, engine.rank
+        self.world, self.rank = world, rank
+        dev = engine.device
+
+        if not self.hybrid:
+            # Elementwise optimizers run unchanged on flat shard parameters.
+            self._flat = []
+            for u in engine.units:
+                p = torch.nn.Parameter(u.master, requires_grad=True)
+                self._flat.append(p)
+            self.inner = optimizer_cls(self._flat, **self.defaults)
+            self.param_groups = self.inner.param_groups
+            return
+
+        pure = _pure_muon(optimizer_cls)
+        max_ar = float(self.defaults.get("muon_max_aspect_ratio", 8.0))
+        self.is_muon = {}
+        for info in engine.params:
+            m = len(info.shape) == 2 and (pure or max(info.shape) <= min(info.shape) * max_ar)
+            if pure and len(info.shape) != 2:
+                raise ValueError(f"Muon only supports 2-D parameters, got {info.name} {info.shape}")
+            self.is_muon[info.index] = m
+
+        # ---- segments of this rank
+        self.segments: List[Segment] = []
+        for u in engine.units:
+            lo, hi = rank * u.shard, (rank + 1) * u.shard
+            for info in u.params:
+                a, b = max(lo, info.offset), min(hi, info.offset + info.numel)
+                if a < b:
+                    self.segments.append(Segment(info.index, u.index, a - lo, a - info.offset, b - a))
+        self.adam_segs = [s for s in self.segments if not self.is_muon[s.pid]]
+        self.muon_segs = [s for s in self.segments if self.is_muon[s.pid]]
+
+        # ---- per-unit state shards
+        need_m = {s.unit for s in self.muon_segs}
+        need_a = {s.unit for s in self.adam_segs}
+        self.momentum = {ui: torch.zeros(engine.units[ui].shard, device=dev) for ui in need_m}
+        self.exp_avg = {ui: torch.zeros(engine.units[ui].shard, device=dev) for ui in need_a}
+        self.exp_avg_sq = {ui: torch.zeros(engine.units[ui].shard, device=dev) for ui in need_a}
+        self.steps: Dict[int, int] = defaultdict(int)
+
+        # ---- Muon ownership (global, deterministic)
+        infos = {i.index: i for i in engine.params}
+        muon_ids = sorted(i for i, m in self.is_muon.items() if m)
+        self.muon_ids = muon_ids
+        self.muon_pos = {pid: k for k, pid in enumerate(muon_ids)}
+        loads = [0.0] * world
+        self.owner: Dict[int, int] = {}
+        for pid in sorted(muon_ids, key=lambda p: (-self._ns_cost(infos[p].shape), p)):
+            r = min(range(world), key=lambda k: (loads[k], k))
+            self.owner[pid] = r
+            loads[r] += self._ns_cost(infos[pid].shape)
+        self._build_exchange(infos)
+
+    @staticmethod
+    def _ns_cost(shape: Tuple[int, ...]) -> float:
+        m, n = shape
+        s, l = min(m, n), max(m, n)
+        return 4.0 * s * s * l + 2.0 * s ** 3
+
+    def _pieces_of(self, info, r: int) -> Optional[Tuple[int, int]]:
+        u = self.engine.units[info.unit]
+        lo, hi = r * u.shard, (r + 1) * u.shard
+        a, b = max(lo, info.offset), min(hi, info.offset + info.numel)
+        return (a - info.offset, b - a) if a < b else None
+
+    def _build_exchange(self, infos) -> None:
+        eng, world, rank, dev = self.engine, self.world, self.rank, self.engine.device
+        # send order: by (owner, pid); each Muon param has at most one segment per rank.
+        seg_by_pid = {s.pid: s for s in self.muon_segs}
+        self.send_order = sorted(self.muon_segs, key=lambda s: (self.owner[s.pid], s.pid))
+        self.send_splits = [0] * world
+        for s in self.send_order:
+            self.send_splits[self.owner[s.pid]] += s.length
+        self.send_total = sum(self.send_splits)
+        # owned matrices, grouped by shape -> stack layout
+        owned = [pid for pid in self.muon_ids if self.owner[pid] == rank]
+        groups: Dict[Tuple[int, int], List[int]] = defaultdict(list)
+        for pid in owned:
+            groups[infos[pid].shape].append(pid)
+        self.groups = list(groups.items())
+        self.stack_base: Dict[int, int] = {}
+        base = 0
+        for shape, pids in self.groups:
+            for pid in pids:
+                self.stack_base[pid] = base
+                base += infos[pid].numel
+        self.stack_total = base
+        # receive layout: for each source rank, pieces of owned matrices in pid order
+        self.recv_splits = [0] * world
+        gather_idx: List[torch.Tensor] = []
+        pos = 0
+        for r in range(world):
+            for pid in owned:
+                pc = self._pieces_of(infos[pid], r)
+                if pc is None:
+                    continue
+                off, ln = pc
+                gather_idx.append(torch.arange(self.stack_base[pid] + off, self.stack_base[pid] + off + ln))
+                self.recv_splits[r] += ln
+                pos += ln
+        self.recv_total = pos
+        # stack_flat[gidx[j]] = recv[j]
+        self.recv_to_stack = torch.cat(gather_idx).to(dev) if gather_idx else torch.zeros(0, dtype=torch.long, device=dev)
+
+    # ------------------------------------------------------------------ step
+    def _views(self, ui: int, seg: Segment, buf: torch.Tensor) -> torch.Tensor:
+        return buf[seg.shard_off: seg.shard_off + seg.length]
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        eng = self.engine
+        eng.wait_grads()
+        if not self.hybrid:
+            for p, u in zip(self._flat, eng.units):
+                p.grad = u.grad_shard
+            self.inner.step()
+            eng.refresh()
+            return loss
+        g = self.param_groups[0]
+        pure = _pure_muon(self.optimizer_cls)
+        lr_m = g["lr"] if pure else g["lr_muon"]
+        wd_m = g.get("weight_decay", 0.0) if pure else g["weight_decay_muon"]
+        mu = g["momentum"]
+        ns_steps = g["ns_steps"]
+        units = eng.units
+
+        if self.adam_segs:
+            pids = sorted({s.pid for s in self.adam_segs})
+            for pid in pids:
+                self.steps[pid] += 1
+            beta1, beta2 = g["betas"]
+            ops.adamw_step(
+                [units[s.unit].master[s.shard_off: s.shard_off + s.length] for s in self.adam_segs],
+                [units[s.unit].grad_shard[s.shard_off: s.shard_off + s.length] for s in self.adam_segs],
+                [self.exp_avg[s.unit][s.shard_off: s.shard_off + s.length] for s in self.adam_segs],
+                [self.exp_avg_sq[s.unit][s.shard_off: s.shard_off + s.length] for s in self.adam_segs],
+                [self.steps[s.pid] for s in self.adam_segs],
+                lr=g["lr_adamw"], beta1=beta1, beta2=beta2, eps=g["eps"], weight_decay=g["weight_decay_adamw"],
+            )
+
+        if self.muon_segs:
+            self._muon_step(lr_m, mu, wd_m, ns_steps)
+        eng.refresh()
+        return loss
+
+    def _muon_step(self, lr: float, mu: float, wd: float, ns_steps: int) -> None:
+        eng, units, dev = self.engine, self.engine.units, self.engine.device
+        send = torch.empty(self.send_total, dtype=torch.bfloat16, device=dev)
+        outs, pos = [], 0
+        for s in self.send_order:
+            outs.append(send[pos: pos + s.length])
+            pos += s.length
+        segs = self.send_order
+        gnorm_seg = ops.muon_prologue_into(
+            [units[s.unit].master[s.shard_off: s.shard_off + s.length] for s in segs],
+            [units[s.unit].grad_shard[s.shard_off: s.shard_off + s.length] for s in segs],
+            [self.momentum[s.unit][s.shard_off: s.shard_off + s.length] for s in segs],
+            outs, float(lr), float(mu), float(wd),
+        )
+        # per-matrix ||g||^2 summed over the ranks holding its pieces
+        gsq = torch.zeros(len(self.muon_ids), device=dev)
+        idx = torch.tensor([self.muon_pos[s.pid] for s in segs], device=dev, dtype=torch.long)
+        gsq.index_add_(0, idx, gnorm_seg.pow(2))
+        if self.world > 1:
+            dist.all_reduce(gsq, group=eng.pg)
+            recv = torch.empty(self.recv_total, dtype=torch.bfloat16, device=dev)
+            dist.all_to_all_single(recv, send, self.recv_splits, self.send_splits, group=eng.pg)
+        else:
+            recv = send
+        stack = torch.empty(self.stack_total, dtype=torch.bfloat16, device=dev)
+        stack.index_copy_(0, self.recv_to_stack, recv)
+        gnorm = gsq.sqrt()
+        base = 0
+        for shape, pids in self.groups:
+            n = len(pids)
+            numel = shape[0] * shape[1]
+            block = stack[base: base + n * numel].view(n, shape[0], shape[1])
+            o = ops.newton_schulz(block, steps=ns_steps)
+            onorm = o.float().flatten(1).norm(dim=1)
+            gn = gnorm[torch.tensor([self.muon_pos[p] for p in pids], device=dev)]
+            scale = (lr * gn / (onorm + 1e-8)).view(n, 1, 1)
+            block.copy_((o.float() * scale).to(torch.bfloat16))
+            base += n * numel
+        back = torch.empty(self.recv_total, dtype=torch.bfloat16, device=dev)
+        back.copy_(stack.index_select(0, self.recv_to_stack))
+        if self.world > 1:
+            upd = torch.empty(self.send_total, dtype=torch.bfloat16, device=dev)
+            dist.all_to_all_single(upd, back, self.send_splits, self.recv_splits, group=eng.pg)
+        else:
+            upd = back
+        masters, deltas, pos = [], [], 0
+        for s in segs:
+            masters.append(units[s.unit].master[s.shard_off: s.shard_off + s.length])
+            deltas.append(upd[pos: pos + s.length])
+            pos += s.length
+        ops.axpy_list(masters, deltas, -1.0)
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        self.engine.zero_grad()
+
+    # ---------------------------------------------------------- checkpoints
+    @torch.no_grad()
+    def state_dict(self) -> Dict[str, Any]:
+        eng = self.engine
+        groups = [{k: v for k, v in self.param_groups[0].items() if k != "params"}]
+        groups[0]["params"] = [i.index for i in eng.params]
+        if not self.hybrid:
+            return {"state": {}, "param_groups": groups, "inner": self.inner.state_dict()}
+        state: Dict[int, Dict[str, Any]] = {}
+        full = {}
+        for name, bufs in (("momentum_buffer", self.momentum), ("exp_avg", self.exp_avg), ("exp_avg_sq", self.exp_avg_sq)):
+            for u in eng.units:
+                src = bufs.get(u.index)
+                if src is None:
+                    src = torch.zeros(u.shard, device=eng.device)
+                full[(name, u.index)] = eng.full_flat(u, src)
+        for info in eng.params:
+            sl = slice(info.offset, info.offset + info.numel)
+            if self.is_muon[info.index]:
+                state[info.index] = {
+                    "type": "muon",
+                    "momentum_buffer": full[("momentum_buffer", info.unit)][sl].view(info.shape).cpu().clone(),
+                }
+            else:
+                state[info.index] = {
+                    "type": "adamw",
+                    "step": int(self._global_step(info.index)),
+                    "exp_avg": full[("exp_avg", info.unit)][sl].view(info.shape).cpu().clone(),
+                    "exp_avg_sq": full[("exp_avg_sq", info.unit)][sl].view(info.shape).cpu().clone(),
+                }
+        return {"state": state, "param_groups": groups}
+
+    def steps_taken(self, pid: int) -> int:
+        return self.steps.get(pid, 0)
+
+    def _global_step(self, pid: int) -> int:
+        t = torch.tensor([self.steps.get(pid, 0)], dtype=torch.long, device=self.engine.device)
+        if self.world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.engine.pg)
+        return int(t.item())
+
+    @torch.no_grad()
+    def load_state_dict(self, sd: Dict[str, Any]) -> None:
+        eng = self.engine
+        if sd.get("param_groups"):
+            for k, v in sd["param_groups"][0].items():
+                if k != "params":
+                    self.param_groups[0][k] = v
+        if not self.hybrid:
+            if "inner" in sd:
+                self.inner.load_state_dict(sd["inner"])
+            return
+        st = sd.get("state", {})
+        for info in eng.params:
+            ent = st.get(info.index) or st.get(str(info.index))
+            if ent is None:
+                continue
+            u = eng.units[info.unit]
+            lo = eng.rank * u.shard
+            a, b = max(lo, info.offset), min(lo + u.shard, info.offset + info.numel)
+            if a >= b:
+                if ent.get("type") == "adamw":
+                    self.steps[info.index] = int(ent.get("step", 0))
+                continue
+            src_sl = slice(a - info.offset, b - info.offset)
+            dst_sl = slice(a - lo, b - lo)
+            if ent.get("type") == "muon" and info.unit in self.momentum:
+                self.momentum[info.unit][dst_sl].copy_(ent["momentum_buffer"].reshape(-1)[src_sl])
+            elif ent.get("type") == "adamw" and info.unit in self.exp_avg:
+                self.exp_avg[info.unit][dst_sl].copy_(ent["exp_avg"].reshape(-1)[src_sl])
+                self.exp_avg_sq[info.unit][dst_sl].copy_(ent["exp_avg_sq"].reshape(-1)[src_sl])
+                self.steps[info.index] = int(ent.get("step", 0))

@@ -1,0 +1,422 @@
+"""Flat-parameter fully sharded data parallel engine (ZeRO-3 style) with
+mixed precision, used for every training run including a single GPU.
+
+Layout.  Parameters are grouped into *units*: every transformer block is one
+unit, everything else (embeddings, gates, pooling, norms, ...) forms the root
+unit.  Each unit owns
+
+* a flat bf16 compute buffer (full size while gathered; its storage is freed
+  between uses when ``reshard_after_forward``) whose views are handed to the
+  module through ``torch.func.functional_call``;
+* a flat fp32 gradient accumulator (local, full size) that the backward of
+  every weight view adds into, so micro-step accumulation happens in fp32;
+* this rank's shard of the fp32 master weights, of the reduced gradient and
+  of the optimizer state (``numel / world`` elements each, 8-element aligned).
+
+Step flow.  Before a unit's forward (and again before its backward) its bf16
+shards are all-gathered into the compute buffer on a communication stream,
+one unit ahead of use.  When the last gradient of a unit has been
+accumulated on the boundary micro-step, the unit's fp32 gradient is
+reduce-scattered into the shard.  The optimizer (:class:`ShardedHybridOptimizer`)
+then updates the shards; Muon matrices are gathered to an owner rank for the
+Newton-Schulz iteration and the scaled update is scattered back (distributed
+Muon), so Muon always sees whole 2-D matrices -- unlike the reference, whose
+FSDP1 flattening routes every parameter to AdamW
+(``olympus/distributed/fsdp_wrapper.py:149`` with
+``olympus/optim/muon_adamw_hybrid.py:113-116``).
+
+With ``world_size == 1`` the same code runs without collectives: the master
+buffer is the whole model and ``refresh`` casts it into the compute buffer.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import math
+from dataclasses import dataclass, field
+from typing import Any, Callable, Dict, Iterator, List, Optional, Sequence, Set, Tuple, Type
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from llm_research_b200 import ops
+
+ALIGN = 8  # elements; keeps every bf16 view 16-byte aligned
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+@dataclass
+class ParamInfo:
+    name: str
+    param: nn.Parameter
+    unit: int
+    offset: int  # in the unit's flat buffer
+    shape: Tuple[int, ...]
+    numel: int
+    index: int  # position in model.parameters() order (optimizer-state key)
+
+
+@dataclass
+class Unit:
+    index: int
+    module: nn.Module
+    params: List[ParamInfo] = field(default_factory=list)
+    total: int = 0      # padded flat size (multiple of world * ALIGN)
+    shard: int = 0      # per-rank shard size
+    compute: Optional[torch.Tensor] = None
+    views: Dict[str, torch.Tensor] = field(default_factory=dict)
+    grad_acc: Optional[torch.Tensor] = None
+    master: Optional[torch.Tensor] = None
+    grad_shard: Optional[torch.Tensor] = None
+    compute_shard: Optional[torch.Tensor] = None
+    gathered: bool = False
+    gather_event: Optional[torch.cuda.Event] = None
+    pending_grads: int = 0
+    grads_seen: Set[int] = field(default_factory=set)
+    reduced: bool = False
+    rs_event: Optional[torch.cuda.Event] = None
+
+
+class _GradSink(torch.autograd.Function):
+    """Identity on a compute-weight view; its gradient is added to the unit's
+    fp32 accumulator instead of flowing to a leaf."""
+
+    @staticmethod
+    def forward(ctx, anchor, view, engine, unit_idx, pidx):
+        ctx.engine = engine
+        ctx.key = (unit_idx, pidx)
+        return view.view_as(view)
+
+    @staticmethod
+    def backward(ctx, grad):
+        ctx.engine._accumulate(ctx.key[0], ctx.key[1], grad)
+        return None, None, None, None, None
+
+
+def default_unit_classes() -> Tuple[Type[nn.Module], ...]:
+    from genesis.model.tier1_token_processor import TransformerBlock
+
+    return (TransformerBlock,)
+
+
+class FlatShardEngine(nn.Module):
+    """Wraps ``module``; call it like the module.  See the module docstring."""
+
+    def __init__(
+        self,
+        module: nn.Module,
+        process_group: Optional[dist.ProcessGroup] = None,
+        compute_dtype: torch.dtype = torch.bfloat16,
+        reshard_after_forward: bool = True,
+        unit_classes: Optional[Sequence[Type[nn.Module]]] = None,
+        device: Optional[torch.device] = None,
+        reduce_dtype: torch.dtype = torch.float32,
+    ) -> None:
+        super().__init__()
+        self.module = module
+        self.pg = process_group
+        self.distributed = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(process_group) if self.distributed else 1
+        self.rank = dist.get_rank(process_group) if self.distributed else 0
+        self.compute_dtype = compute_dtype
+        self.reduce_dtype = reduce_dtype
+        self.reshard_after_forward = reshard_after_forward and self.world > 1
+        self.device = device or next(module.parameters()).device
+        self._sync_grads = True
+        self._in_backward = False
+        self._anchor = torch.zeros((), device=self.device, requires_grad=True)
+        self.comm_stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
+        classes = tuple(unit_classes) if unit_classes is not None else default_unit_classes()
+        self._build_units(classes)
+        self._register_hooks()
+
+    # ------------------------------------------------------------------ layout
+    def _build_units(self, classes: Tuple[Type[nn.Module], ...]) -> None:
+        unit_of_module: Dict[int, int] = {}
+        self.units: List[Unit] = [Unit(index=0, module=self.module)]  # root
+        # Exact type match: only blocks that run on every step become units,
+        # so every rank issues the same collectives in the same order even
+        # when data-dependent branches (HLRT tiers 2/3) differ between ranks.
+        for m in self.module.modules():
+            if m is not self.module and type(m) in classes:
+                unit_of_module[id(m)] = len(self.units)
+                self.units.append(Unit(index=len(self.units), module=m))
+        owner: Dict[int, int] = {}
+        for name, mod in self.module.named_modules():
+            u = unit_of_module.get(id(mod))
+            if u is not None:
+                for pname, p in mod.named_parameters(recurse=True):
+                    owner.setdefault(id(p), u)
+        self.params: List[ParamInfo] = []
+        seen: Set[int] = set()
+        for idx, (name, p) in enumerate(self.module.named_parameters()):
+            if id(p) in seen:
+                continue
+            seen.add(id(p))
+            u = self.units[owner.get(id(p), 0)]
+            info = ParamInfo(name=name, param=p, unit=u.index, offset=u.total, shape=tuple(p.shape),
+                             numel=p.numel(), index=len(self.params))
+            u.params.append(info)
+            u.total = _round_up(u.total + p.numel(), ALIGN)
+            self.params.append(info)
+        dev = self.device
+        for u in self.units:
+            u.total = _round_up(max(u.total, 1), self.world * ALIGN)
+            u.shard = u.total // self.world
+            full = torch.zeros(u.total, dtype=torch.float32, device=dev)
+            for info in u.params:
+                full[info.offset: info.offset + info.numel].copy_(info.param.detach().reshape(-1).float())
+            lo = self.rank * u.shard
+            u.master = full[lo: lo + u.shard].clone() if self.world > 1 else full
+            u.grad_acc = torch.zeros(u.total, dtype=torch.float32, device=dev)
+            u.grad_shard = torch.zeros(u.shard, dtype=torch.float32, device=dev) if self.world > 1 else u.grad_acc
+            u.compute = torch.empty(u.total, dtype=self.compute_dtype, device=dev)
+            u.compute_shard = u.master.to(self.compute_dtype) if self.world > 1 else None
+            for info in u.params:
+                u.views[info.name] = u.compute[info.offset: info.offset + info.numel].view(info.shape)
+            if self.world == 1:
+                u.compute.copy_(u.master)
+                u.gathered = True
+                # The module's parameters alias the master weights.
+                for info in u.params:
+                    info.param.data = u.master[info.offset: info.offset + info.numel].view(info.shape)
+            else:
+                for info in u.params:
+                    info.param.data = torch.empty(0, dtype=torch.float32, device=dev)
+                self._free(u)
+            del full
+        self.unit_order = [u.index for u in self.units[1:]]
+
+    # --------------------------------------------------------------- gathers
+    def _free(self, u: Unit) -> None:
+        if self.world > 1 and u.compute.untyped_storage().size() > 0:
+            u.compute.untyped_storage().resize_(0)
+        u.gathered = self.world == 1
+
+    def _gather(self, u: Unit, wait: bool = True) -> None:
+        if self.world == 1:
+            return
+        if not u.gathered:
+            st = u.compute.untyped_storage()
+            if st.size() == 0:
+                st.resize_(u.total * u.compute.element_size())
+            cur = torch.cuda.current_stream(self.device)
+            self.comm_stream.wait_stream(cur)
+            with torch.cuda.stream(self.comm_stream):
+                dist.all_gather_into_tensor(u.compute, u.compute_shard, group=self.pg)
+                ev = torch.cuda.Event()
+                ev.record(self.comm_stream)
+            u.gather_event = ev
+            u.gathered = True
+        if wait and u.gather_event is not None:
+            torch.cuda.current_stream(self.device).wait_event(u.gather_event)
+            u.gather_event = None
+
+    def _prefetch(self, pos: int) -> None:
+        if 0 <= pos < len(self.unit_order):
+            self._gather(self.units[self.unit_order[pos]], wait=False)
+
+    # ----------------------------------------------------------------- hooks
+    def _register_hooks(self) -> None:
+        self._pos = {ui: i for i, ui in enumerate(self.unit_order)}
+        for ui in self.unit_order:
+            u = self.units[ui]
+            u.module.register_forward_pre_hook(self._make_pre_forward(ui))
+            u.module.register_forward_hook(self._make_post_forward(ui))
+
+    def _make_pre_forward(self, ui: int):
+        def hook(module, args):
+            if not self._active:
+                return
+            self._gather(self.units[ui], wait=True)
+            self._prefetch(self._pos[ui] + 1)
+        return hook
+
+    def _make_post_forward(self, ui: int):
+        def hook(module, args, output):
+            if not self._active:
+                return
+            if self.reshard_after_forward:
+                self._free(self.units[ui])
+            if torch.is_grad_enabled() and isinstance(output, torch.Tensor) and output.requires_grad:
+                output.register_hook(self._make_pre_backward(ui))
+        return hook
+
+    def _make_pre_backward(self, ui: int):
+        def hook(grad):
+            self._begin_backward()
+            self._gather(self.units[ui], wait=True)
+            self._prefetch(self._pos[ui] - 1)
+            return grad
+        return hook
+
+    def _begin_backward(self) -> None:
+        if not self._in_backward:
+            self._in_backward = True
+            torch.autograd.Variable._execution_engine.queue_callback(self._end_backward)
+
+    # ---------------------------------------------------------- grad plumbing
+    def _accumulate(self, ui: int, pidx: int, grad: torch.Tensor) -> None:
+        self._begin_backward()
+        u = self.units[ui]
+        info = u.params[pidx]
+        dst = u.grad_acc[info.offset: info.offset + info.numel].view(info.shape)
+        dst.add_(grad.to(torch.float32) if grad.dtype != torch.float32 else grad)
+        u.grads_seen.add(pidx)
+        if len(u.grads_seen) == len(u.params):
+            self._unit_backward_done(u)
+
+    def _unit_backward_done(self, u: Unit, final: bool = False) -> None:
+        # The root unit is only completed at the end of backward (its
+        # parameters may belong to branches some ranks skip).
+        if u.reduced or (u.index == 0 and not final):
+            return
+        u.reduced = True
+        if u.index != 0 and self.world > 1:
+            self._free(u)
+        if self._sync_grads:
+            self._reduce_scatter(u)
+
+    def _reduce_scatter(self, u: Unit) -> None:
+        if self.world == 1:
+            return
+        cur = torch.cuda.current_stream(self.device)
+        self.comm_stream.wait_stream(cur)
+        with torch.cuda.stream(self.comm_stream):
+            src = u.grad_acc if self.reduce_dtype == torch.float32 else u.grad_acc.to(self.reduce_dtype)
+            out = u.grad_shard if self.reduce_dtype == torch.float32 else torch.empty(u.shard, dtype=self.reduce_dtype, device=self.device)
+            dist.reduce_scatter_tensor(out, src, op=dist.ReduceOp.AVG, group=self.pg)
+            if out is not u.grad_shard:
+                u.grad_shard.copy_(out)
+            u.grad_acc.zero_()
+            ev = torch.cuda.Event()
+            ev.record(self.comm_stream)
+        u.rs_event = ev
+
+    def _end_backward(self) -> None:
+        # Units whose parameters did not all receive gradients (unused
+        # branches) are completed here.
+        for u in self.units:
+            self._unit_backward_done(u, final=True)
+        if self.world > 1:
+            self._free(self.units[0])
+        for u in self.units:
+            u.grads_seen.clear()
+            u.reduced = False
+        self._in_backward = False
+
+    def wait_grads(self) -> None:
+        """Make the current stream wait for every pending reduce-scatter."""
+        cur = torch.cuda.current_stream(self.device) if self.device.type == "cuda" else None
+        for u in self.units:
+            if u.rs_event is not None:
+                cur.wait_event(u.rs_event)
+                u.rs_event = None
+
+    # ---------------------------------------------------------------- forward
+    _active = False
+
+    def forward(self, *args: Any, **kwargs: Any) -> Any:
+        self._gather(self.units[0], wait=True)
+        tensors: Dict[str, torch.Tensor] = {}
+        grad = torch.is_grad_enabled()
+        for u in self.units:
+            for pidx, info in enumerate(u.params):
+                v = u.views[info.name]
+                tensors[info.name] = _GradSink.apply(self._anchor, v, self, u.index, pidx) if grad else v
+        self._active = True
+        try:
+            out = torch.func.functional_call(self.module, tensors, args, kwargs, strict=False, tie_weights=True)
+        finally:
+            self._active = False
+        return out
+
+    @contextlib.contextmanager
+    def no_sync(self) -> Iterator[None]:
+        prev = self._sync_grads
+        self._sync_grads = False
+        try:
+            yield
+        finally:
+            self._sync_grads = prev
+
+    def set_sync(self, flag: bool) -> None:
+        self._sync_grads = flag
+
+    # ------------------------------------------------------------- utilities
+    def grad_shards(self) -> List[torch.Tensor]:
+        return [u.grad_shard for u in self.units]
+
+    @torch.no_grad()
+    def clip_grad_norm_(self, max_norm: float, norm_type: float = 2.0) -> torch.Tensor:
+        self.wait_grads()
+        sq = torch.zeros((), dtype=torch.float32, device=self.device)
+        for u in self.units:
+            sq += u.grad_shard.float().pow(2).sum()
+        if self.world > 1:
+            dist.all_reduce(sq, group=self.pg)
+        norm = sq.sqrt()
+        coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
+        for u in self.units:
+            u.grad_shard.mul_(coef)
+        return norm
+
+    @torch.no_grad()
+    def refresh(self) -> None:
+        """Propagate updated master weights to the compute copies."""
+        for u in self.units:
+            if self.world == 1:
+                u.compute.copy_(u.master)
+            else:
+                u.compute_shard.copy_(u.master)
+                self._free(u)
+
+    @torch.no_grad()
+    def zero_grad(self) -> None:
+        for u in self.units:
+            if self.world > 1:
+                u.grad_shard.zero_()
+            else:
+                u.grad_acc.zero_()
+
+    # ----------------------------------------------------------- checkpoints
+    @torch.no_grad()
+    def full_flat(self, u: Unit, src: torch.Tensor) -> torch.Tensor:
+        """All-gather a per-unit shard-sized fp32 tensor into a full flat tensor."""
+        if self.world == 1:
+            return src
+        out = torch.empty(u.total, dtype=src.dtype, device=self.device)
+        dist.all_gather_into_tensor(out, src.contiguous(), group=self.pg)
+        return out
+
+    @torch.no_grad()
+    def full_state_dict(self) -> Dict[str, torch.Tensor]:
+        """Unsharded fp32 parameters by name (collective on every rank)."""
+        out: Dict[str, torch.Tensor] = {}
+        for u in self.units:
+            full = self.full_flat(u, u.master)
+            for info in u.params:
+                out[info.name] = full[info.offset: info.offset + info.numel].view(info.shape).detach().cpu().clone()
+        return out
+
+    @torch.no_grad()
+    def load_full_state_dict(self, sd: Dict[str, torch.Tensor]) -> None:
+        for u in self.units:
+            full = torch.zeros(u.total, dtype=torch.float32, device=self.device)
+            for info in u.params:
+                if info.name in sd:
+                    full[info.offset: info.offset + info.numel].copy_(sd[info.name].reshape(-1).float())
+                else:
+                    full[info.offset: info.offset + info.numel].copy_(self.full_flat(u, u.master)[info.offset: info.offset + info.numel])
+            lo = self.rank * u.shard
+            u.master.copy_(full[lo: lo + u.shard] if self.world > 1 else full)
+        self.refresh()
+
+    def make_optimizer(self, optimizer_cls: Type[torch.optim.Optimizer], defaults: Dict[str, Any]) -> "ShardedHybridOptimizer":
+        from llm_research_b200.parallel.dmuon import ShardedHybridOptimizer
+
+        return ShardedHybridOptimizer(self, optimizer_cls, defaults)
