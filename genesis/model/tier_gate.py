@@ -43,4 +43,8 @@ class TierGate(nn.Module):
         if self._last_scores is None:
             return torch.tensor(0.0)
         s = self._last_scores
-        return s.mean(dim=0).float().var() + s.mean(dim=-1).float().var()
+        # var() of a single value is NaN (the reference returns NaN for batch 1
+        # or a single chunk); a lone value has zero spread, so it contributes 0.
+        chunk_load, per_sample = s.mean(dim=0).float(), s.mean(dim=-1).float()
+        loss = chunk_load.var() if chunk_load.numel() > 1 else chunk_load.sum() * 0
+        return loss + (per_sample.var() if per_sample.numel() > 1 else per_sample.sum() * 0)

@@ -197,33 +197,36 @@ class ShardedHybridOptimizer:
         ns_steps = g["ns_steps"]
         units = eng.units
 
-        if self.adam_segs:
-            pids = sorted({s.pid for s in self.adam_segs})
-            for pid in pids:
+        active = eng.touched_params()
+        adam_segs = [s for s in self.adam_segs if s.pid in active]
+        if adam_segs:
+            for pid in sorted({s.pid for s in adam_segs}):
                 self.steps[pid] += 1
             beta1, beta2 = g["betas"]
             ops.adamw_step(
-                [units[s.unit].master[s.shard_off: s.shard_off + s.length] for s in self.adam_segs],
-                [units[s.unit].grad_shard[s.shard_off: s.shard_off + s.length] for s in self.adam_segs],
-                [self.exp_avg[s.unit][s.shard_off: s.shard_off + s.length] for s in self.adam_segs],
-                [self.exp_avg_sq[s.unit][s.shard_off: s.shard_off + s.length] for s in self.adam_segs],
-                [self.steps[s.pid] for s in self.adam_segs],
+                [units[s.unit].master[s.shard_off: s.shard_off + s.length] for s in adam_segs],
+                [units[s.unit].grad_shard[s.shard_off: s.shard_off + s.length] for s in adam_segs],
+                [self.exp_avg[s.unit][s.shard_off: s.shard_off + s.length] for s in adam_segs],
+                [self.exp_avg_sq[s.unit][s.shard_off: s.shard_off + s.length] for s in adam_segs],
+                [self.steps[s.pid] for s in adam_segs],
                 lr=g["lr_adamw"], beta1=beta1, beta2=beta2, eps=g["eps"], weight_decay=g["weight_decay_adamw"],
             )
 
-        if self.muon_segs:
-            self._muon_step(lr_m, mu, wd_m, ns_steps)
+        if self.muon_ids and any(p in active for p in self.muon_ids):
+            self._muon_step(lr_m, mu, wd_m, ns_steps, active)
         eng.refresh()
         return loss
 
-    def _muon_step(self, lr: float, mu: float, wd: float, ns_steps: int) -> None:
+    def _muon_step(self, lr: float, mu: float, wd: float, ns_steps: int, active) -> None:
         eng, units, dev = self.engine, self.engine.units, self.engine.device
-        send = torch.empty(self.send_total, dtype=torch.bfloat16, device=dev)
-        outs, pos = [], 0
+        xdt = torch.bfloat16 if dev.type == "cuda" else torch.float32  # exchange / Newton-Schulz dtype
+        send = torch.zeros(self.send_total, dtype=xdt, device=dev)
+        outs, segs, pos = [], [], 0
         for s in self.send_order:
-            outs.append(send[pos: pos + s.length])
+            if s.pid in active:  # matrices without a gradient keep u = 0 -> zero update, no decay
+                outs.append(send[pos: pos + s.length])
+                segs.append(s)
             pos += s.length
-        segs = self.send_order
         gnorm_seg = ops.muon_prologue_into(
             [units[s.unit].master[s.shard_off: s.shard_off + s.length] for s in segs],
             [units[s.unit].grad_shard[s.shard_off: s.shard_off + s.length] for s in segs],
@@ -236,11 +239,11 @@ class ShardedHybridOptimizer:
         gsq.index_add_(0, idx, gnorm_seg.pow(2))
         if self.world > 1:
             dist.all_reduce(gsq, group=eng.pg)
-            recv = torch.empty(self.recv_total, dtype=torch.bfloat16, device=dev)
+            recv = torch.empty(self.recv_total, dtype=xdt, device=dev)
             dist.all_to_all_single(recv, send, self.recv_splits, self.send_splits, group=eng.pg)
         else:
             recv = send
-        stack = torch.empty(self.stack_total, dtype=torch.bfloat16, device=dev)
+        stack = torch.empty(self.stack_total, dtype=xdt, device=dev)
         stack.index_copy_(0, self.recv_to_stack, recv)
         gnorm = gsq.sqrt()
         base = 0
@@ -252,19 +255,20 @@ class ShardedHybridOptimizer:
             onorm = o.float().flatten(1).norm(dim=1)
             gn = gnorm[torch.tensor([self.muon_pos[p] for p in pids], device=dev)]
             scale = (lr * gn / (onorm + 1e-8)).view(n, 1, 1)
-            block.copy_((o.float() * scale).to(torch.bfloat16))
+            block.copy_((o.float() * scale).to(xdt))
             base += n * numel
-        back = torch.empty(self.recv_total, dtype=torch.bfloat16, device=dev)
+        back = torch.empty(self.recv_total, dtype=xdt, device=dev)
         back.copy_(stack.index_select(0, self.recv_to_stack))
         if self.world > 1:
-            upd = torch.empty(self.send_total, dtype=torch.bfloat16, device=dev)
+            upd = torch.empty(self.send_total, dtype=xdt, device=dev)
             dist.all_to_all_single(upd, back, self.send_splits, self.recv_splits, group=eng.pg)
         else:
             upd = back
         masters, deltas, pos = [], [], 0
-        for s in segs:
-            masters.append(units[s.unit].master[s.shard_off: s.shard_off + s.length])
-            deltas.append(upd[pos: pos + s.length])
+        for s in self.send_order:
+            if s.pid in active:
+                masters.append(units[s.unit].master[s.shard_off: s.shard_off + s.length])
+                deltas.append(upd[pos: pos + s.length])
             pos += s.length
         ops.axpy_list(masters, deltas, -1.0)
 

@@ -73,6 +73,7 @@ class Unit:
     master: Optional[torch.Tensor] = None
     grad_shard: Optional[torch.Tensor] = None
     compute_shard: Optional[torch.Tensor] = None
+    writer: Optional[torch.Tensor] = None
     gathered: bool = False
     gather_event: Optional[torch.cuda.Event] = None
     pending_grads: int = 0
@@ -127,6 +128,7 @@ class FlatShardEngine(nn.Module):
         self.reshard_after_forward = reshard_after_forward and self.world > 1
         self.device = device or next(module.parameters()).device
         self._sync_grads = True
+        self._touched: Set[int] = set()  # ParamInfo.index of parameters that received a gradient
         self._in_backward = False
         self._anchor = torch.zeros((), device=self.device, requires_grad=True)
         self.comm_stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
@@ -175,11 +177,16 @@ class FlatShardEngine(nn.Module):
             u.grad_acc = torch.zeros(u.total, dtype=torch.float32, device=dev)
             u.grad_shard = torch.zeros(u.shard, dtype=torch.float32, device=dev) if self.world > 1 else u.grad_acc
             u.compute = torch.empty(u.total, dtype=self.compute_dtype, device=dev)
+            # Writer alias of the same storage with its own version counter:
+            # gathers and refreshes go through it, so autograd does not see
+            # the re-materialisation of weights it saved for the backward.
+            u.writer = torch.empty(0, dtype=self.compute_dtype, device=dev).set_(
+                u.compute.untyped_storage(), 0, (u.total,), (1,))
             u.compute_shard = u.master.to(self.compute_dtype) if self.world > 1 else None
             for info in u.params:
                 u.views[info.name] = u.compute[info.offset: info.offset + info.numel].view(info.shape)
             if self.world == 1:
-                u.compute.copy_(u.master)
+                u.writer.copy_(u.master)
                 u.gathered = True
                 # The module's parameters alias the master weights.
                 for info in u.params:
@@ -200,6 +207,13 @@ class FlatShardEngine(nn.Module):
     def _gather(self, u: Unit, wait: bool = True) -> None:
         if self.world == 1:
             return
+        if not u.gathered and self.comm_stream is None:  # CPU ranks (gloo): synchronous
+            st = u.compute.untyped_storage()
+            if st.size() == 0:
+                st.resize_(u.total * u.compute.element_size())
+            dist.all_gather_into_tensor(u.writer, u.compute_shard, group=self.pg)
+            u.gathered = True
+            return
         if not u.gathered:
             st = u.compute.untyped_storage()
             if st.size() == 0:
@@ -207,7 +221,7 @@ class FlatShardEngine(nn.Module):
             cur = torch.cuda.current_stream(self.device)
             self.comm_stream.wait_stream(cur)
             with torch.cuda.stream(self.comm_stream):
-                dist.all_gather_into_tensor(u.compute, u.compute_shard, group=self.pg)
+                dist.all_gather_into_tensor(u.writer, u.compute_shard, group=self.pg)
                 ev = torch.cuda.Event()
                 ev.record(self.comm_stream)
             u.gather_event = ev
@@ -267,6 +281,7 @@ class FlatShardEngine(nn.Module):
         dst = u.grad_acc[info.offset: info.offset + info.numel].view(info.shape)
         dst.add_(grad.to(torch.float32) if grad.dtype != torch.float32 else grad)
         u.grads_seen.add(pidx)
+        self._touched.add(info.index)
         if len(u.grads_seen) == len(u.params):
             self._unit_backward_done(u)
 
@@ -283,6 +298,10 @@ class FlatShardEngine(nn.Module):
 
     def _reduce_scatter(self, u: Unit) -> None:
         if self.world == 1:
+            return
+        if self.comm_stream is None:
+            dist.reduce_scatter_tensor(u.grad_shard, u.grad_acc, op=dist.ReduceOp.AVG, group=self.pg)
+            u.grad_acc.zero_()
             return
         cur = torch.cuda.current_stream(self.device)
         self.comm_stream.wait_stream(cur)
@@ -311,7 +330,9 @@ class FlatShardEngine(nn.Module):
 
     def wait_grads(self) -> None:
         """Make the current stream wait for every pending reduce-scatter."""
-        cur = torch.cuda.current_stream(self.device) if self.device.type == "cuda" else None
+        if self.device.type != "cuda":
+            return
+        cur = torch.cuda.current_stream(self.device)
         for u in self.units:
             if u.rs_event is not None:
                 cur.wait_event(u.rs_event)
@@ -370,13 +391,24 @@ class FlatShardEngine(nn.Module):
         """Propagate updated master weights to the compute copies."""
         for u in self.units:
             if self.world == 1:
-                u.compute.copy_(u.master)
+                u.writer.copy_(u.master)
             else:
                 u.compute_shard.copy_(u.master)
                 self._free(u)
 
+    def touched_params(self) -> Set[int]:
+        """Parameters that received a gradient on any rank since ``zero_grad``
+        (optimizers skip the others, like ``p.grad is None`` in torch)."""
+        flags = torch.zeros(len(self.params), dtype=torch.float32, device=self.device)
+        if self._touched:
+            flags[list(self._touched)] = 1.0
+        if self.world > 1:
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=self.pg)
+        return {i for i, f in enumerate(flags.tolist()) if f > 0}
+
     @torch.no_grad()
     def zero_grad(self) -> None:
+        self._touched.clear()
         for u in self.units:
             if self.world > 1:
                 u.grad_shard.zero_()

@@ -1,0 +1,37 @@
+"""Run a function on ``world`` CPU ranks (gloo) and collect the per-rank results."""
+
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+from typing import Any, Callable, List
+
+import torch
+import torch.multiprocessing as mp
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _entry(rank: int, world: int, port: int, fn: Callable, args: tuple, outdir: str) -> None:
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    torch.set_num_threads(2)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        res = fn(rank, world, *args)
+        torch.save(res, os.path.join(outdir, f"r{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def run_ranks(fn: Callable, world: int, *args: Any) -> List[Any]:
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_entry, args=(world, free_port(), fn, args, d), nprocs=world, join=True)
+        return [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(world)]
