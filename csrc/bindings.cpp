@@ -44,6 +44,14 @@ std::tuple<at::Tensor, at::Tensor> attn_fwd(const at::Tensor&, const at::Tensor&
 std::tuple<at::Tensor, at::Tensor, at::Tensor> attn_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&,
                                                         const at::Tensor&, const at::Tensor&, const at::Tensor&, bool,
                                                         double);
+// gemm_sm100.cu
+at::Tensor gemm_tn(const at::Tensor&, const at::Tensor&, at::ScalarType, double);
+void gemm_tn_accumulate(const at::Tensor&, const at::Tensor&, at::Tensor&, double);
+int64_t sm100_error(int64_t);
+// attention_sm100.cu
+bool attn_sm100_supported(const at::Tensor&, const at::Tensor&, const at::Tensor&);
+std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor&, const at::Tensor&, const at::Tensor&, bool, double);
+int64_t attn_sm100_error(int64_t);
 }  // namespace lrb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -70,4 +78,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_dequantize", &lrb::nvfp4_dequantize);
   m.def("attn_fwd", &lrb::attn_fwd);
   m.def("attn_bwd", &lrb::attn_bwd);
+  m.def("gemm_tn", &lrb::gemm_tn);
+  m.def("gemm_tn_accumulate", &lrb::gemm_tn_accumulate);
+  m.def("sm100_error", &lrb::sm100_error);
+  m.def("attn_sm100_supported", &lrb::attn_sm100_supported);
+  m.def("attn_fwd_sm100", &lrb::attn_fwd_sm100);
+  m.def("attn_sm100_error", &lrb::attn_sm100_error);
 }

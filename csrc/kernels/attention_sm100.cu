@@ -1,0 +1,366 @@
+// Flash-attention forward on tcgen05 / TMEM for head_dim 128 (bf16, fp32
+// softmax statistics), causal or not, grouped-query heads read in place.
+//
+// CTA = one (batch, head, 128-query tile), 6 warps:
+//   warp 0      TMA: Q once (two 64-column swizzled boxes), then K and V
+//               tiles of 128 keys into 2-stage rings;
+//   warp 1      TMEM owner + MMA issue (one thread):
+//                 S_j = Q K_j^T   -> TMEM columns [128*(j%2), +128)  (two S buffers)
+//                 O  += P_j V_j   -> TMEM columns [256, 384)
+//               P_j is read from shared memory (K-major, 128-B swizzle); V is
+//               the MN-major B operand straight from its TMA tile;
+//   warps 2..5  softmax, one query row per thread (its TMEM lane): read S_j,
+//               mask, running max / sum in the exp2 domain, write P_j (bf16)
+//               to shared memory, rescale the O row in TMEM when the row max
+//               grew by more than 2^8 (lazy rescaling keeps exponents bounded
+//               by 256), and finally normalise O and store it with the row
+//               log-sum-exp.
+// S_{j+1} is computed while the softmax of tile j runs, and P_j V_j while the
+// softmax of tile j+1 runs.  All waits are bounded (sm100.cuh).
+#include "../common.cuh"
+#include "sm100.cuh"
+
+namespace lrb {
+namespace {
+
+using namespace sm100;
+
+constexpr int TQ = 128, TK = 128, HD = 128;
+constexpr int kThreads = 192;
+constexpr uint32_t kTileBytes = TQ * HD * 2;  // 32 KB: one Q/K/V/P tile
+constexpr uint32_t kHalf = kTileBytes / 2;    // 16 KB: one 64-column swizzle block
+constexpr size_t kSmem = 1024 + 6 * (size_t)kTileBytes + 512;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct FwdArgs {
+  void* out;     // (B, Sq, H, 128) contiguous
+  float* lse;    // (B, H, Sq)
+  int B, H, Hkv, Sq, Skv, causal;
+  float scale_log2;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, FwdArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sQ = base;
+  unsigned char* sK = base + kTileBytes;       // 2 stages
+  unsigned char* sV = base + 3 * kTileBytes;   // 2 stages
+  unsigned char* sP = base + 5 * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 6 * kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* v_full = bars + 3;   // [2]
+  uint64_t* k_free = bars + 5;   // [2]
+  uint64_t* v_free = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_free = bars + 11;  // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* o_done = bars + 14;
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = gridDim.x - 1 - blockIdx.x;  // heavy (late) causal tiles first
+  const int m0 = mt * TQ;
+  const int b = blockIdx.y / a.H, h = blockIdx.y % a.H, hk = h / (a.H / a.Hkv);
+  const int off = a.Skv - a.Sq;
+  int kv_end = a.Skv;
+  if (a.causal) kv_end = min(kv_end, m0 + TQ + off);
+  const int nt = kv_end > 0 ? (kv_end + TK - 1) / TK : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&k_free[i], 1);
+      mbar_init(&v_free[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0 && nt > 0) {
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_4d(sQ, &tmQ, q_full, 0, h, m0, b);
+      tma_load_4d(sQ + kHalf, &tmQ, q_full, 64, h, m0, b);
+      int armed_k = 0, armed_v = 0;
+      for (int j = 0; j < nt; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_free[st], ph ^ 1, a.err, kErrTmaWait)) break;
+        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+        tma_load_4d(sK + st * kTileBytes, &tmK, &k_full[st], 0, hk, j * TK, b);
+        tma_load_4d(sK + st * kTileBytes + kHalf, &tmK, &k_full[st], 64, hk, j * TK, b);
+        ++armed_k;
+        if (!mbar_wait(&v_free[st], ph ^ 1, a.err, kErrTmaWait)) break;
+        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+        tma_load_4d(sV + st * kTileBytes, &tmV, &v_full[st], 0, hk, j * TK, b);
+        tma_load_4d(sV + st * kTileBytes + kHalf, &tmV, &v_full[st], 64, hk, j * TK, b);
+        ++armed_v;
+      }
+      // Drain loads that may still be in flight before the CTA can exit.
+      mbar_wait(q_full, 0, nullptr, 0);
+      for (int i = 1; i <= 2 && i <= armed_k; ++i) mbar_wait(&k_full[(armed_k - i) & 1], ((armed_k - i) >> 1) & 1, nullptr, 0);
+      for (int i = 1; i <= 2 && i <= armed_v; ++i) mbar_wait(&v_full[(armed_v - i) & 1], ((armed_v - i) >> 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nt > 0) {
+      constexpr uint32_t idesc_qk = umma_idesc_f16_major(TQ, TK, true, false, false);
+      constexpr uint32_t idesc_pv = umma_idesc_f16_major(TQ, HD, true, false, true);
+      const uint32_t q0 = smem_addr(sQ), p0 = smem_addr(sP);
+      bool ok = mbar_wait(q_full, 0, a.err, kErrMmaWait);
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        if (!mbar_wait(p_full, i & 1, a.err, kErrMmaWait)) return false;
+        if (!mbar_wait(&v_full[st], ph, a.err, kErrMmaWait)) return false;
+        tc_fence_after();
+        const uint32_t v0 = smem_addr(sV + st * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < TK / 16; ++k) {
+          const uint64_t ad = umma_desc_k_sw128(p0 + (k >> 2) * kHalf + (k & 3) * 32);
+          const uint64_t bd = umma_desc_mn_sw128(v0 + k * 16 * 128, kHalf, 1024);
+          umma_f16(tO, ad, bd, idesc_pv, (i | k) != 0);
+        }
+        umma_commit(o_done);
+        umma_commit(&v_free[st]);
+        return true;
+      };
+      for (int j = 0; j < nt && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_full[st], ph, a.err, kErrMmaWait)) { ok = false; break; }
+        if (!mbar_wait(&s_free[st], ph ^ 1, a.err, kErrMmaWait)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k0 = smem_addr(sK + st * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint64_t ad = umma_desc_k_sw128(q0 + (k >> 2) * kHalf + (k & 3) * 32);
+          const uint64_t bd = umma_desc_k_sw128(k0 + (k >> 2) * kHalf + (k & 3) * 32);
+          umma_f16(tmem + st * TK, ad, bd, idesc_qk, k != 0);
+        }
+        umma_commit(&s_full[st]);
+        umma_commit(&k_free[st]);
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok) issue_pv(nt - 1);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    // ---------------------------------------------------------- softmax
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // row inside the tile == TMEM lane
+    const int qrow = m0 + r;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt && ok; ++j) {
+      const int st = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (!mbar_wait(&s_full[st], ph, a.err, kErrEpiWait)) { ok = false; break; }
+      tc_fence_after();
+      float s[TK];
+#pragma unroll
+      for (int c = 0; c < TK / 32; ++c)
+        tmem_ld_32x32b_x32(tmem + lane_base + st * TK + c * 32, reinterpret_cast<uint32_t*>(s + c * 32));
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_free[st]);  // S buffer may be overwritten by S_{j+2}
+      const int k0 = j * TK;
+      const bool edge = (k0 + TK > a.Skv) || (a.causal && k0 + TK - 1 > m0 + off);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < TK; ++i) {
+        float v = s[i] * a.scale_log2;
+        if (edge) {
+          const int key = k0 + i;
+          if (key >= a.Skv || (a.causal && key > qrow + off)) v = -INFINITY;
+        }
+        s[i] = v;
+        mx = fmaxf(mx, v);
+      }
+      float alpha = 1.f;
+      if (mx > m_run + kRescaleThreshold || m_run == -INFINITY) {
+        const float m_new = fmaxf(m_run, mx);
+        alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
+        m_run = m_new;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      float sum = 0.f;
+      uint32_t pk[TK / 2];
+#pragma unroll
+      for (int i = 0; i < TK; i += 2) {
+        const float p0 = exp2f(s[i] - m_use), p1 = exp2f(s[i + 1] - m_use);
+        sum += p0 + p1;
+        pk[i / 2] = pack_bf16(p0, p1);
+      }
+      l_run = l_run * alpha + sum;
+      // P_{j-1} V_{j-1} must have finished before P is overwritten and O rescaled.
+      if (j >= 1 && !mbar_wait(o_done, (j - 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
+      tc_fence_after();
+      if (j >= 1 && alpha != 1.f) {
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tO + lane_base + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(tO + lane_base + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      // P row -> shared memory, K-major 128-byte swizzle (two 64-key blocks).
+#pragma unroll
+      for (int kc = 0; kc < TK / 8; ++kc) {
+        const int blk = kc >> 3, ch = kc & 7;
+        uint4 v = make_uint4(pk[kc * 4], pk[kc * 4 + 1], pk[kc * 4 + 2], pk[kc * 4 + 3]);
+        *reinterpret_cast<uint4*>(sP + blk * kHalf + r * 128 + ((ch ^ (r & 7)) * 16)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ---------------------------------------------------------- epilogue
+    const bool have = ok && nt > 0 && mbar_wait(o_done, (nt - 1) & 1, a.err, kErrEpiWait);
+    tc_fence_after();
+    if (qrow < a.Sq) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + (((int64_t)b * a.Sq + qrow) * a.H + h) * HD;
+      const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o[32];
+        if (have) {
+          tmem_ld_32x32b_x32(tO + lane_base + c * 32, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint4 v = make_uint4(pack_bf16(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
+                               pack_bf16(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
+                               pack_bf16(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
+                               pack_bf16(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
+          *reinterpret_cast<uint4*>(dst + c * 32 + e) = v;
+        }
+      }
+      a.lse[((int64_t)b * a.H + h) * a.Sq + qrow] =
+          (have && l_run > 0.f) ? (m_run == -INFINITY ? 0.f : m_run) * kLn2 + __logf(l_run) : INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    LRB_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    LRB_CHECK(p != nullptr && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled unavailable");
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// (B, S, H, 128) tensor with arbitrary batch/seq/head strides; box = 64 x 1 x 128 x 1.
+CUtensorMap make_bshd_map(const at::Tensor& t) {
+  CUtensorMap m;
+  const cuuint64_t dims[4] = {(cuuint64_t)t.size(3), (cuuint64_t)t.size(2), (cuuint64_t)t.size(1),
+                              (cuuint64_t)t.size(0)};
+  const cuuint64_t strides[3] = {(cuuint64_t)t.stride(2) * 2, (cuuint64_t)t.stride(1) * 2, (cuuint64_t)t.stride(0) * 2};
+  const cuuint32_t box[4] = {64, 1, (cuuint32_t)TQ, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.data_ptr(), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LRB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  return m;
+}
+
+int* attn_error_word(const at::Device& dev) {
+  static at::Tensor words[16];
+  const int idx = dev.index() < 0 ? 0 : dev.index();
+  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().device(dev).dtype(at::kInt));
+  return words[idx].data_ptr<int>();
+}
+
+}  // namespace
+
+bool attn_sm100_supported(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v) {
+  auto ok = [](const at::Tensor& t) {
+    return t.scalar_type() == at::kBFloat16 && t.size(3) == HD && t.stride(3) == 1 &&
+           (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0 && (t.stride(0) * 2) % 16 == 0 &&
+           (t.stride(1) * 2) % 16 == 0 && (t.stride(2) * 2) % 16 == 0;
+  };
+  return ok(q) && ok(k) && ok(v);
+}
+
+std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                                  bool causal, double scale) {
+  LRB_CHECK(attn_sm100_supported(q, k, v), "attn_fwd_sm100: bf16, head_dim 128, 16-byte aligned strides required");
+  c10::cuda::CUDAGuard g(q.device());
+  const int64_t B = q.size(0), Sq = q.size(1), H = q.size(2), Skv = k.size(1), Hkv = k.size(2);
+  LRB_CHECK(Hkv > 0 && H % Hkv == 0 && k.sizes() == v.sizes(), "attn_fwd_sm100: head mismatch");
+  auto o = at::empty({B, Sq, H, HD}, q.options());
+  auto lse = at::empty({B, H, Sq}, q.options().dtype(at::kFloat));
+  if (B * Sq * H == 0) return {o, lse};
+  CUtensorMap tq = make_bshd_map(q), tk = make_bshd_map(k), tv = make_bshd_map(v);
+  FwdArgs args{o.data_ptr(), lse.data_ptr<float>(), (int)B, (int)H, (int)Hkv, (int)Sq, (int)Skv, causal ? 1 : 0,
+               (float)scale * kLog2e, attn_error_word(q.device())};
+  LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+  dim3 grid((unsigned)((Sq + TQ - 1) / TQ), (unsigned)(B * H));
+  attn_fwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, args);
+  LRB_LAUNCH_CHECK();
+  return {o, lse};
+}
+
+int64_t attn_sm100_error(int64_t device) {
+  int* w = attn_error_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
+  int h = 0;
+  LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
+  return h;
+}
+
+}  // namespace lrb

@@ -1,4 +1,5 @@
-// SwiGLU gating and the fused QKV split + RoPE, forward and backward.
+// SwiGLU gating (input [up | gate], output silu(gate) * up) and the fused QKV
+// split + RoPE, forward and backward.
 #include "../common.cuh"
 
 namespace lrb {
@@ -6,14 +7,14 @@ namespace {
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
 
-// gu: (rows, 2F) = [gate | up];  h: (rows, F)
+// gu: (rows, 2F) = [up | gate];  h: (rows, F)
 template <typename T>
 __global__ void swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ h, int64_t rows, int64_t F) {
   const int64_t n = rows * F;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / F, c = i - r * F;
-    const float g = to_f(gu[r * 2 * F + c]);
-    const float u = to_f(gu[r * 2 * F + F + c]);
+    const float u = to_f(gu[r * 2 * F + c]);
+    const float g = to_f(gu[r * 2 * F + F + c]);
     h[i] = from_f<T>(g * sigmoidf_(g) * u);
   }
 }
@@ -24,7 +25,7 @@ __global__ void swiglu_fwd_vec(const T* __restrict__ gu, T* __restrict__ h, int6
   const int64_t nv = rows * (F / 8);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / (F / 8), c = (i - r * (F / 8)) * 8;
-    Vec16<T> g = ld16(gu + r * 2 * F + c), u = ld16(gu + r * 2 * F + F + c), o;
+    Vec16<T> u = ld16(gu + r * 2 * F + c), g = ld16(gu + r * 2 * F + F + c), o;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float gf = to_f(g.v[j]);
@@ -40,7 +41,7 @@ __global__ void swiglu_bwd_vec(const T* __restrict__ dh, const T* __restrict__ g
   const int64_t nv = rows * (F / 8);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / (F / 8), c = (i - r * (F / 8)) * 8;
-    Vec16<T> d = ld16(dh + r * F + c), g = ld16(gu + r * 2 * F + c), u = ld16(gu + r * 2 * F + F + c), og, ou;
+    Vec16<T> d = ld16(dh + r * F + c), u = ld16(gu + r * 2 * F + c), g = ld16(gu + r * 2 * F + F + c), og, ou;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float gf = to_f(g.v[j]), uf = to_f(u.v[j]), df = to_f(d.v[j]);
@@ -48,8 +49,8 @@ __global__ void swiglu_bwd_vec(const T* __restrict__ dh, const T* __restrict__ g
       og.v[j] = from_f<T>(df * uf * s * (1.f + gf * (1.f - s)));
       ou.v[j] = from_f<T>(df * gf * s);
     }
-    st16(dgu + r * 2 * F + c, og);
-    st16(dgu + r * 2 * F + F + c, ou);
+    st16(dgu + r * 2 * F + c, ou);
+    st16(dgu + r * 2 * F + F + c, og);
   }
 }
 
@@ -59,10 +60,10 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ dh, const T* __restrict_
   const int64_t n = rows * F;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / F, c = i - r * F;
-    const float g = to_f(gu[r * 2 * F + c]), u = to_f(gu[r * 2 * F + F + c]), d = to_f(dh[i]);
+    const float u = to_f(gu[r * 2 * F + c]), g = to_f(gu[r * 2 * F + F + c]), d = to_f(dh[i]);
     const float s = sigmoidf_(g);
-    dgu[r * 2 * F + c] = from_f<T>(d * u * s * (1.f + g * (1.f - s)));
-    dgu[r * 2 * F + F + c] = from_f<T>(d * g * s);
+    dgu[r * 2 * F + F + c] = from_f<T>(d * u * s * (1.f + g * (1.f - s)));
+    dgu[r * 2 * F + c] = from_f<T>(d * g * s);
   }
 }
 
@@ -71,7 +72,62 @@ inline int grid_for(int64_t n, int threads) {
 }
 
 // ------------------------------------------------------------------ RoPE
-// qkv row layout [q: H*D | k: Hkv*D | v: Hkv*D]; one thread per (token, head, i < D/2) pair.
+// Vectorised form (2-byte types, D % 16 == 0): one block per token; the
+// token's cos/sin rows are staged in shared memory once and every thread
+// rotates 8 pairs with two 16-byte loads and two 16-byte stores.
+template <typename T, bool BWD>
+__global__ void __launch_bounds__(128) rope_qkv_vec_kernel(const T* __restrict__ src0, const T* __restrict__ src_k,
+                                                          const T* __restrict__ src_v, const float* __restrict__ cos_t,
+                                                          const float* __restrict__ sin_t, T* __restrict__ dst0,
+                                                          T* __restrict__ dst_k, T* __restrict__ dst_v, int S, int H,
+                                                          int Hkv, int D, int offset) {
+  extern __shared__ float tab[];  // cos[0:D], sin[D:2D]
+  const int64_t t = blockIdx.x;
+  const int pos = (int)(t % S) + offset;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    tab[i] = cos_t[(int64_t)pos * D + i];
+    tab[D + i] = sin_t[(int64_t)pos * D + i];
+  }
+  __syncthreads();
+  const int half = D / 2, groups = half / 8, heads = H + 2 * Hkv;
+  const int64_t row = (int64_t)heads * D;
+  for (int w = threadIdx.x; w < heads * groups; w += blockDim.x) {
+    const int h = w / groups, j = (w - (w / groups) * groups) * 8;
+    // forward: src0 = packed qkv row, dst = q/k/v; backward: the reverse.
+    const T* in;
+    T* out;
+    if (!BWD) {
+      in = src0 + t * row + (int64_t)h * D;
+      out = h < H ? dst0 + (t * H + h) * D : (h < H + Hkv ? dst_k + (t * Hkv + h - H) * D : dst_v + (t * Hkv + h - H - Hkv) * D);
+    } else {
+      in = h < H ? src0 + (t * H + h) * D : (h < H + Hkv ? src_k + (t * Hkv + h - H) * D : src_v + (t * Hkv + h - H - Hkv) * D);
+      out = dst0 + t * row + (int64_t)h * D;
+    }
+    Vec16<T> a = ld16(in + j), b = ld16(in + j + half);
+    if (h < H + Hkv) {
+      Vec16<T> oa, ob;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float x = to_f(a.v[e]), y = to_f(b.v[e]);
+        const float c = tab[j + e], s = tab[D + j + e], c2 = tab[half + j + e], s2 = tab[D + half + j + e];
+        if (!BWD) {
+          oa.v[e] = from_f<T>(x * c - y * s);
+          ob.v[e] = from_f<T>(y * c2 + x * s2);
+        } else {
+          oa.v[e] = from_f<T>(x * c + y * s2);
+          ob.v[e] = from_f<T>(y * c2 - x * s);
+        }
+      }
+      st16(out + j, oa);
+      st16(out + j + half, ob);
+    } else {
+      st16(out + j, a);
+      st16(out + j + half, b);
+    }
+  }
+}
+
+// Scalar form: qkv row layout [q: H*D | k: Hkv*D | v: Hkv*D]; one thread per (token, head, i < D/2) pair.
 template <typename T>
 __global__ void rope_qkv_fwd_kernel(const T* __restrict__ qkv, const float* __restrict__ cos_t,
                                     const float* __restrict__ sin_t, T* __restrict__ q, T* __restrict__ k,
@@ -191,6 +247,13 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> rope_qkv_fwd(const at::Tensor& qk
   const int64_t n = B * S * (H + 2 * Hkv) * (D / 2);
   if (n == 0) return {q, k, v};
   LRB_DISPATCH_FLOAT(qkv.scalar_type(), T, [&] {
+    if (sizeof(T) == 2 && D % 16 == 0) {
+      rope_qkv_vec_kernel<T, false><<<(unsigned)(B * S), 128, 2 * D * sizeof(float), stream()>>>(
+          reinterpret_cast<const T*>(qkv.data_ptr()), nullptr, nullptr, cos_t.data_ptr<float>(),
+          sin_t.data_ptr<float>(), reinterpret_cast<T*>(q.data_ptr()), reinterpret_cast<T*>(k.data_ptr()),
+          reinterpret_cast<T*>(v.data_ptr()), (int)S, (int)H, (int)Hkv, (int)D, (int)offset);
+      return;
+    }
     rope_qkv_fwd_kernel<T><<<grid_for(n, 256), 256, 0, stream()>>>(
         reinterpret_cast<const T*>(qkv.data_ptr()), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
         reinterpret_cast<T*>(q.data_ptr()), reinterpret_cast<T*>(k.data_ptr()), reinterpret_cast<T*>(v.data_ptr()),
@@ -208,6 +271,13 @@ at::Tensor rope_qkv_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Te
   const int64_t n = B * S * (H + 2 * Hkv) * (D / 2);
   if (n == 0) return dqkv;
   LRB_DISPATCH_FLOAT(dq.scalar_type(), T, [&] {
+    if (sizeof(T) == 2 && D % 16 == 0) {
+      rope_qkv_vec_kernel<T, true><<<(unsigned)(B * S), 128, 2 * D * sizeof(float), stream()>>>(
+          reinterpret_cast<const T*>(dq.data_ptr()), reinterpret_cast<const T*>(dk.data_ptr()),
+          reinterpret_cast<const T*>(dv.data_ptr()), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+          reinterpret_cast<T*>(dqkv.data_ptr()), nullptr, nullptr, (int)S, (int)H, (int)Hkv, (int)D, (int)offset);
+      return;
+    }
     rope_qkv_bwd_kernel<T><<<grid_for(n, 256), 256, 0, stream()>>>(
         reinterpret_cast<const T*>(dq.data_ptr()), reinterpret_cast<const T*>(dk.data_ptr()),
         reinterpret_cast<const T*>(dv.data_ptr()), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),

@@ -28,6 +28,7 @@ import torch.nn.functional as F
 
 from genesis.model.rotary import apply_rotary_emb
 from llm_research_b200 import ops
+from llm_research_b200.ops.linear import cat_rows
 
 # The reference probes flash-attn here; the fused kernel replaces it.
 FLASH_ATTN_AVAILABLE = True
@@ -60,7 +61,7 @@ class MultiHeadAttention(nn.Module):
 
     # ------------------------------------------------------------------
     def _qkv(self, x: torch.Tensor) -> torch.Tensor:
-        w = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight], 0)
+        w = cat_rows(self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
         b = None
         if self.q_proj.bias is not None:
             b = torch.cat([self.q_proj.bias, self.k_proj.bias, self.v_proj.bias], 0)

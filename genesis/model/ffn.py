@@ -2,7 +2,7 @@
 
 ``FFN(x) = W2( silu(W_gate x) * (W1 x) )``; ``d_ff`` defaults to
 ``ceil(8/3 * d_model / 256) * 256``.  On B200 the two up projections are one
-GEMM against ``[W_gate; W1]`` and the gating runs in one fused kernel
+GEMM against ``[W1; W_gate]`` and the gating runs in one fused kernel
 (``llm_research_b200.ops.swiglu``).
 """
 
@@ -13,6 +13,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from llm_research_b200 import ops
+from llm_research_b200.ops.linear import cat_rows
 
 
 def default_ffn_dim(d_model: int) -> int:
@@ -31,10 +32,10 @@ class SwiGLUFFN(nn.Module):
         self.dropout = nn.Dropout(dropout) if dropout > 0.0 else nn.Identity()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        w = torch.cat([self.w_gate.weight, self.w1.weight], 0)
+        w = cat_rows(self.w1.weight, self.w_gate.weight)
         b = None
         if self.w1.bias is not None:
-            b = torch.cat([self.w_gate.bias, self.w1.bias], 0)
-        gu = F.linear(x, w, b)  # [..., gate | up]
+            b = torch.cat([self.w1.bias, self.w_gate.bias], 0)
+        gu = F.linear(x, w, b)  # [..., up | gate]
         h = ops.swiglu(gu)
         return self.w2(self.dropout(h))

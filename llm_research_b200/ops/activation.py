@@ -1,7 +1,9 @@
-"""SwiGLU gating on the output of the fused ``[W_gate; W1]`` projection.
+"""SwiGLU gating on the output of the fused ``[W1; W_gate]`` projection.
 
-``gu[..., :F]`` is the gate pre-activation and ``gu[..., F:]`` the value;
-``h = silu(gate) * value`` computed in fp32, rounded once.
+``gu[..., :F]`` is the value (``W1 x``) and ``gu[..., F:]`` the gate
+pre-activation (``W_gate x``) -- the order in which ``SwiGLUFFN`` registers
+its weights, so the fused weight is a zero-copy view in the engine's flat
+buffer.  ``h = silu(gate) * value`` computed in fp32, rounded once.
 Backward: ``d_gate = dh * value * s * (1 + gate * (1 - s))`` with
 ``s = sigmoid(gate)``; ``d_value = dh * silu(gate)``.
 """
@@ -28,6 +30,6 @@ class _SwiGLUFn(torch.autograd.Function):
 
 def swiglu(gu: torch.Tensor) -> torch.Tensor:
     if not gu.is_cuda:
-        g, u = gu.chunk(2, dim=-1)
+        u, g = gu.chunk(2, dim=-1)
         return (F.silu(g.float()) * u.float()).to(gu.dtype)
     return _SwiGLUFn.apply(gu.contiguous())

@@ -8,11 +8,18 @@ aligned to the end of the key sequence: query ``i`` sees keys
 ``1/sqrt(D)``.  Output ``(B, Sq, H, D)`` in the input dtype; the row
 log-sum-exp is kept for the backward pass (and is the hook for
 sequence-parallel merging).
+
+Forward: bf16 with head_dim 128 runs the tcgen05/TMEM kernel
+(``csrc/kernels/attention_sm100.cu``); other head dims and fp16 run the
+``mma.sync`` kernel (``csrc/kernels/attention.cu``).  The backward is the
+``mma.sync`` kernel for all shapes.  ``LRB_ATTN_SM100=0`` disables the
+tcgen05 forward (for A/B comparisons).
 """
 
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.nn.functional as F
@@ -35,10 +42,20 @@ def _reference(q, k, v, causal: bool, scale: float) -> torch.Tensor:
     return torch.matmul(p, vh).transpose(1, 2).to(q.dtype)
 
 
+_USE_SM100 = os.environ.get("LRB_ATTN_SM100", "1") != "0"
+
+
+def _forward(q, k, v, causal: bool, scale: float):
+    C = native()
+    if _USE_SM100 and C.attn_sm100_supported(q, k, v):
+        return C.attn_fwd_sm100(q, k, v, bool(causal), float(scale))  # tcgen05 / TMEM kernel
+    return C.attn_fwd(q, k, v, bool(causal), float(scale))          # mma.sync kernel, any head dim
+
+
 class _FlashAttnFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, causal, scale):
-        out, lse = native().attn_fwd(q, k, v, bool(causal), float(scale))
+        out, lse = _forward(q, k, v, causal, scale)
         ctx.save_for_backward(q, k, v, out, lse)
         ctx.causal = causal
         ctx.scale = scale

@@ -279,7 +279,7 @@ class FlatShardEngine(nn.Module):
         u = self.units[ui]
         info = u.params[pidx]
         dst = u.grad_acc[info.offset: info.offset + info.numel].view(info.shape)
-        dst.add_(grad.to(torch.float32) if grad.dtype != torch.float32 else grad)
+        dst.add_(grad)  # bf16 -> fp32 accumulate in one pass (no separate cast)
         u.grads_seen.add(pidx)
         self._touched.add(info.index)
         if len(u.grads_seen) == len(u.params):

@@ -61,7 +61,7 @@ def test_swiglu(F_):
     dh = torch.randn_like(h)
     h.backward(dh)
     ref = gu.detach().float().requires_grad_(True)
-    g, u = ref.chunk(2, -1)
+    u, g = ref.chunk(2, -1)
     hr = F.silu(g) * u
     hr.backward(dh.float())
     torch.testing.assert_close(h.float(), hr.detach(), atol=2e-2, rtol=2e-2)
@@ -233,3 +233,30 @@ def test_nvfp4_quant_roundtrip():
     y = ops.nvfp4_dequantize(pk, sb, st)
     rel = (y - x).norm() / x.norm()
     assert rel.item() < 0.15
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1000, 700, 520), (4096, 6144, 2048), (300, 4000, 4096), (37, 96, 16)])
+@pytest.mark.parametrize("out", [torch.bfloat16, torch.float32])
+def test_tcgen05_gemm(M, N, K, out):
+    from llm_research_b200.ops.gemm import matmul_tn, sm100_error
+
+    a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    b = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    c = matmul_tn(a, b, out_dtype=out)
+    ref = a.float() @ b.float().t()
+    torch.cuda.synchronize()
+    assert sm100_error() == 0
+    torch.testing.assert_close(c.float(), ref, atol=2e-2 * (K ** 0.5), rtol=2e-2)
+
+
+def test_tcgen05_gemm_accumulate():
+    from llm_research_b200.ops.gemm import matmul_tn_accumulate, sm100_error
+
+    a = torch.randn(512, 256, device="cuda").to(torch.bfloat16)
+    b = torch.randn(384, 256, device="cuda").to(torch.bfloat16)
+    c = torch.randn(512, 384, device="cuda")
+    ref = c + 0.5 * (a.float() @ b.float().t())
+    matmul_tn_accumulate(a, b, c, alpha=0.5)
+    torch.cuda.synchronize()
+    assert sm100_error() == 0
+    torch.testing.assert_close(c, ref, atol=0.05, rtol=1e-2)
