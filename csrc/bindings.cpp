@@ -52,6 +52,8 @@ int64_t sm100_error(int64_t);
 bool attn_sm100_supported(const at::Tensor&, const at::Tensor&, const at::Tensor&);
 std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor&, const at::Tensor&, const at::Tensor&, bool, double);
 int64_t attn_sm100_error(int64_t);
+// memory.cu
+std::tuple<at::Tensor, at::Tensor, at::Tensor> topk_softmax_gather(const at::Tensor&, const at::Tensor&, int64_t);
 }  // namespace lrb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -84,4 +86,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_sm100_supported", &lrb::attn_sm100_supported);
   m.def("attn_fwd_sm100", &lrb::attn_fwd_sm100);
   m.def("attn_sm100_error", &lrb::attn_sm100_error);
+  m.def("topk_softmax_gather", &lrb::topk_softmax_gather);
 }

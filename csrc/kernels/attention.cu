@@ -136,13 +136,13 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const AttnParams p) {
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       const float m_new = fmaxf(m_r[r], mx);
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = exp2f(m_r[r] - m_use);
+      const float alpha = fast_exp2(m_r[r] - m_use);
       m_r[r] = m_new;
       float rs = 0.f;
 #pragma unroll
       for (int j = 0; j < BN / 8; ++j) {
-        s[j][2 * r] = exp2f(s[j][2 * r] - m_use);
-        s[j][2 * r + 1] = exp2f(s[j][2 * r + 1] - m_use);
+        s[j][2 * r] = fast_exp2(s[j][2 * r] - m_use);
+        s[j][2 * r + 1] = fast_exp2(s[j][2 * r + 1] - m_use);
         rs += s[j][2 * r] + s[j][2 * r + 1];
       }
       l_r[r] = l_r[r] * alpha + rs;
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnParams p) {
           const int ql = j * 8 + (lane & 3) * 2 + (e & 1);
           const int q = m0 + ql;
           const bool ok = key < p.Skv && q < p.Sq && (!p.causal || key <= q + off);
-          const float pv = ok ? exp2f(st[j][e] * p.scale_log2 - sL[ql]) : 0.f;
+          const float pv = ok ? fast_exp2(st[j][e] * p.scale_log2 - sL[ql]) : 0.f;
           st[j][e] = pv;
           dp[j][e] = pv * (dp[j][e] - sDi[ql]);
         }

@@ -1,7 +1,7 @@
 // Flash-attention forward on tcgen05 / TMEM for head_dim 128 (bf16, fp32
 // softmax statistics), causal or not, grouped-query heads read in place.
 //
-// CTA = one (batch, head, 128-query tile), 6 warps:
+// CTA = one (batch, head, 128-query tile), 10 warps:
 //   warp 0      TMA: Q once (two 64-column swizzled boxes), then K and V
 //               tiles of 128 keys into 2-stage rings;
 //   warp 1      TMEM owner + MMA issue (one thread):
@@ -9,12 +9,16 @@
 //                 O  += P_j V_j   -> TMEM columns [256, 384)
 //               P_j is read from shared memory (K-major, 128-B swizzle); V is
 //               the MN-major B operand straight from its TMA tile;
-//   warps 2..5  softmax, one query row per thread (its TMEM lane): read S_j,
-//               mask, running max / sum in the exp2 domain, write P_j (bf16)
-//               to shared memory, rescale the O row in TMEM when the row max
-//               grew by more than 2^8 (lazy rescaling keeps exponents bounded
-//               by 256), and finally normalise O and store it with the row
-//               log-sum-exp.
+//   warps 2..9  softmax, two threads per query row (its TMEM lane): warps
+//               2..5 own key/head-dim columns 0..63, warps 6..9 columns
+//               64..127 of the same lanes; the row max is exchanged through
+//               shared memory behind an mbarrier.  Each thread reads its half
+//               of S_j, masks, keeps a running max / sum in the exp2 domain
+//               (SFU ex2), writes its 64-key block of P_j (bf16) to shared
+//               memory, rescales its half of the O row in TMEM when the row
+//               max grew by more than 2^8 (lazy rescaling keeps exponents
+//               bounded by 256), and finally normalises and stores its half of
+//               O; the row log-sum-exp combines both partial sums.
 // S_{j+1} is computed while the softmax of tile j runs, and P_j V_j while the
 // softmax of tile j+1 runs.  All waits are bounded (sm100.cuh).
 #include "../common.cuh"
@@ -26,10 +30,13 @@ namespace {
 using namespace sm100;
 
 constexpr int TQ = 128, TK = 128, HD = 128;
-constexpr int kThreads = 192;
+// 2 control warps + 8 softmax warps: two threads per query row, each owning 64
+// of the 128 key columns of S (and 64 of the 128 columns of O).
+constexpr int kThreads = 320;
+constexpr int kSoftmaxThreads = 256;
 constexpr uint32_t kTileBytes = TQ * HD * 2;  // 32 KB: one Q/K/V/P tile
 constexpr uint32_t kHalf = kTileBytes / 2;    // 16 KB: one 64-column swizzle block
-constexpr size_t kSmem = 1024 + 6 * (size_t)kTileBytes + 512;
+constexpr size_t kSmem = 1024 + 6 * (size_t)kTileBytes + 512 + 4 * TQ * sizeof(float) + 2 * TQ * sizeof(float);
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -67,7 +74,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = bars + 13;
   uint64_t* o_done = bars + 14;
   uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* xbar = bars + 16;    // [2 parity][4 quarter]: row-max exchange between paired warps
+  uint64_t* sbar = bars + 24;    // [4 quarter]: row-sum exchange
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 32);
+  float* xmax = reinterpret_cast<float*>(base + 6 * kTileBytes + 512);  // [2 parity][2 half][TQ]
+  float* xsum = xmax + 4 * TQ;                                          // [2 half][TQ]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = gridDim.x - 1 - blockIdx.x;  // heavy (late) causal tiles first
@@ -86,9 +97,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&k_free[i], 1);
       mbar_init(&v_free[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
+      mbar_init(&s_free[i], kSoftmaxThreads);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, kSoftmaxThreads);
+    for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 64);
+    for (int i = 0; i < 4; ++i) mbar_init(&sbar[i], 64);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -177,10 +190,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------- softmax
+    // Warps 2..5 take key/hd columns [0, 64), warps 6..9 columns [64, 128) of
+    // the same rows; the row max and the final row sum are exchanged through
+    // shared memory between the two warps of a lane quarter.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // row inside the tile == TMEM lane
     const int qrow = m0 + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int c0 = half * 64;           // first owned column of S / O
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nt && ok; ++j) {
@@ -188,18 +206,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ph = (j >> 1) & 1;
       if (!mbar_wait(&s_full[st], ph, a.err, kErrEpiWait)) { ok = false; break; }
       tc_fence_after();
-      float s[TK];
-#pragma unroll
-      for (int c = 0; c < TK / 32; ++c)
-        tmem_ld_32x32b_x32(tmem + lane_base + st * TK + c * 32, reinterpret_cast<uint32_t*>(s + c * 32));
+      float s[64];
+      tmem_ld_32x32b_x32(tmem + lane_base + st * TK + c0, reinterpret_cast<uint32_t*>(s));
+      tmem_ld_32x32b_x32(tmem + lane_base + st * TK + c0 + 32, reinterpret_cast<uint32_t*>(s + 32));
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&s_free[st]);  // S buffer may be overwritten by S_{j+2}
-      const int k0 = j * TK;
-      const bool edge = (k0 + TK > a.Skv) || (a.causal && k0 + TK - 1 > m0 + off);
+      const int k0 = j * TK + c0;
+      const bool edge = (j * TK + TK > a.Skv) || (a.causal && j * TK + TK - 1 > m0 + off);
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < TK; ++i) {
+      for (int i = 0; i < 64; ++i) {
         float v = s[i] * a.scale_log2;
         if (edge) {
           const int key = k0 + i;
@@ -208,18 +225,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         s[i] = v;
         mx = fmaxf(mx, v);
       }
+      xmax[(st * 2 + half) * TQ + r] = mx;
+      mbar_arrive(&xbar[st * 4 + quarter]);
+      if (!mbar_wait(&xbar[st * 4 + quarter], ph, a.err, kErrEpiWait)) { ok = false; break; }
+      mx = fmaxf(mx, xmax[(st * 2 + (half ^ 1)) * TQ + r]);
       float alpha = 1.f;
       if (mx > m_run + kRescaleThreshold || m_run == -INFINITY) {
         const float m_new = fmaxf(m_run, mx);
-        alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
+        alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
         m_run = m_new;
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       float sum = 0.f;
-      uint32_t pk[TK / 2];
+      uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < TK; i += 2) {
-        const float p0 = exp2f(s[i] - m_use), p1 = exp2f(s[i + 1] - m_use);
+      for (int i = 0; i < 64; i += 2) {
+        const float p0 = fast_exp2(s[i] - m_use), p1 = fast_exp2(s[i + 1] - m_use);
         sum += p0 + p1;
         pk[i / 2] = pack_bf16(p0, p1);
       }
@@ -227,45 +248,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P_{j-1} V_{j-1} must have finished before P is overwritten and O rescaled.
       if (j >= 1 && !mbar_wait(o_done, (j - 1) & 1, a.err, kErrEpiWait)) { ok = false; break; }
       tc_fence_after();
-      if (j >= 1 && alpha != 1.f) {
+      // tcgen05.ld/st are warp-collective: rescale if any row of the warp needs it.
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
-          tmem_ld_32x32b_x32(tO + lane_base + c * 32, o);
+          tmem_ld_32x32b_x32(tO + lane_base + c0 + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st_32x32b_x32(tO + lane_base + c * 32, o);
+          tmem_st_32x32b_x32(tO + lane_base + c0 + c * 32, o);
         }
         tmem_st_wait();
       }
-      // P row -> shared memory, K-major 128-byte swizzle (two 64-key blocks).
+      // This thread's 64 keys are exactly one 64-key swizzle block of P.
 #pragma unroll
-      for (int kc = 0; kc < TK / 8; ++kc) {
-        const int blk = kc >> 3, ch = kc & 7;
-        uint4 v = make_uint4(pk[kc * 4], pk[kc * 4 + 1], pk[kc * 4 + 2], pk[kc * 4 + 3]);
-        *reinterpret_cast<uint4*>(sP + blk * kHalf + r * 128 + ((ch ^ (r & 7)) * 16)) = v;
+      for (int ch = 0; ch < 8; ++ch) {
+        uint4 v = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(sP + half * kHalf + r * 128 + ((ch ^ (r & 7)) * 16)) = v;
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }
     // ---------------------------------------------------------- epilogue
-    const bool have = ok && nt > 0 && mbar_wait(o_done, (nt - 1) & 1, a.err, kErrEpiWait);
+    xsum[half * TQ + r] = l_run;
+    mbar_arrive(&sbar[quarter]);
+    const bool summed = mbar_wait(&sbar[quarter], 0, a.err, kErrEpiWait);
+    const float l_row = l_run + (summed ? xsum[(half ^ 1) * TQ + r] : 0.f);
+    const bool have = ok && summed && nt > 0 && mbar_wait(o_done, (nt - 1) & 1, a.err, kErrEpiWait);
     tc_fence_after();
-    if (qrow < a.Sq) {
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + (((int64_t)b * a.Sq + qrow) * a.H + h) * HD;
-      const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
+    // Every lane executes the (warp-collective) TMEM loads; only rows < Sq store.
+    const bool have_w = __all_sync(0xffffffffu, have);
+    {
+      __nv_bfloat16* dst =
+          reinterpret_cast<__nv_bfloat16*>(a.out) + (((int64_t)b * a.Sq + qrow) * a.H + h) * HD + c0;
+      const float inv = (have_w && l_row > 0.f) ? 1.f / l_row : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
-        if (have) {
-          tmem_ld_32x32b_x32(tO + lane_base + c * 32, o);
+        if (have_w) {
+          tmem_ld_32x32b_x32(tO + lane_base + c0 + c * 32, o);
           tmem_ld_wait();
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0u;
         }
+        if (qrow >= a.Sq) continue;
 #pragma unroll
         for (int e = 0; e < 32; e += 8) {
           uint4 v = make_uint4(pack_bf16(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
@@ -275,8 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(dst + c * 32 + e) = v;
         }
       }
-      a.lse[((int64_t)b * a.H + h) * a.Sq + qrow] =
-          (have && l_run > 0.f) ? (m_run == -INFINITY ? 0.f : m_run) * kLn2 + __logf(l_run) : INFINITY;
+      if (qrow < a.Sq && half == 0)
+        a.lse[((int64_t)b * a.H + h) * a.Sq + qrow] =
+            (have_w && l_row > 0.f) ? (m_run == -INFINITY ? 0.f : m_run) * kLn2 + __logf(l_row) : INFINITY;
     }
   }
   tc_fence_before();

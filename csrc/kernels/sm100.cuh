@@ -11,7 +11,9 @@
 namespace lrb {
 namespace sm100 {
 
-constexpr uint32_t kSpinLimit = 1u << 26;
+// ~4M polls: orders of magnitude above any legitimate wait in these kernels,
+// short enough that a stuck pipeline gives up within seconds.
+constexpr uint32_t kSpinLimit = 1u << 22;
 
 // Error codes written to the device error word (first writer wins).
 enum : int { kErrNone = 0, kErrTmaWait = 1, kErrMmaWait = 2, kErrEpiWait = 3, kErrAccWait = 4 };

@@ -1,0 +1,109 @@
+"""Configuration loading (``olympus/utils/config.py:18-66``) plus the mapping
+of the reference's nested training YAML schema onto :class:`HLRTConfig`.
+
+``load_config(path, overrides)`` returns an OmegaConf ``DictConfig`` when
+OmegaConf is installed, else a plain dict; dotted override keys
+(``{"model.tier1.layers": 4}``) are applied after loading.
+
+The YAML presets of the reference (``genesis/training/configs/phase*.yaml``)
+describe models as ``model.tier1.layers``, ``model.tier2.d_model``,
+``model.gate.tier2_threshold`` ... and no code of the reference reads them;
+:func:`hlrt_config_from_yaml` does.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Any, Dict, Mapping, Optional, Union
+
+try:  # optional, like the reference
+    from omegaconf import DictConfig, OmegaConf
+
+    _HAS_OMEGACONF = True
+except ImportError:  # pragma: no cover - depends on the environment
+    _HAS_OMEGACONF = False
+
+
+def _apply_overrides(cfg: dict, overrides: Mapping[str, Any]) -> None:
+    for key, value in overrides.items():
+        node = cfg
+        *parents, leaf = key.split(".")
+        for p in parents:
+            node = node.setdefault(p, {})
+        node[leaf] = value
+
+
+def load_config(path: str, overrides: Optional[Dict[str, Any]] = None) -> Union["DictConfig", Dict[str, Any]]:
+    if not os.path.isfile(path):
+        raise FileNotFoundError(f"Config file not found: {path}")
+    if _HAS_OMEGACONF:
+        cfg = OmegaConf.load(path)
+        if overrides:
+            cfg = OmegaConf.merge(cfg, OmegaConf.create(_nest(overrides)))
+        return cfg
+    import yaml
+
+    with open(path) as f:
+        cfg = yaml.safe_load(f) or {}
+    if overrides:
+        _apply_overrides(cfg, overrides)
+    return cfg
+
+
+def _nest(flat: Mapping[str, Any]) -> Dict[str, Any]:
+    out: Dict[str, Any] = {}
+    _apply_overrides(out, flat)
+    return out
+
+
+def _plain(cfg: Any) -> Dict[str, Any]:
+    if _HAS_OMEGACONF and isinstance(cfg, DictConfig):
+        return OmegaConf.to_container(cfg, resolve=True)  # type: ignore[return-value]
+    return dict(cfg)
+
+
+def hlrt_config_from_yaml(path_or_cfg: Any, overrides: Optional[Dict[str, Any]] = None):
+    """Build an :class:`HLRTConfig` from the nested ``model:`` section."""
+    from genesis.model.hlrt import HLRTConfig
+
+    cfg = load_config(path_or_cfg, overrides) if isinstance(path_or_cfg, str) else path_or_cfg
+    m = _plain(cfg).get("model", {})
+    t1, t2, t3, gate = m.get("tier1", {}), m.get("tier2", {}), m.get("tier3", {}), m.get("gate", {})
+    kw: Dict[str, Any] = {}
+
+    def put(key: str, value: Any) -> None:
+        if value is not None:
+            kw[key] = value
+
+    put("vocab_size", m.get("vocab_size"))
+    put("d_model", t1.get("d_model"))
+    put("tier1_num_layers", t1.get("layers"))
+    put("tier1_num_heads", t1.get("heads"))
+    put("tier1_num_kv_heads", t1.get("kv_heads"))
+    put("tier1_d_ff", t1.get("d_ff"))
+    put("tier1_max_seq_len", m.get("max_seq_len"))
+    put("tier2_d_model", t2.get("d_model"))
+    put("tier2_num_layers", t2.get("layers"))
+    put("tier2_num_heads", t2.get("heads"))
+    put("tier2_d_ff", t2.get("d_ff"))
+    put("num_latent_vectors", t2.get("latent_vectors_per_chunk"))
+    put("gate1_chunk_size", t2.get("chunk_size"))
+    put("tier2_moe_num_experts", t2.get("moe_num_experts"))
+    put("tier2_moe_top_k", t2.get("moe_top_k"))
+    put("tier3_d_model", t3.get("d_model"))
+    put("tier3_num_layers", t3.get("layers"))
+    put("tier3_num_heads", t3.get("heads"))
+    put("tier3_d_ff", t3.get("d_ff"))
+    put("tier3_recurrence_steps", t3.get("recurrence_steps"))
+    put("gate1_threshold", gate.get("tier2_threshold"))
+    put("gate2_threshold", gate.get("tier3_threshold"))
+    if "dropout" in m:
+        for k in ("tier1_dropout", "tier2_dropout", "tier3_dropout"):
+            kw[k] = m["dropout"]
+    if "rope_base" in m:
+        for k in ("tier1_rope_base", "tier2_rope_base", "tier3_rope_base"):
+            kw[k] = m["rope_base"]
+    if "use_flash_attention" in m:
+        for k in ("tier1_use_flash_attention", "tier2_use_flash_attention", "tier3_use_flash_attention"):
+            kw[k] = m["use_flash_attention"]
+    return HLRTConfig(**kw)
