@@ -43,7 +43,7 @@ at::Tensor nvfp4_dequantize(const at::Tensor&, const at::Tensor&, const at::Tens
 std::tuple<at::Tensor, at::Tensor> attn_fwd(const at::Tensor&, const at::Tensor&, const at::Tensor&, bool, double);
 std::tuple<at::Tensor, at::Tensor, at::Tensor> attn_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&,
                                                         const at::Tensor&, const at::Tensor&, const at::Tensor&, bool,
-                                                        double);
+                                                        double, bool);
 // gemm_sm100.cu
 at::Tensor gemm_tn(const at::Tensor&, const at::Tensor&, at::ScalarType, double);
 void gemm_tn_accumulate(const at::Tensor&, const at::Tensor&, at::Tensor&, double);
@@ -52,6 +52,8 @@ int64_t sm100_error(int64_t);
 bool attn_sm100_supported(const at::Tensor&, const at::Tensor&, const at::Tensor&);
 std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor&, const at::Tensor&, const at::Tensor&, bool, double);
 int64_t attn_sm100_error(int64_t);
+// attention_bwd_sm100.cu
+int64_t attn_bwd_sm100_error(int64_t);
 // memory.cu
 std::tuple<at::Tensor, at::Tensor, at::Tensor> topk_softmax_gather(const at::Tensor&, const at::Tensor&, int64_t);
 }  // namespace lrb
@@ -86,5 +88,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_sm100_supported", &lrb::attn_sm100_supported);
   m.def("attn_fwd_sm100", &lrb::attn_fwd_sm100);
   m.def("attn_sm100_error", &lrb::attn_sm100_error);
+  m.def("attn_bwd_sm100_error", &lrb::attn_bwd_sm100_error);
   m.def("topk_softmax_gather", &lrb::topk_softmax_gather);
 }

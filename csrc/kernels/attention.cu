@@ -468,10 +468,16 @@ std::tuple<at::Tensor, at::Tensor> attn_fwd(const at::Tensor& q, const at::Tenso
   return {o, lse};
 }
 
+// tcgen05 backward for bf16 / head_dim 128 (attention_bwd_sm100.cu)
+void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                    const at::Tensor& lse, const at::Tensor& di, at::Tensor& dq_acc, at::Tensor& dk, at::Tensor& dv,
+                    bool causal, double scale);
+
+// `sm100`: run the tcgen05 kernel (caller checked attn_sm100_supported for q, k, v and dout)
 std::tuple<at::Tensor, at::Tensor, at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q,
                                                         const at::Tensor& k, const at::Tensor& v,
                                                         const at::Tensor& out, const at::Tensor& lse, bool causal,
-                                                        double scale) {
+                                                        double scale, bool sm100) {
   check_qkv(q, k, v);
   LRB_CHECK(dout.is_contiguous() && out.is_contiguous(), "attn_bwd: dout/out must be contiguous");
   c10::cuda::CUDAGuard g(q.device());
@@ -508,7 +514,12 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> attn_bwd(const at::Tensor& dout, 
       default: LRB_CHECK(false, "attention: unsupported head_dim");
     }
     LRB_LAUNCH_CHECK();
-    if (Sq > 0 && Skv > 0) { LRB_ATTN_DISPATCH_D((int)D, run_bwd, T, p); }
+    if (Sq > 0 && Skv > 0) {
+      if (sm100 && std::is_same<T, __nv_bfloat16>::value && D == 128)
+        attn_bwd_sm100(dout, q, k, v, lse, di, dq_acc, dk, dv, causal, scale);
+      else
+        LRB_ATTN_DISPATCH_D((int)D, run_bwd, T, p);
+    }
     const int64_t n = dq.numel();
     f32_to_kernel<T><<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 16), 256, 0, stream()>>>(
         dq_acc.data_ptr<float>(), reinterpret_cast<T*>(dq.data_ptr()), n);

@@ -1,0 +1,352 @@
+// Flash-attention backward on tcgen05 / TMEM for head_dim 128 (bf16).
+//
+// CTA = one (batch, kv-head, 128-key tile); it loops over the query heads of
+// its group and over 128-query tiles.  Per tile, five tcgen05 GEMMs:
+//   S^T  = K Q^T        (keys x queries) -> TMEM region A   [  0,128)
+//   dP^T = V dO^T       (keys x queries) -> TMEM region B   [128,256)
+//   dV  += P^T dO       (keys x hd)      -> TMEM            [256,384)  (all tiles)
+//   dK  += dS^T Q       (keys x hd)      -> TMEM            [384,512)  (all tiles)
+//   dQ   = dS K         (queries x hd)   -> TMEM region B   (after dP^T was read)
+// P^T and dS^T are written by the softmax-gradient warps to shared memory in
+// the K-major 128-byte-swizzled layout; dS (for dQ) and the Q / dO / K
+// operands of the accumulating GEMMs are read MN-major from the same tiles,
+// so nothing is transposed explicitly.  dQ is added to an fp32 buffer with
+// 16-byte vector atomics; dK and dV leave TMEM once at the end.
+//
+// Warps: 0 TMA (K, V once; Q and dO per tile), 1 TMEM owner + MMA issue,
+// 2..9 softmax-gradient (two threads per key row, 64 query columns each).
+// All waits are bounded (sm100.cuh).
+#include "../common.cuh"
+#include "sm100.cuh"
+
+namespace lrb {
+namespace {
+
+using namespace sm100;
+
+constexpr int TK = 128, TQ = 128, HD = 128;
+constexpr int kThreads = 320;
+constexpr int kSmThreads = 256;
+constexpr uint32_t kTile = 32768, kHalf = 16384;
+constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct BwdArgs {
+  const float* lse;     // (B, H, Sq) natural log
+  const float* di;      // (B, H, Sq)
+  float* dq_acc;        // (B, Sq, H, 128) fp32
+  void* dk;             // (B, Skv, Hkv, 128) bf16
+  void* dv;
+  int B, H, Hkv, Sq, Skv, causal;
+  float scale, scale_log2;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                          BwdArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sK = base;
+  unsigned char* sV = base + kTile;
+  unsigned char* sQ = base + 2 * kTile;
+  unsigned char* sdO = base + 3 * kTile;
+  unsigned char* sPt = base + 4 * kTile;
+  unsigned char* sdSt = base + 5 * kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 6 * kTile);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;
+  uint64_t* qd_free = bars + 2;
+  uint64_t* sdp_ready = bars + 3;
+  uint64_t* p_ready = bars + 4;
+  uint64_t* dq_ready = bars + 5;
+  uint64_t* b_free = bars + 6;
+  uint64_t* acc_done = bars + 7;
+  uint64_t* drain = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * TK;
+  const int b = blockIdx.y / a.Hkv, hk = blockIdx.y % a.Hkv, G = a.H / a.Hkv;
+  const int off = a.Skv - a.Sq;
+  const int q_first = a.causal ? max(0, n0 - off) : 0;
+  const int qt0 = q_first / TQ;
+  const int nqt = q_first < a.Sq ? (a.Sq + TQ - 1) / TQ - qt0 : 0;  // query tiles per head
+  const int total = nqt * G;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qd_full, 1);
+    mbar_init(qd_free, 1);
+    mbar_init(sdp_ready, 1);
+    mbar_init(p_ready, kSmThreads);
+    mbar_init(dq_ready, 1);
+    mbar_init(b_free, kSmThreads);
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmdO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tA = tmem, tB = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
+
+  if (warp == 0) {
+    if (lane == 0 && total > 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * kTile);
+      tma_load_4d(sK, &tmK, kv_full, 0, hk, n0, b);
+      tma_load_4d(sK + kHalf, &tmK, kv_full, 64, hk, n0, b);
+      tma_load_4d(sV, &tmV, kv_full, 0, hk, n0, b);
+      tma_load_4d(sV + kHalf, &tmV, kv_full, 64, hk, n0, b);
+      int loaded = 0;
+      for (int t = 0; t < total; ++t) {
+        const int h = hk * G + t / nqt;
+        const int q0 = (qt0 + t % nqt) * TQ;
+        if (!mbar_wait(qd_free, (t & 1) ^ 1, a.err, kErrTmaWait)) break;
+        mbar_arrive_expect_tx(qd_full, 2 * kTile);
+        tma_load_4d(sQ, &tmQ, qd_full, 0, h, q0, b);
+        tma_load_4d(sQ + kHalf, &tmQ, qd_full, 64, h, q0, b);
+        tma_load_4d(sdO, &tmdO, qd_full, 0, h, q0, b);
+        tma_load_4d(sdO + kHalf, &tmdO, qd_full, 64, h, q0, b);
+        ++loaded;
+      }
+      mbar_wait(kv_full, 0, nullptr, 0);
+      if (loaded > 0) mbar_wait(qd_full, (loaded - 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && total > 0) {
+      constexpr uint32_t id_kk = umma_idesc_f16_major(128, 128, true, false, false);  // both K-major
+      constexpr uint32_t id_km = umma_idesc_f16_major(128, 128, true, false, true);   // A K-major, B MN-major
+      constexpr uint32_t id_mm = umma_idesc_f16_major(128, 128, true, true, true);    // both MN-major
+      const uint32_t k_ = smem_addr(sK), v_ = smem_addr(sV), q_ = smem_addr(sQ), do_ = smem_addr(sdO);
+      const uint32_t pt_ = smem_addr(sPt), ds_ = smem_addr(sdSt);
+      bool ok = mbar_wait(kv_full, 0, a.err, kErrMmaWait);
+      for (int t = 0; t < total && ok; ++t) {
+        const uint32_t par = t & 1;
+        if (!mbar_wait(qd_full, par, a.err, kErrMmaWait)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {  // S^T = K Q^T
+          const uint32_t o = (k >> 2) * kHalf + (k & 3) * 32;
+          umma_f16(tA, umma_desc_k_sw128(k_ + o), umma_desc_k_sw128(q_ + o), id_kk, k != 0);
+        }
+        // dP^T goes to region B, which holds dQ_{t-1} until the epilogue read it.
+        if (t > 0 && !mbar_wait(b_free, par ^ 1, a.err, kErrMmaWait)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {  // dP^T = V dO^T
+          const uint32_t o = (k >> 2) * kHalf + (k & 3) * 32;
+          umma_f16(tB, umma_desc_k_sw128(v_ + o), umma_desc_k_sw128(do_ + o), id_kk, k != 0);
+        }
+        umma_commit(sdp_ready);
+        if (!mbar_wait(p_ready, par, a.err, kErrMmaWait)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < TQ / 16; ++k) {  // dV += P^T dO ; dK += dS^T Q
+          const uint32_t o = (k >> 2) * kHalf + (k & 3) * 32;
+          umma_f16(tdV, umma_desc_k_sw128(pt_ + o), umma_desc_mn_sw128(do_ + k * 2048, kHalf, 1024), id_km,
+                   (t | k) != 0);
+          umma_f16(tdK, umma_desc_k_sw128(ds_ + o), umma_desc_mn_sw128(q_ + k * 2048, kHalf, 1024), id_km,
+                   (t | k) != 0);
+        }
+#pragma unroll
+        for (int k = 0; k < TK / 16; ++k)  // dQ = dS K   (dS = (dS^T)^T read MN-major)
+          umma_f16(tB, umma_desc_mn_sw128(ds_ + k * 2048, kHalf, 1024),
+                   umma_desc_mn_sw128(k_ + k * 2048, kHalf, 1024), id_mm, k != 0);
+        umma_commit(dq_ready);
+        umma_commit(qd_free);
+      }
+      umma_commit(acc_done);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------ softmax-gradient warps
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;         // TMEM lane: key row (S^T, dP^T, dK, dV) / query row (dQ)
+    const int key = n0 + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int c0 = half * 64;
+    bool ok = true;
+    for (int t = 0; t < total && ok; ++t) {
+      const uint32_t par = t & 1;
+      const int h = hk * G + t / nqt;
+      const int q0 = (qt0 + t % nqt) * TQ;
+      if (!mbar_wait(sdp_ready, par, a.err, kErrEpiWait)) { ok = false; break; }
+      tc_fence_after();
+      float s[64], dp[64];
+      tmem_ld_32x32b_x32(tA + lane_base + c0, reinterpret_cast<uint32_t*>(s));
+      tmem_ld_32x32b_x32(tA + lane_base + c0 + 32, reinterpret_cast<uint32_t*>(s + 32));
+      tmem_ld_32x32b_x32(tB + lane_base + c0, reinterpret_cast<uint32_t*>(dp));
+      tmem_ld_32x32b_x32(tB + lane_base + c0 + 32, reinterpret_cast<uint32_t*>(dp + 32));
+      tmem_ld_wait();
+      const float* lse_row = a.lse + ((int64_t)b * a.H + h) * a.Sq;
+      const float* di_row = a.di + ((int64_t)b * a.H + h) * a.Sq;
+      uint32_t pp[32], dd[32];
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        float pv[2], dv2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int q = q0 + c0 + i + e;
+          const bool valid = q < a.Sq && key < a.Skv && (!a.causal || key <= q + off);
+          const float l2 = valid ? lse_row[q] * kLog2e : 0.f;
+          const float dd_q = valid ? di_row[q] : 0.f;
+          const float p = valid ? fast_exp2(s[i + e] * a.scale_log2 - l2) : 0.f;
+          pv[e] = p;
+          dv2[e] = p * (dp[i + e] - dd_q);
+        }
+        pp[i / 2] = pack2(pv[0], pv[1]);
+        dd[i / 2] = pack2(dv2[0], dv2[1]);
+      }
+      // this thread's 64 queries are one 64-column swizzle block of P^T / dS^T
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const uint32_t so = half * kHalf + row * 128 + ((ch ^ (row & 7)) * 16);
+        *reinterpret_cast<uint4*>(sPt + so) = make_uint4(pp[ch * 4], pp[ch * 4 + 1], pp[ch * 4 + 2], pp[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(sdSt + so) = make_uint4(dd[ch * 4], dd[ch * 4 + 1], dd[ch * 4 + 2], dd[ch * 4 + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_ready);
+      // dQ rows: TMEM lane = query row of this tile.
+      if (!mbar_wait(dq_ready, par, a.err, kErrEpiWait)) { ok = false; break; }
+      tc_fence_after();
+      const int q = q0 + row;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tB + lane_base + c0 + c * 32, r);
+        tmem_ld_wait();
+        if (q < a.Sq) {
+          float* dst = a.dq_acc + (((int64_t)b * a.Sq + q) * a.H + h) * HD + c0 + c * 32;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            atomicAdd(reinterpret_cast<float4*>(dst + e),
+                      make_float4(__uint_as_float(r[e]) * a.scale, __uint_as_float(r[e + 1]) * a.scale,
+                                  __uint_as_float(r[e + 2]) * a.scale, __uint_as_float(r[e + 3]) * a.scale));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(b_free);
+    }
+    // ---------------------------------------------------------- dK, dV
+    const bool have = __all_sync(0xffffffffu, ok && total > 0 && mbar_wait(acc_done, 0, a.err, kErrEpiWait));
+    tc_fence_after();
+    __nv_bfloat16* dkp = reinterpret_cast<__nv_bfloat16*>(a.dk) + (((int64_t)b * a.Skv + key) * a.Hkv + hk) * HD + c0;
+    __nv_bfloat16* dvp = reinterpret_cast<__nv_bfloat16*>(a.dv) + (((int64_t)b * a.Skv + key) * a.Hkv + hk) * HD + c0;
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      uint32_t rk[32], rv[32];
+      if (have) {
+        tmem_ld_32x32b_x32(tdK + lane_base + c0 + c * 32, rk);
+        tmem_ld_32x32b_x32(tdV + lane_base + c0 + c * 32, rv);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) rk[e] = rv[e] = 0u;
+      }
+      if (key >= a.Skv) continue;
+#pragma unroll
+      for (int e = 0; e < 32; e += 8) {
+        *reinterpret_cast<uint4*>(dkp + c * 32 + e) = make_uint4(
+            pack2(__uint_as_float(rk[e]) * a.scale, __uint_as_float(rk[e + 1]) * a.scale),
+            pack2(__uint_as_float(rk[e + 2]) * a.scale, __uint_as_float(rk[e + 3]) * a.scale),
+            pack2(__uint_as_float(rk[e + 4]) * a.scale, __uint_as_float(rk[e + 5]) * a.scale),
+            pack2(__uint_as_float(rk[e + 6]) * a.scale, __uint_as_float(rk[e + 7]) * a.scale));
+        *reinterpret_cast<uint4*>(dvp + c * 32 + e) = make_uint4(
+            pack2(__uint_as_float(rv[e]), __uint_as_float(rv[e + 1])),
+            pack2(__uint_as_float(rv[e + 2]), __uint_as_float(rv[e + 3])),
+            pack2(__uint_as_float(rv[e + 4]), __uint_as_float(rv[e + 5])),
+            pack2(__uint_as_float(rv[e + 6]), __uint_as_float(rv[e + 7])));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    LRB_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    LRB_CHECK(p != nullptr && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled unavailable");
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+CUtensorMap bshd_map(const at::Tensor& t) {
+  CUtensorMap m;
+  const cuuint64_t dims[4] = {(cuuint64_t)t.size(3), (cuuint64_t)t.size(2), (cuuint64_t)t.size(1),
+                              (cuuint64_t)t.size(0)};
+  const cuuint64_t strides[3] = {(cuuint64_t)t.stride(2) * 2, (cuuint64_t)t.stride(1) * 2, (cuuint64_t)t.stride(0) * 2};
+  const cuuint32_t box[4] = {64, 1, 128, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.data_ptr(), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LRB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  return m;
+}
+
+int* bwd_error_word(const at::Device& dev) {
+  static at::Tensor words[16];
+  const int idx = dev.index() < 0 ? 0 : dev.index();
+  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().device(dev).dtype(at::kInt));
+  return words[idx].data_ptr<int>();
+}
+
+}  // namespace
+
+// dK, dV (bf16) and dq_acc (fp32, must be zero-initialised; receives scale * dS K)
+void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                    const at::Tensor& lse, const at::Tensor& di, at::Tensor& dq_acc, at::Tensor& dk, at::Tensor& dv,
+                    bool causal, double scale) {
+  c10::cuda::CUDAGuard g(q.device());
+  const int64_t B = q.size(0), Sq = q.size(1), H = q.size(2), Skv = k.size(1), Hkv = k.size(2);
+  if (B * Skv * Hkv == 0) return;
+  CUtensorMap tq = bshd_map(q), tk = bshd_map(k), tv = bshd_map(v), tdo = bshd_map(dout);
+  BwdArgs args{lse.data_ptr<float>(), di.data_ptr<float>(), dq_acc.data_ptr<float>(), dk.data_ptr(), dv.data_ptr(),
+               (int)B, (int)H, (int)Hkv, (int)Sq, (int)Skv, causal ? 1 : 0, (float)scale, (float)scale * kLog2e,
+               bwd_error_word(q.device())};
+  LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+  dim3 grid((unsigned)((Skv + TK - 1) / TK), (unsigned)(B * Hkv));
+  attn_bwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, tdo, args);
+  LRB_LAUNCH_CHECK();
+}
+
+int64_t attn_bwd_sm100_error(int64_t device) {
+  int* w = bwd_error_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
+  int h = 0;
+  LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
+  return h;
+}
+
+}  // namespace lrb

@@ -11,9 +11,10 @@ sequence-parallel merging).
 
 Forward: bf16 with head_dim 128 runs the tcgen05/TMEM kernel
 (``csrc/kernels/attention_sm100.cu``); other head dims and fp16 run the
-``mma.sync`` kernel (``csrc/kernels/attention.cu``).  The backward is the
-``mma.sync`` kernel for all shapes.  ``LRB_ATTN_SM100=0`` disables the
-tcgen05 forward (for A/B comparisons).
+``mma.sync`` kernel (``csrc/kernels/attention.cu``); the backward follows
+the same split (``csrc/kernels/attention_bwd_sm100.cu`` for bf16 / 128).
+``LRB_ATTN_SM100=0`` disables the tcgen05 forward and ``LRB_ATTN_BWD_SM100=0``
+the tcgen05 backward (for A/B comparisons).
 """
 
 from __future__ import annotations
@@ -43,6 +44,7 @@ def _reference(q, k, v, causal: bool, scale: float) -> torch.Tensor:
 
 
 _USE_SM100 = os.environ.get("LRB_ATTN_SM100", "1") != "0"
+_USE_SM100_BWD = os.environ.get("LRB_ATTN_BWD_SM100", "1") != "0"
 
 
 def _forward(q, k, v, causal: bool, scale: float):
@@ -64,7 +66,10 @@ class _FlashAttnFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         q, k, v, out, lse = ctx.saved_tensors
-        dq, dk, dv = native().attn_bwd(dout.contiguous(), q, k, v, out, lse, ctx.causal, ctx.scale)
+        C = native()
+        dout = dout.contiguous()
+        sm100 = _USE_SM100_BWD and C.attn_sm100_supported(q, k, v) and C.attn_sm100_supported(dout, k, v)
+        dq, dk, dv = C.attn_bwd(dout, q, k, v, out, lse, ctx.causal, ctx.scale, sm100)
         return dq, dk, dv, None, None
 
 
