@@ -6,6 +6,12 @@
 // loop.  The weight gradient is reduced per block in shared memory and then
 // across blocks by a second tiny kernel, never with per-element atomics.
 #include "../common.cuh"
+#include "../lrb_noalloc.h"
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
 
 namespace lrb {
 namespace {
@@ -283,3 +289,104 @@ std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::T
 }
 
 }  // namespace lrb
+
+// ------------------------------------------------- allocation-free entry point
+// Variant of rmsnorm_bwd for callers that cannot allocate device memory (the
+// cases are listed in lrb_noalloc.h): the per-block weight-gradient partials go
+// to this fixed 4 MiB array instead of a freshly allocated tensor.
+static __device__ __align__(256) float g_rmsnorm_bwd_scratch[LRB_RMSNORM_BWD_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::atomic<float*> g_noalloc_scratch[kNoAllocMaxDevices];
+int g_noalloc_blocks_cap[kNoAllocMaxDevices];
+std::mutex g_noalloc_setup_mu;
+
+int noalloc_fail(char* buf, int len, int code, const char* fmt, ...) {
+  if (buf != nullptr && len > 0) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, (size_t)len, fmt, ap);
+    va_end(ap);
+  }
+  return code;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int lrb_rmsnorm_bwd_bf16_noalloc(
+    const void* dy, const void* x, const void* w, const float* rstd, const void* ds, void* dx, float* dw,
+    int64_t rows, int64_t d, void* stream, char* errbuf, int errbuf_len) {
+  using lrb::kWarps;
+  using T = __nv_bfloat16;
+  if (dy == nullptr || x == nullptr || w == nullptr || rstd == nullptr || dx == nullptr || dw == nullptr)
+    return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_ARGS, "rmsnorm_bwd_noalloc: null pointer argument");
+  if (rows <= 0 || d <= 0)
+    return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_ARGS,
+                        "rmsnorm_bwd_noalloc: rows (%lld) and d (%lld) must be positive", (long long)rows,
+                        (long long)d);
+  if (d > LRB_RMSNORM_BWD_NOALLOC_MAX_D)
+    return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_TOO_LARGE,
+                        "rmsnorm_bwd_noalloc: row width d=%lld exceeds the maximum %d", (long long)d,
+                        LRB_RMSNORM_BWD_NOALLOC_MAX_D);
+  if (!aligned16(dy) || !aligned16(x) || !aligned16(w) || !aligned16(dx) || (ds != nullptr && !aligned16(ds)))
+    return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_ARGS,
+                        "rmsnorm_bwd_noalloc: dy, x, w, ds and dx must be 16-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_CUDA, "rmsnorm_bwd_noalloc: cudaGetDevice: %s",
+                        cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_ARGS, "rmsnorm_bwd_noalloc: device %d out of range",
+                        dev);
+  const size_t smem = (size_t)kWarps * (size_t)d * sizeof(float);
+  float* scratch = g_noalloc_scratch[dev].load(std::memory_order_acquire);
+  if (scratch == nullptr) {
+    // One-time setup per device, with that device current (the caller's).
+    std::lock_guard<std::mutex> lock(g_noalloc_setup_mu);
+    scratch = g_noalloc_scratch[dev].load(std::memory_order_acquire);
+    if (scratch == nullptr) {
+      float* p = nullptr;
+      e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_rmsnorm_bwd_scratch);
+      if (e != cudaSuccess || p == nullptr)
+        return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_CUDA,
+                            "rmsnorm_bwd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      int sms = 0;
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess)
+        return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_CUDA, "rmsnorm_bwd_noalloc: SM count: %s",
+                            cudaGetErrorString(e));
+      g_noalloc_blocks_cap[dev] = 2 * sms;
+      g_noalloc_scratch[dev].store(p, std::memory_order_release);
+      scratch = p;
+    }
+  }
+  int64_t blocks = (rows + kWarps - 1) / kWarps;
+  blocks = std::min<int64_t>(blocks, g_noalloc_blocks_cap[dev]);
+  blocks = std::min<int64_t>(blocks, LRB_RMSNORM_BWD_NOALLOC_SCRATCH_FLOATS / d);
+  if (smem > 48 * 1024) {
+    // Set on every call: rmsnorm_bwd sets the same attribute for its own sizes.
+    e = cudaFuncSetAttribute(lrb::rmsnorm_bwd_kernel<T, T, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess)
+      return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_CUDA, "rmsnorm_bwd_noalloc: smem attribute: %s",
+                          cudaGetErrorString(e));
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  lrb::rmsnorm_bwd_kernel<T, T, T><<<(unsigned)blocks, kWarps * 32, smem, st>>>(
+      reinterpret_cast<const T*>(dy), reinterpret_cast<const T*>(x), reinterpret_cast<const T*>(w), rstd,
+      reinterpret_cast<const T*>(ds), reinterpret_cast<T*>(dx), scratch, rows, (int)d);
+  e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_CUDA, "rmsnorm_bwd_noalloc: launch: %s",
+                        cudaGetErrorString(e));
+  lrb::reduce_rows_kernel<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(scratch, dw, (int)blocks, (int)d);
+  e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_CUDA, "rmsnorm_bwd_noalloc: reduce launch: %s",
+                        cudaGetErrorString(e));
+  return LRB_NOALLOC_OK;
+}
