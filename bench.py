@@ -50,7 +50,8 @@ def parse_args(argv=None):
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--per-gpu-seqs", type=int, default=32)
     ap.add_argument("--micro-batch", type=int, default=8)
-    ap.add_argument("--ref-micro-batch", type=int, default=1)
+    ap.add_argument("--ref-micro-batch", type=int, default=0,
+                    help="reference micro-batch; 0 = the largest of 8/4/2/1 that fits (1 GPU), 4 on several GPUs")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--count-launches", type=int, default=1)
@@ -242,22 +243,50 @@ def run_reference(args) -> dict:
     rank = int(os.environ.get("RANK", 0))
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    micro = args.ref_micro_batch
-    accum = max(args.per_gpu_seqs // micro, 1)
     S = args.seq_len
-    torch.manual_seed(args.seed)
-    model = HLRT(cfg)
-    trainer = DistributedBootstrapTrainer(
-        model=model,
-        optimizer_cls=MuonAdamWHybrid,
-        optimizer_kwargs={"lr_muon": 0.02, "lr_adamw": 3e-4, "weight_decay_adamw": 0.01, "ns_steps": 5},
-        scheduler_cls=WSDScheduler,
-        scheduler_kwargs={"base_lr": 3e-4, "min_lr": 2e-5, "warmup_steps": 10, "total_steps": 1000},
-        tokenizer=TokenizerWrapper(backend="char"),
-        config={"gradient_accumulation_steps": accum, "max_grad_norm": 1.0},
-    )
-    g = torch.Generator().manual_seed(args.seed * 1000 + rank)
-    host = torch.randint(0, cfg.vocab_size, (accum, micro, S), generator=g, dtype=torch.int64).pin_memory()
+    if args.ref_micro_batch > 0:
+        candidates = [args.ref_micro_batch]
+    else:
+        candidates = [8, 4, 2, 1] if world == 1 else [4]
+
+    def build(micro):
+        torch.manual_seed(args.seed)
+        model = HLRT(cfg)
+        if world == 1:
+            # The stock single-GPU path has no mixed precision and the installed
+            # flash-attn accepts only fp16/bf16, so the weights are cast to bf16
+            # through the public API (the multi-GPU path is FSDP bf16).
+            model = model.to(torch.bfloat16)
+        accum = max(args.per_gpu_seqs // micro, 1)
+        trainer = DistributedBootstrapTrainer(
+            model=model,
+            optimizer_cls=MuonAdamWHybrid,
+            optimizer_kwargs={"lr_muon": 0.02, "lr_adamw": 3e-4, "weight_decay_adamw": 0.01, "ns_steps": 5},
+            scheduler_cls=WSDScheduler,
+            scheduler_kwargs={"base_lr": 3e-4, "min_lr": 2e-5, "warmup_steps": 10, "total_steps": 1000},
+            tokenizer=TokenizerWrapper(backend="char"),
+            config={"gradient_accumulation_steps": accum, "max_grad_norm": 1.0},
+        )
+        g = torch.Generator().manual_seed(args.seed * 1000 + rank)
+        host = torch.randint(0, cfg.vocab_size, (accum, micro, S), generator=g, dtype=torch.int64).pin_memory()
+        return trainer, accum, host
+
+    trainer = None
+    for i, micro in enumerate(candidates):
+        try:
+            trainer, accum, host = build(micro)
+            for j in range(accum):  # one whole optimizer step as the fit probe (extra warm-up)
+                trainer.train_step({"input_ids": host[j].to(device)})
+            torch.cuda.synchronize()
+            break
+        except torch.OutOfMemoryError:
+            trainer = None
+            import gc
+
+            gc.collect()
+            torch.cuda.empty_cache()
+            if i == len(candidates) - 1:
+                raise
     dev_batches = [host[i].to(device) for i in range(accum)]
 
     def step(batches):
@@ -302,12 +331,13 @@ def run_reference(args) -> dict:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "fp32" if world == 1 else "bf16",
+        "dtype": "bf16",
         "data": "synthetic (uniform token ids, seeded); random N(0,0.02) init",
         "impl": "reference",
         "config": {"model": MODEL_NAME, "global_batch": world * accum * micro, "seq_len": S, "micro_batch": micro,
                    "grad_accum": accum,
-                   "parallelism": f"reference stock path: {'FSDP1 FULL_SHARD bf16' if world > 1 else 'single GPU, fp32'}",
+                   "parallelism": ("reference stock path: " + ("FSDP1 FULL_SHARD bf16" if world > 1 else
+                                                              "single GPU, weights cast to bf16")),
                    "final_loss": float(loss)},
         "clocks": sampler.summary(),
         "e2e": e2e,

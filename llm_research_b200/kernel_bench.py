@@ -1,0 +1,173 @@
+"""Per-kernel microbenchmarks on one GPU.
+
+``python -m llm_research_b200.kernel_bench [names...] [--iters N] [--warmup W]``
+times each kernel with CUDA events on the launching stream (after warm-up,
+synchronised on both sides), writes a 256 MiB buffer between timed
+iterations so that every iteration starts with a cold L2, and prints one JSON
+line per case with the achieved FLOP/s or bytes/s and its fraction of the
+measured peaks in ``MEASURED_PEAKS.json`` at the repository root (the copy
+bandwidth and the cuBLAS bf16 GEMM burst rate).
+
+The same command with ``--iters 1 --warmup 1`` is the small case used for
+Nsight Compute captures of one kernel.
+
+Cases (shapes are the GENESIS-1B / 7B working shapes):
+  attn_fwd, attn_bwd     causal flash attention, B=4, S=4096, H=16, hd=128 (tcgen05)
+  attn_fwd_gqa           B=2, S=4096, H=32, Hkv=8, hd=128
+  gemm                   tcgen05 bf16 GEMM 8192x8192x8192 (TN)
+  gemm_cublas            the same shape through torch.matmul (library reference)
+  rmsnorm_fwd/bwd        32768 x 2048 bf16
+  swiglu_fwd             32768 x (2 x 5632) bf16
+  ns                     Newton-Schulz, 5 iterations, batch 8 of 2048 x 5632
+  ce                     cross-entropy fwd+bwd, 32768 x 32000 bf16 logits
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+from typing import Callable, Dict, Tuple
+
+import torch
+
+_REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _peaks() -> Dict[str, float]:
+    path = os.path.join(_REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class _Timer:
+    def __init__(self, warmup: int, iters: int) -> None:
+        self.warmup, self.iters = warmup, iters
+        self.flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+
+    def __call__(self, fn: Callable[[], None]) -> float:
+        for _ in range(self.warmup):
+            fn()
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(self.iters):
+            self.flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+        return total / self.iters
+
+
+def _attn_case(B: int, S: int, H: int, Hkv: int, bwd: bool) -> Tuple[Callable[[], None], float, float]:
+    from llm_research_b200._ext import native
+
+    C = native()
+    q = torch.randn(B, S, H, 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, S, Hkv, 128, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, S, Hkv, 128, device="cuda", dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(128)
+    flops = 4.0 * B * H * S * S * 128 / 2  # causal: half of QK^T and PV
+    if not bwd:
+        return (lambda: C.attn_fwd_sm100(q, k, v, True, scale)), flops, 0.0
+    o, lse = C.attn_fwd_sm100(q, k, v, True, scale)
+    do = torch.randn_like(o)
+    return (lambda: C.attn_bwd(do, q, k, v, o, lse, True, scale, True)), 2.5 * flops, 0.0
+
+
+def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]:
+    from llm_research_b200._ext import native
+
+    C = native()
+
+    def gemm(lib: bool):
+        n = 8192
+        a = torch.randn(n, n, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(n, n, device="cuda", dtype=torch.bfloat16)
+        if lib:
+            return (lambda: torch.matmul(a, b.t())), 2.0 * n ** 3, 0.0
+        return (lambda: C.gemm_tn(a, b, torch.bfloat16, 1.0)), 2.0 * n ** 3, 0.0
+
+    def rms(bwd: bool):
+        rows, d = 32768, 2048
+        x = torch.randn(rows, d, device="cuda", dtype=torch.bfloat16)
+        w = torch.ones(d, device="cuda", dtype=torch.bfloat16)
+        y, rstd, _ = C.rmsnorm_fwd(x, w, 1e-6, None, torch.bfloat16)
+        if not bwd:
+            return (lambda: C.rmsnorm_fwd(x, w, 1e-6, None, torch.bfloat16)), 0.0, 2.0 * x.numel() * 2
+        dy = torch.randn_like(y)
+        return (lambda: C.rmsnorm_bwd(dy, x, w, rstd, None)), 0.0, 3.0 * x.numel() * 2
+
+    def swiglu():
+        from llm_research_b200 import ops
+
+        gu = torch.randn(32768, 2 * 5632, device="cuda", dtype=torch.bfloat16)
+        return (lambda: ops.swiglu(gu)), 0.0, gu.numel() * 2 * 1.5
+
+    def ns():
+        from llm_research_b200 import ops
+
+        g = torch.randn(8, 2048, 5632, device="cuda", dtype=torch.bfloat16)
+        m, n = 2048, 5632
+        flops = 8 * 5 * (2 * m * m * n + 2 * m * m * m + 2 * m * m * n)
+        return (lambda: ops.newton_schulz(g, steps=5)), float(flops), 0.0
+
+    def ce():
+        from llm_research_b200 import ops
+
+        logits = torch.randn(32768, 32000, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        tgt = torch.randint(0, 32000, (32768,), device="cuda")
+
+        def run():
+            logits.grad = None
+            ops.cross_entropy(logits, tgt).backward()
+
+        return run, 0.0, logits.numel() * 2 * 3.0
+
+    return {
+        "attn_fwd": lambda: _attn_case(4, 4096, 16, 16, False),
+        "attn_bwd": lambda: _attn_case(4, 4096, 16, 16, True),
+        "attn_fwd_gqa": lambda: _attn_case(2, 4096, 32, 8, False),
+        "gemm": lambda: gemm(False),
+        "gemm_cublas": lambda: gemm(True),
+        "rmsnorm_fwd": lambda: rms(False),
+        "rmsnorm_bwd": lambda: rms(True),
+        "swiglu_fwd": swiglu,
+        "ns": ns,
+        "ce": ce,
+    }
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("names", nargs="*")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+    peaks = _peaks()
+    cases = _cases()
+    timer = _Timer(args.warmup, args.iters)
+    for name in args.names or list(cases):
+        fn, flops, nbytes = cases[name]()
+        ms = timer(fn)
+        rec = {"case": name, "ms": round(ms, 4)}
+        if flops:
+            tf = flops / ms / 1e9
+            rec.update(tflops=round(tf, 1), frac_of_measured_bf16=round(tf / peaks["bf16_tflops"], 3))
+        if nbytes:
+            gbs = nbytes / ms / 1e6
+            rec.update(gbs=round(gbs, 1), frac_of_measured_hbm=round(gbs / peaks["hbm_gbs"], 3))
+        rec["peaks"] = peaks["source"]
+        print(json.dumps(rec), flush=True)
+        del fn
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()
