@@ -28,7 +28,7 @@ constexpr int TK = 128, TQ = 128, HD = 128;
 constexpr int kThreads = 320;
 constexpr int kSmThreads = 256;
 constexpr uint32_t kTile = 32768, kHalf = 16384;
-constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 512;
+constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 512 + 2 * TQ * sizeof(float);
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdArgs {
@@ -70,6 +70,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_done = bars + 7;
   uint64_t* drain = bars + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  float* sL = reinterpret_cast<float*>(base + 6 * kTile + 512);  // lse * log2(e) of the tile's queries
+  float* sD = sL + TQ;                                             // D = rowsum(dO * O)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * TK;
@@ -82,7 +84,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qd_full, 1);
+    mbar_init(qd_full, 32);  // the producer warp: TMA expect-tx by lane 0, LSE/D staging by all lanes
     mbar_init(qd_free, 1);
     mbar_init(sdp_ready, 1);
     mbar_init(p_ready, kSmThreads);
@@ -107,26 +109,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tA = tmem, tB = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
 
   if (warp == 0) {
-    if (lane == 0 && total > 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * kTile);
-      tma_load_4d(sK, &tmK, kv_full, 0, hk, n0, b);
-      tma_load_4d(sK + kHalf, &tmK, kv_full, 64, hk, n0, b);
-      tma_load_4d(sV, &tmV, kv_full, 0, hk, n0, b);
-      tma_load_4d(sV + kHalf, &tmV, kv_full, 64, hk, n0, b);
+    if (total > 0) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(kv_full, 2 * kTile);
+        tma_load_4d(sK, &tmK, kv_full, 0, hk, n0, b);
+        tma_load_4d(sK + kHalf, &tmK, kv_full, 64, hk, n0, b);
+        tma_load_4d(sV, &tmV, kv_full, 0, hk, n0, b);
+        tma_load_4d(sV + kHalf, &tmV, kv_full, 64, hk, n0, b);
+      }
       int loaded = 0;
       for (int t = 0; t < total; ++t) {
         const int h = hk * G + t / nqt;
         const int q0 = (qt0 + t % nqt) * TQ;
-        if (!mbar_wait(qd_free, (t & 1) ^ 1, a.err, kErrTmaWait)) break;
-        mbar_arrive_expect_tx(qd_full, 2 * kTile);
-        tma_load_4d(sQ, &tmQ, qd_full, 0, h, q0, b);
-        tma_load_4d(sQ + kHalf, &tmQ, qd_full, 64, h, q0, b);
-        tma_load_4d(sdO, &tmdO, qd_full, 0, h, q0, b);
-        tma_load_4d(sdO + kHalf, &tmdO, qd_full, 64, h, q0, b);
+        // Q/dO and the LSE/D stage are free once the MMAs of tile t-1 that read them completed
+        // (the softmax-gradient warps finished with LSE/D before those MMAs were issued).
+        if (!__all_sync(0xffffffffu, mbar_wait(qd_free, (t & 1) ^ 1, a.err, kErrTmaWait))) break;
+        const float* lse_row = a.lse + ((int64_t)b * a.H + h) * a.Sq;
+        const float* di_row = a.di + ((int64_t)b * a.H + h) * a.Sq;
+#pragma unroll
+        for (int i = 0; i < TQ / 32; ++i) {
+          const int c = i * 32 + lane, q = q0 + c;
+          sL[c] = q < a.Sq ? lse_row[q] * kLog2e : 0.f;
+          sD[c] = q < a.Sq ? di_row[q] : 0.f;
+        }
+        // every lane arrives after its own stores (release); lane 0 also registers the TMA bytes
+        if (lane == 0) {
+          mbar_arrive_expect_tx(qd_full, 2 * kTile);
+          tma_load_4d(sQ, &tmQ, qd_full, 0, h, q0, b);
+          tma_load_4d(sQ + kHalf, &tmQ, qd_full, 64, h, q0, b);
+          tma_load_4d(sdO, &tmdO, qd_full, 0, h, q0, b);
+          tma_load_4d(sdO + kHalf, &tmdO, qd_full, 64, h, q0, b);
+        } else {
+          mbar_arrive(qd_full);
+        }
         ++loaded;
       }
-      mbar_wait(kv_full, 0, nullptr, 0);
-      if (loaded > 0) mbar_wait(qd_full, (loaded - 1) & 1, nullptr, 0);
+      if (lane == 0) {
+        mbar_wait(kv_full, 0, nullptr, 0);
+        if (loaded > 0) mbar_wait(qd_full, (loaded - 1) & 1, nullptr, 0);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && total > 0) {
@@ -164,12 +185,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16(tdK, umma_desc_k_sw128(ds_ + o), umma_desc_mn_sw128(q_ + k * 2048, kHalf, 1024), id_km,
                    (t | k) != 0);
         }
+        umma_commit(qd_free);  // Q, dO (and LSE/D) no longer needed: the next tile's loads overlap dQ
 #pragma unroll
         for (int k = 0; k < TK / 16; ++k)  // dQ = dS K   (dS = (dS^T)^T read MN-major)
           umma_f16(tB, umma_desc_mn_sw128(ds_ + k * 2048, kHalf, 1024),
                    umma_desc_mn_sw128(k_ + k * 2048, kHalf, 1024), id_mm, k != 0);
         umma_commit(dq_ready);
-        umma_commit(qd_free);
       }
       umma_commit(acc_done);
       umma_commit(drain);
@@ -188,38 +209,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int h = hk * G + t / nqt;
       const int q0 = (qt0 + t % nqt) * TQ;
       if (!mbar_wait(sdp_ready, par, a.err, kErrEpiWait)) { ok = false; break; }
+      // acquire the producer's LSE/D stores (its phase completed before the MMAs that signalled sdp_ready)
+      if (!mbar_wait(qd_full, par, a.err, kErrEpiWait)) { ok = false; break; }
       tc_fence_after();
-      float s[64], dp[64];
-      tmem_ld_32x32b_x32(tA + lane_base + c0, reinterpret_cast<uint32_t*>(s));
-      tmem_ld_32x32b_x32(tA + lane_base + c0 + 32, reinterpret_cast<uint32_t*>(s + 32));
-      tmem_ld_32x32b_x32(tB + lane_base + c0, reinterpret_cast<uint32_t*>(dp));
-      tmem_ld_32x32b_x32(tB + lane_base + c0 + 32, reinterpret_cast<uint32_t*>(dp + 32));
-      tmem_ld_wait();
-      const float* lse_row = a.lse + ((int64_t)b * a.H + h) * a.Sq;
-      const float* di_row = a.di + ((int64_t)b * a.H + h) * a.Sq;
-      uint32_t pp[32], dd[32];
+      // two passes of 32 query columns; each pass fills four 16-byte chunks of this
+      // thread's 128-byte row of the 64-column swizzle block of P^T / dS^T
+#pragma unroll 1
+      for (int pass = 0; pass < 2; ++pass) {
+        const int cb = c0 + pass * 32;
+        float s[32], dp[32];
+        tmem_ld_32x32b_x32(tA + lane_base + cb, reinterpret_cast<uint32_t*>(s));
+        tmem_ld_32x32b_x32(tB + lane_base + cb, reinterpret_cast<uint32_t*>(dp));
+        tmem_ld_wait();
+        uint32_t pp[16], dd[16];
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
-        float pv[2], dv2[2];
+        for (int i = 0; i < 32; i += 2) {
+          float pv[2], dv2[2];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int q = q0 + c0 + i + e;
-          const bool valid = q < a.Sq && key < a.Skv && (!a.causal || key <= q + off);
-          const float l2 = valid ? lse_row[q] * kLog2e : 0.f;
-          const float dd_q = valid ? di_row[q] : 0.f;
-          const float p = valid ? fast_exp2(s[i + e] * a.scale_log2 - l2) : 0.f;
-          pv[e] = p;
-          dv2[e] = p * (dp[i + e] - dd_q);
+          for (int e = 0; e < 2; ++e) {
+            const int q = q0 + cb + i + e;
+            const bool valid = q < a.Sq && key < a.Skv && (!a.causal || key <= q + off);
+            const float p = valid ? fast_exp2(s[i + e] * a.scale_log2 - sL[cb + i + e]) : 0.f;
+            pv[e] = p;
+            dv2[e] = p * (dp[i + e] - sD[cb + i + e]);
+          }
+          pp[i / 2] = pack2(pv[0], pv[1]);
+          dd[i / 2] = pack2(dv2[0], dv2[1]);
         }
-        pp[i / 2] = pack2(pv[0], pv[1]);
-        dd[i / 2] = pack2(dv2[0], dv2[1]);
-      }
-      // this thread's 64 queries are one 64-column swizzle block of P^T / dS^T
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        const uint32_t so = half * kHalf + row * 128 + ((ch ^ (row & 7)) * 16);
-        *reinterpret_cast<uint4*>(sPt + so) = make_uint4(pp[ch * 4], pp[ch * 4 + 1], pp[ch * 4 + 2], pp[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(sdSt + so) = make_uint4(dd[ch * 4], dd[ch * 4 + 1], dd[ch * 4 + 2], dd[ch * 4 + 3]);
+        for (int j = 0; j < 4; ++j) {
+          const int ch = pass * 4 + j;
+          const uint32_t so = half * kHalf + row * 128 + ((ch ^ (row & 7)) * 16);
+          *reinterpret_cast<uint4*>(sPt + so) = make_uint4(pp[j * 4], pp[j * 4 + 1], pp[j * 4 + 2], pp[j * 4 + 3]);
+          *reinterpret_cast<uint4*>(sdSt + so) = make_uint4(dd[j * 4], dd[j * 4 + 1], dd[j * 4 + 2], dd[j * 4 + 3]);
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
