@@ -101,7 +101,7 @@ def run_ours(args) -> dict:
     from olympus.data.tokenizer import TokenizerWrapper
     from olympus.distributed.fsdp_wrapper import FSDPConfig
 
-    local_rank, world, rank = init_distributed(timeout_s=900.0)
+    local_rank, world, rank = init_distributed(timeout_s=300.0)
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -237,7 +237,13 @@ def run_reference(args) -> dict:
 
     ours = build_hlrt_config(args.preset)
     fields = {k: getattr(ours, k) for k in HLRTConfig.__dataclass_fields__ if hasattr(ours, k)}
+    # The reference runs only in fp32: in bf16 its latent pooling multiplies by a
+    # float mask (genesis/model/latent_pooling.py:171) and the tier-2 linear then
+    # fails on mixed dtypes, and the installed flash-attn rejects fp32, so its
+    # own vanilla attention path is selected through the config flags.
+    fields.update(tier1_use_flash_attention=False, tier2_use_flash_attention=False, tier3_use_flash_attention=False)
     cfg = HLRTConfig(**fields)
+    from olympus.distributed.fsdp_wrapper import FSDPConfig
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     rank = int(os.environ.get("RANK", 0))
@@ -252,13 +258,10 @@ def run_reference(args) -> dict:
     def build(micro):
         torch.manual_seed(args.seed)
         model = HLRT(cfg)
-        if world == 1:
-            # The stock single-GPU path has no mixed precision and the installed
-            # flash-attn accepts only fp16/bf16, so the weights are cast to bf16
-            # through the public API (the multi-GPU path is FSDP bf16).
-            model = model.to(torch.bfloat16)
         accum = max(args.per_gpu_seqs // micro, 1)
         trainer = DistributedBootstrapTrainer(
+            fsdp_config=FSDPConfig(sharding_strategy="FULL_SHARD", mixed_precision="fp32",
+                                   activation_checkpointing=True) if world > 1 else None,
             model=model,
             optimizer_cls=MuonAdamWHybrid,
             optimizer_kwargs={"lr_muon": 0.02, "lr_adamw": 3e-4, "weight_decay_adamw": 0.01, "ns_steps": 5},
@@ -331,13 +334,13 @@ def run_reference(args) -> dict:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "fp32",
         "data": "synthetic (uniform token ids, seeded); random N(0,0.02) init",
         "impl": "reference",
         "config": {"model": MODEL_NAME, "global_batch": world * accum * micro, "seq_len": S, "micro_batch": micro,
                    "grad_accum": accum,
-                   "parallelism": ("reference stock path: " + ("FSDP1 FULL_SHARD bf16" if world > 1 else
-                                                              "single GPU, weights cast to bf16")),
+                   "parallelism": ("reference stock path, fp32, its vanilla attention: "
+                                   + ("FSDP1 FULL_SHARD" if world > 1 else "single GPU")),
                    "final_loss": float(loss)},
         "clocks": sampler.summary(),
         "e2e": e2e,

@@ -56,6 +56,22 @@ int64_t attn_sm100_error(int64_t);
 int64_t attn_bwd_sm100_error(int64_t);
 // memory.cu
 std::tuple<at::Tensor, at::Tensor, at::Tensor> topk_softmax_gather(const at::Tensor&, const at::Tensor&, int64_t);
+// comm/symm.cu
+std::tuple<int64_t, at::Tensor> symm_alloc(int64_t, int64_t);
+int64_t symm_open(const at::Tensor&, int64_t);
+void symm_close(int64_t, int64_t);
+void symm_free(int64_t, int64_t);
+at::Tensor symm_view(int64_t, int64_t, at::IntArrayRef, at::ScalarType, int64_t);
+void p2p_rs_push(at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                 at::Tensor&, at::Tensor&);
+void p2p_rs_reduce(const at::Tensor&, at::Tensor&, int64_t, double, bool, const at::Tensor&, at::Tensor&, int64_t,
+                   c10::optional<at::Tensor>, at::Tensor&, at::Tensor&);
+void p2p_ag_publish(const at::Tensor&, at::Tensor&, at::Tensor&, int64_t, at::Tensor&);
+void p2p_pull(at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int64_t, at::Tensor&);
+void diloco_push(const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int64_t, int64_t,
+                 int64_t, at::Tensor&, at::Tensor&);
+void diloco_reduce_nesterov(const at::Tensor&, at::Tensor&, at::Tensor&, at::Tensor&, int64_t, double, double,
+                            const at::Tensor&, at::Tensor&, at::Tensor&, int64_t, at::Tensor&, at::Tensor&);
 }  // namespace lrb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -90,4 +106,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_sm100_error", &lrb::attn_sm100_error);
   m.def("attn_bwd_sm100_error", &lrb::attn_bwd_sm100_error);
   m.def("topk_softmax_gather", &lrb::topk_softmax_gather);
+  m.def("symm_alloc", &lrb::symm_alloc);
+  m.def("symm_open", &lrb::symm_open);
+  m.def("symm_close", &lrb::symm_close);
+  m.def("symm_free", &lrb::symm_free);
+  m.def("symm_view", &lrb::symm_view);
+  m.def("p2p_rs_push", &lrb::p2p_rs_push);
+  m.def("p2p_rs_reduce", &lrb::p2p_rs_reduce);
+  m.def("p2p_ag_publish", &lrb::p2p_ag_publish);
+  m.def("p2p_pull", &lrb::p2p_pull);
+  m.def("diloco_push", &lrb::diloco_push);
+  m.def("diloco_reduce_nesterov", &lrb::diloco_reduce_nesterov);
 }

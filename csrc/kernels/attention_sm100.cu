@@ -24,6 +24,8 @@
 #include "../common.cuh"
 #include "sm100.cuh"
 
+#include <cstdlib>
+
 namespace lrb {
 namespace {
 
@@ -317,6 +319,302 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// --------------------------------------------------- two Q tiles per CTA
+// CTA = (batch, head, 256 queries as tiles A and B); 10 warps:
+//   warp 0      TMA: Q_A, Q_B once; K_j, V_j (128 keys) into 2-stage rings;
+//   warp 1      TMEM owner + MMA issue.  TMEM columns: S_A [0,128), S_B
+//               [128,256), O_A [256,384), O_B [384,512).  P_X overwrites the
+//               first 64 columns of S_X as packed bf16 and is the A operand of
+//               P_X V_j straight from tensor memory.  Issue order
+//                 S_A(j) S_B(j) | PV_A(j) S_A(j+1) | PV_B(j) S_B(j+1) | ...
+//               so each tile's softmax runs while the other tile's MMAs do;
+//               the MMAs of one CTA execute in issue order, which makes it
+//               safe for S_X(j+1) to overwrite P_X(j) after PV_X(j).
+//   warps 2..5  softmax of tile A, warps 6..9 tile B: one thread per query
+//               row (its TMEM lane), 128 key columns per thread, running max
+//               and sum in the exp2 domain, lazy O rescale (threshold 2^8).
+// s_full_X(j) is committed after PV_X(j-1), so a softmax thread that sees it
+// may also rewrite O_X.  All waits are bounded (sm100.cuh).
+namespace fwd2 {
+constexpr int kThreads = 320;
+constexpr int kRowThreads = 128;
+constexpr size_t kSmem = 1024 + 6 * (size_t)kTileBytes + 256;
+}  // namespace fwd2
+
+__global__ void __launch_bounds__(fwd2::kThreads, 1)
+    attn_fwd_2q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, FwdArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sQ = base;                    // Q_A, Q_B
+  unsigned char* sK = base + 2 * kTileBytes;   // 2 stages
+  unsigned char* sV = base + 4 * kTileBytes;   // 2 stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 6 * kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* v_full = bars + 3;   // [2]
+  uint64_t* k_free = bars + 5;   // [2]
+  uint64_t* v_free = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;   // [tile]
+  uint64_t* p_full = bars + 11;  // [tile]
+  uint64_t* o_done = bars + 13;  // [tile]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = (gridDim.x - 1 - blockIdx.x) * 2 * TQ;  // heavy (late) causal tiles first
+  const int b = blockIdx.y / a.H, h = blockIdx.y % a.H, hk = h / (a.H / a.Hkv);
+  const int off = a.Skv - a.Sq;
+  int nt[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int mx0 = m0 + x * TQ;
+    int kv_end = a.Skv;
+    if (a.causal) kv_end = min(kv_end, mx0 + TQ + off);
+    nt[x] = (mx0 < a.Sq && kv_end > 0) ? (kv_end + TK - 1) / TK : 0;
+  }
+  const int ntl = max(nt[0], nt[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&k_free[i], 1);
+      mbar_init(&v_free[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], fwd2::kRowThreads);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && ntl > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+      tma_load_4d(sQ, &tmQ, q_full, 0, h, m0, b);
+      tma_load_4d(sQ + kHalf, &tmQ, q_full, 64, h, m0, b);
+      tma_load_4d(sQ + kTileBytes, &tmQ, q_full, 0, h, m0 + TQ, b);
+      tma_load_4d(sQ + kTileBytes + kHalf, &tmQ, q_full, 64, h, m0 + TQ, b);
+      int armed_k = 0, armed_v = 0;
+      for (int j = 0; j < ntl; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_free[st], ph ^ 1, a.err, kErrTmaWait)) break;
+        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+        tma_load_4d(sK + st * kTileBytes, &tmK, &k_full[st], 0, hk, j * TK, b);
+        tma_load_4d(sK + st * kTileBytes + kHalf, &tmK, &k_full[st], 64, hk, j * TK, b);
+        ++armed_k;
+        if (!mbar_wait(&v_free[st], ph ^ 1, a.err, kErrTmaWait)) break;
+        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+        tma_load_4d(sV + st * kTileBytes, &tmV, &v_full[st], 0, hk, j * TK, b);
+        tma_load_4d(sV + st * kTileBytes + kHalf, &tmV, &v_full[st], 64, hk, j * TK, b);
+        ++armed_v;
+      }
+      mbar_wait(q_full, 0, nullptr, 0);
+      for (int i = 1; i <= 2 && i <= armed_k; ++i) mbar_wait(&k_full[(armed_k - i) & 1], ((armed_k - i) >> 1) & 1, nullptr, 0);
+      for (int i = 1; i <= 2 && i <= armed_v; ++i) mbar_wait(&v_full[(armed_v - i) & 1], ((armed_v - i) >> 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && ntl > 0) {
+      constexpr uint32_t idesc_qk = umma_idesc_f16_major(TQ, TK, true, false, false);
+      constexpr uint32_t idesc_pv = umma_idesc_f16_major(TQ, HD, true, false, true);
+      const uint32_t q_addr[2] = {smem_addr(sQ), smem_addr(sQ + kTileBytes)};
+      auto issue_s = [&](int x, int j) {
+        const uint32_t k0 = smem_addr(sK + (j & 1) * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t o = (k >> 2) * kHalf + (k & 3) * 32;
+          umma_f16(tmem + x * TQ, umma_desc_k_sw128(q_addr[x] + o), umma_desc_k_sw128(k0 + o), idesc_qk, k != 0);
+        }
+        umma_commit(&s_full[x]);
+      };
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t v0 = smem_addr(sV + (j & 1) * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < TK / 16; ++k)  // 16 keys = 8 columns of packed P
+          umma_f16_tmem_a(tmem + 256 + x * HD, tmem + x * TQ + k * 8, umma_desc_mn_sw128(v0 + k * 16 * 128, kHalf, 1024),
+                          idesc_pv, (j | k) != 0);
+        if (j == nt[x] - 1) umma_commit(&o_done[x]);
+      };
+      bool ok = mbar_wait(q_full, 0, a.err, kErrMmaWait) && mbar_wait(&k_full[0], 0, a.err, kErrMmaWait);
+      if (ok) {
+        tc_fence_after();
+        if (nt[0] > 0) issue_s(0, 0);
+        if (nt[1] > 0) issue_s(1, 0);
+        umma_commit(&k_free[0]);
+      }
+      for (int j = 0; j < ntl && ok; ++j) {
+        const int st = j & 1, nst = (j + 1) & 1;
+        const uint32_t ph = (j >> 1) & 1, nph = ((j + 1) >> 1) & 1;
+        const bool next = j + 1 < ntl;
+        if (!mbar_wait(&v_full[st], ph, a.err, kErrMmaWait)) break;
+        if (j < nt[0]) {
+          if (!mbar_wait(&p_full[0], j & 1, a.err, kErrMmaWait)) break;
+          tc_fence_after();
+          issue_pv(0, j);
+        }
+        if (next) {
+          if (!mbar_wait(&k_full[nst], nph, a.err, kErrMmaWait)) break;
+          tc_fence_after();
+        }
+        if (j + 1 < nt[0]) issue_s(0, j + 1);
+        if (j < nt[1]) {
+          if (!mbar_wait(&p_full[1], j & 1, a.err, kErrMmaWait)) break;
+          tc_fence_after();
+          issue_pv(1, j);
+        }
+        umma_commit(&v_free[st]);
+        if (j + 1 < nt[1]) issue_s(1, j + 1);
+        if (next) umma_commit(&k_free[nst]);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    // ---------------------------------------------------------- softmax
+    const int x = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int mx0 = m0 + x * TQ;
+    const int qrow = mx0 + r;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_base + x * TQ;
+    const uint32_t tO = tmem + lane_base + 256 + x * HD;
+    const int n = nt[x];
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n && ok; ++j) {
+      if (!mbar_wait(&s_full[x], j & 1, a.err, kErrEpiWait)) { ok = false; break; }
+      tc_fence_after();
+      // Keys 64..127 stay in registers; keys 0..63 are read twice (max pass,
+      // then exp pass) so no more than 64 S values are live.  P(keys 2i, 2i+1)
+      // lands in column i of S_X, so writing P for keys 0..31 only overwrites
+      // columns already consumed, and keys 32..63 are re-read before that.
+      const bool edge = (j * TK + TK > a.Skv) || (a.causal && j * TK + TK - 1 > mx0 + off);
+      auto scaled = [&](float v, int key) -> float {
+        v *= a.scale_log2;
+        if (edge && (key >= a.Skv || (a.causal && key > qrow + off))) v = -INFINITY;
+        return v;
+      };
+      float mx = -INFINITY;
+      {
+        float t[64];
+        tmem_ld_32x32b_x32(tS, reinterpret_cast<uint32_t*>(t));
+        tmem_ld_32x32b_x32(tS + 32, reinterpret_cast<uint32_t*>(t + 32));
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, scaled(t[i], j * TK + i));
+      }
+      float hi[64];
+      tmem_ld_32x32b_x32(tS + 64, reinterpret_cast<uint32_t*>(hi));
+      tmem_ld_32x32b_x32(tS + 96, reinterpret_cast<uint32_t*>(hi + 32));
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        hi[i] = scaled(hi[i], j * TK + 64 + i);
+        mx = fmaxf(mx, hi[i]);
+      }
+      float alpha = 1.f;
+      if (mx > m_run + kRescaleThreshold || m_run == -INFINITY) {
+        const float m_new = fmaxf(m_run, mx);
+        alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+        m_run = m_new;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {  // keys 0..63, re-read
+        float lo[32];
+        tmem_ld_32x32b_x32(tS + c * 32, reinterpret_cast<uint32_t*>(lo));
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = fast_exp2(scaled(lo[2 * i], j * TK + c * 32 + 2 * i) - m_use);
+          const float p1 = fast_exp2(scaled(lo[2 * i + 1], j * TK + c * 32 + 2 * i + 1) - m_use);
+          sum += p0 + p1;
+          pk[i] = pack_bf16(p0, p1);
+        }
+        tmem_st_32x32b_x16(tS + c * 16, pk);
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {  // keys 64..127, from registers
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = fast_exp2(hi[c * 32 + 2 * i] - m_use), p1 = fast_exp2(hi[c * 32 + 2 * i + 1] - m_use);
+          sum += p0 + p1;
+          pk[i] = pack_bf16(p0, p1);
+        }
+        tmem_st_32x32b_x16(tS + 32 + c * 16, pk);
+      }
+      l_run = l_run * alpha + sum;
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(tO + c * 32, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[x]);
+    }
+    // ---------------------------------------------------------- epilogue
+    const bool have = ok && n > 0 && mbar_wait(&o_done[x], 0, a.err, kErrEpiWait);
+    tc_fence_after();
+    const bool have_w = __all_sync(0xffffffffu, have);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + (((int64_t)b * a.Sq + qrow) * a.H + h) * HD;
+    const float inv = (have_w && l_run > 0.f) ? 1.f / l_run : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[32];
+      if (have_w) {
+        tmem_ld_32x32b_x32(tO + c * 32, o);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = 0u;
+      }
+      if (qrow >= a.Sq) continue;
+#pragma unroll
+      for (int e = 0; e < 32; e += 8) {
+        uint4 v = make_uint4(pack_bf16(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
+                             pack_bf16(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
+                             pack_bf16(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
+                             pack_bf16(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
+        *reinterpret_cast<uint4*>(dst + c * 32 + e) = v;
+      }
+    }
+    if (qrow < a.Sq)
+      a.lse[((int64_t)b * a.H + h) * a.Sq + qrow] =
+          (have_w && l_run > 0.f) ? (m_run == -INFINITY ? 0.f : m_run) * kLn2 + __logf(l_run) : INFINITY;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ------------------------------------------------------------------ host
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -378,9 +676,20 @@ std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor& q, const at:
   CUtensorMap tq = make_bshd_map(q), tk = make_bshd_map(k), tv = make_bshd_map(v);
   FwdArgs args{o.data_ptr(), lse.data_ptr<float>(), (int)B, (int)H, (int)Hkv, (int)Sq, (int)Skv, causal ? 1 : 0,
                (float)scale * kLog2e, attn_error_word(q.device())};
-  LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-  dim3 grid((unsigned)((Sq + TQ - 1) / TQ), (unsigned)(B * H));
-  attn_fwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, args);
+  static const bool two_tiles = [] {
+    const char* e = std::getenv("LRB_ATTN_FWD_TWO_TILES");
+    return e != nullptr && e[0] == '1';
+  }();
+  if (!two_tiles) {  // one Q tile per CTA, P through shared memory (the faster variant today)
+    LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+    dim3 grid((unsigned)((Sq + TQ - 1) / TQ), (unsigned)(B * H));
+    attn_fwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, args);
+  } else {
+    LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_2q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)fwd2::kSmem));
+    dim3 grid((unsigned)((Sq + 2 * TQ - 1) / (2 * TQ)), (unsigned)(B * H));
+    attn_fwd_2q_kernel<<<grid, fwd2::kThreads, fwd2::kSmem, stream()>>>(tq, tk, tv, args);
+  }
   LRB_LAUNCH_CHECK();
   return {o, lse};
 }

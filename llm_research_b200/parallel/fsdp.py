@@ -27,6 +27,23 @@ FSDP1 flattening routes every parameter to AdamW
 
 With ``world_size == 1`` the same code runs without collectives: the master
 buffer is the whole model and ``refresh`` casts it into the compute buffer.
+
+Collectives.  ``comm="nccl"`` issues NCCL all-gather / reduce-scatter on the
+communication stream (the baseline).  ``comm="p2p"`` (one node) runs the
+framework's own kernels on symmetric memory (:mod:`llm_research_b200.parallel.symm`):
+
+* reduce-scatter = ``p2p_rs_push`` (each rank casts its fp32 accumulator to
+  bf16, stores every owner's slice into that owner's receive slot over NVLink
+  and zeroes the accumulator in the same pass) + ``p2p_rs_reduce`` (the owner
+  sums the slots in fp32, scales by 1/world, writes the shard and adds the
+  sum of squares used by gradient clipping -- no separate norm pass);
+* all-gather = ``p2p_ag_publish`` (the optimizer's fp32 master shard is cast
+  to bf16 straight into the heap) + ``p2p_pull`` (each rank reads all shards).
+
+Ordering argument for reusing the heap shard: a rank republishes a unit's
+shard only after its reduce of that unit, which waited for every peer's push
+of the unit, and each peer pushes only after its backward of the unit, which
+came after its last pull of the unit.
 """
 
 from __future__ import annotations
@@ -43,6 +60,12 @@ import torch.nn as nn
 from llm_research_b200 import ops
 
 ALIGN = 8  # elements; keeps every bf16 view 16-byte aligned
+
+
+def ops_native():
+    from llm_research_b200._ext import native
+
+    return native()
 
 
 def _round_up(x: int, m: int) -> int:
@@ -116,6 +139,7 @@ class FlatShardEngine(nn.Module):
         unit_classes: Optional[Sequence[Type[nn.Module]]] = None,
         device: Optional[torch.device] = None,
         reduce_dtype: torch.dtype = torch.float32,
+        comm: Optional[str] = None,
     ) -> None:
         super().__init__()
         self.module = module
@@ -135,6 +159,18 @@ class FlatShardEngine(nn.Module):
         classes = tuple(unit_classes) if unit_classes is not None else default_unit_classes()
         self._build_units(classes)
         self._register_hooks()
+        import os
+
+        self.comm = (comm or os.environ.get("LRB_FSDP_COMM", "nccl")).lower()
+        self.heap = None
+        self._sumsq: Optional[torch.Tensor] = None
+        if self.comm == "p2p":
+            from llm_research_b200.parallel.symm import single_node
+
+            if not (self.world > 1 and self.device.type == "cuda" and single_node(self.pg)):
+                self.comm = "nccl"
+            else:
+                self._setup_p2p()
 
     # ------------------------------------------------------------------ layout
     def _build_units(self, classes: Tuple[Type[nn.Module], ...]) -> None:
@@ -198,6 +234,45 @@ class FlatShardEngine(nn.Module):
             del full
         self.unit_order = [u.index for u in self.units[1:]]
 
+    # ------------------------------------------------------------ p2p comm
+    def _setup_p2p(self) -> None:
+        from llm_research_b200.parallel.symm import SymmetricHeap
+
+        W = self.world
+        need = 0
+        for u in self.units:
+            need += _round_up(W * u.shard * 2, 256) + 256 * 4 + _round_up(u.shard * 2, 256)
+        self.heap = heap = SymmetricHeap(need + (1 << 20), group=self.pg, device=self.device)
+        for u in self.units:
+            u.recv_off = heap.alloc(W * u.shard * 2)
+            u.ready_off = heap.alloc(4 * W)
+            u.consumed_off = heap.alloc(4)
+            u.ag_off = heap.alloc(u.shard * 2)
+            u.agready_off = heap.alloc(4)
+            u.recv = heap.view(u.recv_off, (W * u.shard,), torch.bfloat16)
+            u.ready = heap.view(u.ready_off, (W,), torch.int32)
+            u.consumed = heap.view(u.consumed_off, (1,), torch.int32)
+            u.agready = heap.view(u.agready_off, (1,), torch.int32)
+            u.compute_shard = heap.view(u.ag_off, (u.shard,), torch.bfloat16)
+            u.counters = torch.zeros(4, dtype=torch.int32, device=self.device)
+            u.rs_epoch = 0
+        self._sumsq = torch.zeros((), dtype=torch.float32, device=self.device)
+        self._ag_epoch = 0
+        dist.barrier(group=self.pg)  # every heap is zeroed before anyone publishes
+        self._publish()
+
+    def _publish(self) -> None:
+        C = ops_native()
+        self._ag_epoch += 1
+        for u in self.units:
+            C.p2p_ag_publish(u.master, u.compute_shard, u.agready, self._ag_epoch, u.counters[2:3])
+
+    def close(self) -> None:
+        """Release the symmetric heap (collective)."""
+        if self.heap is not None:
+            self.heap.close()
+            self.heap = None
+
     # --------------------------------------------------------------- gathers
     def _free(self, u: Unit) -> None:
         if self.world > 1 and u.compute.untyped_storage().size() > 0:
@@ -221,7 +296,11 @@ class FlatShardEngine(nn.Module):
             cur = torch.cuda.current_stream(self.device)
             self.comm_stream.wait_stream(cur)
             with torch.cuda.stream(self.comm_stream):
-                dist.all_gather_into_tensor(u.writer, u.compute_shard, group=self.pg)
+                if self.heap is not None:
+                    ops_native().p2p_pull(u.writer, self.heap.bases, u.ag_off, u.agready_off, self.world,
+                                          self._ag_epoch, self.heap.err)
+                else:
+                    dist.all_gather_into_tensor(u.writer, u.compute_shard, group=self.pg)
                 ev = torch.cuda.Event()
                 ev.record(self.comm_stream)
             u.gather_event = ev
@@ -305,6 +384,18 @@ class FlatShardEngine(nn.Module):
             return
         cur = torch.cuda.current_stream(self.device)
         self.comm_stream.wait_stream(cur)
+        if self.heap is not None:
+            C = ops_native()
+            u.rs_epoch += 1
+            with torch.cuda.stream(self.comm_stream):
+                C.p2p_rs_push(u.grad_acc, self.heap.bases, u.recv_off, u.ready_off, u.consumed_off, self.rank,
+                              self.world, u.shard, u.rs_epoch, u.counters[0:1], self.heap.err)
+                C.p2p_rs_reduce(u.recv, u.grad_shard, self.world, 1.0 / self.world, False, u.ready, u.consumed,
+                                u.rs_epoch, self._sumsq, u.counters[1:2], self.heap.err)
+                ev = torch.cuda.Event()
+                ev.record(self.comm_stream)
+            u.rs_event = ev
+            return
         with torch.cuda.stream(self.comm_stream):
             src = u.grad_acc if self.reduce_dtype == torch.float32 else u.grad_acc.to(self.reduce_dtype)
             out = u.grad_shard if self.reduce_dtype == torch.float32 else torch.empty(u.shard, dtype=self.reduce_dtype, device=self.device)
@@ -375,9 +466,12 @@ class FlatShardEngine(nn.Module):
     @torch.no_grad()
     def clip_grad_norm_(self, max_norm: float, norm_type: float = 2.0) -> torch.Tensor:
         self.wait_grads()
-        sq = torch.zeros((), dtype=torch.float32, device=self.device)
-        for u in self.units:
-            sq += u.grad_shard.float().pow(2).sum()
+        if self.heap is not None:
+            sq = self._sumsq.clone()  # accumulated by the reduce kernels
+        else:
+            sq = torch.zeros((), dtype=torch.float32, device=self.device)
+            for u in self.units:
+                sq += u.grad_shard.float().pow(2).sum()
         if self.world > 1:
             dist.all_reduce(sq, group=self.pg)
         norm = sq.sqrt()
@@ -389,6 +483,12 @@ class FlatShardEngine(nn.Module):
     @torch.no_grad()
     def refresh(self) -> None:
         """Propagate updated master weights to the compute copies."""
+        if self.heap is not None:
+            self.heap.poll_error()
+            self._publish()
+            for u in self.units:
+                self._free(u)
+            return
         for u in self.units:
             if self.world == 1:
                 u.writer.copy_(u.master)
@@ -409,6 +509,8 @@ class FlatShardEngine(nn.Module):
     @torch.no_grad()
     def zero_grad(self) -> None:
         self._touched.clear()
+        if self._sumsq is not None:
+            self._sumsq.zero_()
         for u in self.units:
             if self.world > 1:
                 u.grad_shard.zero_()

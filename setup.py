@@ -42,7 +42,7 @@ def extensions():
     return [
         CUDAExtension(
             name="llm_research_b200._C",
-            sources=sources("csrc/bindings.cpp", "csrc/kernels/*.cu"),
+            sources=sources("csrc/bindings.cpp", "csrc/kernels/*.cu", "csrc/comm/*.cu"),
             include_dirs=[os.path.join(ROOT, "csrc")],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
         ),

@@ -1,4 +1,5 @@
-"""Run a function on ``world`` CPU ranks (gloo) and collect the per-rank results."""
+"""Run a function on ``world`` ranks (gloo on CPU, or NCCL with one GPU per
+rank) and collect the per-rank results."""
 
 from __future__ import annotations
 
@@ -17,13 +18,20 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _entry(rank: int, world: int, port: int, fn: Callable, args: tuple, outdir: str) -> None:
+def _entry(rank: int, world: int, port: int, fn: Callable, args: tuple, outdir: str, backend: str = "gloo") -> None:
+    import datetime
+
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank))
+                      LOCAL_RANK=str(rank), LOCAL_WORLD_SIZE=str(world))
     torch.set_num_threads(2)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    if backend == "nccl":
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", rank))
+    else:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         res = fn(rank, world, *args)
         torch.save(res, os.path.join(outdir, f"r{rank}.pt"))
@@ -31,7 +39,7 @@ def _entry(rank: int, world: int, port: int, fn: Callable, args: tuple, outdir: 
         dist.destroy_process_group()
 
 
-def run_ranks(fn: Callable, world: int, *args: Any) -> List[Any]:
+def run_ranks(fn: Callable, world: int, *args: Any, backend: str = "gloo") -> List[Any]:
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_entry, args=(world, free_port(), fn, args, d), nprocs=world, join=True)
+        mp.spawn(_entry, args=(world, free_port(), fn, args, d, backend), nprocs=world, join=True)
         return [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(world)]
