@@ -11,6 +11,8 @@ tier_escalate, trace_start/end) get ids ``base + i`` for the BPE backends and
 
 from __future__ import annotations
 
+import os
+
 import logging
 from typing import Dict, List, Optional
 
@@ -75,6 +77,23 @@ class _CharLevelBackend:
         return None if tok is None else self._special_to_id.get(tok)
 
 
+class _LocalTiktoken:
+    """The subset of ``tiktoken.Encoding`` the wrapper uses, over :class:`olympus.data.bpe.BytePairEncoder`."""
+
+    def __init__(self, enc) -> None:
+        self._enc = enc
+        self.n_vocab = enc.n_vocab
+
+    def encode_ordinary(self, text: str):
+        return self._enc.encode_ordinary(text)
+
+    def encode(self, text: str, **_):
+        return self._enc.encode_ordinary(text)
+
+    def decode(self, ids):
+        return self._enc.decode(ids)
+
+
 class TokenizerWrapper:
     def __init__(self, backend: str = "tiktoken", vocab_size: int = 100287, sp_model_path: Optional[str] = None) -> None:
         self._backend_name = "none"
@@ -90,7 +109,15 @@ class TokenizerWrapper:
                 self._vocab_size = self._tiktoken_enc.n_vocab + len(SPECIAL_TOKENS)
                 self._backend_name = "tiktoken"
             except Exception:
-                logger.info("tiktoken cl100k_base unavailable; trying sentencepiece")
+                path = os.environ.get("LRB_TIKTOKEN_FILE")
+                if path and os.path.exists(path):  # local cl100k_base.tiktoken, no tiktoken package
+                    from olympus.data.bpe import BytePairEncoder
+
+                    self._tiktoken_enc = _LocalTiktoken(BytePairEncoder.from_file(path))
+                    self._vocab_size = self._tiktoken_enc.n_vocab + len(SPECIAL_TOKENS)
+                    self._backend_name = "tiktoken"
+                else:
+                    logger.info("tiktoken cl100k_base unavailable; trying sentencepiece")
         if self._backend_name == "none" and backend in ("sentencepiece", "tiktoken", "auto") and sp_model_path:
             try:
                 import sentencepiece as spm  # type: ignore
