@@ -503,20 +503,22 @@ __global__ void __launch_bounds__(fwd2::kThreads, 1)
       // then exp pass) so no more than 64 S values are live.  P(keys 2i, 2i+1)
       // lands in column i of S_X, so writing P for keys 0..31 only overwrites
       // columns already consumed, and keys 32..63 are re-read before that.
+      // Maxima and sums use 8 independent accumulators (short dependency
+      // chains); the exponent is one FFMA on the raw score: s*c - m.
       const bool edge = (j * TK + TK > a.Skv) || (a.causal && j * TK + TK - 1 > mx0 + off);
-      auto scaled = [&](float v, int key) -> float {
-        v *= a.scale_log2;
-        if (edge && (key >= a.Skv || (a.causal && key > qrow + off))) v = -INFINITY;
-        return v;
-      };
-      float mx = -INFINITY;
+      const int lim = a.causal ? min(a.Skv, qrow + off + 1) : a.Skv;  // keys >= lim are masked
+      const float c = a.scale_log2;
+      auto masked = [&](float v, int key) -> float { return (edge && key >= lim) ? -INFINITY : v; };
+      float pm[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pm[e] = -INFINITY;
       {
         float t[64];
         tmem_ld_32x32b_x32(tS, reinterpret_cast<uint32_t*>(t));
         tmem_ld_32x32b_x32(tS + 32, reinterpret_cast<uint32_t*>(t + 32));
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, scaled(t[i], j * TK + i));
+        for (int i = 0; i < 64; ++i) pm[i & 7] = fmaxf(pm[i & 7], masked(t[i], j * TK + i));
       }
       float hi[64];
       tmem_ld_32x32b_x32(tS + 64, reinterpret_cast<uint32_t*>(hi));
@@ -524,43 +526,52 @@ __global__ void __launch_bounds__(fwd2::kThreads, 1)
       tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
-        hi[i] = scaled(hi[i], j * TK + 64 + i);
-        mx = fmaxf(mx, hi[i]);
+        hi[i] = masked(hi[i], j * TK + 64 + i);
+        pm[i & 7] = fmaxf(pm[i & 7], hi[i]);
       }
+      const float mraw = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      const float mx = mraw * c;  // c > 0: the max of the scaled scores
       float alpha = 1.f;
       if (mx > m_run + kRescaleThreshold || m_run == -INFINITY) {
         const float m_new = fmaxf(m_run, mx);
         alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
         m_run = m_new;
       }
-      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      float sum = 0.f;
+      const float nm = (m_run == -INFINITY) ? 0.f : -m_run;
+      float ps[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ps[e] = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {  // keys 0..63, re-read
+      for (int cc = 0; cc < 2; ++cc) {  // keys 0..63, re-read
         float lo[32];
-        tmem_ld_32x32b_x32(tS + c * 32, reinterpret_cast<uint32_t*>(lo));
+        tmem_ld_32x32b_x32(tS + cc * 32, reinterpret_cast<uint32_t*>(lo));
         tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = fast_exp2(scaled(lo[2 * i], j * TK + c * 32 + 2 * i) - m_use);
-          const float p1 = fast_exp2(scaled(lo[2 * i + 1], j * TK + c * 32 + 2 * i + 1) - m_use);
-          sum += p0 + p1;
+          const float p0 = fast_exp2(fmaf(masked(lo[2 * i], j * TK + cc * 32 + 2 * i), c, nm));
+          const float p1 = fast_exp2(fmaf(masked(lo[2 * i + 1], j * TK + cc * 32 + 2 * i + 1), c, nm));
+          ps[(2 * i) & 7] += p0;
+          ps[(2 * i + 1) & 7] += p1;
           pk[i] = pack_bf16(p0, p1);
         }
-        tmem_st_32x32b_x16(tS + c * 16, pk);
+        tmem_st_32x32b_x16(tS + cc * 16, pk);
       }
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {  // keys 64..127, from registers
+      for (int cc = 0; cc < 2; ++cc) {  // keys 64..127, from registers
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = fast_exp2(hi[c * 32 + 2 * i] - m_use), p1 = fast_exp2(hi[c * 32 + 2 * i + 1] - m_use);
-          sum += p0 + p1;
+          const float p0 = fast_exp2(fmaf(hi[cc * 32 + 2 * i], c, nm));
+          const float p1 = fast_exp2(fmaf(hi[cc * 32 + 2 * i + 1], c, nm));
+          ps[(2 * i) & 7] += p0;
+          ps[(2 * i + 1) & 7] += p1;
           pk[i] = pack_bf16(p0, p1);
         }
-        tmem_st_32x32b_x16(tS + 32 + c * 16, pk);
+        tmem_st_32x32b_x16(tS + 32 + cc * 16, pk);
       }
+      const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       l_run = l_run * alpha + sum;
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
@@ -676,11 +687,11 @@ std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor& q, const at:
   CUtensorMap tq = make_bshd_map(q), tk = make_bshd_map(k), tv = make_bshd_map(v);
   FwdArgs args{o.data_ptr(), lse.data_ptr<float>(), (int)B, (int)H, (int)Hkv, (int)Sq, (int)Skv, causal ? 1 : 0,
                (float)scale * kLog2e, attn_error_word(q.device())};
-  static const bool two_tiles = [] {
-    const char* e = std::getenv("LRB_ATTN_FWD_TWO_TILES");
+  static const bool one_tile = [] {
+    const char* e = std::getenv("LRB_ATTN_FWD_ONE_TILE");
     return e != nullptr && e[0] == '1';
   }();
-  if (!two_tiles) {  // one Q tile per CTA, P through shared memory (the faster variant today)
+  if (one_tile) {  // one Q tile per CTA, P through shared memory (kept for A/B comparisons)
     LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
     dim3 grid((unsigned)((Sq + TQ - 1) / TQ), (unsigned)(B * H));
     attn_fwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, args);

@@ -14,7 +14,9 @@ Forward: bf16 with head_dim 128 runs the tcgen05/TMEM kernel
 ``mma.sync`` kernel (``csrc/kernels/attention.cu``); the backward follows
 the same split (``csrc/kernels/attention_bwd_sm100.cu`` for bf16 / 128).
 ``LRB_ATTN_SM100=0`` disables the tcgen05 forward and ``LRB_ATTN_BWD_SM100=0``
-the tcgen05 backward (for A/B comparisons).
+the tcgen05 backward; ``LRB_ATTN_FWD_ONE_TILE=1`` selects the earlier
+one-Q-tile-per-CTA forward instead of the two-tile ping-pong kernel (for A/B
+comparisons).
 """
 
 from __future__ import annotations
