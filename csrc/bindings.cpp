@@ -56,6 +56,10 @@ int64_t attn_sm100_error(int64_t);
 int64_t attn_bwd_sm100_error(int64_t);
 // memory.cu
 std::tuple<at::Tensor, at::Tensor, at::Tensor> topk_softmax_gather(const at::Tensor&, const at::Tensor&, int64_t);
+// gemm_nvfp4_sm100.cu
+at::Tensor gemm_nvfp4(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                      const at::Tensor&);
+int64_t gemm_nvfp4_error(int64_t);
 // comm/symm.cu
 std::tuple<int64_t, at::Tensor> symm_alloc(int64_t, int64_t);
 int64_t symm_open(const at::Tensor&, int64_t);
@@ -106,6 +110,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_sm100_error", &lrb::attn_sm100_error);
   m.def("attn_bwd_sm100_error", &lrb::attn_bwd_sm100_error);
   m.def("topk_softmax_gather", &lrb::topk_softmax_gather);
+  m.def("gemm_nvfp4", &lrb::gemm_nvfp4);
+  m.def("gemm_nvfp4_error", &lrb::gemm_nvfp4_error);
   m.def("symm_alloc", &lrb::symm_alloc);
   m.def("symm_open", &lrb::symm_open);
   m.def("symm_close", &lrb::symm_close);

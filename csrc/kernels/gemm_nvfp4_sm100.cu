@@ -1,0 +1,248 @@
+// NVFP4 block-scaled GEMM on tcgen05:  C[M, N] = sA * sB * sum_k (A[m,k] SFA) (B[n,k] SFB)
+// with A, B in E2M1 (two per byte, even element in the low nibble), one e4m3
+// scale per 16 elements along K (SFA, SFB) and one fp32 scale per tensor
+// (sA, sB) -- the NVFP4 format.  Both operands are K-major (nn.Linear layout).
+//
+// Scale factors are stored in the tensor-core atom layout: for every block of
+// 128 rows and 64 K-elements, 512 bytes with the scale of (row m, k-block j)
+// at byte 16*(m % 32) + 4*(m / 32) + j; atoms are ordered K-fastest within a
+// 128-row block (``nvfp4_swizzle_scales`` produces it).
+//
+// CTA = one 128 x 128 output tile, 6 warps:
+//   warp 0      producer: per K-stage (256 elements = 128 bytes per row) TMA
+//               loads of the A and B tiles (128-byte swizzle) and bulk copies
+//               of the four SFA and four SFB atoms, into a 4-stage ring;
+//   warp 1      TMEM owner + MMA issue: tcgen05.cp of the stage's scale atoms
+//               into TMEM (two alternating column sets), then four
+//               kind::mxf4nvf4 block16 MMAs (K = 64 each);
+//   warps 2..5  epilogue: tcgen05.ld, scale by sA*sB, bf16 stores.
+// tcgen05.cp and tcgen05.mma issued by one thread execute in order, so a
+// stage's scale copy precedes its MMAs without a wait.  All waits are bounded.
+#include "../common.cuh"
+#include "sm100.cuh"
+
+namespace lrb {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 128, BKE = 256, STAGES = 4;  // BKE: FP4 elements per stage
+constexpr int kThreads = 192;
+constexpr uint32_t kStageA = BM * BKE / 2, kStageB = BN * BKE / 2;  // 16 KB each
+constexpr uint32_t kAtom = 512, kStageSF = 4 * kAtom;               // four 64-element atoms
+constexpr uint32_t kStageBytes = kStageA + kStageB + 2 * kStageSF;
+constexpr size_t kSmem = 1024 + STAGES * (size_t)kStageBytes + 256;
+
+struct Nvfp4Args {
+  void* C;
+  int64_t ldc;
+  int M, N, K;
+  const uint8_t* sfa;  // atoms
+  const uint8_t* sfb;
+  const float* sa;     // tensor scales
+  const float* sb;
+  int* err;
+  int vec_ok;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Nvfp4Args a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + STAGES * kStageBytes);
+  uint64_t* full = bars;             // [STAGES]
+  uint64_t* empty = bars + STAGES;   // [STAGES]
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+  auto sA = [&](int s) { return base + s * kStageBytes; };
+  auto sB = [&](int s) { return base + s * kStageBytes + kStageA; };
+  auto sSFA = [&](int s) { return base + s * kStageBytes + kStageA + kStageB; };
+  auto sSFB = [&](int s) { return base + s * kStageBytes + kStageA + kStageB + kStageSF; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tm = blockIdx.y, tn = blockIdx.x;
+  const int m0 = tm * BM, n0 = tn * BN;
+  const int nk = a.K / BKE;
+  const int katoms = a.K / 64;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tAcc = tmem, tSFA = tmem + 128, tSFB = tmem + 160;  // SF: 2 sets x 16 columns each
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int armed = 0;
+      for (int j = 0; j < nk; ++j) {
+        const int st = j % STAGES;
+        const uint32_t ph = (j / STAGES) & 1;
+        if (!mbar_wait(&empty[st], ph ^ 1, a.err, kErrTmaWait)) break;
+        mbar_arrive_expect_tx(&full[st], kStageBytes);
+        tma_load_2d(sA(st), &tmA, &full[st], j * (BKE / 2), m0);
+        tma_load_2d(sB(st), &tmB, &full[st], j * (BKE / 2), n0);
+        bulk_load(sSFA(st), a.sfa + ((int64_t)tm * katoms + j * 4) * kAtom, kStageSF, &full[st]);
+        bulk_load(sSFB(st), a.sfb + ((int64_t)tn * katoms + j * 4) * kAtom, kStageSF, &full[st]);
+        ++armed;
+      }
+      for (int i = 1; i <= STAGES && i <= armed; ++i) {
+        const int j = armed - i;
+        mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_nvfp4(BM, BN);
+      bool ok = true;
+      for (int j = 0; j < nk && ok; ++j) {
+        const int st = j % STAGES;
+        const uint32_t ph = (j / STAGES) & 1;
+        if (!mbar_wait(&full[st], ph, a.err, kErrMmaWait)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t set = (j & 1) * 16;
+        const uint32_t fa = smem_addr(sSFA(st)), fb = smem_addr(sSFB(st));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          tmem_cp_32x128b_x4(tSFA + set + kk * 4, sf_desc(fa + kk * kAtom));
+          tmem_cp_32x128b_x4(tSFB + set + kk * 4, sf_desc(fb + kk * kAtom));
+        }
+        const uint32_t pa = smem_addr(sA(st)), pb = smem_addr(sB(st));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // 64 FP4 elements = 32 bytes of the 128-byte swizzled row
+          umma_nvfp4(tAcc, umma_desc_k_sw128(pa + kk * 32), umma_desc_k_sw128(pb + kk * 32), idesc,
+                     tSFA + set + kk * 4, tSFB + set + kk * 4, (j | kk) != 0);
+        umma_commit(&empty[st]);
+      }
+      umma_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = m0 + quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const bool have = __all_sync(0xffffffffu, nk > 0 && mbar_wait(acc_full, 0, a.err, kErrEpiWait));
+    tc_fence_after();
+    const float alpha = *a.sa * *a.sb;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      if (have) {
+        tmem_ld_32x32b_x32(tAcc + lane_base + c * 32, r);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) r[e] = 0u;
+      }
+      const int col0 = n0 + c * 32;
+      if (row >= a.M) continue;
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + (int64_t)row * a.ldc + col0;
+      if (a.vec_ok && col0 + 32 <= a.N) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          Vec16<__nv_bfloat16> v;
+#pragma unroll
+          for (int t = 0; t < 8; ++t) v.v[t] = __float2bfloat16_rn(alpha * __uint_as_float(r[e + t]));
+          st16(dst + e, v);
+        }
+      } else {
+        for (int e = 0; e < 32 && col0 + e < a.N; ++e) dst[e] = __float2bfloat16_rn(alpha * __uint_as_float(r[e]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ------------------------------------------------------------------ host
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    LRB_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    LRB_CHECK(p != nullptr && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled unavailable");
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// packed (rows, K/2) uint8, row pitch ld bytes; box = 128 bytes x 128 rows
+CUtensorMap fp4_map(const void* ptr, int64_t rows, int64_t bytes, int64_t ld) {
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LRB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp4) failed with code ", (int)r);
+  return m;
+}
+
+int* nvfp4_error_word(const at::Device& dev) {
+  static at::Tensor words[16];
+  const int idx = dev.index() < 0 ? 0 : dev.index();
+  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().device(dev).dtype(at::kInt));
+  return words[idx].data_ptr<int>();
+}
+
+}  // namespace
+
+// A (M, K/2) uint8, sfa atoms (ceil(M/128) * K/64 * 512) uint8, sa () fp32; B likewise with N.
+at::Tensor gemm_nvfp4(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& sa, const at::Tensor& B,
+                      const at::Tensor& sfb, const at::Tensor& sb) {
+  LRB_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kByte && B.scalar_type() == at::kByte,
+            "gemm_nvfp4: packed uint8 operands required");
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1) * 2;
+  LRB_CHECK(B.size(1) * 2 == K && K % BKE == 0, "gemm_nvfp4: K must match and be a multiple of 256");
+  LRB_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && A.stride(0) % 16 == 0 && B.stride(0) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(A.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(B.data_ptr()) % 16 == 0,
+            "gemm_nvfp4: operands need 16-byte aligned rows");
+  const int64_t mb = (M + 127) / 128, nb = (N + 127) / 128;
+  LRB_CHECK(sfa.numel() >= mb * (K / 64) * 512 && sfb.numel() >= nb * (K / 64) * 512 && sfa.is_contiguous() &&
+                sfb.is_contiguous(),
+            "gemm_nvfp4: scale atoms must cover ceil(rows/128) x K/64 x 512 bytes");
+  c10::cuda::CUDAGuard g(A.device());
+  auto C = at::empty({M, N}, A.options().dtype(at::kBFloat16));
+  if (M == 0 || N == 0) return C;
+  CUtensorMap ta = fp4_map(A.data_ptr(), M, K / 2, A.stride(0)), tb = fp4_map(B.data_ptr(), N, K / 2, B.stride(0));
+  Nvfp4Args args{C.data_ptr(), N, (int)M, (int)N, (int)K, sfa.data_ptr<uint8_t>(), sfb.data_ptr<uint8_t>(),
+                 sa.data_ptr<float>(), sb.data_ptr<float>(), nvfp4_error_word(A.device()), (N % 8) == 0 ? 1 : 0};
+  LRB_CUDA_CHECK(cudaFuncSetAttribute(gemm_nvfp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+  dim3 grid((unsigned)nb, (unsigned)mb);
+  gemm_nvfp4_kernel<<<grid, kThreads, kSmem, stream()>>>(ta, tb, args);
+  LRB_LAUNCH_CHECK();
+  return C;
+}
+
+int64_t gemm_nvfp4_error(int64_t device) {
+  int* w = nvfp4_error_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
+  int h = 0;
+  LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
+  return h;
+}
+
+}  // namespace lrb

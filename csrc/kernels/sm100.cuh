@@ -74,6 +74,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Untiled bulk copy global -> shared (no multicast); both addresses and the size
+// must be multiples of 16 bytes.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05 / TMEM
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
@@ -113,6 +121,42 @@ __device__ __forceinline__ void umma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem
       "}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// Block-scaled FP4 MMA (NVFP4: E2M1 operands, e4m3 scale per 16 elements):
+// D (+)= (A * SFA) (B * SFB)^T for one K=64 step; the scale factors are read
+// from tensor memory.
+__device__ __forceinline__ void umma_nvfp4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Shared -> tensor memory copy of 32 rows x 16 bytes, replicated into the four
+// 32-lane quarters (the layout block-scaled MMAs read scale factors from).
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Descriptor of 32 contiguous 16-byte rows (no swizzle; 8-row core matrices 128 B apart).
+__device__ __forceinline__ uint64_t sf_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)(128 >> 4) << 16;  // leading byte offset
+  d |= (uint64_t)(128 >> 4) << 32;  // stride byte offset: next 8 rows
+  d |= (uint64_t)1 << 46;           // descriptor version (sm100)
+  return d;                         // layout type 0: no swizzle
+}
+
+// Instruction descriptor of kind::mxf4nvf4: E2M1 A and B (K-major), UE4M3 scales.
+__host__ __device__ constexpr uint32_t umma_idesc_nvfp4(int M, int N) {
+  return (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {

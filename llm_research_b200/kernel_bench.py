@@ -16,6 +16,7 @@ Cases (shapes are the GENESIS-1B / 7B working shapes):
   attn_fwd_gqa           B=2, S=4096, H=32, Hkv=8, hd=128
   gemm                   tcgen05 bf16 GEMM 8192x8192x8192 (TN)
   gemm_cublas            the same shape through torch.matmul (library reference)
+  gemm_nvfp4             tcgen05 block-scaled NVFP4 GEMM 8192x8192x8192 (nominal FP4 dense peak 4.5 PFLOP/s)
   rmsnorm_fwd/bwd        32768 x 2048 bf16
   swiglu_fwd             32768 x (2 x 5632) bf16
   ns                     Newton-Schulz, 5 iterations, batch 8 of 2048 x 5632
@@ -94,6 +95,14 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
             return (lambda: torch.matmul(a, b.t())), 2.0 * n ** 3, 0.0
         return (lambda: C.gemm_tn(a, b, torch.bfloat16, 1.0)), 2.0 * n ** 3, 0.0
 
+    def gemm_fp4():
+        from llm_research_b200.ops.quant import NVFP4Tensor, matmul_nvfp4
+
+        n = 8192
+        a = NVFP4Tensor.quantize(torch.randn(n, n, device="cuda", dtype=torch.bfloat16))
+        b = NVFP4Tensor.quantize(torch.randn(n, n, device="cuda", dtype=torch.bfloat16))
+        return (lambda: matmul_nvfp4(a, b)), 2.0 * n ** 3, 0.0
+
     def rms(bwd: bool):
         rows, d = 32768, 2048
         x = torch.randn(rows, d, device="cuda", dtype=torch.bfloat16)
@@ -136,6 +145,7 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
         "attn_fwd_gqa": lambda: _attn_case(2, 4096, 32, 8, False),
         "gemm": lambda: gemm(False),
         "gemm_cublas": lambda: gemm(True),
+        "gemm_nvfp4": gemm_fp4,
         "rmsnorm_fwd": lambda: rms(False),
         "rmsnorm_bwd": lambda: rms(True),
         "swiglu_fwd": swiglu,

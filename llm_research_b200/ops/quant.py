@@ -112,3 +112,46 @@ def nvfp4_dequantize(packed: torch.Tensor, s_b: torch.Tensor, s_t: torch.Tensor,
     val = torch.where(code >= 8, -mag, mag)
     val = val.view(M, K // 16, 16) * s_b.float()[:, :, None] * s_t.float()
     return val.view(M, K).to(dtype)
+
+
+# ---------------------------------------------------------------- NVFP4 GEMM
+def nvfp4_swizzle_scales(s_b: torch.Tensor) -> torch.Tensor:
+    """Row-major block scales ``(M, K/16)`` (e4m3) -> the tensor-core atom layout
+    used by :func:`matmul_nvfp4`: ``(ceil(M/128), K/64, 512)`` bytes where the
+    scale of (row m, k-block j) in a 128 x 64 block sits at byte
+    ``16*(m % 32) + 4*(m // 32) + j``.  Rows past M are zero."""
+    M, KB = s_b.shape
+    assert KB % 4 == 0, "K must be a multiple of 64"
+    mb = -(-M // 128)
+    raw = s_b.view(torch.uint8) if s_b.dtype != torch.uint8 else s_b
+    if mb * 128 != M:
+        raw = torch.cat([raw, raw.new_zeros(mb * 128 - M, KB)])
+    # (mb, q=4, r=32, kb=KB/4, j=4) -> (mb, kb, r, q, j)
+    return raw.view(mb, 4, 32, KB // 4, 4).permute(0, 3, 2, 1, 4).contiguous().view(mb, KB // 4, 512)
+
+
+class NVFP4Tensor:
+    """A 2-D tensor quantised to NVFP4 for :func:`matmul_nvfp4` (rows = M or N, K-major)."""
+
+    def __init__(self, packed: torch.Tensor, scales: torch.Tensor, tensor_scale: torch.Tensor) -> None:
+        self.packed, self.scales, self.tensor_scale = packed, scales, tensor_scale.float().reshape(())
+        self.atoms = nvfp4_swizzle_scales(scales)
+
+    @classmethod
+    def quantize(cls, x2d: torch.Tensor, stochastic: bool = False, seed: int = 0) -> "NVFP4Tensor":
+        return cls(*nvfp4_quantize(x2d, stochastic, seed))
+
+    def dequantize(self, dtype=torch.float32) -> torch.Tensor:
+        return nvfp4_dequantize(self.packed, self.scales, self.tensor_scale, dtype)
+
+    @property
+    def shape(self):
+        return (self.packed.shape[0], self.packed.shape[1] * 2)
+
+
+def matmul_nvfp4(a: NVFP4Tensor, b: NVFP4Tensor) -> torch.Tensor:
+    """``a @ b.T`` in bf16 with tcgen05 block-scaled FP4 MMAs (fp32 accumulation).
+    K must be a multiple of 256.  On CPU: dequantise and multiply (the oracle)."""
+    if a.packed.is_cuda:
+        return native().gemm_nvfp4(a.packed, a.atoms, a.tensor_scale, b.packed, b.atoms, b.tensor_scale)
+    return (a.dequantize() @ b.dequantize().t()).to(torch.bfloat16)
