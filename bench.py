@@ -169,6 +169,16 @@ def run_ours(args) -> dict:
         per_step = _count_kernels(lambda: step(dev_batches))
         launches = per_step * args.steps
 
+    # Exposed communication: one extra (untimed) step with the compute stream's
+    # waits on communication events bracketed by CUDA events; max over ranks.
+    exposed = None
+    engine = trainer.model
+    if world > 1 and hasattr(engine, "start_exposed_comm_measurement"):
+        _barrier_sync(dist, torch)
+        engine.start_exposed_comm_measurement()
+        step(dev_batches)
+        exposed = _max_over_ranks(engine.stop_exposed_comm_measurement(), dist, device)
+
     tokens_per_step = world * accum * micro * S
     value = tokens_per_step * args.steps / (dev_ms / 1000.0)
     flops = count_flops_per_token(cfg, S)
@@ -196,7 +206,8 @@ def run_ours(args) -> dict:
             "optimizer": "MuonAdamWHybrid (Muon on 2-D, AdamW on embedding/norms)",
             "l2": "inputs+activations >> 126 MB L2; no flush",
             "model_tflops_per_gpu": flops * value / world / 1e12,
-            "exposed_comm_ms_per_step": None,
+            "exposed_comm_ms_per_step": exposed,
+            "comm": getattr(trainer.model, "comm", "none"),
             "final_loss": final_loss,
         },
         "clocks": sampler.summary(),

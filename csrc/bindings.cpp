@@ -76,6 +76,23 @@ void diloco_push(const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_
                  int64_t, at::Tensor&, at::Tensor&);
 void diloco_reduce_nesterov(const at::Tensor&, at::Tensor&, at::Tensor&, at::Tensor&, int64_t, double, double,
                             const at::Tensor&, at::Tensor&, at::Tensor&, int64_t, at::Tensor&, at::Tensor&);
+// comm/ep.cu
+void ep_push(const at::Tensor&, const c10::optional<at::Tensor>&, bool, const at::Tensor&, int64_t, int64_t, int64_t,
+             int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, const at::Tensor&, const at::Tensor&,
+             const at::Tensor&, at::Tensor&, at::Tensor&);
+void ep_pull(at::Tensor&, const c10::optional<at::Tensor>&, const c10::optional<at::Tensor>&, const at::Tensor&,
+             int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, const at::Tensor&,
+             const at::Tensor&, const at::Tensor&, at::Tensor&, at::Tensor&);
+void ep_flag_wait(const at::Tensor&, int64_t, int64_t, at::Tensor&);
+void ep_flag_set(at::Tensor&, int64_t);
+// comm/gemm_comm.cu
+void gemm_rs(const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int64_t, int64_t,
+             int64_t, at::Tensor&, at::Tensor&);
+void tp_reduce(const at::Tensor&, const c10::optional<at::Tensor>&, at::Tensor&, int64_t, const at::Tensor&,
+               at::Tensor&, int64_t, at::Tensor&, at::Tensor&);
+void shard_publish(const at::Tensor&, at::Tensor&, at::Tensor&, int64_t, at::Tensor&);
+at::Tensor ag_gemm(const at::Tensor&, at::Tensor&, at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int64_t,
+                   int64_t, int64_t, at::Tensor&);
 }  // namespace lrb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -112,6 +129,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("topk_softmax_gather", &lrb::topk_softmax_gather);
   m.def("gemm_nvfp4", &lrb::gemm_nvfp4);
   m.def("gemm_nvfp4_error", &lrb::gemm_nvfp4_error);
+  m.def("ep_push", &lrb::ep_push);
+  m.def("ep_pull", &lrb::ep_pull);
+  m.def("ep_flag_wait", &lrb::ep_flag_wait);
+  m.def("ep_flag_set", &lrb::ep_flag_set);
+  m.def("gemm_rs", &lrb::gemm_rs);
+  m.def("tp_reduce", &lrb::tp_reduce);
+  m.def("shard_publish", &lrb::shard_publish);
+  m.def("ag_gemm", &lrb::ag_gemm);
   m.def("symm_alloc", &lrb::symm_alloc);
   m.def("symm_open", &lrb::symm_open);
   m.def("symm_close", &lrb::symm_close);

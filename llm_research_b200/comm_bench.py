@@ -1,0 +1,158 @@
+"""Fused compute + collective paths on N GPUs of one node, against the NCCL baseline.
+
+``python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 -m llm_research_b200.comm_bench``
+
+For every case the time is measured with CUDA events on each rank (warm-up,
+synchronise + barrier on both sides) and the MAX over ranks is reported; one
+JSON line per case on rank 0 with the achieved fraction of its roofline:
+``max(FLOPs / measured bf16 GEMM peak, bytes each GPU must send over NVLink /
+770 GB/s per direction)``.
+
+Cases (M = tokens over all ranks, sequence-sharded; N x K weights):
+  ag_gemm      fused all-gather(rows) -> GEMM    vs  NCCL all_gather + cuBLAS
+  gemm_rs      fused GEMM -> reduce-scatter(rows) vs  cuBLAS + NCCL reduce_scatter
+  fsdp_rs      P2P reduce-scatter (bf16 wire, fp32 accumulate, fused norm) vs NCCL (fp32)
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+NVLINK_GBS = 770.0  # measured peer copy, GB/s per direction per GPU
+
+
+def _peak_tflops() -> float:
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
+
+
+def _time(fn, warmup: int, iters: int, dev) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / iters], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens", type=int, nargs="+", default=[8192, 32768])
+    ap.add_argument("--nk", type=int, nargs="+", default=[4096, 8192])
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args(argv)
+    import datetime
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from llm_research_b200.parallel.tp import TPComm
+
+    peak = _peak_tflops()
+    maxT, maxW = max(args.tokens), max(args.nk)
+    comm = TPComm(None, max_tokens=maxT, max_width=maxW, device=dev)
+
+    def report(case, T, N, K, ms, base_ms, flops, nvbytes):
+        if rank != 0:
+            return
+        roof_ms = max(flops / (peak * 1e12), nvbytes / (NVLINK_GBS * 1e9)) * 1e3
+        print(json.dumps({"case": case, "gpus": world, "M": T, "N": N, "K": K, "ms": round(ms, 4),
+                          "nccl_ms": round(base_ms, 4), "speedup_vs_nccl": round(base_ms / ms, 3),
+                          "roofline_ms": round(roof_ms, 4), "frac_of_roofline": round(roof_ms / ms, 3)}), flush=True)
+
+    for T in args.tokens:
+        for NK in args.nk:
+            N = K = NK
+            Tl = T // world
+            x_shard = torch.randn(Tl, K, device=dev, dtype=torch.bfloat16)
+            w = torch.randn(N // world, K, device=dev, dtype=torch.bfloat16) * 0.02  # column shard
+            full = torch.empty(T, K, device=dev, dtype=torch.bfloat16)
+
+            def nccl_ag():
+                dist.all_gather_into_tensor(full, x_shard)
+                return full @ w.t()
+
+            flops = 2.0 * T * (N // world) * K
+            ag_bytes = (world - 1) * Tl * K * 2
+            ms = _time(lambda: comm.ag_gemm(x_shard, w), args.warmup, args.iters, dev)
+            base = _time(nccl_ag, args.warmup, args.iters, dev)
+            report("ag_gemm", T, N // world, K, ms, base, flops, ag_bytes)
+
+            xk = torch.randn(T, K // world, device=dev, dtype=torch.bfloat16)  # row-parallel input
+            w2 = torch.randn(N, K // world, device=dev, dtype=torch.bfloat16) * 0.02
+            out = torch.empty(Tl, N, device=dev, dtype=torch.bfloat16)
+
+            def nccl_rs():
+                y = xk @ w2.t()
+                dist.reduce_scatter_tensor(out, y)
+                return out
+
+            flops = 2.0 * T * N * (K // world)
+            rs_bytes = (world - 1) * Tl * N * 2
+            ms = _time(lambda: comm.gemm_rs(xk, w2), args.warmup, args.iters, dev)
+            base = _time(nccl_rs, args.warmup, args.iters, dev)
+            report("gemm_rs", T, N, K // world, ms, base, flops, rs_bytes)
+            del x_shard, w, full, xk, w2, out
+    comm.heap.check()
+    comm.close()
+
+    # FSDP gradient reduce-scatter of a 7B-sized unit (fp32 accumulators)
+    from llm_research_b200._ext import native
+    from llm_research_b200.parallel.symm import SymmetricHeap
+
+    C = native()
+    n = 8 * 1024 * 1024 * world  # elements per unit
+    shard = n // world
+    heap = SymmetricHeap(world * shard * 2 + 8192, device=dev)
+    recv_off, ready_off, consumed_off = heap.alloc(world * shard * 2), heap.alloc(4 * world), heap.alloc(4)
+    recv = heap.view(recv_off, (world * shard,), torch.bfloat16)
+    ready, consumed = heap.view(ready_off, (world,), torch.int32), heap.view(consumed_off, (1,), torch.int32)
+    counters = torch.zeros(4, dtype=torch.int32, device=dev)
+    g = torch.randn(n, device=dev)
+    dst = torch.empty(shard, device=dev)
+    sumsq = torch.zeros((), device=dev)
+    state = {"e": 0}
+
+    def p2p():
+        state["e"] += 1
+        C.p2p_rs_push(g, heap.bases, recv_off, ready_off, consumed_off, rank, world, shard, state["e"], counters[0:1],
+                      heap.err)
+        C.p2p_rs_reduce(recv, dst, world, 1.0 / world, False, ready, consumed, state["e"], sumsq, counters[1:2],
+                        heap.err)
+
+    def nccl():
+        dist.reduce_scatter_tensor(dst, g, op=dist.ReduceOp.AVG)
+
+    ms = _time(p2p, args.warmup, args.iters, dev)
+    base = _time(nccl, args.warmup, args.iters, dev)
+    if rank == 0:
+        roof = (world - 1) * shard * 2 / (NVLINK_GBS * 1e9) * 1e3
+        print(json.dumps({"case": "fsdp_rs", "gpus": world, "elements": n, "ms": round(ms, 4), "nccl_fp32_ms": round(base, 4),
+                          "speedup_vs_nccl": round(base / ms, 3), "roofline_ms": round(roof, 4),
+                          "frac_of_roofline": round(roof / ms, 3)}), flush=True)
+    heap.check()
+    heap.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -306,8 +306,34 @@ class FlatShardEngine(nn.Module):
             u.gather_event = ev
             u.gathered = True
         if wait and u.gather_event is not None:
-            torch.cuda.current_stream(self.device).wait_event(u.gather_event)
+            self._wait_comm(u.gather_event)
             u.gather_event = None
+
+    # ----------------------------------------------------- exposed communication
+    _exposed_pairs: Optional[List[Tuple[torch.cuda.Event, torch.cuda.Event]]] = None
+
+    def _wait_comm(self, ev: torch.cuda.Event) -> None:
+        """Make the compute stream wait for a communication event; when measuring,
+        bracket the wait with events so the stall can be timed on the device."""
+        cur = torch.cuda.current_stream(self.device)
+        if self._exposed_pairs is None:
+            cur.wait_event(ev)
+            return
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        cur.wait_event(ev)
+        e1.record(cur)
+        self._exposed_pairs.append((e0, e1))
+
+    def start_exposed_comm_measurement(self) -> None:
+        self._exposed_pairs = []
+
+    def stop_exposed_comm_measurement(self) -> float:
+        """Milliseconds the compute stream spent waiting for communication since
+        ``start_exposed_comm_measurement`` (synchronises the device)."""
+        pairs, self._exposed_pairs = self._exposed_pairs or [], None
+        torch.cuda.synchronize(self.device)
+        return float(sum(a.elapsed_time(b) for a, b in pairs))
 
     def _prefetch(self, pos: int) -> None:
         if 0 <= pos < len(self.unit_order):
@@ -426,7 +452,7 @@ class FlatShardEngine(nn.Module):
         cur = torch.cuda.current_stream(self.device)
         for u in self.units:
             if u.rs_event is not None:
-                cur.wait_event(u.rs_event)
+                self._wait_comm(u.rs_event)
                 u.rs_event = None
 
     # ---------------------------------------------------------------- forward

@@ -1,0 +1,220 @@
+"""Tensor parallelism (Megatron column / row split) with sequence parallelism,
+on the fused GEMM + collective kernels of ``csrc/comm/gemm_comm.cu``.
+
+Activations between layers are sharded along tokens (sequence parallel):
+``x_shard`` is ``(T / tp, d)`` on every rank.
+
+* :class:`ColumnParallelLinear` (QKV, up/gate): ``y = AllGather_T(x) W_r^T``
+  with ``W_r`` the rank's ``out / tp`` rows.  Forward = ``ag_gemm`` (copy CTAs
+  pull peer chunks into a local buffer while the tensor-core CTAs consume
+  them); backward dX = ``gemm_rs`` (dY W_r, reduce-scattered over tokens by
+  the epilogue's stores into the owners' slots), dW = dYᵀ AllGather(x).
+* :class:`RowParallelLinear` (o_proj, down): ``y_shard = ReduceScatter_T(x W_r^T)``
+  with ``W_r`` the rank's ``in / tp`` columns.  Forward = ``gemm_rs`` +
+  ``tp_reduce`` (fp32 sum of the slots, optional fused residual add);
+  backward dX = ``ag_gemm`` (AllGather(dY) W_r), dW = AllGather(dY)ᵀ x.
+
+Buffers live in one :class:`~llm_research_b200.parallel.symm.SymmetricHeap`
+per TP group (:class:`TPComm`).  Every call bumps an epoch that all ranks
+share (calls are collective and in the same order); ``gemm_rs`` slots are
+released by the owner's ``consumed`` flag, ``ag_gemm`` source shards are
+double-buffered by epoch parity: a rank republishes slot ``e % 2`` only after
+its own ``ag_gemm(e-1)``, which waited for every peer's ``e-1`` publish, which
+each peer issued after finishing its ``ag_gemm(e-2)`` reads of that slot
+(one stream per rank).
+
+Without a heap (CPU, several nodes, or ``comm="nccl"``) the same layers run
+NCCL / gloo collectives around ``F.linear`` -- the baseline.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+from llm_research_b200._ext import native
+
+
+class TPComm:
+    """Symmetric buffers for TP collectives of up to ``max_tokens`` tokens and ``max_width`` features."""
+
+    def __init__(self, group: Optional[dist.ProcessGroup], max_tokens: int, max_width: int,
+                 device: torch.device, ncopy: int = 16) -> None:
+        from llm_research_b200.parallel.symm import SymmetricHeap
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = device
+        self.max_tokens, self.max_width, self.ncopy = max_tokens, max_width, ncopy
+        W = self.world
+        slot = (max_tokens // W) * max_width * 2
+        self.heap = h = SymmetricHeap(W * slot + 2 * slot + 8192, group=group, device=device)
+        self.recv_off = h.alloc(W * slot)
+        self.ready_off = h.alloc(4 * W)
+        self.consumed_off = h.alloc(4)
+        self.shard_off = [h.alloc(slot), h.alloc(slot)]
+        self.shard_ready_off = [h.alloc(4), h.alloc(4)]
+        self.ready = h.view(self.ready_off, (W,), torch.int32)
+        self.consumed = h.view(self.consumed_off, (1,), torch.int32)
+        self.shard_ready = [h.view(o, (1,), torch.int32) for o in self.shard_ready_off]
+        self.counters = torch.zeros(W + 4, dtype=torch.int32, device=device)
+        self.chunk_flags = torch.zeros(max_tokens // 128, dtype=torch.int32, device=device)
+        self.rs_epoch = 0
+        self.ag_epoch = 0
+
+    def gemm_rs(self, x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``ReduceScatter_rows(x @ w.T)`` (+ residual): ``(T, K) x (N, K) -> (T / world, N)``."""
+        C = native()
+        T, N = x.shape[0], w.shape[0]
+        self.rs_epoch += 1
+        C.gemm_rs(x.contiguous(), w, self.heap.bases, self.recv_off, self.ready_off, self.consumed_off, self.rank,
+                  self.world, self.rs_epoch, self.counters[: self.world], self.heap.err)
+        out = torch.empty(T // self.world, N, dtype=x.dtype, device=x.device)
+        recv = self.heap.view(self.recv_off, (self.world * out.numel(),), torch.bfloat16)
+        C.tp_reduce(recv, residual.contiguous() if residual is not None else None, out, self.world, self.ready,
+                    self.consumed, self.rs_epoch, self.counters[self.world:self.world + 1], self.heap.err)
+        return out
+
+    def ag_gemm(self, x_shard: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """``AllGather_rows(x_shard) @ w.T``: ``(T / world, K) x (N, K) -> (T, N)``."""
+        C = native()
+        Tl, K = x_shard.shape
+        T = Tl * self.world
+        self.ag_epoch += 1
+        s = self.ag_epoch % 2
+        dst = self.heap.view(self.shard_off[s], (Tl, K), torch.bfloat16)
+        C.shard_publish(x_shard.contiguous(), dst, self.shard_ready[s], self.ag_epoch,
+                        self.counters[self.world + 1:self.world + 2])
+        a_full = torch.empty(T, K, dtype=x_shard.dtype, device=x_shard.device)
+        return C.ag_gemm(w, a_full, self.chunk_flags, self.heap.bases, self.shard_off[s], self.shard_ready_off[s],
+                         self.rank, self.world, self.ag_epoch, self.ncopy, self.heap.err)
+
+    def fits(self, tokens: int, width: int) -> bool:
+        return (tokens <= self.max_tokens and width <= self.max_width and tokens % (128 * self.world) == 0
+                and width % 8 == 0)
+
+    def close(self) -> None:
+        self.heap.close()
+
+
+# ----------------------------------------------------------- collectives (fallback)
+def _all_gather_rows(x: torch.Tensor, group) -> torch.Tensor:
+    W = dist.get_world_size(group)
+    out = torch.empty(x.shape[0] * W, *x.shape[1:], dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+    return out
+
+
+def _reduce_scatter_rows(x: torch.Tensor, group) -> torch.Tensor:
+    W = dist.get_world_size(group)
+    out = torch.empty(x.shape[0] // W, *x.shape[1:], dtype=x.dtype, device=x.device)
+    if x.is_cuda:
+        dist.reduce_scatter_tensor(out, x.contiguous(), group=group)
+    else:  # gloo has no reduce_scatter_tensor
+        full = x.contiguous().clone()
+        dist.all_reduce(full, group=group)
+        out.copy_(full.chunk(W)[dist.get_rank(group)])
+    return out
+
+
+def _fused_ok(comm: Optional[TPComm], x: torch.Tensor, tokens: int, widths) -> bool:
+    return (comm is not None and x.is_cuda and x.dtype == torch.bfloat16
+            and all(comm.fits(tokens, w) for w in widths))
+
+
+class _ColumnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_shard, w, comm, group):
+        ctx.comm, ctx.group = comm, group
+        ctx.save_for_backward(x_shard, w)
+        T = x_shard.shape[0] * dist.get_world_size(group)
+        if _fused_ok(comm, x_shard, T, (x_shard.shape[1], w.shape[0])):
+            return comm.ag_gemm(x_shard, w)
+        return F.linear(_all_gather_rows(x_shard, group), w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x_shard, w = ctx.saved_tensors
+        comm, group = ctx.comm, ctx.group
+        dy = dy.contiguous()
+        T = dy.shape[0]
+        x_full = _all_gather_rows(x_shard, group)
+        dw = dy.t().matmul(x_full) if ctx.needs_input_grad[1] else None
+        if _fused_ok(comm, dy, T, (w.shape[1], w.shape[0])):
+            dx = comm.gemm_rs(dy, w.t().contiguous())
+        else:
+            dx = _reduce_scatter_rows(dy.matmul(w), group)
+        return dx, dw, None, None
+
+
+class _RowFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, residual, comm, group):
+        ctx.comm, ctx.group = comm, group
+        ctx.save_for_backward(x, w)
+        ctx.has_residual = residual is not None
+        T = x.shape[0]
+        if _fused_ok(comm, x, T, (w.shape[0], w.shape[1])):
+            return comm.gemm_rs(x, w, residual)
+        y = _reduce_scatter_rows(F.linear(x, w), group)
+        return y + residual if residual is not None else y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        comm, group = ctx.comm, ctx.group
+        dy = dy.contiguous()
+        T = dy.shape[0] * dist.get_world_size(group)
+        dres = dy if ctx.has_residual else None
+        if _fused_ok(comm, dy, T, (w.shape[0], w.shape[1])):
+            dx = comm.ag_gemm(dy, w.t().contiguous())
+        else:
+            dx = _all_gather_rows(dy, group).matmul(w)
+        dw = _all_gather_rows(dy, group).t().matmul(x) if ctx.needs_input_grad[1] else None
+        return dx, dw, dres, None, None
+
+
+class ColumnParallelLinear(nn.Module):
+    """``(T/tp, in) -> (T, out/tp)``; weight shard ``(out/tp, in)``."""
+
+    def __init__(self, in_features: int, out_features: int, group: Optional[dist.ProcessGroup] = None,
+                 comm: Optional[TPComm] = None, device=None, dtype=None) -> None:
+        super().__init__()
+        self.group, self.comm = group, comm
+        tp = dist.get_world_size(group)
+        assert out_features % tp == 0
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = nn.Parameter(torch.empty(out_features // tp, in_features, device=device, dtype=dtype))
+        nn.init.normal_(self.weight, std=0.02)
+
+    def forward(self, x_shard: torch.Tensor) -> torch.Tensor:
+        return _ColumnFn.apply(x_shard, self.weight, self.comm, self.group)
+
+
+class RowParallelLinear(nn.Module):
+    """``(T, in/tp) -> (T/tp, out)`` (+ residual); weight shard ``(out, in/tp)``."""
+
+    def __init__(self, in_features: int, out_features: int, group: Optional[dist.ProcessGroup] = None,
+                 comm: Optional[TPComm] = None, device=None, dtype=None) -> None:
+        super().__init__()
+        self.group, self.comm = group, comm
+        tp = dist.get_world_size(group)
+        assert in_features % tp == 0
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = nn.Parameter(torch.empty(out_features, in_features // tp, device=device, dtype=dtype))
+        nn.init.normal_(self.weight, std=0.02 / math.sqrt(2.0))
+
+    def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return _RowFn.apply(x, self.weight, residual, self.comm, self.group)
+
+
+def shard_linear_weight(w: torch.Tensor, group: Optional[dist.ProcessGroup], dim: int) -> torch.Tensor:
+    """This rank's slice of a full weight: ``dim=0`` for column parallel, ``1`` for row parallel."""
+    tp, r = dist.get_world_size(group), dist.get_rank(group)
+    return w.chunk(tp, dim=dim)[r].contiguous()
