@@ -38,6 +38,12 @@ import time
 REPO = os.path.dirname(os.path.abspath(__file__))
 METRIC = "train tokens/sec/box (device-timed, max over ranks) at 1/2/4/8 B200; exposed comm ms/step"
 MODEL_NAME = "GENESIS-1B dense (HLRT trunk: 24L, d2048, 16H, SwiGLU 5632, vocab 32000, RoPE)"
+MODEL_NAMES = {
+    "genesis-1b": MODEL_NAME,
+    "genesis-7b": "GENESIS-7B dense (32L, d4096, 32/8 heads, SwiGLU 11008, vocab 32000)",
+    "genesis-7b-nvfp4": "GENESIS-7B dense NVFP4 (32L, d4096, 32/8 heads, SwiGLU 11008, vocab 32000)",
+    "genesis-40b-moe": "GENESIS-40B-A8B MoE (32L, d4096, 32/8 heads, 16 experts x ffn 6144 top-2 + 1 shared)",
+}
 
 
 def parse_args(argv=None):
@@ -53,6 +59,10 @@ def parse_args(argv=None):
     ap.add_argument("--ref-micro-batch", type=int, default=0,
                     help="reference micro-batch; 0 = the largest of 8/4/2/1 that fits (1 GPU), 4 on several GPUs")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--precision", choices=["bf16", "nvfp4"], default="bf16",
+                    help="linear-layer precision of the model (nvfp4: block-scaled FP4 training GEMMs)")
+    ap.add_argument("--ep", action="store_true",
+                    help="expert parallelism over all ranks for MoE presets (each rank holds E/world experts)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--count-launches", type=int, default=1)
     return ap.parse_args(argv)
@@ -110,7 +120,22 @@ def run_ours(args) -> dict:
     S = args.seq_len
     cfg = build_hlrt_config(args.preset)
     torch.manual_seed(args.seed)
-    with torch.device(device):
+    from llm_research_b200.ops.linear import set_linear_precision
+
+    set_linear_precision(args.precision)
+    import contextlib
+
+    ep_ctx = contextlib.nullcontext()
+    if args.ep and cfg.tier1_moe_num_experts:
+        from llm_research_b200.parallel.expert_parallel import EPComm, expert_parallel
+
+        comm = None
+        if world > 1:
+            comm = EPComm(None, max_tokens=micro * S, top_k=cfg.tier1_moe_top_k, d=cfg.d_model,
+                          experts_per_rank=cfg.tier1_moe_num_experts // world,
+                          capacity_factor=cfg.tier1_moe_capacity_factor, device=device)
+        ep_ctx = expert_parallel(None, comm)
+    with torch.device(device), ep_ctx:
         model = HLRT(cfg)
     trainer = DistributedBootstrapTrainer(
         model,
@@ -197,12 +222,15 @@ def run_ours(args) -> dict:
         "data": "synthetic (uniform token ids, seeded); random N(0,0.02) init",
         "impl": "ours",
         "config": {
-            "model": MODEL_NAME,
+            "model": MODEL_NAMES.get(args.preset, args.preset),
             "global_batch": world * accum * micro,
             "seq_len": S,
             "micro_batch": micro,
             "grad_accum": accum,
-            "parallelism": f"fsdp{world} (FULL_SHARD, bf16 compute, fp32 master) + distributed Muon",
+            "parallelism": (f"fsdp{world} (FULL_SHARD, bf16 compute, fp32 master) + distributed Muon"
+                            + (f" + ep{world}" if args.ep else "")),
+            "linear_precision": args.precision,
+            "preset": args.preset,
             "optimizer": "MuonAdamWHybrid (Muon on 2-D, AdamW on embedding/norms)",
             "l2": "inputs+activations >> 126 MB L2; no flush",
             "model_tflops_per_gpu": flops * value / world / 1e12,

@@ -19,6 +19,8 @@
 #include "../common.cuh"
 #include "sm100.cuh"
 
+#include <cstdlib>
+
 namespace lrb {
 namespace {
 
@@ -308,6 +310,306 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------ v3: 64-query sub-tiles
+// CTA = (batch, kv-head, 128 keys); query sub-tiles of 64 rows, double-buffered
+// end to end so the MMAs of sub-tile t+1 overlap the softmax-gradient and the
+// dQ epilogue of sub-tile t.  TMEM (512 columns):
+//   S^T_b  [b*128, b*128+64)   keys x 64 queries, later dQ^T_b (hd x 64 queries)
+//   dP^T_b [b*128+64, b*128+128)
+//   dV [256, 384), dK [384, 512)
+// dQ^T = K^T dS^T is written over S^T_b once the softmax warps have read it,
+// so dQ needs no columns of its own.  Warps: 0 TMA (K, V once; Q, dO and the
+// LSE / D of each sub-tile into one of two buffers), 1 MMA issue, 2..9
+// softmax-gradient (two threads per key row, 32 queries each), 10..13 dQ
+// epilogue (one thread per head-dim lane: coalesced fp32 reductions).
+namespace bwd3 {
+constexpr int TQ3 = 64;
+constexpr int kThreads = 448;
+constexpr uint32_t kKV = 32768, kKVHalf = 16384;   // K or V tile, 64-column half
+constexpr uint32_t kQ = 16384, kQHalf = 8192;       // Q or dO sub-tile, half
+constexpr uint32_t kPT = 16384;                     // P^T or dS^T: 128 keys x 64 queries
+constexpr size_t kSmem = 1024 + 2 * kKV + 4 * (size_t)kQ + 4 * (size_t)kPT + 1024 + 4 * TQ3 * sizeof(float);
+}  // namespace bwd3
+
+__global__ void __launch_bounds__(bwd3::kThreads, 1)
+    attn_bwd_v3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, BwdArgs a) {
+  using namespace bwd3;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sK = base;
+  unsigned char* sV = base + kKV;
+  unsigned char* sQ = base + 2 * kKV;              // [2]
+  unsigned char* sdO = sQ + 2 * kQ;                // [2]
+  unsigned char* sPt = sdO + 2 * kQ;               // [2]
+  unsigned char* sdSt = sPt + 2 * kPT;             // [2]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdSt + 2 * kPT);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;    // [2]
+  uint64_t* qd_free = bars + 3;    // [2]
+  uint64_t* sdp_full = bars + 5;   // [2]
+  uint64_t* p_full = bars + 7;     // [2]
+  uint64_t* dq_full = bars + 9;    // [2]
+  uint64_t* dq_free = bars + 11;   // [2]
+  uint64_t* acc_done = bars + 13;
+  uint64_t* drain = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  float* sL = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(bars) + 1024);  // [2][64]
+  float* sD = sL + 2 * TQ3;                                                           // [2][64]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * TK;
+  const int b = blockIdx.y / a.Hkv, hk = blockIdx.y % a.Hkv, G = a.H / a.Hkv;
+  const int off = a.Skv - a.Sq;
+  const int q_first = a.causal ? max(0, n0 - off) : 0;
+  const int qt0 = q_first / TQ3;
+  const int nqt = q_first < a.Sq ? (a.Sq + TQ3 - 1) / TQ3 - qt0 : 0;
+  const int total = nqt * G;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 32);
+      mbar_init(&qd_free[i], 1);
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&p_full[i], 256);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_free[i], 128);
+    }
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmdO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tdV = tmem + 256, tdK = tmem + 384;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (total > 0) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(kv_full, 2 * kKV);
+        tma_load_4d(sK, &tmK, kv_full, 0, hk, n0, b);
+        tma_load_4d(sK + kKVHalf, &tmK, kv_full, 64, hk, n0, b);
+        tma_load_4d(sV, &tmV, kv_full, 0, hk, n0, b);
+        tma_load_4d(sV + kKVHalf, &tmV, kv_full, 64, hk, n0, b);
+      }
+      int loaded = 0;
+      for (int t = 0; t < total; ++t) {
+        const int bb = t & 1;
+        const uint32_t use = (t >> 1) & 1;
+        const int h = hk * G + t / nqt;
+        const int q0 = (qt0 + t % nqt) * TQ3;
+        if (!__all_sync(0xffffffffu, mbar_wait(&qd_free[bb], use ^ 1, a.err, kErrTmaWait))) break;
+        const float* lse_row = a.lse + ((int64_t)b * a.H + h) * a.Sq;
+        const float* di_row = a.di + ((int64_t)b * a.H + h) * a.Sq;
+#pragma unroll
+        for (int i = 0; i < TQ3 / 32; ++i) {
+          const int c = i * 32 + lane, q = q0 + c;
+          sL[bb * TQ3 + c] = q < a.Sq ? lse_row[q] * kLog2e : 0.f;
+          sD[bb * TQ3 + c] = q < a.Sq ? di_row[q] : 0.f;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&qd_full[bb], 2 * kQ);
+          unsigned char* q_ = sQ + bb * kQ;
+          unsigned char* o_ = sdO + bb * kQ;
+          tma_load_4d(q_, &tmQ, &qd_full[bb], 0, h, q0, b);
+          tma_load_4d(q_ + kQHalf, &tmQ, &qd_full[bb], 64, h, q0, b);
+          tma_load_4d(o_, &tmdO, &qd_full[bb], 0, h, q0, b);
+          tma_load_4d(o_ + kQHalf, &tmdO, &qd_full[bb], 64, h, q0, b);
+        } else {
+          mbar_arrive(&qd_full[bb]);
+        }
+        ++loaded;
+      }
+      if (lane == 0) {
+        mbar_wait(kv_full, 0, nullptr, 0);
+        for (int i = 1; i <= 2 && i <= loaded; ++i) {
+          const int t = loaded - i;
+          mbar_wait(&qd_full[t & 1], (t >> 1) & 1, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0 && total > 0) {
+      constexpr uint32_t id_sdp = umma_idesc_f16_major(128, TQ3, true, false, false);  // K-major A, B
+      constexpr uint32_t id_acc = umma_idesc_f16_major(128, 128, true, false, true);   // A K-major, B MN-major
+      constexpr uint32_t id_dq = umma_idesc_f16_major(128, TQ3, true, true, true);     // both MN-major
+      const uint32_t k_ = smem_addr(sK), v_ = smem_addr(sV);
+      bool ok = mbar_wait(kv_full, 0, a.err, kErrMmaWait);
+      auto issue_sdp = [&](int t) -> bool {
+        const int bb = t & 1;
+        const uint32_t use = (t >> 1) & 1;
+        if (!mbar_wait(&qd_full[bb], use, a.err, kErrMmaWait)) return false;
+        if (t >= 2 && !mbar_wait(&dq_free[bb], use ^ 1, a.err, kErrMmaWait)) return false;  // dQ^T(t-2) read out
+        tc_fence_after();
+        const uint32_t q_ = smem_addr(sQ + bb * kQ), o_ = smem_addr(sdO + bb * kQ);
+        const uint32_t tS = tmem + bb * 128, tP = tS + 64;
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t ka = (k >> 2) * kKVHalf + (k & 3) * 32, kb = (k >> 2) * kQHalf + (k & 3) * 32;
+          umma_f16(tS, umma_desc_k_sw128(k_ + ka), umma_desc_k_sw128(q_ + kb), id_sdp, k != 0);
+          umma_f16(tP, umma_desc_k_sw128(v_ + ka), umma_desc_k_sw128(o_ + kb), id_sdp, k != 0);
+        }
+        umma_commit(&sdp_full[bb]);
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      for (int t = 0; t < total && ok; ++t) {
+        const int bb = t & 1;
+        const uint32_t use = (t >> 1) & 1;
+        if (t + 1 < total && !issue_sdp(t + 1)) { ok = false; break; }
+        if (!mbar_wait(&p_full[bb], use, a.err, kErrMmaWait)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t q_ = smem_addr(sQ + bb * kQ), o_ = smem_addr(sdO + bb * kQ);
+        const uint32_t pt_ = smem_addr(sPt + bb * kPT), ds_ = smem_addr(sdSt + bb * kPT);
+#pragma unroll
+        for (int k = 0; k < TQ3 / 16; ++k) {  // dV += P^T dO ; dK += dS^T Q
+          umma_f16(tdV, umma_desc_k_sw128(pt_ + k * 32), umma_desc_mn_sw128(o_ + k * 2048, kQHalf, 1024), id_acc,
+                   (t | k) != 0);
+          umma_f16(tdK, umma_desc_k_sw128(ds_ + k * 32), umma_desc_mn_sw128(q_ + k * 2048, kQHalf, 1024), id_acc,
+                   (t | k) != 0);
+        }
+        umma_commit(&qd_free[bb]);
+#pragma unroll
+        for (int k = 0; k < TK / 16; ++k)  // dQ^T = K^T dS^T  (into the consumed S^T_b columns)
+          umma_f16(tmem + bb * 128, umma_desc_mn_sw128(k_ + k * 2048, kKVHalf, 1024),
+                   umma_desc_mn_sw128(ds_ + k * 2048, kPT, 1024), id_dq, k != 0);
+        umma_commit(&dq_full[bb]);
+      }
+      umma_commit(acc_done);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else if (warp < 10) {
+    // ------------------------------------------------- softmax-gradient warps
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;  // key row within the tile (TMEM lane)
+    const int key = n0 + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int c0 = half * 32;
+    bool ok = true;
+    for (int t = 0; t < total && ok; ++t) {
+      const int bb = t & 1;
+      const uint32_t use = (t >> 1) & 1;
+      const int q0 = (qt0 + t % nqt) * TQ3;
+      if (!mbar_wait(&sdp_full[bb], use, a.err, kErrEpiWait) || !mbar_wait(&qd_full[bb], use, a.err, kErrEpiWait)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[32], dp[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + c0, reinterpret_cast<uint32_t*>(s));
+      tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + 64 + c0, reinterpret_cast<uint32_t*>(dp));
+      tmem_ld_wait();
+      const float* L = sL + bb * TQ3 + c0;
+      const float* Dd = sD + bb * TQ3 + c0;
+      uint32_t pp[16], dd[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        float pv[2], dv2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int q = q0 + c0 + i + e;
+          const bool valid = q < a.Sq && key < a.Skv && (!a.causal || key <= q + off);
+          const float p = valid ? fast_exp2(fmaf(s[i + e], a.scale_log2, -L[i + e])) : 0.f;
+          pv[e] = p;
+          dv2[e] = p * (dp[i + e] - Dd[i + e]);
+        }
+        pp[i / 2] = pack2(pv[0], pv[1]);
+        dd[i / 2] = pack2(dv2[0], dv2[1]);
+      }
+      unsigned char* pt = sPt + bb * kPT;
+      unsigned char* ds = sdSt + bb * kPT;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int ch = half * 4 + j;
+        const uint32_t so = row * 128 + ((ch ^ (row & 7)) * 16);
+        *reinterpret_cast<uint4*>(pt + so) = make_uint4(pp[j * 4], pp[j * 4 + 1], pp[j * 4 + 2], pp[j * 4 + 3]);
+        *reinterpret_cast<uint4*>(ds + so) = make_uint4(dd[j * 4], dd[j * 4 + 1], dd[j * 4 + 2], dd[j * 4 + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[bb]);
+    }
+    // ---------------------------------------------------------- dK, dV
+    const bool have = __all_sync(0xffffffffu, ok && total > 0 && mbar_wait(acc_done, 0, a.err, kErrEpiWait));
+    tc_fence_after();
+    const int cc = half * 64;
+    __nv_bfloat16* dkp = reinterpret_cast<__nv_bfloat16*>(a.dk) + (((int64_t)b * a.Skv + key) * a.Hkv + hk) * HD + cc;
+    __nv_bfloat16* dvp = reinterpret_cast<__nv_bfloat16*>(a.dv) + (((int64_t)b * a.Skv + key) * a.Hkv + hk) * HD + cc;
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      uint32_t rk[32], rv[32];
+      if (have) {
+        tmem_ld_32x32b_x32(tdK + lane_base + cc + c * 32, rk);
+        tmem_ld_32x32b_x32(tdV + lane_base + cc + c * 32, rv);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) rk[e] = rv[e] = 0u;
+      }
+      if (key >= a.Skv) continue;
+#pragma unroll
+      for (int e = 0; e < 32; e += 8) {
+        *reinterpret_cast<uint4*>(dkp + c * 32 + e) = make_uint4(
+            pack2(__uint_as_float(rk[e]) * a.scale, __uint_as_float(rk[e + 1]) * a.scale),
+            pack2(__uint_as_float(rk[e + 2]) * a.scale, __uint_as_float(rk[e + 3]) * a.scale),
+            pack2(__uint_as_float(rk[e + 4]) * a.scale, __uint_as_float(rk[e + 5]) * a.scale),
+            pack2(__uint_as_float(rk[e + 6]) * a.scale, __uint_as_float(rk[e + 7]) * a.scale));
+        *reinterpret_cast<uint4*>(dvp + c * 32 + e) = make_uint4(
+            pack2(__uint_as_float(rv[e]), __uint_as_float(rv[e + 1])),
+            pack2(__uint_as_float(rv[e + 2]), __uint_as_float(rv[e + 3])),
+            pack2(__uint_as_float(rv[e + 4]), __uint_as_float(rv[e + 5])),
+            pack2(__uint_as_float(rv[e + 6]), __uint_as_float(rv[e + 7])));
+      }
+    }
+  } else {
+    // ------------------------------------------------------- dQ epilogue
+    const int quarter = warp & 3;
+    const int d = quarter * 32 + lane;  // head-dim index (TMEM lane of dQ^T)
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    for (int t = 0; t < total; ++t) {
+      const int bb = t & 1;
+      const uint32_t use = (t >> 1) & 1;
+      const int h = hk * G + t / nqt;
+      const int q0 = (qt0 + t % nqt) * TQ3;
+      if (!mbar_wait(&dq_full[bb], use, a.err, kErrEpiWait)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + c * 32, r);
+        tmem_ld_wait();
+        float* dst = a.dq_acc + (((int64_t)b * a.Sq + q0 + c * 32) * a.H + h) * HD + d;
+        const int64_t qstride = (int64_t)a.H * HD;
+#pragma unroll 8
+        for (int e = 0; e < 32; ++e)
+          if (q0 + c * 32 + e < a.Sq) atomicAdd(dst + e * qstride, __uint_as_float(r[e]) * a.scale);
+      }
+      tc_fence_before();
+      mbar_arrive(&dq_free[bb]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ------------------------------------------------------------------ host
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -324,12 +626,12 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-CUtensorMap bshd_map(const at::Tensor& t) {
+CUtensorMap bshd_map(const at::Tensor& t, int box_rows = 128) {
   CUtensorMap m;
   const cuuint64_t dims[4] = {(cuuint64_t)t.size(3), (cuuint64_t)t.size(2), (cuuint64_t)t.size(1),
                               (cuuint64_t)t.size(0)};
   const cuuint64_t strides[3] = {(cuuint64_t)t.stride(2) * 2, (cuuint64_t)t.stride(1) * 2, (cuuint64_t)t.stride(0) * 2};
-  const cuuint32_t box[4] = {64, 1, 128, 1};
+  const cuuint32_t box[4] = {64, 1, (cuuint32_t)box_rows, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.data_ptr(), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -358,9 +660,20 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
   BwdArgs args{lse.data_ptr<float>(), di.data_ptr<float>(), dq_acc.data_ptr<float>(), dk.data_ptr(), dv.data_ptr(),
                (int)B, (int)H, (int)Hkv, (int)Sq, (int)Skv, causal ? 1 : 0, (float)scale, (float)scale * kLog2e,
                bwd_error_word(q.device())};
-  LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+  static const bool v2 = [] {
+    const char* e = std::getenv("LRB_ATTN_BWD_V3");
+    return !(e != nullptr && e[0] == '1');
+  }();
   dim3 grid((unsigned)((Skv + TK - 1) / TK), (unsigned)(B * Hkv));
-  attn_bwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, tdo, args);
+  if (v2) {  // 128-query tiles, serial per tile (kept for A/B comparisons)
+    LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+    attn_bwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, tdo, args);
+  } else {
+    CUtensorMap tq64 = bshd_map(q, bwd3::TQ3), tdo64 = bshd_map(dout, bwd3::TQ3);
+    LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_v3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)bwd3::kSmem));
+    attn_bwd_v3_kernel<<<grid, bwd3::kThreads, bwd3::kSmem, stream()>>>(tq64, tk, tv, tdo64, args);
+  }
   LRB_LAUNCH_CHECK();
 }
 

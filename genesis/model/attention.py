@@ -28,7 +28,7 @@ import torch.nn.functional as F
 
 from genesis.model.rotary import apply_rotary_emb
 from llm_research_b200 import ops
-from llm_research_b200.ops.linear import cat_rows
+from llm_research_b200.ops.linear import cat_rows, project
 
 # The reference probes flash-attn here; the fused kernel replaces it.
 FLASH_ATTN_AVAILABLE = True
@@ -65,7 +65,7 @@ class MultiHeadAttention(nn.Module):
         b = None
         if self.q_proj.bias is not None:
             b = torch.cat([self.q_proj.bias, self.k_proj.bias, self.v_proj.bias], 0)
-        return F.linear(x, w, b)
+        return project(x, w, b)
 
     def forward(
         self,
@@ -84,7 +84,7 @@ class MultiHeadAttention(nn.Module):
         drop = self.dropout_p if self.training else 0.0
         if kv_cache is None and attention_mask is None and drop == 0.0:
             out = ops.attention(q, k, v, causal=True)
-            return self.o_proj(out.reshape(B, S, H * D))
+            return project(out.reshape(B, S, H * D), self.o_proj.weight, self.o_proj.bias)
 
         # General path: cache / additive mask / dropout.
         qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
@@ -92,12 +92,12 @@ class MultiHeadAttention(nn.Module):
             kh, vh = kv_cache.update(kh, vh)
         if attention_mask is None and drop == 0.0:
             out = ops.attention(qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2), causal=True)
-            return self.o_proj(out.reshape(B, S, H * D))
+            return project(out.reshape(B, S, H * D), self.o_proj.weight, self.o_proj.bias)
         if self.num_kv_groups > 1:
             kh = kh.repeat_interleave(self.num_kv_groups, dim=1)
             vh = vh.repeat_interleave(self.num_kv_groups, dim=1)
         out = self._vanilla_attention(qh, kh, vh, attention_mask)
-        return self.o_proj(out.transpose(1, 2).reshape(B, S, H * D))
+        return project(out.transpose(1, 2).reshape(B, S, H * D), self.o_proj.weight, self.o_proj.bias)
 
     def _vanilla_attention(
         self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, attention_mask: Optional[torch.Tensor] = None

@@ -13,7 +13,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from llm_research_b200 import ops
-from llm_research_b200.ops.linear import cat_rows
+from llm_research_b200.ops.linear import cat_rows, project
 
 
 def default_ffn_dim(d_model: int) -> int:
@@ -36,6 +36,6 @@ class SwiGLUFFN(nn.Module):
         b = None
         if self.w1.bias is not None:
             b = torch.cat([self.w1.bias, self.w_gate.bias], 0)
-        gu = F.linear(x, w, b)  # [..., up | gate]
+        gu = project(x, w, b)  # [..., up | gate]
         h = ops.swiglu(gu)
-        return self.w2(self.dropout(h))
+        return project(self.dropout(h), self.w2.weight, self.w2.bias)

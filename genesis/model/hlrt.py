@@ -55,6 +55,12 @@ class HLRTConfig:
     tier1_use_flash_attention: bool = True
     tier1_max_seq_len: int = 8192
     tier1_rope_base: float = 10000.0
+    # Tier-1 mixture of experts (an extension: the reference trunk is dense)
+    tier1_moe_num_experts: int | None = None
+    tier1_moe_top_k: int = 2
+    tier1_moe_d_ff: int | None = None
+    tier1_moe_shared_experts: int = 0
+    tier1_moe_capacity_factor: float = 1.25
 
     gate1_chunk_size: int = 32
     gate1_threshold: float = 0.5
@@ -108,6 +114,9 @@ class HLRT(StatefulModule):
             num_kv_heads=c.tier1_num_kv_heads, dropout=c.tier1_dropout,
             use_flash_attention=c.tier1_use_flash_attention, max_seq_len=c.tier1_max_seq_len,
             rope_base=c.tier1_rope_base, norm_eps=c.norm_eps,
+            moe=(dict(num_experts=c.tier1_moe_num_experts, top_k=c.tier1_moe_top_k, d_ff=c.tier1_moe_d_ff,
+                      shared=c.tier1_moe_shared_experts, capacity_factor=c.tier1_moe_capacity_factor)
+                 if c.tier1_moe_num_experts else None),
         )
         self.gate1 = TierGate(d_model=c.d_model, chunk_size=c.gate1_chunk_size, threshold=c.gate1_threshold)
         self.latent_pool = LatentPooling(
@@ -189,6 +198,9 @@ class HLRT(StatefulModule):
             acts["gate1_scores"] = g1_scores
         sel1 = g1_mask if g1_mask.dtype == torch.bool else g1_mask > 0.5
         aux = self.config.gate_loss_weight * self.gate1.load_balance_loss()
+        if self.config.tier1_moe_num_experts:
+            for layer in self.tier1.layers:
+                aux = aux + self.config.moe_loss_weight * layer.ffn.load_balance_loss().to(aux.device)
 
         if bool(sel1.any()):
             latents = self.latent_pool(t1, g1_mask)

@@ -46,6 +46,7 @@ class MoEFFN(nn.Module):
         dropout: float = 0.0,
         jitter_noise: float = 0.0,
         enforce_capacity: bool = False,
+        num_shared_experts: int = 0,
     ) -> None:
         super().__init__()
         self.d_model = d_model
@@ -55,6 +56,9 @@ class MoEFFN(nn.Module):
         self.enforce_capacity = enforce_capacity
         self.router = ExpertRouter(d_model=d_model, num_experts=num_experts, top_k=top_k, jitter_noise=jitter_noise)
         self.experts = nn.ModuleList([SwiGLUFFN(d_model=d_model, d_ff=d_ff, dropout=dropout) for _ in range(num_experts)])
+        # always-on experts added to every token (DeepSeek-style shared experts); none in the reference
+        self.shared_experts = nn.ModuleList([SwiGLUFFN(d_model=d_model, d_ff=d_ff, dropout=dropout)
+                                             for _ in range(num_shared_experts)])
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
@@ -64,6 +68,8 @@ class MoEFFN(nn.Module):
             cap = math.ceil(self.capacity_factor * xf.shape[0] * self.top_k / self.num_experts)
             w = w * capacity_mask(idx, self.num_experts, cap).to(w.dtype)
         out = grouped_expert_apply(xf, idx, w, self.experts, self.num_experts)
+        for e in self.shared_experts:
+            out = out + e(xf)
         return out.to(x.dtype).reshape(shape)
 
     def load_balance_loss(self) -> torch.Tensor:

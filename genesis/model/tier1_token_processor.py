@@ -29,8 +29,10 @@ class TransformerBlock(nn.Module):
         dropout: float = 0.0,
         use_flash_attention: bool = True,
         norm_eps: float = 1e-6,
+        moe: Optional[dict] = None,
     ) -> None:
         super().__init__()
+        self._moe = moe
         self.attn_norm = RMSNorm(d_model, eps=norm_eps)
         self.attn = MultiHeadAttention(
             d_model=d_model, num_heads=num_heads, num_kv_heads=num_kv_heads,
@@ -40,6 +42,20 @@ class TransformerBlock(nn.Module):
         self.ffn = self._make_ffn(d_model, d_ff, dropout)
 
     def _make_ffn(self, d_model: int, d_ff: int | None, dropout: float) -> nn.Module:
+        moe = getattr(self, "_moe", None)
+        if moe:
+            from genesis.model.moe import MoEFFN
+            from llm_research_b200.parallel.expert_parallel import ExpertParallelMoE, current_expert_parallel
+
+            ep = current_expert_parallel()
+            if ep is not None:  # this rank's experts only
+                return ExpertParallelMoE(d_model, moe.get("d_ff") or d_ff, moe["num_experts"], top_k=moe.get("top_k", 2),
+                                         capacity_factor=moe.get("capacity_factor", 1.25), group=ep[0],
+                                         shared_expert=moe.get("shared", 0) > 0, comm=ep[1])
+
+            return MoEFFN(d_model=d_model, d_ff=moe.get("d_ff") or d_ff, num_experts=moe["num_experts"],
+                          top_k=moe.get("top_k", 2), capacity_factor=moe.get("capacity_factor", 1.25),
+                          dropout=dropout, enforce_capacity=True, num_shared_experts=moe.get("shared", 0))
         return SwiGLUFFN(d_model=d_model, d_ff=d_ff, dropout=dropout)
 
     def forward(
@@ -70,13 +86,14 @@ class Tier1TokenProcessor(nn.Module):
         max_seq_len: int = 8192,
         rope_base: float = 10000.0,
         norm_eps: float = 1e-6,
+        moe: Optional[dict] = None,
     ) -> None:
         super().__init__()
         self.rotary_emb = RotaryEmbedding(dim=d_model // num_heads, max_seq_len=max_seq_len, base=rope_base)
         self.layers = nn.ModuleList([
             TransformerBlock(
                 d_model=d_model, num_heads=num_heads, d_ff=d_ff, num_kv_heads=num_kv_heads,
-                dropout=dropout, use_flash_attention=use_flash_attention, norm_eps=norm_eps,
+                dropout=dropout, use_flash_attention=use_flash_attention, norm_eps=norm_eps, moe=moe,
             )
             for _ in range(num_layers)
         ])

@@ -8,6 +8,12 @@
                    projections and integration) still runs every step.
 ``genesis-7b``  -- 32 layers, d_model 4096, 32 query / 8 KV heads, ffn 11008,
                    vocab 32000, same tier layout.
+``genesis-7b-nvfp4`` -- genesis-7b, trained with NVFP4 linears (set by the
+                   trainer / bench with ``--precision nvfp4``).
+``genesis-40b-moe`` -- 32 layers, d_model 4096, 32 / 8 heads, vocab 32000,
+                   every Tier-1 FFN a mixture of 16 routed SwiGLU experts
+                   (ffn 6144, top-2 softmax routing, capacity 1.25) plus one
+                   shared expert: ~42B parameters, ~8.6B active per token.
 ``tiny``        -- the CPU plumbing configuration: vocab 32000, d_model 256,
                    every tier 4 layers / 4 heads / ffn 1024, Tier-3
                    recurrence 2.
@@ -45,9 +51,20 @@ def _trunk(vocab: int, d: int, layers: int, heads: int, kv_heads: int | None, ff
     )
 
 
+def _moe_trunk(c: HLRTConfig, experts: int, top_k: int, d_ff: int, shared: int, cap: float) -> HLRTConfig:
+    c.tier1_moe_num_experts = experts
+    c.tier1_moe_top_k = top_k
+    c.tier1_moe_d_ff = d_ff
+    c.tier1_moe_shared_experts = shared
+    c.tier1_moe_capacity_factor = cap
+    return c
+
+
 PRESETS: Dict[str, Callable[[], HLRTConfig]] = {
     "genesis-1b": lambda: _trunk(32000, 2048, 24, 16, None, 5632, 4096),
     "genesis-7b": lambda: _trunk(32000, 4096, 32, 32, 8, 11008, 4096),
+    "genesis-7b-nvfp4": lambda: _trunk(32000, 4096, 32, 32, 8, 11008, 4096),
+    "genesis-40b-moe": lambda: _moe_trunk(_trunk(32000, 4096, 32, 32, 8, 6144, 4096), 16, 2, 6144, 1, 1.25),
     "tiny": lambda: HLRTConfig(
         vocab_size=32000, d_model=256,
         tier1_num_layers=4, tier1_num_heads=4, tier1_d_ff=1024,
@@ -77,6 +94,10 @@ def count_flops_per_token(cfg: HLRTConfig, seq_len: int) -> float:
     hd = d // cfg.tier1_num_heads
     ffn = cfg.tier1_d_ff or ((int(8 / 3 * d) + 255) // 256) * 256
     per_layer = d * d * 2 + 2 * d * hkv * hd + 3 * d * ffn
+    if cfg.tier1_moe_num_experts:  # active parameters: top-k routed + shared experts, and the router
+        mff = cfg.tier1_moe_d_ff or ffn
+        per_layer = (d * d * 2 + 2 * d * hkv * hd + 3 * d * mff * (cfg.tier1_moe_top_k + cfg.tier1_moe_shared_experts)
+                     + d * cfg.tier1_moe_num_experts)
     matmul_params = L * per_layer + cfg.vocab_size * d
     attn = L * 2 * 2 * seq_len * d / 2  # QK^T and PV, causal half, per token (fwd)
     return 6.0 * matmul_params + 3.0 * attn

@@ -51,3 +51,83 @@ def cat_rows(*ws: torch.Tensor) -> torch.Tensor:
         return ws[0].as_strided((sum(w.shape[0] for w in ws), ws[0].shape[1]), (ws[0].shape[1], 1)) \
             if _adjacent(ws) else torch.cat(ws, 0)
     return _CatRows.apply(*ws)
+
+
+# ------------------------------------------------------------ linear precision
+# The model's projections call ``project``; the process-wide precision decides
+# whether it is a bf16 GEMM or an NVFP4 block-scaled training GEMM.
+import contextlib
+import itertools
+
+import torch.nn.functional as F
+
+_PRECISION = "bf16"
+_SEEDS = itertools.count(1)
+
+
+def set_linear_precision(precision: str) -> None:
+    """``"bf16"`` (default) or ``"nvfp4"``."""
+    global _PRECISION
+    if precision not in ("bf16", "nvfp4"):
+        raise ValueError(f"unknown linear precision {precision!r}")
+    _PRECISION = precision
+
+
+def get_linear_precision() -> str:
+    return _PRECISION
+
+
+@contextlib.contextmanager
+def linear_precision(precision: str):
+    old = _PRECISION
+    set_linear_precision(precision)
+    try:
+        yield
+    finally:
+        set_linear_precision(old)
+
+
+class _NVFP4LinearFn(torch.autograd.Function):
+    """y = x W^T with NVFP4 operands (E2M1, e4m3 per 16 elements, fp32 per tensor).
+
+    Forward rounds to nearest; the backward GEMMs (dX = dY W, dW = dY^T X) use
+    stochastic rounding on the gradient operand, so the gradient is unbiased
+    in expectation.  All three GEMMs run on the tcgen05 block-scaled kernel."""
+
+    @staticmethod
+    def forward(ctx, x2d, w):
+        from llm_research_b200.ops.quant import NVFP4Tensor, matmul_nvfp4
+
+        ctx.save_for_backward(x2d, w)
+        return matmul_nvfp4(NVFP4Tensor.quantize(x2d), NVFP4Tensor.quantize(w))
+
+    @staticmethod
+    def backward(ctx, dy):
+        from llm_research_b200.ops.quant import NVFP4Tensor, matmul_nvfp4
+
+        x2d, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        seed = next(_SEEDS)
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = matmul_nvfp4(NVFP4Tensor.quantize(dy, stochastic=True, seed=seed),
+                              NVFP4Tensor.quantize(w.t().contiguous()))
+        if ctx.needs_input_grad[1]:
+            dw = matmul_nvfp4(NVFP4Tensor.quantize(dy.t().contiguous(), stochastic=True, seed=seed + 1),
+                              NVFP4Tensor.quantize(x2d.t().contiguous()))
+        return dx, dw
+
+
+def _fp4_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
+    T = x.numel() // x.shape[-1]
+    return (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and w.shape[1] % 256 == 0
+            and w.shape[0] % 256 == 0 and T % 256 == 0)
+
+
+def project(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.linear`` under the current linear precision (NVFP4 where the shapes allow it:
+    K, N and the token count multiples of 256; bf16 otherwise)."""
+    if _PRECISION == "nvfp4" and _fp4_ok(x, w):
+        y = _NVFP4LinearFn.apply(x.reshape(-1, x.shape[-1]), w).view(*x.shape[:-1], w.shape[0])
+        return y + b if b is not None else y
+    return F.linear(x, w, b)

@@ -65,6 +65,7 @@ class ShardedHybridOptimizer:
         self.param_groups: List[Dict[str, Any]] = [dict(self.defaults, params=[i.param for i in engine.params])]
         self.hybrid = _is_hybrid(optimizer_cls)
         self.state: Dict[Any, Any] = {}
+        self.local_momentum: Dict[str, torch.Tensor] = {}
         world, rank = engine.world, engine.rank
         self.world, self.rank = world, rank
         dev = engine.device
@@ -75,7 +76,7 @@ class ShardedHybridOptimizer:
             for u in engine.units:
                 p = torch.nn.Parameter(u.master, requires_grad=True)
                 self._flat.append(p)
-            self.inner = optimizer_cls(self._flat, **self.defaults)
+            self.inner = optimizer_cls(self._flat + [p for _, p in engine.local_params], **self.defaults)
             self.param_groups = self.inner.param_groups
             return
 
@@ -214,8 +215,26 @@ class ShardedHybridOptimizer:
 
         if self.muon_ids and any(p in active for p in self.muon_ids):
             self._muon_step(lr_m, mu, wd_m, ns_steps, active)
+        self._step_local(lr_m, mu, wd_m, ns_steps)
         eng.refresh()
         return loss
+
+    def _step_local(self, lr: float, mu: float, wd: float, ns_steps: int) -> None:
+        """Muon on the engine's rank-local parameters (expert-parallel experts):
+        every 2-D slice (one expert's matrix) gets its Nesterov direction, one
+        batched Newton-Schulz per parameter orthogonalises all its experts at once."""
+        for name, p in self.engine.local_params:
+            if p.grad is None:
+                continue
+            mats = [p] if p.dim() == 2 else list(p.reshape(-1, p.shape[-2], p.shape[-1]).unbind(0))
+            grads = [p.grad] if p.dim() == 2 else list(p.grad.reshape(-1, p.shape[-2], p.shape[-1]).unbind(0))
+            buf = self.local_momentum.get(name)
+            if buf is None:
+                buf = self.local_momentum[name] = torch.zeros_like(p, dtype=torch.float32)
+            bufs = [buf] if p.dim() == 2 else list(buf.reshape(-1, p.shape[-2], p.shape[-1]).unbind(0))
+            outs, gnorm = ops.muon_prologue(mats, grads, bufs, lr, mu, wd)
+            orth = ops.newton_schulz(torch.stack(outs), steps=ns_steps)
+            ops.muon_epilogue(mats, list(orth.unbind(0)), gnorm, lr)
 
     def _muon_step(self, lr: float, mu: float, wd: float, ns_steps: int, active) -> None:
         eng, units, dev = self.engine, self.engine.units, self.engine.device

@@ -25,6 +25,7 @@ heap) the same layout is exchanged with ``all_to_all_single`` (the baseline).
 
 from __future__ import annotations
 
+import contextlib
 import math
 from typing import Optional, Tuple
 
@@ -35,6 +36,26 @@ import torch.nn.functional as F
 
 from llm_research_b200 import ops
 from llm_research_b200._ext import native
+
+
+_EP_CONTEXT = None
+
+
+@contextlib.contextmanager
+def expert_parallel(group: Optional[dist.ProcessGroup], comm: Optional["EPComm"] = None):
+    """Models built inside this context give their MoE FFNs expert parallelism
+    over ``group`` (each rank allocates only its own experts)."""
+    global _EP_CONTEXT
+    old = _EP_CONTEXT
+    _EP_CONTEXT = (group, comm)
+    try:
+        yield
+    finally:
+        _EP_CONTEXT = old
+
+
+def current_expert_parallel():
+    return _EP_CONTEXT
 
 
 def make_route(idx: torch.Tensor, experts_per_rank: int, num_experts: int, cap: int
@@ -197,6 +218,9 @@ class ExpertParallelMoE(nn.Module):
         nn.init.normal_(self.router.weight, std=0.02)
         nn.init.normal_(self.w_up_gate, std=0.02)
         nn.init.normal_(self.w_down, std=0.02 / math.sqrt(2.0))
+        # this rank's experts: not sharded or reduced by the data-parallel engine
+        self.w_up_gate._lrb_local = True
+        self.w_down._lrb_local = True
         self.shared = None
         if shared_expert:
             from genesis.model.ffn import SwiGLUFFN
@@ -205,9 +229,12 @@ class ExpertParallelMoE(nn.Module):
         self.last_aux: Optional[torch.Tensor] = None
 
     def experts(self, x_e: torch.Tensor) -> torch.Tensor:
-        gu = torch.bmm(x_e, self.w_up_gate.transpose(1, 2))           # (epl, rows, 2*d_ff) = [up | gate]
+        gu = torch.bmm(x_e, self.w_up_gate.to(x_e.dtype).transpose(1, 2))  # (epl, rows, 2*d_ff) = [up | gate]
         h = ops.swiglu(gu.reshape(-1, gu.shape[-1])).view(gu.shape[0], gu.shape[1], -1)
-        return torch.bmm(h, self.w_down.transpose(1, 2))
+        return torch.bmm(h, self.w_down.to(h.dtype).transpose(1, 2))
+
+    def load_balance_loss(self) -> torch.Tensor:
+        return self.last_aux if self.last_aux is not None else torch.zeros((), device=self.router.weight.device)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape

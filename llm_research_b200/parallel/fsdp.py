@@ -190,11 +190,18 @@ class FlatShardEngine(nn.Module):
                 for pname, p in mod.named_parameters(recurse=True):
                     owner.setdefault(id(p), u)
         self.params: List[ParamInfo] = []
+        # Rank-local parameters (expert-parallel experts, marked ``_lrb_local``)
+        # are not sharded: they stay ordinary parameters whose gradients autograd
+        # accumulates in ``.grad``; the optimizer steps them on their rank.
+        self.local_params: List[Tuple[str, nn.Parameter]] = []
         seen: Set[int] = set()
         for idx, (name, p) in enumerate(self.module.named_parameters()):
             if id(p) in seen:
                 continue
             seen.add(id(p))
+            if getattr(p, "_lrb_local", False):
+                self.local_params.append((name, p))
+                continue
             u = self.units[owner.get(id(p), 0)]
             info = ParamInfo(name=name, param=p, unit=u.index, offset=u.total, shape=tuple(p.shape),
                              numel=p.numel(), index=len(self.params))
@@ -498,12 +505,17 @@ class FlatShardEngine(nn.Module):
             sq = torch.zeros((), dtype=torch.float32, device=self.device)
             for u in self.units:
                 sq += u.grad_shard.float().pow(2).sum()
+        local = [p.grad for _, p in self.local_params if p.grad is not None]
+        for gr in local:  # disjoint per rank, like the shards: one sum over the group covers both
+            sq += gr.float().pow(2).sum()
         if self.world > 1:
             dist.all_reduce(sq, group=self.pg)
         norm = sq.sqrt()
         coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
         for u in self.units:
             u.grad_shard.mul_(coef)
+        for gr in local:
+            gr.mul_(coef.to(gr.dtype))
         return norm
 
     @torch.no_grad()
@@ -535,6 +547,8 @@ class FlatShardEngine(nn.Module):
     @torch.no_grad()
     def zero_grad(self) -> None:
         self._touched.clear()
+        for _, p in self.local_params:
+            p.grad = None
         if self._sumsq is not None:
             self._sumsq.zero_()
         for u in self.units:

@@ -32,3 +32,48 @@ def test_nvfp4_scale_swizzle_round_trip():
             mm = m % 128
             off = (blk * (KB // 4) + kb) * 512 + 16 * (mm % 32) + 4 * (mm // 32) + jj
             assert int(at[off]) == int(s[m, j])
+
+
+@pytest.mark.gpu
+def test_nvfp4_linear_forward_backward_close_to_bf16():
+    """The NVFP4 training linear (RNE forward, stochastic-rounding backward) against bf16."""
+    from llm_research_b200.ops.linear import linear_precision, project
+
+    torch.manual_seed(0)
+    x = torch.randn(512, 1024, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(768, 1024, device="cuda") * 0.03).to(torch.bfloat16).requires_grad_()
+    dy = torch.randn(512, 768, device="cuda", dtype=torch.bfloat16)
+    y_ref = torch.nn.functional.linear(x.float(), w.float())
+    gx_ref, gw_ref = torch.autograd.grad(y_ref, (x, w), dy.float())
+    with linear_precision("nvfp4"):
+        y = project(x, w)
+    gx, gw = torch.autograd.grad(y, (x, w), dy)
+    rel = lambda a, b: ((a.float() - b.float()).norm() / b.float().norm()).item()
+    assert rel(y, y_ref) < 0.15
+    assert rel(gx, gx_ref) < 0.2
+    assert rel(gw, gw_ref) < 0.2
+
+
+@pytest.mark.gpu
+def test_hlrt_trains_with_nvfp4_linears():
+    from genesis.model import HLRT, HLRTConfig
+    from llm_research_b200.ops.linear import linear_precision
+
+    torch.manual_seed(0)
+    cfg = HLRTConfig(vocab_size=1024, d_model=256, tier1_num_layers=2, tier1_num_heads=2, tier1_d_ff=512,
+                     gate1_chunk_size=16, num_latent_vectors=4, latent_pool_num_heads=2, tier2_d_model=256,
+                     tier2_num_layers=1, tier2_num_heads=2, tier2_d_ff=512, tier3_d_model=256, tier3_num_layers=1,
+                     tier3_num_heads=2, tier3_d_ff=512)
+    model = HLRT(cfg).cuda().to(torch.bfloat16)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3)
+    ids = torch.randint(0, 1024, (2, 256), device="cuda")
+    losses = []
+    with linear_precision("nvfp4"):
+        for _ in range(6):
+            out = model(ids)
+            loss = torch.nn.functional.cross_entropy(out["logits"][:, :-1].float().reshape(-1, 1024), ids[:, 1:].reshape(-1))
+            loss.backward()
+            opt.step()
+            opt.zero_grad()
+            losses.append(float(loss))
+    assert all(l == l for l in losses) and losses[-1] < losses[0]
