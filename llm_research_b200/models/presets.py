@@ -14,6 +14,7 @@
                    every Tier-1 FFN a mixture of 16 routed SwiGLU experts
                    (ffn 6144, top-2 softmax routing, capacity 1.25) plus one
                    shared expert: ~42B parameters, ~8.6B active per token.
+``genesis-40b-moe-2l`` -- two layers of genesis-40b-moe, for quick checks.
 ``tiny``        -- the CPU plumbing configuration: vocab 32000, d_model 256,
                    every tier 4 layers / 4 heads / ffn 1024, Tier-3
                    recurrence 2.
@@ -65,6 +66,8 @@ PRESETS: Dict[str, Callable[[], HLRTConfig]] = {
     "genesis-7b": lambda: _trunk(32000, 4096, 32, 32, 8, 11008, 4096),
     "genesis-7b-nvfp4": lambda: _trunk(32000, 4096, 32, 32, 8, 11008, 4096),
     "genesis-40b-moe": lambda: _moe_trunk(_trunk(32000, 4096, 32, 32, 8, 6144, 4096), 16, 2, 6144, 1, 1.25),
+    # two layers of genesis-40b-moe (same layer shapes), for quick multi-GPU checks
+    "genesis-40b-moe-2l": lambda: _moe_trunk(_trunk(32000, 4096, 2, 32, 8, 6144, 4096), 16, 2, 6144, 1, 1.25),
     "tiny": lambda: HLRTConfig(
         vocab_size=32000, d_model=256,
         tier1_num_layers=4, tier1_num_heads=4, tier1_d_ff=1024,
