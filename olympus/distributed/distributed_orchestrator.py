@@ -44,6 +44,18 @@ def _is_engine(model: nn.Module) -> bool:
     return isinstance(model, FlatShardEngine)
 
 
+def _engine_extra_state(engine) -> Dict[str, Any]:
+    """Persistent buffers and Olympus state extras of an engine-wrapped model (host copies)."""
+    out: Dict[str, Any] = {}
+    inner = engine.module
+    for bname, buf in inner.named_buffers():
+        if not any(bname.endswith(x) for x in ("inv_freq", "cos_cached", "sin_cached")) and "_state_buf_" not in bname:
+            out[bname] = buf.detach().cpu().clone()
+    if isinstance(inner, StatefulModule):
+        out.update(inner.olympus_extras())
+    return out
+
+
 class DistributedTrainingOrchestrator(TrainingOrchestrator):
     def __init__(
         self,
@@ -103,12 +115,7 @@ class DistributedTrainingOrchestrator(TrainingOrchestrator):
         for name, cfg in self._models.items():
             if _is_engine(cfg.model):
                 state: Dict[str, Any] = dict(cfg.model.full_state_dict())
-                inner = cfg.model.module
-                for bname, buf in inner.named_buffers():
-                    if not any(bname.endswith(x) for x in ("inv_freq", "cos_cached", "sin_cached")) and "_state_buf_" not in bname:
-                        state[bname] = buf.detach().cpu().clone()
-                if isinstance(inner, StatefulModule):
-                    state.update(inner.olympus_extras())
+                state.update(_engine_extra_state(cfg.model))
                 ckpt["models"][name] = state
             elif isinstance(cfg.model, StatefulModule):
                 ckpt["models"][name] = cfg.model.state_dict_with_state()
@@ -122,6 +129,56 @@ class DistributedTrainingOrchestrator(TrainingOrchestrator):
             logger.info("Checkpoint saved to %s (step %d)", path, self._global_step)
         if dist.is_initialized():
             dist.barrier()
+
+    def save_sharded_checkpoint(self, directory: str, asynchronous: bool = True) -> None:
+        """Every rank writes its own parameter and optimizer shards (``{directory}/{model}/rank*.pt``)
+        from a background thread; rank 0 writes ``header.pt`` (step, phase, memory bus, schedulers,
+        models not wrapped by the engine). ``llm_research_b200.parallel.checkpoint.consolidate_checkpoint``
+        turns the directory into the single-file layout that ``load_checkpoint`` reads."""
+        from llm_research_b200.parallel import checkpoint as ck
+
+        ck.wait()  # one checkpoint in flight at a time
+        head = self._checkpoint_dict()
+        head["world_size"] = dist.get_world_size() if dist.is_initialized() else self.world_size
+        head["sharded"] = []
+        for name, cfg in self._models.items():
+            if _is_engine(cfg.model):
+                ck.save_sharded(cfg.model, cfg.optimizer, os.path.join(directory, name),
+                                header={"buffers": _engine_extra_state(cfg.model)}, asynchronous=asynchronous)
+                head["sharded"].append(name)
+            else:
+                head["models"][name] = (cfg.model.state_dict_with_state() if isinstance(cfg.model, StatefulModule)
+                                        else cfg.model.state_dict())
+                head["optimizers"][name] = cfg.optimizer.state_dict()
+            if cfg.scheduler is not None and hasattr(cfg.scheduler, "state_dict"):
+                head["schedulers"][name] = cfg.scheduler.state_dict()
+        if self.is_main_rank:
+            os.makedirs(directory, exist_ok=True)
+            torch.save(head, os.path.join(directory, "header.pt"))
+        if not asynchronous and dist.is_initialized():
+            dist.barrier()
+
+    def load_sharded_checkpoint(self, directory: str) -> Dict[str, Any]:
+        from llm_research_b200.parallel import checkpoint as ck
+
+        ck.wait()
+        if dist.is_initialized():
+            dist.barrier()  # every rank's writer has finished
+        head = torch.load(os.path.join(directory, "header.pt"), map_location="cpu", weights_only=False)
+        self._restore_header(head)
+        for name, cfg in self._models.items():
+            if name in head["sharded"]:
+                sub = ck.load_sharded(cfg.model, cfg.optimizer, os.path.join(directory, name))
+                extras = {k: v for k, v in sub.get("buffers", {}).items() if k.startswith("_olympus_")}
+                inner = cfg.model.module
+                if isinstance(inner, StatefulModule) and extras:
+                    inner.restore_olympus_extras(extras)
+            elif name in head["models"]:
+                load_model_state(cfg.model, head["models"][name], strict=True)
+                cfg.optimizer.load_state_dict(head["optimizers"][name])
+            if cfg.scheduler is not None and name in head.get("schedulers", {}):
+                cfg.scheduler.load_state_dict(head["schedulers"][name])
+        return head
 
     def load_checkpoint(self, path: str, strict: bool = True) -> Dict[str, Any]:
         ckpt = torch.load(path, map_location="cpu", weights_only=False)

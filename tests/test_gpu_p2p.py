@@ -122,3 +122,31 @@ def test_engine_p2p_matches_nccl():
         assert abs(la - lb) < 2e-2 * abs(la), (a[0][0], b[0][0])
     for k in a[0][1]:
         torch.testing.assert_close(a[0][1][k], b[0][1][k], atol=5e-3, rtol=5e-2)
+
+
+def _diloco(rank, world, comm):
+    from llm_research_b200.parallel.diloco import DiLoCo, DiLoCoConfig, make_diloco_groups
+
+    dev = torch.device("cuda", rank)
+    _, rg, ranks, _ = make_diloco_groups(world)
+    g = torch.Generator(device=dev).manual_seed(0)
+    shards = [torch.randn(5000, device=dev, generator=g), torch.randn(300, 7, device=dev, generator=g)]
+    dl = DiLoCo(shards, rg, ranks, DiLoCoConfig(inner_steps=1, comm=comm))
+    assert dl.comm == comm
+    for step in range(3):
+        for s in shards:
+            s.add_(0.01 * (rank + 1) * (step + 1))
+        dl.step()
+    out = dl.anchor[: dl.numel].cpu().clone()
+    dl.close()
+    return out
+
+
+@needs2
+def test_diloco_p2p_outer_step_matches_collective():
+    world = min(torch.cuda.device_count(), 4)
+    a = run_ranks(_diloco, world, "collective", backend="nccl")
+    b = run_ranks(_diloco, world, "p2p", backend="nccl")
+    for r in range(world):
+        torch.testing.assert_close(a[r], a[0])
+        torch.testing.assert_close(b[r], a[r], atol=1e-5, rtol=1e-5)
