@@ -38,6 +38,8 @@ at::Tensor newton_schulz(const at::Tensor&, int64_t, double, double, double);
 std::tuple<at::Tensor, at::Tensor> int4_quantize(const at::Tensor&, int64_t);
 at::Tensor int4_dequantize(const at::Tensor&, const at::Tensor&, int64_t);
 std::tuple<at::Tensor, at::Tensor, at::Tensor> nvfp4_quantize(const at::Tensor&, bool, int64_t);
+std::vector<at::Tensor> nvfp4_quantize_dual(const at::Tensor&, const c10::optional<at::Tensor>&, bool, bool, bool,
+                                            int64_t);
 at::Tensor nvfp4_dequantize(const at::Tensor&, const at::Tensor&, const at::Tensor&, at::ScalarType);
 // attention.cu
 std::tuple<at::Tensor, at::Tensor> attn_fwd(const at::Tensor&, const at::Tensor&, const at::Tensor&, bool, double);
@@ -116,6 +118,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("int4_quantize", &lrb::int4_quantize);
   m.def("int4_dequantize", &lrb::int4_dequantize);
   m.def("nvfp4_quantize", &lrb::nvfp4_quantize);
+  m.def("nvfp4_quantize_dual", &lrb::nvfp4_quantize_dual, "x (M,K) -> row-wise and/or transposed NVFP4 with atom-layout scales",
+        py::arg("x"), py::arg("amax") = py::none(), py::arg("rowwise") = true, py::arg("colwise") = true,
+        py::arg("stochastic") = false, py::arg("seed") = 0);
   m.def("nvfp4_dequantize", &lrb::nvfp4_dequantize);
   m.def("attn_fwd", &lrb::attn_fwd);
   m.def("attn_bwd", &lrb::attn_bwd);

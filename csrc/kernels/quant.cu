@@ -129,6 +129,119 @@ __global__ void nvfp4_quant_kernel(const T* __restrict__ x, const float* __restr
   for (int i = 0; i < 8; ++i) packed[b * 8 + i] = out[i];
 }
 
+
+// E2M1 code of a magnitude, round to nearest with ties to the even code: the
+// midpoints between grid values are 0.25 0.75 1.25 1.75 2.5 3.5 5; a tie at a
+// midpoint goes to the even code (0, 2, 2, 4, 4, 6, 6), which makes the
+// comparisons alternate between strict and non-strict.
+__device__ __forceinline__ int e2m1_rne_fast(float a) {
+  return (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) + (a >= 3.5f) + (a > 5.f);
+}
+
+__device__ __forceinline__ int e2m1_sr_fast(float a, float r) {
+  const int lo = (a >= 0.5f) + (a >= 1.f) + (a >= 1.5f) + (a >= 2.f) + (a >= 3.f) + (a >= 4.f) + (a >= 6.f);
+  if (lo == 7) return 7;
+  const float g = lo < 4 ? 0.5f * lo : (lo == 4 ? 2.f : (lo == 5 ? 3.f : 4.f));
+  const float w = lo < 4 ? 2.f : (lo < 6 ? 1.f : 0.5f);  // 1 / grid spacing
+  return r < (a - g) * w ? lo + 1 : lo;
+}
+
+// One 16-element NVFP4 block: e4m3 scale byte and 8 packed bytes (low nibble first).
+// ridx(i) gives the element index that seeds stochastic rounding.
+__device__ __forceinline__ void quant_block16(const float* v, float st, bool stochastic, uint32_t seed,
+                                              uint32_t hi, uint32_t idx0, uint32_t idx_step, uint8_t& sbyte,
+                                              uint2& packed) {
+  float bm = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) bm = fmaxf(bm, fabsf(v[i]));
+  const __nv_fp8_e4m3 s8(fminf(bm / (6.f * st), 448.f));
+  sbyte = s8.__x;
+  const float denom = fmaxf(float(s8) * st, 1e-30f);
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float y = v[i] / denom;
+    const float a = fabsf(y);
+    int code;
+    if (stochastic) {
+      const float r = (hash3(seed, hi, idx0 + (uint32_t)i * idx_step) >> 8) * (1.f / 16777216.f);
+      code = e2m1_sr_fast(a, r);
+    } else {
+      code = e2m1_rne_fast(a);
+    }
+    if (y < 0.f && code > 0) code |= 8;
+    w[i >> 3] |= (uint32_t)code << (4 * (i & 7));
+  }
+  packed = make_uint2(w[0], w[1]);
+}
+
+// Byte offset of the scale of (row, 16-element block jb) in the tensor-core
+// scale-factor layout: 512-byte atoms of 128 rows x 4 blocks, atoms ordered
+// K-fastest inside each 128-row band, byte 16*(r%32) + 4*(r/32) + jb%4.
+__device__ __forceinline__ int64_t sf_atom_offset(int64_t row, int64_t jb, int64_t kblocks64) {
+  const int r = (int)(row & 127);
+  return ((row >> 7) * kblocks64 + (jb >> 2)) * 512 + 16 * (r & 31) + 4 * (r >> 5) + (int)(jb & 3);
+}
+
+// Tile of 128 rows x 64 columns of x (M, K) per CTA, 256 threads.
+// ROW: x quantised along K -> packed (M, K/2), scales in atom layout (M/128, K/64, 512).
+// COL: x^T quantised along M -> packed (K, M/2), scales (K/128, M/64, 512).
+template <typename T, bool ROW, bool COL>
+__global__ void __launch_bounds__(256) nvfp4_quant_dual_kernel(
+    const T* __restrict__ x, int64_t M, int64_t K, const float* __restrict__ amax, uint8_t* __restrict__ pr,
+    uint8_t* __restrict__ ar, uint8_t* __restrict__ pc, uint8_t* __restrict__ ac, float* __restrict__ st_out,
+    bool stochastic, uint32_t seed) {
+  __shared__ float tile[128][65];
+  const int64_t m0 = (int64_t)blockIdx.y * 128, k0 = (int64_t)blockIdx.x * 64;
+  const float st = fmaxf(amax[0] / (6.f * 448.f), 1e-12f);
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) st_out[0] = st;
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int rep = 0; rep < 2; ++rep) {
+    const int item = t + 256 * rep;
+    const int row = item >> 2, j = item & 3;
+    const T* src = x + (m0 + row) * K + k0 + j * 16;
+    float v[16];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(src) + h);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[h * 8 + i] = to_f(e[i]);
+    }
+    if (COL) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) tile[row][j * 16 + i] = v[i];
+    }
+    if (ROW) {
+      const int64_t e0 = (m0 + row) * K + k0 + j * 16;
+      uint8_t sb;
+      uint2 pk;
+      quant_block16(v, st, stochastic, seed, (uint32_t)(e0 >> 32), (uint32_t)e0, 1u, sb, pk);
+      *reinterpret_cast<uint2*>(pr + ((m0 + row) * K + k0 + j * 16) / 2) = pk;
+      ar[sf_atom_offset(m0 + row, (k0 >> 4) + j, K >> 6)] = sb;
+    }
+  }
+  if (COL) {
+    __syncthreads();
+#pragma unroll
+    for (int rep = 0; rep < 2; ++rep) {
+      const int item = t + 256 * rep;
+      const int k = item & 63, mb = item >> 6;
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = tile[mb * 16 + i][k];
+      const int64_t kr = k0 + k, mc = m0 + mb * 16;
+      const int64_t e0 = kr * M + mc;  // element index of x^T
+      uint8_t sb;
+      uint2 pk;
+      quant_block16(v, st, stochastic, seed ^ 0x5bd1e995u, (uint32_t)(e0 >> 32), (uint32_t)e0, 1u, sb, pk);
+      *reinterpret_cast<uint2*>(pc + (kr * M + mc) / 2) = pk;
+      ac[sf_atom_offset(kr, mc >> 4, M >> 6)] = sb;
+    }
+  }
+}
+
 template <typename O>
 __global__ void nvfp4_dequant_kernel(const uint8_t* __restrict__ packed, const __nv_fp8_e4m3* __restrict__ sb,
                                      const float* __restrict__ st, O* __restrict__ out, int64_t n) {
@@ -194,6 +307,66 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> nvfp4_quantize(const at::Tensor& 
   });
   LRB_LAUNCH_CHECK();
   return {packed, sb, st};
+}
+
+// x (M, K) bf16/fp16/fp32 -> {packed_row (M, K/2), atoms_row (M/128, K/64, 512),
+// packed_col (K, M/2), atoms_col (K/128, M/64, 512), tensor scale}. The per-tensor
+// amax is computed here unless given (x and x^T share it).
+std::vector<at::Tensor> nvfp4_quantize_dual(const at::Tensor& x, const c10::optional<at::Tensor>& amax_in,
+                                            bool rowwise, bool colwise, bool stochastic, int64_t seed) {
+  LRB_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "nvfp4_quantize_dual: 2-D contiguous CUDA input");
+  const int64_t M = x.size(0), K = x.size(1);
+  LRB_CHECK(M % 128 == 0 && K % 128 == 0, "nvfp4_quantize_dual: M and K multiples of 128");
+  LRB_CHECK(rowwise || colwise, "nvfp4_quantize_dual: nothing requested");
+  c10::cuda::CUDAGuard g(x.device());
+  auto u8 = x.options().dtype(at::kByte);
+  at::Tensor pr, ar, pc, ac;
+  if (rowwise) {
+    pr = at::empty({M, K / 2}, u8);
+    ar = at::empty({M / 128, K / 64, 512}, u8);
+  }
+  if (colwise) {
+    pc = at::empty({K, M / 2}, u8);
+    ac = at::empty({K / 128, M / 64, 512}, u8);
+  }
+  auto st = at::empty({}, x.options().dtype(at::kFloat));
+  at::Tensor amax;
+  if (amax_in.has_value()) {
+    amax = *amax_in;
+    LRB_CHECK(amax.is_cuda() && amax.scalar_type() == at::kFloat && amax.numel() == 1, "nvfp4_quantize_dual: amax");
+  } else {
+    amax = at::empty({1}, x.options().dtype(at::kFloat));
+    AT_CUDA_CHECK(cudaMemsetAsync(amax.data_ptr(), 0, sizeof(float), stream()));
+  }
+  const int64_t n = M * K;
+  const dim3 grid((unsigned)(K / 64), (unsigned)(M / 128));
+  LRB_DISPATCH_FLOAT(x.scalar_type(), T, [&] {
+    if (!amax_in.has_value()) {
+      const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 8);
+      absmax_kernel<T><<<blocks, 256, 0, stream()>>>(reinterpret_cast<const T*>(x.data_ptr()), n,
+                                                      amax.data_ptr<float>());
+      LRB_LAUNCH_CHECK();
+    }
+    auto* xp = reinterpret_cast<const T*>(x.data_ptr());
+    uint8_t* p0 = rowwise ? pr.data_ptr<uint8_t>() : nullptr;
+    uint8_t* a0 = rowwise ? ar.data_ptr<uint8_t>() : nullptr;
+    uint8_t* p1 = colwise ? pc.data_ptr<uint8_t>() : nullptr;
+    uint8_t* a1 = colwise ? ac.data_ptr<uint8_t>() : nullptr;
+    if (rowwise && colwise)
+      nvfp4_quant_dual_kernel<T, true, true><<<grid, 256, 0, stream()>>>(xp, M, K, amax.data_ptr<float>(), p0, a0, p1,
+                                                                         a1, st.data_ptr<float>(), stochastic,
+                                                                         (uint32_t)seed);
+    else if (rowwise)
+      nvfp4_quant_dual_kernel<T, true, false><<<grid, 256, 0, stream()>>>(xp, M, K, amax.data_ptr<float>(), p0, a0,
+                                                                          p1, a1, st.data_ptr<float>(), stochastic,
+                                                                          (uint32_t)seed);
+    else
+      nvfp4_quant_dual_kernel<T, false, true><<<grid, 256, 0, stream()>>>(xp, M, K, amax.data_ptr<float>(), p0, a0,
+                                                                          p1, a1, st.data_ptr<float>(), stochastic,
+                                                                          (uint32_t)seed);
+  });
+  LRB_LAUNCH_CHECK();
+  return {pr, ar, pc, ac, st};
 }
 
 at::Tensor nvfp4_dequantize(const at::Tensor& packed, const at::Tensor& sb, const at::Tensor& st,

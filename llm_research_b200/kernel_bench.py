@@ -103,6 +103,28 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
         b = NVFP4Tensor.quantize(torch.randn(n, n, device="cuda", dtype=torch.bfloat16))
         return (lambda: matmul_nvfp4(a, b)), 2.0 * n ** 3, 0.0
 
+    def quant_dual():
+        from llm_research_b200.ops.quant import nvfp4_quantize_dual
+
+        x = torch.randn(8192, 4096, device="cuda", dtype=torch.bfloat16)
+        # one read of x, both FP4 copies with their scales written
+        return (lambda: nvfp4_quantize_dual(x)), 0.0, x.numel() * (2 + 2 * (0.5 + 1 / 16))
+
+    def linear_train(precision: str):
+        from llm_research_b200.ops.linear import linear_precision, project
+
+        T, K, N = 8192, 4096, 11008
+        x = torch.randn(T, K, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        w = (torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02).requires_grad_()
+        dy = torch.randn(T, N, device="cuda", dtype=torch.bfloat16)
+
+        def run():
+            with linear_precision(precision):
+                x.grad = w.grad = None
+                project(x, w).backward(dy)
+
+        return run, 6.0 * T * K * N, 0.0
+
     def rms(bwd: bool):
         rows, d = 32768, 2048
         x = torch.randn(rows, d, device="cuda", dtype=torch.bfloat16)
@@ -146,6 +168,9 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
         "gemm": lambda: gemm(False),
         "gemm_cublas": lambda: gemm(True),
         "gemm_nvfp4": gemm_fp4,
+        "nvfp4_quant_dual": quant_dual,
+        "linear_fwd_bwd_bf16": lambda: linear_train("bf16"),
+        "linear_fwd_bwd_nvfp4": lambda: linear_train("nvfp4"),
         "rmsnorm_fwd": lambda: rms(False),
         "rmsnorm_bwd": lambda: rms(True),
         "swiglu_fwd": swiglu,

@@ -90,31 +90,35 @@ def linear_precision(precision: str):
 class _NVFP4LinearFn(torch.autograd.Function):
     """y = x W^T with NVFP4 operands (E2M1, e4m3 per 16 elements, fp32 per tensor).
 
-    Forward rounds to nearest; the backward GEMMs (dX = dY W, dW = dY^T X) use
-    stochastic rounding on the gradient operand, so the gradient is unbiased
-    in expectation.  All three GEMMs run on the tcgen05 block-scaled kernel."""
+    Forward rounds to nearest and quantises ``x`` and ``W`` once each, in both
+    orientations (one pass per tensor): the row-wise copies feed the forward GEMM,
+    the transposed copies are what the backward needs (``W^T`` for dX, ``X^T`` for
+    dW), so only FP4 operands are kept for backward.  The backward quantises dY
+    (row-wise and transposed, one pass) with stochastic rounding so the gradient
+    is unbiased in expectation.  All three GEMMs run on the tcgen05 block-scaled
+    kernel."""
 
     @staticmethod
     def forward(ctx, x2d, w):
-        from llm_research_b200.ops.quant import NVFP4Tensor, matmul_nvfp4
+        from llm_research_b200.ops.quant import matmul_nvfp4, nvfp4_quantize_dual
 
-        ctx.save_for_backward(x2d, w)
-        return matmul_nvfp4(NVFP4Tensor.quantize(x2d), NVFP4Tensor.quantize(w))
+        need_dx, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        xr, xc, _ = nvfp4_quantize_dual(x2d, colwise=need_dw)
+        wr, wc, _ = nvfp4_quantize_dual(w, colwise=need_dx)
+        ctx.xc, ctx.wc = xc, wc
+        return matmul_nvfp4(xr, wr)
 
     @staticmethod
     def backward(ctx, dy):
-        from llm_research_b200.ops.quant import NVFP4Tensor, matmul_nvfp4
+        from llm_research_b200.ops.quant import matmul_nvfp4, nvfp4_quantize_dual
 
-        x2d, w = ctx.saved_tensors
-        dy = dy.contiguous()
+        need_dx, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         seed = next(_SEEDS)
-        dx = dw = None
-        if ctx.needs_input_grad[0]:
-            dx = matmul_nvfp4(NVFP4Tensor.quantize(dy, stochastic=True, seed=seed),
-                              NVFP4Tensor.quantize(w.t().contiguous()))
-        if ctx.needs_input_grad[1]:
-            dw = matmul_nvfp4(NVFP4Tensor.quantize(dy.t().contiguous(), stochastic=True, seed=seed + 1),
-                              NVFP4Tensor.quantize(x2d.t().contiguous()))
+        dyr, dyc, _ = nvfp4_quantize_dual(dy.contiguous(), rowwise=need_dx, colwise=need_dw, stochastic=True,
+                                          seed=seed)
+        dx = matmul_nvfp4(dyr, ctx.wc) if need_dx else None
+        dw = matmul_nvfp4(dyc, ctx.xc) if need_dw else None
+        ctx.xc = ctx.wc = None
         return dx, dw
 
 

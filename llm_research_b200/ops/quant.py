@@ -18,7 +18,7 @@ proportional to proximity (unbiased), as used for gradients.
 
 from __future__ import annotations
 
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 import torch.nn.functional as F
@@ -130,19 +130,51 @@ def nvfp4_swizzle_scales(s_b: torch.Tensor) -> torch.Tensor:
     return raw.view(mb, 4, 32, KB // 4, 4).permute(0, 3, 2, 1, 4).contiguous().view(mb, KB // 4, 512)
 
 
-class NVFP4Tensor:
-    """A 2-D tensor quantised to NVFP4 for :func:`matmul_nvfp4` (rows = M or N, K-major)."""
+def nvfp4_unswizzle_scales(atoms: torch.Tensor, M: int) -> torch.Tensor:
+    """Inverse of :func:`nvfp4_swizzle_scales`: atoms -> row-major ``(M, K/16)`` e4m3."""
+    mb, kb, _ = atoms.shape
+    raw = atoms.view(mb, kb, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(mb * 128, kb * 4)[:M]
+    return raw.contiguous().view(torch.float8_e4m3fn)
 
-    def __init__(self, packed: torch.Tensor, scales: torch.Tensor, tensor_scale: torch.Tensor) -> None:
+
+def nvfp4_quantize_dual(x2d: torch.Tensor, amax: Optional[torch.Tensor] = None, rowwise: bool = True,
+                        colwise: bool = True, stochastic: bool = False, seed: int = 0):
+    """Quantise ``x`` (M, K) and/or ``x^T`` to NVFP4 in one pass, scales already in the
+    tensor-core atom layout: ``(row, col, tensor_scale)`` where ``row`` / ``col`` are
+    :class:`NVFP4Tensor` (or None) for ``x`` (blocks along K) and ``x^T`` (blocks along M).
+    Both share the per-tensor scale (one amax; ``amax`` may be passed in). M, K multiples
+    of 128. On CPU: :func:`nvfp4_quantize` of ``x`` and of ``x.t()`` (the oracle; stochastic
+    rounding draws from torch's generator there)."""
+    if x2d.is_cuda:
+        pr, ar, pc, ac, st = native().nvfp4_quantize_dual(x2d.contiguous(), amax, rowwise, colwise, stochastic, int(seed))
+        row = NVFP4Tensor.from_atoms(pr, ar, st) if rowwise else None
+        col = NVFP4Tensor.from_atoms(pc, ac, st) if colwise else None
+        return row, col, st
+    row = NVFP4Tensor(*nvfp4_quantize(x2d, stochastic, seed)) if rowwise else None
+    col = NVFP4Tensor(*nvfp4_quantize(x2d.t().contiguous(), stochastic, seed + 1)) if colwise else None
+    return row, col, (row or col).tensor_scale
+
+
+class NVFP4Tensor:
+    """A 2-D tensor quantised to NVFP4 for :func:`matmul_nvfp4` (rows = M or N, K-major).
+    ``scales`` (row-major e4m3) may be None when only the atom layout is known."""
+
+    def __init__(self, packed: torch.Tensor, scales: Optional[torch.Tensor], tensor_scale: torch.Tensor,
+                 atoms: Optional[torch.Tensor] = None) -> None:
         self.packed, self.scales, self.tensor_scale = packed, scales, tensor_scale.float().reshape(())
-        self.atoms = nvfp4_swizzle_scales(scales)
+        self.atoms = nvfp4_swizzle_scales(scales) if atoms is None else atoms
+
+    @classmethod
+    def from_atoms(cls, packed: torch.Tensor, atoms: torch.Tensor, tensor_scale: torch.Tensor) -> "NVFP4Tensor":
+        return cls(packed, None, tensor_scale, atoms)
 
     @classmethod
     def quantize(cls, x2d: torch.Tensor, stochastic: bool = False, seed: int = 0) -> "NVFP4Tensor":
         return cls(*nvfp4_quantize(x2d, stochastic, seed))
 
     def dequantize(self, dtype=torch.float32) -> torch.Tensor:
-        return nvfp4_dequantize(self.packed, self.scales, self.tensor_scale, dtype)
+        scales = self.scales if self.scales is not None else nvfp4_unswizzle_scales(self.atoms, self.packed.shape[0])
+        return nvfp4_dequantize(self.packed, scales, self.tensor_scale, dtype)
 
     @property
     def shape(self):

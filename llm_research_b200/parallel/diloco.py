@@ -45,6 +45,7 @@ import torch
 import torch.distributed as dist
 
 from llm_research_b200.parallel.fault import HeartbeatMonitor, RosterGroup, default_store
+from llm_research_b200.utils.nvtx import nvtx_fn
 
 
 @dataclass
@@ -167,6 +168,7 @@ class DiLoCo:
         return False
 
     @torch.no_grad()
+    @nvtx_fn("lrb/diloco/outer")
     def outer_step(self, _roster: Optional[Tuple[List[int], List[int]]] = None) -> None:
         self._flatten()
         joiners: List[int] = []

@@ -36,6 +36,7 @@ import torch.nn.functional as F
 
 from llm_research_b200 import ops
 from llm_research_b200._ext import native
+from llm_research_b200.utils.nvtx import nvtx_fn
 
 
 _EP_CONTEXT = None
@@ -97,12 +98,14 @@ class EPComm:
         return self.heap.view(off, (self.epl, self.world * cap, self.d), torch.bfloat16)
 
     # pushed channel (sources -> owners)
+    @nvtx_fn("lrb/ep/dispatch_push")
     def push(self, rows: torch.Tensor, scale: Optional[torch.Tensor], per_assignment: bool, route, cap: int, k: int):
         self.eR += 1
         native().ep_push(rows.contiguous(), scale, per_assignment, self.heap.bases, self.recv_off, self.ready_off,
                          self.consumed_off, self.rank, self.world, k, cap, self.epl, self.eR, *route,
                          self.counters[0:1], self.heap.err)
 
+    @nvtx_fn("lrb/ep/dispatch_take")
     def take(self, cap: int) -> torch.Tensor:
         C = native()
         C.ep_flag_wait(self.ready, self.world, self.eR, self.heap.err)
@@ -113,6 +116,7 @@ class EPComm:
         return out
 
     # pulled channel (owners -> sources)
+    @nvtx_fn("lrb/ep/combine_put")
     def put(self, t: torch.Tensor, cap: int) -> None:
         C = native()
         self.eO += 1
@@ -120,6 +124,7 @@ class EPComm:
         self._region(self.out_off, cap).copy_(t)
         C.ep_flag_set(self.outready, self.eO)
 
+    @nvtx_fn("lrb/ep/combine_pull")
     def pull(self, T: int, w: Optional[torch.Tensor], want_rows: bool, route, cap: int, k: int):
         y = torch.empty(T, self.d, dtype=torch.bfloat16, device=self.device)
         rows = torch.empty(T * k, self.d, dtype=torch.bfloat16, device=self.device) if want_rows else None

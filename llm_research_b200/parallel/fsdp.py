@@ -58,6 +58,7 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from llm_research_b200 import ops
+from llm_research_b200.utils.nvtx import nvtx_fn
 
 ALIGN = 8  # elements; keeps every bf16 view 16-byte aligned
 
@@ -268,6 +269,7 @@ class FlatShardEngine(nn.Module):
         dist.barrier(group=self.pg)  # every heap is zeroed before anyone publishes
         self._publish()
 
+    @nvtx_fn("lrb/fsdp/publish")
     def _publish(self) -> None:
         C = ops_native()
         self._ag_epoch += 1
@@ -286,6 +288,7 @@ class FlatShardEngine(nn.Module):
             u.compute.untyped_storage().resize_(0)
         u.gathered = self.world == 1
 
+    @nvtx_fn("lrb/fsdp/ag")
     def _gather(self, u: Unit, wait: bool = True) -> None:
         if self.world == 1:
             return
@@ -408,6 +411,7 @@ class FlatShardEngine(nn.Module):
         if self._sync_grads:
             self._reduce_scatter(u)
 
+    @nvtx_fn("lrb/fsdp/rs")
     def _reduce_scatter(self, u: Unit) -> None:
         if self.world == 1:
             return
@@ -497,6 +501,7 @@ class FlatShardEngine(nn.Module):
         return [u.grad_shard for u in self.units]
 
     @torch.no_grad()
+    @nvtx_fn("lrb/fsdp/clip")
     def clip_grad_norm_(self, max_norm: float, norm_type: float = 2.0) -> torch.Tensor:
         self.wait_grads()
         if self.heap is not None:

@@ -38,6 +38,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from llm_research_b200._ext import native
+from llm_research_b200.utils.nvtx import nvtx_fn
 
 
 class TPComm:
@@ -68,6 +69,7 @@ class TPComm:
         self.rs_epoch = 0
         self.ag_epoch = 0
 
+    @nvtx_fn("lrb/tp/gemm_rs")
     def gemm_rs(self, x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         """``ReduceScatter_rows(x @ w.T)`` (+ residual): ``(T, K) x (N, K) -> (T / world, N)``."""
         C = native()
@@ -81,6 +83,7 @@ class TPComm:
                     self.consumed, self.rs_epoch, self.counters[self.world:self.world + 1], self.heap.err)
         return out
 
+    @nvtx_fn("lrb/tp/ag_gemm")
     def ag_gemm(self, x_shard: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """``AllGather_rows(x_shard) @ w.T``: ``(T / world, K) x (N, K) -> (T, N)``."""
         C = native()

@@ -77,3 +77,57 @@ def test_hlrt_trains_with_nvfp4_linears():
             opt.zero_grad()
             losses.append(float(loss))
     assert all(l == l for l in losses) and losses[-1] < losses[0]
+
+
+def test_nvfp4_unswizzle_inverts_swizzle():
+    from llm_research_b200.ops.quant import nvfp4_swizzle_scales, nvfp4_unswizzle_scales
+
+    s = torch.arange(256 * 32, dtype=torch.int64).remainder(127).to(torch.uint8).view(256, 32)
+    back = nvfp4_unswizzle_scales(nvfp4_swizzle_scales(s), 256).view(torch.uint8)
+    assert torch.equal(back, s)
+
+
+def test_nvfp4_quantize_dual_cpu_oracle_shapes():
+    from llm_research_b200.ops.quant import nvfp4_quantize_dual
+
+    x = torch.randn(256, 384)
+    row, col, st = nvfp4_quantize_dual(x)
+    assert row.shape == (256, 384) and col.shape == (384, 256)
+    torch.testing.assert_close(col.dequantize(), nvfp4_quantize_dual(x.t().contiguous(), colwise=False)[0].dequantize())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K", [(128, 128), (256, 640), (1024, 4096)])
+def test_nvfp4_quantize_dual_matches_rowwise_quantizer(M, K):
+    """Row-wise output == the one-block-per-thread quantiser of x, transposed output ==
+    the same quantiser of x^T (bit-exact, round to nearest); scales land in atom layout."""
+    from llm_research_b200.ops.quant import nvfp4_quantize, nvfp4_quantize_dual, nvfp4_swizzle_scales
+
+    torch.manual_seed(1)
+    x = (torch.randn(M, K, device="cuda") * torch.rand(M, 1, device="cuda") * 4).to(torch.bfloat16)
+    row, col, st = nvfp4_quantize_dual(x)
+    p, s, st1 = nvfp4_quantize(x)
+    pt, sT, st2 = nvfp4_quantize(x.t().contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(row.packed, p) and torch.equal(row.atoms, nvfp4_swizzle_scales(s))
+    assert torch.equal(col.packed, pt) and torch.equal(col.atoms, nvfp4_swizzle_scales(sT))
+    assert float(st) == float(st1) == float(st2)
+
+
+@pytest.mark.gpu
+def test_nvfp4_quantize_dual_stochastic_is_unbiased():
+    from llm_research_b200.ops.quant import nvfp4_quantize_dual
+
+    torch.manual_seed(2)
+    x = torch.randn(256, 256, device="cuda").to(torch.bfloat16)
+    acc_r = torch.zeros(256, 256, device="cuda")
+    acc_c = torch.zeros(256, 256, device="cuda")
+    n = 64
+    for i in range(n):
+        row, col, _ = nvfp4_quantize_dual(x, stochastic=True, seed=100 + i)
+        acc_r += row.dequantize()
+        acc_c += col.dequantize().t()
+    ref = x.float()
+    for acc in (acc_r, acc_c):
+        bias = ((acc / n - ref).norm() / ref.norm()).item()
+        assert bias < 0.035, bias
