@@ -54,10 +54,23 @@ class MultiHeadAttention(nn.Module):
         self.num_kv_groups = num_heads // self.num_kv_heads
         self.dropout_p = dropout
         self.use_flash_attention = use_flash_attention
-        self.q_proj = nn.Linear(d_model, num_heads * self.head_dim, bias=bias)
-        self.k_proj = nn.Linear(d_model, self.num_kv_heads * self.head_dim, bias=bias)
-        self.v_proj = nn.Linear(d_model, self.num_kv_heads * self.head_dim, bias=bias)
-        self.o_proj = nn.Linear(num_heads * self.head_dim, d_model, bias=bias)
+        from llm_research_b200.parallel.tp import current_tensor_parallel, mark_tp
+
+        tp = current_tensor_parallel()
+        self.tp = tp
+        nt = 1 if tp is None else torch.distributed.get_world_size(tp[0])
+        if tp is not None:
+            assert not bias and num_heads % nt == 0 and self.num_kv_heads % nt == 0, \
+                "tensor parallelism splits whole (KV) heads and has no biases"
+        # Under tensor parallelism every projection holds this rank's heads only.
+        self.q_proj = nn.Linear(d_model, num_heads // nt * self.head_dim, bias=bias)
+        self.k_proj = nn.Linear(d_model, self.num_kv_heads // nt * self.head_dim, bias=bias)
+        self.v_proj = nn.Linear(d_model, self.num_kv_heads // nt * self.head_dim, bias=bias)
+        self.o_proj = nn.Linear(num_heads // nt * self.head_dim, d_model, bias=bias)
+        if tp is not None:
+            for lin in (self.q_proj, self.k_proj, self.v_proj):
+                mark_tp(lin.weight, 0)
+            mark_tp(self.o_proj.weight, 1)
 
     # ------------------------------------------------------------------
     def _qkv(self, x: torch.Tensor) -> torch.Tensor:
@@ -66,6 +79,31 @@ class MultiHeadAttention(nn.Module):
         if self.q_proj.bias is not None:
             b = torch.cat([self.q_proj.bias, self.k_proj.bias, self.v_proj.bias], 0)
         return project(x, w, b)
+
+    def forward_tp(self, x_shard: torch.Tensor, seq_shape, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """Tensor + sequence parallel: ``x_shard`` is this rank's ``(B*S/tp, d)`` rows;
+        QKV is an all-gather->GEMM over the group (this rank's heads for all tokens),
+        attention runs on the local heads, ``o_proj`` is a GEMM->reduce-scatter back
+        to ``(B*S/tp, d)``."""
+        from llm_research_b200.parallel.tp import column_parallel, row_parallel
+
+        group, comm = self.tp
+        B, S = seq_shape
+        nt = torch.distributed.get_world_size(group)
+        H, Hkv, D = self.num_heads // nt, self.num_kv_heads // nt, self.head_dim
+        w = cat_rows(self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+        qkv = column_parallel(x_shard, w, group, comm).view(B, S, -1)
+        q, k, v = ops.rope_qkv(qkv, cos, sin, H, Hkv, D, 0)
+        drop = self.dropout_p if self.training else 0.0
+        if drop == 0.0:
+            out = ops.attention(q, k, v, causal=True)
+        else:
+            qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+            if self.num_kv_groups > 1:
+                kh = kh.repeat_interleave(self.num_kv_groups, dim=1)
+                vh = vh.repeat_interleave(self.num_kv_groups, dim=1)
+            out = self._vanilla_attention(qh, kh, vh, None).transpose(1, 2)
+        return row_parallel(out.reshape(B * S, H * D), self.o_proj.weight, group, comm)
 
     def forward(
         self,

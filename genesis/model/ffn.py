@@ -26,10 +26,30 @@ class SwiGLUFFN(nn.Module):
         super().__init__()
         d_ff = default_ffn_dim(d_model) if d_ff is None else d_ff
         self.d_ff = d_ff
-        self.w1 = nn.Linear(d_model, d_ff, bias=bias)
-        self.w_gate = nn.Linear(d_model, d_ff, bias=bias)
-        self.w2 = nn.Linear(d_ff, d_model, bias=bias)
+        from llm_research_b200.parallel.tp import current_tensor_parallel, mark_tp
+
+        self.tp = tp = current_tensor_parallel()
+        nt = 1 if tp is None else torch.distributed.get_world_size(tp[0])
+        assert d_ff % nt == 0 and (tp is None or not bias), "tensor parallelism: d_ff % tp == 0, no biases"
+        # Under tensor parallelism: this rank's d_ff/tp columns of the hidden layer.
+        self.w1 = nn.Linear(d_model, d_ff // nt, bias=bias)
+        self.w_gate = nn.Linear(d_model, d_ff // nt, bias=bias)
+        self.w2 = nn.Linear(d_ff // nt, d_model, bias=bias)
+        if tp is not None:
+            mark_tp(self.w1.weight, 0)
+            mark_tp(self.w_gate.weight, 0)
+            mark_tp(self.w2.weight, 1)
         self.dropout = nn.Dropout(dropout) if dropout > 0.0 else nn.Identity()
+
+    def forward_tp(self, x_shard: torch.Tensor) -> torch.Tensor:
+        """``(B*S/tp, d)`` sequence shard -> all-gather->GEMM (up|gate, this rank's
+        columns) -> SwiGLU -> GEMM->reduce-scatter (down) -> ``(B*S/tp, d)``."""
+        from llm_research_b200.parallel.tp import column_parallel, row_parallel
+
+        group, comm = self.tp
+        gu = column_parallel(x_shard, cat_rows(self.w1.weight, self.w_gate.weight), group, comm)
+        h = ops.swiglu(gu)
+        return row_parallel(self.dropout(h), self.w2.weight, group, comm)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         w = cat_rows(self.w1.weight, self.w_gate.weight)

@@ -66,11 +66,25 @@ class TransformerBlock(nn.Module):
         attention_mask: Optional[torch.Tensor] = None,
         kv_cache: Optional[object] = None,
         position_offset: int = 0,
+        seq_shape: Optional[tuple] = None,
     ) -> torch.Tensor:
+        if seq_shape is not None:  # tensor + sequence parallel: x is this rank's (B*S/tp, d) rows
+            return self._forward_tp(x, cos, sin, seq_shape)
         h = self.attn(self.attn_norm(x), cos, sin, attention_mask=attention_mask,
                       kv_cache=kv_cache, position_offset=position_offset)
         normed, x = self.ffn_norm.forward_residual(h, x)
         return x + self.ffn(normed)
+
+    def _forward_tp(self, x, cos, sin, seq_shape):
+        from llm_research_b200 import ops
+        from llm_research_b200.parallel.tp import sum_grad
+
+        group = self.attn.tp[0]
+        # The norms see this rank's tokens only: their weight gradients are summed over the group.
+        h = self.attn.forward_tp(ops.rms_norm(x, sum_grad(self.attn_norm.weight, group), self.attn_norm.eps),
+                                 seq_shape, cos, sin)
+        normed, x = ops.rms_norm_residual(h, x, sum_grad(self.ffn_norm.weight, group), self.ffn_norm.eps)
+        return x + self.ffn.forward_tp(normed)
 
 
 class Tier1TokenProcessor(nn.Module):
@@ -90,13 +104,16 @@ class Tier1TokenProcessor(nn.Module):
     ) -> None:
         super().__init__()
         self.rotary_emb = RotaryEmbedding(dim=d_model // num_heads, max_seq_len=max_seq_len, base=rope_base)
-        self.layers = nn.ModuleList([
-            TransformerBlock(
-                d_model=d_model, num_heads=num_heads, d_ff=d_ff, num_kv_heads=num_kv_heads,
-                dropout=dropout, use_flash_attention=use_flash_attention, norm_eps=norm_eps, moe=moe,
-            )
-            for _ in range(num_layers)
-        ])
+        from llm_research_b200.parallel.tp import tensor_parallel_scope
+
+        with tensor_parallel_scope():  # blocks split only under an enclosing ``tensor_parallel`` context
+            self.layers = nn.ModuleList([
+                TransformerBlock(
+                    d_model=d_model, num_heads=num_heads, d_ff=d_ff, num_kv_heads=num_kv_heads,
+                    dropout=dropout, use_flash_attention=use_flash_attention, norm_eps=norm_eps, moe=moe,
+                )
+                for _ in range(num_layers)
+            ])
 
     def forward(
         self,
@@ -106,6 +123,16 @@ class Tier1TokenProcessor(nn.Module):
         position_offset: int = 0,
     ) -> torch.Tensor:
         cos, sin = self.rotary_emb(position_offset + x.size(1))
+        tp = self.layers[0].attn.tp if len(self.layers) else None
+        if tp is not None and kv_cache is None and attention_mask is None and position_offset == 0:
+            from llm_research_b200.parallel.tp import gather_sequence, scatter_sequence
+
+            B, S, d = x.shape
+            h = scatter_sequence(x, tp[0])
+            for layer in self.layers:
+                h = layer(h, cos, sin, seq_shape=(B, S))
+            return gather_sequence(h, tp[0], (B, S, d))
+        assert tp is None, "tensor-parallel Tier 1 runs full causal sequences (no cache / mask / offset)"
         for i, layer in enumerate(self.layers):
             x = layer(x, cos, sin, attention_mask=attention_mask,
                       kv_cache=kv_cache[i] if kv_cache is not None else None,

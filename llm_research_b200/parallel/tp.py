@@ -29,8 +29,9 @@ NCCL / gloo collectives around ``F.linear`` -- the baseline.
 
 from __future__ import annotations
 
+import contextlib
 import math
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -38,6 +39,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from llm_research_b200._ext import native
+from llm_research_b200.ops.linear import project
 from llm_research_b200.utils.nvtx import nvtx_fn
 
 
@@ -139,7 +141,7 @@ class _ColumnFn(torch.autograd.Function):
         T = x_shard.shape[0] * dist.get_world_size(group)
         if _fused_ok(comm, x_shard, T, (x_shard.shape[1], w.shape[0])):
             return comm.ag_gemm(x_shard, w)
-        return F.linear(_all_gather_rows(x_shard, group), w)
+        return project(_all_gather_rows(x_shard, group), w)
 
     @staticmethod
     def backward(ctx, dy):
@@ -165,7 +167,7 @@ class _RowFn(torch.autograd.Function):
         T = x.shape[0]
         if _fused_ok(comm, x, T, (w.shape[0], w.shape[1])):
             return comm.gemm_rs(x, w, residual)
-        y = _reduce_scatter_rows(F.linear(x, w), group)
+        y = _reduce_scatter_rows(project(x, w), group)
         return y + residual if residual is not None else y
 
     @staticmethod
@@ -221,3 +223,118 @@ def shard_linear_weight(w: torch.Tensor, group: Optional[dist.ProcessGroup], dim
     """This rank's slice of a full weight: ``dim=0`` for column parallel, ``1`` for row parallel."""
     tp, r = dist.get_world_size(group), dist.get_rank(group)
     return w.chunk(tp, dim=dim)[r].contiguous()
+
+
+# ----------------------------------------------------------- model integration
+_TP_STATE: Optional[Tuple[dist.ProcessGroup, Optional[TPComm]]] = None
+
+
+@contextlib.contextmanager
+def tensor_parallel(group: dist.ProcessGroup, comm: Optional[TPComm] = None):
+    """Modules built inside this context (Tier-1 attention and SwiGLU FFN) hold
+    their ``1/tp`` weight shards and run sequence-parallel over ``group``;
+    ``comm`` (a :class:`TPComm`) selects the fused symmetric-memory kernels,
+    ``None`` the NCCL collectives."""
+    global _TP_STATE
+    prev = _TP_STATE
+    _TP_STATE = (group, comm)
+    try:
+        yield
+    finally:
+        _TP_STATE = prev
+
+
+_TP_SCOPE = False
+
+
+@contextlib.contextmanager
+def tensor_parallel_scope():
+    """Opened by the Tier-1 trunk while it builds its blocks: only modules built
+    inside it are split (the tiers after Tier 1 run replicated)."""
+    global _TP_SCOPE
+    prev = _TP_SCOPE
+    _TP_SCOPE = True
+    try:
+        yield
+    finally:
+        _TP_SCOPE = prev
+
+
+def current_tensor_parallel() -> Optional[Tuple[dist.ProcessGroup, Optional[TPComm]]]:
+    return _TP_STATE if _TP_SCOPE else None
+
+
+def mark_tp(p: nn.Parameter, dim: int) -> nn.Parameter:
+    """Tag a TP weight shard with the dimension along which the shards of the
+    group concatenate to the full weight (0: column parallel, 1: row parallel)."""
+    p._lrb_tp = dim
+    return p
+
+
+class _ScatterSeq(torch.autograd.Function):
+    """Replicated ``(T, d)`` -> this rank's contiguous ``T/tp`` rows; backward all-gathers."""
+
+    @staticmethod
+    def forward(ctx, x2d, group):
+        ctx.group = group
+        W, r = dist.get_world_size(group), dist.get_rank(group)
+        n = x2d.shape[0] // W
+        return x2d[r * n:(r + 1) * n].clone()
+
+    @staticmethod
+    def backward(ctx, g):
+        return _all_gather_rows(g.contiguous(), ctx.group), None
+
+
+class _GatherSeq(torch.autograd.Function):
+    """Sequence shards ``(T/tp, d)`` -> replicated ``(T, d)``; the computation that
+    follows is replicated on every rank, so backward keeps this rank's rows."""
+
+    @staticmethod
+    def forward(ctx, x_shard, group):
+        ctx.group = group
+        return _all_gather_rows(x_shard, group)
+
+    @staticmethod
+    def backward(ctx, g):
+        W, r = dist.get_world_size(ctx.group), dist.get_rank(ctx.group)
+        n = g.shape[0] // W
+        return g[r * n:(r + 1) * n].contiguous(), None
+
+
+class _SumGrad(torch.autograd.Function):
+    """Identity whose backward sums the gradient over the group: a weight that is
+    replicated but applied to sequence shards (the block norms) gets the full gradient."""
+
+    @staticmethod
+    def forward(ctx, w, group):
+        ctx.group = group
+        return w.view_as(w)
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous()
+        dist.all_reduce(g, group=ctx.group)
+        return g, None
+
+
+def scatter_sequence(x: torch.Tensor, group) -> torch.Tensor:
+    """``(B, S, d)`` replicated -> ``(B*S/tp, d)`` sequence shard (flattened token order)."""
+    return _ScatterSeq.apply(x.reshape(-1, x.shape[-1]), group)
+
+
+def gather_sequence(x_shard: torch.Tensor, group, shape) -> torch.Tensor:
+    return _GatherSeq.apply(x_shard, group).view(shape)
+
+
+def sum_grad(w: torch.Tensor, group) -> torch.Tensor:
+    return _SumGrad.apply(w, group)
+
+
+def column_parallel(x_shard: torch.Tensor, w: torch.Tensor, group, comm: Optional[TPComm]) -> torch.Tensor:
+    return _ColumnFn.apply(x_shard, w, comm, group)
+
+
+def row_parallel(x: torch.Tensor, w: torch.Tensor, group, comm: Optional[TPComm],
+                 residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    return _RowFn.apply(x, w, residual, comm, group)

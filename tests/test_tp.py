@@ -71,3 +71,69 @@ def test_tp_layers_collective_fallback_cpu():
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_tp_layers_fused_kernels_gpu():
     _check(run_ranks(_tp_case, 2, True, backend="nccl"), 2, 5e-2)
+
+
+def _hlrt_tp_case(rank, world, fused):
+    """HLRT with a tensor + sequence parallel Tier 1 against the same weights unsharded."""
+    import torch.distributed as dist
+
+    from genesis.model.hlrt import HLRT
+    from llm_research_b200.models.presets import build_hlrt_config
+    from llm_research_b200.parallel.tp import TPComm, tensor_parallel
+
+    dev = torch.device("cuda", rank) if fused else torch.device("cpu")
+    cfg = build_hlrt_config("toy")
+    cfg.gate_loss_weight = 0.0
+    torch.manual_seed(0)
+    full = HLRT(cfg).to(dev)
+    comm = TPComm(None, max_tokens=256, max_width=512, device=dev) if fused else None
+    with tensor_parallel(dist.group.WORLD, comm):
+        tp = HLRT(cfg).to(dev)
+    fp = dict(full.named_parameters())
+    with torch.no_grad():
+        for name, p in tp.named_parameters():
+            src = fp[name]
+            dim = getattr(p, "_lrb_tp", None)
+            p.copy_(src if dim is None else src.chunk(world, dim=dim)[rank])
+    dt = torch.bfloat16 if fused else torch.float32
+    full.to(dt)
+    tp.to(dt)
+    ids = torch.randint(0, cfg.vocab_size, (2, 128), generator=torch.Generator().manual_seed(1)).to(dev)
+    out_f = full(ids)["logits"]
+    out_t = tp(ids)["logits"]
+    gl = torch.randn(out_f.shape, generator=torch.Generator().manual_seed(2)).to(dev, dt)
+    (out_f.float() * gl.float()).sum().backward()
+    (out_t.float() * gl.float()).sum().backward()
+    res = {"logits": (out_f.float().cpu(), out_t.float().cpu()), "grads": {}}
+    for name, p in tp.named_parameters():
+        if p.grad is None:
+            continue
+        g_full = fp[name].grad
+        dim = getattr(p, "_lrb_tp", None)
+        ref = g_full if dim is None else g_full.chunk(world, dim=dim)[rank]
+        res["grads"][name] = (ref.float().cpu(), p.grad.float().cpu())
+    if comm is not None:
+        comm.heap.check()
+        comm.close()
+    return res
+
+
+def test_hlrt_tensor_parallel_tier1_matches_unsharded_cpu():
+    for res in run_ranks(_hlrt_tp_case, 2, False):
+        ref, got = res["logits"]
+        torch.testing.assert_close(got, ref, atol=1e-4, rtol=1e-4)
+        assert any("q_proj" in n for n in res["grads"]) and any("attn_norm" in n for n in res["grads"])
+        for name, (r, g) in res["grads"].items():
+            torch.testing.assert_close(g, r, atol=1e-4, rtol=1e-3, msg=name)
+
+
+@pytest.mark.gpu
+def test_hlrt_tensor_parallel_tier1_fused_kernels():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    for res in run_ranks(_hlrt_tp_case, 2, True, backend="nccl"):
+        ref, got = res["logits"]
+        assert ((got - ref).norm() / ref.norm()).item() < 2e-2
+        for name, (r, g) in res["grads"].items():
+            rel = ((g - r).norm() / (r.norm() + 1e-6)).item()
+            assert rel < 5e-2, (name, rel)
