@@ -61,6 +61,8 @@ def parse_args(argv=None):
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--precision", choices=["bf16", "nvfp4"], default="bf16",
                     help="linear-layer precision of the model (nvfp4: block-scaled FP4 training GEMMs)")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel group size for the Tier-1 trunk (consecutive ranks); FSDP over the rest")
     ap.add_argument("--ep", action="store_true",
                     help="expert parallelism over all ranks for MoE presets (each rank holds E/world experts)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -126,6 +128,26 @@ def run_ours(args) -> dict:
     import contextlib
 
     ep_ctx = contextlib.nullcontext()
+    tp = args.tp
+    assert world % tp == 0, "--tp must divide the number of GPUs"
+    dp_world, dp_rank = world // tp, rank // tp
+    tp_group = dp_group = tp_comm = None
+    if tp > 1:
+        from llm_research_b200.parallel.tp import TPComm, tensor_parallel
+
+        for i in range(dp_world):  # every rank creates every group, in the same order
+            grp = dist.new_group(list(range(i * tp, (i + 1) * tp)))
+            if i == dp_rank:
+                tp_group = grp
+        for j in range(tp):
+            grp = dist.new_group(list(range(j, world, tp)))
+            if j == rank % tp:
+                dp_group = grp
+        d_ff = cfg.tier1_d_ff or 4 * cfg.d_model
+        width = max(2 * d_ff // tp, (cfg.tier1_num_heads + 2 * (cfg.tier1_num_kv_heads or cfg.tier1_num_heads))
+                    * (cfg.d_model // cfg.tier1_num_heads) // tp, cfg.d_model)
+        tp_comm = TPComm(tp_group, max_tokens=micro * S, max_width=width, device=device)
+        ep_ctx = tensor_parallel(tp_group, tp_comm)
     if args.ep and cfg.tier1_moe_num_experts:
         from llm_research_b200.parallel.expert_parallel import EPComm, expert_parallel
 
@@ -143,9 +165,11 @@ def run_ours(args) -> dict:
         scheduler_kwargs={"base_lr": 3e-4, "min_lr": 2e-5, "warmup_steps": 10, "total_steps": 1000},
         tokenizer=TokenizerWrapper(backend="char", vocab_size=cfg.vocab_size),
         config={"gradient_accumulation_steps": accum, "max_grad_norm": 1.0, "sync_metrics": False},
-        fsdp_config=FSDPConfig(sharding_strategy="FULL_SHARD", mixed_precision="bf16", activation_checkpointing=False),
+        fsdp_config=FSDPConfig(sharding_strategy="FULL_SHARD", mixed_precision="bf16", activation_checkpointing=False,
+                               process_group=dp_group, tp_group=tp_group),
     )
-    g = torch.Generator().manual_seed(args.seed * 1000 + rank)
+    # Ranks of one tensor-parallel group train on the same sequences.
+    g = torch.Generator().manual_seed(args.seed * 1000 + dp_rank)
     host = torch.randint(0, cfg.vocab_size, (accum, micro, S), generator=g, dtype=torch.int64).pin_memory()
     dev_batches = [host[i].to(device) for i in range(accum)]
 
@@ -204,7 +228,7 @@ def run_ours(args) -> dict:
         step(dev_batches)
         exposed = _max_over_ranks(engine.stop_exposed_comm_measurement(), dist, device)
 
-    tokens_per_step = world * accum * micro * S
+    tokens_per_step = dp_world * accum * micro * S
     value = tokens_per_step * args.steps / (dev_ms / 1000.0)
     flops = count_flops_per_token(cfg, S)
     res = {
@@ -223,11 +247,12 @@ def run_ours(args) -> dict:
         "impl": "ours",
         "config": {
             "model": MODEL_NAMES.get(args.preset, args.preset),
-            "global_batch": world * accum * micro,
+            "global_batch": dp_world * accum * micro,
             "seq_len": S,
             "micro_batch": micro,
             "grad_accum": accum,
-            "parallelism": (f"fsdp{world} (FULL_SHARD, bf16 compute, fp32 master) + distributed Muon"
+            "parallelism": (f"fsdp{dp_world} (FULL_SHARD, bf16 compute, fp32 master) + distributed Muon"
+                            + (f" + tp{tp} (sequence parallel Tier 1)" if tp > 1 else "")
                             + (f" + ep{world}" if args.ep else "")),
             "linear_precision": args.precision,
             "preset": args.preset,
@@ -244,6 +269,8 @@ def run_ours(args) -> dict:
     }
     if dist.is_initialized():
         dist.barrier()
+        if tp_comm is not None:
+            tp_comm.close()
         dist.destroy_process_group()
     return res if rank == 0 else None
 
@@ -361,7 +388,7 @@ def run_reference(args) -> dict:
         e2e = {"value": world * accum * micro * S * args.steps / e2e_s, "unit": "tokens/s",
                "h2d_bytes_per_step": int(host.numel() * host.element_size()), "d2h_bytes_per_step": 4 * accum,
                "ms_per_step": e2e_s * 1000.0 / args.steps}
-    tokens_per_step = world * accum * micro * S
+    tokens_per_step = dp_world * accum * micro * S
     res = {
         "metric": METRIC,
         "value": tokens_per_step * args.steps / (dev_ms / 1000.0),
@@ -386,6 +413,8 @@ def run_reference(args) -> dict:
     }
     if dist.is_initialized():
         dist.barrier()
+        if tp_comm is not None:
+            tp_comm.close()
         dist.destroy_process_group()
     return res if rank == 0 else None
 

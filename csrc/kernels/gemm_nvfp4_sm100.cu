@@ -8,30 +8,44 @@
 // at byte 16*(m % 32) + 4*(m / 32) + j; atoms are ordered K-fastest within a
 // 128-row block (``nvfp4_swizzle_scales`` produces it).
 //
-// CTA = one 128 x 128 output tile, 6 warps:
+// CTA = one 128 x 256 output tile (two 128-column halves sharing the A tile;
+// 128 x 128 when N is not a multiple of 256), 6 warps:
 //   warp 0      producer: per K-stage (256 elements = 128 bytes per row) TMA
 //               loads of the A and B tiles (128-byte swizzle) and bulk copies
 //               of the four SFA and four SFB atoms, into a 4-stage ring;
 //   warp 1      TMEM owner + MMA issue: tcgen05.cp of the stage's scale atoms
-//               into TMEM (two alternating column sets), then four
-//               kind::mxf4nvf4 block16 MMAs (K = 64 each);
+//               into TMEM (two alternating column sets), then per half four
+//               kind::mxf4nvf4 block16 MMAs (M = N = 128, K = 64 each);
 //   warps 2..5  epilogue: tcgen05.ld, scale by sA*sB, bf16 stores.
 // tcgen05.cp and tcgen05.mma issued by one thread execute in order, so a
 // stage's scale copy precedes its MMAs without a wait.  All waits are bounded.
 #include "../common.cuh"
 #include "sm100.cuh"
 
+#include <cstdlib>
+
 namespace lrb {
 namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 128, BKE = 256, STAGES = 4;  // BKE: FP4 elements per stage
+constexpr int BM = 128, BKE = 256;  // BKE: FP4 elements per stage
 constexpr int kThreads = 192;
-constexpr uint32_t kStageA = BM * BKE / 2, kStageB = BN * BKE / 2;  // 16 KB each
-constexpr uint32_t kAtom = 512, kStageSF = 4 * kAtom;               // four 64-element atoms
-constexpr uint32_t kStageBytes = kStageA + kStageB + 2 * kStageSF;
-constexpr size_t kSmem = 1024 + STAGES * (size_t)kStageBytes + 256;
+constexpr uint32_t kStageA = BM * BKE / 2;  // 16 KB
+constexpr uint32_t kAtom = 512, kAtomsPerStage = 4;  // four 64-element atoms per 128 rows
+// NT = 128-column halves of the output tile (1: 128 x 128, 2: 128 x 256 sharing the A tile).
+template <int NT>
+struct Cfg {
+  static constexpr uint32_t kStageB = NT * 128 * BKE / 2;
+  static constexpr uint32_t kStageSFA = kAtomsPerStage * kAtom;
+  static constexpr uint32_t kStageSFB = NT * kAtomsPerStage * kAtom;
+  static constexpr uint32_t kStageBytes = kStageA + kStageB + kStageSFA + kStageSFB;
+  static constexpr uint32_t kTmemCols = NT == 1 ? 256 : 512;
+  static constexpr uint32_t kSFA = NT * 128;   // TMEM column of the SFA sets (2 sets x 16 columns)
+  static constexpr uint32_t kSFB = kSFA + 32;  // NT halves x 2 sets x 16 columns
+};
+template <int NT, int STG>
+constexpr size_t smem_bytes() { return 1024 + STG * (size_t)Cfg<NT>::kStageBytes + 256; }
 
 struct Nvfp4Args {
   void* C;
@@ -45,19 +59,22 @@ struct Nvfp4Args {
   int vec_ok;
 };
 
+template <int NT, int STG>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Nvfp4Args a) {
+  using C_ = Cfg<NT>;
+  constexpr int BN = NT * 128;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + STAGES * kStageBytes);
-  uint64_t* full = bars;             // [STAGES]
-  uint64_t* empty = bars + STAGES;   // [STAGES]
-  uint64_t* acc_full = bars + 2 * STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
-  auto sA = [&](int s) { return base + s * kStageBytes; };
-  auto sB = [&](int s) { return base + s * kStageBytes + kStageA; };
-  auto sSFA = [&](int s) { return base + s * kStageBytes + kStageA + kStageB; };
-  auto sSFB = [&](int s) { return base + s * kStageBytes + kStageA + kStageB + kStageSF; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + STG * C_::kStageBytes);
+  uint64_t* full = bars;          // [STG]
+  uint64_t* empty = bars + STG;   // [STG]
+  uint64_t* acc_full = bars + 2 * STG;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STG + 1);
+  auto sA = [&](int s) { return base + s * C_::kStageBytes; };
+  auto sB = [&](int s) { return base + s * C_::kStageBytes + kStageA; };
+  auto sSFA = [&](int s) { return base + s * C_::kStageBytes + kStageA + C_::kStageB; };
+  auto sSFB = [&](int s) { return base + s * C_::kStageBytes + kStageA + C_::kStageB + C_::kStageSFA; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tm = blockIdx.y, tn = blockIdx.x;
@@ -66,7 +83,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int katoms = a.K / 64;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
+    for (int i = 0; i < STG; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
@@ -76,41 +93,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, C_::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tAcc = tmem, tSFA = tmem + 128, tSFB = tmem + 160;  // SF: 2 sets x 16 columns each
+  const uint32_t tAcc = tmem, tSFA = tmem + C_::kSFA, tSFB = tmem + C_::kSFB;
 
   if (warp == 0) {
     if (lane == 0) {
       int armed = 0;
       for (int j = 0; j < nk; ++j) {
-        const int st = j % STAGES;
-        const uint32_t ph = (j / STAGES) & 1;
+        const int st = j % STG;
+        const uint32_t ph = (j / STG) & 1;
         if (!mbar_wait(&empty[st], ph ^ 1, a.err, kErrTmaWait)) break;
-        mbar_arrive_expect_tx(&full[st], kStageBytes);
+        mbar_arrive_expect_tx(&full[st], C_::kStageBytes);
         tma_load_2d(sA(st), &tmA, &full[st], j * (BKE / 2), m0);
-        tma_load_2d(sB(st), &tmB, &full[st], j * (BKE / 2), n0);
-        bulk_load(sSFA(st), a.sfa + ((int64_t)tm * katoms + j * 4) * kAtom, kStageSF, &full[st]);
-        bulk_load(sSFB(st), a.sfb + ((int64_t)tn * katoms + j * 4) * kAtom, kStageSF, &full[st]);
+        bulk_load(sSFA(st), a.sfa + ((int64_t)tm * katoms + j * 4) * kAtom, C_::kStageSFA, &full[st]);
+#pragma unroll
+        for (int h = 0; h < NT; ++h) {
+          tma_load_2d(sB(st) + h * (128 * BKE / 2), &tmB, &full[st], j * (BKE / 2), n0 + h * 128);
+          bulk_load(sSFB(st) + h * C_::kStageSFA, a.sfb + ((int64_t)(tn * NT + h) * katoms + j * 4) * kAtom,
+                    C_::kStageSFA, &full[st]);
+        }
         ++armed;
       }
-      for (int i = 1; i <= STAGES && i <= armed; ++i) {
+      for (int i = 1; i <= STG && i <= armed; ++i) {
         const int j = armed - i;
-        mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, 0);
+        mbar_wait(&full[j % STG], (j / STG) & 1, nullptr, 0);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_nvfp4(BM, BN);
+      constexpr uint32_t idesc = umma_idesc_nvfp4(BM, 128);
       bool ok = true;
       for (int j = 0; j < nk && ok; ++j) {
-        const int st = j % STAGES;
-        const uint32_t ph = (j / STAGES) & 1;
+        const int st = j % STG;
+        const uint32_t ph = (j / STG) & 1;
         if (!mbar_wait(&full[st], ph, a.err, kErrMmaWait)) { ok = false; break; }
         tc_fence_after();
         const uint32_t set = (j & 1) * 16;
@@ -118,13 +139,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           tmem_cp_32x128b_x4(tSFA + set + kk * 4, sf_desc(fa + kk * kAtom));
-          tmem_cp_32x128b_x4(tSFB + set + kk * 4, sf_desc(fb + kk * kAtom));
+#pragma unroll
+          for (int h = 0; h < NT; ++h)
+            tmem_cp_32x128b_x4(tSFB + h * 32 + set + kk * 4, sf_desc(fb + h * C_::kStageSFA + kk * kAtom));
         }
         const uint32_t pa = smem_addr(sA(st)), pb = smem_addr(sB(st));
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)  // 64 FP4 elements = 32 bytes of the 128-byte swizzled row
-          umma_nvfp4(tAcc, umma_desc_k_sw128(pa + kk * 32), umma_desc_k_sw128(pb + kk * 32), idesc,
-                     tSFA + set + kk * 4, tSFB + set + kk * 4, (j | kk) != 0);
+        for (int kk = 0; kk < 4; ++kk) {  // 64 FP4 elements = 32 bytes of the 128-byte swizzled row
+#pragma unroll
+          for (int h = 0; h < NT; ++h)
+            umma_nvfp4(tAcc + h * 128, umma_desc_k_sw128(pa + kk * 32),
+                       umma_desc_k_sw128(pb + h * (128 * BKE / 2) + kk * 32), idesc, tSFA + set + kk * 4,
+                       tSFB + h * 32 + set + kk * 4, (j | kk) != 0);
+        }
         umma_commit(&empty[st]);
       }
       umma_commit(acc_full);
@@ -148,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < 32; ++e) r[e] = 0u;
       }
       const int col0 = n0 + c * 32;
-      if (row >= a.M) continue;
+      if (row >= a.M || col0 >= a.N) continue;
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + (int64_t)row * a.ldc + col0;
       if (a.vec_ok && col0 + 32 <= a.N) {
 #pragma unroll
@@ -167,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, C_::kTmemCols);
   }
 }
 
@@ -230,9 +257,21 @@ at::Tensor gemm_nvfp4(const at::Tensor& A, const at::Tensor& sfa, const at::Tens
   CUtensorMap ta = fp4_map(A.data_ptr(), M, K / 2, A.stride(0)), tb = fp4_map(B.data_ptr(), N, K / 2, B.stride(0));
   Nvfp4Args args{C.data_ptr(), N, (int)M, (int)N, (int)K, sfa.data_ptr<uint8_t>(), sfb.data_ptr<uint8_t>(),
                  sa.data_ptr<float>(), sb.data_ptr<float>(), nvfp4_error_word(A.device()), (N % 8) == 0 ? 1 : 0};
-  LRB_CUDA_CHECK(cudaFuncSetAttribute(gemm_nvfp4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-  dim3 grid((unsigned)nb, (unsigned)mb);
-  gemm_nvfp4_kernel<<<grid, kThreads, kSmem, stream()>>>(ta, tb, args);
+  // 128 x 256 tiles (the A tile feeds two N halves) when N allows; LRB_NVFP4_TILE=128 forces 128 x 128.
+  static const int tile_env = [] {
+    const char* e = std::getenv("LRB_NVFP4_TILE");
+    return e ? std::atoi(e) : 256;
+  }();
+  const bool wide = tile_env != 128 && N % 256 == 0;
+  if (wide) {
+    constexpr size_t sm = smem_bytes<2, 4>();
+    LRB_CUDA_CHECK(cudaFuncSetAttribute(gemm_nvfp4_kernel<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    gemm_nvfp4_kernel<2, 4><<<dim3((unsigned)(N / 256), (unsigned)mb), kThreads, sm, stream()>>>(ta, tb, args);
+  } else {
+    constexpr size_t sm = smem_bytes<1, 4>();
+    LRB_CUDA_CHECK(cudaFuncSetAttribute(gemm_nvfp4_kernel<1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    gemm_nvfp4_kernel<1, 4><<<dim3((unsigned)nb, (unsigned)mb), kThreads, sm, stream()>>>(ta, tb, args);
+  }
   LRB_LAUNCH_CHECK();
   return C;
 }

@@ -83,7 +83,16 @@ template <typename T>
 __global__ void absmax_kernel(const T* __restrict__ x, int64_t n, float* __restrict__ out) {
   __shared__ float red[32];
   float m = 0.f;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+  constexpr int V = 16 / sizeof(T);
+  const int64_t nv = (reinterpret_cast<uintptr_t>(x) % 16 == 0) ? n / V : 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += stride) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(x) + i);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(to_f(e[j])));
+  }
+  for (int64_t i = nv * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
     m = fmaxf(m, fabsf(to_f(x[i])));
   m = block_max(m, red);
   if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(out), __float_as_int(m));  // m >= 0: int order == float order
@@ -104,14 +113,14 @@ __global__ void nvfp4_quant_kernel(const T* __restrict__ x, const float* __restr
   for (int i = 0; i < 16; ++i) { v[i] = to_f(xp[i]); bm = fmaxf(bm, fabsf(v[i])); }
   const __nv_fp8_e4m3 s8(fminf(bm / (6.f * st), 448.f));
   sb[b] = s8;
-  const float denom = fmaxf(float(s8) * st, 1e-30f);
+  const float inv = 1.f / fmaxf(float(s8) * st, 1e-30f);  // one reciprocal per block
   uint8_t out[8];
 #pragma unroll
   for (int i = 0; i < 16; i += 2) {
     int c[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const float y = v[i + j] / denom;
+      const float y = v[i + j] * inv;
       const float a = fabsf(y);
       int code;
       if (stochastic) {
@@ -156,11 +165,11 @@ __device__ __forceinline__ void quant_block16(const float* v, float st, bool sto
   for (int i = 0; i < 16; ++i) bm = fmaxf(bm, fabsf(v[i]));
   const __nv_fp8_e4m3 s8(fminf(bm / (6.f * st), 448.f));
   sbyte = s8.__x;
-  const float denom = fmaxf(float(s8) * st, 1e-30f);
+  const float inv = 1.f / fmaxf(float(s8) * st, 1e-30f);
   uint32_t w[2] = {0u, 0u};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const float y = v[i] / denom;
+    const float y = v[i] * inv;
     const float a = fabsf(y);
     int code;
     if (stochastic) {

@@ -82,7 +82,7 @@ def nvfp4_quantize(x2d: torch.Tensor, stochastic: bool = False, seed: int = 0):
     blk = xf.view(M, K // 16, 16)
     s_b = (blk.abs().amax(-1) / (FP4_MAX * s_t)).clamp(max=E4M3_MAX).to(torch.float8_e4m3fn)
     denom = (s_b.float() * s_t).clamp(min=1e-30)[:, :, None]
-    y = blk / denom
+    y = blk * (1.0 / denom)  # one reciprocal per block, as the kernels do
     mag = y.abs()
     if stochastic:
         gen = torch.Generator(device="cpu").manual_seed(seed)

@@ -16,7 +16,10 @@ time assignment by Newton-Schulz FLOPs, identical on all ranks) and:
 
 So the reduce-scatter of the engine plus two bf16 all-to-alls carry all the
 optimizer traffic, and every rank runs Newton-Schulz on ~1/world of the
-matrices.  ``state_dict`` gathers the full per-parameter state in the layout
+matrices.  Under tensor parallelism (engine ``tp_group``) a TP-sharded matrix
+is all-gathered over the TP group on its owner (the TP peers own the same
+matrices), orthogonalised whole, and each peer keeps its slice, so the update
+equals that of the unsharded matrix.  ``state_dict`` gathers the full per-parameter state in the layout
 of ``torch.optim.Optimizer.state_dict`` with the reference's state keys
 (``olympus/optim/muon_adamw_hybrid.py:118-170``).
 """
@@ -82,9 +85,17 @@ class ShardedHybridOptimizer:
 
         pure = _pure_muon(optimizer_cls)
         max_ar = float(self.defaults.get("muon_max_aspect_ratio", 8.0))
+        # Tensor-parallel shards (``_lrb_tp`` = concatenation dim): Muon acts on the full
+        # matrix, gathered over the TP group on the owner (the TP peers own the same pids).
+        tpg = getattr(engine, "tp_group", None)
+        self.tp_world = dist.get_world_size(tpg) if tpg is not None else 1
+        self.tp_dim = {i.index: getattr(i.param, "_lrb_tp", None) for i in engine.params} if tpg is not None else {}
         self.is_muon = {}
         for info in engine.params:
-            m = len(info.shape) == 2 and (pure or max(info.shape) <= min(info.shape) * max_ar)
+            shape = list(info.shape)
+            if self.tp_dim.get(info.index) is not None:
+                shape[self.tp_dim[info.index]] *= self.tp_world
+            m = len(shape) == 2 and (pure or max(shape) <= min(shape) * max_ar)
             if pure and len(info.shape) != 2:
                 raise ValueError(f"Muon only supports 2-D parameters, got {info.name} {info.shape}")
             self.is_muon[info.index] = m
@@ -144,13 +155,13 @@ class ShardedHybridOptimizer:
         self.send_total = sum(self.send_splits)
         # owned matrices, grouped by shape -> stack layout
         owned = [pid for pid in self.muon_ids if self.owner[pid] == rank]
-        groups: Dict[Tuple[int, int], List[int]] = defaultdict(list)
+        groups: Dict[Tuple[Tuple[int, int], Optional[int]], List[int]] = defaultdict(list)
         for pid in owned:
-            groups[infos[pid].shape].append(pid)
+            groups[(infos[pid].shape, self.tp_dim.get(pid))].append(pid)
         self.groups = list(groups.items())
         self.stack_base: Dict[int, int] = {}
         base = 0
-        for shape, pids in self.groups:
+        for _, pids in self.groups:
             for pid in pids:
                 self.stack_base[pid] = base
                 base += infos[pid].numel
@@ -258,6 +269,12 @@ class ShardedHybridOptimizer:
         gsq.index_add_(0, idx, gnorm_seg.pow(2))
         if self.world > 1:
             dist.all_reduce(gsq, group=eng.pg)
+        if self.tp_world > 1:  # ||g||^2 of a TP-sharded matrix: sum over its shards
+            mask = torch.tensor([self.tp_dim.get(p) is not None for p in self.muon_ids], device=dev)
+            part = gsq * mask
+            dist.all_reduce(part, group=eng.tp_group)
+            gsq = torch.where(mask, part, gsq)
+        if self.world > 1:
             recv = torch.empty(self.recv_total, dtype=xdt, device=dev)
             dist.all_to_all_single(recv, send, self.recv_splits, self.send_splits, group=eng.pg)
         else:
@@ -266,12 +283,19 @@ class ShardedHybridOptimizer:
         stack.index_copy_(0, self.recv_to_stack, recv)
         gnorm = gsq.sqrt()
         base = 0
-        for shape, pids in self.groups:
+        for (shape, tpd), pids in self.groups:
             n = len(pids)
             numel = shape[0] * shape[1]
             block = stack[base: base + n * numel].view(n, shape[0], shape[1])
-            o = ops.newton_schulz(block, steps=ns_steps)
-            onorm = o.float().flatten(1).norm(dim=1)
+            if tpd is None:
+                o = ops.newton_schulz(block, steps=ns_steps)
+                onorm = o.float().flatten(1).norm(dim=1)
+            else:
+                parts = [torch.empty_like(block) for _ in range(self.tp_world)]
+                dist.all_gather(parts, block.contiguous(), group=eng.tp_group)
+                o_full = ops.newton_schulz(torch.cat(parts, dim=1 + tpd), steps=ns_steps)
+                onorm = o_full.float().flatten(1).norm(dim=1)
+                o = o_full.chunk(self.tp_world, dim=1 + tpd)[dist.get_rank(eng.tp_group)]
             gn = gnorm[torch.tensor([self.muon_pos[p] for p in pids], device=dev)]
             scale = (lr * gn / (onorm + 1e-8)).view(n, 1, 1)
             block.copy_((o.float() * scale).to(xdt))

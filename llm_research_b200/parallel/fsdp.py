@@ -141,10 +141,14 @@ class FlatShardEngine(nn.Module):
         device: Optional[torch.device] = None,
         reduce_dtype: torch.dtype = torch.float32,
         comm: Optional[str] = None,
+        tp_group: Optional[dist.ProcessGroup] = None,
     ) -> None:
         super().__init__()
         self.module = module
         self.pg = process_group
+        # Tensor parallelism across another group: parameters tagged ``_lrb_tp`` are
+        # this rank's shards of larger weights, the rest are replicated over it.
+        self.tp_group = tp_group
         self.distributed = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(process_group) if self.distributed else 1
         self.rank = dist.get_rank(process_group) if self.distributed else 0
@@ -159,6 +163,7 @@ class FlatShardEngine(nn.Module):
         self.comm_stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
         classes = tuple(unit_classes) if unit_classes is not None else default_unit_classes()
         self._build_units(classes)
+        self._rep_ranges = self._replicated_ranges() if tp_group is not None else None
         self._register_hooks()
         import os
 
@@ -241,6 +246,25 @@ class FlatShardEngine(nn.Module):
                 self._free(u)
             del full
         self.unit_order = [u.index for u in self.units[1:]]
+
+    def _replicated_ranges(self) -> List[Tuple[int, int, int]]:
+        """(unit, lo, hi) spans of this rank's grad shards that hold parameters not
+        tagged ``_lrb_tp`` (replicated over the tensor-parallel group); merged."""
+        out: List[Tuple[int, int, int]] = []
+        for u in self.units:
+            lo_s, hi_s = (self.rank * u.shard, (self.rank + 1) * u.shard) if self.world > 1 else (0, u.total)
+            for info in u.params:
+                if getattr(info.param, "_lrb_tp", None) is not None:
+                    continue
+                lo, hi = max(info.offset, lo_s), min(info.offset + info.numel, hi_s)
+                if lo >= hi:
+                    continue
+                lo, hi = lo - lo_s, hi - lo_s
+                if out and out[-1][0] == u.index and out[-1][2] == lo:
+                    out[-1] = (u.index, out[-1][1], hi)
+                else:
+                    out.append((u.index, lo, hi))
+        return out
 
     # ------------------------------------------------------------ p2p comm
     def _setup_p2p(self) -> None:
@@ -513,8 +537,17 @@ class FlatShardEngine(nn.Module):
         local = [p.grad for _, p in self.local_params if p.grad is not None]
         for gr in local:  # disjoint per rank, like the shards: one sum over the group covers both
             sq += gr.float().pow(2).sum()
+        if self._rep_ranges is not None:
+            # Replicated parameters appear on every TP rank: count them once in the sum below.
+            tp = dist.get_world_size(self.tp_group)
+            rep = torch.zeros((), dtype=torch.float32, device=self.device)
+            for ui, lo, hi in self._rep_ranges:
+                rep += self.units[ui].grad_shard[lo:hi].float().pow(2).sum()
+            sq = sq - (1.0 - 1.0 / tp) * rep
         if self.world > 1:
             dist.all_reduce(sq, group=self.pg)
+        if self.tp_group is not None:
+            dist.all_reduce(sq, group=self.tp_group)
         norm = sq.sqrt()
         coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
         for u in self.units:

@@ -129,7 +129,11 @@ def _reduce_scatter_rows(x: torch.Tensor, group) -> torch.Tensor:
 
 
 def _fused_ok(comm: Optional[TPComm], x: torch.Tensor, tokens: int, widths) -> bool:
-    return (comm is not None and x.is_cuda and x.dtype == torch.bfloat16
+    # The fused kernels multiply in bf16; under NVFP4 linear precision the layers
+    # take the collective path around the NVFP4 GEMM instead.
+    from llm_research_b200.ops.linear import get_linear_precision
+
+    return (comm is not None and x.is_cuda and x.dtype == torch.bfloat16 and get_linear_precision() == "bf16"
             and all(comm.fits(tokens, w) for w in widths))
 
 

@@ -24,7 +24,7 @@ from __future__ import annotations
 import functools
 import logging
 from dataclasses import dataclass
-from typing import Optional, Set, Type
+from typing import Any, Optional, Set, Type
 
 import torch
 import torch.nn as nn
@@ -42,6 +42,10 @@ class FSDPConfig:
     cpu_offload: bool = False
     backward_prefetch: str = "BACKWARD_PRE"
     min_num_params: int = 1_000_000
+    # Extensions (not in the reference): shard over this group instead of the
+    # world; ``tp_group`` is the tensor-parallel group of the Tier-1 trunk.
+    process_group: Any = None
+    tp_group: Any = None
 
 
 def get_sharding_strategy(name: str) -> str:
@@ -87,6 +91,8 @@ def wrap_model_fsdp(model: nn.Module, fsdp_config: FSDPConfig, device_id: Option
         reshard_after_forward=(strategy == "FULL_SHARD"),
         unit_classes=(TransformerBlock,),
         device=device,
+        process_group=fsdp_config.process_group,
+        tp_group=fsdp_config.tp_group,
     )
     logger.info("wrapped %s: %s, compute %s, %.1fM params", type(model).__name__, strategy, dtype,
                 sum(p.numel for p in engine.params) / 1e6)

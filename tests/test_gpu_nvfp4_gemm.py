@@ -4,7 +4,8 @@ import pytest
 import torch
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("M,N,K", [(128, 128, 256), (256, 384, 512), (300, 200, 1024), (1024, 1024, 4096)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 256), (256, 384, 512), (300, 200, 1024), (1024, 1024, 4096),
+                                   (256, 512, 512), (300, 768, 1024)])
 def test_nvfp4_gemm_matches_dequantised_product(M, N, K):
     from llm_research_b200._ext import native
     from llm_research_b200.ops.quant import NVFP4Tensor, matmul_nvfp4

@@ -137,3 +137,52 @@ def test_hlrt_tensor_parallel_tier1_fused_kernels():
         for name, (r, g) in res["grads"].items():
             rel = ((g - r).norm() / (r.norm() + 1e-6)).item()
             assert rel < 5e-2, (name, rel)
+
+
+def _fsdp_tp_train(rank, world):
+    """FSDP x2 (dp) + TP x2 on 4 gloo ranks, Muon hybrid + clipping, two steps."""
+    import torch.distributed as dist
+
+    from genesis.training.train_phase1_bootstrap import ntp_objective
+    from llm_research_b200.parallel.tp import tensor_parallel
+    from olympus.core.training_orchestrator import ModelConfig, ObjectiveConfig
+    from olympus.distributed.distributed_orchestrator import DistributedTrainingOrchestrator
+    from olympus.distributed.fsdp_wrapper import FSDPConfig
+    from olympus.optim import MuonAdamWHybrid
+    from tests.test_engine import _data, _toy_model
+
+    tp = 2
+    tp_groups = [dist.new_group([0, 1]), dist.new_group([2, 3])]
+    dp_groups = [dist.new_group([0, 2]), dist.new_group([1, 3])]
+    tpg, dpg = tp_groups[rank // tp], dp_groups[rank % tp]
+    full = _toy_model()
+    with tensor_parallel(tpg):
+        model = _toy_model()
+    fp = dict(full.named_parameters())
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            dim = getattr(p, "_lrb_tp", None)
+            p.copy_(fp[name] if dim is None else fp[name].chunk(tp, dim=dim)[rank % tp])
+    opt = MuonAdamWHybrid(model.parameters(), lr_muon=0.02, lr_adamw=1e-3, weight_decay_muon=0.01)
+    orch = DistributedTrainingOrchestrator(
+        fsdp_config=FSDPConfig(mixed_precision="fp32", activation_checkpointing=False, process_group=dpg, tp_group=tpg),
+        device=torch.device("cpu"))
+    orch.add_model(ModelConfig("hlrt", model, opt, max_grad_norm=1.0))
+    orch.add_objective(ObjectiveConfig("ntp", ntp_objective))
+    data = _data()
+    d = rank // tp
+    for _ in range(2):
+        orch.step({"input_ids": data[2 * d: 2 * d + 2]})
+    sd = orch._models["hlrt"].model.full_state_dict()
+    return {k: (v, getattr(dict(model.named_parameters())[k], "_lrb_tp", None)) for k, v in sd.items()}
+
+
+def test_fsdp_plus_tensor_parallel_matches_single_process():
+    from tests.test_engine import _data, _toy_model, _train
+
+    single, _ = _train(_toy_model(), [_data()], engine=False, steps=2)
+    res = run_ranks(_fsdp_tp_train, 4)
+    for rank, sd in enumerate(res):
+        for k, (v, dim) in sd.items():
+            ref = single[k] if dim is None else single[k].chunk(2, dim=dim)[rank % 2]
+            torch.testing.assert_close(v, ref, atol=5e-5, rtol=1e-4, msg=f"rank {rank} {k}")
