@@ -58,6 +58,11 @@ int64_t attn_sm100_error(int64_t);
 int64_t attn_bwd_sm100_error(int64_t);
 // memory.cu
 std::tuple<at::Tensor, at::Tensor, at::Tensor> topk_softmax_gather(const at::Tensor&, const at::Tensor&, int64_t);
+std::tuple<at::Tensor, at::Tensor> memory_topk_candidates(const at::Tensor&, const at::Tensor&, int64_t);
+int64_t memory_topk_error(int64_t);
+std::tuple<at::Tensor, at::Tensor> topk_gather_fwd(const at::Tensor&, const at::Tensor&, const at::Tensor&);
+at::Tensor topk_gather_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                           const at::Tensor&);
 // gemm_nvfp4_sm100.cu
 at::Tensor gemm_nvfp4(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
                       const at::Tensor&);
@@ -132,6 +137,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_sm100_error", &lrb::attn_sm100_error);
   m.def("attn_bwd_sm100_error", &lrb::attn_bwd_sm100_error);
   m.def("topk_softmax_gather", &lrb::topk_softmax_gather);
+  m.def("memory_topk_candidates", &lrb::memory_topk_candidates,
+        "tcgen05 similarity + streaming top-32 per query over bank slices");
+  m.def("memory_topk_error", &lrb::memory_topk_error);
+  m.def("topk_gather_fwd", &lrb::topk_gather_fwd);
+  m.def("topk_gather_bwd", &lrb::topk_gather_bwd);
   m.def("gemm_nvfp4", &lrb::gemm_nvfp4);
   m.def("gemm_nvfp4_error", &lrb::gemm_nvfp4_error);
   m.def("ep_push", &lrb::ep_push);

@@ -139,14 +139,6 @@ __global__ void nvfp4_quant_kernel(const T* __restrict__ x, const float* __restr
 }
 
 
-// E2M1 code of a magnitude, round to nearest with ties to the even code: the
-// midpoints between grid values are 0.25 0.75 1.25 1.75 2.5 3.5 5; a tie at a
-// midpoint goes to the even code (0, 2, 2, 4, 4, 6, 6), which makes the
-// comparisons alternate between strict and non-strict.
-__device__ __forceinline__ int e2m1_rne_fast(float a) {
-  return (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) + (a >= 3.5f) + (a > 5.f);
-}
-
 __device__ __forceinline__ int e2m1_sr_fast(float a, float r) {
   const int lo = (a >= 0.5f) + (a >= 1.f) + (a >= 1.5f) + (a >= 2.f) + (a >= 3.f) + (a >= 4.f) + (a >= 6.f);
   if (lo == 7) return 7;
@@ -157,9 +149,25 @@ __device__ __forceinline__ int e2m1_sr_fast(float a, float r) {
 
 // One 16-element NVFP4 block: e4m3 scale byte and 8 packed bytes (low nibble first).
 // ridx(i) gives the element index that seeds stochastic rounding.
-__device__ __forceinline__ void quant_block16(const float* v, float st, bool stochastic, uint32_t seed,
-                                              uint32_t hi, uint32_t idx0, uint32_t idx_step, uint8_t& sbyte,
-                                              uint2& packed) {
+// Two fp32 values -> one byte of E2M1 codes (lo in the low nibble), round to
+// nearest even with saturation to +-6: the hardware conversion, which rounds
+// as e2m1_rne does (ties to the even code; the one-thread-per-block quantiser
+// keeps the software rounding and serves as the check).
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
+  uint32_t out;
+  asm("{\n.reg .b8 t;\ncvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\ncvt.u32.u8 %0, t;\n}" : "=r"(out) : "f"(lo), "f"(hi));
+  return out;
+}
+
+// A value that rounds to zero keeps no sign: -0 nibbles (0x8) become 0x0.
+__device__ __forceinline__ uint32_t clear_negative_zero(uint32_t w) {
+  const uint32_t mag = w & 0x77777777u;
+  return mag | ((mag + 0x77777777u) & 0x88888888u & w);
+}
+
+template <bool SR>
+__device__ __forceinline__ void quant_block16(const float* v, float st, uint32_t seed, uint32_t hi, uint32_t idx0,
+                                              uint8_t& sbyte, uint2& packed) {
   float bm = 0.f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) bm = fmaxf(bm, fabsf(v[i]));
@@ -167,21 +175,21 @@ __device__ __forceinline__ void quant_block16(const float* v, float st, bool sto
   sbyte = s8.__x;
   const float inv = 1.f / fmaxf(float(s8) * st, 1e-30f);
   uint32_t w[2] = {0u, 0u};
+  if constexpr (!SR) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float y = v[i] * inv;
-    const float a = fabsf(y);
-    int code;
-    if (stochastic) {
-      const float r = (hash3(seed, hi, idx0 + (uint32_t)i * idx_step) >> 8) * (1.f / 16777216.f);
-      code = e2m1_sr_fast(a, r);
-    } else {
-      code = e2m1_rne_fast(a);
+    for (int i = 0; i < 16; i += 2) w[i >> 3] |= cvt_e2m1x2(v[i] * inv, v[i + 1] * inv) << (4 * (i & 7));
+    packed = make_uint2(clear_negative_zero(w[0]), clear_negative_zero(w[1]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float y = v[i] * inv;
+      const float r = (hash3(seed, hi, idx0 + (uint32_t)i) >> 8) * (1.f / 16777216.f);
+      int code = e2m1_sr_fast(fabsf(y), r);
+      if (y < 0.f && code > 0) code |= 8;
+      w[i >> 3] |= (uint32_t)code << (4 * (i & 7));
     }
-    if (y < 0.f && code > 0) code |= 8;
-    w[i >> 3] |= (uint32_t)code << (4 * (i & 7));
+    packed = make_uint2(w[0], w[1]);
   }
-  packed = make_uint2(w[0], w[1]);
 }
 
 // Byte offset of the scale of (row, 16-element block jb) in the tensor-core
@@ -195,11 +203,11 @@ __device__ __forceinline__ int64_t sf_atom_offset(int64_t row, int64_t jb, int64
 // Tile of 128 rows x 64 columns of x (M, K) per CTA, 256 threads.
 // ROW: x quantised along K -> packed (M, K/2), scales in atom layout (M/128, K/64, 512).
 // COL: x^T quantised along M -> packed (K, M/2), scales (K/128, M/64, 512).
-template <typename T, bool ROW, bool COL>
+template <typename T, bool ROW, bool COL, bool SR>
 __global__ void __launch_bounds__(256) nvfp4_quant_dual_kernel(
     const T* __restrict__ x, int64_t M, int64_t K, const float* __restrict__ amax, uint8_t* __restrict__ pr,
     uint8_t* __restrict__ ar, uint8_t* __restrict__ pc, uint8_t* __restrict__ ac, float* __restrict__ st_out,
-    bool stochastic, uint32_t seed) {
+    uint32_t seed) {
   __shared__ float tile[128][65];
   const int64_t m0 = (int64_t)blockIdx.y * 128, k0 = (int64_t)blockIdx.x * 64;
   const float st = fmaxf(amax[0] / (6.f * 448.f), 1e-12f);
@@ -226,7 +234,7 @@ __global__ void __launch_bounds__(256) nvfp4_quant_dual_kernel(
       const int64_t e0 = (m0 + row) * K + k0 + j * 16;
       uint8_t sb;
       uint2 pk;
-      quant_block16(v, st, stochastic, seed, (uint32_t)(e0 >> 32), (uint32_t)e0, 1u, sb, pk);
+      quant_block16<SR>(v, st, seed, (uint32_t)(e0 >> 32), (uint32_t)e0, sb, pk);
       *reinterpret_cast<uint2*>(pr + ((m0 + row) * K + k0 + j * 16) / 2) = pk;
       ar[sf_atom_offset(m0 + row, (k0 >> 4) + j, K >> 6)] = sb;
     }
@@ -244,7 +252,7 @@ __global__ void __launch_bounds__(256) nvfp4_quant_dual_kernel(
       const int64_t e0 = kr * M + mc;  // element index of x^T
       uint8_t sb;
       uint2 pk;
-      quant_block16(v, st, stochastic, seed ^ 0x5bd1e995u, (uint32_t)(e0 >> 32), (uint32_t)e0, 1u, sb, pk);
+      quant_block16<SR>(v, st, seed ^ 0x5bd1e995u, (uint32_t)(e0 >> 32), (uint32_t)e0, sb, pk);
       *reinterpret_cast<uint2*>(pc + (kr * M + mc) / 2) = pk;
       ac[sf_atom_offset(kr, mc >> 4, M >> 6)] = sb;
     }
@@ -361,18 +369,19 @@ std::vector<at::Tensor> nvfp4_quantize_dual(const at::Tensor& x, const c10::opti
     uint8_t* a0 = rowwise ? ar.data_ptr<uint8_t>() : nullptr;
     uint8_t* p1 = colwise ? pc.data_ptr<uint8_t>() : nullptr;
     uint8_t* a1 = colwise ? ac.data_ptr<uint8_t>() : nullptr;
-    if (rowwise && colwise)
-      nvfp4_quant_dual_kernel<T, true, true><<<grid, 256, 0, stream()>>>(xp, M, K, amax.data_ptr<float>(), p0, a0, p1,
-                                                                         a1, st.data_ptr<float>(), stochastic,
-                                                                         (uint32_t)seed);
-    else if (rowwise)
-      nvfp4_quant_dual_kernel<T, true, false><<<grid, 256, 0, stream()>>>(xp, M, K, amax.data_ptr<float>(), p0, a0,
-                                                                          p1, a1, st.data_ptr<float>(), stochastic,
-                                                                          (uint32_t)seed);
-    else
-      nvfp4_quant_dual_kernel<T, false, true><<<grid, 256, 0, stream()>>>(xp, M, K, amax.data_ptr<float>(), p0, a0,
-                                                                          p1, a1, st.data_ptr<float>(), stochastic,
-                                                                          (uint32_t)seed);
+    auto launch = [&](auto kern) {
+      kern<<<grid, 256, 0, stream()>>>(xp, M, K, amax.data_ptr<float>(), p0, a0, p1, a1, st.data_ptr<float>(),
+                                       (uint32_t)seed);
+    };
+    if (stochastic) {
+      if (rowwise && colwise) launch(nvfp4_quant_dual_kernel<T, true, true, true>);
+      else if (rowwise) launch(nvfp4_quant_dual_kernel<T, true, false, true>);
+      else launch(nvfp4_quant_dual_kernel<T, false, true, true>);
+    } else {
+      if (rowwise && colwise) launch(nvfp4_quant_dual_kernel<T, true, true, false>);
+      else if (rowwise) launch(nvfp4_quant_dual_kernel<T, true, false, false>);
+      else launch(nvfp4_quant_dual_kernel<T, false, true, false>);
+    }
   });
   LRB_LAUNCH_CHECK();
   return {pr, ar, pc, ac, st};

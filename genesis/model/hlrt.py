@@ -61,6 +61,11 @@ class HLRTConfig:
     tier1_moe_d_ff: int | None = None
     tier1_moe_shared_experts: int = 0
     tier1_moe_capacity_factor: float = 1.25
+    # PHMA semantic-memory reads in the Tier-1 trunk (an extension): after every
+    # ``tier1_memory_every``-th block, top-k over a shared bank of ``memory_slots``.
+    tier1_memory_every: int = 0
+    memory_slots: int = 65536
+    memory_top_k: int = 32
 
     gate1_chunk_size: int = 32
     gate1_threshold: float = 0.5
@@ -117,7 +122,14 @@ class HLRT(StatefulModule):
             moe=(dict(num_experts=c.tier1_moe_num_experts, top_k=c.tier1_moe_top_k, d_ff=c.tier1_moe_d_ff,
                       shared=c.tier1_moe_shared_experts, capacity_factor=c.tier1_moe_capacity_factor)
                  if c.tier1_moe_num_experts else None),
+            memory=(dict(every=c.tier1_memory_every, d_key=c.d_model, d_value=c.d_model, top_k=c.memory_top_k)
+                    if c.tier1_memory_every else None),
         )
+        if c.tier1_memory_every:
+            from genesis.model.memory_layer import MemoryBank
+
+            self.memory_bank = MemoryBank(c.memory_slots, c.d_model, c.d_model)
+            self.tier1.bind_memory(self.memory_bank)
         self.gate1 = TierGate(d_model=c.d_model, chunk_size=c.gate1_chunk_size, threshold=c.gate1_threshold)
         self.latent_pool = LatentPooling(
             input_dim=c.d_model, output_dim=c.tier2_d_model, num_latent_vectors=c.num_latent_vectors,

@@ -101,6 +101,7 @@ class Tier1TokenProcessor(nn.Module):
         rope_base: float = 10000.0,
         norm_eps: float = 1e-6,
         moe: Optional[dict] = None,
+        memory: Optional[dict] = None,
     ) -> None:
         super().__init__()
         self.rotary_emb = RotaryEmbedding(dim=d_model // num_heads, max_seq_len=max_seq_len, base=rope_base)
@@ -114,6 +115,20 @@ class Tier1TokenProcessor(nn.Module):
                 )
                 for _ in range(num_layers)
             ])
+            # PHMA memory reads after every ``memory["every"]``-th block (extension).
+            self.memory_layers = nn.ModuleDict()
+            if memory and memory.get("every"):
+                from genesis.model.memory_layer import MemoryReadLayer
+
+                for i in range(num_layers):
+                    if (i + 1) % memory["every"] == 0:
+                        self.memory_layers[str(i)] = MemoryReadLayer(
+                            d_model, memory["d_key"], memory["d_value"], top_k=memory.get("top_k", 32),
+                            norm_eps=norm_eps)
+
+    def bind_memory(self, bank) -> None:
+        for m in self.memory_layers.values():
+            m.bind(bank)
 
     def forward(
         self,
@@ -129,12 +144,16 @@ class Tier1TokenProcessor(nn.Module):
 
             B, S, d = x.shape
             h = scatter_sequence(x, tp[0])
-            for layer in self.layers:
+            for i, layer in enumerate(self.layers):
                 h = layer(h, cos, sin, seq_shape=(B, S))
+                if str(i) in self.memory_layers:
+                    h = self.memory_layers[str(i)](h)
             return gather_sequence(h, tp[0], (B, S, d))
         assert tp is None, "tensor-parallel Tier 1 runs full causal sequences (no cache / mask / offset)"
         for i, layer in enumerate(self.layers):
             x = layer(x, cos, sin, attention_mask=attention_mask,
                       kv_cache=kv_cache[i] if kv_cache is not None else None,
                       position_offset=position_offset)
+            if str(i) in self.memory_layers:
+                x = self.memory_layers[str(i)](x)
         return x

@@ -125,6 +125,17 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
 
         return run, 6.0 * T * K * N, 0.0
 
+    def memory_read():
+        import torch.nn.functional as F
+
+        from llm_research_b200.ops.memory import bank_read
+
+        T, N, D = 8192, 65536, 4096  # one micro-batch of 2 x 4096 tokens against the 7B bank
+        keys = F.normalize(torch.randn(N, D, device="cuda"), dim=-1).to(torch.bfloat16)
+        values = torch.randn(N, D, device="cuda", dtype=torch.bfloat16)
+        q = torch.randn(T, D, device="cuda", dtype=torch.bfloat16)
+        return (lambda: bank_read(q, keys, values, 32)), 2.0 * T * N * D, 0.0
+
     def rms(bwd: bool):
         rows, d = 32768, 2048
         x = torch.randn(rows, d, device="cuda", dtype=torch.bfloat16)
@@ -169,6 +180,7 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
         "gemm_cublas": lambda: gemm(True),
         "gemm_nvfp4": gemm_fp4,
         "nvfp4_quant_dual": quant_dual,
+        "memory_read": memory_read,
         "linear_fwd_bwd_bf16": lambda: linear_train("bf16"),
         "linear_fwd_bwd_nvfp4": lambda: linear_train("nvfp4"),
         "rmsnorm_fwd": lambda: rms(False),

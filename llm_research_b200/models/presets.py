@@ -7,7 +7,9 @@
                    (gate, latent pooling, plan conditioning, Tier-3
                    projections and integration) still runs every step.
 ``genesis-7b``  -- 32 layers, d_model 4096, 32 query / 8 KV heads, ffn 11008,
-                   vocab 32000, same tier layout.
+                   vocab 32000, same tier layout, and a PHMA semantic-memory
+                   read after every 4th block (65536 slots x 4096, top-32).
+``genesis-7b-nomem`` -- the same trunk without the memory reads.
 ``genesis-7b-nvfp4`` -- genesis-7b, trained with NVFP4 linears (set by the
                    trainer / bench with ``--precision nvfp4``).
 ``genesis-40b-moe`` -- 32 layers, d_model 4096, 32 / 8 heads, vocab 32000,
@@ -61,10 +63,19 @@ def _moe_trunk(c: HLRTConfig, experts: int, top_k: int, d_ff: int, shared: int, 
     return c
 
 
+def _phma(c: HLRTConfig, every: int = 4, slots: int = 65536, top_k: int = 32) -> HLRTConfig:
+    c.tier1_memory_every = every
+    c.memory_slots = slots
+    c.memory_top_k = top_k
+    return c
+
+
 PRESETS: Dict[str, Callable[[], HLRTConfig]] = {
     "genesis-1b": lambda: _trunk(32000, 2048, 24, 16, None, 5632, 4096),
-    "genesis-7b": lambda: _trunk(32000, 4096, 32, 32, 8, 11008, 4096),
-    "genesis-7b-nvfp4": lambda: _trunk(32000, 4096, 32, 32, 8, 11008, 4096),
+    "genesis-7b": lambda: _phma(_trunk(32000, 4096, 32, 32, 8, 11008, 4096)),
+    "genesis-7b-nvfp4": lambda: _phma(_trunk(32000, 4096, 32, 32, 8, 11008, 4096)),
+    # the dense 7B trunk without the memory reads
+    "genesis-7b-nomem": lambda: _trunk(32000, 4096, 32, 32, 8, 11008, 4096),
     "genesis-40b-moe": lambda: _moe_trunk(_trunk(32000, 4096, 32, 32, 8, 6144, 4096), 16, 2, 6144, 1, 1.25),
     # two layers of genesis-40b-moe (same layer shapes), for quick multi-GPU checks
     "genesis-40b-moe-2l": lambda: _moe_trunk(_trunk(32000, 4096, 2, 32, 8, 6144, 4096), 16, 2, 6144, 1, 1.25),
@@ -103,4 +114,8 @@ def count_flops_per_token(cfg: HLRTConfig, seq_len: int) -> float:
                      + d * cfg.tier1_moe_num_experts)
     matmul_params = L * per_layer + cfg.vocab_size * d
     attn = L * 2 * 2 * seq_len * d / 2  # QK^T and PV, causal half, per token (fwd)
-    return 6.0 * matmul_params + 3.0 * attn
+    mem = 0.0
+    if cfg.tier1_memory_every:  # q / value / gate projections (trained) + the bank similarity (forward only)
+        n_mem = L // cfg.tier1_memory_every
+        mem = n_mem * (6.0 * 4 * d * d + 2.0 * cfg.memory_slots * d)
+    return 6.0 * matmul_params + 3.0 * attn + mem

@@ -123,9 +123,10 @@ class _GradSink(torch.autograd.Function):
 
 
 def default_unit_classes() -> Tuple[Type[nn.Module], ...]:
+    from genesis.model.memory_layer import MemoryReadLayer
     from genesis.model.tier1_token_processor import TransformerBlock
 
-    return (TransformerBlock,)
+    return (TransformerBlock, MemoryReadLayer)
 
 
 class FlatShardEngine(nn.Module):

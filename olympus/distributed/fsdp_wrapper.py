@@ -77,6 +77,7 @@ def get_hlrt_wrap_policy(min_num_params: int = 1_000_000):
 
 
 def wrap_model_fsdp(model: nn.Module, fsdp_config: FSDPConfig, device_id: Optional[int] = None):
+    from genesis.model.memory_layer import MemoryReadLayer
     from genesis.model.tier1_token_processor import TransformerBlock
     from llm_research_b200.parallel.fsdp import FlatShardEngine
 
@@ -89,7 +90,7 @@ def wrap_model_fsdp(model: nn.Module, fsdp_config: FSDPConfig, device_id: Option
         model,
         compute_dtype=dtype,
         reshard_after_forward=(strategy == "FULL_SHARD"),
-        unit_classes=(TransformerBlock,),
+        unit_classes=(TransformerBlock, MemoryReadLayer),
         device=device,
         process_group=fsdp_config.process_group,
         tp_group=fsdp_config.tp_group,

@@ -73,7 +73,7 @@ def test_tp_layers_fused_kernels_gpu():
     _check(run_ranks(_tp_case, 2, True, backend="nccl"), 2, 5e-2)
 
 
-def _hlrt_tp_case(rank, world, fused):
+def _hlrt_tp_case(rank, world, fused, memory=False):
     """HLRT with a tensor + sequence parallel Tier 1 against the same weights unsharded."""
     import torch.distributed as dist
 
@@ -84,6 +84,10 @@ def _hlrt_tp_case(rank, world, fused):
     dev = torch.device("cuda", rank) if fused else torch.device("cpu")
     cfg = build_hlrt_config("toy")
     cfg.gate_loss_weight = 0.0
+    if memory:  # memory reads between the sequence-parallel blocks
+        cfg.tier1_memory_every = 1
+        cfg.memory_slots = 512
+        cfg.memory_top_k = 4
     torch.manual_seed(0)
     full = HLRT(cfg).to(dev)
     comm = TPComm(None, max_tokens=256, max_width=512, device=dev) if fused else None
@@ -95,6 +99,9 @@ def _hlrt_tp_case(rank, world, fused):
             src = fp[name]
             dim = getattr(p, "_lrb_tp", None)
             p.copy_(src if dim is None else src.chunk(world, dim=dim)[rank])
+        fb = dict(full.named_buffers())
+        for name, b in tp.named_buffers():
+            b.copy_(fb[name])
     dt = torch.bfloat16 if fused else torch.float32
     full.to(dt)
     tp.to(dt)
@@ -118,8 +125,9 @@ def _hlrt_tp_case(rank, world, fused):
     return res
 
 
-def test_hlrt_tensor_parallel_tier1_matches_unsharded_cpu():
-    for res in run_ranks(_hlrt_tp_case, 2, False):
+@pytest.mark.parametrize("memory", [False, True])
+def test_hlrt_tensor_parallel_tier1_matches_unsharded_cpu(memory):
+    for res in run_ranks(_hlrt_tp_case, 2, False, memory):
         ref, got = res["logits"]
         torch.testing.assert_close(got, ref, atol=1e-4, rtol=1e-4)
         assert any("q_proj" in n for n in res["grads"]) and any("attn_norm" in n for n in res["grads"])
