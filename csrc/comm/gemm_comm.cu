@@ -3,11 +3,14 @@
 //
 // gemm_rs   Y = X W^T with the sequence reduce-scatter of a row-parallel
 //           layer: every rank computes the full partial product (M x N); the
-//           epilogue stores each 128 x 256 tile (bf16) straight into the
-//           owning rank's receive slot over NVLink (rows [o*Mr, (o+1)*Mr) are
-//           owned by rank o), and the last tile of an owner's rows raises that
-//           owner's ready flag.  `tp_reduce` then sums the world slots (fp32)
-//           on the owner, adds an optional residual and releases the slots.
+//           epilogue converts each 128 x 256 tile to bf16 in 32 x 32 blocks
+//           staged in shared memory and pushes every block with one 2 KB bulk
+//           store into the owning rank's receive slot over NVLink (rows
+//           [o*Mr, (o+1)*Mr) are owned by rank o; the slot is tile-major so a
+//           block is contiguous), and the last tile of an owner's rows raises
+//           that owner's ready flag.  `tp_reduce` then sums the world slots
+//           (fp32) on the owner into the row-major output, adds an optional
+//           residual and releases the slots.
 //
 // ag_gemm   Y = AllGather_rows(X) W^T for a column-parallel layer: one
 //           persistent launch in which the first `ncopy` CTAs pull 128-row
@@ -32,7 +35,9 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr size_t kStageA = (size_t)BM * BK * 2, kStageB = (size_t)BN * BK * 2;
-constexpr size_t kSmem = 1024 + STAGES * (kStageA + kStageB) + 256;
+// gemm_rs epilogue staging: per epilogue warp two 32 x 32 bf16 blocks (2 KB each).
+constexpr uint32_t kStageBlk = 32 * 32 * 2;
+constexpr size_t kSmem = 1024 + STAGES * (kStageA + kStageB) + 256 + 4 * 2 * kStageBlk;
 constexpr long long kPollLimit = 1ll << 24;
 enum : int { kErrPeer = 21, kErrSlot = 22, kErrChunk = 23 };
 
@@ -279,6 +284,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       epi_bar();
       slots_ok = sok != 0;
     }
+    // gemm_rs staging: warp q owns two 2 KB blocks after the barrier area.
+    unsigned char* stg = reinterpret_cast<unsigned char*>(full) + 256 + q * 2 * kStageBlk;
+    const int64_t npad = (int64_t)tiles_n * BN;
+    int pending = 0;  // bulk groups this warp has committed and not yet waited for
     for (int t = first; t < num_tiles; t += stride) {
       int tm, tn;
       tile_of(t, tiles_m, tiles_n, rot, tm, tn);
@@ -286,38 +295,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = tm * BM + q * 32 + lane;
       const int owner = (tm * BM) / a.rows_per_rank;
+      const int tm_local = tm - owner * (a.rows_per_rank / BM);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
         tmem_ld_wait();
         const int col0 = tn * BN + c * 32;
-        if (col0 >= a.N) continue;
-        __nv_bfloat16* dst;
         if (AG) {
-          dst = reinterpret_cast<__nv_bfloat16*>(a.C) + (int64_t)row * a.ldc + col0;
+          if (col0 >= a.N) continue;
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.C) + (int64_t)row * a.ldc + col0;
+          if (col0 + 32 <= a.N) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              Vec16<__nv_bfloat16> v;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) v.v[k] = __float2bfloat16_rn(__uint_as_float(r[e + k]));
+              st16(dst + e, v);
+            }
+          } else {
+            for (int e = 0; e < 32 && col0 + e < a.N; ++e) dst[e] = __float2bfloat16_rn(__uint_as_float(r[e]));
+          }
         } else {
           if (!slots_ok) continue;
-          const int lr = row - owner * a.rows_per_rank;
-          dst = reinterpret_cast<__nv_bfloat16*>(a.bases[owner] + a.off0) +
-                ((int64_t)a.rank * a.rows_per_rank + lr) * a.N + col0;
-        }
-        if (col0 + 32 <= a.N) {
+          unsigned char* blk = stg + (c & 1) * kStageBlk;
+          // the bulk store issued from this buffer two blocks ago has finished reading it
+          if (lane == 0 && pending >= 2) {
+            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            pending = 1;
+          }
+          __syncwarp();
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
             Vec16<__nv_bfloat16> v;
 #pragma unroll
             for (int k = 0; k < 8; ++k) v.v[k] = __float2bfloat16_rn(__uint_as_float(r[e + k]));
-            st16(dst + e, v);
+            *reinterpret_cast<uint4*>(blk + lane * 64 + e * 2) = v.raw;
           }
-        } else {
-          for (int e = 0; e < 32 && col0 + e < a.N; ++e) dst[e] = __float2bfloat16_rn(__uint_as_float(r[e]));
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            // slot of (this rank -> owner): tile-major, then 32-column block, then row, then 32 columns
+            const int64_t elem = (int64_t)a.rank * a.rows_per_rank * npad +
+                                 ((((int64_t)tm_local * tiles_n + tn) * (BN / 32) + c) * BM + q * 32) * 32;
+            unsigned char* dst = reinterpret_cast<unsigned char*>(a.bases[owner] + a.off0) + elem * 2;
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                         "r"(smem_addr(blk)), "r"(kStageBlk)
+                         : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            ++pending;
+          }
         }
       }
       tc_fence_before();
       mbar_arrive(&accempty[acc]);
       if (!AG && slots_ok) {
-        __threadfence_system();
+        if (lane == 0) {  // this warp's blocks of the tile have landed in the owner's memory
+          asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+          pending = 0;
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          __threadfence_system();
+        }
         epi_bar();
         if (threadIdx.x == 64) {
           const unsigned int per_owner = (unsigned int)(chunks_per_rank * tiles_n);
@@ -331,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    if (!AG && lane == 0 && pending > 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -341,33 +380,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Owner side of gemm_rs: out[Mr x N] = sum_p slot_p (+ residual), fp32 accumulation.
+// Slots are tile-major (see the gemm_rs epilogue): 8 consecutive elements of a
+// slot are 8 consecutive columns of one output row.
 __global__ void tp_reduce_kernel(const uint4* __restrict__ recv, const uint4* __restrict__ residual,
-                                 uint4* __restrict__ out, int64_t n8, int world, const uint32_t* ready,
-                                 uint32_t* consumed, uint32_t epoch, unsigned int* counter, int* err) {
+                                 uint4* __restrict__ out, int64_t region8, int Mr, int N, int tiles_n, int world,
+                                 const uint32_t* ready, uint32_t* consumed, uint32_t epoch, unsigned int* counter,
+                                 int* err) {
   __shared__ int ok;
   if (threadIdx.x == 0) ok = 1;
   __syncthreads();
   if ((int)threadIdx.x < world && !poll<true>(ready + threadIdx.x, epoch, err, kErrPeer)) atomicExch(&ok, 0);
   __syncthreads();
   if (ok) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < region8; i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t e = i * 8;
+      const int within = (int)(e & 31);
+      const int rr = (int)((e >> 5) & (BM - 1));
+      const int c = (int)((e >> 12) & (BN / 32 - 1));
+      const int64_t t = e >> 15;  // (BM * BN) elements per tile
+      const int tm = (int)(t / tiles_n), tn = (int)(t % tiles_n);
+      const int col = tn * BN + c * 32 + within;
+      const int row = tm * BM + rr;
+      if (col >= N || row >= Mr) continue;
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int p = 0; p < world; ++p) {
         Vec16<__nv_bfloat16> v;
-        v.raw = recv[(int64_t)p * n8 + i];
+        v.raw = recv[(int64_t)p * region8 + i];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += __bfloat162float(v.v[e]);
+        for (int k = 0; k < 8; ++k) acc[k] += __bfloat162float(v.v[k]);
       }
+      const int64_t o8 = ((int64_t)row * N + col) / 8;
       if (residual != nullptr) {
         Vec16<__nv_bfloat16> v;
-        v.raw = residual[i];
+        v.raw = residual[o8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += __bfloat162float(v.v[e]);
+        for (int k = 0; k < 8; ++k) acc[k] += __bfloat162float(v.v[k]);
       }
       Vec16<__nv_bfloat16> o;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o.v[e] = __float2bfloat16_rn(acc[e]);
-      out[i] = o.raw;
+      for (int k = 0; k < 8; ++k) o.v[k] = __float2bfloat16_rn(acc[k]);
+      out[o8] = o.raw;
     }
   }
   __shared__ bool last;
@@ -434,7 +486,8 @@ void check_bf16_kmajor(const at::Tensor& t, const char* what) {
 }  // namespace
 
 // X (M x K, this rank's full-M partial input), W (N x K): partial products go to
-// the owners' receive slots (recv_off: world x (M/world) x N bf16).
+// the owners' receive slots (recv_off: world x (M/world) x ceil(N/256)*256 bf16,
+// tile-major).
 void gemm_rs(const at::Tensor& X, const at::Tensor& W, const at::Tensor& bases, int64_t recv_off, int64_t ready_off,
              int64_t consumed_off, int64_t rank, int64_t world, int64_t epoch, at::Tensor& counters,
              at::Tensor& err) {
@@ -460,17 +513,20 @@ void gemm_rs(const at::Tensor& X, const at::Tensor& W, const at::Tensor& bases, 
 
 void tp_reduce(const at::Tensor& recv, const c10::optional<at::Tensor>& residual, at::Tensor& out, int64_t world,
                const at::Tensor& ready, at::Tensor& consumed, int64_t epoch, at::Tensor& counter, at::Tensor& err) {
-  const int64_t n = out.numel();
-  LRB_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && n % 8 == 0 && recv.numel() == world * n,
-            "tp_reduce: shape mismatch");
+  LRB_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.dim() == 2, "tp_reduce: out (Mr, N) bf16");
+  const int64_t Mr = out.size(0), N = out.size(1);
+  const int64_t tiles_n = (N + BN - 1) / BN;
+  const int64_t region = ((Mr + BM - 1) / BM) * BM * tiles_n * BN;  // elements per source slot (tile-major)
+  LRB_CHECK(N % 8 == 0 && recv.numel() >= world * region, "tp_reduce: receive slots too small");
+  if (residual) LRB_CHECK(residual->is_contiguous() && residual->numel() == out.numel(), "tp_reduce: residual shape");
   c10::cuda::CUDAGuard g(out.device());
-  const int64_t n8 = n / 8;
-  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((n8 + 255) / 256, (int64_t)num_sms() * 4));
+  const int64_t region8 = region / 8;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((region8 + 255) / 256, (int64_t)num_sms() * 4));
   tp_reduce_kernel<<<blocks, 256, 0, stream()>>>(
       reinterpret_cast<const uint4*>(recv.data_ptr()), residual ? reinterpret_cast<const uint4*>(residual->data_ptr()) : nullptr,
-      reinterpret_cast<uint4*>(out.data_ptr()), n8, (int)world, reinterpret_cast<const uint32_t*>(ready.data_ptr<int>()),
-      reinterpret_cast<uint32_t*>(consumed.data_ptr<int>()), (uint32_t)epoch,
-      reinterpret_cast<unsigned int*>(counter.data_ptr<int>()), err.data_ptr<int>());
+      reinterpret_cast<uint4*>(out.data_ptr()), region8, (int)Mr, (int)N, (int)tiles_n, (int)world,
+      reinterpret_cast<const uint32_t*>(ready.data_ptr<int>()), reinterpret_cast<uint32_t*>(consumed.data_ptr<int>()),
+      (uint32_t)epoch, reinterpret_cast<unsigned int*>(counter.data_ptr<int>()), err.data_ptr<int>());
   LRB_LAUNCH_CHECK();
 }
 

@@ -56,7 +56,8 @@ class TPComm:
         self.device = device
         self.max_tokens, self.max_width, self.ncopy = max_tokens, max_width, ncopy
         W = self.world
-        slot = (max_tokens // W) * max_width * 2
+        # gemm_rs slots are tile-major with the width padded to whole 256-column tiles
+        slot = (max_tokens // W) * (-(-max_width // 256) * 256) * 2
         self.heap = h = SymmetricHeap(W * slot + 2 * slot + 8192, group=group, device=device)
         self.recv_off = h.alloc(W * slot)
         self.ready_off = h.alloc(4 * W)
@@ -80,7 +81,8 @@ class TPComm:
         C.gemm_rs(x.contiguous(), w, self.heap.bases, self.recv_off, self.ready_off, self.consumed_off, self.rank,
                   self.world, self.rs_epoch, self.counters[: self.world], self.heap.err)
         out = torch.empty(T // self.world, N, dtype=x.dtype, device=x.device)
-        recv = self.heap.view(self.recv_off, (self.world * out.numel(),), torch.bfloat16)
+        npad = -(-N // 256) * 256
+        recv = self.heap.view(self.recv_off, (self.world * (T // self.world) * npad,), torch.bfloat16)
         C.tp_reduce(recv, residual.contiguous() if residual is not None else None, out, self.world, self.ready,
                     self.consumed, self.rs_epoch, self.counters[self.world:self.world + 1], self.heap.err)
         return out
