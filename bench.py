@@ -388,7 +388,7 @@ def run_reference(args) -> dict:
         e2e = {"value": world * accum * micro * S * args.steps / e2e_s, "unit": "tokens/s",
                "h2d_bytes_per_step": int(host.numel() * host.element_size()), "d2h_bytes_per_step": 4 * accum,
                "ms_per_step": e2e_s * 1000.0 / args.steps}
-    tokens_per_step = dp_world * accum * micro * S
+    tokens_per_step = world * accum * micro * S
     res = {
         "metric": METRIC,
         "value": tokens_per_step * args.steps / (dev_ms / 1000.0),
@@ -413,8 +413,6 @@ def run_reference(args) -> dict:
     }
     if dist.is_initialized():
         dist.barrier()
-        if tp_comm is not None:
-            tp_comm.close()
         dist.destroy_process_group()
     return res if rank == 0 else None
 
