@@ -326,7 +326,11 @@ def run_reference(args) -> dict:
         model = HLRT(cfg)
         accum = max(args.per_gpu_seqs // micro, 1)
         trainer = DistributedBootstrapTrainer(
-            fsdp_config=FSDPConfig(sharding_strategy="FULL_SHARD", mixed_precision="fp32",
+            # FULL_SHARD fails in the reference at world > 1: the tied output head reads
+            # embeddings.weight outside the embedding's FSDP unit and gets the flat shard
+            # ("size mismatch, got input (16384), mat (16384x2048), vec (32768000)").  Its
+            # SHARD_GRAD_OP strategy keeps parameters gathered through the forward.
+            fsdp_config=FSDPConfig(sharding_strategy="SHARD_GRAD_OP", mixed_precision="fp32",
                                    activation_checkpointing=True) if world > 1 else None,
             model=model,
             optimizer_cls=MuonAdamWHybrid,
@@ -406,7 +410,7 @@ def run_reference(args) -> dict:
         "config": {"model": MODEL_NAME, "global_batch": world * accum * micro, "seq_len": S, "micro_batch": micro,
                    "grad_accum": accum,
                    "parallelism": ("reference stock path, fp32, its vanilla attention: "
-                                   + ("FSDP1 FULL_SHARD" if world > 1 else "single GPU")),
+                                   + ("FSDP1 SHARD_GRAD_OP" if world > 1 else "single GPU")),
                    "final_loss": float(loss)},
         "clocks": sampler.summary(),
         "e2e": e2e,

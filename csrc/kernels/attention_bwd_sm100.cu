@@ -10,8 +10,9 @@
 // P^T and dS^T are written by the softmax-gradient warps to shared memory in
 // the K-major 128-byte-swizzled layout; dS (for dQ) and the Q / dO / K
 // operands of the accumulating GEMMs are read MN-major from the same tiles,
-// so nothing is transposed explicitly.  dQ is added to an fp32 buffer with
-// 16-byte vector atomics; dK and dV leave TMEM once at the end.
+// so nothing is transposed explicitly.  dQ is added to an fp32 buffer by TMA
+// reduce-adds of 128 x 32 blocks staged in shared memory; dK and dV leave TMEM
+// once at the end.
 //
 // Warps: 0 TMA (K, V once; Q and dO per tile), 1 TMEM owner + MMA issue,
 // 2..9 softmax-gradient (two threads per key row, 64 query columns each).
@@ -30,7 +31,9 @@ constexpr int TK = 128, TQ = 128, HD = 128;
 constexpr int kThreads = 320;
 constexpr int kSmThreads = 256;
 constexpr uint32_t kTile = 32768, kHalf = 16384;
-constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 512 + 2 * TQ * sizeof(float);
+// + dQ staging: two 128 x 32 fp32 blocks (one per column half), 128-byte swizzled
+constexpr uint32_t kDqStage = TQ * 32 * 4;  // 16 KB
+constexpr size_t kSmem = 1024 + 6 * (size_t)kTile + 2048 + 2 * (size_t)kDqStage;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdArgs {
@@ -44,6 +47,19 @@ struct BwdArgs {
   int* err;
 };
 
+// AND of `v` over the 128 threads of named barrier `id` (also a barrier): the
+// softmax-gradient warps of one column half leave their loop together, so the
+// named barriers of the dQ reduction can never wait for a thread that left.
+__device__ __forceinline__ bool group_all(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 q, %1, 0;\nbar.red.and.pred p, %2, 128, q;\nselp.u32 %0, 1, 0, p;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -52,7 +68,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                          BwdArgs a) {
+                          const __grid_constant__ CUtensorMap tmdQ, BwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sK = base;
@@ -74,6 +90,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   float* sL = reinterpret_cast<float*>(base + 6 * kTile + 512);  // lse * log2(e) of the tile's queries
   float* sD = sL + TQ;                                             // D = rowsum(dO * O)
+  unsigned char* sDQ = base + 6 * kTile + 2048;                    // [2][128 rows x 128 B], swizzled
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * TK;
@@ -210,9 +227,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t par = t & 1;
       const int h = hk * G + t / nqt;
       const int q0 = (qt0 + t % nqt) * TQ;
-      if (!mbar_wait(sdp_ready, par, a.err, kErrEpiWait)) { ok = false; break; }
+      bool got = mbar_wait(sdp_ready, par, a.err, kErrEpiWait);
       // acquire the producer's LSE/D stores (its phase completed before the MMAs that signalled sdp_ready)
-      if (!mbar_wait(qd_full, par, a.err, kErrEpiWait)) { ok = false; break; }
+      got = got && mbar_wait(qd_full, par, a.err, kErrEpiWait);
+      if (!group_all(2 + half, got)) { ok = false; break; }
       tc_fence_after();
       // two passes of 32 query columns; each pass fills four 16-byte chunks of this
       // thread's 128-byte row of the 64-column swizzle block of P^T / dS^T
@@ -249,27 +267,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_ready);
-      // dQ rows: TMEM lane = query row of this tile.
-      if (!mbar_wait(dq_ready, par, a.err, kErrEpiWait)) { ok = false; break; }
+      // dQ rows: TMEM lane = query row of this tile.  Both 32-column blocks of this
+      // thread's half come out of TMEM first, so region B is released before the
+      // reduction; each block is staged (x scale) in the half's swizzled buffer and
+      // added to dq_acc by one TMA reduce-add (rows past Sq hold exact zeros).
+      if (!group_all(2 + half, mbar_wait(dq_ready, par, a.err, kErrEpiWait))) { ok = false; break; }
       tc_fence_after();
-      const int q = q0 + row;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tB + lane_base + c0 + c * 32, r);
-        tmem_ld_wait();
-        if (q < a.Sq) {
-          float* dst = a.dq_acc + (((int64_t)b * a.Sq + q) * a.H + h) * HD + c0 + c * 32;
-#pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            atomicAdd(reinterpret_cast<float4*>(dst + e),
-                      make_float4(__uint_as_float(r[e]) * a.scale, __uint_as_float(r[e + 1]) * a.scale,
-                                  __uint_as_float(r[e + 2]) * a.scale, __uint_as_float(r[e + 3]) * a.scale));
-        }
-      }
+      uint32_t r0[32], r1[32];
+      tmem_ld_32x32b_x32(tB + lane_base + c0, r0);
+      tmem_ld_32x32b_x32(tB + lane_base + c0 + 32, r1);
+      tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(b_free);
+      unsigned char* stg = sDQ + half * kDqStage;
+      const bool issuer = quarter == 0 && lane == 0;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        // the previous reduce-add from this buffer has finished reading it
+        if (issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        asm volatile("bar.sync %0, 128;" ::"r"(2 + half) : "memory");
+        const uint32_t* r = c == 0 ? r0 : r1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(stg + row * 128 + ((j ^ (row & 7)) * 16)) =
+              make_float4(__uint_as_float(r[4 * j]) * a.scale, __uint_as_float(r[4 * j + 1]) * a.scale,
+                          __uint_as_float(r[4 * j + 2]) * a.scale, __uint_as_float(r[4 * j + 3]) * a.scale);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("bar.sync %0, 128;" ::"r"(2 + half) : "memory");
+        if (issuer) {
+          asm volatile(
+              "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(&tmdQ),
+              "r"(smem_addr(stg)), "r"(h * HD + c0 + c * 32), "r"(b * a.Sq + q0)
+              : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+      }
     }
+    if (quarter == 0 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     // ---------------------------------------------------------- dK, dV
     const bool have = __all_sync(0xffffffffu, ok && total > 0 && mbar_wait(acc_done, 0, a.err, kErrEpiWait));
     tc_fence_after();
@@ -640,6 +674,20 @@ CUtensorMap bshd_map(const at::Tensor& t, int box_rows = 128) {
   return m;
 }
 
+// dq_acc viewed as (rows = B*Sq, cols = H*128) fp32; box 32 columns x 128 rows, 128-byte swizzle.
+CUtensorMap dq_map(float* ptr, int64_t rows, int64_t cols) {
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+  const cuuint32_t box[2] = {32, (cuuint32_t)TQ};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LRB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (dq) failed with code ", (int)r);
+  return m;
+}
+
 int* bwd_error_word(const at::Device& dev) {
   static at::Tensor words[16];
   const int idx = dev.index() < 0 ? 0 : dev.index();
@@ -666,8 +714,11 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
   }();
   dim3 grid((unsigned)((Skv + TK - 1) / TK), (unsigned)(B * Hkv));
   if (v2) {  // 128-query tiles, serial per tile (kept for A/B comparisons)
+    LRB_CHECK(dq_acc.is_contiguous() && dq_acc.scalar_type() == at::kFloat && dq_acc.numel() == B * Sq * H * HD,
+              "attn_bwd: dq_acc must be a contiguous fp32 (B, Sq, H, 128) buffer");
+    CUtensorMap tdq = dq_map(dq_acc.data_ptr<float>(), B * Sq, H * HD);
     LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-    attn_bwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, tdo, args);
+    attn_bwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, tdo, tdq, args);
   } else {
     CUtensorMap tq64 = bshd_map(q, bwd3::TQ3), tdo64 = bshd_map(dout, bwd3::TQ3);
     LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_v3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
