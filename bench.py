@@ -319,7 +319,9 @@ def run_reference(args) -> dict:
     if args.ref_micro_batch > 0:
         candidates = [args.ref_micro_batch]
     else:
-        candidates = [8, 4, 2, 1] if world == 1 else [4]
+        # one GPU: the largest that fits (2 on B200); several: 2 directly, since a
+        # probe that runs out of memory on one rank would leave the others in a collective
+        candidates = [8, 4, 2, 1] if world == 1 else [2]
 
     def build(micro):
         torch.manual_seed(args.seed)
