@@ -355,19 +355,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 // so dQ needs no columns of its own.  Warps: 0 TMA (K, V once; Q, dO and the
 // LSE / D of each sub-tile into one of two buffers), 1 MMA issue, 2..9
 // softmax-gradient (two threads per key row, 32 queries each), 10..13 dQ
-// epilogue (one thread per head-dim lane: coalesced fp32 reductions).
+// epilogue (one thread per head-dim lane; staged boxes, TMA reduce-adds).
 namespace bwd3 {
 constexpr int TQ3 = 64;
 constexpr int kThreads = 448;
 constexpr uint32_t kKV = 32768, kKVHalf = 16384;   // K or V tile, 64-column half
 constexpr uint32_t kQ = 16384, kQHalf = 8192;       // Q or dO sub-tile, half
 constexpr uint32_t kPT = 16384;                     // P^T or dS^T: 128 keys x 64 queries
-constexpr size_t kSmem = 1024 + 2 * kKV + 4 * (size_t)kQ + 4 * (size_t)kPT + 1024 + 4 * TQ3 * sizeof(float);
+constexpr uint32_t kDq = 128 * TQ3 * 4;            // dQ staging: 4 boxes of 32 head dims x 64 queries (fp32)
+constexpr size_t kSmem = 1024 + 2 * kKV + 4 * (size_t)kQ + 4 * (size_t)kPT + 2048 + kDq;
 }  // namespace bwd3
 
 __global__ void __launch_bounds__(bwd3::kThreads, 1)
     attn_bwd_v3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, BwdArgs a) {
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                       const __grid_constant__ CUtensorMap tmdQ, BwdArgs a) {
   using namespace bwd3;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -390,6 +392,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   float* sL = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(bars) + 1024);  // [2][64]
   float* sD = sL + 2 * TQ3;                                                           // [2][64]
+  unsigned char* sDQ = reinterpret_cast<unsigned char*>(bars) + 2048;  // 4 x (64 rows x 128 B), swizzled
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * TK;
@@ -611,30 +614,50 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
     }
   } else {
     // ------------------------------------------------------- dQ epilogue
+    // dQ^T leaves TMEM (lane = head dim d, 64 query columns), is staged x scale as
+    // four 32-dim x 64-query boxes (128-byte swizzle) and added to dq_acc by TMA
+    // reduce-adds; rows past Sq hold exact zeros.
     const int quarter = warp & 3;
     const int d = quarter * 32 + lane;  // head-dim index (TMEM lane of dQ^T)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const bool issuer = quarter == 0 && lane == 0;
+    unsigned char* box = sDQ + (d >> 5) * (TQ3 * 128);
+    const int chunk = (d & 31) >> 2, sub = (d & 3) * 4;
     for (int t = 0; t < total; ++t) {
       const int bb = t & 1;
       const uint32_t use = (t >> 1) & 1;
       const int h = hk * G + t / nqt;
       const int q0 = (qt0 + t % nqt) * TQ3;
-      if (!mbar_wait(&dq_full[bb], use, a.err, kErrEpiWait)) break;
+      if (!group_all(1, mbar_wait(&dq_full[bb], use, a.err, kErrEpiWait))) break;
       tc_fence_after();
+      // the previous sub-tile's reduce-adds have finished reading the staging boxes
+      if (issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      asm volatile("bar.sync 1, 128;" ::: "memory");
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + c * 32, r);
         tmem_ld_wait();
-        float* dst = a.dq_acc + (((int64_t)b * a.Sq + q0 + c * 32) * a.H + h) * HD + d;
-        const int64_t qstride = (int64_t)a.H * HD;
-#pragma unroll 8
+#pragma unroll
         for (int e = 0; e < 32; ++e)
-          if (q0 + c * 32 + e < a.Sq) atomicAdd(dst + e * qstride, __uint_as_float(r[e]) * a.scale);
+          *reinterpret_cast<float*>(box + (c * 32 + e) * 128 + ((chunk ^ (e & 7)) * 16) + sub) =
+              __uint_as_float(r[e]) * a.scale;
       }
       tc_fence_before();
       mbar_arrive(&dq_free[bb]);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (issuer) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          asm volatile(
+              "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(&tmdQ),
+              "r"(smem_addr(sDQ + j * (TQ3 * 128))), "r"(h * HD + j * 32), "r"(b * a.Sq + q0)
+              : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
     }
+    if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -675,11 +698,11 @@ CUtensorMap bshd_map(const at::Tensor& t, int box_rows = 128) {
 }
 
 // dq_acc viewed as (rows = B*Sq, cols = H*128) fp32; box 32 columns x 128 rows, 128-byte swizzle.
-CUtensorMap dq_map(float* ptr, int64_t rows, int64_t cols) {
+CUtensorMap dq_map(float* ptr, int64_t rows, int64_t cols, int box_rows = TQ) {
   CUtensorMap m;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
-  const cuuint32_t box[2] = {32, (cuuint32_t)TQ};
+  const cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -713,17 +736,18 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
     return !(e != nullptr && e[0] == '1');
   }();
   dim3 grid((unsigned)((Skv + TK - 1) / TK), (unsigned)(B * Hkv));
-  if (v2) {  // 128-query tiles, serial per tile (kept for A/B comparisons)
-    LRB_CHECK(dq_acc.is_contiguous() && dq_acc.scalar_type() == at::kFloat && dq_acc.numel() == B * Sq * H * HD,
-              "attn_bwd: dq_acc must be a contiguous fp32 (B, Sq, H, 128) buffer");
+  LRB_CHECK(dq_acc.is_contiguous() && dq_acc.scalar_type() == at::kFloat && dq_acc.numel() == B * Sq * H * HD,
+            "attn_bwd: dq_acc must be a contiguous fp32 (B, Sq, H, 128) buffer");
+  if (v2) {  // 128-query tiles, serial per tile
     CUtensorMap tdq = dq_map(dq_acc.data_ptr<float>(), B * Sq, H * HD);
     LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
     attn_bwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, tdo, tdq, args);
   } else {
     CUtensorMap tq64 = bshd_map(q, bwd3::TQ3), tdo64 = bshd_map(dout, bwd3::TQ3);
+    CUtensorMap tdq64 = dq_map(dq_acc.data_ptr<float>(), B * Sq, H * HD, bwd3::TQ3);
     LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_v3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)bwd3::kSmem));
-    attn_bwd_v3_kernel<<<grid, bwd3::kThreads, bwd3::kSmem, stream()>>>(tq64, tk, tv, tdo64, args);
+    attn_bwd_v3_kernel<<<grid, bwd3::kThreads, bwd3::kSmem, stream()>>>(tq64, tk, tv, tdo64, tdq64, args);
   }
   LRB_LAUNCH_CHECK();
 }

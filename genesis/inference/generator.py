@@ -2,7 +2,8 @@
 
 Prefill runs the full hierarchy with a Tier-1 KV cache; every decode step
 feeds one token, which takes HLRT's single-token path (Tier 1 + cached plan
-vector).  ``use_kv_cache=False`` recomputes the whole sequence every step
+vector).  On a GPU the decode steps replay one captured CUDA graph
+(``genesis.inference.graph_decode``).  ``use_kv_cache=False`` recomputes the whole sequence every step
 (the reference's uncached mode).  Gate-threshold overrides in
 :class:`GenerationConfig` are applied to the model's gates for the duration of
 the call (the reference records them but never applies them).
@@ -38,9 +39,23 @@ class GenerationConfig:
 
 
 class Generator:
-    def __init__(self, model: HLRT) -> None:
+    """``cuda_graph``: decode through :class:`GraphDecoder` (one captured CUDA graph
+    replayed per token) when the model is on a GPU -- the default; ``False`` keeps
+    the eager cached decode."""
+
+    def __init__(self, model: HLRT, cuda_graph: bool | None = None) -> None:
         self.model = model
         self.config = model.config
+        self.cuda_graph = cuda_graph
+
+    def _graph_decoder(self, input_ids: torch.Tensor, cfg: "GenerationConfig"):
+        on_gpu = input_ids.is_cuda and self.model.embeddings.weight.is_cuda
+        if not cfg.use_kv_cache or not on_gpu or self.cuda_graph is False:
+            return None
+        from genesis.inference.graph_decode import GraphDecoder
+
+        B, S = input_ids.shape
+        return GraphDecoder(self.model, B, S + cfg.max_new_tokens + 1)
 
     @contextlib.contextmanager
     def _thresholds(self, cfg: GenerationConfig):
@@ -65,9 +80,16 @@ class Generator:
         self.model.eval()
         B, S = input_ids.shape
         router = CascadeRouter(cfg.gate1_threshold, cfg.gate2_threshold)
-        cache = KVCache(self.config.tier1_num_layers) if cfg.use_kv_cache else None
+        graph = self._graph_decoder(input_ids, cfg)
+        cache = KVCache(self.config.tier1_num_layers) if cfg.use_kv_cache and graph is None else None
         with self._thresholds(cfg):
-            logits, t2, t3 = self._forward(input_ids, cache, 0)
+            if graph is not None:
+                cache_out = KVCache(self.config.tier1_num_layers)
+                logits, t2, t3 = self._forward(input_ids, cache_out, 0)
+                graph.cache.load(cache_out)
+                del cache_out
+            else:
+                logits, t2, t3 = self._forward(input_ids, cache, 0)
             router.record(S, t2, t3)
             tok = sample(logits, cfg.sampling)
             new = [tok]
@@ -75,7 +97,9 @@ class Generator:
             for step in range(1, cfg.max_new_tokens):
                 if cfg.eos_token_id is not None and bool((tok == cfg.eos_token_id).all()):
                     break
-                if cache is not None:
+                if graph is not None:  # single-token path: Tier 1 + cached plan, no upper tiers
+                    logits, t2, t3 = graph.step(tok), False, False
+                elif cache is not None:
                     logits, t2, t3 = self._forward(tok[:, None], cache, S + step - 1)
                 else:
                     logits, t2, t3 = self._forward(seq, None, 0)

@@ -114,6 +114,8 @@ class MultiHeadAttention(nn.Module):
         kv_cache: Optional[object] = None,
         position_offset: int = 0,
     ) -> torch.Tensor:
+        if kv_cache is not None and getattr(kv_cache, "is_static", False):
+            return self._forward_static(x, cos, sin, kv_cache)
         B, S, _ = x.shape
         H, Hkv, D = self.num_heads, self.num_kv_heads, self.head_dim
         qkv = self._qkv(x)
@@ -136,6 +138,24 @@ class MultiHeadAttention(nn.Module):
             vh = vh.repeat_interleave(self.num_kv_groups, dim=1)
         out = self._vanilla_attention(qh, kh, vh, attention_mask)
         return project(out.transpose(1, 2).reshape(B, S, H * D), self.o_proj.weight, self.o_proj.bias)
+
+    def _forward_static(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, cache) -> torch.Tensor:
+        """One decode token against a fixed-capacity cache whose position lives on the
+        device (``cache.pos``), so the step has the same shapes and the same launches
+        every time and can be replayed from a CUDA graph.  ``cos``/``sin`` are the full
+        tables; the row of the current position is gathered on the device.  Slots past
+        the position are masked; GQA reads the shared K/V heads without repeating them."""
+        B, S, _ = x.shape
+        H, Hkv, D = self.num_heads, self.num_kv_heads, self.head_dim
+        qkv = self._qkv(x)
+        q, k, v = ops.rope_qkv(qkv, cos.index_select(0, cache.pos), sin.index_select(0, cache.pos), H, Hkv, D, 0)
+        K, V = cache.write(k, v)  # (B, capacity, Hkv, D)
+        qg = q.reshape(B, Hkv, H // Hkv, D)
+        scores = torch.matmul(qg, K.permute(0, 2, 3, 1)).float() * (1.0 / math.sqrt(D))
+        scores = scores.masked_fill(~cache.valid, float("-inf"))
+        p = torch.softmax(scores, dim=-1).to(V.dtype)
+        out = torch.matmul(p, V.permute(0, 2, 1, 3))  # (B, Hkv, G, D)
+        return project(out.reshape(B, 1, H * D), self.o_proj.weight, self.o_proj.bias)
 
     def _vanilla_attention(
         self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, attention_mask: Optional[torch.Tensor] = None
