@@ -274,12 +274,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool slots_ok = true;
-    if (!AG) {  // owners must have consumed the previous epoch before their slots are rewritten
+    __shared__ unsigned int owner_tiles[8];  // gemm_rs: tiles of each owner pushed by this CTA
+    if (!AG) {  // slots alternate by epoch parity: owners must have consumed epoch - 2 before they are rewritten
       __shared__ int sok;
       if (threadIdx.x == 64) sok = 1;
+      if (threadIdx.x >= 64 && threadIdx.x < 72) owner_tiles[threadIdx.x - 64] = 0u;
       epi_bar();
       const int t = threadIdx.x - 64;
-      if (t < a.world && !poll<true>(reinterpret_cast<const uint32_t*>(a.bases[t] + a.off2), a.epoch - 1, a.err, kErrSlot))
+      if (t < a.world && !poll<true>(reinterpret_cast<const uint32_t*>(a.bases[t] + a.off2), a.epoch - 2, a.err, kErrSlot))
         atomicExch(&sok, 0);
       epi_bar();
       slots_ok = sok != 0;
@@ -349,27 +351,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&accempty[acc]);
-      if (!AG && slots_ok) {
-        if (lane == 0) {  // this warp's blocks of the tile have landed in the owner's memory
-          asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-          pending = 0;
-          asm volatile("fence.proxy.async.global;" ::: "memory");
-          __threadfence_system();
-        }
-        epi_bar();
-        if (threadIdx.x == 64) {
-          const unsigned int per_owner = (unsigned int)(chunks_per_rank * tiles_n);
-          if (atomicAdd(&a.counters[owner], 1u) + 1u == per_owner) {
-            a.counters[owner] = 0u;
+      if (!AG && slots_ok && threadIdx.x == 64) ++owner_tiles[owner];
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+    if (!AG && slots_ok) {
+      // Completion is awaited once, after the CTA's last tile, so the bulk stores of
+      // all its tiles stay in flight together; then the tiles count toward their
+      // owners and the CTA that completes an owner's rows raises its flag.
+      if (lane == 0) {
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence_system();
+      }
+      epi_bar();
+      if (threadIdx.x == 64) {
+        const unsigned int per_owner = (unsigned int)(chunks_per_rank * tiles_n);
+        for (int o = 0; o < a.world; ++o) {
+          const unsigned int n = owner_tiles[o];
+          if (n == 0) continue;
+          if (atomicAdd(&a.counters[o], n) + n == per_owner) {
+            a.counters[o] = 0u;
             __threadfence_system();
             if (no_error(a.err))
-              st_release_sys(reinterpret_cast<uint32_t*>(a.bases[owner] + a.off1) + a.rank, a.epoch);
+              st_release_sys(reinterpret_cast<uint32_t*>(a.bases[o] + a.off1) + a.rank, a.epoch);
           }
         }
       }
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    } else if (!AG && lane == 0 && pending > 0) {
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
-    if (!AG && lane == 0 && pending > 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -495,6 +505,7 @@ void gemm_rs(const at::Tensor& X, const at::Tensor& W, const at::Tensor& bases, 
   check_bf16_kmajor(W, "gemm_rs W");
   const int64_t M = X.size(0), K = X.size(1), N = W.size(0);
   LRB_CHECK(W.size(1) == K && M % (BM * world) == 0 && N % 8 == 0, "gemm_rs: M % (128*world) == 0, N % 8 == 0");
+  LRB_CHECK(world <= 8, "gemm_rs: at most 8 ranks per tensor-parallel group");
   c10::cuda::CUDAGuard g(X.device());
   CUtensorMap ta = kmajor_map(X.data_ptr(), M, K, X.stride(0), BM), tb = kmajor_map(W.data_ptr(), N, K, W.stride(0), BN);
   CommGemmArgs args{};

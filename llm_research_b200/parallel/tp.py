@@ -58,8 +58,10 @@ class TPComm:
         W = self.world
         # gemm_rs slots are tile-major with the width padded to whole 256-column tiles
         slot = (max_tokens // W) * (-(-max_width // 256) * 256) * 2
-        self.heap = h = SymmetricHeap(W * slot + 2 * slot + 8192, group=group, device=device)
-        self.recv_off = h.alloc(W * slot)
+        self.heap = h = SymmetricHeap(2 * W * slot + 2 * slot + 8192, group=group, device=device)
+        # gemm_rs receive slots, two sets alternating by epoch parity (a call only waits
+        # for the owners to have consumed the call before the previous one)
+        self.recv_offs = [h.alloc(W * slot), h.alloc(W * slot)]
         self.ready_off = h.alloc(4 * W)
         self.consumed_off = h.alloc(4)
         self.shard_off = [h.alloc(slot), h.alloc(slot)]
@@ -78,11 +80,12 @@ class TPComm:
         C = native()
         T, N = x.shape[0], w.shape[0]
         self.rs_epoch += 1
-        C.gemm_rs(x.contiguous(), w, self.heap.bases, self.recv_off, self.ready_off, self.consumed_off, self.rank,
+        recv_off = self.recv_offs[self.rs_epoch % 2]
+        C.gemm_rs(x.contiguous(), w, self.heap.bases, recv_off, self.ready_off, self.consumed_off, self.rank,
                   self.world, self.rs_epoch, self.counters[: self.world], self.heap.err)
         out = torch.empty(T // self.world, N, dtype=x.dtype, device=x.device)
         npad = -(-N // 256) * 256
-        recv = self.heap.view(self.recv_off, (self.world * (T // self.world) * npad,), torch.bfloat16)
+        recv = self.heap.view(recv_off, (self.world * (T // self.world) * npad,), torch.bfloat16)
         C.tp_reduce(recv, residual.contiguous() if residual is not None else None, out, self.world, self.ready,
                     self.consumed, self.rs_epoch, self.counters[self.world:self.world + 1], self.heap.err)
         return out
