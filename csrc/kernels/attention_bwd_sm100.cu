@@ -731,9 +731,11 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
   BwdArgs args{lse.data_ptr<float>(), di.data_ptr<float>(), dq_acc.data_ptr<float>(), dk.data_ptr(), dv.data_ptr(),
                (int)B, (int)H, (int)Hkv, (int)Sq, (int)Skv, causal ? 1 : 0, (float)scale, (float)scale * kLog2e,
                bwd_error_word(q.device())};
+  // The 64-query double-buffered kernel is the default; LRB_ATTN_BWD_V2=1 selects
+  // the 128-query kernel that runs its tiles one after another.
   static const bool v2 = [] {
-    const char* e = std::getenv("LRB_ATTN_BWD_V3");
-    return !(e != nullptr && e[0] == '1');
+    const char* e = std::getenv("LRB_ATTN_BWD_V2");
+    return e != nullptr && e[0] == '1';
   }();
   dim3 grid((unsigned)((Skv + TK - 1) / TK), (unsigned)(B * Hkv));
   LRB_CHECK(dq_acc.is_contiguous() && dq_acc.scalar_type() == at::kFloat && dq_acc.numel() == B * Sq * H * HD,

@@ -199,7 +199,7 @@ class HLRT(StatefulModule):
             out: Dict[str, Any] = {
                 "logits": self._head(h),
                 "hidden_states": h,
-                "aux_loss": torch.tensor(0.0, device=input_ids.device),
+                "aux_loss": torch.zeros((), device=input_ids.device),  # filled on the device (graph-capturable)
             }
             if return_tier_activations:
                 out["tier_activations"] = acts

@@ -166,9 +166,10 @@ class ShardedHybridOptimizer:
                 self.stack_base[pid] = base
                 base += infos[pid].numel
         self.stack_total = base
-        # receive layout: for each source rank, pieces of owned matrices in pid order
+        # receive layout: for each source rank, pieces of owned matrices in pid order;
+        # (recv offset, stack offset, length) segments map it onto the stack
         self.recv_splits = [0] * world
-        gather_idx: List[torch.Tensor] = []
+        self.r2s: List[Tuple[int, int, int]] = []
         pos = 0
         for r in range(world):
             for pid in owned:
@@ -176,12 +177,11 @@ class ShardedHybridOptimizer:
                 if pc is None:
                     continue
                 off, ln = pc
-                gather_idx.append(torch.arange(self.stack_base[pid] + off, self.stack_base[pid] + off + ln))
+                self.r2s.append((pos, self.stack_base[pid] + off, ln))
                 self.recv_splits[r] += ln
                 pos += ln
         self.recv_total = pos
-        # stack_flat[gidx[j]] = recv[j]
-        self.recv_to_stack = torch.cat(gather_idx).to(dev) if gather_idx else torch.zeros(0, dtype=torch.long, device=dev)
+        self._bufs = None  # persistent exchange buffers and their segment views (first step)
 
     # ------------------------------------------------------------------ step
     def _views(self, ui: int, seg: Segment, buf: torch.Tensor) -> torch.Tensor:
@@ -247,13 +247,36 @@ class ShardedHybridOptimizer:
             orth = ops.newton_schulz(torch.stack(outs), steps=ns_steps)
             ops.muon_epilogue(mats, list(orth.unbind(0)), gnorm, lr)
 
+    def _exchange_buffers(self, xdt: torch.dtype):
+        """send / recv / stack / back / upd buffers, allocated once, with the views that
+        the segment copies between the receive layout and the stack use."""
+        if self._bufs is None or self._bufs["dtype"] != xdt:
+            dev = self.engine.device
+            send = torch.zeros(self.send_total, dtype=xdt, device=dev)
+            recv = send if self.world == 1 else torch.empty(self.recv_total, dtype=xdt, device=dev)
+            stack = torch.empty(self.stack_total, dtype=xdt, device=dev)
+            back = torch.empty(self.recv_total, dtype=xdt, device=dev)
+            upd = back if self.world == 1 else torch.empty(self.send_total, dtype=xdt, device=dev)
+            self._bufs = dict(dtype=xdt, send=send, recv=recv, stack=stack, back=back, upd=upd,
+                              recv_v=[recv[a: a + n] for a, _, n in self.r2s],
+                              back_v=[back[a: a + n] for a, _, n in self.r2s],
+                              stack_v=[stack[b: b + n] for _, b, n in self.r2s])
+        return self._bufs
+
+    @staticmethod
+    def _copy_segments(dst, src) -> None:
+        if dst:
+            torch._foreach_copy_(dst, src)
+
     def _muon_step(self, lr: float, mu: float, wd: float, ns_steps: int, active) -> None:
         eng, units, dev = self.engine, self.engine.units, self.engine.device
         xdt = torch.bfloat16 if dev.type == "cuda" else torch.float32  # exchange / Newton-Schulz dtype
-        send = torch.zeros(self.send_total, dtype=xdt, device=dev)
+        B = self._exchange_buffers(xdt)
+        send, recv, stack, back, upd = B["send"], B["recv"], B["stack"], B["back"], B["upd"]
+        send.zero_()  # matrices without a gradient keep u = 0 -> zero update, no decay
         outs, segs, pos = [], [], 0
         for s in self.send_order:
-            if s.pid in active:  # matrices without a gradient keep u = 0 -> zero update, no decay
+            if s.pid in active:
                 outs.append(send[pos: pos + s.length])
                 segs.append(s)
             pos += s.length
@@ -275,12 +298,8 @@ class ShardedHybridOptimizer:
             dist.all_reduce(part, group=eng.tp_group)
             gsq = torch.where(mask, part, gsq)
         if self.world > 1:
-            recv = torch.empty(self.recv_total, dtype=xdt, device=dev)
             dist.all_to_all_single(recv, send, self.recv_splits, self.send_splits, group=eng.pg)
-        else:
-            recv = send
-        stack = torch.empty(self.stack_total, dtype=xdt, device=dev)
-        stack.index_copy_(0, self.recv_to_stack, recv)
+        self._copy_segments(B["stack_v"], B["recv_v"])
         gnorm = gsq.sqrt()
         base = 0
         for (shape, tpd), pids in self.groups:
@@ -289,24 +308,20 @@ class ShardedHybridOptimizer:
             block = stack[base: base + n * numel].view(n, shape[0], shape[1])
             if tpd is None:
                 o = ops.newton_schulz(block, steps=ns_steps)
-                onorm = o.float().flatten(1).norm(dim=1)
+                onorm = torch.linalg.vector_norm(o.flatten(1), dim=1, dtype=torch.float32)
             else:
                 parts = [torch.empty_like(block) for _ in range(self.tp_world)]
                 dist.all_gather(parts, block.contiguous(), group=eng.tp_group)
                 o_full = ops.newton_schulz(torch.cat(parts, dim=1 + tpd), steps=ns_steps)
-                onorm = o_full.float().flatten(1).norm(dim=1)
+                onorm = torch.linalg.vector_norm(o_full.flatten(1), dim=1, dtype=torch.float32)
                 o = o_full.chunk(self.tp_world, dim=1 + tpd)[dist.get_rank(eng.tp_group)]
             gn = gnorm[torch.tensor([self.muon_pos[p] for p in pids], device=dev)]
             scale = (lr * gn / (onorm + 1e-8)).view(n, 1, 1)
-            block.copy_((o.float() * scale).to(xdt))
+            torch.mul(o, scale, out=block)  # fp32 product, one rounding into the stack
             base += n * numel
-        back = torch.empty(self.recv_total, dtype=xdt, device=dev)
-        back.copy_(stack.index_select(0, self.recv_to_stack))
+        self._copy_segments(B["back_v"], B["stack_v"])
         if self.world > 1:
-            upd = torch.empty(self.send_total, dtype=xdt, device=dev)
             dist.all_to_all_single(upd, back, self.send_splits, self.recv_splits, group=eng.pg)
-        else:
-            upd = back
         masters, deltas, pos = [], [], 0
         for s in self.send_order:
             if s.pid in active:
