@@ -315,6 +315,12 @@ def run_reference(args) -> dict:
     rank = int(os.environ.get("RANK", 0))
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    if world > 1 and not dist.is_initialized():
+        # The reference joins an existing process group; a short timeout makes a rank
+        # whose peer failed end with an error instead of waiting ten minutes.
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
     S = args.seq_len
     if args.ref_micro_batch > 0:
         candidates = [args.ref_micro_batch]
@@ -328,11 +334,13 @@ def run_reference(args) -> dict:
         model = HLRT(cfg)
         accum = max(args.per_gpu_seqs // micro, 1)
         trainer = DistributedBootstrapTrainer(
-            # FULL_SHARD fails in the reference at world > 1: the tied output head reads
-            # embeddings.weight outside the embedding's FSDP unit and gets the flat shard
-            # ("size mismatch, got input (16384), mat (16384x2048), vec (32768000)").  Its
-            # SHARD_GRAD_OP strategy keeps parameters gathered through the forward.
-            fsdp_config=FSDPConfig(sharding_strategy="SHARD_GRAD_OP", mixed_precision="fp32",
+            # The reference's sharded strategies fail at world > 1: FULL_SHARD in the tied
+            # output head, which reads embeddings.weight after its FSDP unit resharded it
+            # ("size mismatch, got input (16384), mat (16384x2048), vec (32768000)");
+            # SHARD_GRAD_OP in FSDP's gradient finalisation after its no_sync accumulation
+            # ("All sharded parameters that received a gradient in the post-backward should
+            # use `_saved_grad_shard`").  Its NO_SHARD strategy (replicated, DDP-like) runs.
+            fsdp_config=FSDPConfig(sharding_strategy="NO_SHARD", mixed_precision="fp32",
                                    activation_checkpointing=True) if world > 1 else None,
             model=model,
             optimizer_cls=MuonAdamWHybrid,
@@ -412,7 +420,7 @@ def run_reference(args) -> dict:
         "config": {"model": MODEL_NAME, "global_batch": world * accum * micro, "seq_len": S, "micro_batch": micro,
                    "grad_accum": accum,
                    "parallelism": ("reference stock path, fp32, its vanilla attention: "
-                                   + ("FSDP1 SHARD_GRAD_OP" if world > 1 else "single GPU")),
+                                   + ("FSDP1 NO_SHARD" if world > 1 else "single GPU")),
                    "final_loss": float(loss)},
         "clocks": sampler.summary(),
         "e2e": e2e,
