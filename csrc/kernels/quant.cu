@@ -165,6 +165,18 @@ __device__ __forceinline__ uint32_t clear_negative_zero(uint32_t w) {
   return mag | ((mag + 0x77777777u) & 0x88888888u & w);
 }
 
+// 32-bit integer mixer ("lowbias32", C. Wellons' hash-prospector): two 32-bit
+// multiplies per call, so the stochastic-rounding draws stay cheap next to the
+// 64-bit splitmix hash of the one-block-per-thread quantiser.
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
 template <bool SR>
 __device__ __forceinline__ void quant_block16(const float* v, float st, uint32_t seed, uint32_t hi, uint32_t idx0,
                                               uint8_t& sbyte, uint2& packed) {
@@ -180,13 +192,19 @@ __device__ __forceinline__ void quant_block16(const float* v, float st, uint32_t
     for (int i = 0; i < 16; i += 2) w[i >> 3] |= cvt_e2m1x2(v[i] * inv, v[i + 1] * inv) << (4 * (i & 7));
     packed = make_uint2(clear_negative_zero(w[0]), clear_negative_zero(w[1]));
   } else {
+    // one 32-bit draw per element pair: 16 random bits per element
+    const uint32_t key = mix32(seed ^ mix32(hi + 0x9e3779b9u));
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float y = v[i] * inv;
-      const float r = (hash3(seed, hi, idx0 + (uint32_t)i) >> 8) * (1.f / 16777216.f);
-      int code = e2m1_sr_fast(fabsf(y), r);
-      if (y < 0.f && code > 0) code |= 8;
-      w[i >> 3] |= (uint32_t)code << (4 * (i & 7));
+    for (int i = 0; i < 16; i += 2) {
+      const uint32_t h = mix32(key ^ ((idx0 + (uint32_t)i) >> 1));
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float y = v[i + j] * inv;
+        const float r = (float)((h >> (16 * j)) & 0xFFFFu) * (1.f / 65536.f);
+        int code = e2m1_sr_fast(fabsf(y), r);
+        if (y < 0.f && code > 0) code |= 8;
+        w[(i + j) >> 3] |= (uint32_t)code << (4 * ((i + j) & 7));
+      }
     }
     packed = make_uint2(w[0], w[1]);
   }
