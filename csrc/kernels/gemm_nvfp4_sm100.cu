@@ -257,13 +257,18 @@ at::Tensor gemm_nvfp4(const at::Tensor& A, const at::Tensor& sfa, const at::Tens
   CUtensorMap ta = fp4_map(A.data_ptr(), M, K / 2, A.stride(0)), tb = fp4_map(B.data_ptr(), N, K / 2, B.stride(0));
   Nvfp4Args args{C.data_ptr(), N, (int)M, (int)N, (int)K, sfa.data_ptr<uint8_t>(), sfb.data_ptr<uint8_t>(),
                  sa.data_ptr<float>(), sb.data_ptr<float>(), nvfp4_error_word(A.device()), (N % 8) == 0 ? 1 : 0};
-  // 128 x 256 tiles (the A tile feeds two N halves) when N allows; LRB_NVFP4_TILE=128 forces 128 x 128.
+  // 128 x 256 tiles (the A tile feeds two N halves) when N allows; LRB_NVFP4_TILE=128 forces 128 x 128,
+  // LRB_NVFP4_TILE=129 128 x 128 with two resident CTAs per SM.
   static const int tile_env = [] {
     const char* e = std::getenv("LRB_NVFP4_TILE");
     return e ? std::atoi(e) : 256;
   }();
-  const bool wide = tile_env != 128 && N % 256 == 0;
-  if (wide) {
+  const bool wide = tile_env != 128 && tile_env != 129 && N % 256 == 0;
+  if (tile_env == 129) {  // 128 x 128 tiles, 3 stages: two CTAs per SM overlap each other's epilogue
+    constexpr size_t sm = smem_bytes<1, 3>();
+    LRB_CUDA_CHECK(cudaFuncSetAttribute(gemm_nvfp4_kernel<1, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    gemm_nvfp4_kernel<1, 3><<<dim3((unsigned)nb, (unsigned)mb), kThreads, sm, stream()>>>(ta, tb, args);
+  } else if (wide) {
     constexpr size_t sm = smem_bytes<2, 4>();
     LRB_CUDA_CHECK(cudaFuncSetAttribute(gemm_nvfp4_kernel<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
     gemm_nvfp4_kernel<2, 4><<<dim3((unsigned)(N / 256), (unsigned)mb), kThreads, sm, stream()>>>(ta, tb, args);
