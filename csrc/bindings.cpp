@@ -34,7 +34,7 @@ void adamw_step(std::vector<at::Tensor>, std::vector<at::Tensor>, std::vector<at
                 std::vector<double>, std::vector<double>, double, double, double, double, double);
 // ns.cu
 at::Tensor newton_schulz(const at::Tensor&, int64_t, double, double, double);
-void gemm_batched(const at::Tensor&, const at::Tensor&, bool, at::Tensor&, const c10::optional<at::Tensor>&, double,
+void gemm_batched(const at::Tensor&, const at::Tensor&, bool, const at::Tensor&, const c10::optional<at::Tensor>&, double,
                   double);
 int64_t gemm_batched_error(int64_t);
 // quant.cu
@@ -123,9 +123,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &lrb::adamw_step);
   m.def("axpy_list", &lrb::axpy_list);
   m.def("newton_schulz", &lrb::newton_schulz);
-  m.def("gemm_batched", &lrb::gemm_batched, "C = alpha A op(B) + beta D, batched tcgen05 (bf16)", py::arg("A"),
-        py::arg("B"), py::arg("b_mn"), py::arg("C"), py::arg("D") = py::none(), py::arg("alpha") = 1.0,
-        py::arg("beta") = 0.0);
+  m.def("gemm_batched", &lrb::gemm_batched, "C = alpha A op(B) + beta D, batched tcgen05 (bf16); C written in place");
   m.def("gemm_batched_error", &lrb::gemm_batched_error);
   m.def("int4_quantize", &lrb::int4_quantize);
   m.def("int4_dequantize", &lrb::int4_dequantize);

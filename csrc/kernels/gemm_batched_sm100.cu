@@ -259,7 +259,7 @@ void check3(const at::Tensor& t, const char* name) {
 }  // namespace
 
 // C = alpha * A op(B) + beta * D, see the header.  C is written in place.
-void gemm_batched(const at::Tensor& A, const at::Tensor& B, bool b_mn, at::Tensor& C,
+void gemm_batched(const at::Tensor& A, const at::Tensor& B, bool b_mn, const at::Tensor& C,
                   const c10::optional<at::Tensor>& D, double alpha, double beta) {
   check3(A, "A");
   check3(B, "B");

@@ -11,7 +11,7 @@
 
 namespace lrb {
 
-void gemm_batched(const at::Tensor& A, const at::Tensor& B, bool b_mn, at::Tensor& C,
+void gemm_batched(const at::Tensor& A, const at::Tensor& B, bool b_mn, const at::Tensor& C,
                   const c10::optional<at::Tensor>& D, double alpha, double beta);
 
 at::Tensor newton_schulz(const at::Tensor& X0, int64_t steps, double a, double b, double c) {

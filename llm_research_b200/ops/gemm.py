@@ -49,7 +49,7 @@ class _GroupedLinearFn(torch.autograd.Function):
         C = native()
         x, w = x.contiguous(), w.contiguous()
         y = torch.empty(x.shape[0], x.shape[1], w.shape[1], device=x.device, dtype=x.dtype)
-        C.gemm_batched(x, w, False, y)
+        C.gemm_batched(x, w, False, y, None, 1.0, 0.0)
         ctx.save_for_backward(x, w)
         return y
 
@@ -61,10 +61,10 @@ class _GroupedLinearFn(torch.autograd.Function):
         dx = dw = None
         if ctx.needs_input_grad[0]:
             dx = torch.empty_like(x)
-            C.gemm_batched(dy, w, True, dx)
+            C.gemm_batched(dy, w, True, dx, None, 1.0, 0.0)
         if ctx.needs_input_grad[1]:
             dw = torch.empty_like(w)
-            C.gemm_batched(dy.transpose(1, 2).contiguous(), x, True, dw)
+            C.gemm_batched(dy.transpose(1, 2).contiguous(), x, True, dw, None, 1.0, 0.0)
         return dx, dw
 
 
