@@ -234,12 +234,9 @@ class ExpertParallelMoE(nn.Module):
         self.last_aux: Optional[torch.Tensor] = None
 
     def experts(self, x_e: torch.Tensor) -> torch.Tensor:
-        from llm_research_b200.ops.gemm import grouped_linear
-
-        # one batched tcgen05 GEMM over this rank's experts per projection
-        gu = grouped_linear(x_e, self.w_up_gate.to(x_e.dtype))  # (epl, rows, 2*d_ff) = [up | gate]
+        gu = torch.bmm(x_e, self.w_up_gate.to(x_e.dtype).transpose(1, 2))  # (epl, rows, 2*d_ff) = [up | gate]
         h = ops.swiglu(gu.reshape(-1, gu.shape[-1])).view(gu.shape[0], gu.shape[1], -1)
-        return grouped_linear(h, self.w_down.to(h.dtype))
+        return torch.bmm(h, self.w_down.to(h.dtype).transpose(1, 2))
 
     def load_balance_loss(self) -> torch.Tensor:
         return self.last_aux if self.last_aux is not None else torch.zeros((), device=self.router.weight.device)
