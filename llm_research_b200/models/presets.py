@@ -19,7 +19,8 @@
 ``genesis-40b-moe-2l`` -- two layers of genesis-40b-moe, for quick checks.
 ``tiny``        -- the CPU plumbing configuration: vocab 32000, d_model 256,
                    every tier 4 layers / 4 heads / ffn 1024, Tier-3
-                   recurrence 2.
+                   recurrence 2, a PHMA read of 1024 slots x 256 (top-8)
+                   after the 4th block.
 ``toy``         -- a few-hundred-thousand-parameter model for smoke tests.
 """
 
@@ -79,13 +80,13 @@ PRESETS: Dict[str, Callable[[], HLRTConfig]] = {
     "genesis-40b-moe": lambda: _moe_trunk(_trunk(32000, 4096, 32, 32, 8, 6144, 4096), 16, 2, 6144, 1, 1.25),
     # two layers of genesis-40b-moe (same layer shapes), for quick multi-GPU checks
     "genesis-40b-moe-2l": lambda: _moe_trunk(_trunk(32000, 4096, 2, 32, 8, 6144, 4096), 16, 2, 6144, 1, 1.25),
-    "tiny": lambda: HLRTConfig(
+    "tiny": lambda: _phma(HLRTConfig(
         vocab_size=32000, d_model=256,
         tier1_num_layers=4, tier1_num_heads=4, tier1_d_ff=1024,
         tier2_d_model=256, tier2_num_layers=4, tier2_num_heads=4, tier2_d_ff=1024,
         tier3_d_model=256, tier3_num_layers=4, tier3_num_heads=4, tier3_d_ff=1024,
         tier3_recurrence_steps=2, latent_pool_num_heads=4,
-    ),
+    ), every=4, slots=1024, top_k=8),
     "toy": lambda: HLRTConfig(
         vocab_size=512, d_model=128, tier1_num_layers=2, tier1_num_heads=2, tier1_d_ff=256,
         gate1_chunk_size=16, num_latent_vectors=4, latent_pool_num_heads=2,
