@@ -12,6 +12,9 @@ Cases (M = tokens over all ranks, sequence-sharded; N x K weights):
   ag_gemm      fused all-gather(rows) -> GEMM    vs  NCCL all_gather + cuBLAS
   gemm_rs      fused GEMM -> reduce-scatter(rows) vs  cuBLAS + NCCL reduce_scatter
   fsdp_rs      P2P reduce-scatter (bf16 wire, fp32 accumulate, fused norm) vs NCCL (fp32)
+  ep_dispatch  MoE dispatch (P2P stores into the owners' expert slots) vs NCCL all_to_all
+  ep_combine   MoE combine (P2P loads fused with the top-k weighted sum) vs NCCL all_to_all + gather
+               (``--ep-tokens`` per rank x d 4096, top-2 of 16 experts, random-normal router logits)
 """
 
 from __future__ import annotations
@@ -57,6 +60,7 @@ def main(argv=None) -> None:
     ap.add_argument("--nk", type=int, nargs="+", default=[4096, 8192])
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--ep-tokens", type=int, nargs="*", default=[1024, 8192, 65536])
     args = ap.parse_args(argv)
     import datetime
 
@@ -150,8 +154,57 @@ def main(argv=None) -> None:
                           "frac_of_roofline": round(roof / ms, 3)}), flush=True)
     heap.check()
     heap.close()
+    if args.ep_tokens:
+        _ep_cases(args, rank, world, dev)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def _ep_cases(args, rank: int, world: int, dev) -> None:
+    """MoE dispatch / combine at T tokens per rank, d 4096, top-2 of 16 experts."""
+    import math
+
+    from llm_research_b200 import ops
+    from llm_research_b200.parallel.expert_parallel import EPComm, _combine_collective, _dispatch_collective, make_route
+
+    E, K, D = 16, 2, 4096
+    if E % world:
+        return
+    epl = E // world
+    comm = EPComm(None, max_tokens=max(args.ep_tokens), top_k=K, d=D, experts_per_rank=epl, capacity_factor=1.25,
+                  device=dev)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    for T in args.ep_tokens:
+        x = torch.randn(T, D, device=dev, generator=g).to(torch.bfloat16)
+        logits = torch.randn(T, E, device=dev, generator=g)
+        w, idx, _ = ops.softmax_topk(logits, K)
+        cap = math.ceil(1.25 * T * K / E)
+        route = make_route(idx, epl, E, cap)
+        xe = torch.randn(epl, world * cap, D, device=dev, generator=g).to(torch.bfloat16)
+        wf = w.reshape(-1).float().contiguous()
+
+        def fused_dispatch():
+            comm.push(x, None, False, route, cap, K)
+            return comm.take(cap)
+
+        def fused_combine():
+            comm.put(xe, cap)
+            return comm.pull(T, wf, False, route, cap, K)
+
+        ms_d = _time(fused_dispatch, args.warmup, args.iters, dev)
+        base_d = _time(lambda: _dispatch_collective(x, route, cap, world, epl, None), args.warmup, args.iters, dev)
+        ms_c = _time(fused_combine, args.warmup, args.iters, dev)
+        base_c = _time(lambda: _combine_collective(xe, w, route, cap, world, epl, None), args.warmup, args.iters, dev)
+        if rank == 0:
+            # rows that leave this GPU: the (world-1)/world share of its T*K assignments
+            nv = T * K * (world - 1) / world * D * 2
+            roof = nv / (NVLINK_GBS * 1e9) * 1e3
+            for case, ms, base in (("ep_dispatch", ms_d, base_d), ("ep_combine", ms_c, base_c)):
+                print(json.dumps({"case": case, "gpus": world, "tokens_per_rank": T, "d": D, "experts": E,
+                                  "top_k": K, "ms": round(ms, 4), "nccl_ms": round(base, 4),
+                                  "speedup_vs_nccl": round(base / ms, 3), "roofline_ms": round(roof, 4),
+                                  "frac_of_roofline": round(roof / ms, 3)}), flush=True)
+    comm.close()
 
 
 if __name__ == "__main__":

@@ -152,6 +152,14 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
         gu = torch.randn(32768, 2 * 5632, device="cuda", dtype=torch.bfloat16)
         return (lambda: ops.swiglu(gu)), 0.0, gu.numel() * 2 * 1.5
 
+    def ns_shape(m, n, batch):
+        from llm_research_b200 import ops
+
+        g = torch.randn(batch, m, n, device="cuda", dtype=torch.bfloat16)
+        s, l = min(m, n), max(m, n)
+        flops = batch * 5 * (2 * s * s * l + 2 * s * s * s + 2 * s * s * l)
+        return (lambda: ops.newton_schulz(g, steps=5)), float(flops), 0.0
+
     def ns():
         from llm_research_b200 import ops
 
@@ -187,6 +195,8 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
         "rmsnorm_bwd": lambda: rms(True),
         "swiglu_fwd": swiglu,
         "ns": ns,
+        "ns_4096x4096": lambda: ns_shape(4096, 4096, 8),
+        "ns_4096x11008": lambda: ns_shape(4096, 11008, 8),
         "ce": ce,
     }
 
