@@ -15,6 +15,9 @@ Cases (M = tokens over all ranks, sequence-sharded; N x K weights):
   ep_dispatch  MoE dispatch (P2P stores into the owners' expert slots) vs NCCL all_to_all
   ep_combine   MoE combine (P2P loads fused with the top-k weighted sum) vs NCCL all_to_all + gather
                (``--ep-tokens`` per rank x d 4096, top-2 of 16 experts, random-normal router logits)
+  diloco_outer DiLoCo outer step over all ranks as replicas (fused pseudo-gradient exchange +
+               Nesterov on symmetric memory) vs the all-reduce path, ``--diloco-elements`` fp32
+               per rank
 """
 
 from __future__ import annotations
@@ -61,6 +64,8 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--ep-tokens", type=int, nargs="*", default=[1024, 8192, 65536])
+    ap.add_argument("--diloco-elements", type=int, default=0,
+                    help="per-rank fp32 elements of the DiLoCo outer-step case (0: skip)")
     args = ap.parse_args(argv)
     import datetime
 
@@ -156,6 +161,8 @@ def main(argv=None) -> None:
     heap.close()
     if args.ep_tokens:
         _ep_cases(args, rank, world, dev)
+    if args.diloco_elements:
+        _diloco_case(args, rank, world, dev)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -205,6 +212,32 @@ def _ep_cases(args, rank: int, world: int, dev) -> None:
                                   "speedup_vs_nccl": round(base / ms, 3), "roofline_ms": round(roof, 4),
                                   "frac_of_roofline": round(roof / ms, 3)}), flush=True)
     comm.close()
+
+
+
+def _diloco_case(args, rank: int, world: int, dev) -> None:
+    """One outer step of DiLoCo with every rank a replica: P2P (push pseudo-gradient
+    slices to their owners, fused average + Nesterov, pull the new anchor) against
+    the collective path (all-reduce of the pseudo-gradient, local Nesterov)."""
+    from llm_research_b200.parallel.diloco import DiLoCo, DiLoCoConfig
+
+    n = args.diloco_elements
+    shard = torch.randn(n, device=dev)
+    times = {}
+    for comm in ("p2p", "collective"):
+        dl = DiLoCo([shard], dist.group.WORLD, list(range(world)),
+                    DiLoCoConfig(comm=comm, fault_tolerance=False), tag=f"bench-{comm}")
+        times[comm] = _time(dl.outer_step, args.warmup, args.iters, dev)
+        dl.close()
+    if rank == 0:
+        # each rank sends (world-1)/world of its fp32 pseudo-gradient and receives the same of the anchor
+        nv = n * 4 * (world - 1) / world
+        roof = nv / (NVLINK_GBS * 1e9) * 1e3
+        print(json.dumps({"case": "diloco_outer", "gpus": world, "elements_per_rank": n,
+                          "ms": round(times["p2p"], 4), "collective_ms": round(times["collective"], 4),
+                          "speedup_vs_nccl": round(times["collective"] / times["p2p"], 3),
+                          "roofline_ms": round(roof, 4), "frac_of_roofline": round(roof / times["p2p"], 3)}),
+              flush=True)
 
 
 if __name__ == "__main__":
