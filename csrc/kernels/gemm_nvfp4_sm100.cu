@@ -269,6 +269,9 @@ at::Tensor gemm_nvfp4(const at::Tensor& A, const at::Tensor& sfa, const at::Tens
   if (tile_env == 129) {  // 128 x 128 tiles, 3 stages: two CTAs per SM overlap each other's epilogue
     constexpr size_t sm = smem_bytes<1, 3>();
     LRB_CUDA_CHECK(cudaFuncSetAttribute(gemm_nvfp4_kernel<1, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    // two CTAs of ~110 KB need the largest shared-memory carve-out of the SM
+    LRB_CUDA_CHECK(cudaFuncSetAttribute(gemm_nvfp4_kernel<1, 3>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        (int)cudaSharedmemCarveoutMaxShared));
     gemm_nvfp4_kernel<1, 3><<<dim3((unsigned)nb, (unsigned)mb), kThreads, sm, stream()>>>(ta, tb, args);
   } else if (wide) {
     constexpr size_t sm = smem_bytes<2, 4>();
