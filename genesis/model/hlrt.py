@@ -185,7 +185,12 @@ class HLRT(StatefulModule):
         return_tier_activations: bool = False,
         kv_cache: Optional[Any] = None,
         position_offset: int = 0,
+        labels: Optional[torch.Tensor] = None,
     ) -> Dict[str, Any]:
+        """``labels`` (an extension; per-position targets, ``-100`` ignored): the
+        head and the token cross-entropy run chunk by chunk
+        (``llm_research_b200.ops.loss.linear_cross_entropy``) and the output
+        carries ``lm_loss`` instead of the ``(B, S, vocab)`` logits."""
         B, S = input_ids.shape
         acts: Dict[str, Any] = {}
         x = self.embeddings(input_ids)
@@ -240,7 +245,13 @@ class HLRT(StatefulModule):
             t1 = self.conditioning.apply_cached_plan(t1, self._cached_plan(B))
 
         h = self.output_norm(t1)
-        out = {"logits": self._head(h), "hidden_states": h, "aux_loss": aux}
+        if labels is not None:
+            from llm_research_b200.ops.loss import linear_cross_entropy
+
+            w = self.output_proj.weight if self.output_proj is not None else self.embeddings.weight
+            out = {"logits": None, "lm_loss": linear_cross_entropy(h, w, labels), "hidden_states": h, "aux_loss": aux}
+        else:
+            out = {"logits": self._head(h), "hidden_states": h, "aux_loss": aux}
         if return_tier_activations:
             out["tier_activations"] = acts
         return out

@@ -42,8 +42,13 @@ def ntp_objective(models: Dict[str, nn.Module], ctx: TrainingContext, batch: Any
     input_ids = batch["input_ids"]
     if input_ids.device != device:
         input_ids = input_ids.to(device, non_blocking=True)
-    out = model(input_ids)
-    loss = shifted_cross_entropy(out["logits"], input_ids, ignore_index=-100)
+    if batch.get("fused_lm_loss", False):  # extension: chunked head + CE, no full logits
+        targets = torch.cat([input_ids[:, 1:], input_ids.new_full((input_ids.shape[0], 1), -100)], dim=1)
+        out = model(input_ids, labels=targets)
+        loss = out["lm_loss"]
+    else:
+        out = model(input_ids)
+        loss = shifted_cross_entropy(out["logits"], input_ids, ignore_index=-100)
     aux = out.get("aux_loss", 0.0)
     if isinstance(aux, torch.Tensor):
         loss = loss + aux.to(loss.dtype)
