@@ -191,10 +191,24 @@ class HLRT(StatefulModule):
         head and the token cross-entropy run chunk by chunk
         (``llm_research_b200.ops.loss.linear_cross_entropy``) and the output
         carries ``lm_loss`` instead of the ``(B, S, vocab)`` logits."""
-        B, S = input_ids.shape
-        acts: Dict[str, Any] = {}
         x = self.embeddings(input_ids)
         t1 = self.tier1(x, attention_mask=attention_mask, kv_cache=kv_cache, position_offset=position_offset)
+        return self.forward_after_tier1(t1, attention_mask=attention_mask,
+                                        return_tier_activations=return_tier_activations, kv_cache=kv_cache,
+                                        labels=labels)
+
+    def forward_after_tier1(
+        self,
+        t1: torch.Tensor,
+        attention_mask: Optional[torch.Tensor] = None,
+        return_tier_activations: bool = False,
+        kv_cache: Optional[Any] = None,
+        labels: Optional[torch.Tensor] = None,
+    ) -> Dict[str, Any]:
+        """Everything after the Tier-1 trunk: gates, Tiers 2/3, plan conditioning and
+        the head (the last pipeline stage runs this on the trunk's output)."""
+        B, S = t1.shape[0], t1.shape[1]
+        acts: Dict[str, Any] = {}
         if return_tier_activations:
             acts["tier1"] = t1
 
@@ -204,7 +218,7 @@ class HLRT(StatefulModule):
             out: Dict[str, Any] = {
                 "logits": self._head(h),
                 "hidden_states": h,
-                "aux_loss": torch.zeros((), device=input_ids.device),  # filled on the device (graph-capturable)
+                "aux_loss": torch.zeros((), device=t1.device),  # filled on the device (graph-capturable)
             }
             if return_tier_activations:
                 out["tier_activations"] = acts

@@ -136,8 +136,18 @@ class Tier1TokenProcessor(nn.Module):
         attention_mask: Optional[torch.Tensor] = None,
         kv_cache: Optional[object] = None,
         position_offset: int = 0,
+        layer_range: Optional[tuple] = None,
     ) -> torch.Tensor:
+        """``layer_range = (start, end)`` runs blocks ``start .. end-1`` only (a pipeline
+        stage); the memory read after a block belongs to that block's stage."""
         cos, sin = self.rotary_emb(position_offset + x.size(1))
+        if layer_range is not None:
+            start, end = layer_range
+            for i in range(start, end):
+                x = self.layers[i](x, cos, sin, attention_mask=attention_mask, position_offset=position_offset)
+                if str(i) in self.memory_layers:
+                    x = self.memory_layers[str(i)](x)
+            return x
         tp = self.layers[0].attn.tp if len(self.layers) else None
         if tp is not None and kv_cache is None and attention_mask is None and position_offset == 0:
             from llm_research_b200.parallel.tp import gather_sequence, scatter_sequence
