@@ -90,11 +90,26 @@ def hlrt_config_from_yaml(path_or_cfg: Any, overrides: Optional[Dict[str, Any]] 
     put("gate1_chunk_size", t2.get("chunk_size"))
     put("tier2_moe_num_experts", t2.get("moe_num_experts"))
     put("tier2_moe_top_k", t2.get("moe_top_k"))
+    put("tier2_max_seq_len", t2.get("max_seq_len"))
+    put("tier2_num_kv_heads", t2.get("kv_heads"))
+    put("latent_pool_num_heads", t2.get("latent_pool_heads"))
+    # extensions of the schema: a Tier-1 mixture of experts and PHMA memory reads
+    put("tier1_moe_num_experts", t1.get("moe_num_experts"))
+    put("tier1_moe_top_k", t1.get("moe_top_k"))
+    put("tier1_moe_d_ff", t1.get("moe_d_ff"))
+    put("tier1_moe_shared_experts", t1.get("moe_shared_experts"))
+    put("tier1_moe_capacity_factor", t1.get("moe_capacity_factor"))
+    mem = m.get("memory", {}) or {}
+    put("tier1_memory_every", mem.get("every"))
+    put("memory_slots", mem.get("slots"))
+    put("memory_top_k", mem.get("top_k"))
     put("tier3_d_model", t3.get("d_model"))
     put("tier3_num_layers", t3.get("layers"))
     put("tier3_num_heads", t3.get("heads"))
     put("tier3_d_ff", t3.get("d_ff"))
     put("tier3_recurrence_steps", t3.get("recurrence_steps"))
+    put("tier3_max_seq_len", t3.get("max_seq_len"))
+    put("tier3_num_kv_heads", t3.get("kv_heads"))
     put("gate1_threshold", gate.get("tier2_threshold"))
     put("gate2_threshold", gate.get("tier3_threshold"))
     if "dropout" in m:
