@@ -84,7 +84,10 @@ class FlywheelTrainer:
             ctx = torch.stack([prompts[i].to(self.device) for i in idxs])
             gen = sample_group_batch(self.model, ctx, self.max_trace_tokens, self.temperature, self.device)
             reward = self.reward_fn(self.model, ctx, gen)
-            rewards = reward.float().flatten().tolist() if isinstance(reward, torch.Tensor) else [float(reward)] * len(idxs)
+            if isinstance(reward, torch.Tensor) and reward.numel() == len(idxs):
+                rewards = reward.float().flatten().tolist()
+            else:  # one scalar for the whole group (a plain float or a 0-d tensor)
+                rewards = [float(reward)] * len(idxs)
             ctx_host, gen_host = ctx.cpu(), gen.cpu()
             for j, i in enumerate(idxs):
                 results[i] = {"context_ids": ctx_host[j], "trace_ids": gen_host[j], "reward": rewards[j],

@@ -39,6 +39,13 @@ def int4_quantize(x2d: torch.Tensor, group_size: int) -> Tuple[torch.Tensor, tor
     g = _resolve_group(group_size, D)
     if x2d.is_cuda:
         return native().int4_quantize(x2d.contiguous(), g)
+    return int4_quantize_torch(x2d, g)
+
+
+def int4_quantize_torch(x2d: torch.Tensor, group_size: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The same quantiser in plain PyTorch on any device (the oracle of the kernel)."""
+    M, D = x2d.shape
+    g = _resolve_group(group_size, D)
     ng = (D + g - 1) // g
     xp = F.pad(x2d, (0, ng * g - D)).view(M, ng, g).float()
     scale = (xp.abs().amax(-1, keepdim=True) / INT4_MAX).clamp(min=SCALE_EPS)
@@ -51,6 +58,12 @@ def int4_dequantize(q2d: torch.Tensor, scales: torch.Tensor, group_size: int) ->
     g = _resolve_group(group_size, D)
     if q2d.is_cuda:
         return native().int4_dequantize(q2d.contiguous(), scales.contiguous().float(), g)
+    return int4_dequantize_torch(q2d, scales, g)
+
+
+def int4_dequantize_torch(q2d: torch.Tensor, scales: torch.Tensor, group_size: int) -> torch.Tensor:
+    M, D = q2d.shape
+    g = _resolve_group(group_size, D)
     ng = scales.shape[1]
     qp = F.pad(q2d, (0, ng * g - D)).view(M, ng, g).float()
     return (qp * scales[:, :, None]).view(M, ng * g)[:, :D]

@@ -39,6 +39,19 @@ class _FP4MatmulFn(torch.autograd.Function):
         return gx, gw, gb, None, None
 
 
+def _fp4_matmul_pt(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                   act_group_size: int = -1, weight_group_size: int = -1) -> torch.Tensor:
+    """Plain-PyTorch fake-quantised linear (``fp4_matmul.py:37-57``):
+    ``qdq(x) @ qdq(w)^T + b`` with straight-through gradients to x, w and b."""
+    from olympus.kernels.fp4_quantize import _dequantize_pt, _quantize_pt
+
+    def qdq(t, g):
+        q, s = _quantize_pt(t.detach(), g)
+        return t + (_dequantize_pt(q, s, g).to(t.dtype) - t).detach()
+
+    return F.linear(qdq(x, act_group_size), qdq(weight, weight_group_size), bias)
+
+
 def _nvfp4_linear(x, weight, bias):
     from llm_research_b200.ops.nvfp4 import nvfp4_linear
 

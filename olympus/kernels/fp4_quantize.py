@@ -12,11 +12,31 @@ from __future__ import annotations
 
 import torch
 
-from llm_research_b200.ops.quant import INT4_MAX, INT4_MIN, SCALE_EPS, _resolve_group, int4_dequantize, int4_quantize
+from llm_research_b200.ops.quant import (INT4_MAX, INT4_MIN, SCALE_EPS, _resolve_group, int4_dequantize,
+                                         int4_dequantize_torch, int4_quantize, int4_quantize_torch)
 
 __all__ = ["quantize", "dequantize", "quantize_dequantize", "INT4_MIN", "INT4_MAX", "SCALE_EPS", "_resolve_group_size"]
 
 _resolve_group_size = _resolve_group
+# The reference exposes HAS_TRITON for its Triton path; this framework has none.
+HAS_TRITON = False
+
+
+def _quantize_pt(x: torch.Tensor, group_size: int = -1):
+    """Plain-PyTorch quantiser on any device (``fp4_quantize.py:38-62``):
+    ``(q int8 (..., D), scales fp32 (..., ceil(D / g)))``."""
+    D = x.shape[-1]
+    q, s = int4_quantize_torch(x.reshape(-1, D), group_size)
+    return q.reshape(x.shape), s.reshape(*x.shape[:-1], s.shape[-1])
+
+
+def _dequantize_pt(q: torch.Tensor, scales: torch.Tensor, group_size: int = -1, orig_D: int | None = None):
+    """Plain-PyTorch dequantiser (``fp4_quantize.py:65-83``); ``orig_D`` trims
+    a padded last dimension."""
+    D = q.shape[-1] if orig_D is None else orig_D
+    q2 = q.reshape(-1, q.shape[-1])[:, :D]
+    out = int4_dequantize_torch(q2.contiguous(), scales.reshape(-1, scales.shape[-1]).float(), group_size)
+    return out.reshape(*q.shape[:-1], D)
 
 
 def quantize(x: torch.Tensor, group_size: int = -1):

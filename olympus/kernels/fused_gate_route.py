@@ -12,11 +12,22 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from llm_research_b200._ext import available as _native_available
-from llm_research_b200.ops.routing import chunk_mean_pool, softmax_topk
+from llm_research_b200.ops.routing import _softmax_topk_ref, chunk_mean_pool, softmax_topk
 
 # The reference exposes HAS_TRITON; this framework has no Triton path.
 HAS_TRITON = False
 HAS_NATIVE = _native_available()
+
+
+def _chunk_mean_pool_pt(x: torch.Tensor, chunk_size: int) -> torch.Tensor:
+    """Plain-PyTorch chunk mean (``fused_gate_route.py:30-34``), the kernel's oracle."""
+    B, S, D = x.shape
+    return x.view(B, S // chunk_size, chunk_size, D).mean(dim=2)
+
+
+def _softmax_topk_pt(logits: torch.Tensor, top_k: int):
+    """Plain-PyTorch softmax + top-k + renormalisation (``fused_gate_route.py:37-47``)."""
+    return _softmax_topk_ref(logits, top_k)
 
 
 def fused_gate_route(

@@ -27,3 +27,9 @@ def _naive_expert_dispatch(x, expert_indices, expert_weights, experts, num_exper
 def sparse_expert_matmul(x: torch.Tensor, expert_indices: torch.Tensor, expert_weights: torch.Tensor,
                          experts: nn.ModuleList, num_experts: int, top_k: int) -> torch.Tensor:
     return grouped_expert_apply(x, expert_indices[:, :top_k], expert_weights[:, :top_k], experts, num_experts).to(x.dtype)
+
+
+def _sorted_expert_dispatch(x, expert_indices, expert_weights, experts, num_experts, top_k):
+    """The sorted dispatch itself (``sparse_expert_matmul.py:26-99``): one stable
+    sort by expert, one contiguous slice per expert, one ``index_add`` back."""
+    return grouped_expert_apply(x, expert_indices[:, :top_k], expert_weights[:, :top_k], experts, num_experts).to(x.dtype)
