@@ -65,6 +65,8 @@ def parse_args(argv=None):
                     help="tensor-parallel group size for the Tier-1 trunk (consecutive ranks); FSDP over the rest")
     ap.add_argument("--ep", action="store_true",
                     help="expert parallelism over all ranks for MoE presets (each rank holds E/world experts)")
+    ap.add_argument("--fused-loss", action="store_true",
+                    help="head + cross-entropy chunk by chunk without the full logits (vocabulary-parallel under --tp)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--count-launches", type=int, default=1)
     return ap.parse_args(argv)
@@ -176,7 +178,7 @@ def run_ours(args) -> dict:
     def step(batches):
         out = None
         for b in batches:
-            out = trainer.train_step({"input_ids": b})
+            out = trainer.train_step({"input_ids": b, "fused_lm_loss": args.fused_loss})
         return out["loss"]
 
     for _ in range(args.warmup):
@@ -255,6 +257,7 @@ def run_ours(args) -> dict:
                             + (f" + tp{tp} (sequence parallel Tier 1)" if tp > 1 else "")
                             + (f" + ep{world}" if args.ep else "")),
             "linear_precision": args.precision,
+            "loss": ("fused head + CE" + (" (vocabulary-parallel)" if tp > 1 else "")) if args.fused_loss else "logits + CE",
             "preset": args.preset,
             "optimizer": "MuonAdamWHybrid (Muon on 2-D, AdamW on embedding/norms)",
             "l2": "inputs+activations >> 126 MB L2; no flush",

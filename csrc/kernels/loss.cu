@@ -67,7 +67,10 @@ __global__ void __launch_bounds__(kThreads) ce_fwd_kernel(const T* __restrict__ 
   }
 }
 
-template <typename T>
+// kShard: the logits are one vocabulary shard and lse is the row's log-sum-exp over the
+// whole vocabulary; a target outside [0, V) belongs to another shard, so the row still
+// takes the softmax gradient, without the one-hot term.  Otherwise such a row is ignored.
+template <typename T, bool kShard>
 __global__ void __launch_bounds__(kThreads) ce_bwd_kernel(const T* __restrict__ logits, const int64_t* __restrict__ tgt,
                                                           const float* __restrict__ lse, const float* __restrict__ scale,
                                                           T* __restrict__ dx, int64_t V, int64_t ignore) {
@@ -75,7 +78,8 @@ __global__ void __launch_bounds__(kThreads) ce_bwd_kernel(const T* __restrict__ 
   const T* x = logits + row * V;
   T* d = dx + row * V;
   const int64_t t = tgt[row];
-  const float g = (t == ignore || t < 0 || t >= V) ? 0.f : scale[0];
+  const bool counted = kShard ? (t != ignore) : (t != ignore && t >= 0 && t < V);
+  const float g = counted ? scale[0] : 0.f;
   const float l = lse[row];
   const bool vec = (sizeof(T) == 2) && (V % 8 == 0);
   if (vec) {
@@ -122,21 +126,41 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> ce_fwd(const at::Tensor& logits, 
   return {acc[0], acc[1], lse};
 }
 
-at::Tensor ce_bwd(const at::Tensor& logits, const at::Tensor& targets, const at::Tensor& lse, const at::Tensor& scale,
-                  int64_t ignore_index) {
+namespace {
+at::Tensor ce_bwd_impl(const at::Tensor& logits, const at::Tensor& targets, const at::Tensor& lse,
+                       const at::Tensor& scale, int64_t ignore_index, bool shard) {
+  LRB_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.is_contiguous(), "ce_bwd: logits must be contiguous 2-D");
+  LRB_CHECK(targets.scalar_type() == at::kLong && targets.numel() == logits.size(0), "ce_bwd: bad targets");
+  LRB_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == logits.size(0), "ce_bwd: lse must be fp32 per row");
   c10::cuda::CUDAGuard g(logits.device());
   const int64_t R = logits.size(0), V = logits.size(1);
   auto dx = at::empty_like(logits);
   auto sc = scale.to(at::kFloat).reshape({1}).contiguous();
+  auto tg = targets.contiguous();
+  auto ls = lse.contiguous();
   if (R > 0) {
     LRB_DISPATCH_FLOAT(logits.scalar_type(), T, [&] {
-      ce_bwd_kernel<T><<<(unsigned)R, kThreads, 0, stream()>>>(
-          reinterpret_cast<const T*>(logits.data_ptr()), targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
+      auto kern = shard ? ce_bwd_kernel<T, true> : ce_bwd_kernel<T, false>;
+      kern<<<(unsigned)R, kThreads, 0, stream()>>>(
+          reinterpret_cast<const T*>(logits.data_ptr()), tg.data_ptr<int64_t>(), ls.data_ptr<float>(),
           sc.data_ptr<float>(), reinterpret_cast<T*>(dx.data_ptr()), V, ignore_index);
     });
     LRB_LAUNCH_CHECK();
   }
   return dx;
+}
+}  // namespace
+
+at::Tensor ce_bwd(const at::Tensor& logits, const at::Tensor& targets, const at::Tensor& lse, const at::Tensor& scale,
+                  int64_t ignore_index) {
+  return ce_bwd_impl(logits, targets, lse, scale, ignore_index, false);
+}
+
+// Gradient of one vocabulary shard's logits: targets are shard-local ids (outside
+// [0, V) when another shard owns the target), lse the full-vocabulary log-sum-exp.
+at::Tensor ce_bwd_vocab_shard(const at::Tensor& logits, const at::Tensor& targets, const at::Tensor& lse,
+                              const at::Tensor& scale, int64_t ignore_index) {
+  return ce_bwd_impl(logits, targets, lse, scale, ignore_index, true);
 }
 
 }  // namespace lrb

@@ -153,6 +153,11 @@ class HLRT(StatefulModule):
         self.conditioning = TopDownConditioning(d_model=c.d_model, tier2_dim=c.tier2_d_model, chunk_size=c.gate1_chunk_size)
         self.output_norm = RMSNorm(c.d_model, eps=c.norm_eps)
         self.output_proj = None if c.tie_word_embeddings else nn.Linear(c.d_model, c.vocab_size, bias=False)
+        # built under a tensor-parallel context: the fused head + loss splits the vocabulary
+        # over that group (head weights stay replicated, the gradients come back replicated)
+        from llm_research_b200.parallel.tp import enclosing_tensor_parallel_group
+
+        self._vocab_parallel_group = enclosing_tensor_parallel_group()
         self.register_state("last_plan_vector", torch.zeros(1, c.d_model), persistent=False)
         self._init_weights()
 
@@ -260,10 +265,14 @@ class HLRT(StatefulModule):
 
         h = self.output_norm(t1)
         if labels is not None:
-            from llm_research_b200.ops.loss import linear_cross_entropy
+            from llm_research_b200.ops.loss import linear_cross_entropy, vocab_parallel_linear_cross_entropy
 
             w = self.output_proj.weight if self.output_proj is not None else self.embeddings.weight
-            out = {"logits": None, "lm_loss": linear_cross_entropy(h, w, labels), "hidden_states": h, "aux_loss": aux}
+            if self._vocab_parallel_group is not None:
+                lm_loss = vocab_parallel_linear_cross_entropy(h, w, labels, self._vocab_parallel_group)
+            else:
+                lm_loss = linear_cross_entropy(h, w, labels)
+            out = {"logits": None, "lm_loss": lm_loss, "hidden_states": h, "aux_loss": aux}
         else:
             out = {"logits": self._head(h), "hidden_states": h, "aux_loss": aux}
         if return_tier_activations:

@@ -273,6 +273,15 @@ def current_tensor_parallel() -> Optional[Tuple[dist.ProcessGroup, Optional[TPCo
     return _TP_STATE if _TP_SCOPE else None
 
 
+def enclosing_tensor_parallel_group() -> Optional[dist.ProcessGroup]:
+    """The group of an enclosing ``tensor_parallel`` context with more than one
+    rank, inside or outside the trunk's scope (the head uses it for the
+    vocabulary-parallel loss); ``None`` otherwise."""
+    if _TP_STATE is None or dist.get_world_size(_TP_STATE[0]) < 2:
+        return None
+    return _TP_STATE[0]
+
+
 def mark_tp(p: nn.Parameter, dim: int) -> nn.Parameter:
     """Tag a TP weight shard with the dimension along which the shards of the
     group concatenate to the full weight (0: column parallel, 1: row parallel)."""

@@ -1,6 +1,7 @@
 """Chunked linear + cross-entropy (the head without full logits) against the
 logits path: the loss and every gradient agree."""
 
+import pytest
 import torch
 import torch.nn.functional as F
 
@@ -40,3 +41,58 @@ def test_hlrt_ntp_with_fused_head_matches_logits_path():
     assert abs(grads[0][0] - grads[1][0]) < 1e-5
     for n, g in grads[0][1].items():
         torch.testing.assert_close(grads[1][1][n], g, atol=1e-5, rtol=1e-4, msg=n)
+
+
+@pytest.mark.gpu
+def test_ce_bwd_vocab_shard_kernel_matches_fp32():
+    """Gradient of one vocabulary shard's logits against the fp32 softmax of the full row."""
+    from llm_research_b200._ext import native
+
+    g = torch.Generator().manual_seed(5)
+    R, V, v0, v1 = 300, 1000, 400, 720
+    full = torch.randn(R, V, generator=g) * 3
+    t = torch.randint(0, V, (R,), generator=g)
+    t[::9] = -100
+    lse = torch.logsumexp(full, dim=-1)
+    loc = full[:, v0:v1].to(torch.bfloat16)
+    owned = (t >= v0) & (t < v1)
+    t_loc = torch.where(owned, t - v0, torch.where(t != -100, torch.full_like(t, -1), t))
+    scale = torch.tensor([0.25])
+    got = native().ce_bwd_vocab_shard(loc.cuda(), t_loc.cuda(), lse.cuda(), scale.cuda(), -100).float().cpu()
+    p = torch.exp(loc.float() - lse[:, None])
+    rows = torch.arange(R)[owned]
+    p[rows, t_loc[owned]] -= 1.0
+    ref = p * ((t != -100).float() * 0.25)[:, None]
+    torch.testing.assert_close(got, ref, atol=2e-3, rtol=2e-2)
+
+
+@pytest.mark.gpu
+def test_vocab_parallel_linear_cross_entropy_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from tests.dist_utils import run_ranks
+
+    for res in run_ranks(_vocab_ce_gpu_case, 2, backend="nccl"):
+        for r, got in zip(res["full"], res["vp"]):
+            torch.testing.assert_close(got.float(), r.float(), atol=2e-2, rtol=2e-2)
+
+
+def _vocab_ce_gpu_case(rank, world):
+    import torch.distributed as dist
+
+    from llm_research_b200.ops.loss import linear_cross_entropy, vocab_parallel_linear_cross_entropy
+
+    dev = torch.device("cuda", rank)
+    g = torch.Generator().manual_seed(7)
+    h = (torch.randn(1024, 256, generator=g)).to(dev, torch.bfloat16)
+    w = (torch.randn(4000, 256, generator=g) * 0.05).to(dev, torch.bfloat16)
+    t = torch.randint(0, 4000, (1024,), generator=g).to(dev)
+    t[::11] = -100
+    out = {}
+    for name, fn in (("full", lambda a, b: linear_cross_entropy(a, b, t, chunk=512)),
+                     ("vp", lambda a, b: vocab_parallel_linear_cross_entropy(a, b, t, dist.group.WORLD, chunk=512))):
+        a, b = h.clone().requires_grad_(), w.clone().requires_grad_()
+        loss = fn(a, b)
+        loss.backward()
+        out[name] = (loss.detach().cpu(), a.grad.cpu(), b.grad.cpu())
+    return out

@@ -73,7 +73,7 @@ def test_tp_layers_fused_kernels_gpu():
     _check(run_ranks(_tp_case, 2, True, backend="nccl"), 2, 5e-2)
 
 
-def _hlrt_tp_case(rank, world, fused, memory=False):
+def _hlrt_tp_case(rank, world, fused, memory=False, labels=False):
     """HLRT with a tensor + sequence parallel Tier 1 against the same weights unsharded."""
     import torch.distributed as dist
 
@@ -106,11 +106,19 @@ def _hlrt_tp_case(rank, world, fused, memory=False):
     full.to(dt)
     tp.to(dt)
     ids = torch.randint(0, cfg.vocab_size, (2, 128), generator=torch.Generator().manual_seed(1)).to(dev)
-    out_f = full(ids)["logits"]
-    out_t = tp(ids)["logits"]
-    gl = torch.randn(out_f.shape, generator=torch.Generator().manual_seed(2)).to(dev, dt)
-    (out_f.float() * gl.float()).sum().backward()
-    (out_t.float() * gl.float()).sum().backward()
+    if labels:  # fused head + loss: vocabulary-parallel over the TP group
+        assert tp._vocab_parallel_group is not None and full._vocab_parallel_group is None
+        tgt = torch.cat([ids[:, 1:], ids.new_full((2, 1), -100)], dim=1)
+        out_f = full(ids, labels=tgt)["lm_loss"]
+        out_t = tp(ids, labels=tgt)["lm_loss"]
+        out_f.backward()
+        out_t.backward()
+    else:
+        out_f = full(ids)["logits"]
+        out_t = tp(ids)["logits"]
+        gl = torch.randn(out_f.shape, generator=torch.Generator().manual_seed(2)).to(dev, dt)
+        (out_f.float() * gl.float()).sum().backward()
+        (out_t.float() * gl.float()).sum().backward()
     res = {"logits": (out_f.float().cpu(), out_t.float().cpu()), "grads": {}}
     for name, p in tp.named_parameters():
         if p.grad is None:
@@ -133,6 +141,42 @@ def test_hlrt_tensor_parallel_tier1_matches_unsharded_cpu(memory):
         assert any("q_proj" in n for n in res["grads"]) and any("attn_norm" in n for n in res["grads"])
         for name, (r, g) in res["grads"].items():
             torch.testing.assert_close(g, r, atol=1e-4, rtol=1e-3, msg=name)
+
+
+def test_hlrt_tensor_parallel_vocab_parallel_loss_cpu():
+    for res in run_ranks(_hlrt_tp_case, 2, False, False, True):
+        ref, got = res["logits"]
+        torch.testing.assert_close(got, ref, atol=1e-5, rtol=1e-5)
+        assert any("embeddings" in n for n in res["grads"])
+        for name, (r, g) in res["grads"].items():
+            torch.testing.assert_close(g, r, atol=1e-4, rtol=1e-3, msg=name)
+
+
+def _vocab_ce_case(rank, world, V):
+    import torch.distributed as dist
+
+    from llm_research_b200.ops.loss import linear_cross_entropy, vocab_parallel_linear_cross_entropy
+
+    g = torch.Generator().manual_seed(3)
+    h = torch.randn(50, 16, generator=g)
+    w = torch.randn(V, 16, generator=g) * 0.5
+    t = torch.randint(0, V, (50,), generator=g)
+    t[::7] = -100
+    out = {}
+    for name, fn in (("full", lambda a, b: linear_cross_entropy(a, b, t, chunk=16)),
+                     ("vp", lambda a, b: vocab_parallel_linear_cross_entropy(a, b, t, dist.group.WORLD, chunk=16))):
+        a, b = h.clone().requires_grad_(), w.clone().requires_grad_()
+        loss = fn(a, b)
+        (loss * 1.5).backward()
+        out[name] = (loss.detach(), a.grad, b.grad)
+    return out
+
+
+@pytest.mark.parametrize("V", [40, 37])
+def test_vocab_parallel_linear_cross_entropy_cpu(V):
+    for res in run_ranks(_vocab_ce_case, 2, V):
+        for r, g in zip(res["full"], res["vp"]):
+            torch.testing.assert_close(g, r, atol=1e-5, rtol=1e-5)
 
 
 @pytest.mark.gpu
