@@ -180,10 +180,11 @@ def test_vocab_parallel_linear_cross_entropy_cpu(V):
 
 
 @pytest.mark.gpu
-def test_hlrt_tensor_parallel_tier1_fused_kernels():
+@pytest.mark.parametrize("labels", [False, True])
+def test_hlrt_tensor_parallel_tier1_fused_kernels(labels):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    for res in run_ranks(_hlrt_tp_case, 2, True, backend="nccl"):
+    for res in run_ranks(_hlrt_tp_case, 2, True, False, labels, backend="nccl"):
         ref, got = res["logits"]
         assert ((got - ref).norm() / ref.norm()).item() < 2e-2
         for name, (r, g) in res["grads"].items():
