@@ -26,7 +26,7 @@ namespace lrb {
 namespace {
 
 constexpr long long kPollLimit = 1ll << 24;
-enum : int { kErrEpReady = 31, kErrEpSlot = 32 };
+enum : int { kErrEpReady = 31, kErrEpSlot = 32, kErrEpIndex = 33 };
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -89,6 +89,16 @@ __device__ __forceinline__ int64_t slot_row(const EpArgs& a, int le, int src, in
   return ((int64_t)le * a.world + src) * a.cap + slot;
 }
 
+// Routing indices come from data: an owner, local expert or slot outside the
+// buffers records kErrEpIndex and the row is skipped, never written or read
+// out of bounds on a peer.
+__device__ __forceinline__ bool route_ok(const EpArgs& a, int64_t as, int s) {
+  const int dst = a.dest[as], le = a.le[as];
+  const bool ok = s < a.cap && dst >= 0 && dst < a.world && le >= 0 && le < a.epl;
+  if (!ok) atomicCAS(a.err, 0, kErrEpIndex);
+  return ok;
+}
+
 // rows: per_assignment ? (T*k, d) : (T, d)
 __global__ void ep_push_kernel(const __nv_bfloat16* __restrict__ rows, const float* __restrict__ scale, int64_t TK,
                                int per_assignment, EpArgs a) {
@@ -97,7 +107,7 @@ __global__ void ep_push_kernel(const __nv_bfloat16* __restrict__ rows, const flo
   if (ok) {
     for (int64_t as = (int64_t)blockIdx.x * wpb + warp; as < TK; as += (int64_t)gridDim.x * wpb) {
       const int s = a.slot[as];
-      if (s < 0) continue;
+      if (s < 0 || !route_ok(a, as, s)) continue;
       const int64_t src_row = per_assignment ? as : as / a.k;
       const float sc = scale != nullptr ? scale[as] : 1.f;
       const uint4* src = reinterpret_cast<const uint4*>(rows + src_row * a.d);
@@ -133,7 +143,7 @@ __global__ void ep_pull_kernel(__nv_bfloat16* __restrict__ out, __nv_bfloat16* _
           const int64_t as = t * a.k + j;
           const int s = a.slot[as];
           Vec16<__nv_bfloat16> v;
-          if (s >= 0) {
+          if (s >= 0 && route_ok(a, as, s)) {
             v.raw = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.bases[a.dest[as]] + a.buf_off) +
                                                    slot_row(a, a.le[as], a.rank, s) * a.d)[i];
           } else {

@@ -195,12 +195,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename V>
 __global__ void topk_gather_fwd_kernel(const float* __restrict__ s, const int* __restrict__ idx,
                                        const V* __restrict__ values, V* __restrict__ out, float* __restrict__ w_out,
-                                       int T, int Dv) {
+                                       int T, int Dv, int N) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= T) return;
   const float sv = s[(int64_t)row * TOPK + lane];
-  const int iv = idx[(int64_t)row * TOPK + lane];
+  int iv = idx[(int64_t)row * TOPK + lane];
+  if (iv >= N) iv = -1;  // an index past the bank is treated like an empty candidate
   const bool valid = iv >= 0;
   float m = warp_max(valid ? sv : -INFINITY);
   const float e = valid ? __expf(sv - m) : 0.f;
@@ -227,12 +228,13 @@ __global__ void topk_gather_fwd_kernel(const float* __restrict__ s, const int* _
 template <typename V>
 __global__ void topk_gather_bwd_kernel(const V* __restrict__ g, const float* __restrict__ w, const int* __restrict__ idx,
                                        const V* __restrict__ values, const V* __restrict__ keys,
-                                       float* __restrict__ dq, int T, int Dv, int Dk) {
+                                       float* __restrict__ dq, int T, int Dv, int Dk, int N) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= T) return;
   const float wv = w[(int64_t)row * TOPK + lane];
-  const int iv = idx[(int64_t)row * TOPK + lane];
+  int iv = idx[(int64_t)row * TOPK + lane];
+  if (iv >= N) iv = -1;
   float dw_mine = 0.f;
   for (int j = 0; j < TOPK; ++j) {
     const int ij = __shfl_sync(0xffffffffu, iv, j);
@@ -351,7 +353,7 @@ std::tuple<at::Tensor, at::Tensor> topk_gather_fwd(const at::Tensor& s, const at
   LRB_DISPATCH_FLOAT(values.scalar_type(), V, [&] {
     topk_gather_fwd_kernel<V><<<(T + 7) / 8, 256, 0, stream()>>>(
         s.data_ptr<float>(), idx.data_ptr<int>(), reinterpret_cast<const V*>(values.data_ptr()),
-        reinterpret_cast<V*>(out.data_ptr()), w.data_ptr<float>(), T, Dv);
+        reinterpret_cast<V*>(out.data_ptr()), w.data_ptr<float>(), T, Dv, (int)values.size(0));
   });
   LRB_LAUNCH_CHECK();
   return {out, w};
@@ -371,7 +373,7 @@ at::Tensor topk_gather_bwd(const at::Tensor& g, const at::Tensor& w, const at::T
     topk_gather_bwd_kernel<V><<<(T + 7) / 8, 256, 0, stream()>>>(
         reinterpret_cast<const V*>(g.data_ptr()), w.data_ptr<float>(), idx.data_ptr<int>(),
         reinterpret_cast<const V*>(values.data_ptr()), reinterpret_cast<const V*>(keys.data_ptr()),
-        dq.data_ptr<float>(), T, Dv, Dk);
+        dq.data_ptr<float>(), T, Dv, Dk, (int)std::min(values.size(0), keys.size(0)));
   });
   LRB_LAUNCH_CHECK();
   return dq;

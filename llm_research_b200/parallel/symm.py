@@ -25,7 +25,12 @@ import torch.distributed as dist
 
 from llm_research_b200._ext import native
 
-_ERR_NAMES = {11: "timed out waiting for a peer's data flag", 12: "timed out waiting for a peer to free its slot"}
+_ERR_NAMES = {11: "timed out waiting for a peer's data flag", 12: "timed out waiting for a peer to free its slot",
+              21: "tensor parallel: timed out waiting for a peer", 22: "tensor parallel: timed out waiting for "
+              "a slot", 23: "tensor parallel: timed out waiting for a gathered chunk",
+              31: "expert parallel: timed out waiting for an owner's output", 32: "expert parallel: timed out "
+              "waiting for an owner to release its slots", 33: "expert parallel: routing index outside the "
+              "buffers (row skipped)"}
 
 
 def _round_up(x: int, m: int) -> int:
