@@ -135,6 +135,9 @@ class DistributedBootstrapTrainer:
                 logger.info("Step %d | loss=%.4f | lr=%.2e | %.0f tok/s", gs, loss, m["lr"], m["tokens_per_sec"])
             if save_every > 0 and gs > 0 and gs % save_every == 0 and self.orchestrator._accumulation_step == 0:
                 self.save_checkpoint(os.path.join(ckpt_dir, f"checkpoint_step{gs}.pt"))
+            max_steps = self.config.get("max_steps")  # extension: stop inside the epoch at the step budget
+            if max_steps is not None and gs >= max_steps and self.orchestrator._accumulation_step == 0:
+                break
         avg = tot / max(steps, 1)
         if self.is_main_rank:
             logger.info("Epoch complete | avg_loss=%.4f | %d steps in %.1fs", avg, steps, time.time() - start)
@@ -159,38 +162,66 @@ def main(argv=None) -> None:
 
     ap = argparse.ArgumentParser(description="GENESIS phase-1 distributed training")
     ap.add_argument("--preset", default="genesis-1b")
-    ap.add_argument("--config", default=None, help="YAML in the reference's nested model schema")
+    ap.add_argument("--config", default=None, help="YAML in the reference's nested schema (model, optimizer, "
+                    "scheduler, training, hardware sections)")
+    ap.add_argument("--set", dest="overrides", action="append", default=[], metavar="KEY.PATH=VALUE",
+                    help="dotted override of the YAML, repeatable (e.g. --set model.tier1.layers=4)")
     ap.add_argument("--data-dir", default=None, help="packed data; synthetic tokens when omitted")
     ap.add_argument("--checkpoint-dir", default="checkpoints/phase1")
     ap.add_argument("--resume", default=None)
-    ap.add_argument("--max-steps", type=int, default=50000)
-    ap.add_argument("--batch-size", type=int, default=8)
-    ap.add_argument("--grad-accum", type=int, default=4)
-    ap.add_argument("--lr", type=float, default=3e-4)
-    ap.add_argument("--muon-lr", type=float, default=0.02)
-    ap.add_argument("--warmup-steps", type=int, default=2000)
-    ap.add_argument("--log-interval", type=int, default=10)
-    ap.add_argument("--save-interval", type=int, default=1000)
-    ap.add_argument("--seq-len", type=int, default=4096)
+    # None: take the value from --config, else the default in brackets
+    ap.add_argument("--max-steps", type=int, default=None, help="[50000]")
+    ap.add_argument("--batch-size", type=int, default=None, help="[8]")
+    ap.add_argument("--grad-accum", type=int, default=None, help="[4]")
+    ap.add_argument("--lr", type=float, default=None, help="AdamW / base learning rate [3e-4]")
+    ap.add_argument("--muon-lr", type=float, default=None, help="[0.02]")
+    ap.add_argument("--warmup-steps", type=int, default=None, help="[2000]")
+    ap.add_argument("--log-interval", type=int, default=None, help="[10]")
+    ap.add_argument("--save-interval", type=int, default=None, help="[1000]")
+    ap.add_argument("--seq-len", type=int, default=None, help="[4096]")
     args = ap.parse_args(argv)
     logging.basicConfig(level=logging.INFO, format=f"[rank {os.environ.get('RANK', 0)}] %(name)s | %(message)s")
+    opt_kw: dict = {"lr_muon": 0.02, "lr_adamw": 3e-4, "weight_decay_adamw": 0.01, "ns_steps": 5}
+    sched_kw: dict = {"min_lr": 2e-5}
+    run = {"max_steps": 50000, "batch_size": 8, "gradient_accumulation_steps": 4, "log_interval": 10,
+           "save_interval": 1000, "seq_len": 4096, "max_grad_norm": 1.0}
     if args.config:
-        from olympus.utils.config import hlrt_config_from_yaml
+        from olympus.utils.config import hlrt_config_from_yaml, load_config, parse_overrides, trainer_settings_from_yaml
 
-        cfg = hlrt_config_from_yaml(args.config)
+        yaml_cfg = load_config(args.config, parse_overrides(args.overrides))
+        cfg = hlrt_config_from_yaml(yaml_cfg)
+        settings = trainer_settings_from_yaml(yaml_cfg)
+        opt_kw.update(settings["optimizer_kwargs"])
+        sched_kw.update(settings["scheduler_kwargs"])
+        run.update({k: v for k, v in settings["trainer"].items() if k in run})
     else:
+        if args.overrides:
+            ap.error("--set needs --config")
         cfg = build_hlrt_config(args.preset)
+    for flag, key in (("max_steps", "max_steps"), ("batch_size", "batch_size"), ("grad_accum", "gradient_accumulation_steps"),
+                      ("log_interval", "log_interval"), ("save_interval", "save_interval"), ("seq_len", "seq_len")):
+        if getattr(args, flag) is not None:
+            run[key] = getattr(args, flag)
+    if args.lr is not None:
+        opt_kw["lr_adamw"] = sched_kw["base_lr"] = args.lr
+    if args.muon_lr is not None:
+        opt_kw["lr_muon"] = args.muon_lr
+    if args.warmup_steps is not None:
+        sched_kw["warmup_steps"] = args.warmup_steps
+    sched_kw.setdefault("base_lr", opt_kw["lr_adamw"])
+    sched_kw.setdefault("warmup_steps", 2000)
+    sched_kw.setdefault("total_steps", run["max_steps"])
+    sched_kw.setdefault("decay_start", int(sched_kw["total_steps"] * 0.9))
     torch.manual_seed(0)
     model = HLRT(cfg)
     trainer = DistributedBootstrapTrainer(
         model,
-        optimizer_kwargs={"lr_muon": args.muon_lr, "lr_adamw": args.lr, "weight_decay_adamw": 0.01, "ns_steps": 5},
-        scheduler_kwargs={"base_lr": args.lr, "min_lr": 2e-5, "warmup_steps": args.warmup_steps,
-                          "total_steps": args.max_steps, "decay_start": int(args.max_steps * 0.9)},
+        optimizer_kwargs=opt_kw,
+        scheduler_kwargs=sched_kw,
         tokenizer=TokenizerWrapper(backend="char", vocab_size=cfg.vocab_size),
-        config={"gradient_accumulation_steps": args.grad_accum, "max_grad_norm": 1.0,
-                "log_interval": args.log_interval, "save_interval": args.save_interval,
-                "checkpoint_dir": args.checkpoint_dir},
+        config={"gradient_accumulation_steps": run["gradient_accumulation_steps"], "max_grad_norm": run["max_grad_norm"],
+                "log_interval": run["log_interval"], "save_interval": run["save_interval"],
+                "checkpoint_dir": args.checkpoint_dir, "max_steps": run["max_steps"]},
     )
     if args.resume:
         trainer.load_checkpoint(args.resume)
@@ -201,10 +232,10 @@ def main(argv=None) -> None:
     else:
         from olympus.data.packed_dataset import SyntheticTokenDataset
 
-        ds = SyntheticTokenDataset(max(args.batch_size * trainer.world_size * 64, 64), args.seq_len, cfg.vocab_size)
-    loader = trainer.make_dataloader(ds, batch_size=args.batch_size, num_workers=2)
+        ds = SyntheticTokenDataset(max(run["batch_size"] * trainer.world_size * 64, 64), run["seq_len"], cfg.vocab_size)
+    loader = trainer.make_dataloader(ds, batch_size=run["batch_size"], num_workers=2)
     epoch = 0
-    while trainer.orchestrator.global_step < args.max_steps:
+    while trainer.orchestrator.global_step < run["max_steps"]:
         if isinstance(loader.sampler, DistributedSampler):
             loader.sampler.set_epoch(epoch)
         trainer.orchestrator.set_epoch(epoch)

@@ -122,3 +122,61 @@ def hlrt_config_from_yaml(path_or_cfg: Any, overrides: Optional[Dict[str, Any]] 
         for k in ("tier1_use_flash_attention", "tier2_use_flash_attention", "tier3_use_flash_attention"):
             kw[k] = m["use_flash_attention"]
     return HLRTConfig(**kw)
+
+
+def parse_overrides(items) -> Dict[str, Any]:
+    """``["model.tier1.layers=4", "optimizer.muon_lr=0.01"]`` -> dotted-key dict; values
+    are parsed as YAML scalars/lists (``4`` -> int, ``[0.9, 0.95]`` -> list, ``true`` -> bool)."""
+    import yaml
+
+    out: Dict[str, Any] = {}
+    for item in items or ():
+        key, sep, value = item.partition("=")
+        if not sep or not key:
+            raise ValueError(f"override must look like key.path=value, got {item!r}")
+        out[key.strip()] = yaml.safe_load(value)
+    return out
+
+
+def trainer_settings_from_yaml(path_or_cfg: Any, overrides: Optional[Dict[str, Any]] = None) -> Dict[str, Any]:
+    """The ``optimizer:``, ``scheduler:``, ``training:`` and ``hardware:`` sections of
+    the nested schema as the trainer's arguments: ``optimizer_kwargs`` for
+    ``MuonAdamWHybrid``, ``scheduler_kwargs`` for ``WSDScheduler`` and the trainer
+    ``config`` keys.  Keys absent from the file are absent from the result."""
+    cfg = load_config(path_or_cfg, overrides) if isinstance(path_or_cfg, str) else path_or_cfg
+    c = _plain(cfg)
+    opt, sch, tr, hw = (c.get(k, {}) or {} for k in ("optimizer", "scheduler", "training", "hardware"))
+    optimizer: Dict[str, Any] = {}
+    scheduler: Dict[str, Any] = {}
+    trainer: Dict[str, Any] = {}
+
+    def put(d: Dict[str, Any], key: str, value: Any, conv=None) -> None:
+        if value is not None:
+            d[key] = conv(value) if conv else value
+
+    put(optimizer, "lr_muon", opt.get("muon_lr"), float)
+    put(optimizer, "lr_adamw", opt.get("adamw_lr"), float)
+    put(optimizer, "momentum", opt.get("muon_momentum"), float)
+    put(optimizer, "betas", opt.get("adamw_betas"), lambda b: tuple(float(x) for x in b))
+    put(optimizer, "weight_decay_adamw", opt.get("weight_decay"), float)
+    put(optimizer, "ns_steps", opt.get("ns_iterations"), int)
+    warm, stable, decay = sch.get("warmup_steps"), sch.get("stable_steps"), sch.get("decay_steps")
+    put(scheduler, "base_lr", opt.get("adamw_lr"), float)
+    put(scheduler, "min_lr", sch.get("min_lr"), float)
+    put(scheduler, "warmup_steps", warm, int)
+    put(scheduler, "decay_steps", decay, int)
+    if warm is not None and stable is not None:
+        scheduler["decay_start"] = int(warm) + int(stable)
+        if decay is not None:
+            scheduler["total_steps"] = int(warm) + int(stable) + int(decay)
+    put(trainer, "batch_size", tr.get("batch_size"), int)
+    put(trainer, "gradient_accumulation_steps", tr.get("gradient_accumulation_steps"), int)
+    put(trainer, "max_steps", tr.get("max_steps"), int)
+    put(trainer, "max_grad_norm", tr.get("gradient_clip"), float)
+    put(trainer, "save_interval", tr.get("checkpoint_interval"), int)
+    put(trainer, "eval_interval", tr.get("eval_interval"), int)
+    put(trainer, "log_interval", tr.get("log_interval"), int)
+    put(trainer, "seq_len", tr.get("seq_len", (c.get("data", {}) or {}).get("max_seq_len")), int)
+    put(trainer, "device", hw.get("device"))
+    put(trainer, "precision", hw.get("precision", tr.get("precision")))
+    return {"optimizer_kwargs": optimizer, "scheduler_kwargs": scheduler, "trainer": trainer}

@@ -4,6 +4,7 @@ named presets."""
 import os
 
 import pytest
+import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -17,3 +18,52 @@ def test_yaml_matches_preset(name, preset):
     got = hlrt_config_from_yaml(os.path.join(ROOT, "genesis", "training", "configs", f"{name}.yaml"))
     want = build_hlrt_config(preset)
     assert got.to_dict() == want.to_dict()
+
+
+_TRAIN_YAML = """
+model:
+  vocab_size: 256
+  max_seq_len: 64
+  tier1: {layers: 2, d_model: 64, heads: 4, d_ff: 128}
+  tier2: {layers: 0, d_model: 64, heads: 4, latent_vectors_per_chunk: 8, chunk_size: 32, max_seq_len: 64,
+          latent_pool_heads: 4}
+  tier3: {layers: 0, d_model: 64, heads: 4, recurrence_steps: 1, max_seq_len: 64}
+optimizer: {muon_lr: 0.01, adamw_lr: 1.0e-3, muon_momentum: 0.9, adamw_betas: [0.9, 0.95], weight_decay: 0.1,
+            ns_iterations: 3}
+scheduler: {warmup_steps: 1, stable_steps: 2, decay_steps: 1, min_lr: 1.0e-5}
+training: {batch_size: 2, gradient_accumulation_steps: 1, max_steps: 3, gradient_clip: 0.5,
+           checkpoint_interval: 100, log_interval: 1, seq_len: 64}
+hardware: {device: cpu, precision: fp32}
+"""
+
+
+def test_trainer_settings_and_dotted_overrides(tmp_path):
+    from olympus.utils.config import hlrt_config_from_yaml, load_config, parse_overrides, trainer_settings_from_yaml
+
+    path = tmp_path / "run.yaml"
+    path.write_text(_TRAIN_YAML)
+    ov = parse_overrides(["model.tier1.layers=1", "optimizer.adamw_betas=[0.8, 0.9]", "training.max_steps=2"])
+    assert ov == {"model.tier1.layers": 1, "optimizer.adamw_betas": [0.8, 0.9], "training.max_steps": 2}
+    cfg = load_config(str(path), ov)
+    assert hlrt_config_from_yaml(cfg).tier1_num_layers == 1
+    s = trainer_settings_from_yaml(cfg)
+    assert s["optimizer_kwargs"] == {"lr_muon": 0.01, "lr_adamw": 1e-3, "momentum": 0.9, "betas": (0.8, 0.9),
+                                     "weight_decay_adamw": 0.1, "ns_steps": 3}
+    assert s["scheduler_kwargs"] == {"base_lr": 1e-3, "min_lr": 1e-5, "warmup_steps": 1, "decay_steps": 1,
+                                     "decay_start": 3, "total_steps": 4}
+    assert s["trainer"]["max_steps"] == 2 and s["trainer"]["max_grad_norm"] == 0.5
+    with pytest.raises(ValueError):
+        parse_overrides(["no_equals_sign"])
+
+
+def test_distributed_trainer_cli_runs_from_yaml(tmp_path):
+    from genesis.training.train_phase1_distributed import main
+
+    path = tmp_path / "run.yaml"
+    path.write_text(_TRAIN_YAML)
+    ck = tmp_path / "ck"
+    main(["--config", str(path), "--set", "model.tier1.layers=1", "--max-steps", "2", "--checkpoint-dir", str(ck)])
+    state = torch.load(ck / "checkpoint_final.pt", weights_only=False)
+    assert state["global_step"] == 2
+    n_blocks = {k.split(".")[2] for k in state["models"]["hlrt"] if k.startswith("tier1.layers.")}
+    assert n_blocks == {"0"}
