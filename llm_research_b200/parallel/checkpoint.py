@@ -66,9 +66,12 @@ def _layout(engine) -> Dict[str, Any]:
 
 
 def save_sharded(engine, optimizer, directory: str, header: Optional[Dict[str, Any]] = None,
-                 asynchronous: bool = True) -> None:
+                 asynchronous: bool = True, rank_extra: Optional[Dict[str, Any]] = None) -> None:
+    """``header``: rank 0's metadata; ``rank_extra``: this rank's own entries (its RNG
+    states, say), returned by :func:`load_sharded` when the world size is unchanged."""
     os.makedirs(directory, exist_ok=True)
     state = _shard_state(engine, optimizer)
+    state["extra"] = dict(rank_extra or {})
     if engine.device.type == "cuda":
         torch.cuda.synchronize(engine.device)  # host copies complete before the writer reads them
     path = os.path.join(directory, f"rank{engine.rank:05d}.pt")
@@ -102,8 +105,10 @@ def _load_rank(directory: str, rank: int) -> Dict[str, Any]:
 @torch.no_grad()
 def load_sharded(engine, optimizer, directory: str) -> Dict[str, Any]:
     meta = torch.load(os.path.join(directory, "layout.pt"), map_location="cpu", weights_only=False)
+    out = dict(meta["header"])
     if meta["layout"]["world"] == engine.world:
         st = _load_rank(directory, engine.rank)
+        out.update(st.get("extra", {}))
         for u, s in zip(engine.units, st["units"]):
             u.master.copy_(s["master"].to(u.master.device))
         for key, bufs in st["optimizer"].items():
@@ -130,7 +135,7 @@ def load_sharded(engine, optimizer, directory: str) -> Dict[str, Any]:
     engine.refresh()
     if dist.is_available() and dist.is_initialized() and engine.world > 1:
         dist.barrier(group=engine.pg)
-    return meta["header"]
+    return out
 
 
 def consolidate(directory: str, model_name: str = "model") -> Dict[str, Any]:

@@ -61,6 +61,39 @@ class ObjectiveConfig:
         return self.enabled_phases is None or phase in self.enabled_phases
 
 
+def rng_state() -> Dict[str, Any]:
+    """Python, NumPy, torch CPU and (when present) this process's CUDA generator
+    states: an extension of the reference's checkpoint, which saves none, so a
+    resumed run draws the same dropout masks, jitter and samples as an
+    uninterrupted one.  Readers of the reference ignore the extra key.  Only
+    tensors, numbers and strings, so ``weights_only`` loaders accept it."""
+    import random
+
+    import numpy as np
+
+    kind, keys, pos, has_gauss, gauss = np.random.get_state()
+    out: Dict[str, Any] = {"python": random.getstate(),
+                           "numpy": (kind, torch.from_numpy(keys.astype(np.int64)), int(pos), int(has_gauss),
+                                     float(gauss)),
+                           "torch": torch.get_rng_state()}
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        out["cuda"] = torch.cuda.get_rng_state()
+    return out
+
+
+def set_rng_state(state: Dict[str, Any]) -> None:
+    import random
+
+    import numpy as np
+
+    random.setstate(state["python"])
+    kind, keys, pos, has_gauss, gauss = state["numpy"]
+    np.random.set_state((kind, np.asarray(keys, dtype=np.int64).astype(np.uint32), pos, has_gauss, gauss))
+    torch.set_rng_state(state["torch"].cpu())
+    if "cuda" in state and torch.cuda.is_available():
+        torch.cuda.set_rng_state(state["cuda"].cpu())
+
+
 def model_state_for_checkpoint(model: nn.Module) -> Dict[str, Any]:
     if isinstance(model, StatefulModule):
         return model.state_dict_with_state()
@@ -216,6 +249,7 @@ class TrainingOrchestrator:
             "models": {},
             "optimizers": {},
             "schedulers": {},
+            "rng_state": rng_state(),
         }
 
     def save_checkpoint(self, path: str) -> None:
@@ -235,6 +269,11 @@ class TrainingOrchestrator:
         self._phase = ckpt["phase"]
         self._prev_loss = ckpt["prev_loss"]
         self.memory_bus.load_state_dict(ckpt["memory_bus"])
+        self._restore_rng(ckpt)
+
+    def _restore_rng(self, ckpt: Dict[str, Any]) -> None:
+        if "rng_state" in ckpt:  # absent in the reference's checkpoints
+            set_rng_state(ckpt["rng_state"])
 
     def load_checkpoint(self, path: str, strict: bool = True) -> Dict[str, Any]:
         ckpt = torch.load(path, map_location=self.device, weights_only=False)

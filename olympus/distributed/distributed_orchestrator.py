@@ -32,7 +32,8 @@ import torch.nn as nn
 
 from olympus.core.memory_bus import MemoryBus
 from olympus.core.stateful_module import StatefulModule
-from olympus.core.training_orchestrator import ModelConfig, ObjectiveConfig, TrainingOrchestrator, load_model_state
+from olympus.core.training_orchestrator import (ModelConfig, ObjectiveConfig, TrainingOrchestrator, load_model_state,
+                                               rng_state, set_rng_state)
 from olympus.distributed.fsdp_wrapper import FSDPConfig, wrap_model_fsdp
 
 logger = logging.getLogger(__name__)
@@ -112,6 +113,10 @@ class DistributedTrainingOrchestrator(TrainingOrchestrator):
             os.makedirs(os.path.dirname(path) or ".", exist_ok=True)
         ckpt = self._checkpoint_dict()
         ckpt["world_size"] = self.world_size
+        if dist.is_initialized():  # every rank's generators, restored rank by rank
+            states: list = [None] * dist.get_world_size()
+            dist.all_gather_object(states, ckpt["rng_state"])
+            ckpt["rng_state"] = states
         for name, cfg in self._models.items():
             if _is_engine(cfg.model):
                 state: Dict[str, Any] = dict(cfg.model.full_state_dict())
@@ -130,6 +135,15 @@ class DistributedTrainingOrchestrator(TrainingOrchestrator):
         if dist.is_initialized():
             dist.barrier()
 
+    def _restore_rng(self, ckpt: Dict[str, Any]) -> None:
+        state = ckpt.get("rng_state")
+        world = dist.get_world_size() if dist.is_initialized() else 1
+        if isinstance(state, list):  # one entry per rank of the saving job
+            if len(state) == world:
+                set_rng_state(state[dist.get_rank() if dist.is_initialized() else 0])
+        elif state is not None and world == 1:
+            set_rng_state(state)
+
     def save_sharded_checkpoint(self, directory: str, asynchronous: bool = True) -> None:
         """Every rank writes its own parameter and optimizer shards (``{directory}/{model}/rank*.pt``)
         from a background thread; rank 0 writes ``header.pt`` (step, phase, memory bus, schedulers,
@@ -144,7 +158,8 @@ class DistributedTrainingOrchestrator(TrainingOrchestrator):
         for name, cfg in self._models.items():
             if _is_engine(cfg.model):
                 ck.save_sharded(cfg.model, cfg.optimizer, os.path.join(directory, name),
-                                header={"buffers": _engine_extra_state(cfg.model)}, asynchronous=asynchronous)
+                                header={"buffers": _engine_extra_state(cfg.model)}, asynchronous=asynchronous,
+                                rank_extra={"rng_state": rng_state()})
                 head["sharded"].append(name)
             else:
                 head["models"][name] = (cfg.model.state_dict_with_state() if isinstance(cfg.model, StatefulModule)
@@ -169,6 +184,8 @@ class DistributedTrainingOrchestrator(TrainingOrchestrator):
         for name, cfg in self._models.items():
             if name in head["sharded"]:
                 sub = ck.load_sharded(cfg.model, cfg.optimizer, os.path.join(directory, name))
+                if "rng_state" in sub:  # this rank's generators (same world size only)
+                    set_rng_state(sub["rng_state"])
                 extras = {k: v for k, v in sub.get("buffers", {}).items() if k.startswith("_olympus_")}
                 inner = cfg.model.module
                 if isinstance(inner, StatefulModule) and extras:

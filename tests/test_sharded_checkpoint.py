@@ -96,3 +96,28 @@ def test_orchestrator_sharded_resume_and_consolidation(tmp_path):
     out = str(tmp_path / "full.pt")
     main([d, out])
     assert torch.load(out, weights_only=False)["phase"] == full["phase"]
+
+
+def test_checkpoint_restores_rng_streams(tmp_path):
+    """A resumed run draws the same random numbers as an uninterrupted one
+    (Python, NumPy and torch generators are saved with the checkpoint)."""
+    import random
+
+    import numpy as np
+    import torch.nn as nn
+
+    from olympus.core.training_orchestrator import ModelConfig, TrainingOrchestrator
+
+    torch.manual_seed(0)
+    model = nn.Linear(4, 4)
+    orch = TrainingOrchestrator(device="cpu")
+    orch.add_model(ModelConfig(name="m", model=model, optimizer=torch.optim.SGD(model.parameters(), lr=0.1)))
+    random.seed(1), np.random.seed(2), torch.manual_seed(3)
+    path = str(tmp_path / "c.pt")
+    orch.save_checkpoint(path)
+    expect = (random.random(), float(np.random.rand()), torch.rand(3))
+    random.seed(9), np.random.seed(9), torch.manual_seed(9)
+    orch.load_checkpoint(path)
+    got = (random.random(), float(np.random.rand()), torch.rand(3))
+    assert got[0] == expect[0] and got[1] == expect[1] and torch.equal(got[2], expect[2])
+    torch.load(path, weights_only=True)  # plain tensors, numbers and strings only
