@@ -192,8 +192,9 @@ def test_hlrt_tensor_parallel_tier1_fused_kernels(labels):
             assert rel < 5e-2, (name, rel)
 
 
-def _fsdp_tp_train(rank, world):
-    """FSDP x2 (dp) + TP x2 on 4 gloo ranks, Muon hybrid + clipping, two steps."""
+def _fsdp_tp_train(rank, world, fused_loss=False):
+    """FSDP x2 (dp) + TP x2 on 4 gloo ranks, Muon hybrid + clipping, two steps;
+    ``fused_loss``: the head + loss run vocabulary-parallel over the TP group."""
     import torch.distributed as dist
 
     from genesis.training.train_phase1_bootstrap import ntp_objective
@@ -225,16 +226,17 @@ def _fsdp_tp_train(rank, world):
     data = _data()
     d = rank // tp
     for _ in range(2):
-        orch.step({"input_ids": data[2 * d: 2 * d + 2]})
+        orch.step({"input_ids": data[2 * d: 2 * d + 2], "fused_lm_loss": fused_loss})
     sd = orch._models["hlrt"].model.full_state_dict()
     return {k: (v, getattr(dict(model.named_parameters())[k], "_lrb_tp", None)) for k, v in sd.items()}
 
 
-def test_fsdp_plus_tensor_parallel_matches_single_process():
+@pytest.mark.parametrize("fused_loss", [False, True])
+def test_fsdp_plus_tensor_parallel_matches_single_process(fused_loss):
     from tests.test_engine import _data, _toy_model, _train
 
     single, _ = _train(_toy_model(), [_data()], engine=False, steps=2)
-    res = run_ranks(_fsdp_tp_train, 4)
+    res = run_ranks(_fsdp_tp_train, 4, fused_loss)
     for rank, sd in enumerate(res):
         for k, (v, dim) in sd.items():
             ref = single[k] if dim is None else single[k].chunk(2, dim=dim)[rank % 2]
