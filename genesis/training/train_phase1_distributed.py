@@ -42,11 +42,20 @@ from olympus.optim.schedulers import WSDScheduler
 logger = logging.getLogger(__name__)
 
 
-def init_distributed(timeout_s: float = 600.0) -> tuple[int, int, int]:
+def init_distributed(timeout_s: Optional[float] = None) -> tuple[int, int, int]:
+    """Process group from the launcher's environment.  Collectives that do not
+    finish within ``timeout_s`` (default ``LRB_PG_TIMEOUT_S`` or 600 s) are
+    failed by NCCL's watchdog, and with asynchronous error handling on (the
+    default set here unless the caller set ``TORCH_NCCL_ASYNC_ERROR_HANDLING``)
+    the rank aborts its communicators and exits instead of hanging, so the
+    launcher sees the failure."""
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     rank = int(os.environ.get("RANK", 0))
+    if timeout_s is None:
+        timeout_s = float(os.environ.get("LRB_PG_TIMEOUT_S", 600.0))
     if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
         if torch.cuda.is_available():
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s),
@@ -69,7 +78,7 @@ class DistributedBootstrapTrainer:
         fsdp_config: Optional[FSDPConfig] = None,
     ) -> None:
         config = dict(config or {})
-        self.local_rank, self.world_size, self.global_rank = init_distributed(config.get("dist_timeout_s", 600.0))
+        self.local_rank, self.world_size, self.global_rank = init_distributed(config.get("dist_timeout_s"))
         self.is_distributed = self.world_size > 1
         if torch.cuda.is_available() and config.get("device", "cuda") != "cpu":
             self.device = torch.device(f"cuda:{self.local_rank}")

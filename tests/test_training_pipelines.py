@@ -230,3 +230,31 @@ def test_actv_co_training_and_distillation():
     m2 = tr.co_training_step({"input_ids": ids, "labels": ids})
     assert m2["v_replay_loss"] > 0 and "distillation_loss" in m2
     assert m2["g_ntp_loss"] > 0 and 0 <= m2["g_v_scores"]["overall_score"] <= 1
+
+
+def test_init_distributed_sets_async_error_handling_and_timeout(monkeypatch):
+    """Two gloo ranks come up through the trainer's initialiser with the
+    watchdog's error handling switched on and the timeout from the environment."""
+    from tests.dist_utils import run_ranks
+
+    monkeypatch.delenv("TORCH_NCCL_ASYNC_ERROR_HANDLING", raising=False)
+    monkeypatch.setenv("LRB_PG_TIMEOUT_S", "45")
+    for res in run_ranks(_init_case, 2):
+        assert res == ("1", 45.0)
+
+
+def _init_case(rank, world):
+    import os
+
+    import torch.distributed as dist
+
+    from genesis.training.train_phase1_distributed import init_distributed
+
+    dist.destroy_process_group()  # the harness initialised one; the trainer's initialiser makes its own
+    os.environ.pop("TORCH_NCCL_ASYNC_ERROR_HANDLING", None)
+    init_distributed()
+    import torch
+    from torch.distributed.distributed_c10d import _get_default_group
+
+    backend = _get_default_group()._get_backend(torch.device("cpu"))
+    return os.environ["TORCH_NCCL_ASYNC_ERROR_HANDLING"], backend.options._timeout.total_seconds()
