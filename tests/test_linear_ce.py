@@ -96,3 +96,14 @@ def _vocab_ce_gpu_case(rank, world):
         loss.backward()
         out[name] = (loss.detach().cpu(), a.grad.cpu(), b.grad.cpu())
     return out
+
+
+@pytest.mark.gpu
+def test_vocab_parallel_linear_cross_entropy_one_rank_gpu():
+    """The GPU path of the vocabulary-parallel op (NCCL collectives, shard kernel)
+    on a one-rank group equals the plain chunked op."""
+    from tests.dist_utils import run_ranks
+
+    for res in run_ranks(_vocab_ce_gpu_case, 1, backend="nccl"):
+        for r, got in zip(res["full"], res["vp"]):
+            torch.testing.assert_close(got.float(), r.float(), atol=2e-2, rtol=2e-2)
