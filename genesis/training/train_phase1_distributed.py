@@ -92,6 +92,8 @@ class DistributedBootstrapTrainer:
         optimizer = optimizer_cls(model.parameters(), **(optimizer_kwargs or {}))
         scheduler = scheduler_cls(optimizer, **(scheduler_kwargs or {}))
         self.tokenizer = tokenizer or TokenizerWrapper(backend="tiktoken")
+        self.sampler = None  # set by make_dataloader
+        self._resume_position = None
         self.orchestrator = DistributedTrainingOrchestrator(
             fsdp_config=fsdp_config if (self.is_distributed or explicit) else None,
             local_rank=self.local_rank, world_size=self.world_size,
@@ -135,6 +137,8 @@ class DistributedBootstrapTrainer:
         start = time.time()
         for batch in dataloader:
             m = self.train_step(batch)
+            if self.sampler is not None and getattr(dataloader, "sampler", None) is self.sampler:
+                self.sampler.advance(batch["input_ids"].shape[0])
             loss = float(m["loss"])
             tot += loss
             tps += m["tokens_per_sec"]
@@ -154,16 +158,37 @@ class DistributedBootstrapTrainer:
                 "avg_tokens_per_sec": tps / max(steps, 1), "total_steps": steps}
 
     def save_checkpoint(self, path: str) -> None:
+        if self.sampler is not None:  # extension: where in the epoch each rank stands
+            states = [self.sampler.state_dict()]
+            if self.is_distributed:
+                states = [None] * self.world_size
+                dist.all_gather_object(states, self.sampler.state_dict())
+            self.orchestrator.extra_state["data_position"] = states
         self.orchestrator.save_checkpoint(path)
 
     def load_checkpoint(self, path: str) -> None:
-        self.orchestrator.load_checkpoint(path)
+        ckpt = self.orchestrator.load_checkpoint(path)
+        self._resume_position = ckpt.get("data_position") if isinstance(ckpt, dict) else None
+        if self.sampler is not None:
+            self._apply_resume_position()
+
+    def _apply_resume_position(self) -> None:
+        pos = self._resume_position
+        if pos and len(pos) == self.world_size:
+            self.sampler.load_state_dict(pos[self.global_rank if self.is_distributed else 0])
+        self._resume_position = None
 
     def make_dataloader(self, dataset, batch_size: int = 32, num_workers: int = 4) -> DataLoader:
-        sampler = DistributedSampler(dataset, num_replicas=self.world_size, rank=self.global_rank, shuffle=True) \
-            if self.is_distributed else None
-        return DataLoader(dataset, batch_size=batch_size, shuffle=sampler is None, sampler=sampler,
-                          num_workers=num_workers, pin_memory=self.device.type == "cuda", drop_last=True)
+        """Shuffled, split over the ranks, and resumable mid-epoch
+        (:class:`olympus.data.resumable_sampler.ResumableDistributedSampler`)."""
+        from olympus.data.resumable_sampler import ResumableDistributedSampler
+
+        self.sampler = ResumableDistributedSampler(len(dataset), num_replicas=self.world_size if self.is_distributed else 1,
+                                                   rank=self.global_rank if self.is_distributed else 0, shuffle=True)
+        if self._resume_position is not None:
+            self._apply_resume_position()
+        return DataLoader(dataset, batch_size=batch_size, sampler=self.sampler, num_workers=num_workers,
+                          pin_memory=self.device.type == "cuda", drop_last=True)
 
 
 def main(argv=None) -> None:
@@ -243,9 +268,9 @@ def main(argv=None) -> None:
 
         ds = SyntheticTokenDataset(max(run["batch_size"] * trainer.world_size * 64, 64), run["seq_len"], cfg.vocab_size)
     loader = trainer.make_dataloader(ds, batch_size=run["batch_size"], num_workers=2)
-    epoch = 0
+    epoch = trainer.sampler.epoch  # the resumed epoch, 0 on a fresh start
     while trainer.orchestrator.global_step < run["max_steps"]:
-        if isinstance(loader.sampler, DistributedSampler):
+        if hasattr(loader.sampler, "set_epoch"):
             loader.sampler.set_epoch(epoch)
         trainer.orchestrator.set_epoch(epoch)
         trainer.train_epoch(loader)

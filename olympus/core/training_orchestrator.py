@@ -127,6 +127,8 @@ class TrainingOrchestrator:
         self._phase = "bootstrap"
         self._global_step = 0
         self._epoch = 0
+        # further top-level checkpoint entries set by the trainer (its data position, say)
+        self.extra_state: Dict[str, Any] = {}
         self._prev_loss: Any = float("inf")
         self._accumulation_step = 0
 
@@ -250,6 +252,7 @@ class TrainingOrchestrator:
             "optimizers": {},
             "schedulers": {},
             "rng_state": rng_state(),
+            **self.extra_state,
         }
 
     def save_checkpoint(self, path: str) -> None:

@@ -67,3 +67,47 @@ def test_distributed_trainer_cli_runs_from_yaml(tmp_path):
     assert state["global_step"] == 2
     n_blocks = {k.split(".")[2] for k in state["models"]["hlrt"] if k.startswith("tier1.layers.")}
     assert n_blocks == {"0"}
+
+
+def test_resumable_sampler_continues_mid_epoch():
+    from olympus.data.resumable_sampler import ResumableDistributedSampler
+
+    full = [list(ResumableDistributedSampler(50, 2, r, seed=3)) for r in range(2)]
+    assert sorted(full[0] + full[1]) == sorted(set(full[0] + full[1])) and len(full[0]) == 25
+    s = ResumableDistributedSampler(50, 2, 1, seed=3)
+    s.advance(6)
+    t = ResumableDistributedSampler(50, 2, 1, seed=3)
+    t.load_state_dict(s.state_dict())
+    assert list(t) == full[1][6:] and len(t) == 19
+    t.set_epoch(1)
+    assert len(t) == 25 and list(t) != full[1]
+
+
+def test_trainer_resume_sees_the_remaining_samples(tmp_path):
+    """Stop after 3 steps of an epoch, resume from the checkpoint: the resumed
+    trainer's loader yields exactly the batches an uninterrupted run had left."""
+    from genesis.model.hlrt import HLRT
+    from genesis.training.train_phase1_distributed import DistributedBootstrapTrainer
+    from llm_research_b200.models.presets import build_hlrt_config
+    from olympus.data.packed_dataset import SyntheticTokenDataset
+
+    cfg = build_hlrt_config("toy")
+    ds = SyntheticTokenDataset(16, 32, cfg.vocab_size)
+
+    def trainer():
+        torch.manual_seed(0)
+        return DistributedBootstrapTrainer(HLRT(cfg), config={"log_interval": 100, "save_interval": 0,
+                                                              "gradient_accumulation_steps": 1,
+                                                              "max_steps": 3, "checkpoint_dir": str(tmp_path)})
+
+    a = trainer()
+    loader = a.make_dataloader(ds, batch_size=2, num_workers=0)
+    expect = [b["input_ids"].clone() for b in loader]
+    a.train_epoch(loader)  # stops after 3 steps
+    a.save_checkpoint(str(tmp_path / "c.pt"))
+    b = trainer()
+    b.load_checkpoint(str(tmp_path / "c.pt"))
+    rest = [x["input_ids"] for x in b.make_dataloader(ds, batch_size=2, num_workers=0)]
+    assert len(rest) == len(expect) - 3
+    for x, y in zip(rest, expect[3:]):
+        assert torch.equal(x, y)
