@@ -111,3 +111,38 @@ def test_trainer_resume_sees_the_remaining_samples(tmp_path):
     assert len(rest) == len(expect) - 3
     for x, y in zip(rest, expect[3:]):
         assert torch.equal(x, y)
+
+
+def _resume_case(rank, world, d):
+    from genesis.model.hlrt import HLRT
+    from genesis.training.train_phase1_distributed import DistributedBootstrapTrainer
+    from llm_research_b200.models.presets import build_hlrt_config
+    from olympus.data.packed_dataset import SyntheticTokenDataset
+
+    cfg = build_hlrt_config("toy")
+    ds = SyntheticTokenDataset(16, 32, cfg.vocab_size)
+
+    def trainer():
+        torch.manual_seed(0)
+        return DistributedBootstrapTrainer(HLRT(cfg), config={"log_interval": 100, "save_interval": 0, "max_steps": 2,
+                                                              "gradient_accumulation_steps": 1, "checkpoint_dir": d})
+
+    a = trainer()
+    loader = a.make_dataloader(ds, batch_size=2, num_workers=0)
+    expect = [b["input_ids"].clone() for b in loader]
+    a.train_epoch(loader)
+    a.save_checkpoint(os.path.join(d, "c.pt"))
+    b = trainer()
+    b.load_checkpoint(os.path.join(d, "c.pt"))
+    rest = [x["input_ids"] for x in b.make_dataloader(ds, batch_size=2, num_workers=0)]
+    return expect, rest
+
+
+def test_trainer_resume_mid_epoch_two_ranks(tmp_path):
+    from tests.dist_utils import run_ranks
+
+    res = run_ranks(_resume_case, 2, str(tmp_path))
+    for expect, rest in res:
+        assert len(expect) == 4 and len(rest) == 2
+        assert all(torch.equal(x, y) for x, y in zip(rest, expect[2:]))
+    assert not torch.equal(res[0][0][0], res[1][0][0])  # the ranks read different samples
