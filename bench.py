@@ -46,6 +46,105 @@ MODEL_NAMES = {
 }
 
 
+# HLRTConfig fields of the benchmarked model for the reference arm, written out
+# here so that the reference process imports nothing from this repository.  The
+# 24-layer dense trunk is Tier 1; tiers 2 and 3 carry no transformer layers.
+REFERENCE_FIELDS = {
+    "genesis-1b": dict(
+        vocab_size=32000, d_model=2048,
+        tier1_num_layers=24, tier1_num_heads=16, tier1_num_kv_heads=None, tier1_d_ff=5632, tier1_max_seq_len=4096,
+        gate1_chunk_size=32, num_latent_vectors=8, latent_pool_num_heads=16,
+        tier2_d_model=2048, tier2_num_layers=0, tier2_num_heads=16, tier2_max_seq_len=1024,
+        tier3_d_model=2048, tier3_num_layers=0, tier3_num_heads=16, tier3_max_seq_len=1024,
+        tier3_recurrence_steps=1,
+    ),
+}
+
+
+_REASON_BITS = {
+    "applications_clocks_setting": 0x2,
+    "sw_power_cap": 0x4,
+    "hw_slowdown": 0x8,
+    "sync_boost": 0x10,
+    "sw_thermal_slowdown": 0x20,
+    "hw_thermal_slowdown": 0x40,
+    "hw_power_brake_slowdown": 0x80,
+    "display_clock_setting": 0x100,
+}
+
+
+class ClockSampler:
+    """Read-only NVML sampling of SM clock, power and active clock-event reasons
+    every ``period_s`` while the timed region runs (nothing is ever set).
+
+    Defined here rather than imported so that the reference arm loads no module
+    of this repository."""
+
+    def __init__(self, device_index: int = 0, period_s: float = 0.2) -> None:
+        import threading
+
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._ok = False
+        try:
+            import pynvml  # nvidia_ml_py
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+            self._ok = True
+        except Exception:
+            self._ok = False
+
+    def _run(self) -> None:
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                util = nv.nvmlDeviceGetUtilizationRates(self._h).gpu
+                self.samples.append({"sm_mhz": float(sm), "power_w": pw, "util": float(util)})
+                for name, bit in _REASON_BITS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        import threading
+
+        if self._ok:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2.0)
+
+    def summary(self) -> dict:
+        import statistics
+
+        if not self._ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml_unavailable"]}
+        loaded = [x["sm_mhz"] for x in self.samples if x["util"] > 50] or [x["sm_mhz"] for x in self.samples]
+        return {
+            "sm_mhz": statistics.median(loaded) if loaded else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+            "power_w_max": max((x["power_w"] for x in self.samples), default=None),
+        }
+
+
 def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -57,7 +156,10 @@ def parse_args(argv=None):
     ap.add_argument("--per-gpu-seqs", type=int, default=32)
     ap.add_argument("--micro-batch", type=int, default=8)
     ap.add_argument("--ref-micro-batch", type=int, default=0,
-                    help="reference micro-batch; 0 = the largest of 8/4/2/1 that fits (1 GPU), 4 on several GPUs")
+                    help="reference micro-batch; 0 = 2 (the largest that fits its fp32 O(S^2) attention on one "
+                         "B200 at seq 4096), then 1 if that runs out of memory on one GPU")
+    ap.add_argument("--ref-e2e-steps", type=int, default=3,
+                    help="end-to-end steps of the reference arm (its step takes tens of seconds)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--precision", choices=["bf16", "nvfp4"], default="bf16",
                     help="linear-layer precision of the model (nvfp4: block-scaled FP4 training GEMMs)")
@@ -111,7 +213,6 @@ def run_ours(args) -> dict:
     from genesis.model.hlrt import HLRT
     from genesis.training.train_phase1_distributed import DistributedBootstrapTrainer, init_distributed
     from llm_research_b200.models.presets import build_hlrt_config, count_flops_per_token
-    from llm_research_b200.utils.clocks import ClockSampler
     from olympus.data.tokenizer import TokenizerWrapper
     from olympus.distributed.fsdp_wrapper import FSDPConfig
 
@@ -170,10 +271,14 @@ def run_ours(args) -> dict:
         fsdp_config=FSDPConfig(sharding_strategy="FULL_SHARD", mixed_precision="bf16", activation_checkpointing=False,
                                process_group=dp_group, tp_group=tp_group),
     )
-    # Ranks of one tensor-parallel group train on the same sequences.
+    # A distinct batch for every step (warm-up, device-timed and end-to-end
+    # phases draw from one pool in order), so the loss is a real cross-N check
+    # rather than memorisation of one batch.  Ranks of one tensor-parallel group
+    # train on the same sequences.
     g = torch.Generator().manual_seed(args.seed * 1000 + dp_rank)
-    host = torch.randint(0, cfg.vocab_size, (accum, micro, S), generator=g, dtype=torch.int64).pin_memory()
-    dev_batches = [host[i].to(device) for i in range(accum)]
+    n_pool = args.warmup + args.steps
+    host = torch.randint(0, cfg.vocab_size, (n_pool, accum, micro, S), generator=g, dtype=torch.int64).pin_memory()
+    dev_pool = host.to(device)
 
     def step(batches):
         out = None
@@ -181,8 +286,8 @@ def run_ours(args) -> dict:
             out = trainer.train_step({"input_ids": b, "fused_lm_loss": args.fused_loss})
         return out["loss"]
 
-    for _ in range(args.warmup):
-        step(dev_batches)
+    for i in range(args.warmup):
+        step(dev_pool[i])
     _barrier_sync(dist, torch)
 
     sampler = ClockSampler(device_index=local_rank)
@@ -190,34 +295,35 @@ def run_ours(args) -> dict:
     with sampler:
         _barrier_sync(dist, torch)
         e0.record()
-        for _ in range(args.steps):
-            loss = step(dev_batches)
+        for i in range(args.steps):
+            loss = step(dev_pool[args.warmup + i])
         e1.record()
         _barrier_sync(dist, torch)
     dev_ms = _max_over_ranks(e0.elapsed_time(e1), dist, device)
     final_loss = float(loss)
+    del dev_pool
 
     e2e = None
     if not args.no_e2e:
-        host_batches = [host[i] for i in range(accum)]
         _barrier_sync(dist, torch)
         t0 = time.perf_counter()
-        for _ in range(args.steps):
-            l = step(host_batches)
+        for i in range(args.steps):
+            # pinned host batch, copied host -> device inside the step
+            l = step(host[(args.warmup + i) % n_pool])
             lv = float(l)  # device -> host read of the step's result
         _barrier_sync(dist, torch)
         e2e_s = _max_over_ranks(time.perf_counter() - t0, dist, device)
         e2e = {
-            "value": world * accum * micro * S * args.steps / e2e_s,
+            "value": dp_world * accum * micro * S * args.steps / e2e_s,
             "unit": "tokens/s",
-            "h2d_bytes_per_step": int(host[0].numel() * host.element_size() * accum),
+            "h2d_bytes_per_step": int(host[0].numel() * host.element_size()),
             "d2h_bytes_per_step": 4,
             "ms_per_step": e2e_s * 1000.0 / args.steps,
         }
 
     launches = None
     if args.count_launches:
-        per_step = _count_kernels(lambda: step(dev_batches))
+        per_step = _count_kernels(lambda: step(host[0].to(device)))
         launches = per_step * args.steps
 
     # Exposed communication: one extra (untimed) step with the compute stream's
@@ -227,7 +333,7 @@ def run_ours(args) -> dict:
     if world > 1 and hasattr(engine, "start_exposed_comm_measurement"):
         _barrier_sync(dist, torch)
         engine.start_exposed_comm_measurement()
-        step(dev_batches)
+        step(host[1 % n_pool].to(device))
         exposed = _max_over_ranks(engine.stop_exposed_comm_measurement(), dist, device)
 
     tokens_per_step = dp_world * accum * micro * S
@@ -299,13 +405,9 @@ def run_reference(args) -> dict:
     from olympus.optim.schedulers import WSDScheduler
 
     assert os.path.abspath(genesis.__file__).startswith(ref), genesis.__file__
-    sys.path.insert(0, REPO)
-    from llm_research_b200.models.presets import build_hlrt_config  # only for the field values
-    from llm_research_b200.utils.clocks import ClockSampler
-    sys.path.pop(0)
-
-    ours = build_hlrt_config(args.preset)
-    fields = {k: getattr(ours, k) for k in HLRTConfig.__dataclass_fields__ if hasattr(ours, k)}
+    if args.preset not in REFERENCE_FIELDS:
+        return {"impl": "reference", "unavailable": f"no reference configuration for preset {args.preset}"}
+    fields = dict(REFERENCE_FIELDS[args.preset])
     # The reference runs only in fp32: in bf16 its latent pooling multiplies by a
     # float mask (genesis/model/latent_pooling.py:171) and the tier-2 linear then
     # fails on mixed dtypes, and the installed flash-attn rejects fp32, so its
@@ -328,9 +430,10 @@ def run_reference(args) -> dict:
     if args.ref_micro_batch > 0:
         candidates = [args.ref_micro_batch]
     else:
-        # one GPU: the largest that fits (2 on B200); several: 2 directly, since a
-        # probe that runs out of memory on one rank would leave the others in a collective
-        candidates = [8, 4, 2, 1] if world == 1 else [2]
+        # 2 fits on a B200 (4 and 8 run out of memory); on several GPUs no fallback,
+        # since a probe that runs out of memory on one rank would leave the others
+        # in a collective
+        candidates = [2, 1] if world == 1 else [2]
 
     def build(micro):
         torch.manual_seed(args.seed)
@@ -395,16 +498,17 @@ def run_reference(args) -> dict:
     dev_ms = _max_over_ranks(e0.elapsed_time(e1), dist, device)
     e2e = None
     if not args.no_e2e:
+        n_e2e = max(1, min(args.steps, args.ref_e2e_steps))
         host_batches = [host[i] for i in range(accum)]
         _barrier_sync(dist, torch)
         t0 = time.perf_counter()
-        for _ in range(args.steps):
+        for _ in range(n_e2e):
             lv = float(step(host_batches))
         _barrier_sync(dist, torch)
         e2e_s = _max_over_ranks(time.perf_counter() - t0, dist, device)
-        e2e = {"value": world * accum * micro * S * args.steps / e2e_s, "unit": "tokens/s",
+        e2e = {"value": world * accum * micro * S * n_e2e / e2e_s, "unit": "tokens/s",
                "h2d_bytes_per_step": int(host.numel() * host.element_size()), "d2h_bytes_per_step": 4 * accum,
-               "ms_per_step": e2e_s * 1000.0 / args.steps}
+               "ms_per_step": e2e_s * 1000.0 / n_e2e, "steps": n_e2e}
     tokens_per_step = world * accum * micro * S
     res = {
         "metric": METRIC,

@@ -125,6 +125,8 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   float* acc = sh + (size_t)wid * d;
   for (int c = lane; c < d; c += 32) acc[c] = 0.f;
+  // The vectorised loop below updates acc[8 * lane + j], elements another lane zeroed.
+  __syncwarp();
   const bool vec = (d % 256) == 0;
   for (int64_t row = (int64_t)blockIdx.x * kWarps + wid; row < rows; row += (int64_t)gridDim.x * kWarps) {
     const float r = rstd[row];
@@ -194,6 +196,28 @@ __global__ void reduce_rows_kernel(const float* __restrict__ part, float* __rest
   out[c] = s;
 }
 
+// Dynamic shared memory of rmsnorm_bwd_kernel: kWarps rows x d fp32 accumulators,
+// at most 200 KiB (d <= 6400).
+constexpr int kBwdSmemMax = 200 * 1024;
+
+// Raises the kernel's dynamic shared-memory limit to kBwdSmemMax once per
+// device and never lowers it, so callers with different row widths on several
+// host threads cannot undo each other's setting between set and launch (a
+// larger limit does not change occupancy: that follows the launch's own size).
+template <typename T, typename W, typename O>
+cudaError_t raise_bwd_smem_limit(int dev) {
+  static std::atomic<bool> done[64];
+  static std::mutex mu;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev].load(std::memory_order_relaxed)) return cudaSuccess;
+  const cudaError_t e =
+      cudaFuncSetAttribute(rmsnorm_bwd_kernel<T, W, O>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmemMax);
+  if (e == cudaSuccess) done[dev].store(true, std::memory_order_release);
+  return e;
+}
+
 template <typename T, typename W, typename O>
 void launch_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& res, at::Tensor& s, const at::Tensor& w,
                 at::Tensor& y, at::Tensor& rstd, int64_t rows, int d, float eps) {
@@ -259,7 +283,7 @@ std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::T
   auto dw = at::zeros({d}, x.options().dtype(at::kFloat));
   if (rows == 0) return {dx, dw};
   const size_t smem = (size_t)kWarps * d * sizeof(float);
-  LRB_CHECK(smem <= 200 * 1024, "rmsnorm_bwd: row too wide");
+  LRB_CHECK(smem <= (size_t)kBwdSmemMax, "rmsnorm_bwd: row too wide");
   int blocks = (int)std::min<int64_t>((rows + kWarps - 1) / kWarps, 2 * num_sms());
   auto part = at::empty({blocks, d}, x.options().dtype(at::kFloat));
   auto st = stream();
@@ -268,7 +292,7 @@ std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::T
     using W = decltype(tag_w);
     using O = decltype(tag_o);
     auto k = rmsnorm_bwd_kernel<T, W, O>;
-    if (smem > 48 * 1024) LRB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (smem > 48 * 1024) LRB_CUDA_CHECK((raise_bwd_smem_limit<T, W, O>(x.get_device())));
     k<<<blocks, kWarps * 32, smem, st>>>(
         reinterpret_cast<const O*>(dy.data_ptr()), reinterpret_cast<const T*>(x.data_ptr()),
         reinterpret_cast<const W*>(w.data_ptr()), rstd.data_ptr<float>(),
@@ -369,8 +393,9 @@ extern "C" __attribute__((visibility("default"))) int lrb_rmsnorm_bwd_bf16_noall
   blocks = std::min<int64_t>(blocks, g_noalloc_blocks_cap[dev]);
   blocks = std::min<int64_t>(blocks, LRB_RMSNORM_BWD_NOALLOC_SCRATCH_FLOATS / d);
   if (smem > 48 * 1024) {
-    // Set on every call: rmsnorm_bwd sets the same attribute for its own sizes.
-    e = cudaFuncSetAttribute(lrb::rmsnorm_bwd_kernel<T, T, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // Raised once per device to the kernel's maximum and never lowered (shared
+    // with rmsnorm_bwd, which launches the same kernel instance).
+    e = lrb::raise_bwd_smem_limit<T, T, T>(dev);
     if (e != cudaSuccess)
       return noalloc_fail(errbuf, errbuf_len, LRB_NOALLOC_ERR_CUDA, "rmsnorm_bwd_noalloc: smem attribute: %s",
                           cudaGetErrorString(e));

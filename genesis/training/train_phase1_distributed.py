@@ -183,7 +183,11 @@ class DistributedBootstrapTrainer:
         (:class:`olympus.data.resumable_sampler.ResumableDistributedSampler`)."""
         from olympus.data.resumable_sampler import ResumableDistributedSampler
 
-        self.sampler = ResumableDistributedSampler(len(dataset), num_replicas=self.world_size if self.is_distributed else 1,
+        replicas = self.world_size if self.is_distributed else 1
+        if len(dataset) // replicas < batch_size:
+            raise ValueError(f"dataset of {len(dataset)} samples gives each of {replicas} rank(s) fewer than one "
+                             f"batch of {batch_size} (drop_last=True): no training step would run")
+        self.sampler = ResumableDistributedSampler(len(dataset), num_replicas=replicas,
                                                    rank=self.global_rank if self.is_distributed else 0, shuffle=True)
         if self._resume_position is not None:
             self._apply_resume_position()
@@ -269,12 +273,18 @@ def main(argv=None) -> None:
         ds = SyntheticTokenDataset(max(run["batch_size"] * trainer.world_size * 64, 64), run["seq_len"], cfg.vocab_size)
     loader = trainer.make_dataloader(ds, batch_size=run["batch_size"], num_workers=2)
     epoch = trainer.sampler.epoch  # the resumed epoch, 0 on a fresh start
+    empty_epochs = 0
     while trainer.orchestrator.global_step < run["max_steps"]:
         if hasattr(loader.sampler, "set_epoch"):
             loader.sampler.set_epoch(epoch)
         trainer.orchestrator.set_epoch(epoch)
-        trainer.train_epoch(loader)
+        ran = trainer.train_epoch(loader)["total_steps"]
         epoch += 1
+        # A resumed epoch may already be used up; a second empty epoch in a row
+        # means the loader yields nothing and the loop would never end.
+        empty_epochs = empty_epochs + 1 if ran == 0 else 0
+        if empty_epochs >= 2:
+            raise RuntimeError("two epochs in a row yielded no batch; the dataset is too small for the batch size")
     trainer.save_checkpoint(os.path.join(args.checkpoint_dir, "checkpoint_final.pt"))
     if trainer.is_distributed:
         dist.destroy_process_group()

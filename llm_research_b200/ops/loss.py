@@ -149,10 +149,17 @@ class _VocabParallelLinearCEFn(torch.autograd.Function):
         w_loc = w[v0:v1]
         valid = targets != ignore_index
         owned = valid & (targets >= v0) & (targets < v1)
-        t_loc = torch.where(owned, targets - v0, torch.where(valid, torch.full_like(targets, -1), targets))
+        # Rows whose target lives on another shard get a sentinel outside
+        # [0, v1 - v0) that also differs from ignore_index, so the shard kernels
+        # count them (softmax gradient, no one-hot) instead of ignoring them.
+        other = -2 if ignore_index == -1 else -1
+        t_loc = torch.where(owned, targets - v0, torch.where(valid, torch.full_like(targets, other), targets))
         stats = torch.zeros(2, N, dtype=torch.float32, device=h.device)  # (local lse, local target logit)
         logits = []
-        for s in range(0, N, chunk):
+        empty = v1 == v0  # V < world * ceil(V / world): the last ranks own no rows
+        if empty:
+            stats[0].fill_(float("-inf"))  # log-sum-exp over an empty set of logits
+        for s in range(0, 0 if empty else N, chunk):
             lg = F.linear(h[s:s + chunk], w_loc).contiguous()
             tc = t_loc[s:s + chunk].contiguous()
             if lg.is_cuda:
@@ -174,7 +181,7 @@ class _VocabParallelLinearCEFn(torch.autograd.Function):
         need_h, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         dh = torch.zeros_like(h) if need_h else None
         dw = torch.zeros(per, d, dtype=torch.float32, device=h.device) if need_w else None
-        for i, s in enumerate(range(0, N, chunk)):
+        for i, s in enumerate(range(0, 0 if empty else N, chunk)):
             lg, tc = logits[i], t_loc[s:s + chunk].contiguous()
             if not (need_h or need_w):
                 break

@@ -143,6 +143,7 @@ class FlatShardEngine(nn.Module):
         reduce_dtype: torch.dtype = torch.float32,
         comm: Optional[str] = None,
         tp_group: Optional[dist.ProcessGroup] = None,
+        replicate: bool = False,
     ) -> None:
         super().__init__()
         self.module = module
@@ -153,6 +154,13 @@ class FlatShardEngine(nn.Module):
         self.distributed = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(process_group) if self.distributed else 1
         self.rank = dist.get_rank(process_group) if self.distributed else 0
+        # ``replicate``: every rank keeps the whole model and optimizer (one
+        # shard per rank of a world of one) and the unit gradients are averaged
+        # with an all-reduce over the group instead of reduce-scattered -- the
+        # DDP-like NO_SHARD strategy.
+        self.replicas = 1
+        if replicate and self.world > 1:
+            self.replicas, self.world, self.rank = self.world, 1, 0
         self.compute_dtype = compute_dtype
         self.reduce_dtype = reduce_dtype
         self.reshard_after_forward = reshard_after_forward and self.world > 1
@@ -439,6 +447,8 @@ class FlatShardEngine(nn.Module):
     @nvtx_fn("lrb/fsdp/rs")
     def _reduce_scatter(self, u: Unit) -> None:
         if self.world == 1:
+            if self.replicas > 1:
+                self._all_reduce(u)
             return
         if self.comm_stream is None:
             dist.reduce_scatter_tensor(u.grad_shard, u.grad_acc, op=dist.ReduceOp.AVG, group=self.pg)
@@ -465,6 +475,22 @@ class FlatShardEngine(nn.Module):
             if out is not u.grad_shard:
                 u.grad_shard.copy_(out)
             u.grad_acc.zero_()
+            ev = torch.cuda.Event()
+            ev.record(self.comm_stream)
+        u.rs_event = ev
+
+    def _all_reduce(self, u: Unit) -> None:
+        """Replicated parameters: average the unit's fp32 gradient over the group
+        in place (sum, then 1/replicas: gloo has no average)."""
+        if self.comm_stream is None:
+            dist.all_reduce(u.grad_acc, group=self.pg)
+            u.grad_acc.mul_(1.0 / self.replicas)
+            return
+        cur = torch.cuda.current_stream(self.device)
+        self.comm_stream.wait_stream(cur)
+        with torch.cuda.stream(self.comm_stream):
+            dist.all_reduce(u.grad_acc, group=self.pg)
+            u.grad_acc.mul_(1.0 / self.replicas)
             ev = torch.cuda.Event()
             ev.record(self.comm_stream)
         u.rs_event = ev
@@ -579,7 +605,7 @@ class FlatShardEngine(nn.Module):
         flags = torch.zeros(len(self.params), dtype=torch.float32, device=self.device)
         if self._touched:
             flags[list(self._touched)] = 1.0
-        if self.world > 1:
+        if self.world > 1 or self.replicas > 1:
             dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=self.pg)
         return {i for i, f in enumerate(flags.tolist()) if f > 0}
 

@@ -6,8 +6,10 @@
 
 * ``sharding_strategy``: ``FULL_SHARD`` (ZeRO-3: parameters re-gathered for
   the backward), ``SHARD_GRAD_OP`` (ZeRO-2: gathered once per micro-step),
-  ``NO_SHARD``/``HYBRID_SHARD`` (accepted; on one NVSwitch island they
-  behave like ``SHARD_GRAD_OP``);
+  ``NO_SHARD`` (DDP-like: every rank holds the whole model and optimizer,
+  unit gradients are averaged with an all-reduce), ``HYBRID_SHARD`` (sharded
+  within a node, replicated across nodes; on a single node it is
+  ``FULL_SHARD``, and a group spanning several nodes is rejected);
 * ``mixed_precision``: ``bf16``/``fp16`` compute copies (fp32 master weights
   and fp32 gradient accumulation always), ``fp32`` computes in fp32;
 * ``activation_checkpointing``: per-transformer-block recomputation (the
@@ -84,12 +86,19 @@ def wrap_model_fsdp(model: nn.Module, fsdp_config: FSDPConfig, device_id: Option
     strategy = get_sharding_strategy(fsdp_config.sharding_strategy)
     dtype = get_mixed_precision(fsdp_config.mixed_precision) or torch.float32
     device = torch.device("cuda", device_id) if device_id is not None and torch.cuda.is_available() else next(model.parameters()).device
+    if strategy == "HYBRID_SHARD" and torch.distributed.is_initialized():
+        from llm_research_b200.parallel.symm import single_node
+
+        if not single_node(fsdp_config.process_group):
+            raise NotImplementedError("HYBRID_SHARD across several nodes (shard within a node, replicate across "
+                                      "nodes) is not supported; use FULL_SHARD or NO_SHARD")
     if fsdp_config.activation_checkpointing:
         apply_activation_checkpointing(model)
     engine = FlatShardEngine(
         model,
         compute_dtype=dtype,
-        reshard_after_forward=(strategy == "FULL_SHARD"),
+        reshard_after_forward=(strategy in ("FULL_SHARD", "HYBRID_SHARD")),
+        replicate=(strategy == "NO_SHARD"),
         unit_classes=(TransformerBlock, MemoryReadLayer),
         device=device,
         process_group=fsdp_config.process_group,

@@ -18,7 +18,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
-CANDIDATES = [os.path.join(REPO, "baseline", "_ref"), "/root/reference"]
+# The installed reference (``baseline/_ref``, made by ``__graft_entry__.build``)
+# or a source tree named by ``LRB_REFERENCE_DIR``.
+CANDIDATES = [p for p in (os.environ.get("LRB_REFERENCE_DIR"), os.path.join(REPO, "baseline", "_ref")) if p]
 
 
 def reference_root() -> Optional[str]:

@@ -28,7 +28,7 @@ def _data():
     return torch.randint(0, 512, (4, 32), generator=torch.Generator().manual_seed(5))
 
 
-def _train(model, batches, engine: bool, steps=3):
+def _train(model, batches, engine: bool, steps=3, strategy="FULL_SHARD"):
     from genesis.training.train_phase1_bootstrap import ntp_objective
     from olympus.core.training_orchestrator import ModelConfig, ObjectiveConfig, TrainingOrchestrator
     from olympus.distributed.distributed_orchestrator import DistributedTrainingOrchestrator
@@ -37,7 +37,8 @@ def _train(model, batches, engine: bool, steps=3):
 
     opt = MuonAdamWHybrid(model.parameters(), lr_muon=0.02, lr_adamw=1e-3, weight_decay_muon=0.01)
     if engine:
-        orch = DistributedTrainingOrchestrator(fsdp_config=FSDPConfig(mixed_precision="fp32", activation_checkpointing=False),
+        orch = DistributedTrainingOrchestrator(fsdp_config=FSDPConfig(sharding_strategy=strategy, mixed_precision="fp32",
+                                                                      activation_checkpointing=False),
                                                gradient_accumulation_steps=len(batches), device=torch.device("cpu"))
     else:
         orch = TrainingOrchestrator(gradient_accumulation_steps=len(batches))
@@ -83,3 +84,25 @@ def test_distributed_fsdp_and_muon_match_single_process(world):
             torch.testing.assert_close(res[r]["params"][k], v, atol=5e-5, rtol=1e-4, msg=f"rank {r} {k}")
     st = res[0]["opt"]["state"]
     assert any(s["type"] == "muon" for s in st.values()) and any(s["type"] == "adamw" for s in st.values())
+
+
+def _no_shard_rank_fn(rank, world):
+    data = _data()
+    per = data.shape[0] // world
+    sd, orch = _train(_toy_model(), [data[rank * per:(rank + 1) * per]], engine=True, strategy="NO_SHARD")
+    eng = orch._models["hlrt"].model
+    return {"params": sd, "replicas": eng.replicas, "world": eng.world,
+            "master_numel": sum(u.master.numel() for u in eng.units)}
+
+
+def test_no_shard_replicates_and_matches_single_process():
+    """NO_SHARD keeps the whole model on each rank (a shard world of one) and
+    averages gradients with an all-reduce: 2 ranks on half batches each equal
+    one process on the whole batch."""
+    single, _ = _train(_toy_model(), [_data()], engine=False)
+    total = sum(v.numel() for v in single.values())
+    for r, res in enumerate(run_ranks(_no_shard_rank_fn, 2)):
+        assert res["replicas"] == 2 and res["world"] == 1
+        assert res["master_numel"] >= total  # replicated, not sharded
+        for k, v in single.items():
+            torch.testing.assert_close(res["params"][k], v, atol=5e-5, rtol=1e-4, msg=f"rank {r} {k}")

@@ -44,25 +44,29 @@ def test_hlrt_ntp_with_fused_head_matches_logits_path():
 
 
 @pytest.mark.gpu
-def test_ce_bwd_vocab_shard_kernel_matches_fp32():
-    """Gradient of one vocabulary shard's logits against the fp32 softmax of the full row."""
+@pytest.mark.parametrize("ignore", [-100, -1])
+def test_ce_bwd_vocab_shard_kernel_matches_fp32(ignore):
+    """Gradient of one vocabulary shard's logits against the fp32 softmax of the
+    full row; rows owned by another shard carry the marker the op assigns them
+    (-1, or -2 when ignore_index is -1)."""
     from llm_research_b200._ext import native
 
     g = torch.Generator().manual_seed(5)
     R, V, v0, v1 = 300, 1000, 400, 720
     full = torch.randn(R, V, generator=g) * 3
     t = torch.randint(0, V, (R,), generator=g)
-    t[::9] = -100
+    t[::9] = ignore
     lse = torch.logsumexp(full, dim=-1)
     loc = full[:, v0:v1].to(torch.bfloat16)
     owned = (t >= v0) & (t < v1)
-    t_loc = torch.where(owned, t - v0, torch.where(t != -100, torch.full_like(t, -1), t))
+    other = -2 if ignore == -1 else -1
+    t_loc = torch.where(owned, t - v0, torch.where(t != ignore, torch.full_like(t, other), t))
     scale = torch.tensor([0.25])
-    got = native().ce_bwd_vocab_shard(loc.cuda(), t_loc.cuda(), lse.cuda(), scale.cuda(), -100).float().cpu()
+    got = native().ce_bwd_vocab_shard(loc.cuda(), t_loc.cuda(), lse.cuda(), scale.cuda(), ignore).float().cpu()
     p = torch.exp(loc.float() - lse[:, None])
     rows = torch.arange(R)[owned]
     p[rows, t_loc[owned]] -= 1.0
-    ref = p * ((t != -100).float() * 0.25)[:, None]
+    ref = p * ((t != ignore).float() * 0.25)[:, None]
     torch.testing.assert_close(got, ref, atol=2e-3, rtol=2e-2)
 
 

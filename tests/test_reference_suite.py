@@ -4,8 +4,9 @@ The reference's tests import ``genesis.*`` and ``olympus.*`` by name; a child
 interpreter puts this repository first on ``sys.path`` (and checks that the
 imports resolve here), then runs the reference's ``tests/`` directory with
 ``-m "not gpu"``.  Every test must pass: the public and the test-visible
-private API of the reference is reproduced.  Skipped when the reference's
-sources are not present on the machine.
+private API of the reference is reproduced.  The reference's source tree is
+read from ``LRB_REFERENCE_DIR`` (its ``tests/`` directory is not part of the
+installed package); skipped when that variable is unset or has no tests.
 """
 
 from __future__ import annotations
@@ -17,7 +18,7 @@ import sys
 import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REFERENCE_TESTS = "/root/reference/tests"
+REFERENCE_TESTS = os.path.join(os.environ.get("LRB_REFERENCE_DIR", os.path.join(REPO, "baseline", "_ref")), "tests")
 
 _RUNNER = r"""
 import sys

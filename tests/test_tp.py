@@ -152,7 +152,7 @@ def test_hlrt_tensor_parallel_vocab_parallel_loss_cpu():
             torch.testing.assert_close(g, r, atol=1e-4, rtol=1e-3, msg=name)
 
 
-def _vocab_ce_case(rank, world, V):
+def _vocab_ce_case(rank, world, V, ignore=-100):
     import torch.distributed as dist
 
     from llm_research_b200.ops.loss import linear_cross_entropy, vocab_parallel_linear_cross_entropy
@@ -161,10 +161,11 @@ def _vocab_ce_case(rank, world, V):
     h = torch.randn(50, 16, generator=g)
     w = torch.randn(V, 16, generator=g) * 0.5
     t = torch.randint(0, V, (50,), generator=g)
-    t[::7] = -100
+    t[::7] = ignore
     out = {}
-    for name, fn in (("full", lambda a, b: linear_cross_entropy(a, b, t, chunk=16)),
-                     ("vp", lambda a, b: vocab_parallel_linear_cross_entropy(a, b, t, dist.group.WORLD, chunk=16))):
+    for name, fn in (("full", lambda a, b: linear_cross_entropy(a, b, t, ignore_index=ignore, chunk=16)),
+                     ("vp", lambda a, b: vocab_parallel_linear_cross_entropy(a, b, t, dist.group.WORLD,
+                                                                             ignore_index=ignore, chunk=16))):
         a, b = h.clone().requires_grad_(), w.clone().requires_grad_()
         loss = fn(a, b)
         (loss * 1.5).backward()
@@ -175,6 +176,20 @@ def _vocab_ce_case(rank, world, V):
 @pytest.mark.parametrize("V", [40, 37])
 def test_vocab_parallel_linear_cross_entropy_cpu(V):
     for res in run_ranks(_vocab_ce_case, 2, V):
+        for r, g in zip(res["full"], res["vp"]):
+            torch.testing.assert_close(g, r, atol=1e-5, rtol=1e-5)
+
+
+def test_vocab_parallel_linear_cross_entropy_ignore_minus_one_cpu():
+    """ignore_index=-1 must not collide with the marker of rows owned by another shard."""
+    for res in run_ranks(_vocab_ce_case, 2, 40, -1):
+        for r, g in zip(res["full"], res["vp"]):
+            torch.testing.assert_close(g, r, atol=1e-5, rtol=1e-5)
+
+
+def test_vocab_parallel_linear_cross_entropy_empty_shard_cpu():
+    """V=5 over 4 ranks: ceil(5/4)=2 rows per rank, so the last rank owns none."""
+    for res in run_ranks(_vocab_ce_case, 4, 5):
         for r, g in zip(res["full"], res["vp"]):
             torch.testing.assert_close(g, r, atol=1e-5, rtol=1e-5)
 
