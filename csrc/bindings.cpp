@@ -54,6 +54,9 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> attn_bwd(const at::Tensor&, const
 at::Tensor gemm_tn(const at::Tensor&, const at::Tensor&, at::ScalarType, double);
 void gemm_tn_accumulate(const at::Tensor&, const at::Tensor&, at::Tensor&, double);
 int64_t sm100_error(int64_t);
+// gemm_pair_sm100.cu
+void gemm_pair(const at::Tensor&, const at::Tensor&, bool, bool, at::Tensor&, bool, double);
+int64_t gemm_pair_error(int64_t);
 // attention_sm100.cu
 bool attn_sm100_supported(const at::Tensor&, const at::Tensor&, const at::Tensor&);
 std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor&, const at::Tensor&, const at::Tensor&, bool, double);
@@ -139,6 +142,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tn", &lrb::gemm_tn);
   m.def("gemm_tn_accumulate", &lrb::gemm_tn_accumulate);
   m.def("sm100_error", &lrb::sm100_error);
+  m.def("gemm_pair", &lrb::gemm_pair,
+        "C (=|+=) alpha op(A) op(B)^T on CTA pairs (tcgen05 cta_group::2); a_mn/b_mn: operand stored (K, M)/(K, N)");
+  m.def("gemm_pair_error", &lrb::gemm_pair_error);
   m.def("attn_sm100_supported", &lrb::attn_sm100_supported);
   m.def("attn_fwd_sm100", &lrb::attn_fwd_sm100);
   m.def("attn_sm100_error", &lrb::attn_sm100_error);

@@ -1,0 +1,434 @@
+// Persistent CTA-pair tcgen05 GEMM for the model's linears (forward, dgrad and
+// wgrad), bf16/fp16 operands, fp32 accumulation in tensor memory:
+//
+//   C[M, N]  = alpha * op(A) op(B)^T          (bf16 / fp16 / fp32 C), or
+//   C[M, N] += alpha * op(A) op(B)^T          (fp32 C: gradient accumulation)
+//
+// Each operand is K-major (A stored (M, K), B stored (N, K): the nn.Linear
+// layout) or MN-major (A stored (K, M), B stored (K, N)), so the three GEMMs of
+// a linear layer read the activations, weights and output gradients where they
+// lie, without transposed copies:
+//   forward  Y  = X W^T     A = X  (K-major),  B = W  (K-major)
+//   dgrad    dX = dY W      A = dY (K-major),  B = W  (MN-major)
+//   wgrad    dW = dY^T X    A = dY (MN-major), B = X  (MN-major)
+//
+// A cluster of two CTAs (the two SMs of a TPC) computes one 256 x 256 output
+// tile per step with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16): each
+// CTA loads its 128 rows of A and its 128 rows (N) of B by TMA into its own
+// shared memory, so per output element the shared-memory traffic is half that
+// of a one-CTA 128 x 256 tile.  No TMA load uses multicast.
+//
+// Roles per CTA (6 warps):
+//   warp 0     TMA producer: waits for a free stage (its own `empty`), loads its
+//              halves; the completion bytes of both CTAs go to the leader's
+//              `full` barrier (the leader announces 2 x stage bytes);
+//   warp 1     owns tensor memory (512 columns: two 128 x 256 fp32
+//              accumulators, allocated as a pair); on the leader (cluster rank 0)
+//              lane 0 issues the MMAs and commits `empty` and `accfull` to both
+//              CTAs;
+//   warps 2-5  epilogue: tcgen05.ld of their 32-lane quarter, convert, store or
+//              accumulate; then arrive on the leader's `accempty`, so the next
+//              tile's MMAs overlap this epilogue.
+// Tiles are visited in groups of GROUP_M tile rows so that the tiles in flight
+// share A rows and B columns in L2.
+//
+// Every wait is bounded (sm100.cuh); on timeout the kernel records an error code
+// in a device word, skips its remaining work, and both CTAs meet at a cluster
+// barrier (after the leader drained its MMAs) before freeing tensor memory.
+#include "../common.cuh"
+#include "sm100.cuh"
+
+#include <mutex>
+
+namespace lrb {
+
+// Device error word of this kernel (module global: one per device, no allocation).
+__device__ int g_gemm_pair_err;
+
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;         // rows of A per CTA (256 per pair)
+constexpr int BN = 256;         // columns of the output tile (128 rows of B per CTA)
+constexpr int BK = 64;          // K per stage (128 bytes of bf16: one swizzle row)
+constexpr int STAGES = 6;
+constexpr int GROUP_M = 8;      // tile rows per raster group
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kHalfA = BM * BK * 2;        // 16 KB
+constexpr uint32_t kHalfB = (BN / 2) * BK * 2;  // 16 KB
+constexpr uint32_t kStage = kHalfA + kHalfB;
+constexpr uint32_t kMnBox = 64 * BK * 2;        // 8 KB: 64 MN elements x 64 K rows
+constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + 256;
+
+enum Epi : int { kStore = 0, kAccumF32 = 1 };
+
+struct PairArgs {
+  void* C;
+  int64_t ldc;
+  int M, N, K;
+  float alpha;
+  int vec_ok;  // C base and row pitch 16-byte aligned
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int per_group = GROUP_M * tiles_n;
+  const int g = tile / per_group;
+  const int first = g * GROUP_M;
+  const int gsize = min(tiles_m - first, GROUP_M);
+  const int r = tile % per_group;
+  tm = first + r % gsize;
+  tn = r / gsize;
+}
+
+template <typename OutT, int EPI>
+__device__ __forceinline__ void store_chunk(const PairArgs& a, int row, int col0, const uint32_t* r) {
+  if (row >= a.M || col0 >= a.N) return;
+  if constexpr (EPI == kAccumF32) {
+    float* c = reinterpret_cast<float*>(a.C) + (int64_t)row * a.ldc + col0;
+    if (a.vec_ok && col0 + 32 <= a.N) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 v = *reinterpret_cast<float4*>(c + j);
+        v.x += a.alpha * __uint_as_float(r[j]);
+        v.y += a.alpha * __uint_as_float(r[j + 1]);
+        v.z += a.alpha * __uint_as_float(r[j + 2]);
+        v.w += a.alpha * __uint_as_float(r[j + 3]);
+        *reinterpret_cast<float4*>(c + j) = v;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)  // unrolled: r[] stays in registers
+        if (col0 + j < a.N) c[j] += a.alpha * __uint_as_float(r[j]);
+    }
+  } else {
+    OutT* c = reinterpret_cast<OutT*>(a.C) + (int64_t)row * a.ldc + col0;
+    constexpr int V = 16 / sizeof(OutT);
+    if (a.vec_ok && col0 + 32 <= a.N) {
+#pragma unroll
+      for (int j = 0; j < 32; j += V) {
+        Vec16<OutT> v;
+#pragma unroll
+        for (int t = 0; t < V; ++t) v.v[t] = from_f<OutT>(a.alpha * __uint_as_float(r[j + t]));
+        st16(c + j, v);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < a.N) c[j] = from_f<OutT>(a.alpha * __uint_as_float(r[j]));
+    }
+  }
+}
+
+// Loads this CTA's half of one stage: A rows [m0, m0 + 128) and B rows [n0, n0 + 128)
+// at K offset k0.  MN-major operands are two 64-wide boxes each.
+template <bool A_MN, bool B_MN>
+__device__ __forceinline__ void load_stage(unsigned char* sa, unsigned char* sb, const CUtensorMap* tmA,
+                                           const CUtensorMap* tmB, uint32_t bar, int m0, int n0, int k0) {
+  if (A_MN) {
+    tma_load_2d_pair(sa, tmA, bar, m0, k0);
+    tma_load_2d_pair(sa + kMnBox, tmA, bar, m0 + 64, k0);
+  } else {
+    tma_load_2d_pair(sa, tmA, bar, k0, m0);
+  }
+  if (B_MN) {
+    tma_load_2d_pair(sb, tmB, bar, n0, k0);
+    tma_load_2d_pair(sb + kMnBox, tmB, bar, n0 + 64, k0);
+  } else {
+    tma_load_2d_pair(sb, tmB, bar, k0, n0);
+  }
+}
+
+template <typename OutT, int EPI, bool BF16IN, bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, PairArgs args) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sA = base;
+  unsigned char* sB = base + STAGES * kHalfA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kHalfB);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accfull = empty + STAGES;
+  uint64_t* accempty = accfull + 2;
+  uint64_t* drain = accempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* err = &g_gemm_pair_err;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = (int)cluster_id_x(), npairs = (int)nclusters_x();
+  const int tiles_m = (args.M + 2 * BM - 1) / (2 * BM), tiles_n = (args.N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int nk = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accfull[b], 1);
+      mbar_init(&accempty[b], 8);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, tensor memory allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t armed = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        int tm, tn;
+        tile_coords(tile, tiles_m, tiles_n, tm, tn);
+        const int m0 = tm * 2 * BM + (int)rank * BM, n0 = tn * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrTmaWait)) { ok = false; break; }
+          const uint32_t fb = mapa_shared(smem_addr(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStage);
+          load_stage<A_MN, B_MN>(sA + stage * kHalfA, sB + stage * kHalfB, &tmA, &tmB, fb, m0, n0, kb * BK);
+          ++armed;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // The leader can wait for its last stages to land (which needs both CTAs'
+      // bytes); the peer's loads land before the leader's MMAs read them, and
+      // the cluster barrier below keeps the peer resident until then.
+      if (leader) {
+        for (int i = 1; i <= STAGES && i <= armed; ++i) {
+          const int64_t pos = armed - i;
+          mbar_wait(&full[pos % STAGES], (uint32_t)((pos / STAGES) & 1), nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16_major(2 * BM, BN, BF16IN, A_MN, B_MN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        if (!mbar_wait(&accempty[acc], acc_phase ^ 1, err, kErrAccWait)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err, kErrMmaWait)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(sA + stage * kHalfA), b0 = smem_addr(sB + stage * kHalfB);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? umma_desc_mn_sw128(a0 + k * 2048, kMnBox, 1024) : umma_desc_k_sw128(a0 + k * 32);
+            const uint64_t bd = B_MN ? umma_desc_mn_sw128(b0 + k * 2048, kMnBox, 1024) : umma_desc_k_sw128(b0 + k * 32);
+            umma_f16_pair(d, ad, bd, idesc, (kb | k) != 0);
+          }
+          umma_commit_pair_mc(&empty[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        umma_commit_pair_mc(&accfull[acc], 0x3);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      umma_commit_pair(drain);
+      mbar_wait(drain, 0, nullptr, 0);  // every issued MMA retired before the pair frees tensor memory
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs) {
+      int tm, tn;
+      tile_coords(tile, tiles_m, tiles_n, tm, tn);
+      if (!mbar_wait(&accfull[acc], acc_phase, err, kErrEpiWait)) break;
+      tc_fence_after();
+      const int row = tm * 2 * BM + (int)rank * BM + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+        tmem_ld_wait();
+        store_chunk<OutT, EPI>(args, row, tn * BN + c * 32, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&accempty[acc]), 0));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs into both CTAs' tensor memory have retired
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    LRB_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    LRB_CHECK(p != nullptr && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled unavailable");
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Row-major (rows x cols) 16-bit matrix with row pitch `ld` elements; box = box_cols x box_rows,
+// 128-byte swizzle (box_cols = 64).
+CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, bool bf16) {
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                           const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LRB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  return m;
+}
+
+// Clusters of two that fit at once on this device (cached per device).
+int max_pairs(int dev) {
+  static int cached[64] = {0};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+  int sms = 0;
+  LRB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  int n = sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * n, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto k = gemm_pair_kernel<__nv_bfloat16, kStore, true, false, false>;
+  LRB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) == cudaSuccess && clusters > 0) n = std::min(n, clusters);
+  (void)cudaGetLastError();
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  return n;
+}
+
+template <typename OutT, int EPI, bool BF16IN, bool A_MN, bool B_MN>
+void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const PairArgs& args, int pairs) {
+  auto k = gemm_pair_kernel<OutT, EPI, BF16IN, A_MN, B_MN>;
+  LRB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+  k<<<2 * pairs, kThreads, kSmem, stream()>>>(ta, tb, args);
+  LRB_LAUNCH_CHECK();
+}
+
+template <typename OutT, int EPI, bool BF16IN>
+void launch_layout(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const PairArgs& args,
+                   int pairs) {
+  if (!a_mn && !b_mn) launch_t<OutT, EPI, BF16IN, false, false>(ta, tb, args, pairs);
+  else if (!a_mn && b_mn) launch_t<OutT, EPI, BF16IN, false, true>(ta, tb, args, pairs);
+  else if (a_mn && b_mn) launch_t<OutT, EPI, BF16IN, true, true>(ta, tb, args, pairs);
+  else launch_t<OutT, EPI, BF16IN, true, false>(ta, tb, args, pairs);
+}
+
+void check_operand(const at::Tensor& t, const char* name) {
+  LRB_CHECK(t.is_cuda() && t.dim() == 2 && t.stride(1) == 1, "gemm_pair: ", name,
+            " must be a 2-D CUDA tensor with unit column stride");
+  LRB_CHECK(t.scalar_type() == at::kBFloat16 || t.scalar_type() == at::kHalf, "gemm_pair: ", name,
+            " must be bf16/fp16");
+  LRB_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0 && (t.stride(0) * 2) % 16 == 0 && t.stride(0) > 0,
+            "gemm_pair: ", name, " needs a 16-byte aligned base and row pitch");
+}
+
+}  // namespace
+
+// C (M x N, row pitch C.stride(0)) = alpha * op(A) op(B)^T, or += when `accumulate`
+// (then C is fp32).  a_mn: A is stored (K, M); otherwise (M, K).  b_mn: B is stored
+// (K, N); otherwise (N, K).
+void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, at::Tensor& C, bool accumulate,
+               double alpha) {
+  check_operand(A, "A");
+  check_operand(B, "B");
+  LRB_CHECK(A.scalar_type() == B.scalar_type(), "gemm_pair: A and B must have the same dtype");
+  const int64_t M = a_mn ? A.size(1) : A.size(0), K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0), KB = b_mn ? B.size(0) : B.size(1);
+  LRB_CHECK(K == KB, "gemm_pair: K mismatch (", K, " vs ", KB, ")");
+  LRB_CHECK(C.is_cuda() && C.dim() == 2 && C.size(0) == M && C.size(1) == N && C.stride(1) == 1,
+            "gemm_pair: C must be (M, N) with unit column stride");
+  LRB_CHECK(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), "gemm_pair: dimensions too large");
+  LRB_CHECK(!accumulate || C.scalar_type() == at::kFloat, "gemm_pair: accumulation needs an fp32 C");
+  LRB_CHECK(C.data_ptr() != A.data_ptr() && C.data_ptr() != B.data_ptr(), "gemm_pair: C must not alias A or B");
+  c10::cuda::CUDAGuard g(A.device());
+  if (M == 0 || N == 0) return;
+  if (K == 0) {
+    if (!accumulate) C.zero_();
+    return;
+  }
+  const bool bf = A.scalar_type() == at::kBFloat16;
+  // TMA boxes: K-major 64 (K) x 128 rows; MN-major 64 (MN) x 64 (K) rows.
+  CUtensorMap ta = a_mn ? make_map(A.data_ptr(), K, M, A.stride(0), 64, BK, bf)
+                        : make_map(A.data_ptr(), M, K, A.stride(0), BK, BM, bf);
+  CUtensorMap tb = b_mn ? make_map(B.data_ptr(), K, N, B.stride(0), 64, BK, bf)
+                        : make_map(B.data_ptr(), N, K, B.stride(0), BK, BN / 2, bf);
+  const int esz = (int)C.element_size();
+  const int vec_ok = (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0) && ((C.stride(0) * esz) % 16 == 0);
+  PairArgs args{C.data_ptr(), C.stride(0), (int)M, (int)N, (int)K, (float)alpha, vec_ok};
+  const int tiles = (int)(((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN));
+  const int pairs = std::max(1, std::min(tiles, max_pairs(A.get_device())));
+  const auto ct = C.scalar_type();
+  if (accumulate) {
+    if (bf) launch_layout<float, kAccumF32, true>(a_mn, b_mn, ta, tb, args, pairs);
+    else launch_layout<float, kAccumF32, false>(a_mn, b_mn, ta, tb, args, pairs);
+  } else if (ct == at::kBFloat16) {
+    if (bf) launch_layout<__nv_bfloat16, kStore, true>(a_mn, b_mn, ta, tb, args, pairs);
+    else launch_layout<__nv_bfloat16, kStore, false>(a_mn, b_mn, ta, tb, args, pairs);
+  } else if (ct == at::kHalf) {
+    if (bf) launch_layout<__half, kStore, true>(a_mn, b_mn, ta, tb, args, pairs);
+    else launch_layout<__half, kStore, false>(a_mn, b_mn, ta, tb, args, pairs);
+  } else if (ct == at::kFloat) {
+    if (bf) launch_layout<float, kStore, true>(a_mn, b_mn, ta, tb, args, pairs);
+    else launch_layout<float, kStore, false>(a_mn, b_mn, ta, tb, args, pairs);
+  } else {
+    LRB_CHECK(false, "gemm_pair: unsupported output dtype");
+  }
+}
+
+// Returns and clears the error word of the pair GEMM on `device` (0 = no timeout).
+int64_t gemm_pair_error(int64_t device) {
+  int prev = 0;
+  LRB_CUDA_CHECK(cudaGetDevice(&prev));
+  LRB_CUDA_CHECK(cudaSetDevice((int)device));
+  int h = 0;
+  LRB_CUDA_CHECK(cudaMemcpyFromSymbol(&h, g_gemm_pair_err, sizeof(int)));
+  if (h) {
+    const int zero = 0;
+    LRB_CUDA_CHECK(cudaMemcpyToSymbol(g_gemm_pair_err, &zero, sizeof(int)));
+  }
+  LRB_CUDA_CHECK(cudaSetDevice(prev));
+  return h;
+}
+
+}  // namespace lrb

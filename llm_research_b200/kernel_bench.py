@@ -16,6 +16,9 @@ Cases (shapes are the GENESIS-1B / 7B working shapes):
   attn_fwd_gqa           B=2, S=4096, H=32, Hkv=8, hd=128
   gemm                   tcgen05 bf16 GEMM 8192x8192x8192 (TN)
   gemm_cublas            the same shape through torch.matmul (library reference)
+  gemm_pair              CTA-pair tcgen05 GEMM (cta_group::2) 8192x8192x8192
+  lin_<name>_<kind>[_cublas]  fwd / dgrad / wgrad GEMM of a GENESIS-1B linear at
+                         32768 tokens (qkv, o, upgate, down, head), pair kernel or cuBLAS
   gemm_nvfp4             tcgen05 block-scaled NVFP4 GEMM 8192x8192x8192 (nominal FP4 dense peak 4.5 PFLOP/s)
   rmsnorm_fwd/bwd        32768 x 2048 bf16
   swiglu_fwd             32768 x (2 x 5632) bf16
@@ -94,6 +97,13 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
         if lib:
             return (lambda: torch.matmul(a, b.t())), 2.0 * n ** 3, 0.0
         return (lambda: C.gemm_tn(a, b, torch.bfloat16, 1.0)), 2.0 * n ** 3, 0.0
+
+    def gemm_pair():
+        n = 8192
+        a = torch.randn(n, n, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(n, n, device="cuda", dtype=torch.bfloat16)
+        c = torch.empty(n, n, device="cuda", dtype=torch.bfloat16)
+        return (lambda: C.gemm_pair(a, b, False, False, c, False, 1.0)), 2.0 * n ** 3, 0.0
 
     def gemm_fp4():
         from llm_research_b200.ops.quant import NVFP4Tensor, matmul_nvfp4
@@ -180,7 +190,7 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
 
         return run, 0.0, logits.numel() * 2 * 3.0
 
-    return {
+    cases = {
         "attn_fwd": lambda: _attn_case(4, 4096, 16, 16, False),
         "attn_bwd": lambda: _attn_case(4, 4096, 16, 16, True),
         "attn_fwd_gqa": lambda: _attn_case(2, 4096, 32, 8, False),
@@ -198,7 +208,42 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
         "ns_4096x4096": lambda: ns_shape(4096, 4096, 8),
         "ns_4096x11008": lambda: ns_shape(4096, 11008, 8),
         "ce": ce,
+        "gemm_pair": gemm_pair,
     }
+    for name, (N, K) in LINEAR_SHAPES.items():
+        for kind in ("fwd", "dgrad", "wgrad"):
+            for lib in (False, True):
+                cases[f"lin_{name}_{kind}" + ("_cublas" if lib else "")] = (
+                    lambda N=N, K=K, kind=kind, lib=lib: _linear_gemm_case(N, K, kind, lib))
+    return cases
+
+
+# (N, K) of the GENESIS-1B linears; M = 32768 tokens (8 sequences of 4096).
+LINEAR_SHAPES = {"qkv": (6144, 2048), "o": (2048, 2048), "upgate": (11264, 2048), "down": (2048, 5632),
+                 "head": (32000, 2048)}
+LINEAR_TOKENS = 32768
+
+
+def _linear_gemm_case(N: int, K: int, kind: str, lib: bool):
+    """One of the three GEMMs of a linear layer y = x W^T at the training shape,
+    on the CTA-pair kernel or through torch.matmul (cuBLAS)."""
+    from llm_research_b200.ops.gemm import linear_dgrad, linear_fwd, linear_wgrad
+
+    T = LINEAR_TOKENS
+    x = torch.randn(T, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+    dy = torch.randn(T, N, device="cuda", dtype=torch.bfloat16)
+    flops = 2.0 * T * N * K
+    if kind == "fwd":
+        out = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
+        fn = (lambda: torch.matmul(x, w.t(), out=out)) if lib else (lambda: linear_fwd(x, w, out=out))
+    elif kind == "dgrad":
+        out = torch.empty(T, K, device="cuda", dtype=torch.bfloat16)
+        fn = (lambda: torch.matmul(dy, w, out=out)) if lib else (lambda: linear_dgrad(dy, w, out=out))
+    else:
+        out = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
+        fn = (lambda: torch.matmul(dy.t(), x, out=out)) if lib else (lambda: linear_wgrad(dy, x, out=out))
+    return fn, flops, 0.0
 
 
 def main(argv=None) -> None:

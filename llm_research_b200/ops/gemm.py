@@ -1,12 +1,25 @@
-"""tcgen05 GEMMs: ``C = alpha * A @ B^T`` and ``C += alpha * A @ B^T`` (fp32 C).
+"""tcgen05 GEMMs.
 
-Both operands K-major (row-major ``A (M, K)``, ``B (N, K)``: the nn.Linear
-weight layout), bf16 or fp16, fp32 accumulation in tensor memory; see
-``csrc/kernels/gemm_sm100.cu`` for the pipeline.  Requirements: unit column
-stride, 16-byte aligned base and row stride (``K % 8 == 0`` for packed rows).
+``matmul_tn`` / ``matmul_tn_accumulate``: ``C = alpha * A @ B^T`` and
+``C += alpha * A @ B^T`` on the one-CTA kernel (``csrc/kernels/gemm_sm100.cu``;
+the TP fused kernels share its pipeline).
+
+``gemm``: the CTA-pair kernel (``csrc/kernels/gemm_pair_sm100.cu``) with either
+operand K-major or MN-major, which the model's linears use for all three of
+their GEMMs:
+
+* ``linear_fwd(x, w)``         ``x @ w.T``   (x (T, K), w (N, K))
+* ``linear_dgrad(dy, w)``      ``dy @ w``    (dy (T, N), w (N, K))
+* ``linear_wgrad(dy, x)``      ``dy.T @ x``  (dy (T, N), x (T, K)); with ``out``
+  fp32 and ``accumulate=True`` it adds into ``out`` (gradient accumulation).
+
+Operands: bf16 or fp16, unit column stride, 16-byte aligned base and row
+pitch.  CPU tensors take the plain PyTorch path (fp32 math).
 """
 
 from __future__ import annotations
+
+from typing import Optional
 
 import torch
 
@@ -26,6 +39,51 @@ def matmul_tn_accumulate(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor, alph
         return c
     native().gemm_tn_accumulate(a, b, c, float(alpha))
     return c
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, a_mn: bool = False, b_mn: bool = False,
+         out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+         accumulate: bool = False, alpha: float = 1.0) -> torch.Tensor:
+    """``C = alpha * op(A) op(B)^T`` (``+=`` into an fp32 ``out`` with ``accumulate``).
+
+    ``op(A)`` is ``a`` (M, K), or ``a.T`` when ``a_mn`` (``a`` stored (K, M));
+    ``op(B)^T`` is ``b.T`` for ``b`` (N, K), or ``b`` when ``b_mn`` (``b`` stored
+    (K, N))."""
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if out is None:
+        if accumulate:
+            raise ValueError("accumulate needs an output tensor")
+        out = torch.empty(M, N, dtype=out_dtype or a.dtype, device=a.device)
+    if not a.is_cuda:
+        av = a.float().t() if a_mn else a.float()
+        bv = b.float() if b_mn else b.float().t()
+        r = alpha * (av @ bv)
+        if accumulate:
+            out.add_(r.to(out.dtype))
+        else:
+            out.copy_(r)
+        return out
+    native().gemm_pair(a, b, bool(a_mn), bool(b_mn), out, bool(accumulate), float(alpha))
+    return out
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    return gemm(x, w, False, False, out=out)
+
+
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    return gemm(dy, w, False, True, out=out)
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 accumulate: bool = False) -> torch.Tensor:
+    return gemm(dy, x, True, True, out=out, accumulate=accumulate)
+
+
+def gemm_pair_error(device: int = 0) -> int:
+    """Read and clear the error word of the CTA-pair GEMM (0 = no timeout recorded)."""
+    return int(native().gemm_pair_error(int(device)))
 
 
 def sm100_error(device: int = 0) -> int:

@@ -1,0 +1,106 @@
+"""CTA-pair tcgen05 GEMM (cta_group::2, 256 x 256 tiles) in every operand layout
+against fp32 PyTorch: ragged M / N / K (tile and stage remainders, a pair whose
+second CTA's rows lie wholly past M), bf16 / fp16 inputs, bf16 / fp16 / fp32
+outputs and fp32 accumulation; then the three GEMMs of a linear layer."""
+
+import pytest
+import torch
+
+
+def _ref(A, B, a_mn, b_mn):
+    a = A.float().t() if a_mn else A.float()
+    b = B.float() if b_mn else B.float().t()
+    return a @ b
+
+
+def _operands(M, N, K, a_mn, b_mn, dtype, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    A = torch.randn(*((K, M) if a_mn else (M, K)), device="cuda", generator=g).to(dtype)
+    B = torch.randn(*((K, N) if b_mn else (N, K)), device="cuda", generator=g).to(dtype)
+    return A, B
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (264, 520, 200), (1024, 768, 1024), (96, 40, 8)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+def test_gemm_pair_layouts_bf16(M, N, K, a_mn, b_mn):
+    from llm_research_b200.ops.gemm import gemm, gemm_pair_error
+
+    A, B = _operands(M, N, K, a_mn, b_mn, torch.bfloat16)
+    C = gemm(A, B, a_mn, b_mn, alpha=0.5)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    ref = 0.5 * _ref(A, B, a_mn, b_mn)
+    err = ((C.float() - ref).norm() / ref.norm()).item()
+    assert err < 1e-2, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
+def test_gemm_pair_fp16_inputs_and_outputs(out_dtype):
+    from llm_research_b200.ops.gemm import gemm, gemm_pair_error
+
+    A, B = _operands(520, 392, 328, False, True, torch.float16, seed=3)
+    C = gemm(A, B, False, True, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    ref = _ref(A, B, False, True)
+    err = ((C.float() - ref).norm() / ref.norm()).item()
+    assert err < 2e-3 if out_dtype == torch.float32 else 1e-2, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("a_mn,b_mn", [(True, True), (False, False)])
+def test_gemm_pair_accumulates_into_fp32(a_mn, b_mn):
+    from llm_research_b200.ops.gemm import gemm, gemm_pair_error
+
+    A, B = _operands(384, 1000, 520, a_mn, b_mn, torch.bfloat16, seed=5)
+    C0 = torch.randn(384, 1000, device="cuda")
+    C = C0.clone()
+    gemm(A, B, a_mn, b_mn, out=C, accumulate=True, alpha=2.0)
+    gemm(A, B, a_mn, b_mn, out=C, accumulate=True, alpha=-1.0)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    ref = C0 + _ref(A, B, a_mn, b_mn)
+    torch.testing.assert_close(C, ref, atol=2e-2, rtol=1e-3)
+
+
+@pytest.mark.gpu
+def test_gemm_pair_strided_operands_and_output():
+    """Row pitches larger than the row (views into wider buffers)."""
+    from llm_research_b200.ops.gemm import gemm, gemm_pair_error
+
+    g = torch.Generator(device="cuda").manual_seed(7)
+    Abuf = torch.randn(300, 264, device="cuda", generator=g).bfloat16()
+    Bbuf = torch.randn(520, 264, device="cuda", generator=g).bfloat16()
+    A, B = Abuf[:, :200], Bbuf[:, :200]  # (300, 200) and (520, 200), pitch 264
+    Cbuf = torch.zeros(300, 640, device="cuda", dtype=torch.bfloat16)
+    C = Cbuf[:, 8:528]
+    gemm(A, B, out=C)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    ref = A.float() @ B.float().t()
+    err = ((C.float() - ref).norm() / ref.norm()).item()
+    assert err < 1e-2, err
+    assert Cbuf[:, :8].abs().sum().item() == 0 and Cbuf[:, 528:].abs().sum().item() == 0
+
+
+@pytest.mark.gpu
+def test_linear_gemms_match_fp32():
+    """forward x W^T, dgrad dY W and wgrad dY^T X at a small training shape."""
+    from llm_research_b200.ops.gemm import gemm_pair_error, linear_dgrad, linear_fwd, linear_wgrad
+
+    g = torch.Generator(device="cuda").manual_seed(11)
+    T, K, N = 2048, 512, 1536
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    dy = torch.randn(T, N, device="cuda", generator=g).bfloat16()
+    y, dx, dw = linear_fwd(x, w), linear_dgrad(dy, w), linear_wgrad(dy, x)
+    acc = torch.zeros(N, K, device="cuda")
+    linear_wgrad(dy, x, out=acc, accumulate=True)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    for got, ref in ((y, x.float() @ w.float().t()), (dx, dy.float() @ w.float()), (dw, dy.float().t() @ x.float()),
+                     (acc, dy.float().t() @ x.float())):
+        err = ((got.float() - ref).norm() / ref.norm()).item()
+        assert err < 1e-2, err
