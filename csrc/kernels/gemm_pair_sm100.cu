@@ -38,6 +38,7 @@
 #include "../common.cuh"
 #include "sm100.cuh"
 
+#include <cstring>
 #include <mutex>
 
 namespace lrb {
@@ -60,7 +61,11 @@ constexpr uint32_t kHalfA = BM * BK * 2;        // 16 KB
 constexpr uint32_t kHalfB = (BN / 2) * BK * 2;  // 16 KB
 constexpr uint32_t kStage = kHalfA + kHalfB;
 constexpr uint32_t kMnBox = 64 * BK * 2;        // 8 KB: 64 MN elements x 64 K rows
-constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + 256;
+// Epilogue staging: per epilogue warp two boxes of 32 rows x 32 columns (one
+// being written while the previous one's TMA store drains), up to 4 KB each (fp32).
+constexpr uint32_t kOutBox = 32 * 32 * 4;
+constexpr uint32_t kOutSmem = 4 * 2 * kOutBox;  // 32 KB
+constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + kOutSmem + 256;
 
 enum Epi : int { kStore = 0, kAccumF32 = 1 };
 
@@ -69,17 +74,66 @@ struct PairArgs {
   int64_t ldc;
   int M, N, K;
   float alpha;
-  int vec_ok;  // C base and row pitch 16-byte aligned
+  int vec_ok;   // C base and row pitch 16-byte aligned
+  int tma_out;  // the epilogue stages boxes in shared memory and writes them with TMA
+                // (stores, or reduce-adds when accumulating); else direct stores
+  int splits;   // K ranges per output tile (accumulation only: partial sums reduce-add)
+  int group_m;  // tile rows per raster group
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
-  const int per_group = GROUP_M * tiles_n;
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
+  const int per_group = group_m * tiles_n;
   const int g = tile / per_group;
-  const int first = g * GROUP_M;
-  const int gsize = min(tiles_m - first, GROUP_M);
+  const int first = g * group_m;
+  const int gsize = min(tiles_m - first, group_m);
   const int r = tile % per_group;
   tm = first + r % gsize;
   tn = r / gsize;
+}
+
+// Work unit -> (tile row, tile column, k-block range).  Units of one split index
+// are consecutive, so the units in flight share the same K range of A and B.
+__device__ __forceinline__ void unit_coords(int unit, int num_tiles, int tiles_m, int tiles_n, int nk,
+                                            const PairArgs& a, int& tm, int& tn, int& kb0, int& kb1) {
+  const int split = unit / num_tiles;
+  tile_coords(unit - split * num_tiles, tiles_m, tiles_n, a.group_m, tm, tn);
+  kb0 = (int)((int64_t)nk * split / a.splits);
+  kb1 = (int)((int64_t)nk * (split + 1) / a.splits);
+}
+
+// Writes this thread's row of a 32 x 32 box into the staging buffer in the TMA
+// swizzle of its tensor map: 16-bit outputs are 64-byte rows (64-byte swizzle:
+// 16-byte chunk j of row r at j ^ ((r >> 1) & 3)), fp32 outputs 128-byte rows
+// (128-byte swizzle: chunk j at j ^ (r & 7)).  Conflict-free for 8 rows at a time.
+template <typename OutT>
+__device__ __forceinline__ void stage_row(unsigned char* box, int lane, float alpha, const uint32_t* r) {
+  if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 v = make_float4(alpha * __uint_as_float(r[4 * j]), alpha * __uint_as_float(r[4 * j + 1]),
+                             alpha * __uint_as_float(r[4 * j + 2]), alpha * __uint_as_float(r[4 * j + 3]));
+      *reinterpret_cast<float4*>(box + lane * 128 + ((j ^ (lane & 7)) * 16)) = v;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      Vec16<OutT> v;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v.v[t] = from_f<OutT>(alpha * __uint_as_float(r[8 * j + t]));
+      *reinterpret_cast<uint4*>(box + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16)) = v.raw;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_store_box(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_box(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y)
+               : "memory");
 }
 
 template <typename OutT, int EPI>
@@ -142,12 +196,14 @@ __device__ __forceinline__ void load_stage(unsigned char* sa, unsigned char* sb,
 
 template <typename OutT, int EPI, bool BF16IN, bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, PairArgs args) {
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, PairArgs args) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sA = base;
   unsigned char* sB = base + STAGES * kHalfA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kHalfB);
+  unsigned char* sOut = sB + STAGES * kHalfB;  // 1024-byte aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kOutSmem);
   uint64_t* empty = full + STAGES;
   uint64_t* accfull = empty + STAGES;
   uint64_t* accempty = accfull + 2;
@@ -162,6 +218,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int tiles_m = (args.M + 2 * BM - 1) / (2 * BM), tiles_n = (args.N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
   const int nk = (args.K + BK - 1) / BK;
+  const int num_units = num_tiles * args.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -176,6 +233,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (args.tma_out) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -192,11 +250,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int64_t armed = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        int tm, tn;
-        tile_coords(tile, tiles_m, tiles_n, tm, tn);
+      for (int unit = pair; unit < num_units && ok; unit += npairs) {
+        int tm, tn, kb0, kb1;
+        unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1);
         const int m0 = tm * 2 * BM + (int)rank * BM, n0 = tn * BN + (int)rank * (BN / 2);
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrTmaWait)) { ok = false; break; }
           const uint32_t fb = mapa_shared(smem_addr(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStage);
@@ -221,11 +279,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      for (int unit = pair; unit < num_units && ok; unit += npairs) {
+        int tm, tn, kb0, kb1;
+        unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1);
         if (!mbar_wait(&accempty[acc], acc_phase ^ 1, err, kErrAccWait)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, err, kErrMmaWait)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_addr(sA + stage * kHalfA), b0 = smem_addr(sB + stage * kHalfB);
@@ -233,7 +293,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = A_MN ? umma_desc_mn_sw128(a0 + k * 2048, kMnBox, 1024) : umma_desc_k_sw128(a0 + k * 32);
             const uint64_t bd = B_MN ? umma_desc_mn_sw128(b0 + k * 2048, kMnBox, 1024) : umma_desc_k_sw128(b0 + k * 32);
-            umma_f16_pair(d, ad, bd, idesc, (kb | k) != 0);
+            umma_f16_pair(d, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit_pair_mc(&empty[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -246,26 +306,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    int acc = 0;
+    unsigned char* boxes = sOut + (warp - 2) * 2 * kOutBox;
+    int acc = 0, nbox = 0;
     uint32_t acc_phase = 0;
-    for (int tile = pair; tile < num_tiles; tile += npairs) {
-      int tm, tn;
-      tile_coords(tile, tiles_m, tiles_n, tm, tn);
+    for (int unit = pair; unit < num_units; unit += npairs) {
+      int tm, tn, kb0, kb1;
+      unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1);
       if (!mbar_wait(&accfull[acc], acc_phase, err, kErrEpiWait)) break;
       tc_fence_after();
-      const int row = tm * 2 * BM + (int)rank * BM + q * 32 + lane;
+      const int row0 = tm * 2 * BM + (int)rank * BM + q * 32;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
         tmem_ld_wait();
-        store_chunk<OutT, EPI>(args, row, tn * BN + c * 32, r);
+        if (c == BN / 32 - 1) {  // the accumulator is read out: the MMAs may reuse it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&accempty[acc]), 0));
+        }
+        const int col0 = tn * BN + c * 32;
+        if (args.tma_out) {
+          if (row0 >= args.M || col0 >= args.N) continue;
+          unsigned char* box = boxes + (nbox & 1) * kOutBox;
+          // the store issued from this buffer two boxes ago has finished reading it
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+          stage_row<OutT>(box, lane, args.alpha, r);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (EPI == kAccumF32) tma_reduce_add_box(&tmC, box, col0, row0);
+            else tma_store_box(&tmC, box, col0, row0);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          ++nbox;
+        } else {
+          store_chunk<OutT, EPI>(args, row0 + lane, col0, r);
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&accempty[acc]), 0));
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // stores complete before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -308,6 +390,25 @@ CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, in
   return m;
 }
 
+// Output box map: (rows x cols) C with row pitch `ld` elements, box 32 x 32,
+// 64-byte swizzle for 16-bit outputs and 128-byte swizzle for fp32.
+CUtensorMap make_out_map(void* ptr, int64_t rows, int64_t cols, int64_t ld, at::ScalarType t) {
+  CUtensorMap m;
+  const int esz = t == at::kFloat ? 4 : 2;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = t == at::kFloat      ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : t == at::kBFloat16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = encode_fn()(&m, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           esz == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LRB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (gemm_pair output) failed with code ", (int)r);
+  return m;
+}
+
 // Clusters of two that fit at once on this device (cached per device).
 int max_pairs(int dev) {
   static int cached[64] = {0};
@@ -330,6 +431,7 @@ int max_pairs(int dev) {
   cfg.numAttrs = 1;
   auto k = gemm_pair_kernel<__nv_bfloat16, kStore, true, false, false>;
   LRB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+  cfg.numAttrs = 0;  // the kernel declares its cluster shape
   int clusters = 0;
   if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) == cudaSuccess && clusters > 0) n = std::min(n, clusters);
   (void)cudaGetLastError();
@@ -338,20 +440,38 @@ int max_pairs(int dev) {
 }
 
 template <typename OutT, int EPI, bool BF16IN, bool A_MN, bool B_MN>
-void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const PairArgs& args, int pairs) {
+void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const PairArgs& args, int pairs) {
   auto k = gemm_pair_kernel<OutT, EPI, BF16IN, A_MN, B_MN>;
   LRB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-  k<<<2 * pairs, kThreads, kSmem, stream()>>>(ta, tb, args);
+  k<<<2 * pairs, kThreads, kSmem, stream()>>>(ta, tb, tc, args);
   LRB_LAUNCH_CHECK();
 }
 
 template <typename OutT, int EPI, bool BF16IN>
-void launch_layout(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const PairArgs& args,
-                   int pairs) {
-  if (!a_mn && !b_mn) launch_t<OutT, EPI, BF16IN, false, false>(ta, tb, args, pairs);
-  else if (!a_mn && b_mn) launch_t<OutT, EPI, BF16IN, false, true>(ta, tb, args, pairs);
-  else if (a_mn && b_mn) launch_t<OutT, EPI, BF16IN, true, true>(ta, tb, args, pairs);
-  else launch_t<OutT, EPI, BF16IN, true, false>(ta, tb, args, pairs);
+void launch_layout(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                   const PairArgs& args, int pairs) {
+  if (!a_mn && !b_mn) launch_t<OutT, EPI, BF16IN, false, false>(ta, tb, tc, args, pairs);
+  else if (!a_mn && b_mn) launch_t<OutT, EPI, BF16IN, false, true>(ta, tb, tc, args, pairs);
+  else if (a_mn && b_mn) launch_t<OutT, EPI, BF16IN, true, true>(ta, tb, tc, args, pairs);
+  else launch_t<OutT, EPI, BF16IN, true, false>(ta, tb, tc, args, pairs);
+}
+
+// Split count for an accumulating GEMM: the number of K ranges per tile (each of
+// at least 16 k-blocks) that best fills whole waves of CTA pairs.
+int choose_splits(int tiles, int pairs, int nk) {
+  if (tiles >= 4 * pairs) return 1;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= 8 && nk / s >= 16; ++s) {
+    const int units = tiles * s;
+    const int waves = (units + pairs - 1) / pairs;
+    const double eff = (double)units / ((double)waves * pairs);
+    if (eff > best_eff + 0.03) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
 }
 
 void check_operand(const at::Tensor& t, const char* name) {
@@ -393,26 +513,36 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, a
                         : make_map(A.data_ptr(), M, K, A.stride(0), BK, BM, bf);
   CUtensorMap tb = b_mn ? make_map(B.data_ptr(), K, N, B.stride(0), 64, BK, bf)
                         : make_map(B.data_ptr(), N, K, B.stride(0), BK, BN / 2, bf);
-  const int esz = (int)C.element_size();
-  const int vec_ok = (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0) && ((C.stride(0) * esz) % 16 == 0);
-  PairArgs args{C.data_ptr(), C.stride(0), (int)M, (int)N, (int)K, (float)alpha, vec_ok};
-  const int tiles = (int)(((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN));
-  const int pairs = std::max(1, std::min(tiles, max_pairs(A.get_device())));
   const auto ct = C.scalar_type();
+  LRB_CHECK(ct == at::kBFloat16 || ct == at::kHalf || ct == at::kFloat, "gemm_pair: unsupported output dtype");
+  const int esz = (int)C.element_size();
+  const bool aligned = (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0) && ((C.stride(0) * esz) % 16 == 0);
+  const int tiles = (int)(((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN));
+  const int nk = (int)((K + BK - 1) / BK);
+  const int maxp = max_pairs(A.get_device());
+  // Partial sums of one tile may only meet in C through the TMA reduce-add.
+  const int splits = (accumulate && aligned) ? choose_splits(tiles, maxp, nk) : 1;
+  const int pairs = std::max(1, std::min(tiles * splits, maxp));
+  // Raster groups of 8 tile rows; 16 when the B panel of a group is large (wide
+  // outputs), so it is streamed from DRAM fewer times.
+  const int group_m = N >= 16384 ? 16 : GROUP_M;
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  if (aligned) tc = make_out_map(C.data_ptr(), M, N, C.stride(0), ct);
+  PairArgs args{C.data_ptr(), C.stride(0), (int)M, (int)N, (int)K, (float)alpha, aligned ? 1 : 0, aligned ? 1 : 0,
+                splits, group_m};
   if (accumulate) {
-    if (bf) launch_layout<float, kAccumF32, true>(a_mn, b_mn, ta, tb, args, pairs);
-    else launch_layout<float, kAccumF32, false>(a_mn, b_mn, ta, tb, args, pairs);
+    if (bf) launch_layout<float, kAccumF32, true>(a_mn, b_mn, ta, tb, tc, args, pairs);
+    else launch_layout<float, kAccumF32, false>(a_mn, b_mn, ta, tb, tc, args, pairs);
   } else if (ct == at::kBFloat16) {
-    if (bf) launch_layout<__nv_bfloat16, kStore, true>(a_mn, b_mn, ta, tb, args, pairs);
-    else launch_layout<__nv_bfloat16, kStore, false>(a_mn, b_mn, ta, tb, args, pairs);
+    if (bf) launch_layout<__nv_bfloat16, kStore, true>(a_mn, b_mn, ta, tb, tc, args, pairs);
+    else launch_layout<__nv_bfloat16, kStore, false>(a_mn, b_mn, ta, tb, tc, args, pairs);
   } else if (ct == at::kHalf) {
-    if (bf) launch_layout<__half, kStore, true>(a_mn, b_mn, ta, tb, args, pairs);
-    else launch_layout<__half, kStore, false>(a_mn, b_mn, ta, tb, args, pairs);
-  } else if (ct == at::kFloat) {
-    if (bf) launch_layout<float, kStore, true>(a_mn, b_mn, ta, tb, args, pairs);
-    else launch_layout<float, kStore, false>(a_mn, b_mn, ta, tb, args, pairs);
+    if (bf) launch_layout<__half, kStore, true>(a_mn, b_mn, ta, tb, tc, args, pairs);
+    else launch_layout<__half, kStore, false>(a_mn, b_mn, ta, tb, tc, args, pairs);
   } else {
-    LRB_CHECK(false, "gemm_pair: unsupported output dtype");
+    if (bf) launch_layout<float, kStore, true>(a_mn, b_mn, ta, tb, tc, args, pairs);
+    else launch_layout<float, kStore, false>(a_mn, b_mn, ta, tb, tc, args, pairs);
   }
 }
 

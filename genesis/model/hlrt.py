@@ -36,6 +36,7 @@ from genesis.model.tier1_token_processor import Tier1TokenProcessor
 from genesis.model.tier2_semantic_planner import Tier2SemanticPlanner
 from genesis.model.tier3_deliberative import Tier3DeliberativeReasoner
 from genesis.model.tier_gate import TierGate
+from llm_research_b200.ops.linear import dense
 from olympus.core.stateful_module import StatefulModule
 
 
@@ -181,7 +182,7 @@ class HLRT(StatefulModule):
 
     def _head(self, h: torch.Tensor) -> torch.Tensor:
         w = self.output_proj.weight if self.output_proj is not None else self.embeddings.weight
-        return F.linear(h, w)
+        return dense(h, w)
 
     def forward(
         self,

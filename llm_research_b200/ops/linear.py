@@ -44,13 +44,19 @@ class _CatRows(torch.autograd.Function):
 
 
 def cat_rows(*ws: torch.Tensor) -> torch.Tensor:
-    """``torch.cat(ws, 0)`` for 2-D weights, without a copy when they are adjacent."""
+    """``torch.cat(ws, 0)`` for 2-D weights, without a copy when they are adjacent.
+    When the pieces' fp32 gradient accumulators (``_lrb_acc``) are adjacent too,
+    the result carries their concatenation as its own accumulator view."""
     if len(ws) == 1:
         return ws[0]
     if not any(w.requires_grad for w in ws):
         return ws[0].as_strided((sum(w.shape[0] for w in ws), ws[0].shape[1]), (ws[0].shape[1], 1)) \
             if _adjacent(ws) else torch.cat(ws, 0)
-    return _CatRows.apply(*ws)
+    out = _CatRows.apply(*ws)
+    accs = [getattr(w, "_lrb_acc", None) for w in ws]
+    if all(a is not None for a in accs) and _adjacent(accs):
+        out._lrb_acc = accs[0].as_strided((out.shape[0], out.shape[1]), (out.shape[1], 1))
+    return out
 
 
 # ------------------------------------------------------------ linear precision
@@ -122,6 +128,115 @@ class _NVFP4LinearFn(torch.autograd.Function):
         return dx, dw
 
 
+# ------------------------------------------------ direct gradient accumulation
+# A weight handed to the model by the sharding engine carries ``_lrb_acc``: the
+# fp32 gradient-accumulator view its gradient belongs to.  The pair kernel's
+# wgrad then adds ``dY^T x`` straight into it (fp32 epilogue) and the backward
+# returns ACCUMULATED -- an all-zero gradient, a broadcast view of one zero
+# scalar -- for the weight; the engine's gradient sink recognises that storage
+# and only does its bookkeeping.  Anything autograd sums with the marker is a
+# real gradient again (the marker is zero), so tied or reused weights stay exact.
+_ZEROS: dict = {}
+
+
+def accumulated_marker(like: torch.Tensor) -> torch.Tensor:
+    key = (like.device, like.dtype)
+    z = _ZEROS.get(key)
+    if z is None:
+        z = _ZEROS[key] = torch.zeros((), dtype=like.dtype, device=like.device)
+    return z.expand(like.shape)
+
+
+def is_accumulated_marker(g: torch.Tensor) -> bool:
+    z = _ZEROS.get((g.device, g.dtype))
+    return z is not None and g.untyped_storage().data_ptr() == z.untyped_storage().data_ptr()
+
+
+_DIRECT_ACC = True
+
+
+def set_direct_grad_accumulation(on: bool) -> None:
+    """Switch the direct fp32 wgrad accumulation on (default) or off (dW is then
+    returned in the weight's dtype and the engine adds it)."""
+    global _DIRECT_ACC
+    _DIRECT_ACC = bool(on)
+
+
+def _acc_of(w: torch.Tensor):
+    if not _DIRECT_ACC:
+        return None
+    acc = getattr(w, "_lrb_acc", None)
+    if acc is None or acc.shape != w.shape or acc.dtype != torch.float32 or acc.stride(-1) != 1:
+        return None
+    return acc
+
+
+class _PairLinearFn(torch.autograd.Function):
+    """y = x W^T with all three GEMMs on the CTA-pair tcgen05 kernel, each operand
+    read where it lies: forward (x, W K-major), dgrad dY W (W MN-major), wgrad
+    dY^T x (dY and x MN-major) -- accumulated in fp32 into the weight's gradient
+    buffer when the engine provides one."""
+
+    @staticmethod
+    def forward(ctx, x2d, w, acc):
+        from llm_research_b200.ops.gemm import linear_fwd
+
+        ctx.save_for_backward(x2d, w)
+        ctx.acc = acc
+        return linear_fwd(x2d, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from llm_research_b200.ops.gemm import linear_dgrad, linear_wgrad
+
+        x2d, w = ctx.saved_tensors
+        dy = _rows(dy)
+        dx = linear_dgrad(dy, w) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            if ctx.acc is not None:
+                linear_wgrad(dy, x2d, out=ctx.acc, accumulate=True)
+                dw = accumulated_marker(w)
+            else:
+                dw = linear_wgrad(dy, x2d)
+        ctx.acc = None
+        return dx, dw, None
+
+
+def _aligned_rows(t: torch.Tensor) -> bool:
+    return t.dim() == 2 and t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
+
+
+def _rows(t: torch.Tensor) -> torch.Tensor:
+    """``t`` as a 2-D matrix with unit column stride and a 16-byte aligned row pitch."""
+    return t if _aligned_rows(t) else t.contiguous()
+
+
+def _pair_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """Shapes the pair kernel takes: 16-bit CUDA operands of one dtype, the weight's
+    row pitch and both of its dimensions multiples of 8 elements (its rows are the
+    K-major B of the forward, its columns the MN-major B of dgrad; the output
+    width is the MN-major A pitch of wgrad)."""
+    return (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype and w.dim() == 2
+            and w.shape[0] % 8 == 0 and w.shape[1] % 8 == 0 and _aligned_rows(w) and x.shape[-1] == w.shape[1])
+
+
+def linear_bf16(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x @ w.T`` over the last dimension of ``x`` on the pair kernel (no bias)."""
+    x2d = _rows(x.reshape(-1, x.shape[-1]))
+    acc = _acc_of(w) if torch.is_grad_enabled() and w.requires_grad else None
+    return _PairLinearFn.apply(x2d, w, acc).view(*x.shape[:-1], w.shape[0])
+
+
+def dense(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.linear`` in the input precision whatever the linear precision (the output
+    head stays bf16 under NVFP4 training): the pair kernel where it applies."""
+    if x.numel() > 0 and _pair_ok(x, w):
+        y = linear_bf16(x, w)
+        return y + b if b is not None else y
+    return F.linear(x, w, b)
+
+
 def _fp4_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
     T = x.numel() // x.shape[-1]
     return (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and w.shape[1] % 256 == 0
@@ -129,9 +244,14 @@ def _fp4_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
 
 
 def project(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
-    """``F.linear`` under the current linear precision (NVFP4 where the shapes allow it:
-    K, N and the token count multiples of 256; bf16 otherwise)."""
+    """``F.linear`` under the current linear precision: NVFP4 block-scaled GEMMs where
+    the shapes allow it (K, N and the token count multiples of 256), otherwise the
+    bf16/fp16 CTA-pair kernel on CUDA (K and N multiples of 8); PyTorch for CPU
+    tensors, fp32 and the remaining shapes."""
     if _PRECISION == "nvfp4" and _fp4_ok(x, w):
         y = _NVFP4LinearFn.apply(x.reshape(-1, x.shape[-1]), w).view(*x.shape[:-1], w.shape[0])
+        return y + b if b is not None else y
+    if x.numel() > 0 and _pair_ok(x, w):
+        y = linear_bf16(x, w)
         return y + b if b is not None else y
     return F.linear(x, w, b)

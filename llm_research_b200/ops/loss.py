@@ -27,6 +27,7 @@ import torch.nn.functional as F
 import torch.distributed as dist
 
 from llm_research_b200._ext import native
+from llm_research_b200.ops.linear import _pair_ok, _rows
 
 
 class _CEFn(torch.autograd.Function):
@@ -80,9 +81,12 @@ class _LinearCEFn(torch.autograd.Function):
         loss_sum = torch.zeros((), dtype=torch.float32, device=h.device)
         dh = torch.empty_like(h) if need_h else None
         dw = torch.zeros(V, d, dtype=torch.float32, device=h.device) if need_w else None
+        pair = h.is_cuda and _pair_ok(h, w)
+        if pair:
+            from llm_research_b200.ops.gemm import linear_dgrad, linear_fwd, linear_wgrad
         for s in range(0, N, chunk):
             hc, tc = h[s:s + chunk], targets[s:s + chunk].contiguous()
-            logits = F.linear(hc, w)
+            logits = linear_fwd(_rows(hc), w) if pair else F.linear(hc, w)
             if logits.is_cuda:
                 ls, _, lse = native().ce_fwd(logits.contiguous(), tc, int(ignore_index))
                 loss_sum += ls.reshape(())
@@ -99,9 +103,15 @@ class _LinearCEFn(torch.autograd.Function):
                     p[torch.arange(p.shape[0]), tc.clamp(0, V - 1)] -= 1.0
                     dl = (p * (valid.float() * inv)[:, None]).to(logits.dtype)
             if need_h:
-                dh[s:s + chunk] = dl @ w
+                if pair:
+                    linear_dgrad(dl, w, out=dh[s:s + chunk])
+                else:
+                    dh[s:s + chunk] = dl @ w
             if need_w:
-                dw += (dl.t() @ hc).float()
+                if pair:  # fp32 accumulation in the GEMM epilogue
+                    linear_wgrad(dl, _rows(hc), out=dw, accumulate=True)
+                else:
+                    dw += (dl.t() @ hc).float()
             del logits
         ctx.save_for_backward(dh, dw)
         ctx.w_dtype = w.dtype
@@ -159,8 +169,11 @@ class _VocabParallelLinearCEFn(torch.autograd.Function):
         empty = v1 == v0  # V < world * ceil(V / world): the last ranks own no rows
         if empty:
             stats[0].fill_(float("-inf"))  # log-sum-exp over an empty set of logits
+        pair = h.is_cuda and not empty and _pair_ok(h, w_loc)
+        if pair:
+            from llm_research_b200.ops.gemm import linear_dgrad, linear_fwd, linear_wgrad
         for s in range(0, 0 if empty else N, chunk):
-            lg = F.linear(h[s:s + chunk], w_loc).contiguous()
+            lg = linear_fwd(_rows(h[s:s + chunk]), w_loc) if pair else F.linear(h[s:s + chunk], w_loc).contiguous()
             tc = t_loc[s:s + chunk].contiguous()
             if lg.is_cuda:
                 _, _, lse = native().ce_fwd(lg, tc, int(ignore_index))
@@ -194,9 +207,15 @@ class _VocabParallelLinearCEFn(torch.autograd.Function):
                 p[rows, tc[own]] -= 1.0
                 dl = (p * (valid[s:s + chunk].float() * inv)[:, None]).to(lg.dtype)
             if need_h:
-                dh[s:s + chunk] = dl @ w_loc
+                if pair:
+                    linear_dgrad(dl, w_loc, out=dh[s:s + chunk])
+                else:
+                    dh[s:s + chunk] = dl @ w_loc
             if need_w:
-                dw[: v1 - v0] += (dl.t() @ h[s:s + chunk]).float()
+                if pair:
+                    linear_wgrad(dl, _rows(h[s:s + chunk]), out=dw[: v1 - v0], accumulate=True)
+                else:
+                    dw[: v1 - v0] += (dl.t() @ h[s:s + chunk]).float()
             logits[i] = None
         ctx.save_for_backward(dh, dw)
         ctx.group, ctx.V, ctx.w_dtype = group, V, w.dtype

@@ -118,7 +118,11 @@ class _GradSink(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad):
-        ctx.engine._accumulate(ctx.key[0], ctx.key[1], grad)
+        from llm_research_b200.ops.linear import is_accumulated_marker
+
+        # The marker means the producing GEMM already added this gradient into the
+        # accumulator (see llm_research_b200.ops.linear): bookkeeping only.
+        ctx.engine._accumulate(ctx.key[0], ctx.key[1], None if is_accumulated_marker(grad) else grad)
         return None, None, None, None, None
 
 
@@ -426,8 +430,9 @@ class FlatShardEngine(nn.Module):
         self._begin_backward()
         u = self.units[ui]
         info = u.params[pidx]
-        dst = u.grad_acc[info.offset: info.offset + info.numel].view(info.shape)
-        dst.add_(grad)  # bf16 -> fp32 accumulate in one pass (no separate cast)
+        if grad is not None:
+            dst = u.grad_acc[info.offset: info.offset + info.numel].view(info.shape)
+            dst.add_(grad)  # bf16 -> fp32 accumulate in one pass (no separate cast)
         u.grads_seen.add(pidx)
         self._touched.add(info.index)
         if len(u.grads_seen) == len(u.params):
@@ -527,7 +532,14 @@ class FlatShardEngine(nn.Module):
         for u in self.units:
             for pidx, info in enumerate(u.params):
                 v = u.views[info.name]
-                tensors[info.name] = _GradSink.apply(self._anchor, v, self, u.index, pidx) if grad else v
+                if grad:
+                    t = _GradSink.apply(self._anchor, v, self, u.index, pidx)
+                    # fp32 accumulator view: GEMMs that produce this weight's gradient
+                    # may add into it directly (llm_research_b200.ops.linear)
+                    t._lrb_acc = u.grad_acc[info.offset: info.offset + info.numel].view(info.shape)
+                    tensors[info.name] = t
+                else:
+                    tensors[info.name] = v
         self._active = True
         try:
             out = torch.func.functional_call(self.module, tensors, args, kwargs, strict=False, tie_weights=True)

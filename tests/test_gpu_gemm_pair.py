@@ -104,3 +104,85 @@ def test_linear_gemms_match_fp32():
                      (acc, dy.float().t() @ x.float())):
         err = ((got.float() - ref).norm() / ref.norm()).item()
         assert err < 1e-2, err
+
+
+@pytest.mark.gpu
+def test_engine_direct_wgrad_accumulation_matches_returned_grads():
+    """The sharding engine's fp32 gradient buffers after one bf16 micro-step: wgrad
+    accumulated by the pair kernel straight into them equals dW returned through
+    autograd and added by the engine, and both track an fp32 model."""
+    import copy
+
+    from genesis.model.hlrt import HLRT
+    from llm_research_b200.models.presets import build_hlrt_config
+    from llm_research_b200.ops.linear import set_direct_grad_accumulation
+    from llm_research_b200.parallel.fsdp import FlatShardEngine
+
+    cfg = build_hlrt_config("toy")
+    torch.manual_seed(0)
+    base = HLRT(cfg).cuda()
+    ids = torch.randint(0, cfg.vocab_size, (2, 128), device="cuda", generator=torch.Generator(device="cuda").manual_seed(3))
+
+    def grads(direct):
+        set_direct_grad_accumulation(direct)
+        try:
+            eng = FlatShardEngine(copy.deepcopy(base), compute_dtype=torch.bfloat16)
+            out = eng(ids)
+            loss = torch.nn.functional.cross_entropy(out["logits"].float().flatten(0, 1), ids.flatten())
+            (loss + out["aux_loss"]).backward()
+            torch.cuda.synchronize()
+            return {info.name: eng.units[info.unit].grad_acc[info.offset: info.offset + info.numel].clone()
+                    for info in eng.params}
+        finally:
+            set_direct_grad_accumulation(True)
+
+    direct, returned = grads(True), grads(False)
+    ref_model = copy.deepcopy(base).float()
+    out = ref_model(ids)
+    (torch.nn.functional.cross_entropy(out["logits"].flatten(0, 1), ids.flatten()) + out["aux_loss"]).backward()
+    ref = {n: p.grad.reshape(-1) for n, p in ref_model.named_parameters() if p.grad is not None}
+    checked = 0
+    for name, g in direct.items():
+        r = returned[name]
+        if r.norm() == 0:
+            continue
+        assert ((g - r).norm() / r.norm()).item() < 1e-2, name
+        if name in ref:
+            assert ((g - ref[name]).norm() / (ref[name].norm() + 1e-12)).item() < 5e-2, name
+        checked += 1
+    assert checked > 10
+
+
+@pytest.mark.gpu
+def test_gemm_pair_split_k_accumulation():
+    """Few output tiles and a long K: the accumulating GEMM splits K over several
+    CTA pairs whose partial sums meet in C through TMA reduce-adds."""
+    from llm_research_b200.ops.gemm import gemm, gemm_pair_error
+
+    A, B = _operands(512, 512, 8192, True, True, torch.bfloat16, seed=9)
+    C0 = torch.randn(512, 512, device="cuda")
+    C = C0.clone()
+    gemm(A, B, True, True, out=C, accumulate=True, alpha=0.25)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    ref = C0 + 0.25 * _ref(A, B, True, True)
+    torch.testing.assert_close(C, ref, atol=5e-2, rtol=1e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_gemm_pair_unaligned_output_takes_direct_stores(out_dtype):
+    """An output whose base is not 16-byte aligned cannot be a TMA target: the
+    epilogue stores from registers instead."""
+    from llm_research_b200.ops.gemm import gemm, gemm_pair_error
+
+    A, B = _operands(300, 264, 136, False, False, torch.bfloat16, seed=13)
+    Cbuf = torch.zeros(300, 272, device="cuda", dtype=out_dtype)
+    C = Cbuf[:, 1:265]
+    gemm(A, B, out=C)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    ref = _ref(A, B, False, False)
+    err = ((C.float() - ref).norm() / ref.norm()).item()
+    assert err < 1e-2, err
+    assert Cbuf[:, 0].abs().sum().item() == 0 and Cbuf[:, 265:].abs().sum().item() == 0
