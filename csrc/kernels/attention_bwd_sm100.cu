@@ -345,25 +345,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------ v3: 64-query sub-tiles
-// CTA = (batch, kv-head, 128 keys); query sub-tiles of 64 rows, double-buffered
-// end to end so the MMAs of sub-tile t+1 overlap the softmax-gradient and the
-// dQ epilogue of sub-tile t.  TMEM (512 columns):
+// CTA = (batch, kv-head, 128 keys); query sub-tiles of 64 rows.  TMEM (512 columns):
 //   S^T_b  [b*128, b*128+64)   keys x 64 queries, later dQ^T_b (hd x 64 queries)
 //   dP^T_b [b*128+64, b*128+128)
 //   dV [256, 384), dK [384, 512)
 // dQ^T = K^T dS^T is written over S^T_b once the softmax warps have read it,
-// so dQ needs no columns of its own.  Warps: 0 TMA (K, V once; Q, dO and the
-// LSE / D of each sub-tile into one of two buffers), 1 MMA issue, 2..9
-// softmax-gradient (two threads per key row, 32 queries each), 10..13 dQ
-// epilogue (one thread per head-dim lane; staged boxes, TMA reduce-adds).
+// so dQ needs no columns of its own.  TMEM and the P^T / dS^T tiles are
+// double-buffered (b = t & 1); Q, dO and their LSE / D rows sit in a ring of
+// three slots (t % 3), so the producer fills sub-tile t+2 while t and t+1 are in
+// use and no refill (TMA or the LSE / D loads) lies between the MMAs of one
+// sub-tile and the next.  The dQ epilogue stages its fp32 boxes in the P^T /
+// dS^T tiles of its buffer, which the MMAs have finished reading by then; the
+// softmax warps wait for that staging's TMA read (stage_free) before they
+// write the buffer again.  Warps: 0 TMA, 1 MMA issue, 2..9 softmax-gradient (two
+// threads per key row, 32 queries each), 10..13 dQ epilogue (one thread per
+// head-dim lane; TMA reduce-adds).
 namespace bwd3 {
 constexpr int TQ3 = 64;
 constexpr int kThreads = 448;
+constexpr int kRing = 3;                            // Q / dO slots
 constexpr uint32_t kKV = 32768, kKVHalf = 16384;   // K or V tile, 64-column half
 constexpr uint32_t kQ = 16384, kQHalf = 8192;       // Q or dO sub-tile, half
 constexpr uint32_t kPT = 16384;                     // P^T or dS^T: 128 keys x 64 queries
-constexpr uint32_t kDq = 128 * TQ3 * 4;            // dQ staging: 4 boxes of 32 head dims x 64 queries (fp32)
-constexpr size_t kSmem = 1024 + 2 * kKV + 4 * (size_t)kQ + 4 * (size_t)kPT + 2048 + kDq;
+constexpr uint32_t kPD = 2 * kPT;                   // [P^T | dS^T] of one buffer; also the dQ staging:
+                                                    // 4 boxes of 32 head dims x 64 queries (fp32)
+constexpr size_t kSmem = 1024 + 2 * kKV + 2 * kRing * (size_t)kQ + 2 * (size_t)kPD + 2048;
+static_assert(kSmem <= 232448, "attention backward: shared memory over the 227 KB limit");
 }  // namespace bwd3
 
 __global__ void __launch_bounds__(bwd3::kThreads, 1)
@@ -375,24 +382,23 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sK = base;
   unsigned char* sV = base + kKV;
-  unsigned char* sQ = base + 2 * kKV;              // [2]
-  unsigned char* sdO = sQ + 2 * kQ;                // [2]
-  unsigned char* sPt = sdO + 2 * kQ;               // [2]
-  unsigned char* sdSt = sPt + 2 * kPT;             // [2]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sdSt + 2 * kPT);
+  unsigned char* sQ = base + 2 * kKV;              // [kRing]
+  unsigned char* sdO = sQ + kRing * kQ;            // [kRing]
+  unsigned char* sPD = sdO + kRing * kQ;           // [2] x (P^T | dS^T), later the dQ staging
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sPD + 2 * kPD);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;    // [2]
-  uint64_t* qd_free = bars + 3;    // [2]
-  uint64_t* sdp_full = bars + 5;   // [2]
-  uint64_t* p_full = bars + 7;     // [2]
-  uint64_t* dq_full = bars + 9;    // [2]
-  uint64_t* dq_free = bars + 11;   // [2]
-  uint64_t* acc_done = bars + 13;
-  uint64_t* drain = bars + 14;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  float* sL = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(bars) + 1024);  // [2][64]
-  float* sD = sL + 2 * TQ3;                                                           // [2][64]
-  unsigned char* sDQ = reinterpret_cast<unsigned char*>(bars) + 2048;  // 4 x (64 rows x 128 B), swizzled
+  uint64_t* qd_full = bars + 1;     // [kRing]
+  uint64_t* qd_free = bars + 4;     // [kRing]
+  uint64_t* sdp_full = bars + 7;    // [2]
+  uint64_t* p_full = bars + 9;      // [2]
+  uint64_t* dq_full = bars + 11;    // [2]
+  uint64_t* dq_free = bars + 13;    // [2]
+  uint64_t* stage_free = bars + 15; // [2]
+  uint64_t* acc_done = bars + 17;
+  uint64_t* drain = bars + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  float* sL = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(bars) + 512);  // [kRing][64]
+  float* sD = sL + kRing * TQ3;                                                       // [kRing][64]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * TK;
@@ -405,13 +411,16 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kRing; ++i) {
       mbar_init(&qd_full[i], 32);
       mbar_init(&qd_free[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&sdp_full[i], 1);
       mbar_init(&p_full[i], 256);
       mbar_init(&dq_full[i], 1);
       mbar_init(&dq_free[i], 128);
+      mbar_init(&stage_free[i], 1);
     }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
@@ -443,37 +452,36 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       }
       int loaded = 0;
       for (int t = 0; t < total; ++t) {
-        const int bb = t & 1;
-        const uint32_t use = (t >> 1) & 1;
+        const int sl = t % kRing;
+        const uint32_t use = (uint32_t)(t / kRing) & 1;
         const int h = hk * G + t / nqt;
         const int q0 = (qt0 + t % nqt) * TQ3;
-        if (!__all_sync(0xffffffffu, mbar_wait(&qd_free[bb], use ^ 1, a.err, kErrTmaWait))) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(&qd_free[sl], use ^ 1, a.err, kErrTmaWait))) break;
+        if (lane == 0) {
+          mbar_expect_tx(&qd_full[sl], 2 * kQ);  // the 32 arrivals come after the LSE / D staging
+          unsigned char* q_ = sQ + sl * kQ;
+          unsigned char* o_ = sdO + sl * kQ;
+          tma_load_4d(q_, &tmQ, &qd_full[sl], 0, h, q0, b);
+          tma_load_4d(q_ + kQHalf, &tmQ, &qd_full[sl], 64, h, q0, b);
+          tma_load_4d(o_, &tmdO, &qd_full[sl], 0, h, q0, b);
+          tma_load_4d(o_ + kQHalf, &tmdO, &qd_full[sl], 64, h, q0, b);
+        }
         const float* lse_row = a.lse + ((int64_t)b * a.H + h) * a.Sq;
         const float* di_row = a.di + ((int64_t)b * a.H + h) * a.Sq;
 #pragma unroll
         for (int i = 0; i < TQ3 / 32; ++i) {
           const int c = i * 32 + lane, q = q0 + c;
-          sL[bb * TQ3 + c] = q < a.Sq ? lse_row[q] * kLog2e : 0.f;
-          sD[bb * TQ3 + c] = q < a.Sq ? di_row[q] : 0.f;
+          sL[sl * TQ3 + c] = q < a.Sq ? lse_row[q] * kLog2e : 0.f;
+          sD[sl * TQ3 + c] = q < a.Sq ? di_row[q] : 0.f;
         }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&qd_full[bb], 2 * kQ);
-          unsigned char* q_ = sQ + bb * kQ;
-          unsigned char* o_ = sdO + bb * kQ;
-          tma_load_4d(q_, &tmQ, &qd_full[bb], 0, h, q0, b);
-          tma_load_4d(q_ + kQHalf, &tmQ, &qd_full[bb], 64, h, q0, b);
-          tma_load_4d(o_, &tmdO, &qd_full[bb], 0, h, q0, b);
-          tma_load_4d(o_ + kQHalf, &tmdO, &qd_full[bb], 64, h, q0, b);
-        } else {
-          mbar_arrive(&qd_full[bb]);
-        }
+        mbar_arrive(&qd_full[sl]);  // release: the LSE / D rows above are visible to the waiters
         ++loaded;
       }
       if (lane == 0) {
         mbar_wait(kv_full, 0, nullptr, 0);
-        for (int i = 1; i <= 2 && i <= loaded; ++i) {
+        for (int i = 1; i <= kRing && i <= loaded; ++i) {
           const int t = loaded - i;
-          mbar_wait(&qd_full[t & 1], (t >> 1) & 1, nullptr, 0);
+          mbar_wait(&qd_full[t % kRing], (uint32_t)(t / kRing) & 1, nullptr, 0);
         }
       }
     }
@@ -486,12 +494,12 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       const uint32_t k_ = smem_addr(sK), v_ = smem_addr(sV);
       bool ok = mbar_wait(kv_full, 0, a.err, kErrMmaWait);
       auto issue_sdp = [&](int t) -> bool {
-        const int bb = t & 1;
+        const int bb = t & 1, sl = t % kRing;
         const uint32_t use = (t >> 1) & 1;
-        if (!mbar_wait(&qd_full[bb], use, a.err, kErrMmaWait)) return false;
+        if (!mbar_wait(&qd_full[sl], (uint32_t)(t / kRing) & 1, a.err, kErrMmaWait)) return false;
         if (t >= 2 && !mbar_wait(&dq_free[bb], use ^ 1, a.err, kErrMmaWait)) return false;  // dQ^T(t-2) read out
         tc_fence_after();
-        const uint32_t q_ = smem_addr(sQ + bb * kQ), o_ = smem_addr(sdO + bb * kQ);
+        const uint32_t q_ = smem_addr(sQ + sl * kQ), o_ = smem_addr(sdO + sl * kQ);
         const uint32_t tS = tmem + bb * 128, tP = tS + 64;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
@@ -504,13 +512,13 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       };
       if (ok) ok = issue_sdp(0);
       for (int t = 0; t < total && ok; ++t) {
-        const int bb = t & 1;
+        const int bb = t & 1, sl = t % kRing;
         const uint32_t use = (t >> 1) & 1;
         if (t + 1 < total && !issue_sdp(t + 1)) { ok = false; break; }
         if (!mbar_wait(&p_full[bb], use, a.err, kErrMmaWait)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t q_ = smem_addr(sQ + bb * kQ), o_ = smem_addr(sdO + bb * kQ);
-        const uint32_t pt_ = smem_addr(sPt + bb * kPT), ds_ = smem_addr(sdSt + bb * kPT);
+        const uint32_t q_ = smem_addr(sQ + sl * kQ), o_ = smem_addr(sdO + sl * kQ);
+        const uint32_t pt_ = smem_addr(sPD + bb * kPD), ds_ = pt_ + kPT;
 #pragma unroll
         for (int k = 0; k < TQ3 / 16; ++k) {  // dV += P^T dO ; dK += dS^T Q
           umma_f16(tdV, umma_desc_k_sw128(pt_ + k * 32), umma_desc_mn_sw128(o_ + k * 2048, kQHalf, 1024), id_acc,
@@ -518,7 +526,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
           umma_f16(tdK, umma_desc_k_sw128(ds_ + k * 32), umma_desc_mn_sw128(q_ + k * 2048, kQHalf, 1024), id_acc,
                    (t | k) != 0);
         }
-        umma_commit(&qd_free[bb]);
+        umma_commit(&qd_free[sl]);
 #pragma unroll
         for (int k = 0; k < TK / 16; ++k)  // dQ^T = K^T dS^T  (into the consumed S^T_b columns)
           umma_f16(tmem + bb * 128, umma_desc_mn_sw128(k_ + k * 2048, kKVHalf, 1024),
@@ -538,10 +546,14 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
     const int c0 = half * 32;
     bool ok = true;
     for (int t = 0; t < total && ok; ++t) {
-      const int bb = t & 1;
+      const int bb = t & 1, sl = t % kRing;
       const uint32_t use = (t >> 1) & 1;
       const int q0 = (qt0 + t % nqt) * TQ3;
-      if (!mbar_wait(&sdp_full[bb], use, a.err, kErrEpiWait) || !mbar_wait(&qd_full[bb], use, a.err, kErrEpiWait)) {
+      // S^T / dP^T in TMEM, the LSE / D rows, and (from t = 2) the TMA read of the
+      // dQ staging that last used this buffer's P^T / dS^T tiles
+      if (!mbar_wait(&sdp_full[bb], use, a.err, kErrEpiWait) ||
+          !mbar_wait(&qd_full[sl], (uint32_t)(t / kRing) & 1, a.err, kErrEpiWait) ||
+          (t >= 2 && !mbar_wait(&stage_free[bb], use ^ 1, a.err, kErrEpiWait))) {
         ok = false;
         break;
       }
@@ -550,8 +562,8 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + c0, reinterpret_cast<uint32_t*>(s));
       tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + 64 + c0, reinterpret_cast<uint32_t*>(dp));
       tmem_ld_wait();
-      const float* L = sL + bb * TQ3 + c0;
-      const float* Dd = sD + bb * TQ3 + c0;
+      const float* L = sL + sl * TQ3 + c0;
+      const float* Dd = sD + sl * TQ3 + c0;
       uint32_t pp[16], dd[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
@@ -567,8 +579,8 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
         pp[i / 2] = pack2(pv[0], pv[1]);
         dd[i / 2] = pack2(dv2[0], dv2[1]);
       }
-      unsigned char* pt = sPt + bb * kPT;
-      unsigned char* ds = sdSt + bb * kPT;
+      unsigned char* pt = sPD + bb * kPD;
+      unsigned char* ds = pt + kPT;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int ch = half * 4 + j;
@@ -621,18 +633,18 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
     const int d = quarter * 32 + lane;  // head-dim index (TMEM lane of dQ^T)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const bool issuer = quarter == 0 && lane == 0;
-    unsigned char* box = sDQ + (d >> 5) * (TQ3 * 128);
     const int chunk = (d & 31) >> 2, sub = (d & 3) * 4;
     for (int t = 0; t < total; ++t) {
       const int bb = t & 1;
       const uint32_t use = (t >> 1) & 1;
       const int h = hk * G + t / nqt;
       const int q0 = (qt0 + t % nqt) * TQ3;
+      // dq_full: dQ^T(t) is in TMEM, and every MMA of sub-tile t -- the last readers
+      // of this buffer's P^T / dS^T tiles, the staging area -- has completed
       if (!group_all(1, mbar_wait(&dq_full[bb], use, a.err, kErrEpiWait))) break;
       tc_fence_after();
-      // the previous sub-tile's reduce-adds have finished reading the staging boxes
-      if (issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      unsigned char* sDQ = sPD + bb * kPD;  // 4 x (64 rows x 128 B), swizzled
+      unsigned char* box = sDQ + (d >> 5) * (TQ3 * 128);
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
@@ -655,6 +667,9 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
               "r"(smem_addr(sDQ + j * (TQ3 * 128))), "r"(h * HD + j * 32), "r"(b * a.Sq + q0)
               : "memory");
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        // the reduce-adds have read the staging: the softmax warps may overwrite it
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        mbar_arrive(&stage_free[bb]);
       }
     }
     if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");

@@ -45,7 +45,11 @@ class TopDownConditioning(nn.Module):
         tier3_out: torch.Tensor,
         tier2_mask: torch.Tensor,
         tier3_mask: torch.Tensor,
+        fixed: bool = False,
     ) -> torch.Tensor:
+        """``fixed`` (an extension): Tier 3 ran on the fixed-capacity buffer of all
+        ``C`` chunk slots; the slot mapping is computed at that width, with no host
+        read, and selects the same chunks."""
         if tier3_out is None or tier3_out.numel() == 0:
             return tier1_out
         B, S, D = tier1_out.shape
@@ -54,7 +58,11 @@ class TopDownConditioning(nn.Module):
         chunk_cond = self.tier3_proj(tier3_out).mean(dim=2)  # (B, N3, D)
 
         sel2 = tier2_mask if tier2_mask.dtype == torch.bool else tier2_mask > 0.5
-        t2_idx, t2_valid, n2 = ops.compact_chunks(sel2)  # (B, n2)
+        if fixed:  # all C slots; slots past the reference's count are never valid
+            t2_idx, t2_valid, _, _ = ops.compact_chunks_fixed(sel2)
+            n2 = t2_idx.shape[1]
+        else:
+            t2_idx, t2_valid, n2 = ops.compact_chunks(sel2)  # (B, n2)
         C = sel2.shape[1]
         sel3 = tier3_mask if tier3_mask.dtype == torch.bool else tier3_mask > 0.5
         width = min(n2, sel3.shape[1])
@@ -77,5 +85,12 @@ class TopDownConditioning(nn.Module):
             return x[:, :S]
         return torch.cat([x, tier1_out[:, C * cs:]], dim=1)
 
-    def compute_plan_vector(self, tier2_out: torch.Tensor) -> torch.Tensor:
-        return self.plan_proj(tier2_out.mean(dim=(1, 2)))
+    def compute_plan_vector(self, tier2_out: torch.Tensor, n_slots: torch.Tensor | None = None) -> torch.Tensor:
+        """``n_slots`` (a device scalar, an extension): average over the first
+        ``n_slots`` chunk slots only (the fixed-capacity escalation path)."""
+        if n_slots is None:
+            return self.plan_proj(tier2_out.mean(dim=(1, 2)))
+        B, N, L, D = tier2_out.shape
+        m = (torch.arange(N, device=tier2_out.device) < n_slots).to(tier2_out.dtype)
+        mean = (tier2_out * m[None, :, None, None]).sum(dim=(1, 2)) / (n_slots.to(tier2_out.dtype) * L)
+        return self.plan_proj(mean)

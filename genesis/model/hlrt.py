@@ -180,6 +180,58 @@ class HLRT(StatefulModule):
             plan = plan[:1].expand(batch, -1)
         return plan
 
+    # ------------------------------------------------------------------
+    # Escalation without host reads.  The reference decides on the host whether
+    # any chunk escalates (``bool(mask.any())``) and sizes the latent buffer by the
+    # largest per-sample count (another host read).  Here Tiers 2/3 always run on a
+    # buffer of all C chunk slots and the decisions are device-side selects:
+    #   * slots past the reference's count n (a device scalar) hold zero latents and
+    #     come after every real slot, so the causal Tier-2/3 transformers leave the
+    #     first n slots exactly as the reference computes them;
+    #   * the plan averages the first n slots and the Tier-2 gate's balance loss
+    #     counts the first n * L latent positions only;
+    #   * "nothing escalated" selects the cached-plan path with torch.where (the
+    #     other branch gets zero gradient), and the stored plan is updated only
+    #     when something escalated.
+    # Tier-2 MoE balances its router over every token it sees, so with a Tier-2
+    # MoE the reference path (with its host reads) is kept.
+    fixed_escalation = True
+
+    def _fixed_escalation(self) -> bool:
+        return self.fixed_escalation and not self.config.tier2_moe_num_experts
+
+    def _escalate_fixed(self, t1, g1_mask, sel1, acts, keep_acts):
+        B = t1.shape[0]
+        L = self.config.num_latent_vectors
+        any1 = sel1.any()
+        latents, n1 = self.latent_pool.forward_fixed(t1, g1_mask)
+        if keep_acts:
+            acts["latent_vectors"] = latents
+        t2 = self.tier2(latents)
+        if keep_acts:
+            acts["tier2"] = t2
+        plan = self.conditioning.compute_plan_vector(t2, n1)
+        cached = self._cached_plan(B)
+        old = self.get_state("last_plan_vector")
+        new = plan.detach().mean(dim=0, keepdim=True).to(old.dtype)
+        self.set_state("last_plan_vector", torch.where(any1, new, old))
+        t1_plan = self.conditioning.apply_cached_plan(t1, plan)
+
+        g2_mask, g2_scores = self.gate2(t2.reshape(B, -1, self.config.tier2_d_model))
+        if keep_acts:
+            acts["gate2_scores"] = g2_scores
+        aux = self.config.gate_loss_weight * self.gate2.load_balance_loss(valid_len=n1 * L)
+        sel2 = g2_mask if g2_mask.dtype == torch.bool else g2_mask > 0.5
+        live = torch.arange(sel2.shape[1], device=sel2.device) < n1 * L
+        any2 = (sel2 & live).any()
+        t3 = self.tier3(t2)
+        if keep_acts:
+            acts["tier3"] = t3
+        t1_t3 = self.conditioning.integrate_tier3(t1_plan, t3, g1_mask, g2_mask, fixed=True)
+        t1_esc = torch.where(any2, t1_t3, t1_plan)
+        t1_out = torch.where(any1, t1_esc, self.conditioning.apply_cached_plan(t1, cached))
+        return t1_out, aux * any1.to(aux.dtype)
+
     def _head(self, h: torch.Tensor) -> torch.Tensor:
         w = self.output_proj.weight if self.output_proj is not None else self.embeddings.weight
         return dense(h, w)
@@ -239,7 +291,10 @@ class HLRT(StatefulModule):
             for layer in self.tier1.layers:
                 aux = aux + self.config.moe_loss_weight * layer.ffn.load_balance_loss().to(aux.device)
 
-        if bool(sel1.any()):
+        if self._fixed_escalation():
+            t1, aux_esc = self._escalate_fixed(t1, g1_mask, sel1, acts, return_tier_activations)
+            aux = aux + aux_esc
+        elif bool(sel1.any()):
             latents = self.latent_pool(t1, g1_mask)
             if return_tier_activations:
                 acts["latent_vectors"] = latents

@@ -56,14 +56,30 @@ class LatentPooling(nn.Module):
         self.norm = nn.LayerNorm(output_dim)
 
     def forward(self, x: torch.Tensor, chunk_mask: torch.Tensor) -> torch.Tensor:
-        B, S, _ = x.shape
+        x, C, sel = self._chunks(x, chunk_mask)
+        idx, valid, n_max = ops.compact_chunks(sel)  # (B, N) chunk ids (C = padding), (B, N) bool
+        return self._pool(x, C, idx, valid, n_max)
+
+    def forward_fixed(self, x: torch.Tensor, chunk_mask: torch.Tensor):
+        """The same pooling into all ``C`` chunk slots (no host read of the slot
+        count): returns ``(out (B, C, L, d2), n)`` where the first ``n`` slots (a
+        device scalar) are exactly ``forward``'s output and the rest are zero."""
+        x, C, sel = self._chunks(x, chunk_mask)
+        idx, valid, _, n = ops.compact_chunks_fixed(sel)
+        return self._pool(x, C, idx, valid, C), n
+
+    def _chunks(self, x: torch.Tensor, chunk_mask: torch.Tensor):
+        S = x.shape[1]
         cs = self.chunk_size
         pad = (-S) % cs
         if pad:
             x = F.pad(x, (0, 0, 0, pad))
-        C = x.shape[1] // cs
         sel = chunk_mask if chunk_mask.dtype == torch.bool else chunk_mask > 0.5
-        idx, valid, n_max = ops.compact_chunks(sel)  # (B, N) chunk ids (C = padding), (B, N) bool
+        return x, x.shape[1] // cs, sel
+
+    def _pool(self, x: torch.Tensor, C: int, idx: torch.Tensor, valid: torch.Tensor, n_max: int) -> torch.Tensor:
+        B = x.shape[0]
+        cs = self.chunk_size
         chunks = x.view(B, C, cs, self.input_dim)
         chunks = torch.cat([chunks, chunks.new_zeros(B, 1, cs, self.input_dim)], dim=1)
         gathered = chunks[torch.arange(B, device=x.device)[:, None], idx]  # (B, N, cs, d1)

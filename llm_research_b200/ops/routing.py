@@ -11,6 +11,9 @@
   ``(B, C)`` mask to the front: returns ``ids (B, N)`` (unused slots hold
   ``C``), ``valid (B, N)`` and ``N = max(max row count, 1)``.  One kernel does
   the per-row prefix sum and scatter; ``N`` is the only host read.
+* :func:`compact_chunks_fixed` -- the same packing at the fixed width ``C``
+  (every chunk could be selected), with the row counts and ``N`` left on the
+  device: no host read, so the escalation path never stalls the launch queue.
 """
 
 from __future__ import annotations
@@ -97,3 +100,24 @@ def compact_chunks(mask: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, int]
         ids = ids[:, :n]
     valid = torch.arange(n, device=mask.device)[None, :] < counts[:, None]
     return ids, valid, n
+
+
+def compact_chunks_fixed(mask: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``(ids (B, C), valid (B, C), counts (B,), n (0-d))`` for a bool ``(B, C)`` mask:
+    selected chunk ids packed to the front in ascending order, unused slots ``C``;
+    ``n = max(max row count, 1)`` as a device scalar (the reference's slot count)."""
+    B, C = mask.shape
+    if mask.is_cuda:
+        ids, counts = native().compact_chunks(mask.contiguous())
+        ids = ids[:, :C]
+    else:
+        counts = mask.sum(-1)
+        rank = torch.cumsum(mask.to(torch.int64), dim=1) - 1
+        pos = torch.where(mask, rank, torch.full_like(rank, C))
+        ids = torch.full((B, C + 1), C, dtype=torch.long, device=mask.device)
+        ids.scatter_(1, pos, torch.arange(C, device=mask.device).expand(B, C).contiguous())
+        ids = ids[:, :C]
+    counts = counts.to(torch.int64)
+    valid = torch.arange(C, device=mask.device)[None, :] < counts[:, None]
+    n = counts.max().clamp_min(1) if B > 0 else torch.ones((), dtype=torch.int64, device=mask.device)
+    return ids.to(torch.long), valid, counts, n

@@ -137,10 +137,10 @@ def test_engine_direct_wgrad_accumulation_matches_returned_grads():
             set_direct_grad_accumulation(True)
 
     direct, returned = grads(True), grads(False)
-    ref_model = copy.deepcopy(base).float()
-    out = ref_model(ids)
-    (torch.nn.functional.cross_entropy(out["logits"].flatten(0, 1), ids.flatten()) + out["aux_loss"]).backward()
-    ref = {n: p.grad.reshape(-1) for n, p in ref_model.named_parameters() if p.grad is not None}
+    ref_model = copy.deepcopy(base).float().cpu()  # fp32 oracle on the host
+    out = ref_model(ids.cpu())
+    (torch.nn.functional.cross_entropy(out["logits"].flatten(0, 1), ids.cpu().flatten()) + out["aux_loss"]).backward()
+    ref = {n: p.grad.reshape(-1).cuda() for n, p in ref_model.named_parameters() if p.grad is not None}
     checked = 0
     for name, g in direct.items():
         r = returned[name]
