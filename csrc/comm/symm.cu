@@ -214,6 +214,33 @@ __global__ void pull_kernel(uint4* __restrict__ dst, int64_t bytes, const uint64
   }
 }
 
+// All-to-all-v by pulling: dst[dst_off[r] ..] = heap_r[src_off[r] ..] for lens[r]
+// bytes from every rank r (r = this rank included), after rank r raised its
+// ready flag (at `ready_off` of its heap) to `epoch`.  `plan` is a (3, world)
+// int64 table of byte offsets / lengths, all multiples of 16.
+__global__ void a2av_pull_kernel(unsigned char* __restrict__ dst, const uint64_t* __restrict__ bases,
+                                 const int64_t* __restrict__ plan, int64_t ready_off, int world, uint32_t epoch,
+                                 int* err) {
+  __shared__ int64_t s_src[16], s_dst[16], s_end[16];
+  if (threadIdx.x == 0) {
+    int64_t acc = 0;
+    for (int r = 0; r < world; ++r) {
+      s_src[r] = plan[r];
+      s_dst[r] = plan[world + r];
+      acc += plan[2 * world + r] / 16;
+      s_end[r] = acc;  // prefix end, in 16-byte units
+    }
+  }
+  if (!block_wait_flags(bases, ready_off, world, epoch, err, kErrPeerWait)) return;
+  const int64_t total = s_end[world - 1];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int r = 0;
+    while (i >= s_end[r]) ++r;
+    const int64_t j = i - (r ? s_end[r - 1] : 0);
+    reinterpret_cast<uint4*>(dst + s_dst[r])[j] = reinterpret_cast<const uint4*>(bases[r] + s_src[r])[j];
+  }
+}
+
 // ----------------------------------------------------------------- DiLoCo
 // Pseudo-gradient delta = anchor - local, pushed in fp32 into slot `rank` of
 // each owner (owner r holds elements [r*shard, (r+1)*shard)).
@@ -376,6 +403,24 @@ void p2p_pull(at::Tensor& dst, const at::Tensor& bases, int64_t src_off, int64_t
   pull_kernel<<<grid_for(bytes / 16), 256, 0, stream()>>>(reinterpret_cast<uint4*>(dst.data_ptr()), bytes / world,
                                                            dev_u64(bases), src_off, ready_off, (int)world,
                                                            (uint32_t)epoch, err.data_ptr<int>());
+  LRB_LAUNCH_CHECK();
+}
+
+// dst <- pieces of every rank's heap per `plan` (3, world) int64 byte table
+// [src offsets in the peers' heaps; dst offsets; lengths], each peer's pieces
+// read once its ready flag (heap offset `ready_off`) reached `epoch`.
+void p2p_a2av_pull(at::Tensor& dst, const at::Tensor& bases, const at::Tensor& plan, int64_t ready_off, int64_t world,
+                   int64_t epoch, at::Tensor& err) {
+  LRB_CHECK(world >= 1 && world <= 16, "p2p_a2av_pull: 1..16 ranks");
+  LRB_CHECK(plan.is_cuda() && plan.scalar_type() == at::kLong && plan.is_contiguous() && plan.numel() == 3 * world,
+            "p2p_a2av_pull: plan must be a contiguous (3, world) int64 CUDA tensor");
+  LRB_CHECK(dst.is_contiguous() && reinterpret_cast<uintptr_t>(dst.data_ptr()) % 16 == 0,
+            "p2p_a2av_pull: dst must be contiguous and 16-byte aligned");
+  c10::cuda::CUDAGuard g(dst.device());
+  const int64_t bytes = dst.numel() * dst.element_size();
+  a2av_pull_kernel<<<grid_for(std::max<int64_t>(bytes / 16, 1)), 256, 0, stream()>>>(
+      reinterpret_cast<unsigned char*>(dst.data_ptr()), dev_u64(bases), plan.data_ptr<int64_t>(), ready_off,
+      (int)world, (uint32_t)epoch, err.data_ptr<int>());
   LRB_LAUNCH_CHECK();
 }
 

@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #define LRB_CHECK(cond, ...) TORCH_CHECK(cond, __VA_ARGS__)
 #define LRB_CUDA_CHECK(expr)                                                              \
   do {                                                                                    \
@@ -21,6 +23,39 @@
 namespace lrb {
 
 inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// Device address of a file-scope `__device__ int` error word (one copy per
+// device, part of the module image) on device `dev`.  Looked up once per device
+// with that device current and cached in atomics: safe from any host thread
+// (the autograd engine runs backward kernels on its own thread), and nothing
+// to destroy at process exit.
+struct DeviceWord {
+  const void* symbol;
+  std::atomic<int*> addr[64];
+  int* get(int dev) {
+    if (dev < 0) LRB_CUDA_CHECK(cudaGetDevice(&dev));
+    TORCH_CHECK(dev < 64, "device index ", dev, " out of range");
+    int* p = addr[dev].load(std::memory_order_acquire);
+    if (p != nullptr) return p;
+    int prev = 0;
+    LRB_CUDA_CHECK(cudaGetDevice(&prev));
+    LRB_CUDA_CHECK(cudaSetDevice(dev));
+    void* q = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&q, symbol);
+    LRB_CUDA_CHECK(cudaSetDevice(prev));
+    LRB_CUDA_CHECK(e);
+    addr[dev].store(static_cast<int*>(q), std::memory_order_release);
+    return static_cast<int*>(q);
+  }
+  // Returns and clears the first word on `dev` (0 = nothing recorded).
+  int64_t take(int dev) {
+    int* w = get(dev);
+    int h = 0;
+    LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
+    return h;
+  }
+};
 
 inline int num_sms() {
   static int n = [] {

@@ -23,6 +23,8 @@
 #include <cstdlib>
 
 namespace lrb {
+
+__device__ int g_attn_bwd_err[4];
 namespace {
 
 using namespace sm100;
@@ -726,12 +728,10 @@ CUtensorMap dq_map(float* ptr, int64_t rows, int64_t cols, int box_rows = TQ) {
   return m;
 }
 
-int* bwd_error_word(const at::Device& dev) {
-  static at::Tensor words[16];
-  const int idx = dev.index() < 0 ? 0 : dev.index();
-  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().device(dev).dtype(at::kInt));
-  return words[idx].data_ptr<int>();
-}
+// Error words of this file's kernels: module globals (one copy per device).
+DeviceWord g_attn_bwd_err_word{g_attn_bwd_err, {}};
+
+int* bwd_error_word(const at::Device& dev) { return g_attn_bwd_err_word.get(dev.index()); }
 
 }  // namespace
 
@@ -769,12 +769,6 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
   LRB_LAUNCH_CHECK();
 }
 
-int64_t attn_bwd_sm100_error(int64_t device) {
-  int* w = bwd_error_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
-  int h = 0;
-  LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
-  if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
-  return h;
-}
+int64_t attn_bwd_sm100_error(int64_t device) { return g_attn_bwd_err_word.take((int)device); }
 
 }  // namespace lrb

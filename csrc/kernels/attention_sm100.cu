@@ -27,6 +27,8 @@
 #include <cstdlib>
 
 namespace lrb {
+
+__device__ int g_attn_fwd_err[4];
 namespace {
 
 using namespace sm100;
@@ -657,12 +659,10 @@ CUtensorMap make_bshd_map(const at::Tensor& t) {
   return m;
 }
 
-int* attn_error_word(const at::Device& dev) {
-  static at::Tensor words[16];
-  const int idx = dev.index() < 0 ? 0 : dev.index();
-  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().device(dev).dtype(at::kInt));
-  return words[idx].data_ptr<int>();
-}
+// Error words of this file's kernels: module globals (one copy per device).
+DeviceWord g_attn_fwd_err_word{g_attn_fwd_err, {}};
+
+int* attn_error_word(const at::Device& dev) { return g_attn_fwd_err_word.get(dev.index()); }
 
 }  // namespace
 
@@ -705,12 +705,6 @@ std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor& q, const at:
   return {o, lse};
 }
 
-int64_t attn_sm100_error(int64_t device) {
-  int* w = attn_error_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
-  int h = 0;
-  LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
-  if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
-  return h;
-}
+int64_t attn_sm100_error(int64_t device) { return g_attn_fwd_err_word.take((int)device); }
 
 }  // namespace lrb

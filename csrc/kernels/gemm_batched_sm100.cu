@@ -20,6 +20,8 @@
 #include "sm100.cuh"
 
 namespace lrb {
+
+__device__ int g_gemm_batched_err[4];
 namespace {
 
 using namespace sm100;
@@ -241,12 +243,10 @@ CUtensorMap map3d(const at::Tensor& t, int box_cols, int box_rows) {
   return m;
 }
 
-int* batched_error_word(const at::Device& dev) {
-  static at::Tensor words[16];
-  const int idx = dev.index() < 0 ? 0 : dev.index();
-  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().device(dev).dtype(at::kInt));
-  return words[idx].data_ptr<int>();
-}
+// Error words of this file's kernels: module globals (one copy per device).
+DeviceWord g_gemm_batched_err_word{g_gemm_batched_err, {}};
+
+int* batched_error_word(const at::Device& dev) { return g_gemm_batched_err_word.get(dev.index()); }
 
 void check3(const at::Tensor& t, const char* name) {
   LRB_CHECK(t.is_cuda() && t.dim() == 3 && t.scalar_type() == at::kBFloat16 && t.stride(2) == 1,
@@ -297,12 +297,6 @@ void gemm_batched(const at::Tensor& A, const at::Tensor& B, bool b_mn, const at:
   LRB_LAUNCH_CHECK();
 }
 
-int64_t gemm_batched_error(int64_t device) {
-  int* w = batched_error_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
-  int h = 0;
-  LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
-  if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
-  return h;
-}
+int64_t gemm_batched_error(int64_t device) { return g_gemm_batched_err_word.take((int)device); }
 
 }  // namespace lrb

@@ -25,6 +25,8 @@
 #include <cstdlib>
 
 namespace lrb {
+
+__device__ int g_gemm_nvfp4_err[4];
 namespace {
 
 using namespace sm100;
@@ -228,12 +230,10 @@ CUtensorMap fp4_map(const void* ptr, int64_t rows, int64_t bytes, int64_t ld) {
   return m;
 }
 
-int* nvfp4_error_word(const at::Device& dev) {
-  static at::Tensor words[16];
-  const int idx = dev.index() < 0 ? 0 : dev.index();
-  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().device(dev).dtype(at::kInt));
-  return words[idx].data_ptr<int>();
-}
+// Error words of this file's kernels: module globals (one copy per device).
+DeviceWord g_gemm_nvfp4_err_word{g_gemm_nvfp4_err, {}};
+
+int* nvfp4_error_word(const at::Device& dev) { return g_gemm_nvfp4_err_word.get(dev.index()); }
 
 }  // namespace
 
@@ -286,12 +286,6 @@ at::Tensor gemm_nvfp4(const at::Tensor& A, const at::Tensor& sfa, const at::Tens
   return C;
 }
 
-int64_t gemm_nvfp4_error(int64_t device) {
-  int* w = nvfp4_error_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
-  int h = 0;
-  LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
-  if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
-  return h;
-}
+int64_t gemm_nvfp4_error(int64_t device) { return g_gemm_nvfp4_err_word.take((int)device); }
 
 }  // namespace lrb

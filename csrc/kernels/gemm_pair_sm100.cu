@@ -45,6 +45,7 @@ namespace lrb {
 
 // Device error word of this kernel (module global: one per device, no allocation).
 __device__ int g_gemm_pair_err;
+DeviceWord g_gemm_pair_err_word{&g_gemm_pair_err, {}};
 
 namespace {
 
@@ -79,6 +80,8 @@ struct PairArgs {
                 // (stores, or reduce-adds when accumulating); else direct stores
   int splits;   // K ranges per output tile (accumulation only: partial sums reduce-add)
   int group_m;  // tile rows per raster group
+  int batch;    // independent GEMMs of equal shape (the third tensor-map coordinate)
+  int64_t c_batch;  // C stride between batches (elements)
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
@@ -94,9 +97,11 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
 // Work unit -> (tile row, tile column, k-block range).  Units of one split index
 // are consecutive, so the units in flight share the same K range of A and B.
 __device__ __forceinline__ void unit_coords(int unit, int num_tiles, int tiles_m, int tiles_n, int nk,
-                                            const PairArgs& a, int& tm, int& tn, int& kb0, int& kb1) {
-  const int split = unit / num_tiles;
-  tile_coords(unit - split * num_tiles, tiles_m, tiles_n, a.group_m, tm, tn);
+                                            const PairArgs& a, int& tm, int& tn, int& kb0, int& kb1, int& bi) {
+  const int split = unit / num_tiles;  // num_tiles counts every batch
+  const int t = unit - split * num_tiles, per_batch = tiles_m * tiles_n;
+  bi = t / per_batch;
+  tile_coords(t - bi * per_batch, tiles_m, tiles_n, a.group_m, tm, tn);
   kb0 = (int)((int64_t)nk * split / a.splits);
   kb1 = (int)((int64_t)nk * (split + 1) / a.splits);
 }
@@ -125,22 +130,22 @@ __device__ __forceinline__ void stage_row(unsigned char* box, int lane, float al
   }
 }
 
-__device__ __forceinline__ void tma_store_box(const CUtensorMap* map, const void* src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
-               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y)
+__device__ __forceinline__ void tma_store_box(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
-__device__ __forceinline__ void tma_reduce_add_box(const CUtensorMap* map, const void* src, int x, int y) {
-  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
-               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y)
+__device__ __forceinline__ void tma_reduce_add_box(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
 
 template <typename OutT, int EPI>
-__device__ __forceinline__ void store_chunk(const PairArgs& a, int row, int col0, const uint32_t* r) {
+__device__ __forceinline__ void store_chunk(const PairArgs& a, int bi, int row, int col0, const uint32_t* r) {
   if (row >= a.M || col0 >= a.N) return;
   if constexpr (EPI == kAccumF32) {
-    float* c = reinterpret_cast<float*>(a.C) + (int64_t)row * a.ldc + col0;
+    float* c = reinterpret_cast<float*>(a.C) + bi * a.c_batch + (int64_t)row * a.ldc + col0;
     if (a.vec_ok && col0 + 32 <= a.N) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
@@ -157,7 +162,7 @@ __device__ __forceinline__ void store_chunk(const PairArgs& a, int row, int col0
         if (col0 + j < a.N) c[j] += a.alpha * __uint_as_float(r[j]);
     }
   } else {
-    OutT* c = reinterpret_cast<OutT*>(a.C) + (int64_t)row * a.ldc + col0;
+    OutT* c = reinterpret_cast<OutT*>(a.C) + bi * a.c_batch + (int64_t)row * a.ldc + col0;
     constexpr int V = 16 / sizeof(OutT);
     if (a.vec_ok && col0 + 32 <= a.N) {
 #pragma unroll
@@ -175,22 +180,32 @@ __device__ __forceinline__ void store_chunk(const PairArgs& a, int row, int col0
   }
 }
 
+// 3-D tiled load (x, y, batch) into this CTA's shared memory, completion on an
+// mbarrier that may live in the peer CTA.  No multicast.
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // Loads this CTA's half of one stage: A rows [m0, m0 + 128) and B rows [n0, n0 + 128)
 // at K offset k0.  MN-major operands are two 64-wide boxes each.
 template <bool A_MN, bool B_MN>
 __device__ __forceinline__ void load_stage(unsigned char* sa, unsigned char* sb, const CUtensorMap* tmA,
-                                           const CUtensorMap* tmB, uint32_t bar, int m0, int n0, int k0) {
+                                           const CUtensorMap* tmB, uint32_t bar, int m0, int n0, int k0, int bi) {
   if (A_MN) {
-    tma_load_2d_pair(sa, tmA, bar, m0, k0);
-    tma_load_2d_pair(sa + kMnBox, tmA, bar, m0 + 64, k0);
+    tma_load_3d_pair(sa, tmA, bar, m0, k0, bi);
+    tma_load_3d_pair(sa + kMnBox, tmA, bar, m0 + 64, k0, bi);
   } else {
-    tma_load_2d_pair(sa, tmA, bar, k0, m0);
+    tma_load_3d_pair(sa, tmA, bar, k0, m0, bi);
   }
   if (B_MN) {
-    tma_load_2d_pair(sb, tmB, bar, n0, k0);
-    tma_load_2d_pair(sb + kMnBox, tmB, bar, n0 + 64, k0);
+    tma_load_3d_pair(sb, tmB, bar, n0, k0, bi);
+    tma_load_3d_pair(sb + kMnBox, tmB, bar, n0 + 64, k0, bi);
   } else {
-    tma_load_2d_pair(sb, tmB, bar, k0, n0);
+    tma_load_3d_pair(sb, tmB, bar, k0, n0, bi);
   }
 }
 
@@ -216,7 +231,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool leader = rank == 0;
   const int pair = (int)cluster_id_x(), npairs = (int)nclusters_x();
   const int tiles_m = (args.M + 2 * BM - 1) / (2 * BM), tiles_n = (args.N + BN - 1) / BN;
-  const int num_tiles = tiles_m * tiles_n;
+  const int num_tiles = tiles_m * tiles_n * args.batch;
   const int nk = (args.K + BK - 1) / BK;
   const int num_units = num_tiles * args.splits;
 
@@ -251,14 +266,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int64_t armed = 0;
       bool ok = true;
       for (int unit = pair; unit < num_units && ok; unit += npairs) {
-        int tm, tn, kb0, kb1;
-        unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1);
+        int tm, tn, kb0, kb1, bi;
+        unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1, bi);
         const int m0 = tm * 2 * BM + (int)rank * BM, n0 = tn * BN + (int)rank * (BN / 2);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrTmaWait)) { ok = false; break; }
           const uint32_t fb = mapa_shared(smem_addr(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStage);
-          load_stage<A_MN, B_MN>(sA + stage * kHalfA, sB + stage * kHalfB, &tmA, &tmB, fb, m0, n0, kb * BK);
+          load_stage<A_MN, B_MN>(sA + stage * kHalfA, sB + stage * kHalfB, &tmA, &tmB, fb, m0, n0, kb * BK, bi);
           ++armed;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -280,8 +295,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int unit = pair; unit < num_units && ok; unit += npairs) {
-        int tm, tn, kb0, kb1;
-        unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1);
+        int tm, tn, kb0, kb1, bi;
+        unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1, bi);
         if (!mbar_wait(&accempty[acc], acc_phase ^ 1, err, kErrAccWait)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * BN);
@@ -310,8 +325,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int acc = 0, nbox = 0;
     uint32_t acc_phase = 0;
     for (int unit = pair; unit < num_units; unit += npairs) {
-      int tm, tn, kb0, kb1;
-      unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1);
+      int tm, tn, kb0, kb1, bi;
+      unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1, bi);
       if (!mbar_wait(&accfull[acc], acc_phase, err, kErrEpiWait)) break;
       tc_fence_after();
       const int row0 = tm * 2 * BM + (int)rank * BM + q * 32;
@@ -336,13 +351,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if constexpr (EPI == kAccumF32) tma_reduce_add_box(&tmC, box, col0, row0);
-            else tma_store_box(&tmC, box, col0, row0);
+            if constexpr (EPI == kAccumF32) tma_reduce_add_box(&tmC, box, col0, row0, bi);
+            else tma_store_box(&tmC, box, col0, row0, bi);
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
           ++nbox;
         } else {
-          store_chunk<OutT, EPI>(args, row0 + lane, col0, r);
+          store_chunk<OutT, EPI>(args, bi, row0 + lane, col0, r);
         }
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
@@ -374,15 +389,16 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Row-major (rows x cols) 16-bit matrix with row pitch `ld` elements; box = box_cols x box_rows,
-// 128-byte swizzle (box_cols = 64).
-CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows, bool bf16) {
+// `batch` row-major (rows x cols) matrices, row pitch `ld` and batch pitch `bstride`
+// elements, 16-bit; box = box_cols x box_rows x 1, 128-byte swizzle (box_cols = 64).
+CUtensorMap make_map(const void* ptr, int64_t batch, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+                     int box_cols, int box_rows, bool bf16) {
   CUtensorMap m;
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode_fn()(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+  const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+  const cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(std::max<int64_t>(bstride, 1) * 2)};
+  const cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                            const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -390,19 +406,20 @@ CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, in
   return m;
 }
 
-// Output box map: (rows x cols) C with row pitch `ld` elements, box 32 x 32,
-// 64-byte swizzle for 16-bit outputs and 128-byte swizzle for fp32.
-CUtensorMap make_out_map(void* ptr, int64_t rows, int64_t cols, int64_t ld, at::ScalarType t) {
+// Output box map: `batch` (rows x cols) C, box 32 x 32 x 1, 64-byte swizzle for
+// 16-bit outputs and 128-byte swizzle for fp32.
+CUtensorMap make_out_map(void* ptr, int64_t batch, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+                         at::ScalarType t) {
   CUtensorMap m;
   const int esz = t == at::kFloat ? 4 : 2;
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
-  const cuuint32_t box[2] = {32, 32};
-  const cuuint32_t estr[2] = {1, 1};
+  const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+  const cuuint64_t strides[2] = {(cuuint64_t)(ld * esz), (cuuint64_t)(std::max<int64_t>(bstride, 1) * esz)};
+  const cuuint32_t box[3] = {32, 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapDataType dt = t == at::kFloat      ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : t == at::kBFloat16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r = encode_fn()(&m, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = encode_fn()(&m, dt, 3, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            esz == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   LRB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (gemm_pair output) failed with code ", (int)r);
@@ -474,50 +491,65 @@ int choose_splits(int tiles, int pairs, int nk) {
   return best;
 }
 
-void check_operand(const at::Tensor& t, const char* name) {
-  LRB_CHECK(t.is_cuda() && t.dim() == 2 && t.stride(1) == 1, "gemm_pair: ", name,
-            " must be a 2-D CUDA tensor with unit column stride");
-  LRB_CHECK(t.scalar_type() == at::kBFloat16 || t.scalar_type() == at::kHalf, "gemm_pair: ", name,
-            " must be bf16/fp16");
-  LRB_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0 && (t.stride(0) * 2) % 16 == 0 && t.stride(0) > 0,
-            "gemm_pair: ", name, " needs a 16-byte aligned base and row pitch");
+// (rows, cols) or (batch, rows, cols) view: returns (batch, rows, cols, row pitch, batch pitch).
+struct Mat {
+  int64_t batch, rows, cols, ld, bstride;
+};
+
+Mat check_operand(const at::Tensor& t, const char* name, bool sixteen_bit) {
+  LRB_CHECK(t.is_cuda() && (t.dim() == 2 || t.dim() == 3) && t.stride(-1) == 1, "gemm_pair: ", name,
+            " must be a 2-D or 3-D CUDA tensor with unit column stride");
+  if (sixteen_bit)
+    LRB_CHECK(t.scalar_type() == at::kBFloat16 || t.scalar_type() == at::kHalf, "gemm_pair: ", name,
+              " must be bf16/fp16");
+  const int64_t esz = t.element_size();
+  Mat m{t.dim() == 3 ? t.size(0) : 1, t.size(-2), t.size(-1), t.stride(-2), t.dim() == 3 ? t.stride(0) : 0};
+  LRB_CHECK(m.ld > 0 || m.rows <= 1, "gemm_pair: ", name, " row pitch must be positive");
+  return m;
+}
+
+bool tma_ok(const at::Tensor& t, const Mat& m) {
+  const int64_t esz = t.element_size();
+  return reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0 && (m.ld * esz) % 16 == 0 && (m.bstride * esz) % 16 == 0;
 }
 
 }  // namespace
 
-// C (M x N, row pitch C.stride(0)) = alpha * op(A) op(B)^T, or += when `accumulate`
-// (then C is fp32).  a_mn: A is stored (K, M); otherwise (M, K).  b_mn: B is stored
-// (K, N); otherwise (N, K).
+// C = alpha * op(A) op(B)^T, or += when `accumulate` (then C is fp32).  a_mn: A is
+// stored (K, M), otherwise (M, K); b_mn: B is stored (K, N), otherwise (N, K).  All
+// three may carry a leading batch dimension (the same for each): one launch runs
+// every batch entry.
 void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, at::Tensor& C, bool accumulate,
                double alpha) {
-  check_operand(A, "A");
-  check_operand(B, "B");
+  const Mat a = check_operand(A, "A", true), b = check_operand(B, "B", true), c = check_operand(C, "C", false);
   LRB_CHECK(A.scalar_type() == B.scalar_type(), "gemm_pair: A and B must have the same dtype");
-  const int64_t M = a_mn ? A.size(1) : A.size(0), K = a_mn ? A.size(0) : A.size(1);
-  const int64_t N = b_mn ? B.size(1) : B.size(0), KB = b_mn ? B.size(0) : B.size(1);
+  LRB_CHECK(A.dim() == B.dim() && A.dim() == C.dim() && a.batch == b.batch && a.batch == c.batch,
+            "gemm_pair: A, B and C must all be 2-D or all 3-D with one batch size");
+  LRB_CHECK(tma_ok(A, a) && tma_ok(B, b), "gemm_pair: A and B need 16-byte aligned bases and pitches");
+  const int64_t M = a_mn ? a.cols : a.rows, K = a_mn ? a.rows : a.cols;
+  const int64_t N = b_mn ? b.cols : b.rows, KB = b_mn ? b.rows : b.cols;
   LRB_CHECK(K == KB, "gemm_pair: K mismatch (", K, " vs ", KB, ")");
-  LRB_CHECK(C.is_cuda() && C.dim() == 2 && C.size(0) == M && C.size(1) == N && C.stride(1) == 1,
-            "gemm_pair: C must be (M, N) with unit column stride");
-  LRB_CHECK(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), "gemm_pair: dimensions too large");
+  LRB_CHECK(c.rows == M && c.cols == N, "gemm_pair: C must be (M, N)");
+  LRB_CHECK(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31) && a.batch < (1LL << 16),
+            "gemm_pair: dimensions too large");
   LRB_CHECK(!accumulate || C.scalar_type() == at::kFloat, "gemm_pair: accumulation needs an fp32 C");
   LRB_CHECK(C.data_ptr() != A.data_ptr() && C.data_ptr() != B.data_ptr(), "gemm_pair: C must not alias A or B");
   c10::cuda::CUDAGuard g(A.device());
-  if (M == 0 || N == 0) return;
+  if (M == 0 || N == 0 || a.batch == 0) return;
   if (K == 0) {
     if (!accumulate) C.zero_();
     return;
   }
   const bool bf = A.scalar_type() == at::kBFloat16;
   // TMA boxes: K-major 64 (K) x 128 rows; MN-major 64 (MN) x 64 (K) rows.
-  CUtensorMap ta = a_mn ? make_map(A.data_ptr(), K, M, A.stride(0), 64, BK, bf)
-                        : make_map(A.data_ptr(), M, K, A.stride(0), BK, BM, bf);
-  CUtensorMap tb = b_mn ? make_map(B.data_ptr(), K, N, B.stride(0), 64, BK, bf)
-                        : make_map(B.data_ptr(), N, K, B.stride(0), BK, BN / 2, bf);
+  CUtensorMap ta = a_mn ? make_map(A.data_ptr(), a.batch, K, M, a.ld, a.bstride, 64, BK, bf)
+                        : make_map(A.data_ptr(), a.batch, M, K, a.ld, a.bstride, BK, BM, bf);
+  CUtensorMap tb = b_mn ? make_map(B.data_ptr(), b.batch, K, N, b.ld, b.bstride, 64, BK, bf)
+                        : make_map(B.data_ptr(), b.batch, N, K, b.ld, b.bstride, BK, BN / 2, bf);
   const auto ct = C.scalar_type();
   LRB_CHECK(ct == at::kBFloat16 || ct == at::kHalf || ct == at::kFloat, "gemm_pair: unsupported output dtype");
-  const int esz = (int)C.element_size();
-  const bool aligned = (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0) && ((C.stride(0) * esz) % 16 == 0);
-  const int tiles = (int)(((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN));
+  const bool aligned = tma_ok(C, c);
+  const int tiles = (int)(a.batch * ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN));
   const int nk = (int)((K + BK - 1) / BK);
   const int maxp = max_pairs(A.get_device());
   // Partial sums of one tile may only meet in C through the TMA reduce-add.
@@ -528,9 +560,9 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, a
   const int group_m = N >= 16384 ? 16 : GROUP_M;
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
-  if (aligned) tc = make_out_map(C.data_ptr(), M, N, C.stride(0), ct);
-  PairArgs args{C.data_ptr(), C.stride(0), (int)M, (int)N, (int)K, (float)alpha, aligned ? 1 : 0, aligned ? 1 : 0,
-                splits, group_m};
+  if (aligned) tc = make_out_map(C.data_ptr(), c.batch, M, N, c.ld, c.bstride, ct);
+  PairArgs args{C.data_ptr(), c.ld, (int)M, (int)N, (int)K, (float)alpha, aligned ? 1 : 0, aligned ? 1 : 0,
+                splits, group_m, (int)a.batch, c.bstride};
   if (accumulate) {
     if (bf) launch_layout<float, kAccumF32, true>(a_mn, b_mn, ta, tb, tc, args, pairs);
     else launch_layout<float, kAccumF32, false>(a_mn, b_mn, ta, tb, tc, args, pairs);
@@ -547,18 +579,6 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, a
 }
 
 // Returns and clears the error word of the pair GEMM on `device` (0 = no timeout).
-int64_t gemm_pair_error(int64_t device) {
-  int prev = 0;
-  LRB_CUDA_CHECK(cudaGetDevice(&prev));
-  LRB_CUDA_CHECK(cudaSetDevice((int)device));
-  int h = 0;
-  LRB_CUDA_CHECK(cudaMemcpyFromSymbol(&h, g_gemm_pair_err, sizeof(int)));
-  if (h) {
-    const int zero = 0;
-    LRB_CUDA_CHECK(cudaMemcpyToSymbol(g_gemm_pair_err, &zero, sizeof(int)));
-  }
-  LRB_CUDA_CHECK(cudaSetDevice(prev));
-  return h;
-}
+int64_t gemm_pair_error(int64_t device) { return g_gemm_pair_err_word.take((int)device); }
 
 }  // namespace lrb

@@ -17,6 +17,8 @@
 #include "sm100.cuh"
 
 namespace lrb {
+
+__device__ int g_gemm_tn_err[4];
 namespace {
 
 using namespace sm100;
@@ -237,12 +239,10 @@ CUtensorMap make_map_k_major(const void* ptr, int64_t rows, int64_t cols, int64_
   return m;
 }
 
-int* error_word(const at::Device& dev) {
-  static at::Tensor words[16];
-  const int idx = dev.index() < 0 ? 0 : dev.index();
-  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().device(dev).dtype(at::kInt));
-  return words[idx].data_ptr<int>();
-}
+// Error words of this file's kernels: module globals (one copy per device).
+DeviceWord g_gemm_tn_err_word{g_gemm_tn_err, {}};
+
+int* error_word(const at::Device& dev) { return g_gemm_tn_err_word.get(dev.index()); }
 
 template <typename OutT, int EPI, bool BF16IN>
 void launch(const at::Tensor& A, const at::Tensor& B, void* C, int64_t ldc, float alpha) {
@@ -307,12 +307,6 @@ void gemm_tn_accumulate(const at::Tensor& A, const at::Tensor& B, at::Tensor& C,
 }
 
 // Returns and clears the device error word of the tcgen05 kernels (0 = no error).
-int64_t sm100_error(int64_t device) {
-  int* w = error_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
-  int h = 0;
-  LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
-  if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
-  return h;
-}
+int64_t sm100_error(int64_t device) { return g_gemm_tn_err_word.take((int)device); }
 
 }  // namespace lrb

@@ -20,6 +20,8 @@
 #include "sm100.cuh"
 
 namespace lrb {
+
+__device__ int g_mem_topk_err[4];
 namespace {
 
 using namespace sm100;
@@ -288,12 +290,10 @@ CUtensorMap bf16_map(const void* ptr, int64_t rows, int64_t cols, int box_rows) 
   return m;
 }
 
-int* topk_error_word(const at::Device& dev) {
-  static at::Tensor words[16];
-  const int idx = dev.index() < 0 ? 0 : dev.index();
-  if (!words[idx].defined()) words[idx] = at::zeros({4}, at::TensorOptions().device(dev).dtype(at::kInt));
-  return words[idx].data_ptr<int>();
-}
+// Error words of this file's kernels: module globals (one copy per device).
+DeviceWord g_mem_topk_err_word{g_mem_topk_err, {}};
+
+int* topk_error_word(const at::Device& dev) { return g_mem_topk_err_word.get(dev.index()); }
 
 }  // namespace
 
@@ -331,13 +331,7 @@ std::tuple<at::Tensor, at::Tensor> memory_topk_candidates(const at::Tensor& q, c
   return {out_s, out_i};
 }
 
-int64_t memory_topk_error(int64_t device) {
-  int* w = topk_error_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
-  int h = 0;
-  LRB_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
-  if (h) LRB_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
-  return h;
-}
+int64_t memory_topk_error(int64_t device) { return g_mem_topk_err_word.take((int)device); }
 
 // scores / idx (T, 32) -> (out (T, Dv) in values' dtype, softmax weights (T, 32) fp32)
 std::tuple<at::Tensor, at::Tensor> topk_gather_fwd(const at::Tensor& s, const at::Tensor& idx, const at::Tensor& values) {

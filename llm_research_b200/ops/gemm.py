@@ -48,16 +48,17 @@ def gemm(a: torch.Tensor, b: torch.Tensor, a_mn: bool = False, b_mn: bool = Fals
 
     ``op(A)`` is ``a`` (M, K), or ``a.T`` when ``a_mn`` (``a`` stored (K, M));
     ``op(B)^T`` is ``b.T`` for ``b`` (N, K), or ``b`` when ``b_mn`` (``b`` stored
-    (K, N))."""
-    M = a.shape[1] if a_mn else a.shape[0]
-    N = b.shape[1] if b_mn else b.shape[0]
+    (K, N)).  With a leading batch dimension on ``a``, ``b`` (and ``out``) every
+    batch entry is one GEMM of the same shape, all in one launch."""
+    M = a.shape[-1] if a_mn else a.shape[-2]
+    N = b.shape[-1] if b_mn else b.shape[-2]
     if out is None:
         if accumulate:
             raise ValueError("accumulate needs an output tensor")
-        out = torch.empty(M, N, dtype=out_dtype or a.dtype, device=a.device)
+        out = torch.empty(*a.shape[:-2], M, N, dtype=out_dtype or a.dtype, device=a.device)
     if not a.is_cuda:
-        av = a.float().t() if a_mn else a.float()
-        bv = b.float() if b_mn else b.float().t()
+        av = a.float().transpose(-1, -2) if a_mn else a.float()
+        bv = b.float() if b_mn else b.float().transpose(-1, -2)
         r = alpha * (av @ bv)
         if accumulate:
             out.add_(r.to(out.dtype))

@@ -255,3 +255,51 @@ def project(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> 
         y = linear_bf16(x, w)
         return y + b if b is not None else y
     return F.linear(x, w, b)
+
+
+# ------------------------------------------------------------ grouped experts
+class _GroupedSwiGLUFn(torch.autograd.Function):
+    """``y_e = (silu(x_e W_gate,e^T) * x_e W_up,e^T) W_down,e^T`` for every expert e at
+    once: the four GEMMs of forward and backward that involve weights, and the
+    two activation GEMMs, are batched CTA-pair launches over the expert dimension
+    (equal row counts per expert: the capacity-padded dispatch buffer)."""
+
+    @staticmethod
+    def forward(ctx, x_e, w_ug, w_down):
+        from llm_research_b200.ops.activation import swiglu
+        from llm_research_b200.ops.gemm import gemm
+
+        gu = gemm(x_e, w_ug)                       # (E, R, 2F) = [up | gate]
+        h = swiglu(gu)                             # (E, R, F)
+        ctx.save_for_backward(x_e, w_ug, w_down, gu, h)
+        return gemm(h, w_down)                     # (E, R, d)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from llm_research_b200._ext import native
+        from llm_research_b200.ops.gemm import gemm
+
+        x_e, w_ug, w_down, gu, h = ctx.saved_tensors
+        dy = dy.contiguous()
+        dh = gemm(dy, w_down, b_mn=True)           # dY W_down         (E, R, F)
+        dw_down = gemm(dy, h, a_mn=True, b_mn=True)  # dY^T h          (E, d, F)
+        dgu = native().swiglu_bwd(dh, gu)          # (E, R, 2F)
+        dx = gemm(dgu, w_ug, b_mn=True) if ctx.needs_input_grad[0] else None  # dGU W_ug  (E, R, d)
+        dw_ug = gemm(dgu, x_e, a_mn=True, b_mn=True)  # dGU^T x_e      (E, 2F, d)
+        return dx, dw_ug, dw_down
+
+
+def grouped_swiglu(x_e: torch.Tensor, w_ug: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    """SwiGLU experts over capacity-padded rows: ``x_e (E, R, d)``, ``w_ug (E, 2F, d)``
+    (``[up; gate]`` rows), ``w_down (E, d, F)`` -> ``(E, R, d)``."""
+    from llm_research_b200.ops.activation import swiglu
+
+    E, R, d = x_e.shape
+    F2 = w_ug.shape[1]
+    ok = (x_e.is_cuda and x_e.dtype in (torch.bfloat16, torch.float16) and w_ug.dtype == x_e.dtype
+          and w_down.dtype == x_e.dtype and d % 8 == 0 and F2 % 16 == 0 and R % 8 == 0 and R > 0)
+    if ok:
+        return _GroupedSwiGLUFn.apply(x_e.contiguous(), w_ug.contiguous(), w_down.contiguous())
+    gu = torch.bmm(x_e, w_ug.transpose(1, 2))
+    h = swiglu(gu.reshape(-1, F2)).view(E, R, -1)
+    return torch.bmm(h, w_down.transpose(1, 2))

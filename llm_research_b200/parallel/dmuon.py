@@ -16,7 +16,19 @@ time assignment by Newton-Schulz FLOPs, identical on all ranks) and:
 
 So the reduce-scatter of the engine plus two bf16 all-to-alls carry all the
 optimizer traffic, and every rank runs Newton-Schulz on ~1/world of the
-matrices.  Under tensor parallelism (engine ``tp_group``) a TP-sharded matrix
+matrices.
+
+On one node (``comm="p2p"``, the default for CUDA ranks of one node; set
+``LRB_DMUON_COMM=nccl`` for the collective path) the exchanges use no NCCL
+call: the prologue writes each rank's pieces straight into its symmetric heap,
+the rank raises a ready flag, and every rank pulls the pieces it needs from its
+peers' heaps with P2P loads (``p2p_a2av_pull``) -- gradients to the owners'
+Newton-Schulz stacks, scaled updates back.  The per-matrix ``||g||^2`` partials
+and the "received a gradient" flags travel the same way (each rank pulls every
+rank's small vector and reduces locally).  Reuse of a heap region across steps
+needs no extra handshake: a rank rewrites its step-t gradient pieces only after
+it pulled its step-t updates, which every owner published only after pulling
+its step-t gradients, and symmetrically for the update region.  Under tensor parallelism (engine ``tp_group``) a TP-sharded matrix
 is all-gathered over the TP group on its owner (the TP peers own the same
 matrices), orthogonalised whole, and each peer keeps its slice, so the update
 equals that of the unsharded matrix.  ``state_dict`` gathers the full per-parameter state in the layout
@@ -43,6 +55,10 @@ class Segment:
     shard_off: int      # offset inside this rank's shard of the unit
     param_off: int      # offset inside the flattened parameter
     length: int
+
+
+def _pad8(n: int) -> int:
+    return (n + 7) // 8 * 8
 
 
 def _is_hybrid(cls: type) -> bool:
@@ -132,6 +148,17 @@ class ShardedHybridOptimizer:
             loads[r] += self._ns_cost(infos[pid].shape)
         self._build_exchange(infos)
 
+    def _want_p2p(self) -> bool:
+        import os
+
+        eng = self.engine
+        mode = os.environ.get("LRB_DMUON_COMM", "p2p").lower()
+        if mode != "p2p" or self.world == 1 or eng.device.type != "cuda":
+            return False
+        from llm_research_b200.parallel.symm import single_node
+
+        return single_node(eng.pg)
+
     @staticmethod
     def _ns_cost(shape: Tuple[int, ...]) -> float:
         m, n = shape
@@ -149,10 +176,16 @@ class ShardedHybridOptimizer:
         # send order: by (owner, pid); each Muon param has at most one segment per rank.
         seg_by_pid = {s.pid: s for s in self.muon_segs}
         self.send_order = sorted(self.muon_segs, key=lambda s: (self.owner[s.pid], s.pid))
+        # every piece starts on a 16-byte boundary of the bf16 exchange buffers
+        # (P2P pulls move 16-byte words); the padding is zero and never read back
+        self.send_pos: Dict[int, int] = {}
         self.send_splits = [0] * world
+        pos = 0
         for s in self.send_order:
-            self.send_splits[self.owner[s.pid]] += s.length
-        self.send_total = sum(self.send_splits)
+            self.send_pos[s.pid] = pos
+            pos += _pad8(s.length)
+            self.send_splits[self.owner[s.pid]] += _pad8(s.length)
+        self.send_total = pos
         # owned matrices, grouped by shape -> stack layout
         owned = [pid for pid in self.muon_ids if self.owner[pid] == rank]
         groups: Dict[Tuple[Tuple[int, int], Optional[int]], List[int]] = defaultdict(list)
@@ -178,10 +211,13 @@ class ShardedHybridOptimizer:
                     continue
                 off, ln = pc
                 self.r2s.append((pos, self.stack_base[pid] + off, ln))
-                self.recv_splits[r] += ln
-                pos += ln
+                self.recv_splits[r] += _pad8(ln)
+                pos += _pad8(ln)
         self.recv_total = pos
         self._bufs = None  # persistent exchange buffers and their segment views (first step)
+        self.p2p = None
+        if self._want_p2p():
+            self.p2p = _P2PExchange(self)
 
     # ------------------------------------------------------------------ step
     def _views(self, ui: int, seg: Segment, buf: torch.Tensor) -> torch.Tensor:
@@ -209,7 +245,7 @@ class ShardedHybridOptimizer:
         ns_steps = g["ns_steps"]
         units = eng.units
 
-        active = eng.touched_params()
+        active = eng.touched_params(self.p2p.max_flags if self.p2p is not None else None)
         adam_segs = [s for s in self.adam_segs if s.pid in active]
         if adam_segs:
             for pid in sorted({s.pid for s in adam_segs}):
@@ -224,7 +260,9 @@ class ShardedHybridOptimizer:
                 lr=g["lr_adamw"], beta1=beta1, beta2=beta2, eps=g["eps"], weight_decay=g["weight_decay_adamw"],
             )
 
-        if self.muon_ids and any(p in active for p in self.muon_ids):
+        # with the P2P exchange every rank takes part every step (lockstep epochs
+        # keep the heap regions' reuse safe); a matrix without a gradient sends zeros
+        if self.muon_ids and (self.p2p is not None or any(p in active for p in self.muon_ids)):
             self._muon_step(lr_m, mu, wd_m, ns_steps, active)
         self._step_local(lr_m, mu, wd_m, ns_steps)
         eng.refresh()
@@ -252,10 +290,13 @@ class ShardedHybridOptimizer:
         the segment copies between the receive layout and the stack use."""
         if self._bufs is None or self._bufs["dtype"] != xdt:
             dev = self.engine.device
-            send = torch.zeros(self.send_total, dtype=xdt, device=dev)
+            if self.p2p is not None:  # the two published regions live in the symmetric heap
+                send, back = self.p2p.send, self.p2p.back
+            else:
+                send = torch.zeros(self.send_total, dtype=xdt, device=dev)
+                back = torch.empty(self.recv_total, dtype=xdt, device=dev)
             recv = send if self.world == 1 else torch.empty(self.recv_total, dtype=xdt, device=dev)
             stack = torch.empty(self.stack_total, dtype=xdt, device=dev)
-            back = torch.empty(self.recv_total, dtype=xdt, device=dev)
             upd = back if self.world == 1 else torch.empty(self.send_total, dtype=xdt, device=dev)
             self._bufs = dict(dtype=xdt, send=send, recv=recv, stack=stack, back=back, upd=upd,
                               recv_v=[recv[a: a + n] for a, _, n in self.r2s],
@@ -274,12 +315,12 @@ class ShardedHybridOptimizer:
         B = self._exchange_buffers(xdt)
         send, recv, stack, back, upd = B["send"], B["recv"], B["stack"], B["back"], B["upd"]
         send.zero_()  # matrices without a gradient keep u = 0 -> zero update, no decay
-        outs, segs, pos = [], [], 0
+        outs, segs = [], []
         for s in self.send_order:
             if s.pid in active:
+                pos = self.send_pos[s.pid]
                 outs.append(send[pos: pos + s.length])
                 segs.append(s)
-            pos += s.length
         gnorm_seg = ops.muon_prologue_into(
             [units[s.unit].master[s.shard_off: s.shard_off + s.length] for s in segs],
             [units[s.unit].grad_shard[s.shard_off: s.shard_off + s.length] for s in segs],
@@ -289,15 +330,18 @@ class ShardedHybridOptimizer:
         # per-matrix ||g||^2 summed over the ranks holding its pieces
         gsq = torch.zeros(len(self.muon_ids), device=dev)
         idx = torch.tensor([self.muon_pos[s.pid] for s in segs], device=dev, dtype=torch.long)
-        gsq.index_add_(0, idx, gnorm_seg.pow(2))
-        if self.world > 1:
+        if segs:
+            gsq.index_add_(0, idx, gnorm_seg.pow(2))
+        if self.p2p is not None:
+            gsq = self.p2p.exchange_grads(gsq, recv)  # pieces to the owners + sum of the norm partials
+        elif self.world > 1:
             dist.all_reduce(gsq, group=eng.pg)
         if self.tp_world > 1:  # ||g||^2 of a TP-sharded matrix: sum over its shards
             mask = torch.tensor([self.tp_dim.get(p) is not None for p in self.muon_ids], device=dev)
             part = gsq * mask
             dist.all_reduce(part, group=eng.tp_group)
             gsq = torch.where(mask, part, gsq)
-        if self.world > 1:
+        if self.world > 1 and self.p2p is None:
             dist.all_to_all_single(recv, send, self.recv_splits, self.send_splits, group=eng.pg)
         self._copy_segments(B["stack_v"], B["recv_v"])
         gnorm = gsq.sqrt()
@@ -320,14 +364,16 @@ class ShardedHybridOptimizer:
             torch.mul(o, scale, out=block)  # fp32 product, one rounding into the stack
             base += n * numel
         self._copy_segments(B["back_v"], B["stack_v"])
-        if self.world > 1:
+        if self.p2p is not None:
+            self.p2p.exchange_updates(upd)
+        elif self.world > 1:
             dist.all_to_all_single(upd, back, self.send_splits, self.recv_splits, group=eng.pg)
-        masters, deltas, pos = [], [], 0
+        masters, deltas = [], []
         for s in self.send_order:
             if s.pid in active:
+                pos = self.send_pos[s.pid]
                 masters.append(units[s.unit].master[s.shard_off: s.shard_off + s.length])
                 deltas.append(upd[pos: pos + s.length])
-            pos += s.length
         ops.axpy_list(masters, deltas, -1.0)
 
     def zero_grad(self, set_to_none: bool = True) -> None:
@@ -405,3 +451,103 @@ class ShardedHybridOptimizer:
                 self.exp_avg[info.unit][dst_sl].copy_(ent["exp_avg"].reshape(-1)[src_sl])
                 self.exp_avg_sq[info.unit][dst_sl].copy_(ent["exp_avg_sq"].reshape(-1)[src_sl])
                 self.steps[info.index] = int(ent.get("step", 0))
+
+
+class _P2PExchange:
+    """The optimizer's exchanges over a symmetric heap of the engine's group.
+
+    Heap layout (same offsets on every rank): the gradient-piece region (the
+    largest send layout of any rank), the update region (the largest receive
+    layout), one small fp32 vector slot per kind (norm partials, gradient
+    flags), and one ready flag per kind.  Each exchange: the rank's data is in
+    its own region, it raises its flag to the exchange's epoch, and it pulls
+    its pieces from every rank's region once that rank's flag reached the
+    epoch."""
+
+    FLAG_GRADS, FLAG_UPDATES, FLAG_TOUCHED = 0, 1, 2
+
+    def __init__(self, opt: "ShardedHybridOptimizer") -> None:
+        from llm_research_b200.parallel.symm import SymmetricHeap
+
+        eng = opt.engine
+        self.opt, self.world, self.rank, dev = opt, opt.world, opt.rank, eng.device
+        splits: List[Any] = [None] * self.world
+        dist.all_gather_object(splits, list(opt.send_splits), group=eng.pg)
+        self.all_send = [list(map(int, x)) for x in splits]  # all_send[r][o]: r's elements for owner o
+        max_send = max(sum(x) for x in self.all_send)
+        max_recv = max(sum(self.all_send[r][o] for r in range(self.world)) for o in range(self.world))
+        self.n_small = max(len(opt.muon_ids), len(eng.params), 1)
+        small = _pad8(self.n_small) * 4
+        need = 2 * max_send + 2 * max_recv + 2 * small + 4096
+        self.heap = heap = SymmetricHeap(need, group=eng.pg, device=dev)
+        self.send_off = heap.alloc(2 * max(max_send, 8))
+        self.back_off = heap.alloc(2 * max(max_recv, 8))
+        self.small_off = [heap.alloc(small), heap.alloc(small)]  # norm partials, gradient flags
+        self.flag_off = [heap.alloc(4) for _ in range(3)]
+        self.send = heap.view(self.send_off, (opt.send_total,), torch.bfloat16)
+        self.back = heap.view(self.back_off, (opt.recv_total,), torch.bfloat16)
+        self.small = [heap.view(o, (self.n_small,), torch.float32) for o in self.small_off]
+        self.flags = [heap.view(o, (1,), torch.int32) for o in self.flag_off]
+        self.epoch = [0, 0, 0]
+        W, me, A = self.world, self.rank, self.all_send
+
+        def prefix(xs, k):
+            return sum(xs[:k])
+
+        # gradients: from rank r, r's block for owner `me`, into my receive layout
+        self.plan_grads = self._plan(
+            [self.send_off + 2 * prefix(A[r], me) for r in range(W)],
+            [2 * prefix([A[q][me] for q in range(W)], r) for r in range(W)],
+            [2 * A[r][me] for r in range(W)], dev)
+        # updates: from owner r, its back-region block for source `me`, into my send layout
+        self.plan_updates = self._plan(
+            [self.back_off + 2 * prefix([A[q][r] for q in range(W)], me) for r in range(W)],
+            [2 * prefix(A[me], r) for r in range(W)],
+            [2 * A[me][r] for r in range(W)], dev)
+        self.gather_small = torch.empty(W, _pad8(self.n_small), dtype=torch.float32, device=dev)
+
+    @staticmethod
+    def _plan(src, dst, lens, dev) -> torch.Tensor:
+        return torch.tensor([src, dst, lens], dtype=torch.int64, device=dev)
+
+    def _publish_and_pull(self, kind: int, dst: torch.Tensor, plan: torch.Tensor) -> None:
+        from llm_research_b200._ext import native
+
+        self.epoch[kind] += 1
+        C = native()
+        C.ep_flag_set(self.flags[kind], self.epoch[kind])
+        C.p2p_a2av_pull(dst, self.heap.bases, plan, self.flag_off[kind], self.world, self.epoch[kind], self.heap.err)
+
+    def _small_plan(self, slot: int, n: int) -> torch.Tensor:
+        row = _pad8(self.n_small) * 4
+        return self._plan([self.small_off[slot]] * self.world, [r * row for r in range(self.world)],
+                          [_pad8(n) * 4] * self.world, self.gather_small.device)
+
+    def exchange_grads(self, gsq: torch.Tensor, recv: torch.Tensor) -> torch.Tensor:
+        """Publishes the gradient pieces (already in the heap) and the norm partials;
+        pulls this rank's pieces into ``recv``; returns the summed partials."""
+        n = gsq.numel()
+        self.small[0][:n].copy_(gsq)
+        if not hasattr(self, "_plan_gsq"):
+            self._plan_gsq = self._small_plan(0, n)
+        self._publish_and_pull(self.FLAG_GRADS, recv, self.plan_grads)
+        from llm_research_b200._ext import native
+
+        # same flag and epoch: the partials were written before it was raised
+        native().p2p_a2av_pull(self.gather_small, self.heap.bases, self._plan_gsq, self.flag_off[self.FLAG_GRADS],
+                               self.world, self.epoch[self.FLAG_GRADS], self.heap.err)
+        return self.gather_small[:, :n].sum(0)
+
+    def exchange_updates(self, upd: torch.Tensor) -> None:
+        self._publish_and_pull(self.FLAG_UPDATES, upd, self.plan_updates)
+
+    def max_flags(self, flags: torch.Tensor) -> torch.Tensor:
+        n = flags.numel()
+        self.small[1][:n].copy_(flags)
+        if not hasattr(self, "_plan_flags"):
+            self._plan_flags = self._small_plan(1, n)
+        self._publish_and_pull(self.FLAG_TOUCHED, self.gather_small, self._plan_flags)
+        return self.gather_small[:, :n].amax(0)
+
+    def close(self) -> None:
+        self.heap.close()

@@ -234,9 +234,11 @@ class ExpertParallelMoE(nn.Module):
         self.last_aux: Optional[torch.Tensor] = None
 
     def experts(self, x_e: torch.Tensor) -> torch.Tensor:
-        gu = torch.bmm(x_e, self.w_up_gate.to(x_e.dtype).transpose(1, 2))  # (epl, rows, 2*d_ff) = [up | gate]
-        h = ops.swiglu(gu.reshape(-1, gu.shape[-1])).view(gu.shape[0], gu.shape[1], -1)
-        return torch.bmm(h, self.w_down.to(h.dtype).transpose(1, 2))
+        """This rank's experts on their dispatch rows ``(epl, rows, d)``: batched
+        CTA-pair GEMMs over the expert dimension (``ops.linear.grouped_swiglu``)."""
+        from llm_research_b200.ops.linear import grouped_swiglu
+
+        return grouped_swiglu(x_e, self.w_up_gate.to(x_e.dtype), self.w_down.to(x_e.dtype))
 
     def load_balance_loss(self) -> torch.Tensor:
         return self.last_aux if self.last_aux is not None else torch.zeros((), device=self.router.weight.device)

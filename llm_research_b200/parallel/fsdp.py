@@ -611,13 +611,17 @@ class FlatShardEngine(nn.Module):
                 u.compute_shard.copy_(u.master)
                 self._free(u)
 
-    def touched_params(self) -> Set[int]:
+    def touched_params(self, reduce_max: Optional[Callable[[torch.Tensor], torch.Tensor]] = None) -> Set[int]:
         """Parameters that received a gradient on any rank since ``zero_grad``
-        (optimizers skip the others, like ``p.grad is None`` in torch)."""
+        (optimizers skip the others, like ``p.grad is None`` in torch).
+        ``reduce_max``: the group-wide elementwise maximum to use instead of an
+        all-reduce (the optimizer's symmetric-memory exchange)."""
         flags = torch.zeros(len(self.params), dtype=torch.float32, device=self.device)
         if self._touched:
             flags[list(self._touched)] = 1.0
-        if self.world > 1 or self.replicas > 1:
+        if reduce_max is not None and (self.world > 1 or self.replicas > 1):
+            flags = reduce_max(flags)
+        elif self.world > 1 or self.replicas > 1:
             dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=self.pg)
         return {i for i, f in enumerate(flags.tolist()) if f > 0}
 

@@ -186,3 +186,54 @@ def test_gemm_pair_unaligned_output_takes_direct_stores(out_dtype):
     err = ((C.float() - ref).norm() / ref.norm()).item()
     assert err < 1e-2, err
     assert Cbuf[:, 0].abs().sum().item() == 0 and Cbuf[:, 265:].abs().sum().item() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("a_mn,b_mn,acc", [(False, False, False), (False, True, False), (True, True, True)])
+def test_gemm_pair_batched(a_mn, b_mn, acc):
+    """A leading batch dimension: every entry is its own GEMM (grouped experts of
+    equal shape), in one launch; ragged M / N per entry."""
+    from llm_research_b200.ops.gemm import gemm, gemm_pair_error
+
+    g = torch.Generator(device="cuda").manual_seed(17)
+    E, M, N, K = 3, 200, 392, 264
+    A = torch.randn(E, *((K, M) if a_mn else (M, K)), device="cuda", generator=g).bfloat16()
+    B = torch.randn(E, *((K, N) if b_mn else (N, K)), device="cuda", generator=g).bfloat16()
+    ref = torch.stack([_ref(A[e], B[e], a_mn, b_mn) for e in range(E)])
+    if acc:
+        C0 = torch.randn(E, M, N, device="cuda", generator=g)
+        C = C0.clone()
+        gemm(A, B, a_mn, b_mn, out=C, accumulate=True)
+        ref = ref + C0
+    else:
+        C = gemm(A, B, a_mn, b_mn)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    err = ((C.float() - ref).norm() / ref.norm()).item()
+    assert err < 1e-2, err
+
+
+@pytest.mark.gpu
+def test_grouped_swiglu_experts_match_fp32():
+    """Grouped SwiGLU experts (forward and all gradients) against fp32 autograd."""
+    from llm_research_b200.ops.gemm import gemm_pair_error
+    from llm_research_b200.ops.linear import grouped_swiglu
+
+    g = torch.Generator(device="cuda").manual_seed(19)
+    E, R, d, F = 4, 136, 256, 384
+    x = (torch.randn(E, R, d, device="cuda", generator=g)).bfloat16().requires_grad_()
+    wug = (torch.randn(E, 2 * F, d, device="cuda", generator=g) * 0.05).bfloat16().requires_grad_()
+    wd = (torch.randn(E, d, F, device="cuda", generator=g) * 0.05).bfloat16().requires_grad_()
+    dy = torch.randn(E, R, d, device="cuda", generator=g).bfloat16()
+    y = grouped_swiglu(x, wug, wd)
+    y.backward(dy)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    xf, wugf, wdf = (t.detach().float().requires_grad_() for t in (x, wug, wd))
+    gu = torch.bmm(xf, wugf.transpose(1, 2))
+    u, gt = gu.chunk(2, dim=-1)
+    yf = torch.bmm(torch.nn.functional.silu(gt) * u, wdf.transpose(1, 2))
+    yf.backward(dy.float())
+    for name, got, ref in (("y", y, yf), ("dx", x.grad, xf.grad), ("dwug", wug.grad, wugf.grad), ("dwd", wd.grad, wdf.grad)):
+        err = ((got.float() - ref).norm() / ref.norm()).item()
+        assert err < 2e-2, (name, err)

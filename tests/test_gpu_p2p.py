@@ -150,3 +150,53 @@ def test_diloco_p2p_outer_step_matches_collective():
     for r in range(world):
         torch.testing.assert_close(a[r], a[0])
         torch.testing.assert_close(b[r], a[r], atol=1e-5, rtol=1e-5)
+
+
+def _dmuon_steps(rank, world, dmuon_comm):
+    """Three MuonAdamWHybrid steps through the engine with the distributed-Muon
+    exchange on symmetric memory (P2P pulls) or on NCCL all-to-alls."""
+    import os
+
+    import torch.distributed as dist
+
+    os.environ["LRB_DMUON_COMM"] = dmuon_comm
+    from genesis.model import HLRT, HLRTConfig
+    from llm_research_b200.parallel.fsdp import FlatShardEngine
+    from olympus.optim import MuonAdamWHybrid
+
+    torch.manual_seed(0)
+    cfg = HLRTConfig(vocab_size=512, d_model=128, tier1_num_layers=2, tier1_num_heads=2, tier1_d_ff=256,
+                     gate1_chunk_size=16, num_latent_vectors=4, latent_pool_num_heads=2,
+                     tier2_d_model=128, tier2_num_layers=1, tier2_num_heads=2, tier2_d_ff=256,
+                     tier3_d_model=128, tier3_num_layers=1, tier3_num_heads=2, tier3_d_ff=256)
+    dev = torch.device("cuda", rank)
+    eng = FlatShardEngine(HLRT(cfg).to(dev), comm="nccl")
+    opt = eng.make_optimizer(MuonAdamWHybrid, {"lr_muon": 0.02, "lr_adamw": 1e-3, "momentum": 0.95,
+                                               "betas": (0.9, 0.999), "eps": 1e-8, "weight_decay_muon": 0.0,
+                                               "weight_decay_adamw": 0.01, "ns_steps": 5,
+                                               "muon_max_aspect_ratio": 8.0})
+    assert (opt.p2p is not None) == (dmuon_comm == "p2p")
+    g = torch.Generator().manual_seed(rank)
+    for _ in range(3):
+        ids = torch.randint(0, 512, (2, 64), generator=g).to(dev)
+        out = eng(ids)
+        loss = torch.nn.functional.cross_entropy(out["logits"][:, :-1].float().reshape(-1, 512), ids[:, 1:].reshape(-1))
+        loss.backward()
+        opt.step()
+        opt.zero_grad()
+    full = eng.full_state_dict()
+    if opt.p2p is not None:
+        opt.p2p.heap.check()
+        opt.p2p.close()
+    torch.cuda.synchronize()
+    dist.barrier()
+    return {k: v for k, v in full.items() if v.dim() == 2}
+
+
+@needs2
+def test_distributed_muon_p2p_exchange_matches_nccl():
+    a = run_ranks(_dmuon_steps, 2, "nccl", backend="nccl")
+    b = run_ranks(_dmuon_steps, 2, "p2p", backend="nccl")
+    assert a[0].keys() == b[0].keys() and len(a[0]) > 4
+    for k in a[0]:
+        torch.testing.assert_close(b[0][k], a[0][k], atol=2e-3, rtol=2e-2, msg=k)
