@@ -484,7 +484,8 @@ def run_reference(args) -> dict:
             m = trainer.train_step({"input_ids": b})
         return m["loss"]
 
-    for _ in range(args.warmup):
+    # the fit probe above was one whole optimizer step: it counts as a warm-up step
+    for _ in range(max(args.warmup - 1, 0)):
         step(dev_batches)
     sampler = ClockSampler(device_index=local_rank)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -63,6 +63,7 @@ std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor&, const at::T
 int64_t attn_sm100_error(int64_t);
 // attention_bwd_sm100.cu
 int64_t attn_bwd_sm100_error(int64_t);
+void attn_bwd_set_trace(const c10::optional<at::Tensor>&);
 // memory.cu
 std::tuple<at::Tensor, at::Tensor, at::Tensor> topk_softmax_gather(const at::Tensor&, const at::Tensor&, int64_t);
 std::tuple<at::Tensor, at::Tensor> memory_topk_candidates(const at::Tensor&, const at::Tensor&, int64_t);
@@ -150,6 +151,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd_sm100", &lrb::attn_fwd_sm100);
   m.def("attn_sm100_error", &lrb::attn_sm100_error);
   m.def("attn_bwd_sm100_error", &lrb::attn_bwd_sm100_error);
+  m.def("attn_bwd_set_trace", &lrb::attn_bwd_set_trace, "stage timestamps of CTA (0,0) of the next backward launches");
   m.def("topk_softmax_gather", &lrb::topk_softmax_gather);
   m.def("memory_topk_candidates", &lrb::memory_topk_candidates,
         "tcgen05 similarity + streaming top-32 per query over bank slices");

@@ -47,7 +47,35 @@ struct BwdArgs {
   int B, H, Hkv, Sq, Skv, causal;
   float scale, scale_log2;
   int* err;
+  // Stage timestamps of CTA (0, 0) (globaltimer, ns) for pipeline analysis; null
+  // in normal runs.  Layout: [event][sub-tile], kTraceT sub-tiles per event.
+  unsigned long long* trace;
 };
+
+constexpr int kTraceT = 64;
+std::atomic<unsigned long long*> g_attn_bwd_trace{nullptr};
+enum TraceEv : int {
+  kTrProdWait = 0,   // producer: slot free (after qd_free wait)
+  kTrProdDone,       // producer: LSE / D staged, arrival done
+  kTrSdpIssue,       // MMA: S^T / dP^T issued
+  kTrPWait,          // MMA: p_full passed
+  kTrAccIssue,       // MMA: dV / dK / dQ^T issued
+  kTrSmStart,        // softmax warp 2 lane 0: S^T / dP^T ready
+  kTrSmDone,         // softmax: P^T / dS^T written, p_full arrived
+  kTrDqStart,        // dQ warp: dQ^T ready
+  kTrDqFree,         // dQ warp: TMEM read, dq_free arrived
+  kTrDqStaged,       // dQ issuer: reduce-adds read the staging (stage_free)
+  kTrEvents
+};
+
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void trace_at(const BwdArgs& a, int ev, int t) {
+  if (a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && t < kTraceT) a.trace[ev * kTraceT + t] = gtime();
+}
 
 // AND of `v` over the 128 threads of named barrier `id` (also a barrier): the
 // softmax-gradient warps of one column half leave their loop together, so the
@@ -459,6 +487,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
         const int h = hk * G + t / nqt;
         const int q0 = (qt0 + t % nqt) * TQ3;
         if (!__all_sync(0xffffffffu, mbar_wait(&qd_free[sl], use ^ 1, a.err, kErrTmaWait))) break;
+        if (lane == 0) trace_at(a, kTrProdWait, t);
         if (lane == 0) {
           mbar_expect_tx(&qd_full[sl], 2 * kQ);  // the 32 arrivals come after the LSE / D staging
           unsigned char* q_ = sQ + sl * kQ;
@@ -477,6 +506,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
           sD[sl * TQ3 + c] = q < a.Sq ? di_row[q] : 0.f;
         }
         mbar_arrive(&qd_full[sl]);  // release: the LSE / D rows above are visible to the waiters
+        if (lane == 0) trace_at(a, kTrProdDone, t);
         ++loaded;
       }
       if (lane == 0) {
@@ -510,6 +540,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
           umma_f16(tP, umma_desc_k_sw128(v_ + ka), umma_desc_k_sw128(o_ + kb), id_sdp, k != 0);
         }
         umma_commit(&sdp_full[bb]);
+        trace_at(a, kTrSdpIssue, t);
         return true;
       };
       if (ok) ok = issue_sdp(0);
@@ -518,6 +549,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
         const uint32_t use = (t >> 1) & 1;
         if (t + 1 < total && !issue_sdp(t + 1)) { ok = false; break; }
         if (!mbar_wait(&p_full[bb], use, a.err, kErrMmaWait)) { ok = false; break; }
+        trace_at(a, kTrPWait, t);
         tc_fence_after();
         const uint32_t q_ = smem_addr(sQ + sl * kQ), o_ = smem_addr(sdO + sl * kQ);
         const uint32_t pt_ = smem_addr(sPD + bb * kPD), ds_ = pt_ + kPT;
@@ -534,6 +566,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
           umma_f16(tmem + bb * 128, umma_desc_mn_sw128(k_ + k * 2048, kKVHalf, 1024),
                    umma_desc_mn_sw128(ds_ + k * 2048, kPT, 1024), id_dq, k != 0);
         umma_commit(&dq_full[bb]);
+        trace_at(a, kTrAccIssue, t);
       }
       umma_commit(acc_done);
       umma_commit(drain);
@@ -559,6 +592,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
         ok = false;
         break;
       }
+      if (warp == 2 && lane == 0) trace_at(a, kTrSmStart, t);
       tc_fence_after();
       float s[32], dp[32];
       tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + c0, reinterpret_cast<uint32_t*>(s));
@@ -593,6 +627,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[bb]);
+      if (warp == 2 && lane == 0) trace_at(a, kTrSmDone, t);
     }
     // ---------------------------------------------------------- dK, dV
     const bool have = __all_sync(0xffffffffu, ok && total > 0 && mbar_wait(acc_done, 0, a.err, kErrEpiWait));
@@ -644,6 +679,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       // dq_full: dQ^T(t) is in TMEM, and every MMA of sub-tile t -- the last readers
       // of this buffer's P^T / dS^T tiles, the staging area -- has completed
       if (!group_all(1, mbar_wait(&dq_full[bb], use, a.err, kErrEpiWait))) break;
+      if (issuer) trace_at(a, kTrDqStart, t);
       tc_fence_after();
       unsigned char* sDQ = sPD + bb * kPD;  // 4 x (64 rows x 128 B), swizzled
       unsigned char* box = sDQ + (d >> 5) * (TQ3 * 128);
@@ -659,6 +695,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&dq_free[bb]);
+      if (issuer) trace_at(a, kTrDqFree, t);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (issuer) {
@@ -672,6 +709,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
         // the reduce-adds have read the staging: the softmax warps may overwrite it
         asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         mbar_arrive(&stage_free[bb]);
+        trace_at(a, kTrDqStaged, t);
       }
     }
     if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -745,7 +783,7 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
   CUtensorMap tq = bshd_map(q), tk = bshd_map(k), tv = bshd_map(v), tdo = bshd_map(dout);
   BwdArgs args{lse.data_ptr<float>(), di.data_ptr<float>(), dq_acc.data_ptr<float>(), dk.data_ptr(), dv.data_ptr(),
                (int)B, (int)H, (int)Hkv, (int)Sq, (int)Skv, causal ? 1 : 0, (float)scale, (float)scale * kLog2e,
-               bwd_error_word(q.device())};
+               bwd_error_word(q.device()), g_attn_bwd_trace.load(std::memory_order_acquire)};
   // The 64-query double-buffered kernel is the default; LRB_ATTN_BWD_V2=1 selects
   // the 128-query kernel that runs its tiles one after another.
   static const bool v2 = [] {
@@ -767,6 +805,19 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
     attn_bwd_v3_kernel<<<grid, bwd3::kThreads, bwd3::kSmem, stream()>>>(tq64, tk, tv, tdo64, tdq64, args);
   }
   LRB_LAUNCH_CHECK();
+}
+
+// Stage timestamps of the next backward launches go to `buf` (int64, at least
+// kTrEvents * kTraceT entries) -- a pipeline-analysis hook; None switches it off.
+void attn_bwd_set_trace(const c10::optional<at::Tensor>& buf) {
+  if (buf) {
+    LRB_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->is_contiguous() &&
+                  buf->numel() >= (int64_t)kTrEvents * kTraceT,
+              "attn_bwd_set_trace: an int64 CUDA buffer of ", (int64_t)kTrEvents * kTraceT, " entries");
+    g_attn_bwd_trace.store(reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>()), std::memory_order_release);
+  } else {
+    g_attn_bwd_trace.store(nullptr, std::memory_order_release);
+  }
 }
 
 int64_t attn_bwd_sm100_error(int64_t device) { return g_attn_bwd_err_word.take((int)device); }

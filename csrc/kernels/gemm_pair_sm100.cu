@@ -38,6 +38,7 @@
 #include "../common.cuh"
 #include "sm100.cuh"
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -394,8 +395,11 @@ EncodeTiledFn encode_fn() {
 CUtensorMap make_map(const void* ptr, int64_t batch, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
                      int box_cols, int box_rows, bool bf16) {
   CUtensorMap m;
+  // A single matrix gets the batch pitch of a packed stack (rows * ld): a valid
+  // 16-byte multiple that no coordinate ever steps by.
+  const int64_t bp = batch > 1 ? bstride : std::max<int64_t>(rows, 1) * ld;
   const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
-  const cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(std::max<int64_t>(bstride, 1) * 2)};
+  const cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(bp * 2)};
   const cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = encode_fn()(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
@@ -412,8 +416,9 @@ CUtensorMap make_out_map(void* ptr, int64_t batch, int64_t rows, int64_t cols, i
                          at::ScalarType t) {
   CUtensorMap m;
   const int esz = t == at::kFloat ? 4 : 2;
+  const int64_t bp = batch > 1 ? bstride : std::max<int64_t>(rows, 1) * ld;
   const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
-  const cuuint64_t strides[2] = {(cuuint64_t)(ld * esz), (cuuint64_t)(std::max<int64_t>(bstride, 1) * esz)};
+  const cuuint64_t strides[2] = {(cuuint64_t)(ld * esz), (cuuint64_t)(bp * esz)};
   const cuuint32_t box[3] = {32, 32, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapDataType dt = t == at::kFloat      ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -448,7 +453,6 @@ int max_pairs(int dev) {
   cfg.numAttrs = 1;
   auto k = gemm_pair_kernel<__nv_bfloat16, kStore, true, false, false>;
   LRB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-  cfg.numAttrs = 0;  // the kernel declares its cluster shape
   int clusters = 0;
   if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) == cudaSuccess && clusters > 0) n = std::min(n, clusters);
   (void)cudaGetLastError();
@@ -526,6 +530,8 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, a
   LRB_CHECK(A.dim() == B.dim() && A.dim() == C.dim() && a.batch == b.batch && a.batch == c.batch,
             "gemm_pair: A, B and C must all be 2-D or all 3-D with one batch size");
   LRB_CHECK(tma_ok(A, a) && tma_ok(B, b), "gemm_pair: A and B need 16-byte aligned bases and pitches");
+  LRB_CHECK(a.batch == 1 || (a.bstride >= a.rows * a.ld && b.bstride >= b.rows * b.ld && c.bstride >= c.rows * c.ld),
+            "gemm_pair: batch entries must not overlap (batch pitch >= rows * row pitch)");
   const int64_t M = a_mn ? a.cols : a.rows, K = a_mn ? a.rows : a.cols;
   const int64_t N = b_mn ? b.cols : b.rows, KB = b_mn ? b.rows : b.cols;
   LRB_CHECK(K == KB, "gemm_pair: K mismatch (", K, " vs ", KB, ")");
@@ -556,8 +562,13 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, a
   const int splits = (accumulate && aligned) ? choose_splits(tiles, maxp, nk) : 1;
   const int pairs = std::max(1, std::min(tiles * splits, maxp));
   // Raster groups of 8 tile rows; 16 when the B panel of a group is large (wide
-  // outputs), so it is streamed from DRAM fewer times.
-  const int group_m = N >= 16384 ? 16 : GROUP_M;
+  // outputs), so it is streamed from DRAM fewer times.  LRB_GEMM_GROUP_M
+  // overrides it (a tuning knob for the raster study).
+  static const int group_env = [] {
+    const char* e = std::getenv("LRB_GEMM_GROUP_M");
+    return e != nullptr ? std::atoi(e) : 0;
+  }();
+  const int group_m = group_env > 0 ? group_env : (N >= 16384 ? 16 : GROUP_M);
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   if (aligned) tc = make_out_map(C.data_ptr(), c.batch, M, N, c.ld, c.bstride, ct);

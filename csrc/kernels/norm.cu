@@ -48,6 +48,18 @@ __device__ __forceinline__ void store8(T* p, const float* f) {
 template <typename T>
 __device__ __forceinline__ float round_to(float v) { return to_f(from_f<T>(v)); }
 
+// 8 bf16 from global memory through a volatile load, which the compiler may not
+// merge with an earlier load of the same address (a second pass re-reads from
+// L1 instead of holding the whole row in registers).
+__device__ __forceinline__ void reload8_bf16(const __nv_bfloat16* p, float* f) {
+  Vec16<__nv_bfloat16> v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.raw.x), "=r"(v.raw.y), "=r"(v.raw.z), "=r"(v.raw.w)
+               : "l"(p));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = __bfloat162float(v.v[i]);
+}
+
 // ---------------------------------------------------------------- forward
 template <typename T, typename W, typename O, int NV>
 __global__ void __launch_bounds__(kWarps * 32) rmsnorm_fwd_reg(
@@ -188,6 +200,79 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(
   }
 }
 
+// bf16 rows of width d = NV * 256 (NV <= 8), one warp per row.  The second
+// pass re-reads the row's x and dy, which the first pass has just brought into
+// L1, so HBM sees each once; each warp adds its rows' weight-gradient terms to
+// its own fp32 slice of shared memory with 16-byte read-modify-writes (lane
+// stride 32 bytes: two-way at most), and the block's warps are summed once at
+// the end.
+template <int NV>
+__global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_reg(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+    const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ ds, __nv_bfloat16* __restrict__ dx,
+    float* __restrict__ dw_part, int64_t rows, int d) {
+  using T = __nv_bfloat16;
+  extern __shared__ float sh[];  // kWarps * d floats
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float* acc = sh + (size_t)wid * d;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float4* a4 = reinterpret_cast<float4*>(acc + (i * 32 + lane) * 8);
+    a4[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    a4[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + wid; row < rows; row += (int64_t)gridDim.x * kWarps) {
+    const float r = rstd[row];
+    const T* xr = x + row * d;
+    const T* gr = dy + row * d;
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      float xf[8], gf[8], wf[8];
+      load8(xr + c, xf);
+      load8(gr + c, gf);
+      load8(w + c, wf);
+      float4* a4 = reinterpret_cast<float4*>(acc + c);
+      float4 lo = a4[0], hi = a4[1];
+      float t[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xh = xf[j] * r;
+        dot += gf[j] * wf[j] * xh;
+        t[j] = gf[j] * round_to<T>(xh);
+      }
+      lo.x += t[0]; lo.y += t[1]; lo.z += t[2]; lo.w += t[3];
+      hi.x += t[4]; hi.y += t[5]; hi.z += t[6]; hi.w += t[7];
+      a4[0] = lo;
+      a4[1] = hi;
+    }
+    dot = warp_sum(dot) / d;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      float xf[8], gf[8], wf[8], o[8], dsf[8];
+      reload8_bf16(xr + c, xf);
+      reload8_bf16(gr + c, gf);
+      reload8_bf16(w + c, wf);
+      if (ds != nullptr) load8(ds + row * d + c, dsf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xh = xf[j] * r;
+        o[j] = r * (gf[j] * wf[j] - xh * dot) + (ds != nullptr ? dsf[j] : 0.f);
+      }
+      store8(dx + row * d + c, o);
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) t += sh[(size_t)k * d + c];
+    dw_part[(size_t)blockIdx.x * d + c] = t;
+  }
+}
+
 __global__ void reduce_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int nrows, int d) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= d) return;
@@ -284,9 +369,38 @@ std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::T
   if (rows == 0) return {dx, dw};
   const size_t smem = (size_t)kWarps * d * sizeof(float);
   LRB_CHECK(smem <= (size_t)kBwdSmemMax, "rmsnorm_bwd: row too wide");
+  const auto xt = x.scalar_type(), wt = w.scalar_type(), ot = dy.scalar_type();
+  const bool reg = xt == at::kBFloat16 && wt == at::kBFloat16 && ot == at::kBFloat16 && d % 256 == 0 &&
+                   d / 256 <= 8 && (!ds || ds->is_contiguous());
   int blocks = (int)std::min<int64_t>((rows + kWarps - 1) / kWarps, 2 * num_sms());
   auto part = at::empty({blocks, d}, x.options().dtype(at::kFloat));
   auto st = stream();
+  if (reg) {
+    using B16 = __nv_bfloat16;
+    auto go = [&](auto kernel) {
+      if (smem > 48 * 1024) LRB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                                (int)kBwdSmemMax));
+      kernel<<<blocks, kWarps * 32, smem, st>>>(
+          reinterpret_cast<const B16*>(dy.data_ptr()), reinterpret_cast<const B16*>(x.data_ptr()),
+          reinterpret_cast<const B16*>(w.data_ptr()), rstd.data_ptr<float>(),
+          ds ? reinterpret_cast<const B16*>(ds->data_ptr()) : nullptr, reinterpret_cast<B16*>(dx.data_ptr()),
+          part.data_ptr<float>(), rows, d);
+      LRB_LAUNCH_CHECK();
+    };
+    switch (d / 256) {
+      case 1: go(rmsnorm_bwd_reg<1>); break;
+      case 2: go(rmsnorm_bwd_reg<2>); break;
+      case 3: go(rmsnorm_bwd_reg<3>); break;
+      case 4: go(rmsnorm_bwd_reg<4>); break;
+      case 5: go(rmsnorm_bwd_reg<5>); break;
+      case 6: go(rmsnorm_bwd_reg<6>); break;
+      case 7: go(rmsnorm_bwd_reg<7>); break;
+      default: go(rmsnorm_bwd_reg<8>); break;
+    }
+    reduce_rows_kernel<<<(d + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), dw.data_ptr<float>(), blocks, d);
+    LRB_LAUNCH_CHECK();
+    return {dx, dw};
+  }
   auto run = [&](auto tag_t, auto tag_w, auto tag_o) {
     using T = decltype(tag_t);
     using W = decltype(tag_w);
@@ -300,7 +414,6 @@ std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::T
         part.data_ptr<float>(), rows, d);
     LRB_LAUNCH_CHECK();
   };
-  const auto xt = x.scalar_type(), wt = w.scalar_type(), ot = dy.scalar_type();
   if (xt == at::kBFloat16 && wt == at::kBFloat16 && ot == at::kBFloat16) run(__nv_bfloat16{}, __nv_bfloat16{}, __nv_bfloat16{});
   else if (xt == at::kBFloat16 && wt == at::kFloat && ot == at::kFloat) run(__nv_bfloat16{}, float{}, float{});
   else if (xt == at::kFloat && wt == at::kFloat && ot == at::kFloat) run(float{}, float{}, float{});

@@ -35,3 +35,19 @@ def test_bench_py_has_no_undefined_names():
 
 def test_graft_entry_has_no_undefined_names():
     assert _undefined(os.path.join(ROOT, "__graft_entry__.py")) == []
+
+
+def test_reference_arm_config_matches_the_preset():
+    """The reference arm's model fields are written out in bench.py (so that its
+    process imports nothing from this repository); they must be the preset's."""
+    import importlib.util
+
+    from llm_research_b200.models.presets import build_hlrt_config
+
+    spec = importlib.util.spec_from_file_location("bench_under_test", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    for preset, fields in bench.REFERENCE_FIELDS.items():
+        cfg = build_hlrt_config(preset)
+        for k, v in fields.items():
+            assert getattr(cfg, k) == v, (preset, k)

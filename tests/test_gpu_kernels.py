@@ -23,13 +23,15 @@ def _rms_ref(x, w, eps):
     return n.float() * w.float()
 
 
-@pytest.mark.parametrize("d", [64, 96, 2048, 4096])
+@pytest.mark.parametrize("d,rows", [(64, 37), (96, 37), (768, 37), (2048, 37), (4096, 37), (2048, 5000)])
 @pytest.mark.parametrize("residual", [False, True])
-def test_rmsnorm_fwd_bwd(d, residual):
+def test_rmsnorm_fwd_bwd(d, rows, residual):
+    """d a multiple of 256 up to 2048 takes the one-HBM-read backward (rows over
+    several blocks and several rows per warp with 5000 rows)."""
     from llm_research_b200 import ops
 
-    x = torch.randn(37, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    r = torch.randn(37, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    x = torch.randn(rows, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    r = torch.randn(rows, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     w = (1 + 0.1 * torch.randn(d, device="cuda")).to(torch.bfloat16).requires_grad_(True)
     if residual:
         y, s = ops.rms_norm_residual(x, r, w, 1e-6)
@@ -47,7 +49,7 @@ def test_rmsnorm_fwd_bwd(d, residual):
     outr.backward()
     torch.testing.assert_close(y.float(), yr.detach(), atol=3e-2, rtol=3e-2)
     torch.testing.assert_close(x.grad.float(), xr.grad, atol=3e-2, rtol=3e-2)
-    torch.testing.assert_close(w.grad.float(), wr.grad, atol=0.5, rtol=3e-2)
+    torch.testing.assert_close(w.grad.float(), wr.grad, atol=0.5 * max(1.0, rows / 37) ** 0.5, rtol=3e-2)
     if residual:
         torch.testing.assert_close(r.grad.float(), rr.grad, atol=3e-2, rtol=3e-2)
 
