@@ -14,6 +14,7 @@ std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor&, const at::Tens
 // elementwise.cu
 at::Tensor swiglu_fwd(const at::Tensor&);
 at::Tensor swiglu_bwd(const at::Tensor&, const at::Tensor&);
+at::Tensor exp2_fma_eval(const at::Tensor&);
 std::tuple<at::Tensor, at::Tensor, at::Tensor> rope_qkv_fwd(const at::Tensor&, const at::Tensor&, const at::Tensor&,
                                                             int64_t, int64_t, int64_t, int64_t);
 at::Tensor rope_qkv_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
@@ -57,6 +58,7 @@ int64_t sm100_error(int64_t);
 // gemm_pair_sm100.cu
 void gemm_pair(const at::Tensor&, const at::Tensor&, bool, bool, at::Tensor&, bool, double);
 int64_t gemm_pair_error(int64_t);
+void gemm_pair_swiglu(const at::Tensor&, const at::Tensor&, const at::Tensor&, at::Tensor&, at::Tensor&);
 // attention_sm100.cu
 bool attn_sm100_supported(const at::Tensor&, const at::Tensor&, const at::Tensor&);
 std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor&, const at::Tensor&, const at::Tensor&, bool, double);
@@ -117,6 +119,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_bwd", &lrb::rmsnorm_bwd);
   m.def("swiglu_fwd", &lrb::swiglu_fwd);
   m.def("swiglu_bwd", &lrb::swiglu_bwd);
+  m.def("exp2_fma_eval", &lrb::exp2_fma_eval, "2^x by the FMA-pipe polynomial of the attention softmax");
   m.def("rope_qkv_fwd", &lrb::rope_qkv_fwd);
   m.def("rope_qkv_bwd", &lrb::rope_qkv_bwd);
   m.def("ce_fwd", &lrb::ce_fwd);
@@ -147,6 +150,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair", &lrb::gemm_pair,
         "C (=|+=) alpha op(A) op(B)^T on CTA pairs (tcgen05 cta_group::2); a_mn/b_mn: operand stored (K, M)/(K, N)");
   m.def("gemm_pair_error", &lrb::gemm_pair_error);
+  m.def("gemm_pair_swiglu", &lrb::gemm_pair_swiglu, "gu = [x W1^T | x Wg^T], h = silu(x Wg^T) * x W1^T in one launch");
   m.def("attn_sm100_supported", &lrb::attn_sm100_supported);
   m.def("attn_fwd_sm100", &lrb::attn_fwd_sm100);
   m.def("attn_sm100_error", &lrb::attn_sm100_error);

@@ -85,6 +85,23 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, for spreading a softmax's exponentials over both the
+// SFU and the FMA units: x = i + f with i = floor(x) and f in [0, 1); 2^f is
+// the degree-3 minimax polynomial of 2^f on [0, 1] with p(0) = 1, its three
+// coefficients found by the Remez exchange algorithm (maximum relative error
+// 8.6e-5 -- far below the bf16 rounding of a probability); 2^i is added into
+// the exponent field.  Inputs are clamped at -127, where the result is +0
+// exactly (so a masked -inf score gives a zero probability); valid up to 2^127.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -127.f);
+  const int i = __float2int_rd(x);
+  const float f = x - __int2float_rn(i);
+  float p = fmaf(f, 0.07706704f, 0.22764500f);
+  p = fmaf(f, p, 0.69511676f);
+  p = fmaf(f, p, 1.0f);
+  return __int_as_float(__float_as_int(p) + (i << 23));
+}
+
 // ---- reductions ----------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

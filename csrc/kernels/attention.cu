@@ -206,6 +206,33 @@ __global__ void attn_dot_kernel(const T* __restrict__ dout, const T* __restrict_
   }
 }
 
+// D = rowsum(dO * O) for head_dim 128: eight lanes per (b, q, h) row, each with
+// two 16-byte loads per tensor; the partial sums meet through three shuffles.
+// Grid-stride over rows, so a few blocks per SM stream the two tensors once.
+template <typename T>
+__global__ void __launch_bounds__(256) attn_dot128_kernel(const T* __restrict__ dout, const T* __restrict__ out,
+                                                           float* __restrict__ di, int B, int Sq, int H) {
+  const int64_t rows = (int64_t)B * Sq * H;
+  const int sub = threadIdx.x & 7;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3; row < rows;
+       row += ((int64_t)gridDim.x * blockDim.x) >> 3) {
+    const T* a = dout + row * 128 + sub * 16;
+    const T* o = out + row * 128 + sub * 16;
+    const Vec16<T> a0 = ld16(a), a1 = ld16(a + 8), o0 = ld16(o), o1 = ld16(o + 8);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += to_f(a0.v[i]) * to_f(o0.v[i]) + to_f(a1.v[i]) * to_f(o1.v[i]);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if (sub == 0) {
+      const int h = (int)(row % H);
+      const int64_t bq = row / H;
+      di[((int64_t)(bq / Sq) * H + h) * Sq + (int)(bq % Sq)] = s;
+    }
+  }
+}
+
 template <typename T, int D, int BMQ>
 __global__ void __launch_bounds__(128) attn_bwd_kernel(const AttnParams p) {
   constexpr int BN = 64, NW = 4, LD = D + 8, LDS = BMQ + 8, CPR = D / 8;
@@ -510,7 +537,18 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> attn_bwd(const at::Tensor& dout, 
       case 32: dot(std::integral_constant<int, 32>{}); break;
       case 64: dot(std::integral_constant<int, 64>{}); break;
       case 96: dot(std::integral_constant<int, 96>{}); break;
-      case 128: dot(std::integral_constant<int, 128>{}); break;
+      case 128:
+        if (dout.is_contiguous() && out.is_contiguous() && reinterpret_cast<uintptr_t>(dout.data_ptr()) % 16 == 0 &&
+            reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0) {
+          const int64_t threads = rows * 8;
+          attn_dot128_kernel<T><<<(unsigned)std::min<int64_t>((threads + 255) / 256, (int64_t)num_sms() * 8), 256, 0,
+                                  stream()>>>(reinterpret_cast<const T*>(dout.data_ptr()),
+                                              reinterpret_cast<const T*>(out.data_ptr()), di.data_ptr<float>(),
+                                              (int)B, (int)Sq, (int)H);
+        } else {
+          dot(std::integral_constant<int, 128>{});
+        }
+        break;
       default: LRB_CHECK(false, "attention: unsupported head_dim");
     }
     LRB_LAUNCH_CHECK();

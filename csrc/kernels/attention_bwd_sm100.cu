@@ -525,12 +525,14 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       constexpr uint32_t id_dq = umma_idesc_f16_major(128, TQ3, true, true, true);     // both MN-major
       const uint32_t k_ = smem_addr(sK), v_ = smem_addr(sV);
       bool ok = mbar_wait(kv_full, 0, a.err, kErrMmaWait);
-      auto issue_sdp = [&](int t) -> bool {
+      // Event-driven issue: the thread polls the conditions of both pending
+      // steps and issues whichever is ready, so a finished softmax of one
+      // buffer never waits behind the other buffer's dQ read-out.  Steps:
+      //   S^T / dP^T of sub-tile ns: its Q / dO slot landed and the dQ^T of
+      //     sub-tile ns-2 (same TMEM buffer) has been read out;
+      //   dV / dK / dQ^T of sub-tile na (in order): its P^T / dS^T are written.
+      auto issue_sdp = [&](int t) {
         const int bb = t & 1, sl = t % kRing;
-        const uint32_t use = (t >> 1) & 1;
-        if (!mbar_wait(&qd_full[sl], (uint32_t)(t / kRing) & 1, a.err, kErrMmaWait)) return false;
-        if (t >= 2 && !mbar_wait(&dq_free[bb], use ^ 1, a.err, kErrMmaWait)) return false;  // dQ^T(t-2) read out
-        tc_fence_after();
         const uint32_t q_ = smem_addr(sQ + sl * kQ), o_ = smem_addr(sdO + sl * kQ);
         const uint32_t tS = tmem + bb * 128, tP = tS + 64;
 #pragma unroll
@@ -541,16 +543,9 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
         }
         umma_commit(&sdp_full[bb]);
         trace_at(a, kTrSdpIssue, t);
-        return true;
       };
-      if (ok) ok = issue_sdp(0);
-      for (int t = 0; t < total && ok; ++t) {
+      auto issue_acc = [&](int t) {
         const int bb = t & 1, sl = t % kRing;
-        const uint32_t use = (t >> 1) & 1;
-        if (t + 1 < total && !issue_sdp(t + 1)) { ok = false; break; }
-        if (!mbar_wait(&p_full[bb], use, a.err, kErrMmaWait)) { ok = false; break; }
-        trace_at(a, kTrPWait, t);
-        tc_fence_after();
         const uint32_t q_ = smem_addr(sQ + sl * kQ), o_ = smem_addr(sdO + sl * kQ);
         const uint32_t pt_ = smem_addr(sPD + bb * kPD), ds_ = pt_ + kPT;
 #pragma unroll
@@ -567,6 +562,34 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
                    umma_desc_mn_sw128(ds_ + k * 2048, kPT, 1024), id_dq, k != 0);
         umma_commit(&dq_full[bb]);
         trace_at(a, kTrAccIssue, t);
+      };
+      int ns = 0, na = 0;
+      uint32_t idle = 0;
+      while (ok && na < total) {
+        bool did = false;
+        if (ns < total && ns <= na + 1) {
+          const int bb = ns & 1, sl = ns % kRing;
+          if (mbar_try_wait(&qd_full[sl], (uint32_t)(ns / kRing) & 1) &&
+              (ns < 2 || mbar_try_wait(&dq_free[bb], (((uint32_t)ns >> 1) & 1) ^ 1))) {
+            tc_fence_after();
+            issue_sdp(ns++);
+            did = true;
+          }
+        }
+        if (!did && na < ns && mbar_try_wait(&p_full[na & 1], ((uint32_t)na >> 1) & 1)) {
+          trace_at(a, kTrPWait, na);
+          tc_fence_after();
+          issue_acc(na++);
+          did = true;
+        }
+        if (did) {
+          idle = 0;
+        } else if (++idle > kSpinLimit) {
+          record_error(a.err, kErrMmaWait);
+          ok = false;
+        } else if ((idle & 1023u) == 0 && *reinterpret_cast<volatile int*>(a.err) != 0) {
+          ok = false;  // another role gave up: stop issuing
+        }
       }
       umma_commit(acc_done);
       umma_commit(drain);
@@ -683,18 +706,15 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       tc_fence_after();
       unsigned char* sDQ = sPD + bb * kPD;  // 4 x (64 rows x 128 B), swizzled
       unsigned char* box = sDQ + (d >> 5) * (TQ3 * 128);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + c * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          *reinterpret_cast<float*>(box + (c * 32 + e) * 128 + ((chunk ^ (e & 7)) * 16) + sub) =
-              __uint_as_float(r[e]) * a.scale;
-      }
+      uint32_t r[64];
+      tmem_ld_32x32b_x32(tmem + lane_base + bb * 128, r);  // both loads in flight, one wait
+      tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + 32, r + 32);
+      tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(&dq_free[bb]);
+      mbar_arrive(&dq_free[bb]);  // dQ^T is in registers: the MMAs may reuse the columns
+#pragma unroll
+      for (int e = 0; e < 64; ++e)
+        *reinterpret_cast<float*>(box + e * 128 + ((chunk ^ (e & 7)) * 16) + sub) = __uint_as_float(r[e]) * a.scale;
       if (issuer) trace_at(a, kTrDqFree, t);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       asm volatile("bar.sync 1, 128;" ::: "memory");

@@ -287,4 +287,24 @@ at::Tensor rope_qkv_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Te
   return dqkv;
 }
 
+
+// y = exp2_fma(x) elementwise (fp32): the FMA-pipe 2^x of the attention softmax,
+// exposed so its accuracy can be checked against the library's exp2.
+__global__ void exp2_fma_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = exp2_fma(x[i]);
+}
+
+at::Tensor exp2_fma_eval(const at::Tensor& x) {
+  LRB_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous(), "exp2_fma_eval: contiguous fp32 CUDA");
+  c10::cuda::CUDAGuard g(x.device());
+  auto y = at::empty_like(x);
+  const int64_t n = x.numel();
+  if (n == 0) return y;
+  exp2_fma_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, stream()>>>(x.data_ptr<float>(),
+                                                                                          y.data_ptr<float>(), n);
+  LRB_LAUNCH_CHECK();
+  return y;
+}
+
 }  // namespace lrb

@@ -69,7 +69,13 @@ constexpr uint32_t kOutBox = 32 * 32 * 4;
 constexpr uint32_t kOutSmem = 4 * 2 * kOutBox;  // 32 KB
 constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + kOutSmem + 256;
 
-enum Epi : int { kStore = 0, kAccumF32 = 1 };
+// kSwiGLU: the up / gate projection of a SwiGLU FFN.  CTA rank 0 loads its B
+// half from W1 (map tmB) and rank 1 from W_gate (map tmB2), both at rows
+// [tn * 128, +128), so accumulator columns 0..127 hold u = x W1^T and 128..255
+// g = x W_gate^T of the same 128 hidden units.  The epilogue writes u and g into
+// gu (rows x 2F: [u | g], kept for the backward) through tmC and
+// h = silu(g) * u through tmH, each from the bf16-rounded u and g.
+enum Epi : int { kStore = 0, kAccumF32 = 1, kSwiGLU = 2 };
 
 struct PairArgs {
   void* C;
@@ -213,7 +219,8 @@ __device__ __forceinline__ void load_stage(unsigned char* sa, unsigned char* sb,
 template <typename OutT, int EPI, bool BF16IN, bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, PairArgs args) {
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmB2,
+                     const __grid_constant__ CUtensorMap tmH, PairArgs args) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sA = base;
@@ -231,7 +238,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = (int)cluster_id_x(), npairs = (int)nclusters_x();
-  const int tiles_m = (args.M + 2 * BM - 1) / (2 * BM), tiles_n = (args.N + BN - 1) / BN;
+  constexpr int TN = EPI == kSwiGLU ? BN / 2 : BN;  // output columns per tile (h columns for kSwiGLU)
+  const int tiles_m = (args.M + 2 * BM - 1) / (2 * BM), tiles_n = (args.N + TN - 1) / TN;
   const int num_tiles = tiles_m * tiles_n * args.batch;
   const int nk = (args.K + BK - 1) / BK;
   const int num_units = num_tiles * args.splits;
@@ -250,6 +258,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (args.tma_out) tma_prefetch_desc(&tmC);
+    if constexpr (EPI == kSwiGLU) {
+      tma_prefetch_desc(&tmB2);
+      tma_prefetch_desc(&tmH);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -269,12 +281,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int unit = pair; unit < num_units && ok; unit += npairs) {
         int tm, tn, kb0, kb1, bi;
         unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1, bi);
-        const int m0 = tm * 2 * BM + (int)rank * BM, n0 = tn * BN + (int)rank * (BN / 2);
+        const int m0 = tm * 2 * BM + (int)rank * BM;
+        const int n0 = EPI == kSwiGLU ? tn * (BN / 2) : tn * BN + (int)rank * (BN / 2);
+        const CUtensorMap* mb = (EPI == kSwiGLU && rank == 1) ? &tmB2 : &tmB;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrTmaWait)) { ok = false; break; }
           const uint32_t fb = mapa_shared(smem_addr(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStage);
-          load_stage<A_MN, B_MN>(sA + stage * kHalfA, sB + stage * kHalfB, &tmA, &tmB, fb, m0, n0, kb * BK, bi);
+          load_stage<A_MN, B_MN>(sA + stage * kHalfA, sB + stage * kHalfB, &tmA, mb, fb, m0, n0, kb * BK, bi);
           ++armed;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -331,6 +345,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&accfull[acc], acc_phase, err, kErrEpiWait)) break;
       tc_fence_after();
       const int row0 = tm * 2 * BM + (int)rank * BM + q * 32;
+      // one 32 x 32 box through the staging ring: stage this thread's row, TMA-store it
+      auto put_box = [&](const CUtensorMap* map, const uint32_t* r, int x) {
+        unsigned char* box = boxes + (nbox & 1) * kOutBox;
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncwarp();
+        stage_row<__nv_bfloat16>(box, lane, 1.f, r);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_box(map, box, x, row0, bi);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        ++nbox;
+      };
+      if constexpr (EPI == kSwiGLU) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t u[32], g[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), u);
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + 128 + c * 32), g);
+          tmem_ld_wait();
+          if (c == 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&accempty[acc]), 0));
+          }
+          const int col0 = tn * (BN / 2) + c * 32;
+          if (row0 >= args.M || col0 >= args.N) continue;
+          uint32_t h[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float uf = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[j])));
+            const float gf = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[j])));
+            h[j] = __float_as_uint(gf * (1.f / (1.f + __expf(-gf))) * uf);
+          }
+          put_box(&tmC, u, col0);
+          put_box(&tmC, g, args.N + col0);
+          put_box(&tmH, h, col0);
+        }
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -461,10 +517,11 @@ int max_pairs(int dev) {
 }
 
 template <typename OutT, int EPI, bool BF16IN, bool A_MN, bool B_MN>
-void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const PairArgs& args, int pairs) {
+void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const PairArgs& args, int pairs,
+              const CUtensorMap* tb2 = nullptr, const CUtensorMap* th = nullptr) {
   auto k = gemm_pair_kernel<OutT, EPI, BF16IN, A_MN, B_MN>;
   LRB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-  k<<<2 * pairs, kThreads, kSmem, stream()>>>(ta, tb, tc, args);
+  k<<<2 * pairs, kThreads, kSmem, stream()>>>(ta, tb, tc, tb2 ? *tb2 : tb, th ? *th : tc, args);
   LRB_LAUNCH_CHECK();
 }
 
@@ -587,6 +644,35 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, a
     if (bf) launch_layout<float, kStore, true>(a_mn, b_mn, ta, tb, tc, args, pairs);
     else launch_layout<float, kStore, false>(a_mn, b_mn, ta, tb, tc, args, pairs);
   }
+}
+
+// SwiGLU up / gate projection: gu = [x W1^T | x W_gate^T] (rows x 2F) and
+// h = silu(x W_gate^T) * (x W1^T) (rows x F) in one launch; bf16, all K-major.
+void gemm_pair_swiglu(const at::Tensor& X, const at::Tensor& W1, const at::Tensor& Wg, at::Tensor& GU, at::Tensor& Hout) {
+  const Mat x = check_operand(X, "x", true), w1 = check_operand(W1, "w1", true), wg = check_operand(Wg, "w_gate", true);
+  const Mat gu = check_operand(GU, "gu", false), hm = check_operand(Hout, "h", false);
+  LRB_CHECK(X.dim() == 2 && W1.dim() == 2 && Wg.dim() == 2 && GU.dim() == 2 && Hout.dim() == 2,
+            "gemm_pair_swiglu: 2-D operands");
+  LRB_CHECK(X.scalar_type() == at::kBFloat16 && W1.scalar_type() == at::kBFloat16 && Wg.scalar_type() == at::kBFloat16 &&
+                GU.scalar_type() == at::kBFloat16 && Hout.scalar_type() == at::kBFloat16,
+            "gemm_pair_swiglu: bf16 operands");
+  const int64_t M = x.rows, K = x.cols, F = w1.rows;
+  LRB_CHECK(w1.cols == K && wg.cols == K && wg.rows == F && gu.rows == M && gu.cols == 2 * F && hm.rows == M &&
+                hm.cols == F,
+            "gemm_pair_swiglu: shape mismatch");
+  LRB_CHECK(tma_ok(X, x) && tma_ok(W1, w1) && tma_ok(Wg, wg) && tma_ok(GU, gu) && tma_ok(Hout, hm),
+            "gemm_pair_swiglu: 16-byte aligned bases and pitches required");
+  c10::cuda::CUDAGuard g(X.device());
+  if (M == 0 || F == 0) return;
+  CUtensorMap ta = make_map(X.data_ptr(), 1, M, K, x.ld, 0, BK, BM, true);
+  CUtensorMap tb = make_map(W1.data_ptr(), 1, F, K, w1.ld, 0, BK, BN / 2, true);
+  CUtensorMap tb2 = make_map(Wg.data_ptr(), 1, F, K, wg.ld, 0, BK, BN / 2, true);
+  CUtensorMap tc = make_out_map(GU.data_ptr(), 1, M, 2 * F, gu.ld, 0, at::kBFloat16);
+  CUtensorMap th = make_out_map(Hout.data_ptr(), 1, M, F, hm.ld, 0, at::kBFloat16);
+  const int tiles = (int)(((M + 2 * BM - 1) / (2 * BM)) * ((F + BN / 2 - 1) / (BN / 2)));
+  const int pairs = std::max(1, std::min(tiles, max_pairs(X.get_device())));
+  PairArgs args{GU.data_ptr(), gu.ld, (int)M, (int)F, (int)K, 1.f, 1, 1, 1, GROUP_M, 1, 0};
+  launch_t<__nv_bfloat16, kSwiGLU, true, false, false>(ta, tb, tc, args, pairs, &tb2, &th);
 }
 
 // Returns and clears the error word of the pair GEMM on `device` (0 = no timeout).

@@ -1,7 +1,7 @@
 // Blackwell (sm_100a) device primitives: mbarriers with bounded waits, TMA
 // tile loads, tcgen05 MMA / TMEM management, UMMA descriptors.
 //
-// Every wait is bounded: after kSpinLimit polls it records an error code in
+// Every wait is bounded: after kWaitLimitNs of wall time it records an error code in
 // the caller's flag and returns false instead of spinning forever.
 #pragma once
 #include <cuda.h>
@@ -56,14 +56,44 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Returns false (and records `code`) if the phase did not complete in time.
+// try_wait that lets the hardware suspend the thread for up to `ns` nanoseconds
+// while the phase is incomplete (it resumes as soon as the phase completes), so
+// a waiting warp issues no instructions instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// A wait gives up after this much wall time (far above any legitimate wait).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Returns false (and records `code`) if the phase did not complete in time.  The
+// thread sleeps in the barrier between polls; the error word (another role gave
+// up) and the wall-time bound are checked whenever a sleep runs out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return false;
+    if (global_ns() - start > kWaitLimitNs) {
+      record_error(err, code);
+      return false;
+    }
   }
-  record_error(err, code);
-  return false;
 }
 
 // ---------------------------------------------------------------- TMA

@@ -13,7 +13,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from llm_research_b200 import ops
-from llm_research_b200.ops.linear import cat_rows, project
+from llm_research_b200.ops.linear import cat_rows, project, swiglu_up
 
 
 def default_ffn_dim(d_model: int) -> int:
@@ -52,6 +52,10 @@ class SwiGLUFFN(nn.Module):
         return row_parallel(self.dropout(h), self.w2.weight, group, comm)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.w1.bias is None and not isinstance(self.dropout, nn.Dropout):
+            h = swiglu_up(x, self.w1.weight, self.w_gate.weight)  # one launch: both projections + gating
+            if h is not None:
+                return project(h, self.w2.weight, self.w2.bias)
         w = cat_rows(self.w1.weight, self.w_gate.weight)
         b = None
         if self.w1.bias is not None:

@@ -303,3 +303,61 @@ def grouped_swiglu(x_e: torch.Tensor, w_ug: torch.Tensor, w_down: torch.Tensor) 
     gu = torch.bmm(x_e, w_ug.transpose(1, 2))
     h = swiglu(gu.reshape(-1, F2)).view(E, R, -1)
     return torch.bmm(h, w_down.transpose(1, 2))
+
+
+# ------------------------------------------------------- fused SwiGLU up/gate
+class _SwiGLUUpFn(torch.autograd.Function):
+    """``h = silu(x W_gate^T) * (x W1^T)`` with both projections and the gating in
+    one CTA-pair launch (``gemm_pair_swiglu``); ``gu = [u | g]`` is kept for the
+    backward: ``dgu = swiglu_bwd(dh, gu)``, ``dx = dgu [W1; W_gate]``,
+    ``[dW1; dW_gate] = dgu^T x`` (added straight into the engine's fp32 buffer
+    when the two weights' accumulators are adjacent)."""
+
+    @staticmethod
+    def forward(ctx, x2d, w1, wg, acc):
+        from llm_research_b200._ext import native
+
+        F = w1.shape[0]
+        gu = torch.empty(x2d.shape[0], 2 * F, dtype=x2d.dtype, device=x2d.device)
+        h = torch.empty(x2d.shape[0], F, dtype=x2d.dtype, device=x2d.device)
+        native().gemm_pair_swiglu(x2d, w1, wg, gu, h)
+        ctx.save_for_backward(x2d, w1, wg, gu)
+        ctx.acc = acc
+        return h
+
+    @staticmethod
+    def backward(ctx, dh):
+        from llm_research_b200._ext import native
+        from llm_research_b200.ops.gemm import linear_dgrad, linear_wgrad
+
+        x2d, w1, wg, gu = ctx.saved_tensors
+        dgu = native().swiglu_bwd(_rows(dh), gu)
+        w = w1.as_strided((2 * w1.shape[0], w1.shape[1]), (w1.shape[1], 1)) if _adjacent([w1, wg]) \
+            else torch.cat([w1, wg], 0)
+        dx = linear_dgrad(dgu, w) if ctx.needs_input_grad[0] else None
+        dw1 = dwg = None
+        if ctx.needs_input_grad[1] or ctx.needs_input_grad[2]:
+            if ctx.acc is not None:
+                linear_wgrad(dgu, x2d, out=ctx.acc, accumulate=True)
+                dw1, dwg = accumulated_marker(w1), accumulated_marker(wg)
+            else:
+                dw = linear_wgrad(dgu, x2d)
+                dw1, dwg = dw[: w1.shape[0]], dw[w1.shape[0]:]
+        ctx.acc = None
+        return dx, dw1, dwg, None
+
+
+def swiglu_up(x: torch.Tensor, w1: torch.Tensor, wg: torch.Tensor) -> torch.Tensor:
+    """``silu(x W_gate^T) * (x W1^T)`` over the last dimension of ``x`` (bf16 CUDA,
+    shapes the pair kernel takes), or None when the fused path does not apply."""
+    if not (_PRECISION == "bf16" and x.is_cuda and x.dtype == torch.bfloat16 and x.numel() > 0
+            and _pair_ok(x, w1) and _pair_ok(x, wg) and w1.shape == wg.shape):
+        return None
+    x2d = _rows(x.reshape(-1, x.shape[-1]))
+    acc = None
+    if torch.is_grad_enabled() and (w1.requires_grad or wg.requires_grad) and _DIRECT_ACC:
+        a1, ag = getattr(w1, "_lrb_acc", None), getattr(wg, "_lrb_acc", None)
+        if a1 is not None and ag is not None and _adjacent([a1, ag]):
+            acc = a1.as_strided((2 * a1.shape[0], a1.shape[1]), (a1.shape[1], 1))
+    h = _SwiGLUUpFn.apply(x2d, w1, wg, acc)
+    return h.view(*x.shape[:-1], w1.shape[0])

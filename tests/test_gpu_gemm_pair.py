@@ -239,3 +239,34 @@ def test_grouped_swiglu_experts_match_fp32():
     for name, got, ref in (("y", y, yf), ("dx", x.grad, xf.grad), ("dwug", wug.grad, wugf.grad), ("dwd", wd.grad, wdf.grad)):
         err = ((got.float() - ref).norm() / ref.norm()).item()
         assert err < 2e-2, (name, err)
+
+
+@pytest.mark.gpu
+def test_swiglu_up_projection_matches_two_kernel_path():
+    """One launch for [x W1^T | x Wg^T] and silu(g) * u, forward and backward,
+    against the unfused GEMM + SwiGLU kernel and an fp32 oracle; ragged F and rows."""
+    from llm_research_b200.ops.activation import swiglu
+    from llm_research_b200.ops.gemm import gemm_pair_error
+    from llm_research_b200.ops.linear import cat_rows, linear_bf16, swiglu_up
+
+    g = torch.Generator(device="cuda").manual_seed(23)
+    T, K, F = 1000, 512, 392
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16().requires_grad_()
+    wbuf = (torch.randn(2 * F, K, device="cuda", generator=g) * 0.05).bfloat16()
+    w1 = wbuf[:F].clone().requires_grad_()
+    wg = wbuf[F:].clone().requires_grad_()
+    dh = torch.randn(T, F, device="cuda", generator=g).bfloat16()
+    h = swiglu_up(x, w1, wg)
+    h.backward(dh)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    x2, w12, wg2 = (t.detach().clone().requires_grad_() for t in (x, w1, wg))
+    h2 = swiglu(linear_bf16(x2, torch.cat([w12, wg2], 0)))
+    h2.backward(dh)
+    torch.testing.assert_close(h, h2, atol=2e-2, rtol=2e-2)
+    xf, w1f, wgf = (t.detach().float().requires_grad_() for t in (x, w1, wg))
+    hf = torch.nn.functional.silu(xf @ wgf.t()) * (xf @ w1f.t())
+    hf.backward(dh.float())
+    for name, got, ref in (("h", h, hf), ("dx", x.grad, xf.grad), ("dw1", w1.grad, w1f.grad), ("dwg", wg.grad, wgf.grad)):
+        err = ((got.float() - ref).norm() / ref.norm()).item()
+        assert err < 2e-2, (name, err)
