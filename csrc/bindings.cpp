@@ -58,7 +58,10 @@ int64_t sm100_error(int64_t);
 // gemm_pair_sm100.cu
 void gemm_pair(const at::Tensor&, const at::Tensor&, bool, bool, at::Tensor&, bool, double);
 int64_t gemm_pair_error(int64_t);
+void gemm_pair_set_trace(const c10::optional<at::Tensor>&);
 void gemm_pair_swiglu(const at::Tensor&, const at::Tensor&, const at::Tensor&, at::Tensor&, at::Tensor&);
+void gemm_pair_rope(const at::Tensor&, const at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t,
+                    int64_t, int64_t);
 // attention_sm100.cu
 bool attn_sm100_supported(const at::Tensor&, const at::Tensor&, const at::Tensor&);
 std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor&, const at::Tensor&, const at::Tensor&, bool, double);
@@ -150,6 +153,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair", &lrb::gemm_pair,
         "C (=|+=) alpha op(A) op(B)^T on CTA pairs (tcgen05 cta_group::2); a_mn/b_mn: operand stored (K, M)/(K, N)");
   m.def("gemm_pair_error", &lrb::gemm_pair_error);
+  m.def("gemm_pair_rope", &lrb::gemm_pair_rope, "QKV projection with RoPE on the query/key heads in the epilogue");
+  m.def("gemm_pair_set_trace", &lrb::gemm_pair_set_trace, "pipeline trace of the pair GEMM (None switches it off)");
   m.def("gemm_pair_swiglu", &lrb::gemm_pair_swiglu, "gu = [x W1^T | x Wg^T], h = silu(x Wg^T) * x W1^T in one launch");
   m.def("attn_sm100_supported", &lrb::attn_sm100_supported);
   m.def("attn_fwd_sm100", &lrb::attn_fwd_sm100);

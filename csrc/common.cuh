@@ -85,6 +85,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 1/x with the SFU instruction (rcp.approx, flush-to-zero; 1/inf = +0).
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // 2^x on the FMA pipe, for spreading a softmax's exponentials over both the
 // SFU and the FMA units: x = i + f with i = floor(x) and f in [0, 1); 2^f is
 // the degree-3 minimax polynomial of 2^f on [0, 1] with p(0) = 1, its three

@@ -552,11 +552,8 @@ __global__ void __launch_bounds__(fwd2::kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          // every fourth pair on the FMA pipe, the rest on the SFU (both pipes saturate together)
-          const float a0 = fmaf(masked(lo[2 * i], j * TK + cc * 32 + 2 * i), c, nm);
-          const float a1 = fmaf(masked(lo[2 * i + 1], j * TK + cc * 32 + 2 * i + 1), c, nm);
-          const float p0 = (i & 3) == 3 ? exp2_fma(a0) : fast_exp2(a0);
-          const float p1 = (i & 3) == 3 ? exp2_fma(a1) : fast_exp2(a1);
+          const float p0 = fast_exp2(fmaf(masked(lo[2 * i], j * TK + cc * 32 + 2 * i), c, nm));
+          const float p1 = fast_exp2(fmaf(masked(lo[2 * i + 1], j * TK + cc * 32 + 2 * i + 1), c, nm));
           ps[(2 * i) & 7] += p0;
           ps[(2 * i + 1) & 7] += p1;
           pk[i] = pack_bf16(p0, p1);
@@ -568,9 +565,8 @@ __global__ void __launch_bounds__(fwd2::kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float a0 = fmaf(hi[cc * 32 + 2 * i], c, nm), a1 = fmaf(hi[cc * 32 + 2 * i + 1], c, nm);
-          const float p0 = (i & 3) == 3 ? exp2_fma(a0) : fast_exp2(a0);
-          const float p1 = (i & 3) == 3 ? exp2_fma(a1) : fast_exp2(a1);
+          const float p0 = fast_exp2(fmaf(hi[cc * 32 + 2 * i], c, nm));
+          const float p1 = fast_exp2(fmaf(hi[cc * 32 + 2 * i + 1], c, nm));
           ps[(2 * i) & 7] += p0;
           ps[(2 * i + 1) & 7] += p1;
           pk[i] = pack_bf16(p0, p1);

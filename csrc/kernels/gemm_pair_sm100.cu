@@ -58,24 +58,32 @@ constexpr int BK = 64;          // K per stage (128 bytes of bf16: one swizzle r
 constexpr int STAGES = 6;
 constexpr int GROUP_M = 8;      // tile rows per raster group
 constexpr int kThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kHalfA = BM * BK * 2;        // 16 KB
 constexpr uint32_t kHalfB = (BN / 2) * BK * 2;  // 16 KB
 constexpr uint32_t kStage = kHalfA + kHalfB;
 constexpr uint32_t kMnBox = 64 * BK * 2;        // 8 KB: 64 MN elements x 64 K rows
-// Epilogue staging: per epilogue warp two boxes of 32 rows x 32 columns (one
-// being written while the previous one's TMA store drains), up to 4 KB each (fp32).
-constexpr uint32_t kOutBox = 32 * 32 * 4;
-constexpr uint32_t kOutSmem = 4 * 2 * kOutBox;  // 32 KB
+// Epilogue staging: 8 KB per epilogue warp, a ring of boxes of 32 rows x 32
+// columns -- two fp32 boxes or four 16-bit boxes -- so a box is written while the
+// TMA stores of the previous ones drain.
+constexpr uint32_t kOutWarpBytes = 8192;
+constexpr uint32_t kOutSmem = 4 * kOutWarpBytes;  // 32 KB
 constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + kOutSmem + 256;
 
 // kSwiGLU: the up / gate projection of a SwiGLU FFN.  CTA rank 0 loads its B
 // half from W1 (map tmB) and rank 1 from W_gate (map tmB2), both at rows
 // [tn * 128, +128), so accumulator columns 0..127 hold u = x W1^T and 128..255
 // g = x W_gate^T of the same 128 hidden units.  The epilogue writes u and g into
-// gu (rows x 2F: [u | g], kept for the backward) through tmC and
-// h = silu(g) * u through tmH, each from the bf16-rounded u and g.
-enum Epi : int { kStore = 0, kAccumF32 = 1, kSwiGLU = 2 };
+// gu (rows x 2F: [u | g], kept for the backward) through tmC (u) and tmG (g),
+// and h = silu(g) * u through tmH, each from the bf16-rounded u and g.
+// kRoPE: the fused QKV projection of attention (head_dim 128, so a 256-column
+// tile is two heads).  Heads whose first column lies below args.rot_cols (the
+// query and key heads) are rotated at position (row % args.seq) + args.pos0 with
+// the rotate-half rule out[i] = x[i] cos[i] - x[i+64] sin[i],
+// out[i+64] = x[i+64] cos[i+64] + x[i] sin[i+64] on the bf16-rounded products,
+// the fp32 tables args.cos / args.sin, stored column-major (128 x positions).
+enum Epi : int { kStore = 0, kAccumF32 = 1, kSwiGLU = 2, kRoPE = 3 };
 
 struct PairArgs {
   void* C;
@@ -89,7 +97,27 @@ struct PairArgs {
   int group_m;  // tile rows per raster group
   int batch;    // independent GEMMs of equal shape (the third tensor-map coordinate)
   int64_t c_batch;  // C stride between batches (elements)
+  // kRoPE only: column-major (128 x tab_pitch) fp32 tables
+  const float* cos;
+  const float* sin;
+  int seq, pos0, rot_cols;
+  int64_t tab_pitch;
+  // Pipeline trace (null in normal runs): %globaltimer stamps of the first
+  // kTraceUnits work units of CTA pair 0, layout [event][unit].
+  unsigned long long* trace;
 };
+
+constexpr int kTraceUnits = 64;
+enum PairTraceEv : int {
+  kTrProdStart = 0, kTrMmaStart, kTrMmaEnd, kTrEpiStart, kTrEpiFreed, kTrEpiEnd,
+  kTrC0Loaded, kTrC0Math, kTrC0Stored,  // first chunk of a tile: accumulator read, math done, boxes issued
+  kTrEvents
+};
+std::atomic<unsigned long long*> g_gemm_pair_trace{nullptr};
+
+__device__ __forceinline__ void trace_unit(const PairArgs& a, int ev, int i) {
+  if (a.trace != nullptr && blockIdx.x == 0 && i < kTraceUnits) a.trace[ev * kTraceUnits + i] = global_ns();
+}
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
   const int per_group = group_m * tiles_n;
@@ -220,7 +248,7 @@ template <typename OutT, int EPI, bool BF16IN, bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmB2,
-                     const __grid_constant__ CUtensorMap tmH, PairArgs args) {
+                     const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmG, PairArgs args) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sA = base;
@@ -286,6 +314,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const CUtensorMap* mb = (EPI == kSwiGLU && rank == 1) ? &tmB2 : &tmB;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrTmaWait)) { ok = false; break; }
+          if (kb == kb0) trace_unit(args, kTrProdStart, (unit - pair) / npairs);
           const uint32_t fb = mapa_shared(smem_addr(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStage);
           load_stage<A_MN, B_MN>(sA + stage * kHalfA, sB + stage * kHalfB, &tmA, mb, fb, m0, n0, kb * BK, bi);
@@ -314,6 +343,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1, bi);
         if (!mbar_wait(&accempty[acc], acc_phase ^ 1, err, kErrAccWait)) break;
         tc_fence_after();
+        trace_unit(args, kTrMmaStart, (unit - pair) / npairs);
         const uint32_t d = tmem + (uint32_t)(acc * BN);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, err, kErrMmaWait)) { ok = false; break; }
@@ -329,6 +359,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         umma_commit_pair_mc(&accfull[acc], 0x3);
+        trace_unit(args, kTrMmaEnd, (unit - pair) / npairs);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
       umma_commit_pair(drain);
@@ -336,7 +367,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    unsigned char* boxes = sOut + (warp - 2) * 2 * kOutBox;
+    unsigned char* boxes = sOut + (warp - 2) * kOutWarpBytes;
+    constexpr uint32_t kBox = 32 * 32 * sizeof(OutT);           // bytes of one staged box
+    constexpr int kSlots = (int)(kOutWarpBytes / kBox);         // 2 (fp32) or 4 (16-bit)
     int acc = 0, nbox = 0;
     uint32_t acc_phase = 0;
     for (int unit = pair; unit < num_units; unit += npairs) {
@@ -344,11 +377,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1, bi);
       if (!mbar_wait(&accfull[acc], acc_phase, err, kErrEpiWait)) break;
       tc_fence_after();
+      const bool tracer = warp == 2 && lane == 0;  // one epilogue warp of the leader stamps
+      const int ui = (unit - pair) / npairs;
+      if (tracer) trace_unit(args, kTrEpiStart, ui);
       const int row0 = tm * 2 * BM + (int)rank * BM + q * 32;
       // one 32 x 32 box through the staging ring: stage this thread's row, TMA-store it
       auto put_box = [&](const CUtensorMap* map, const uint32_t* r, int x) {
-        unsigned char* box = boxes + (nbox & 1) * kOutBox;
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        unsigned char* box = boxes + (nbox % kSlots) * kBox;
+        // the store issued from this slot kSlots boxes ago has finished reading it
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kSlots - 1) : "memory");
         __syncwarp();
         stage_row<__nv_bfloat16>(box, lane, 1.f, r);
         fence_proxy_async_smem();
@@ -359,6 +396,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         ++nbox;
       };
+      if constexpr (EPI == kRoPE) {
+        const int row = row0 + lane;
+        const int pos = (row < args.M ? row % args.seq : 0) + args.pos0;
+        // column-major (128 x positions) tables: the warp's 32 consecutive
+        // positions of one column are one coalesced line
+        const float* ct = args.cos + pos;
+        const float* st = args.sin + pos;
+        const int64_t P = args.tab_pitch;
+#pragma unroll 1
+        for (int pc = 0; pc < 4; ++pc) {  // chunk pairs (0,2) (1,3) (4,6) (5,7): columns i and i + 64 of a head
+          const int ca = (pc >> 1) * 4 + (pc & 1), cb = ca + 2;
+          uint32_t xa[32], xb[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ca * 32), xa);
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + cb * 32), xb);
+          tmem_ld_wait();
+          if (tracer && pc == 0) trace_unit(args, kTrC0Loaded, ui);
+          if (pc == 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&accempty[acc]), 0));
+            if (tracer) trace_unit(args, kTrEpiFreed, ui);
+          }
+          const int col_a = tn * BN + ca * 32, col_b = tn * BN + cb * 32;
+          if (row0 >= args.M || col_a >= args.N) continue;
+          const int head_col0 = tn * BN + (pc >> 1) * 128;
+          if (head_col0 < args.rot_cols) {
+            const int i0 = (pc & 1) * 32;  // index within the first half of the head
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float c1 = __ldg(ct + (i0 + j) * P), s1 = __ldg(st + (i0 + j) * P);
+              const float c2 = __ldg(ct + (64 + i0 + j) * P), s2 = __ldg(st + (64 + i0 + j) * P);
+              const float x = __bfloat162float(__float2bfloat16_rn(__uint_as_float(xa[j])));
+              const float y = __bfloat162float(__float2bfloat16_rn(__uint_as_float(xb[j])));
+              xa[j] = __float_as_uint(x * c1 - y * s1);
+              xb[j] = __float_as_uint(y * c2 + x * s2);
+            }
+          }
+          if (tracer && pc == 0) trace_unit(args, kTrC0Math, ui);
+          put_box(&tmC, xa, col_a);
+          if (col_b < args.N) put_box(&tmC, xb, col_b);
+          if (tracer && pc == 0) trace_unit(args, kTrC0Stored, ui);
+        }
+        if (tracer) trace_unit(args, kTrEpiEnd, ui);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        continue;
+      }
       if constexpr (EPI == kSwiGLU) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -366,10 +449,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), u);
           tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + 128 + c * 32), g);
           tmem_ld_wait();
+          if (tracer && c == 0) trace_unit(args, kTrC0Loaded, ui);
           if (c == 3) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&accempty[acc]), 0));
+            if (tracer) trace_unit(args, kTrEpiFreed, ui);
           }
           const int col0 = tn * (BN / 2) + c * 32;
           if (row0 >= args.M || col0 >= args.N) continue;
@@ -378,12 +463,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j) {
             const float uf = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[j])));
             const float gf = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[j])));
-            h[j] = __float_as_uint(gf * (1.f / (1.f + __expf(-gf))) * uf);
+            h[j] = __float_as_uint(gf * fast_rcp(1.f + fast_exp2(-kLog2e * gf)) * uf);
           }
+          if (tracer && c == 0) trace_unit(args, kTrC0Math, ui);
+          // u and g through maps F columns wide each, so a ragged last tile is
+          // clipped at F and never spills into the other half of gu
           put_box(&tmC, u, col0);
-          put_box(&tmC, g, args.N + col0);
+          put_box(&tmG, g, col0);
           put_box(&tmH, h, col0);
+          if (tracer && c == 0) trace_unit(args, kTrC0Stored, ui);
         }
+        if (tracer) trace_unit(args, kTrEpiEnd, ui);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
         continue;
       }
@@ -392,17 +482,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
         tmem_ld_wait();
+        if (tracer && c == 0) trace_unit(args, kTrC0Loaded, ui);
         if (c == BN / 32 - 1) {  // the accumulator is read out: the MMAs may reuse it
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&accempty[acc]), 0));
+          if (tracer) trace_unit(args, kTrEpiFreed, ui);
         }
         const int col0 = tn * BN + c * 32;
         if (args.tma_out) {
           if (row0 >= args.M || col0 >= args.N) continue;
-          unsigned char* box = boxes + (nbox & 1) * kOutBox;
-          // the store issued from this buffer two boxes ago has finished reading it
-          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          unsigned char* box = boxes + (nbox % kSlots) * kBox;
+          // the store issued from this slot kSlots boxes ago has finished reading it
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kSlots - 1) : "memory");
           __syncwarp();
           stage_row<OutT>(box, lane, args.alpha, r);
           fence_proxy_async_smem();
@@ -416,7 +508,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         } else {
           store_chunk<OutT, EPI>(args, bi, row0 + lane, col0, r);
         }
+        if (tracer && c == 0) trace_unit(args, kTrC0Stored, ui);
       }
+      if (tracer) trace_unit(args, kTrEpiEnd, ui);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // stores complete before exit
@@ -518,10 +612,12 @@ int max_pairs(int dev) {
 
 template <typename OutT, int EPI, bool BF16IN, bool A_MN, bool B_MN>
 void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const PairArgs& args, int pairs,
-              const CUtensorMap* tb2 = nullptr, const CUtensorMap* th = nullptr) {
+              const CUtensorMap* tb2 = nullptr, const CUtensorMap* th = nullptr, const CUtensorMap* tg = nullptr) {
   auto k = gemm_pair_kernel<OutT, EPI, BF16IN, A_MN, B_MN>;
   LRB_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
-  k<<<2 * pairs, kThreads, kSmem, stream()>>>(ta, tb, tc, tb2 ? *tb2 : tb, th ? *th : tc, args);
+  PairArgs a = args;
+  a.trace = g_gemm_pair_trace.load(std::memory_order_acquire);
+  k<<<2 * pairs, kThreads, kSmem, stream()>>>(ta, tb, tc, tb2 ? *tb2 : tb, th ? *th : tc, tg ? *tg : tc, a);
   LRB_LAUNCH_CHECK();
 }
 
@@ -630,7 +726,7 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, a
   std::memset(&tc, 0, sizeof(tc));
   if (aligned) tc = make_out_map(C.data_ptr(), c.batch, M, N, c.ld, c.bstride, ct);
   PairArgs args{C.data_ptr(), c.ld, (int)M, (int)N, (int)K, (float)alpha, aligned ? 1 : 0, aligned ? 1 : 0,
-                splits, group_m, (int)a.batch, c.bstride};
+                splits, group_m, (int)a.batch, c.bstride, nullptr, nullptr, 1, 0, 0};
   if (accumulate) {
     if (bf) launch_layout<float, kAccumF32, true>(a_mn, b_mn, ta, tb, tc, args, pairs);
     else launch_layout<float, kAccumF32, false>(a_mn, b_mn, ta, tb, tc, args, pairs);
@@ -667,12 +763,58 @@ void gemm_pair_swiglu(const at::Tensor& X, const at::Tensor& W1, const at::Tenso
   CUtensorMap ta = make_map(X.data_ptr(), 1, M, K, x.ld, 0, BK, BM, true);
   CUtensorMap tb = make_map(W1.data_ptr(), 1, F, K, w1.ld, 0, BK, BN / 2, true);
   CUtensorMap tb2 = make_map(Wg.data_ptr(), 1, F, K, wg.ld, 0, BK, BN / 2, true);
-  CUtensorMap tc = make_out_map(GU.data_ptr(), 1, M, 2 * F, gu.ld, 0, at::kBFloat16);
+  LRB_CHECK(F % 8 == 0, "gemm_pair_swiglu: F must be a multiple of 8 (the gate half of gu starts 16-byte aligned)");
+  CUtensorMap tc = make_out_map(GU.data_ptr(), 1, M, F, gu.ld, 0, at::kBFloat16);
+  CUtensorMap tg = make_out_map(static_cast<__nv_bfloat16*>(GU.data_ptr()) + F, 1, M, F, gu.ld, 0, at::kBFloat16);
   CUtensorMap th = make_out_map(Hout.data_ptr(), 1, M, F, hm.ld, 0, at::kBFloat16);
   const int tiles = (int)(((M + 2 * BM - 1) / (2 * BM)) * ((F + BN / 2 - 1) / (BN / 2)));
   const int pairs = std::max(1, std::min(tiles, max_pairs(X.get_device())));
-  PairArgs args{GU.data_ptr(), gu.ld, (int)M, (int)F, (int)K, 1.f, 1, 1, 1, GROUP_M, 1, 0};
-  launch_t<__nv_bfloat16, kSwiGLU, true, false, false>(ta, tb, tc, args, pairs, &tb2, &th);
+  PairArgs args{GU.data_ptr(), gu.ld, (int)M, (int)F, (int)K, 1.f, 1, 1, 1, GROUP_M, 1, 0, nullptr, nullptr, 1, 0, 0};
+  launch_t<__nv_bfloat16, kSwiGLU, true, false, false>(ta, tb, tc, args, pairs, &tb2, &th, &tg);
+}
+
+// Fused QKV projection with RoPE: out = x W^T (rows x N, N = (H + 2 Hkv) * 128),
+// the first rot_cols columns (query and key heads) rotated at position
+// (row % seq) + pos0 with the fp32 tables cos / sin, given transposed:
+// (128, positions) contiguous.
+void gemm_pair_rope(const at::Tensor& X, const at::Tensor& W, at::Tensor& Out, const at::Tensor& cos_t,
+                    const at::Tensor& sin_t, int64_t seq, int64_t pos0, int64_t rot_cols) {
+  const Mat x = check_operand(X, "x", true), w = check_operand(W, "w", true), o = check_operand(Out, "out", false);
+  LRB_CHECK(X.dim() == 2 && W.dim() == 2 && Out.dim() == 2 && X.scalar_type() == at::kBFloat16 &&
+                W.scalar_type() == at::kBFloat16 && Out.scalar_type() == at::kBFloat16,
+            "gemm_pair_rope: 2-D bf16 operands");
+  const int64_t M = x.rows, K = x.cols, N = w.rows;
+  LRB_CHECK(w.cols == K && o.rows == M && o.cols == N && N % 256 == 0 && rot_cols % 128 == 0 && rot_cols <= N,
+            "gemm_pair_rope: shapes (N a multiple of 256, 128-wide heads)");
+  LRB_CHECK(tma_ok(X, x) && tma_ok(W, w) && tma_ok(Out, o), "gemm_pair_rope: 16-byte aligned bases and pitches");
+  LRB_CHECK(cos_t.is_cuda() && sin_t.is_cuda() && cos_t.scalar_type() == at::kFloat && sin_t.scalar_type() == at::kFloat &&
+                cos_t.is_contiguous() && sin_t.is_contiguous() && cos_t.dim() == 2 && cos_t.size(0) == 128 &&
+                sin_t.sizes() == cos_t.sizes() && seq > 0 && pos0 >= 0 && seq + pos0 <= cos_t.size(1),
+            "gemm_pair_rope: fp32 column-major (128, positions) cos / sin tables covering the positions");
+  c10::cuda::CUDAGuard g(X.device());
+  if (M == 0) return;
+  CUtensorMap ta = make_map(X.data_ptr(), 1, M, K, x.ld, 0, BK, BM, true);
+  CUtensorMap tb = make_map(W.data_ptr(), 1, N, K, w.ld, 0, BK, BN / 2, true);
+  CUtensorMap tc = make_out_map(Out.data_ptr(), 1, M, N, o.ld, 0, at::kBFloat16);
+  const int tiles = (int)(((M + 2 * BM - 1) / (2 * BM)) * (N / BN));
+  const int pairs = std::max(1, std::min(tiles, max_pairs(X.get_device())));
+  PairArgs args{Out.data_ptr(), o.ld, (int)M, (int)N, (int)K, 1.f, 1, 1, 1, GROUP_M, 1, 0,
+                cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), (int)seq, (int)pos0, (int)rot_cols, cos_t.size(1)};
+  launch_t<__nv_bfloat16, kRoPE, true, false, false>(ta, tb, tc, args, pairs);
+}
+
+// Points the pair GEMM's pipeline trace at `buf` (int64 CUDA, at least
+// kTrEvents * kTraceUnits entries: producer start, MMA start / end, epilogue start /
+// accumulator freed / end of the first units of pair 0), or switches it off (None).
+void gemm_pair_set_trace(const c10::optional<at::Tensor>& buf) {
+  if (buf.has_value()) {
+    LRB_CHECK(buf->is_cuda() && buf->scalar_type() == at::kLong && buf->is_contiguous() &&
+                  buf->numel() >= (int64_t)kTrEvents * kTraceUnits,
+              "gemm_pair_set_trace: an int64 CUDA buffer of ", (int64_t)kTrEvents * kTraceUnits, " entries");
+    g_gemm_pair_trace.store(reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>()), std::memory_order_release);
+  } else {
+    g_gemm_pair_trace.store(nullptr, std::memory_order_release);
+  }
 }
 
 // Returns and clears the error word of the pair GEMM on `device` (0 = no timeout).

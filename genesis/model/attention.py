@@ -28,7 +28,7 @@ import torch.nn.functional as F
 
 from genesis.model.rotary import apply_rotary_emb
 from llm_research_b200 import ops
-from llm_research_b200.ops.linear import cat_rows, project
+from llm_research_b200.ops.linear import cat_rows, project, qkv_rope
 
 # The reference probes flash-attn here; the fused kernel replaces it.
 FLASH_ATTN_AVAILABLE = True
@@ -118,10 +118,17 @@ class MultiHeadAttention(nn.Module):
             return self._forward_static(x, cos, sin, kv_cache)
         B, S, _ = x.shape
         H, Hkv, D = self.num_heads, self.num_kv_heads, self.head_dim
+        drop = self.dropout_p if self.training else 0.0
+        if kv_cache is None and attention_mask is None and drop == 0.0 and self.q_proj.bias is None:
+            # one launch: QKV projection with RoPE in the GEMM epilogue (q, k, v are views)
+            fused = qkv_rope(x, cat_rows(self.q_proj.weight, self.k_proj.weight, self.v_proj.weight), cos, sin,
+                             H, Hkv, D, position_offset)
+            if fused is not None:
+                out = ops.attention(*fused, causal=True)
+                return project(out.reshape(B, S, H * D), self.o_proj.weight, self.o_proj.bias)
         qkv = self._qkv(x)
         # (B,S,H,D) q and (B,S,Hkv,D) k, v with RoPE applied to q and k.
         q, k, v = ops.rope_qkv(qkv, cos, sin, H, Hkv, D, position_offset)
-        drop = self.dropout_p if self.training else 0.0
         if kv_cache is None and attention_mask is None and drop == 0.0:
             out = ops.attention(q, k, v, causal=True)
             return project(out.reshape(B, S, H * D), self.o_proj.weight, self.o_proj.bias)

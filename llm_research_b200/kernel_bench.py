@@ -210,6 +210,8 @@ def _cases() -> Dict[str, Callable[[], Tuple[Callable[[], None], float, float]]]
         "ce": ce,
         "gemm_pair": gemm_pair,
     }
+    cases["lin_upgate_swiglu"] = _swiglu_up_case
+    cases["lin_qkv_rope"] = _qkv_rope_case
     for name, (N, K) in LINEAR_SHAPES.items():
         for kind in ("fwd", "dgrad", "wgrad"):
             for lib in (False, True):
@@ -244,6 +246,40 @@ def _linear_gemm_case(N: int, K: int, kind: str, lib: bool):
         out = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
         fn = (lambda: torch.matmul(dy.t(), x, out=out)) if lib else (lambda: linear_wgrad(dy, x, out=out))
     return fn, flops, 0.0
+
+
+def _swiglu_up_case():
+    """The fused SwiGLU up / gate projection (u, g and h = silu(g) * u from one
+    CTA-pair launch) at the training shape; FLOPs of the two projections."""
+    from llm_research_b200._ext import native
+
+    T, (N2, K) = LINEAR_TOKENS, LINEAR_SHAPES["upgate"]
+    F = N2 // 2
+    x = torch.randn(T, K, device="cuda", dtype=torch.bfloat16)
+    w1 = torch.randn(F, K, device="cuda", dtype=torch.bfloat16) * 0.02
+    wg = torch.randn(F, K, device="cuda", dtype=torch.bfloat16) * 0.02
+    gu = torch.empty(T, 2 * F, device="cuda", dtype=torch.bfloat16)
+    h = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+    C = native()
+    return (lambda: C.gemm_pair_swiglu(x, w1, wg, gu, h)), 2.0 * T * N2 * K, 0.0
+
+
+def _qkv_rope_case():
+    """The fused QKV projection with RoPE on the query and key heads (16 + 2 x 16
+    heads of 128) at the training shape, sequences of 4096."""
+    from llm_research_b200._ext import native
+
+    T, (N, K) = LINEAR_TOKENS, LINEAR_SHAPES["qkv"]
+    S, D = 4096, 128
+    x = torch.randn(T, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+    out = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))
+    ang = torch.outer(torch.arange(S, device="cuda", dtype=torch.float32), inv)
+    emb = torch.cat([ang, ang], dim=-1)
+    cos, sin = emb.cos().t().contiguous(), emb.sin().t().contiguous()  # column-major (128, S)
+    C = native()
+    return (lambda: C.gemm_pair_rope(x, w, out, cos, sin, S, 0, 2 * N // 3)), 2.0 * T * N * K, 0.0
 
 
 def main(argv=None) -> None:

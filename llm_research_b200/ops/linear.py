@@ -361,3 +361,79 @@ def swiglu_up(x: torch.Tensor, w1: torch.Tensor, wg: torch.Tensor) -> torch.Tens
             acc = a1.as_strided((2 * a1.shape[0], a1.shape[1]), (a1.shape[1], 1))
     h = _SwiGLUUpFn.apply(x2d, w1, wg, acc)
     return h.view(*x.shape[:-1], w1.shape[0])
+
+
+# ------------------------------------------------------------ fused QKV + RoPE
+_TABLES_T: dict = {}
+
+
+def _columns_major(cos: torch.Tensor, sin: torch.Tensor):
+    """``(128, positions)`` contiguous copies of the RoPE tables, as the fused
+    QKV epilogue reads them (a warp's 32 consecutive positions of one column are
+    one coalesced line).  Cached per table storage, shape and version (the
+    tables of a model are built once and reused every step); an entry holds its
+    source tensors, so their storage cannot be freed and reused under the key."""
+    key = (cos.data_ptr(), cos._version, sin.data_ptr(), sin._version, tuple(cos.shape), cos.device)
+    hit = _TABLES_T.get(key)
+    if hit is None:
+        if len(_TABLES_T) >= 8:
+            _TABLES_T.clear()
+        hit = (cos, sin, cos.t().contiguous(), sin.t().contiguous())
+        _TABLES_T[key] = hit
+    return hit[2], hit[3]
+
+
+class _QKVRopeFn(torch.autograd.Function):
+    """``qkv = x W^T`` with RoPE applied to the query and key heads in the GEMM
+    epilogue (one launch, no separate rotation pass); q, k, v are returned as
+    strided views of ``qkv``.  Backward: the inverse rotation packs ``dq, dk, dv``
+    back into ``dqkv`` (one pass), then the linear's dgrad / wgrad."""
+
+    @staticmethod
+    def forward(ctx, x2d, w, acc, cos, sin, H, Hkv, D, B, S, offset):
+        from llm_research_b200._ext import native
+
+        out = torch.empty(x2d.shape[0], w.shape[0], dtype=x2d.dtype, device=x2d.device)
+        cos_t, sin_t = _columns_major(cos, sin)
+        native().gemm_pair_rope(x2d, w, out, cos_t, sin_t, S, offset, (H + Hkv) * D)
+        ctx.save_for_backward(x2d, w, cos, sin)
+        ctx.acc, ctx.meta = acc, (H, Hkv, D, B, S, offset)
+        v4 = out.view(B, S, H + 2 * Hkv, D)
+        return v4[:, :, :H], v4[:, :, H:H + Hkv], v4[:, :, H + Hkv:]
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        from llm_research_b200._ext import native
+        from llm_research_b200.ops.gemm import linear_dgrad, linear_wgrad
+
+        x2d, w, cos, sin = ctx.saved_tensors
+        H, Hkv, D, B, S, offset = ctx.meta
+        dqkv = native().rope_qkv_bwd(dq.contiguous(), dk.contiguous(), dv.contiguous(), cos, sin, H, Hkv, D, offset)
+        dqkv = dqkv.view(B * S, -1)
+        dx = linear_dgrad(dqkv, w) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            if ctx.acc is not None:
+                linear_wgrad(dqkv, x2d, out=ctx.acc, accumulate=True)
+                dw = accumulated_marker(w)
+            else:
+                dw = linear_wgrad(dqkv, x2d)
+        ctx.acc = None
+        return dx, dw, None, None, None, None, None, None, None, None, None
+
+
+def qkv_rope(x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, H: int, Hkv: int, D: int,
+             offset: int = 0):
+    """``(q, k, v)`` of ``(B, S, heads, D)`` for ``x (B, S, d)`` and the fused weight
+    ``w ((H + 2 Hkv) D, d)``, RoPE on q and k, or None when the fused path does not
+    apply (head_dim 128, bf16 CUDA, the pair kernel's shapes, tables covering
+    the positions)."""
+    B, S, _ = x.shape
+    N = (H + 2 * Hkv) * D
+    if not (_PRECISION == "bf16" and x.is_cuda and x.dtype == torch.bfloat16 and D == 128 and N % 256 == 0
+            and w.shape[0] == N and _pair_ok(x, w) and B * S > 0 and cos.shape[0] >= offset + S):
+        return None
+    x2d = _rows(x.reshape(-1, x.shape[-1]))
+    acc = _acc_of(w) if torch.is_grad_enabled() and w.requires_grad else None
+    return _QKVRopeFn.apply(x2d, w, acc, cos.float().contiguous(), sin.float().contiguous(), H, Hkv, D, B, S,
+                            int(offset))

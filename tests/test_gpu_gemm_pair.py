@@ -270,3 +270,35 @@ def test_swiglu_up_projection_matches_two_kernel_path():
     for name, got, ref in (("h", h, hf), ("dx", x.grad, xf.grad), ("dw1", w1.grad, w1f.grad), ("dwg", wg.grad, wgf.grad)):
         err = ((got.float() - ref).norm() / ref.norm()).item()
         assert err < 2e-2, (name, err)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,Hkv,offset", [(4, 4, 0), (8, 2, 5)])
+def test_qkv_rope_epilogue_matches_separate_rotation(H, Hkv, offset):
+    """QKV projection with RoPE in the epilogue against the GEMM followed by the
+    rotation kernel, forward and backward (GQA, a position offset, ragged rows)."""
+    from genesis.model.rotary import RotaryEmbedding
+    from llm_research_b200 import ops
+    from llm_research_b200.ops.gemm import gemm_pair_error
+    from llm_research_b200.ops.linear import linear_bf16, qkv_rope
+
+    g = torch.Generator(device="cuda").manual_seed(29)
+    B, S, d, D = 2, 300, 256, 128
+    N = (H + 2 * Hkv) * D
+    rot = RotaryEmbedding(dim=D, max_seq_len=1024).cuda()
+    cos, sin = rot(offset + S)
+    x = torch.randn(B, S, d, device="cuda", generator=g).bfloat16().requires_grad_()
+    w = (torch.randn(N, d, device="cuda", generator=g) * 0.05).bfloat16().requires_grad_()
+    q, k, v = qkv_rope(x, w, cos, sin, H, Hkv, D, offset)
+    x2, w2 = x.detach().clone().requires_grad_(), w.detach().clone().requires_grad_()
+    q2, k2, v2 = ops.rope_qkv(linear_bf16(x2, w2), cos, sin, H, Hkv, D, offset)
+    for a, b in ((q, q2), (k, k2), (v, v2)):
+        torch.testing.assert_close(a.float(), b.float(), atol=2e-2, rtol=2e-2)
+    gq, gk, gv = (torch.randn(t.shape, device="cuda", generator=g).bfloat16() for t in (q, k, v))
+    torch.autograd.backward((q, k, v), (gq, gk, gv))
+    torch.autograd.backward((q2, k2, v2), (gq, gk, gv))
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    for name, a, b in (("dx", x.grad, x2.grad), ("dw", w.grad, w2.grad)):
+        err = ((a.float() - b.float()).norm() / b.float().norm()).item()
+        assert err < 1e-2, (name, err)
