@@ -401,6 +401,7 @@ constexpr uint32_t kPD = 2 * kPT;                   // [P^T | dS^T] of one buffe
                                                     // 4 boxes of 32 head dims x 64 queries (fp32)
 constexpr size_t kSmem = 1024 + 2 * kKV + 2 * kRing * (size_t)kQ + 2 * (size_t)kPD + 2048;
 static_assert(kSmem <= 232448, "attention backward: shared memory over the 227 KB limit");
+constexpr int kHeadGroup = 8;  // (batch, kv-head) pairs per launch group
 }  // namespace bwd3
 
 __global__ void __launch_bounds__(bwd3::kThreads, 1)
@@ -427,12 +428,28 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
   uint64_t* acc_done = bars + 17;
   uint64_t* drain = bars + 18;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* pd_read = bars + 22;    // [2] dV / dK MMAs of the buffer done: P^T / dS^T consumed
   float* sL = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(bars) + 512);  // [kRing][64]
   float* sD = sL + kRing * TQ3;                                                       // [kRing][64]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * TK;
-  const int b = blockIdx.y / a.Hkv, hk = blockIdx.y % a.Hkv, G = a.H / a.Hkv;
+  // 1-D grid over (head group, key tile, head in group): groups of kHeadGroup
+  // (batch, kv-head) pairs run one after another, so the CTAs in flight add
+  // their dQ into a few heads' rows (an L2-resident working set), and within a
+  // group the key tiles launch in ascending order -- under a causal mask the
+  // longest first, the short ones filling the tail
+  int n0, b, hk;
+  {
+    const int bh = a.B * a.Hkv, nkt = (a.Skv + TK - 1) / TK;
+    const int grp = (int)blockIdx.x / (kHeadGroup * nkt);
+    const int r = (int)blockIdx.x - grp * kHeadGroup * nkt;
+    const int gs = min(kHeadGroup, bh - grp * kHeadGroup);
+    n0 = (r / gs) * TK;
+    const int head = grp * kHeadGroup + r % gs;
+    b = head / a.Hkv;
+    hk = head % a.Hkv;
+  }
+  const int G = a.H / a.Hkv;
   const int off = a.Skv - a.Sq;
   const int q_first = a.causal ? max(0, n0 - off) : 0;
   const int qt0 = q_first / TQ3;
@@ -451,6 +468,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       mbar_init(&dq_full[i], 1);
       mbar_init(&dq_free[i], 128);
       mbar_init(&stage_free[i], 1);
+      mbar_init(&pd_read[i], 1);
     }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
@@ -544,10 +562,17 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
         umma_commit(&sdp_full[bb]);
         trace_at(a, kTrSdpIssue, t);
       };
+      // dQ^T first: its read-out (and with it the next S^T / dP^T of this
+      // buffer) overlaps the dV / dK MMAs that follow
       auto issue_acc = [&](int t) {
         const int bb = t & 1, sl = t % kRing;
         const uint32_t q_ = smem_addr(sQ + sl * kQ), o_ = smem_addr(sdO + sl * kQ);
         const uint32_t pt_ = smem_addr(sPD + bb * kPD), ds_ = pt_ + kPT;
+#pragma unroll
+        for (int k = 0; k < TK / 16; ++k)  // dQ^T = K^T dS^T  (into the consumed S^T_b columns)
+          umma_f16(tmem + bb * 128, umma_desc_mn_sw128(k_ + k * 2048, kKVHalf, 1024),
+                   umma_desc_mn_sw128(ds_ + k * 2048, kPT, 1024), id_dq, k != 0);
+        umma_commit(&dq_full[bb]);
 #pragma unroll
         for (int k = 0; k < TQ3 / 16; ++k) {  // dV += P^T dO ; dK += dS^T Q
           umma_f16(tdV, umma_desc_k_sw128(pt_ + k * 32), umma_desc_mn_sw128(o_ + k * 2048, kQHalf, 1024), id_acc,
@@ -556,11 +581,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
                    (t | k) != 0);
         }
         umma_commit(&qd_free[sl]);
-#pragma unroll
-        for (int k = 0; k < TK / 16; ++k)  // dQ^T = K^T dS^T  (into the consumed S^T_b columns)
-          umma_f16(tmem + bb * 128, umma_desc_mn_sw128(k_ + k * 2048, kKVHalf, 1024),
-                   umma_desc_mn_sw128(ds_ + k * 2048, kPT, 1024), id_dq, k != 0);
-        umma_commit(&dq_full[bb]);
+        umma_commit(&pd_read[bb]);
         trace_at(a, kTrAccIssue, t);
       };
       int ns = 0, na = 0;
@@ -699,8 +720,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       const uint32_t use = (t >> 1) & 1;
       const int h = hk * G + t / nqt;
       const int q0 = (qt0 + t % nqt) * TQ3;
-      // dq_full: dQ^T(t) is in TMEM, and every MMA of sub-tile t -- the last readers
-      // of this buffer's P^T / dS^T tiles, the staging area -- has completed
+      // dq_full: dQ^T(t) is in TMEM
       if (!group_all(1, mbar_wait(&dq_full[bb], use, a.err, kErrEpiWait))) break;
       if (issuer) trace_at(a, kTrDqStart, t);
       tc_fence_after();
@@ -712,6 +732,9 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&dq_free[bb]);  // dQ^T is in registers: the MMAs may reuse the columns
+      // pd_read: the dV / dK MMAs of sub-tile t, the last readers of this buffer's
+      // P^T / dS^T tiles (the staging area), have completed
+      if (!group_all(1, mbar_wait(&pd_read[bb], use, a.err, kErrEpiWait))) break;
 #pragma unroll
       for (int e = 0; e < 64; ++e)
         *reinterpret_cast<float*>(box + e * 128 + ((chunk ^ (e & 7)) * 16) + sub) = __uint_as_float(r[e]) * a.scale;
@@ -822,7 +845,9 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
     CUtensorMap tdq64 = dq_map(dq_acc.data_ptr<float>(), B * Sq, H * HD, bwd3::TQ3);
     LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_v3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)bwd3::kSmem));
-    attn_bwd_v3_kernel<<<grid, bwd3::kThreads, bwd3::kSmem, stream()>>>(tq64, tk, tv, tdo64, tdq64, args);
+    LRB_CHECK(B * Hkv * ((Skv + TK - 1) / TK) < (1LL << 31), "attn_bwd: too many CTAs");
+    const dim3 grid3((unsigned)(B * Hkv * ((Skv + TK - 1) / TK)));
+    attn_bwd_v3_kernel<<<grid3, bwd3::kThreads, bwd3::kSmem, stream()>>>(tq64, tk, tv, tdo64, tdq64, args);
   }
   LRB_LAUNCH_CHECK();
 }

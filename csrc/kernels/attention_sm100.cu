@@ -341,6 +341,7 @@ namespace fwd2 {
 constexpr int kThreads = 320;
 constexpr int kRowThreads = 128;
 constexpr size_t kSmem = 1024 + 6 * (size_t)kTileBytes + 256;
+constexpr int kHeadGroup = 16;  // (batch, head) pairs per launch group
 }  // namespace fwd2
 
 __global__ void __launch_bounds__(fwd2::kThreads, 1)
@@ -364,8 +365,22 @@ __global__ void __launch_bounds__(fwd2::kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = (gridDim.x - 1 - blockIdx.x) * 2 * TQ;  // heavy (late) causal tiles first
-  const int b = blockIdx.y / a.H, h = blockIdx.y % a.H, hk = h / (a.H / a.Hkv);
+  // 1-D grid over (head group, tile pair, head in group): groups of
+  // fwd2::kHeadGroup (batch, head) pairs run one after another (the K / V rows
+  // in flight stay L2-resident), and within a group the tile pairs launch in
+  // descending order -- under a causal mask the longest first
+  int m0, b, h;
+  {
+    const int bh = a.B * a.H, npairs = (a.Sq + 2 * TQ - 1) / (2 * TQ);
+    const int grp = (int)blockIdx.x / (fwd2::kHeadGroup * npairs);
+    const int r = (int)blockIdx.x - grp * fwd2::kHeadGroup * npairs;
+    const int gs = min(fwd2::kHeadGroup, bh - grp * fwd2::kHeadGroup);
+    m0 = (npairs - 1 - r / gs) * 2 * TQ;
+    const int head = grp * fwd2::kHeadGroup + r % gs;
+    b = head / a.H;
+    h = head % a.H;
+  }
+  const int hk = h / (a.H / a.Hkv);
   const int off = a.Skv - a.Sq;
   int nt[2];
 #pragma unroll
@@ -698,7 +713,8 @@ std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor& q, const at:
   } else {
     LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_2q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)fwd2::kSmem));
-    dim3 grid((unsigned)((Sq + 2 * TQ - 1) / (2 * TQ)), (unsigned)(B * H));
+    LRB_CHECK(B * H * ((Sq + 2 * TQ - 1) / (2 * TQ)) < (1LL << 31), "attention: too many CTAs");
+    dim3 grid((unsigned)(B * H * ((Sq + 2 * TQ - 1) / (2 * TQ))));
     attn_fwd_2q_kernel<<<grid, fwd2::kThreads, fwd2::kSmem, stream()>>>(tq, tk, tv, args);
   }
   LRB_LAUNCH_CHECK();

@@ -180,7 +180,13 @@ class FlatShardEngine(nn.Module):
         self._register_hooks()
         import os
 
-        self.comm = (comm or os.environ.get("LRB_FSDP_COMM", "nccl")).lower()
+        # Default: the own P2P gather / reduce-scatter on a single node of up to 4
+        # ranks (at 2 ranks its reduce-scatter measured 1.34x NCCL and the training
+        # step 1.3 % faster), NCCL above that (at 8 ranks NCCL's in-switch
+        # reduction measured ahead, 0.95x for the P2P reduce-scatter).
+        self.comm = (comm or os.environ.get("LRB_FSDP_COMM", "auto")).lower()
+        if self.comm == "auto":
+            self.comm = "p2p" if self.world <= 4 else "nccl"
         self.heap = None
         self._sumsq: Optional[torch.Tensor] = None
         if self.comm == "p2p":
