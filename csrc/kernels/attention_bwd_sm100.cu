@@ -64,7 +64,7 @@ enum TraceEv : int {
   kTrSmDone,         // softmax: P^T / dS^T written, p_full arrived
   kTrDqStart,        // dQ warp: dQ^T ready
   kTrDqFree,         // dQ warp: TMEM read, dq_free arrived
-  kTrDqStaged,       // dQ issuer: reduce-adds read the staging (stage_free)
+  kTrDqStaged,       // dQ warp: adds into dq_acc issued
   kTrEvents
 };
 
@@ -384,12 +384,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 // double-buffered (b = t & 1); Q, dO and their LSE / D rows sit in a ring of
 // three slots (t % 3), so the producer fills sub-tile t+2 while t and t+1 are in
 // use and no refill (TMA or the LSE / D loads) lies between the MMAs of one
-// sub-tile and the next.  The dQ epilogue stages its fp32 boxes in the P^T /
-// dS^T tiles of its buffer, which the MMAs have finished reading by then; the
-// softmax warps wait for that staging's TMA read (stage_free) before they
-// write the buffer again.  Warps: 0 TMA, 1 MMA issue, 2..9 softmax-gradient (two
-// threads per key row, 32 queries each), 10..13 dQ epilogue (one thread per
-// head-dim lane; TMA reduce-adds).
+// sub-tile and the next.  Per sub-tile the MMAs run dQ^T first, then dV / dK;
+// the dQ epilogue reads dQ^T out of TMEM (freeing the columns for the next
+// S^T of the buffer) and adds it into the fp32 dQ buffer straight from
+// registers (red.global.add, one coalesced 128-byte line per warp and query):
+// no shared-memory staging, so the epilogue holds no slot and no tile that
+// the next sub-tiles need.  The softmax warps of sub-tile t+2 wait for
+// pd_read(t) (the dV / dK MMAs, the last readers of the P^T / dS^T tiles)
+// before they rewrite them.  Warps: 0 TMA, 1 MMA issue, 2..9 softmax-gradient
+// (two threads per key row, 32 queries each), 10..13 dQ epilogue (one thread
+// per head-dim lane).
 namespace bwd3 {
 constexpr int TQ3 = 64;
 constexpr int kThreads = 448;
@@ -406,8 +410,7 @@ constexpr int kHeadGroup = 8;  // (batch, kv-head) pairs per launch group
 
 __global__ void __launch_bounds__(bwd3::kThreads, 1)
     attn_bwd_v3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                       const __grid_constant__ CUtensorMap tmdQ, BwdArgs a) {
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, BwdArgs a) {
   using namespace bwd3;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -424,7 +427,6 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
   uint64_t* p_full = bars + 9;      // [2]
   uint64_t* dq_full = bars + 11;    // [2]
   uint64_t* dq_free = bars + 13;    // [2]
-  uint64_t* stage_free = bars + 15; // [2]
   uint64_t* acc_done = bars + 17;
   uint64_t* drain = bars + 18;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
@@ -467,7 +469,6 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       mbar_init(&p_full[i], 256);
       mbar_init(&dq_full[i], 1);
       mbar_init(&dq_free[i], 128);
-      mbar_init(&stage_free[i], 1);
       mbar_init(&pd_read[i], 1);
     }
     mbar_init(acc_done, 1);
@@ -628,11 +629,11 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       const int bb = t & 1, sl = t % kRing;
       const uint32_t use = (t >> 1) & 1;
       const int q0 = (qt0 + t % nqt) * TQ3;
-      // S^T / dP^T in TMEM, the LSE / D rows, and (from t = 2) the TMA read of the
-      // dQ staging that last used this buffer's P^T / dS^T tiles
+      // S^T / dP^T in TMEM, the LSE / D rows, and (from t = 2) the MMAs that last
+      // read this buffer's P^T / dS^T tiles
       if (!mbar_wait(&sdp_full[bb], use, a.err, kErrEpiWait) ||
           !mbar_wait(&qd_full[sl], (uint32_t)(t / kRing) & 1, a.err, kErrEpiWait) ||
-          (t >= 2 && !mbar_wait(&stage_free[bb], use ^ 1, a.err, kErrEpiWait))) {
+          (t >= 2 && !mbar_wait(&pd_read[bb], use ^ 1, a.err, kErrEpiWait))) {
         ok = false;
         break;
       }
@@ -707,55 +708,42 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
     }
   } else {
     // ------------------------------------------------------- dQ epilogue
-    // dQ^T leaves TMEM (lane = head dim d, 64 query columns), is staged x scale as
-    // four 32-dim x 64-query boxes (128-byte swizzle) and added to dq_acc by TMA
-    // reduce-adds; rows past Sq hold exact zeros.
+    // dQ^T leaves TMEM (lane = head dim d, 64 query columns) and is added x scale
+    // into dq_acc with red.global.add: for one query the 32 lanes of a warp
+    // cover 32 consecutive head dims, one 128-byte line.
     const int quarter = warp & 3;
     const int d = quarter * 32 + lane;  // head-dim index (TMEM lane of dQ^T)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const bool issuer = quarter == 0 && lane == 0;
-    const int chunk = (d & 31) >> 2, sub = (d & 3) * 4;
     for (int t = 0; t < total; ++t) {
       const int bb = t & 1;
       const uint32_t use = (t >> 1) & 1;
       const int h = hk * G + t / nqt;
       const int q0 = (qt0 + t % nqt) * TQ3;
       // dq_full: dQ^T(t) is in TMEM
-      if (!group_all(1, mbar_wait(&dq_full[bb], use, a.err, kErrEpiWait))) break;
+      if (!mbar_wait(&dq_full[bb], use, a.err, kErrEpiWait)) break;
       if (issuer) trace_at(a, kTrDqStart, t);
       tc_fence_after();
-      unsigned char* sDQ = sPD + bb * kPD;  // 4 x (64 rows x 128 B), swizzled
-      unsigned char* box = sDQ + (d >> 5) * (TQ3 * 128);
       uint32_t r[64];
       tmem_ld_32x32b_x32(tmem + lane_base + bb * 128, r);  // both loads in flight, one wait
       tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + 32, r + 32);
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&dq_free[bb]);  // dQ^T is in registers: the MMAs may reuse the columns
-      // pd_read: the dV / dK MMAs of sub-tile t, the last readers of this buffer's
-      // P^T / dS^T tiles (the staging area), have completed
-      if (!group_all(1, mbar_wait(&pd_read[bb], use, a.err, kErrEpiWait))) break;
-#pragma unroll
-      for (int e = 0; e < 64; ++e)
-        *reinterpret_cast<float*>(box + e * 128 + ((chunk ^ (e & 7)) * 16) + sub) = __uint_as_float(r[e]) * a.scale;
       if (issuer) trace_at(a, kTrDqFree, t);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (issuer) {
+      float* dst = a.dq_acc + (((int64_t)b * a.Sq + q0) * a.H + h) * HD + d;
+      const int64_t qstride = (int64_t)a.H * HD;
+      const int nq = min(TQ3, a.Sq - q0);
+      if (nq == TQ3) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          asm volatile(
-              "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(&tmdQ),
-              "r"(smem_addr(sDQ + j * (TQ3 * 128))), "r"(h * HD + j * 32), "r"(b * a.Sq + q0)
-              : "memory");
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        // the reduce-adds have read the staging: the softmax warps may overwrite it
-        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-        mbar_arrive(&stage_free[bb]);
-        trace_at(a, kTrDqStaged, t);
+        for (int e = 0; e < TQ3; ++e) atomicAdd(dst + e * qstride, __uint_as_float(r[e]) * a.scale);
+      } else {
+#pragma unroll
+        for (int e = 0; e < TQ3; ++e)
+          if (e < nq) atomicAdd(dst + e * qstride, __uint_as_float(r[e]) * a.scale);
       }
+      if (issuer) trace_at(a, kTrDqStaged, t);
     }
-    if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -842,12 +830,11 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
     attn_bwd_sm100_kernel<<<grid, kThreads, kSmem, stream()>>>(tq, tk, tv, tdo, tdq, args);
   } else {
     CUtensorMap tq64 = bshd_map(q, bwd3::TQ3), tdo64 = bshd_map(dout, bwd3::TQ3);
-    CUtensorMap tdq64 = dq_map(dq_acc.data_ptr<float>(), B * Sq, H * HD, bwd3::TQ3);
     LRB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_v3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)bwd3::kSmem));
     LRB_CHECK(B * Hkv * ((Skv + TK - 1) / TK) < (1LL << 31), "attn_bwd: too many CTAs");
     const dim3 grid3((unsigned)(B * Hkv * ((Skv + TK - 1) / TK)));
-    attn_bwd_v3_kernel<<<grid3, bwd3::kThreads, bwd3::kSmem, stream()>>>(tq64, tk, tv, tdo64, tdq64, args);
+    attn_bwd_v3_kernel<<<grid3, bwd3::kThreads, bwd3::kSmem, stream()>>>(tq64, tk, tv, tdo64, args);
   }
   LRB_LAUNCH_CHECK();
 }
