@@ -65,6 +65,8 @@ enum TraceEv : int {
   kTrDqStart,        // dQ warp: dQ^T ready
   kTrDqFree,         // dQ warp: TMEM read, dq_free arrived
   kTrDqStaged,       // dQ warp: adds into dq_acc issued
+  kTrSdpStart,       // MMA: S^T / dP^T issue begins (its conditions met)
+  kTrDvdkStart,      // MMA: dV / dK issue begins
   kTrEvents
 };
 
@@ -521,7 +523,7 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < TQ3 / 32; ++i) {
           const int c = i * 32 + lane, q = q0 + c;
-          sL[sl * TQ3 + c] = q < a.Sq ? lse_row[q] * kLog2e : 0.f;
+          sL[sl * TQ3 + c] = q < a.Sq ? -lse_row[q] * kLog2e : 0.f;  // negated: P = 2^(s * scale_log2 + L)
           sD[sl * TQ3 + c] = q < a.Sq ? di_row[q] : 0.f;
         }
         mbar_arrive(&qd_full[sl]);  // release: the LSE / D rows above are visible to the waiters
@@ -544,73 +546,97 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       constexpr uint32_t id_dq = umma_idesc_f16_major(128, TQ3, true, true, true);     // both MN-major
       const uint32_t k_ = smem_addr(sK), v_ = smem_addr(sV);
       bool ok = mbar_wait(kv_full, 0, a.err, kErrMmaWait);
-      // Event-driven issue: the thread polls the conditions of both pending
-      // steps and issues whichever is ready, so a finished softmax of one
-      // buffer never waits behind the other buffer's dQ read-out.  Steps:
+      // Event-driven issue: the thread polls the conditions of three pending
+      // steps and issues whichever is ready first in priority order.  Steps:
+      //   dQ^T of sub-tile nd: its P^T / dS^T are written (p_full);
       //   S^T / dP^T of sub-tile ns: its Q / dO slot landed and the dQ^T of
-      //     sub-tile ns-2 (same TMEM buffer) has been read out;
-      //   dV / dK / dQ^T of sub-tile na (in order): its P^T / dS^T are written.
+      //     sub-tile ns-2 (same TMEM buffer) has been read out (dq_free);
+      //   dV / dK of sub-tile nv (after its dQ^T).
+      // Descriptors are built once and advanced by integer adds (desc_add): the
+      // issuing thread shares its SM sub-partition with softmax warps, so every
+      // instruction it saves shortens the issue of a sub-tile's 32 MMAs.
+      const uint64_t dK = umma_desc_k_sw128(k_), dV = umma_desc_k_sw128(v_);
+      const uint64_t dKmn = umma_desc_mn_sw128(k_, kKVHalf, 1024);
+      const uint64_t dQ0 = umma_desc_k_sw128(smem_addr(sQ)), dO0 = umma_desc_k_sw128(smem_addr(sdO));
+      const uint64_t dQmn0 = umma_desc_mn_sw128(smem_addr(sQ), kQHalf, 1024);
+      const uint64_t dOmn0 = umma_desc_mn_sw128(smem_addr(sdO), kQHalf, 1024);
+      const uint64_t dPt0 = umma_desc_k_sw128(smem_addr(sPD));
+      const uint64_t dDsmn0 = umma_desc_mn_sw128(smem_addr(sPD) + kPT, kPT, 1024);
       auto issue_sdp = [&](int t) {
+        trace_at(a, kTrSdpStart, t);
         const int bb = t & 1, sl = t % kRing;
-        const uint32_t q_ = smem_addr(sQ + sl * kQ), o_ = smem_addr(sdO + sl * kQ);
+        const uint64_t dq = desc_add(dQ0, sl * kQ), dop = desc_add(dO0, sl * kQ);
         const uint32_t tS = tmem + bb * 128, tP = tS + 64;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint32_t ka = (k >> 2) * kKVHalf + (k & 3) * 32, kb = (k >> 2) * kQHalf + (k & 3) * 32;
-          umma_f16(tS, umma_desc_k_sw128(k_ + ka), umma_desc_k_sw128(q_ + kb), id_sdp, k != 0);
-          umma_f16(tP, umma_desc_k_sw128(v_ + ka), umma_desc_k_sw128(o_ + kb), id_sdp, k != 0);
+          umma_f16(tS, desc_add(dK, ka), desc_add(dq, kb), id_sdp, k != 0);
+          umma_f16(tP, desc_add(dV, ka), desc_add(dop, kb), id_sdp, k != 0);
         }
         umma_commit(&sdp_full[bb]);
         trace_at(a, kTrSdpIssue, t);
       };
-      // dQ^T first: its read-out (and with it the next S^T / dP^T of this
-      // buffer) overlaps the dV / dK MMAs that follow
-      auto issue_acc = [&](int t) {
-        const int bb = t & 1, sl = t % kRing;
-        const uint32_t q_ = smem_addr(sQ + sl * kQ), o_ = smem_addr(sdO + sl * kQ);
-        const uint32_t pt_ = smem_addr(sPD + bb * kPD), ds_ = pt_ + kPT;
+      // dQ^T = K^T dS^T of sub-tile t, into the consumed S^T_b columns
+      auto issue_dq = [&](int t) {
+        const int bb = t & 1;
+        const uint64_t dsmn = desc_add(dDsmn0, bb * kPD);
 #pragma unroll
-        for (int k = 0; k < TK / 16; ++k)  // dQ^T = K^T dS^T  (into the consumed S^T_b columns)
-          umma_f16(tmem + bb * 128, umma_desc_mn_sw128(k_ + k * 2048, kKVHalf, 1024),
-                   umma_desc_mn_sw128(ds_ + k * 2048, kPT, 1024), id_dq, k != 0);
+        for (int k = 0; k < TK / 16; ++k)
+          umma_f16(tmem + bb * 128, desc_add(dKmn, k * 2048), desc_add(dsmn, k * 2048), id_dq, k != 0);
         umma_commit(&dq_full[bb]);
+      };
+      // dV += P^T dO ; dK += dS^T Q of sub-tile t
+      auto issue_dvdk = [&](int t) {
+        trace_at(a, kTrDvdkStart, t);
+        const int bb = t & 1, sl = t % kRing;
+        const uint64_t qmn = desc_add(dQmn0, sl * kQ), omn = desc_add(dOmn0, sl * kQ);
+        const uint64_t pt = desc_add(dPt0, bb * kPD), ds = desc_add(dPt0, bb * kPD + kPT);
+        const uint32_t first = t != 0;
 #pragma unroll
-        for (int k = 0; k < TQ3 / 16; ++k) {  // dV += P^T dO ; dK += dS^T Q
-          umma_f16(tdV, umma_desc_k_sw128(pt_ + k * 32), umma_desc_mn_sw128(o_ + k * 2048, kQHalf, 1024), id_acc,
-                   (t | k) != 0);
-          umma_f16(tdK, umma_desc_k_sw128(ds_ + k * 32), umma_desc_mn_sw128(q_ + k * 2048, kQHalf, 1024), id_acc,
-                   (t | k) != 0);
+        for (int k = 0; k < TQ3 / 16; ++k) {
+          umma_f16(tdV, desc_add(pt, k * 32), desc_add(omn, k * 2048), id_acc, k != 0 ? 1u : first);
+          umma_f16(tdK, desc_add(ds, k * 32), desc_add(qmn, k * 2048), id_acc, k != 0 ? 1u : first);
         }
         umma_commit(&qd_free[sl]);
         umma_commit(&pd_read[bb]);
         trace_at(a, kTrAccIssue, t);
       };
-      int ns = 0, na = 0;
+      // Issue order: dQ^T(t) as soon as its softmax is done, dV / dK(t) right
+      // behind it (the softmax of t+2 waits for them, pd_read), then S^T / dP^T.
+      // Queuing S^T(t+2) ahead of dV / dK(t) measured slower: it lengthens the
+      // chain to the softmax of t+2 by the dV / dK MMAs.
+      int ns = 0, nd = 0, nv = 0;
       uint32_t idle = 0;
-      while (ok && na < total) {
+      uint64_t idle_since = 0;
+      while (ok && nv < total) {
         bool did = false;
-        if (ns < total && ns <= na + 1) {
-          const int bb = ns & 1, sl = ns % kRing;
-          if (mbar_try_wait(&qd_full[sl], (uint32_t)(ns / kRing) & 1) &&
-              (ns < 2 || mbar_try_wait(&dq_free[bb], (((uint32_t)ns >> 1) & 1) ^ 1))) {
-            tc_fence_after();
-            issue_sdp(ns++);
-            did = true;
-          }
-        }
-        if (!did && na < ns && mbar_try_wait(&p_full[na & 1], ((uint32_t)na >> 1) & 1)) {
-          trace_at(a, kTrPWait, na);
+        if (nd < ns && mbar_test(&p_full[nd & 1], ((uint32_t)nd >> 1) & 1)) {
+          trace_at(a, kTrPWait, nd);
           tc_fence_after();
-          issue_acc(na++);
+          issue_dq(nd++);
+          did = true;
+        } else if (nv < nd) {
+          issue_dvdk(nv++);
+          did = true;
+        } else if (ns < total && ns <= nd + 1 && mbar_test(&qd_full[ns % kRing], (uint32_t)(ns / kRing) & 1) &&
+                   (ns < 2 || mbar_test(&dq_free[ns & 1], (((uint32_t)ns >> 1) & 1) ^ 1))) {
+          tc_fence_after();
+          issue_sdp(ns++);
           did = true;
         }
+        // polls return at once; every 1024 idle polls the wall-time bound and the
+        // error word (another role gave up) are checked
         if (did) {
           idle = 0;
-        } else if (++idle > kSpinLimit) {
-          record_error(a.err, kErrMmaWait);
-          ok = false;
-        } else if ((idle & 1023u) == 0 && *reinterpret_cast<volatile int*>(a.err) != 0) {
-          ok = false;  // another role gave up: stop issuing
+        } else if ((++idle & 1023u) == 0) {
+          const uint64_t now = global_ns();
+          if (idle == 1024u) idle_since = now;
+          if (*reinterpret_cast<volatile int*>(a.err) != 0) {
+            ok = false;  // another role gave up: stop issuing
+          } else if (now - idle_since > kWaitLimitNs) {
+            record_error(a.err, kErrMmaWait);
+            ok = false;
+          }
         }
       }
       umma_commit(acc_done);
@@ -643,22 +669,40 @@ __global__ void __launch_bounds__(bwd3::kThreads, 1)
       tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + c0, reinterpret_cast<uint32_t*>(s));
       tmem_ld_32x32b_x32(tmem + lane_base + bb * 128 + 64 + c0, reinterpret_cast<uint32_t*>(dp));
       tmem_ld_wait();
-      const float* L = sL + sl * TQ3 + c0;
+      const float* L = sL + sl * TQ3 + c0;  // -LSE * log2(e)
       const float* Dd = sD + sl * TQ3 + c0;
       uint32_t pp[16], dd[16];
+      // warp-uniform: all 32 keys x 32 queries of this warp are valid (inside the
+      // sequences and on or below the causal diagonal) -- no per-element masks
+      const int key_hi = n0 + quarter * 32 + 31, qlo = q0 + c0;
+      const bool full = qlo + 32 <= a.Sq && key_hi < a.Skv && (!a.causal || key_hi <= qlo + off);
+      if (full) {
+        const uint64_t sc2 = f2_pack(a.scale_log2, a.scale_log2);
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        float pv[2], dv2[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int q = q0 + c0 + i + e;
-          const bool valid = q < a.Sq && key < a.Skv && (!a.causal || key <= q + off);
-          const float p = valid ? fast_exp2(fmaf(s[i + e], a.scale_log2, -L[i + e])) : 0.f;
-          pv[e] = p;
-          dv2[e] = p * (dp[i + e] - Dd[i + e]);
+        for (int i = 0; i < 32; i += 2) {
+          const uint64_t l2 = *reinterpret_cast<const uint64_t*>(L + i);
+          const uint64_t d2 = *reinterpret_cast<const uint64_t*>(Dd + i);
+          const float2 x = f2_unpack(f2_fma(f2_pack(s[i], s[i + 1]), sc2, l2));
+          const float p0 = fast_exp2(x.x), p1 = fast_exp2(x.y);
+          const float2 g = f2_unpack(f2_mul(f2_pack(p0, p1), f2_sub(f2_pack(dp[i], dp[i + 1]), d2)));
+          pp[i / 2] = pack2(p0, p1);
+          dd[i / 2] = pack2(g.x, g.y);
         }
-        pp[i / 2] = pack2(pv[0], pv[1]);
-        dd[i / 2] = pack2(dv2[0], dv2[1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float pv[2], dv2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int q = qlo + i + e;
+            const bool valid = q < a.Sq && key < a.Skv && (!a.causal || key <= q + off);
+            const float p = valid ? fast_exp2(fmaf(s[i + e], a.scale_log2, L[i + e])) : 0.f;
+            pv[e] = p;
+            dv2[e] = p * (dp[i + e] - Dd[i + e]);
+          }
+          pp[i / 2] = pack2(pv[0], pv[1]);
+          dd[i / 2] = pack2(dv2[0], dv2[1]);
+        }
       }
       unsigned char* pt = sPD + bb * kPD;
       unsigned char* ds = pt + kPT;

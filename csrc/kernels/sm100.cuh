@@ -56,6 +56,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of the phase (mbarrier.test_wait): returns at once.  For
+// threads that poll several barriers in turn -- try_wait may suspend the thread
+// for a system-dependent time while the phase is incomplete, which would delay
+// the poll of the next barrier.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // try_wait that lets the hardware suspend the thread for up to `ns` nanoseconds
 // while the phase is incomplete (it resumes as soon as the phase completes), so
 // a waiting warp issues no instructions instead of spinning.
@@ -92,6 +109,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     if (global_ns() - start > kWaitLimitNs) {
       record_error(err, code);
       return false;
+    }
+  }
+}
+
+// The same bound, polling with test_wait instead of sleeping in the barrier: for
+// waits on the critical path of a pipeline, where a suspended thread's wake-up
+// latency would add to every step.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if ((i & 1023u) == 0) {
+      if (err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return false;
+      if (global_ns() - start > kWaitLimitNs) {
+        record_error(err, code);
+        return false;
+      }
     }
   }
 }
@@ -278,6 +313,16 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t addr) {
   d |= (uint64_t)1 << 46;                          // descriptor version (sm_100)
   d |= (uint64_t)2 << 61;                          // layout: 128-byte swizzle
   return d;
+}
+
+// The descriptor of the same operand `bytes` further on (a multiple of 16).  The
+// start address sits in the low 14 bits as addr >> 4, and shared-memory
+// addresses stay below 2^18, so a 32-bit add on the low word never carries out
+// of the field: one integer add instead of rebuilding the descriptor, which
+// keeps the single MMA-issuing thread short.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) {
+  const uint32_t lo = (uint32_t)d + (bytes >> 4), hi = (uint32_t)(d >> 32);
+  return ((uint64_t)hi << 32) | lo;
 }
 
 // Instruction descriptor, kind::f16: fp32 accumulate, bf16 (is_bf16) or fp16 A/B,
