@@ -24,6 +24,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> ce_fwd(const at::Tensor&, const a
 at::Tensor ce_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t);
 at::Tensor ce_bwd_vocab_shard(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t);
 // routing.cu
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> route_slots(const at::Tensor&, int64_t, int64_t, int64_t);
 std::tuple<at::Tensor, at::Tensor, at::Tensor> softmax_topk_fwd(const at::Tensor&, int64_t);
 at::Tensor chunk_mean_pool_fwd(const at::Tensor&, int64_t);
 std::tuple<at::Tensor, at::Tensor> compact_chunks(const at::Tensor&);
@@ -128,6 +129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fwd", &lrb::ce_fwd);
   m.def("ce_bwd", &lrb::ce_bwd);
   m.def("ce_bwd_vocab_shard", &lrb::ce_bwd_vocab_shard);
+  m.def("route_slots", &lrb::route_slots, "capacity slots, owner ranks and per-expert counts of routed assignments");
   m.def("softmax_topk_fwd", &lrb::softmax_topk_fwd);
   m.def("chunk_mean_pool_fwd", &lrb::chunk_mean_pool_fwd);
   m.def("compact_chunks", &lrb::compact_chunks);

@@ -102,7 +102,82 @@ __global__ void compact_kernel(const bool* __restrict__ mask, int64_t* __restric
   if (threadIdx.x == 0) counts[b] = base;
 }
 
+// Capacity slots of the routed assignments, in (token, k) order: assignment a
+// (expert e = idx[a]) gets slot = its rank among the assignments to e that come
+// before it, or -1 when that rank is >= cap (cap < 0: no limit); also its
+// owner rank e / epl and local expert e % epl, and the per-expert totals.  One
+// CTA of 32 warps: warp w owns the contiguous range [w A / 32, (w+1) A / 32);
+// pass 1 counts per warp and expert (shared-memory atomics), an exclusive scan
+// over the warps gives each warp's starting rank per expert, pass 2 walks the
+// range again in order, 32 assignments at a time, ranking equal experts inside
+// the batch by __match_any_sync.  Deterministic; no host read.
+__global__ void __launch_bounds__(1024) route_slots_kernel(const int64_t* __restrict__ idx, int64_t A, int E,
+                                                           int epl, int cap, int* __restrict__ dest,
+                                                           int* __restrict__ le, int* __restrict__ slot,
+                                                           int* __restrict__ counts) {
+  extern __shared__ int cnt[];  // [32 warps][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int64_t a0 = A * warp / 32, a1 = A * (warp + 1) / 32;
+  for (int64_t b = a0; b < a1; b += 32) {
+    const int64_t a = b + lane;
+    if (a < a1) atomicAdd(&cnt[warp * E + (int)idx[a]], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = cnt[w * E + e];
+      cnt[w * E + e] = run;
+      run += c;
+    }
+    counts[e] = run;
+  }
+  __syncthreads();
+  const unsigned below = (1u << lane) - 1u;
+  for (int64_t b = a0; b < a1; b += 32) {
+    const int64_t a = b + lane;
+    const bool in = a < a1;
+    const int e = in ? (int)idx[a] : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    int rank = 0;
+    if (in) {
+      rank = cnt[warp * E + e] + __popc(same & below);
+      slot[a] = (cap < 0 || rank < cap) ? rank : -1;
+      dest[a] = e / epl;
+      le[a] = e % epl;
+    }
+    __syncwarp();
+    if (in && (same & below) == 0) cnt[warp * E + e] += __popc(same);  // the group's first lane advances
+    __syncwarp();
+  }
+}
+
 }  // namespace
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> route_slots(const at::Tensor& idx, int64_t num_experts,
+                                                                       int64_t experts_per_rank, int64_t cap) {
+  LRB_CHECK(idx.is_cuda() && idx.scalar_type() == at::kLong && idx.is_contiguous(),
+            "route_slots: contiguous int64 CUDA expert indices");
+  LRB_CHECK(num_experts >= 1 && num_experts <= 1024 && experts_per_rank >= 1 && num_experts % experts_per_rank == 0,
+            "route_slots: 1 <= E <= 1024 experts, E a multiple of the experts per rank");
+  const int64_t A = idx.numel();
+  LRB_CHECK(A < (1LL << 31), "route_slots: too many assignments");
+  c10::cuda::CUDAGuard g(idx.device());
+  auto i32 = idx.options().dtype(at::kInt);
+  auto dest = at::empty({A}, i32), le = at::empty({A}, i32), slot = at::empty({A}, i32);
+  auto counts = at::zeros({num_experts}, i32);
+  if (A == 0) return {dest, le, slot, counts};
+  const int smem = 32 * (int)num_experts * (int)sizeof(int);
+  if (smem > 48 * 1024)
+    LRB_CUDA_CHECK(cudaFuncSetAttribute(route_slots_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  route_slots_kernel<<<1, 1024, smem, stream()>>>(idx.data_ptr<int64_t>(), A, (int)num_experts, (int)experts_per_rank,
+                                                  (int)cap, dest.data_ptr<int>(), le.data_ptr<int>(),
+                                                  slot.data_ptr<int>(), counts.data_ptr<int>());
+  LRB_LAUNCH_CHECK();
+  return {dest, le, slot, counts};
+}
 
 std::tuple<at::Tensor, at::Tensor, at::Tensor> softmax_topk_fwd(const at::Tensor& logits, int64_t k) {
   LRB_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.is_contiguous(), "softmax_topk: 2-D contiguous logits");

@@ -13,13 +13,13 @@ from llm_research_b200.ops.activation import swiglu
 from llm_research_b200.ops.rope import rope_qkv
 from llm_research_b200.ops.attention import attention
 from llm_research_b200.ops.loss import cross_entropy
-from llm_research_b200.ops.routing import softmax_topk, chunk_mean_pool, compact_chunks, compact_chunks_fixed
+from llm_research_b200.ops.routing import softmax_topk, chunk_mean_pool, compact_chunks, compact_chunks_fixed, route_slots
 from llm_research_b200.ops.optim import muon_prologue, muon_prologue_into, muon_epilogue, newton_schulz, adamw_step, axpy_list
 from llm_research_b200.ops.quant import int4_quantize, int4_dequantize, nvfp4_quantize, nvfp4_dequantize
 
 __all__ = [
     "rms_norm", "rms_norm_residual", "swiglu", "rope_qkv", "attention", "cross_entropy",
-    "softmax_topk", "chunk_mean_pool", "compact_chunks", "compact_chunks_fixed",
+    "softmax_topk", "chunk_mean_pool", "compact_chunks", "compact_chunks_fixed", "route_slots",
     "muon_prologue", "muon_prologue_into", "muon_epilogue", "newton_schulz", "adamw_step", "axpy_list",
     "int4_quantize", "int4_dequantize", "nvfp4_quantize", "nvfp4_dequantize",
 ]

@@ -5,6 +5,12 @@
   ``(weights fp32, indices int64, probs fp32)``
   (``olympus/kernels/fused_gate_route.py:36-46``).  Differentiable in
   ``weights`` and ``probs``.
+* :func:`route_slots` -- for routed assignments ``idx (T, k)`` in (token, k)
+  order: the capacity slot of each (its rank among earlier assignments to the
+  same expert, ``-1`` at or over ``cap``; ``cap < 0`` keeps all), its owner
+  rank and local expert under ``experts_per_rank``, and the per-expert counts
+  -- one device kernel, no host read (the capacity rule of
+  ``genesis/model/moe.py`` and of the expert-parallel dispatch).
 * :func:`chunk_mean_pool` -- ``(B, S, D) -> (B, S/c, D)`` mean over chunks of
   ``c`` tokens, fp32 accumulation.
 * :func:`compact_chunks` -- pack the selected chunk ids of every row of a bool
@@ -60,6 +66,18 @@ def softmax_topk(logits: torch.Tensor, top_k: int):
         return _softmax_topk_ref(logits, top_k)
     w, idx, probs = _SoftmaxTopkFn.apply(logits.contiguous(), top_k)
     return w, idx, probs
+
+
+def route_slots(idx: torch.Tensor, num_experts: int, experts_per_rank: int | None = None, cap: int = -1):
+    """``(dest, local_expert, slot, counts)``, int32: see the module docstring."""
+    epl = num_experts if experts_per_rank is None else int(experts_per_rank)
+    if idx.is_cuda:
+        return native().route_slots(idx.contiguous().long(), int(num_experts), epl, int(cap))
+    flat = idx.reshape(-1).long()
+    onehot = F.one_hot(flat, num_experts)
+    pos = (onehot.cumsum(0) * onehot).sum(-1) - 1
+    slot = pos if cap < 0 else torch.where(pos < cap, pos, torch.full_like(pos, -1))
+    return ((flat // epl).int(), (flat % epl).int(), slot.int(), onehot.sum(0).int())
 
 
 class _ChunkPoolFn(torch.autograd.Function):

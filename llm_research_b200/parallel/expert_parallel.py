@@ -59,15 +59,13 @@ def current_expert_parallel():
     return _EP_CONTEXT
 
 
-def make_route(idx: torch.Tensor, experts_per_rank: int, num_experts: int, cap: int
-               ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """``(dest, local_expert, slot)`` int32 per assignment (``slot = -1``: over capacity)."""
-    flat = idx.reshape(-1).long()
-    onehot = F.one_hot(flat, num_experts)
-    pos = (onehot.cumsum(0) * onehot).sum(-1) - 1
-    slot = torch.where(pos < cap, pos, torch.full_like(pos, -1))
-    return ((flat // experts_per_rank).int().contiguous(), (flat % experts_per_rank).int().contiguous(),
-            slot.int().contiguous())
+def make_route(idx: torch.Tensor, experts_per_rank: int, num_experts: int, cap: int, with_counts: bool = False):
+    """``(dest, local_expert, slot)`` int32 per assignment (``slot = -1``: over
+    capacity), and the per-expert assignment counts when ``with_counts``: one
+    device kernel (``ops.route_slots``) on CUDA."""
+    dest, le, slot, counts = ops.route_slots(idx, num_experts, experts_per_rank, cap)
+    route = (dest.contiguous(), le.contiguous(), slot.contiguous())
+    return (route, counts) if with_counts else route
 
 
 class EPComm:
@@ -247,13 +245,16 @@ class ExpertParallelMoE(nn.Module):
         shape = x.shape
         xf = x.reshape(-1, shape[-1])
         T = xf.shape[0]
-        logits = self.router(xf)
+        from llm_research_b200.ops.linear import dense
+
+        logits = dense(xf, self.router.weight)  # the pair GEMM where it applies
         w, idx, probs = ops.softmax_topk(logits.float(), self.top_k)
-        # Switch-style load balance: E * sum_e fraction_e * mean_prob_e
-        frac = F.one_hot(idx.reshape(-1).long(), self.num_experts).float().mean(0)
-        self.last_aux = self.num_experts * (frac * probs.mean(0)).sum()
         cap = math.ceil(self.capacity_factor * T * self.top_k / self.num_experts)
-        route = make_route(idx, self.epl, self.num_experts, cap)
+        route, counts = make_route(idx, self.epl, self.num_experts, cap, with_counts=True)
+        # Switch-style load balance: E * sum_e fraction_e * mean_prob_e, the
+        # fractions from the routing kernel's per-expert counts
+        frac = counts.float() / max(T * self.top_k, 1)
+        self.last_aux = self.num_experts * (frac * probs.mean(0)).sum()
         fused = self.comm is not None and xf.is_cuda and xf.dtype == torch.bfloat16 and cap <= self.comm.cap_max
         if fused:
             x_e = _Dispatch.apply(xf, self.comm, route, cap, self.top_k)
