@@ -69,7 +69,7 @@ constexpr uint32_t kMnBox = 64 * BK * 2;        // 8 KB: 64 MN elements x 64 K r
 // TMA stores of the previous ones drain.
 constexpr uint32_t kOutWarpBytes = 8192;
 constexpr uint32_t kOutSmem = 4 * kOutWarpBytes;  // 32 KB
-constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + kOutSmem + 256;
+constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + kOutSmem + 512;
 
 // kSwiGLU: the up / gate projection of a SwiGLU FFN.  CTA rank 0 loads its B
 // half from W1 (map tmB) and rank 1 from W_gate (map tmB2), both at rows
@@ -83,7 +83,12 @@ constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + kOutSmem + 256;
 // the rotate-half rule out[i] = x[i] cos[i] - x[i+64] sin[i],
 // out[i+64] = x[i+64] cos[i+64] + x[i] sin[i+64] on the bf16-rounded products,
 // the fp32 tables args.cos / args.sin, stored column-major (128 x positions).
-enum Epi : int { kStore = 0, kAccumF32 = 1, kSwiGLU = 2, kRoPE = 3 };
+// kAxpby: C = alpha * acc + beta * D (16-bit C and D, D through map tmH): each
+// epilogue warp TMA-loads the D box of a 32-column chunk into that chunk's
+// staging slot two chunks ahead (an mbarrier per warp and slot), combines in
+// place and stores the slot -- the Newton-Schulz updates P = c A A + b A and
+// X' = P X + a X, and residual additions.
+enum Epi : int { kStore = 0, kAccumF32 = 1, kSwiGLU = 2, kRoPE = 3, kAxpby = 4 };
 
 struct PairArgs {
   void* C;
@@ -102,6 +107,8 @@ struct PairArgs {
   const float* sin;
   int seq, pos0, rot_cols;
   int64_t tab_pitch;
+  // kAxpby only
+  float beta;
   // Pipeline trace (null in normal runs): %globaltimer stamps of the first
   // kTraceUnits work units of CTA pair 0, layout [event][unit].
   unsigned long long* trace;
@@ -174,6 +181,15 @@ __device__ __forceinline__ void tma_reduce_add_box(const CUtensorMap* map, const
   asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];"
                ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
+}
+
+// 3-D tiled load of one epilogue box into this CTA's shared memory, completion on
+// this CTA's mbarrier.  No multicast.
+__device__ __forceinline__ void tma_load_box(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
 }
 
 template <typename OutT, int EPI>
@@ -260,6 +276,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* accempty = accfull + 2;
   uint64_t* drain = accempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* dbar = drain + 3;  // [4 epilogue warps][4 slots] (kAxpby)
   int* err = &g_gemm_pair_err;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -282,6 +299,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&accempty[b], 8);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(drain, 1);
+    if constexpr (EPI == kAxpby)
+      for (int i = 0; i < 16; ++i) mbar_init(&dbar[i], 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -290,6 +309,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmB2);
       tma_prefetch_desc(&tmH);
     }
+    if constexpr (EPI == kAxpby) tma_prefetch_desc(&tmH);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -371,7 +391,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr uint32_t kBox = 32 * 32 * sizeof(OutT);           // bytes of one staged box
     constexpr int kSlots = (int)(kOutWarpBytes / kBox);         // 2 (fp32) or 4 (16-bit)
     int acc = 0, nbox = 0;
-    uint32_t acc_phase = 0;
+    uint32_t acc_phase = 0, dpar = 0;
     for (int unit = pair; unit < num_units; unit += npairs) {
       int tm, tn, kb0, kb1, bi;
       unit_coords(unit, num_tiles, tiles_m, tiles_n, nk, args, tm, tn, kb0, kb1, bi);
@@ -437,6 +457,81 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           put_box(&tmC, xa, col_a);
           if (col_b < args.N) put_box(&tmC, xb, col_b);
           if (tracer && pc == 0) trace_unit(args, kTrC0Stored, ui);
+        }
+        if (tracer) trace_unit(args, kTrEpiEnd, ui);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        continue;
+      }
+      if constexpr (EPI == kAxpby) {
+        uint64_t* db = dbar + (warp - 2) * 4;
+        const int nbase = nbox;
+        auto valid = [&](int c) { return row0 < args.M && tn * BN + c * 32 < args.N; };
+        auto load_d = [&](int c) {  // lane 0: the D box of chunk c into its slot
+          const int sd = (nbase + c) % kSlots;
+          mbar_arrive_expect_tx(&db[sd], kBox);
+          tma_load_box(boxes + sd * kBox, &tmH, &db[sd], tn * BN + c * 32, row0, bi);
+        };
+        uint32_t pend = 0;  // slots with a D load issued and not yet waited for (same in every lane)
+        if (lane == 0) {
+          // the slots of chunks 0 and 1 last held the stores of chunks nbase-4 and nbase-3
+          if (valid(0)) {
+            asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory");
+            load_d(0);
+          }
+          if (valid(1)) {
+            asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory");
+            load_d(1);
+          }
+        }
+        if (valid(0)) pend |= 1u << (nbase % kSlots);
+        if (valid(1)) pend |= 1u << ((nbase + 1) % kSlots);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+          tmem_ld_wait();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&accempty[acc]), 0));
+            if (tracer) trace_unit(args, kTrEpiFreed, ui);
+          }
+          if (!valid(c)) continue;  // and so every later chunk of the tile
+          if (c + 2 < BN / 32 && valid(c + 2)) {
+            if (lane == 0) {
+              asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // chunk c-2's store read its slot
+              load_d(c + 2);
+            }
+            pend |= 1u << ((nbase + c + 2) % kSlots);
+          }
+          const int sd = (nbase + c) % kSlots;
+          unsigned char* box = boxes + sd * kBox;
+          const bool got = mbar_wait(&db[sd], (dpar >> sd) & 1u, err, kErrEpiWait);
+          dpar ^= 1u << sd;
+          pend &= ~(1u << sd);
+          if (!got) {
+            // give up, but only after the loads still in flight have landed (bounded waits)
+            for (int s2 = 0; s2 < kSlots; ++s2)
+              if (pend & (1u << s2)) mbar_wait(&db[s2], (dpar >> s2) & 1u, nullptr, 0);
+            break;
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4* p = reinterpret_cast<uint4*>(box + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16));
+            Vec16<OutT> dv;
+            dv.raw = *p;
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              dv.v[t] = from_f<OutT>(fmaf(args.alpha, __uint_as_float(r[8 * j + t]), args.beta * to_f(dv.v[t])));
+            *p = dv.raw;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_box(&tmC, box, tn * BN + c * 32, row0, bi);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          ++nbox;
         }
         if (tracer) trace_unit(args, kTrEpiEnd, ui);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
@@ -739,6 +834,51 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, a
   } else {
     if (bf) launch_layout<float, kStore, true>(a_mn, b_mn, ta, tb, tc, args, pairs);
     else launch_layout<float, kStore, false>(a_mn, b_mn, ta, tb, tc, args, pairs);
+  }
+}
+
+// C = alpha * op(A) op(B)^T + beta * D (2-D, or 3-D batched), 16-bit A, B, C, D;
+// A K-major, B K-major or MN-major (b_mn).  D may alias neither C nor A / B.
+void gemm_pair_axpby(const at::Tensor& A, const at::Tensor& B, bool b_mn, at::Tensor& C, const at::Tensor& D,
+                     double alpha, double beta) {
+  const Mat a = check_operand(A, "A", true), b = check_operand(B, "B", true), c = check_operand(C, "C", true);
+  const Mat dm = check_operand(D, "D", true);
+  LRB_CHECK(A.scalar_type() == B.scalar_type() && C.scalar_type() == A.scalar_type() &&
+                D.scalar_type() == A.scalar_type(),
+            "gemm_pair_axpby: A, B, C and D of one 16-bit dtype");
+  LRB_CHECK(A.dim() == B.dim() && A.dim() == C.dim() && A.dim() == D.dim() && a.batch == b.batch &&
+                a.batch == c.batch && a.batch == dm.batch,
+            "gemm_pair_axpby: operands all 2-D or all 3-D with one batch size");
+  LRB_CHECK(tma_ok(A, a) && tma_ok(B, b) && tma_ok(C, c) && tma_ok(D, dm),
+            "gemm_pair_axpby: 16-byte aligned bases and pitches");
+  const int64_t M = a.rows, K = a.cols;
+  const int64_t N = b_mn ? b.cols : b.rows, KB = b_mn ? b.rows : b.cols;
+  LRB_CHECK(K == KB && c.rows == M && c.cols == N && dm.rows == M && dm.cols == N, "gemm_pair_axpby: shape mismatch");
+  LRB_CHECK(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31) && a.batch < (1LL << 16),
+            "gemm_pair_axpby: dimensions too large");
+  LRB_CHECK(a.batch == 1 || (a.bstride >= a.rows * a.ld && b.bstride >= b.rows * b.ld && c.bstride >= c.rows * c.ld),
+            "gemm_pair_axpby: batch entries must not overlap");
+  LRB_CHECK(C.data_ptr() != A.data_ptr() && C.data_ptr() != B.data_ptr() && C.data_ptr() != D.data_ptr(),
+            "gemm_pair_axpby: C must not alias A, B or D");
+  c10::cuda::CUDAGuard g(A.device());
+  if (M == 0 || N == 0 || a.batch == 0) return;
+  LRB_CHECK(K > 0, "gemm_pair_axpby: K must be positive");
+  const bool bf = A.scalar_type() == at::kBFloat16;
+  CUtensorMap ta = make_map(A.data_ptr(), a.batch, M, K, a.ld, a.bstride, BK, BM, bf);
+  CUtensorMap tb = b_mn ? make_map(B.data_ptr(), b.batch, K, N, b.ld, b.bstride, 64, BK, bf)
+                        : make_map(B.data_ptr(), b.batch, N, K, b.ld, b.bstride, BK, BN / 2, bf);
+  CUtensorMap tc = make_out_map(C.data_ptr(), c.batch, M, N, c.ld, c.bstride, C.scalar_type());
+  CUtensorMap td = make_out_map(D.data_ptr(), dm.batch, M, N, dm.ld, dm.bstride, D.scalar_type());
+  const int tiles = (int)(a.batch * ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN));
+  const int pairs = std::max(1, std::min(tiles, max_pairs(A.get_device())));
+  PairArgs args{C.data_ptr(), c.ld, (int)M, (int)N, (int)K, (float)alpha, 1, 1, 1, GROUP_M, (int)a.batch, c.bstride,
+                nullptr, nullptr, 1, 0, 0, 0, (float)beta};
+  if (bf) {
+    if (b_mn) launch_t<__nv_bfloat16, kAxpby, true, false, true>(ta, tb, tc, args, pairs, nullptr, &td);
+    else launch_t<__nv_bfloat16, kAxpby, true, false, false>(ta, tb, tc, args, pairs, nullptr, &td);
+  } else {
+    if (b_mn) launch_t<__half, kAxpby, false, false, true>(ta, tb, tc, args, pairs, nullptr, &td);
+    else launch_t<__half, kAxpby, false, false, false>(ta, tb, tc, args, pairs, nullptr, &td);
   }
 }
 

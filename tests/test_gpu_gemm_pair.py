@@ -302,3 +302,27 @@ def test_qkv_rope_epilogue_matches_separate_rotation(H, Hkv, offset):
     for name, a, b in (("dx", x.grad, x2.grad), ("dw", w.grad, w2.grad)):
         err = ((a.float() - b.float()).norm() / b.float().norm()).item()
         assert err < 1e-2, (name, err)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch,M,N,K", [(None, 264, 520, 200), (3, 512, 768, 256), (8, 256, 704, 256), (None, 96, 40, 64)])
+@pytest.mark.parametrize("b_mn", [False, True])
+def test_gemm_pair_axpby(batch, M, N, K, b_mn):
+    """C = alpha A op(B)^T + beta D (the Newton-Schulz / residual epilogue, D staged
+    by TMA two chunks ahead) against fp32, 2-D and batched, ragged tiles."""
+    from llm_research_b200._ext import native
+    from llm_research_b200.ops.gemm import gemm_pair_error
+
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    lead = () if batch is None else (batch,)
+    A = torch.randn(*lead, M, K, device="cuda", generator=g).bfloat16()
+    B = torch.randn(*lead, *((K, N) if b_mn else (N, K)), device="cuda", generator=g).bfloat16()
+    D = torch.randn(*lead, M, N, device="cuda", generator=g).bfloat16()
+    C = torch.empty(*lead, M, N, device="cuda", dtype=torch.bfloat16)
+    native().gemm_pair_axpby(A, B, b_mn, C, D, 0.75, -1.5)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    Bf = B.float() if b_mn else B.float().transpose(-1, -2)
+    ref = 0.75 * (A.float() @ Bf) - 1.5 * D.float()
+    err = ((C.float() - ref).norm() / ref.norm()).item()
+    assert err < 1e-2, err
