@@ -13,7 +13,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from llm_research_b200 import ops
-from llm_research_b200.ops.linear import cat_rows, project, swiglu_up
+from llm_research_b200.ops.linear import cat_rows, project, project_residual, swiglu_up
 
 
 def default_ffn_dim(d_model: int) -> int:
@@ -51,15 +51,21 @@ class SwiGLUFFN(nn.Module):
         h = ops.swiglu(gu)
         return row_parallel(self.dropout(h), self.w2.weight, group, comm)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``FFN(x)``, or ``residual + FFN(x)`` with the addition folded into the down
+        projection's GEMM epilogue when ``residual`` is given."""
         if self.w1.bias is None and not isinstance(self.dropout, nn.Dropout):
             h = swiglu_up(x, self.w1.weight, self.w_gate.weight)  # one launch: both projections + gating
             if h is not None:
-                return project(h, self.w2.weight, self.w2.bias)
+                if residual is not None and self.w2.bias is None:
+                    return project_residual(h, self.w2.weight, residual)
+                y = project(h, self.w2.weight, self.w2.bias)
+                return y if residual is None else residual + y
         w = cat_rows(self.w1.weight, self.w_gate.weight)
         b = None
         if self.w1.bias is not None:
             b = torch.cat([self.w1.bias, self.w_gate.bias], 0)
         gu = project(x, w, b)  # [..., up | gate]
         h = ops.swiglu(gu)
-        return project(self.dropout(h), self.w2.weight, self.w2.bias)
+        y = project(self.dropout(h), self.w2.weight, self.w2.bias)
+        return y if residual is None else residual + y

@@ -73,6 +73,8 @@ class TransformerBlock(nn.Module):
         h = self.attn(self.attn_norm(x), cos, sin, attention_mask=attention_mask,
                       kv_cache=kv_cache, position_offset=position_offset)
         normed, x = self.ffn_norm.forward_residual(h, x)
+        if isinstance(self.ffn, SwiGLUFFN):
+            return self.ffn(normed, residual=x)  # the residual added in the down projection's epilogue
         return x + self.ffn(normed)
 
     def _forward_tp(self, x, cos, sin, seq_shape):

@@ -203,6 +203,40 @@ class _PairLinearFn(torch.autograd.Function):
         return dx, dw, None
 
 
+class _PairLinearResidualFn(torch.autograd.Function):
+    """y = r + x W^T with the residual added in the forward GEMM's epilogue (the
+    pair kernel's axpby mode reads r by TMA): no separate add over the
+    activations.  Backward: dr = dY, and the linear's dgrad / wgrad."""
+
+    @staticmethod
+    def forward(ctx, x2d, w, acc, r2d):
+        from llm_research_b200._ext import native
+
+        ctx.save_for_backward(x2d, w)
+        ctx.acc = acc
+        y = torch.empty(x2d.shape[0], w.shape[0], dtype=x2d.dtype, device=x2d.device)
+        native().gemm_pair_axpby(x2d, w, False, y, r2d, 1.0, 1.0)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        dx, dw, _ = _PairLinearFn.backward(ctx, dy)
+        return dx, dw, None, dy
+
+
+def project_residual(x: torch.Tensor, w: torch.Tensor, r: torch.Tensor) -> torch.Tensor:
+    """``r + project(x, w)``: on the pair kernel with the residual added in the GEMM
+    epilogue where it applies (bf16 precision, 16-bit CUDA operands of one dtype,
+    aligned rows), else the separate add."""
+    if (_PRECISION == "bf16" and x.numel() > 0 and _pair_ok(x, w) and r.dtype == x.dtype and r.is_cuda
+            and r.shape == (*x.shape[:-1], w.shape[0])):
+        r2d = _rows(r.reshape(-1, w.shape[0]))
+        x2d = _rows(x.reshape(-1, x.shape[-1]))
+        acc = _acc_of(w) if torch.is_grad_enabled() and w.requires_grad else None
+        return _PairLinearResidualFn.apply(x2d, w, acc, r2d).view(r.shape)
+    return r + project(x, w)
+
+
 def _aligned_rows(t: torch.Tensor) -> bool:
     return t.dim() == 2 and t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
 

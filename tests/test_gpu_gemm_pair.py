@@ -326,3 +326,28 @@ def test_gemm_pair_axpby(batch, M, N, K, b_mn):
     ref = 0.75 * (A.float() @ Bf) - 1.5 * D.float()
     err = ((C.float() - ref).norm() / ref.norm()).item()
     assert err < 1e-2, err
+
+
+@pytest.mark.gpu
+def test_project_residual_epilogue_matches_separate_add():
+    """r + x W^T with the residual in the GEMM epilogue: forward and the gradients
+    of x, W and r against fp32 autograd; ragged rows."""
+    from llm_research_b200.ops.gemm import gemm_pair_error
+    from llm_research_b200.ops.linear import project_residual
+
+    g = torch.Generator(device="cuda").manual_seed(31)
+    T, K, N = 1000, 768, 520
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16().requires_grad_()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16().requires_grad_()
+    r = torch.randn(T, N, device="cuda", generator=g).bfloat16().requires_grad_()
+    dy = torch.randn(T, N, device="cuda", generator=g).bfloat16()
+    y = project_residual(x, w, r)
+    y.backward(dy)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    xf, wf, rf = (t.detach().float().requires_grad_() for t in (x, w, r))
+    yf = rf + xf @ wf.t()
+    yf.backward(dy.float())
+    for name, got, ref in (("y", y, yf), ("dx", x.grad, xf.grad), ("dw", w.grad, wf.grad), ("dr", r.grad, rf.grad)):
+        err = ((got.float() - ref).norm() / ref.norm()).item()
+        assert err < 1e-2, (name, err)
