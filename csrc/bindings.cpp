@@ -60,6 +60,7 @@ int64_t sm100_error(int64_t);
 void gemm_pair(const at::Tensor&, const at::Tensor&, bool, bool, at::Tensor&, bool, double);
 int64_t gemm_pair_error(int64_t);
 void gemm_pair_axpby(const at::Tensor&, const at::Tensor&, bool, at::Tensor&, const at::Tensor&, double, double);
+void gemm_pair_swiglu_bwd(const at::Tensor&, const at::Tensor&, const at::Tensor&, at::Tensor&);
 void gemm_pair_set_trace(const c10::optional<at::Tensor>&);
 void gemm_pair_swiglu(const at::Tensor&, const at::Tensor&, const at::Tensor&, at::Tensor&, at::Tensor&);
 void gemm_pair_rope(const at::Tensor&, const at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t,
@@ -158,6 +159,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair_error", &lrb::gemm_pair_error);
   m.def("gemm_pair_rope", &lrb::gemm_pair_rope, "QKV projection with RoPE on the query/key heads in the epilogue");
   m.def("gemm_pair_axpby", &lrb::gemm_pair_axpby, "C = alpha A op(B)^T + beta D on the CTA-pair kernel (2-D or batched)");
+  m.def("gemm_pair_swiglu_bwd", &lrb::gemm_pair_swiglu_bwd, "dgu = swiglu_bwd(dY W2, gu) in one CTA-pair launch");
   m.def("gemm_pair_set_trace", &lrb::gemm_pair_set_trace, "pipeline trace of the pair GEMM (None switches it off)");
   m.def("gemm_pair_swiglu", &lrb::gemm_pair_swiglu, "gu = [x W1^T | x Wg^T], h = silu(x Wg^T) * x W1^T in one launch");
   m.def("attn_sm100_supported", &lrb::attn_sm100_supported);

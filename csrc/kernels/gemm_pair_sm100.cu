@@ -88,7 +88,12 @@ constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + kOutSmem + 512;
 // staging slot two chunks ahead (an mbarrier per warp and slot), combines in
 // place and stores the slot -- the Newton-Schulz updates P = c A A + b A and
 // X' = P X + a X, and residual additions.
-enum Epi : int { kStore = 0, kAccumF32 = 1, kSwiGLU = 2, kRoPE = 3, kAxpby = 4 };
+// kSwiGLUBwd: the down projection's dgrad dh = dY W2 followed by the SwiGLU
+// backward: the epilogue TMA-loads the u and g boxes of the chunk (maps tmB2,
+// tmH over gu = [u | g]) one chunk ahead into two staging slots and writes
+// du = dh silu(g) and dg = dh u s (1 + g (1 - s)), s = sigmoid(g), through tmC
+// and tmG (dgu = [du | dg]) from the same slots; dh itself never reaches memory.
+enum Epi : int { kStore = 0, kAccumF32 = 1, kSwiGLU = 2, kRoPE = 3, kAxpby = 4, kSwiGLUBwd = 5 };
 
 struct PairArgs {
   void* C;
@@ -299,7 +304,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&accempty[b], 8);  // one arrival per epilogue warp of both CTAs
     }
     mbar_init(drain, 1);
-    if constexpr (EPI == kAxpby)
+    if constexpr (EPI == kAxpby || EPI == kSwiGLUBwd)
       for (int i = 0; i < 16; ++i) mbar_init(&dbar[i], 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -310,6 +315,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmH);
     }
     if constexpr (EPI == kAxpby) tma_prefetch_desc(&tmH);
+    if constexpr (EPI == kSwiGLUBwd) {
+      tma_prefetch_desc(&tmB2);
+      tma_prefetch_desc(&tmH);
+      tma_prefetch_desc(&tmG);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -529,6 +539,88 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) {
             tma_store_box(&tmC, box, tn * BN + c * 32, row0, bi);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          ++nbox;
+        }
+        if (tracer) trace_unit(args, kTrEpiEnd, ui);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        continue;
+      }
+      if constexpr (EPI == kSwiGLUBwd) {
+        // slots 2 (n & 1) and 2 (n & 1) + 1 hold the u and g boxes of chunk n
+        uint64_t* db = dbar + (warp - 2) * 4;
+        const int nbase = nbox;
+        auto valid = [&](int c) { return row0 < args.M && tn * BN + c * 32 < args.N; };
+        auto load_ug = [&](int c) {  // lane 0
+          const int s0 = 2 * ((nbase + c) & 1);
+          mbar_arrive_expect_tx(&db[s0], kBox);
+          tma_load_box(boxes + s0 * kBox, &tmB2, &db[s0], tn * BN + c * 32, row0, 0);
+          mbar_arrive_expect_tx(&db[s0 + 1], kBox);
+          tma_load_box(boxes + (s0 + 1) * kBox, &tmH, &db[s0 + 1], tn * BN + c * 32, row0, 0);
+        };
+        uint32_t pend = 0;
+        if (valid(0)) {
+          if (lane == 0) {
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // earlier stores have read their slots
+            load_ug(0);
+          }
+          pend |= 3u << (2 * (nbase & 1));
+        }
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+          tmem_ld_wait();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&accempty[acc]), 0));
+            if (tracer) trace_unit(args, kTrEpiFreed, ui);
+          }
+          if (!valid(c)) continue;  // and so every later chunk of the tile
+          if (c + 1 < BN / 32 && valid(c + 1)) {
+            if (lane == 0) {
+              asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // chunk c-1's stores read the slots
+              load_ug(c + 1);
+            }
+            pend |= 3u << (2 * ((nbase + c + 1) & 1));
+          }
+          const int s0 = 2 * ((nbase + c) & 1);
+          bool got = mbar_wait(&db[s0], (dpar >> s0) & 1u, err, kErrEpiWait);
+          dpar ^= 1u << s0;
+          got = got && mbar_wait(&db[s0 + 1], (dpar >> (s0 + 1)) & 1u, err, kErrEpiWait);
+          dpar ^= 1u << (s0 + 1);
+          pend &= ~(3u << s0);
+          if (!got) {
+            for (int s2 = 0; s2 < kSlots; ++s2)
+              if (pend & (1u << s2)) mbar_wait(&db[s2], (dpar >> s2) & 1u, nullptr, 0);
+            break;
+          }
+          unsigned char* ub = boxes + s0 * kBox;
+          unsigned char* gb = ub + kBox;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int off = lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16);
+            Vec16<__nv_bfloat16> uv, gv;
+            uv.raw = *reinterpret_cast<const uint4*>(ub + off);
+            gv.raw = *reinterpret_cast<const uint4*>(gb + off);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              const float d = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * j + t])));  // dh in bf16
+              const float u = __bfloat162float(uv.v[t]), g = __bfloat162float(gv.v[t]);
+              const float sg = fast_rcp(1.f + fast_exp2(-kLog2e * g));
+              uv.v[t] = __float2bfloat16_rn(d * g * sg);
+              gv.v[t] = __float2bfloat16_rn(d * u * sg * (1.f + g * (1.f - sg)));
+            }
+            *reinterpret_cast<uint4*>(ub + off) = uv.raw;
+            *reinterpret_cast<uint4*>(gb + off) = gv.raw;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_box(&tmC, ub, tn * BN + c * 32, row0, 0);
+            tma_store_box(&tmG, gb, tn * BN + c * 32, row0, 0);
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
           ++nbox;
@@ -880,6 +972,40 @@ void gemm_pair_axpby(const at::Tensor& A, const at::Tensor& B, bool b_mn, at::Te
     if (b_mn) launch_t<__half, kAxpby, false, false, true>(ta, tb, tc, args, pairs, nullptr, &td);
     else launch_t<__half, kAxpby, false, false, false>(ta, tb, tc, args, pairs, nullptr, &td);
   }
+}
+
+// The down projection's dgrad with the SwiGLU backward in the epilogue:
+// dgu = swiglu_bwd(dY W2, gu), i.e. [dh silu(g) | dh u s (1 + g (1 - s))] with
+// dh = dY W2 (rows x F, never written), dY (rows x d), W2 (d x F, the nn.Linear
+// weight, read MN-major), gu = [u | g] and dgu (rows x 2F), all bf16.
+void gemm_pair_swiglu_bwd(const at::Tensor& DY, const at::Tensor& W2, const at::Tensor& GU, at::Tensor& DGU) {
+  const Mat dy = check_operand(DY, "dy", true), w = check_operand(W2, "w2", true);
+  const Mat gu = check_operand(GU, "gu", true), dg = check_operand(DGU, "dgu", true);
+  LRB_CHECK(DY.dim() == 2 && W2.dim() == 2 && GU.dim() == 2 && DGU.dim() == 2, "gemm_pair_swiglu_bwd: 2-D operands");
+  LRB_CHECK(DY.scalar_type() == at::kBFloat16 && W2.scalar_type() == at::kBFloat16 && GU.scalar_type() == at::kBFloat16 &&
+                DGU.scalar_type() == at::kBFloat16,
+            "gemm_pair_swiglu_bwd: bf16 operands");
+  const int64_t M = dy.rows, K = dy.cols, F = w.cols;
+  LRB_CHECK(w.rows == K && gu.rows == M && gu.cols == 2 * F && dg.rows == M && dg.cols == 2 * F,
+            "gemm_pair_swiglu_bwd: shape mismatch");
+  LRB_CHECK(F % 8 == 0, "gemm_pair_swiglu_bwd: F must be a multiple of 8 (the gate halves start 16-byte aligned)");
+  LRB_CHECK(tma_ok(DY, dy) && tma_ok(W2, w) && tma_ok(GU, gu) && tma_ok(DGU, dg),
+            "gemm_pair_swiglu_bwd: 16-byte aligned bases and pitches required");
+  LRB_CHECK(DGU.data_ptr() != GU.data_ptr(), "gemm_pair_swiglu_bwd: dgu must not alias gu");
+  c10::cuda::CUDAGuard g(DY.device());
+  if (M == 0 || F == 0) return;
+  LRB_CHECK(K > 0, "gemm_pair_swiglu_bwd: K must be positive");
+  CUtensorMap ta = make_map(DY.data_ptr(), 1, M, K, dy.ld, 0, BK, BM, true);
+  CUtensorMap tb = make_map(W2.data_ptr(), 1, K, F, w.ld, 0, 64, BK, true);  // MN-major B
+  CUtensorMap tu = make_out_map(GU.data_ptr(), 1, M, F, gu.ld, 0, at::kBFloat16);
+  CUtensorMap tg = make_out_map(static_cast<__nv_bfloat16*>(GU.data_ptr()) + F, 1, M, F, gu.ld, 0, at::kBFloat16);
+  CUtensorMap tdu = make_out_map(DGU.data_ptr(), 1, M, F, dg.ld, 0, at::kBFloat16);
+  CUtensorMap tdg = make_out_map(static_cast<__nv_bfloat16*>(DGU.data_ptr()) + F, 1, M, F, dg.ld, 0, at::kBFloat16);
+  const int tiles = (int)(((M + 2 * BM - 1) / (2 * BM)) * ((F + BN - 1) / BN));
+  const int pairs = std::max(1, std::min(tiles, max_pairs(DY.get_device())));
+  PairArgs args{DGU.data_ptr(), dg.ld, (int)M, (int)F, (int)K, 1.f, 1, 1, 1, GROUP_M, 1, 0,
+                nullptr, nullptr, 1, 0, 0, 0, 0.f};
+  launch_t<__nv_bfloat16, kSwiGLUBwd, true, false, true>(ta, tb, tdu, args, pairs, &tu, &tg, &tdg);
 }
 
 // SwiGLU up / gate projection: gu = [x W1^T | x W_gate^T] (rows x 2F) and

@@ -13,7 +13,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from llm_research_b200 import ops
-from llm_research_b200.ops.linear import cat_rows, project, project_residual, swiglu_up
+from llm_research_b200.ops.linear import cat_rows, project, project_residual, swiglu_ffn, swiglu_up
 
 
 def default_ffn_dim(d_model: int) -> int:
@@ -54,6 +54,13 @@ class SwiGLUFFN(nn.Module):
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         """``FFN(x)``, or ``residual + FFN(x)`` with the addition folded into the down
         projection's GEMM epilogue when ``residual`` is given."""
+        if self.w1.bias is None and self.w2.bias is None and not isinstance(self.dropout, nn.Dropout):
+            # one autograd node: up/gate + SwiGLU in one launch, the down projection
+            # (+ residual in its epilogue), and a backward whose down-projection
+            # dgrad runs the SwiGLU backward in its epilogue
+            y = swiglu_ffn(x, self.w1.weight, self.w_gate.weight, self.w2.weight, residual)
+            if y is not None:
+                return y
         if self.w1.bias is None and not isinstance(self.dropout, nn.Dropout):
             h = swiglu_up(x, self.w1.weight, self.w_gate.weight)  # one launch: both projections + gating
             if h is not None:

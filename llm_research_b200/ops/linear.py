@@ -397,6 +397,92 @@ def swiglu_up(x: torch.Tensor, w1: torch.Tensor, wg: torch.Tensor) -> torch.Tens
     return h.view(*x.shape[:-1], w1.shape[0])
 
 
+# ---------------------------------------------------- whole SwiGLU FFN, fused
+class _SwiGLUFFNFn(torch.autograd.Function):
+    """y = [r +] silu(x Wg^T) * (x W1^T) W2^T as one autograd node, so the backward
+    can run the down projection's dgrad and the SwiGLU backward as one launch
+    (``gemm_pair_swiglu_bwd``: dh = dY W2 never reaches memory).  Forward: the
+    up/gate GEMM with the SwiGLU epilogue, then the down GEMM (with the residual
+    in its epilogue when given).  Backward: dgu (fused), dW2 = dY^T h,
+    dx = dgu [W1; Wg], [dW1; dWg] = dgu^T x, dr = dY; weight gradients go straight
+    into the engine's fp32 accumulators when it provides them."""
+
+    @staticmethod
+    def forward(ctx, x2d, w1, wg, w2, r2d, acc_ug, acc_2):
+        from llm_research_b200._ext import native
+        from llm_research_b200.ops.gemm import linear_fwd
+
+        F = w1.shape[0]
+        gu = torch.empty(x2d.shape[0], 2 * F, dtype=x2d.dtype, device=x2d.device)
+        h = torch.empty(x2d.shape[0], F, dtype=x2d.dtype, device=x2d.device)
+        native().gemm_pair_swiglu(x2d, w1, wg, gu, h)
+        if r2d is not None:
+            y = torch.empty(x2d.shape[0], w2.shape[0], dtype=x2d.dtype, device=x2d.device)
+            native().gemm_pair_axpby(h, w2, False, y, r2d, 1.0, 1.0)
+        else:
+            y = linear_fwd(h, w2)
+        ctx.save_for_backward(x2d, w1, wg, w2, gu, h)
+        ctx.accs = (acc_ug, acc_2)
+        ctx.has_r = r2d is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from llm_research_b200._ext import native
+        from llm_research_b200.ops.gemm import linear_dgrad, linear_wgrad
+
+        x2d, w1, wg, w2, gu, h = ctx.saved_tensors
+        acc_ug, acc_2 = ctx.accs
+        dy = _rows(dy)
+        dgu = torch.empty_like(gu)
+        native().gemm_pair_swiglu_bwd(dy, w2, gu, dgu)
+        dw2 = None
+        if ctx.needs_input_grad[3]:
+            if acc_2 is not None:
+                linear_wgrad(dy, h, out=acc_2, accumulate=True)
+                dw2 = accumulated_marker(w2)
+            else:
+                dw2 = linear_wgrad(dy, h)
+        w = w1.as_strided((2 * w1.shape[0], w1.shape[1]), (w1.shape[1], 1)) if _adjacent([w1, wg]) \
+            else torch.cat([w1, wg], 0)
+        dx = linear_dgrad(dgu, w) if ctx.needs_input_grad[0] else None
+        dw1 = dwg = None
+        if ctx.needs_input_grad[1] or ctx.needs_input_grad[2]:
+            if acc_ug is not None:
+                linear_wgrad(dgu, x2d, out=acc_ug, accumulate=True)
+                dw1, dwg = accumulated_marker(w1), accumulated_marker(wg)
+            else:
+                dw = linear_wgrad(dgu, x2d)
+                dw1, dwg = dw[: w1.shape[0]], dw[w1.shape[0]:]
+        ctx.accs = None
+        return dx, dw1, dwg, dw2, (dy if ctx.has_r else None), None, None
+
+
+def swiglu_ffn(x: torch.Tensor, w1: torch.Tensor, wg: torch.Tensor, w2: torch.Tensor,
+               residual: torch.Tensor | None = None):
+    """``[residual +] W2(silu(x Wg^T) * (x W1^T))`` over the last dimension of ``x`` as
+    one fused node (see ``_SwiGLUFFNFn``), or None when it does not apply (bf16
+    CUDA and the pair kernel's shapes)."""
+    if not (_PRECISION == "bf16" and x.is_cuda and x.dtype == torch.bfloat16 and x.numel() > 0
+            and _pair_ok(x, w1) and _pair_ok(x, wg) and w1.shape == wg.shape and w2.dtype == x.dtype
+            and w2.dim() == 2 and w2.shape[1] == w1.shape[0] and w2.shape[0] % 8 == 0 and _aligned_rows(w2)):
+        return None
+    if residual is not None and not (residual.is_cuda and residual.dtype == x.dtype
+                                     and residual.shape == (*x.shape[:-1], w2.shape[0])):
+        return None
+    x2d = _rows(x.reshape(-1, x.shape[-1]))
+    r2d = None if residual is None else _rows(residual.reshape(-1, w2.shape[0]))
+    acc_ug = acc_2 = None
+    if torch.is_grad_enabled() and _DIRECT_ACC:
+        a1, ag = getattr(w1, "_lrb_acc", None), getattr(wg, "_lrb_acc", None)
+        if (w1.requires_grad or wg.requires_grad) and a1 is not None and ag is not None and _adjacent([a1, ag]):
+            acc_ug = a1.as_strided((2 * a1.shape[0], a1.shape[1]), (a1.shape[1], 1))
+        if w2.requires_grad:
+            acc_2 = _acc_of(w2)
+    y = _SwiGLUFFNFn.apply(x2d, w1, wg, w2, r2d, acc_ug, acc_2)
+    return y.view(*x.shape[:-1], w2.shape[0])
+
+
 # ------------------------------------------------------------ fused QKV + RoPE
 _TABLES_T: dict = {}
 

@@ -351,3 +351,40 @@ def test_project_residual_epilogue_matches_separate_add():
     for name, got, ref in (("y", y, yf), ("dx", x.grad, xf.grad), ("dw", w.grad, wf.grad), ("dr", r.grad, rf.grad)):
         err = ((got.float() - ref).norm() / ref.norm()).item()
         assert err < 1e-2, (name, err)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("with_residual", [False, True])
+def test_swiglu_ffn_fused_node_matches_fp32(with_residual):
+    """The whole SwiGLU FFN as one node (up/gate + SwiGLU epilogue, down GEMM with
+    the residual epilogue, down dgrad with the SwiGLU-backward epilogue) against
+    fp32 autograd: output and the gradients of x, W1, Wg, W2 and the residual;
+    ragged F and rows."""
+    from llm_research_b200.ops.gemm import gemm_pair_error
+    from llm_research_b200.ops.linear import swiglu_ffn
+
+    g = torch.Generator(device="cuda").manual_seed(37)
+    T, d, F = 1000, 512, 392
+    x = torch.randn(T, d, device="cuda", generator=g).bfloat16().requires_grad_()
+    w1 = (torch.randn(F, d, device="cuda", generator=g) * 0.05).bfloat16().requires_grad_()
+    wg = (torch.randn(F, d, device="cuda", generator=g) * 0.05).bfloat16().requires_grad_()
+    w2 = (torch.randn(d, F, device="cuda", generator=g) * 0.05).bfloat16().requires_grad_()
+    r = torch.randn(T, d, device="cuda", generator=g).bfloat16().requires_grad_() if with_residual else None
+    dy = torch.randn(T, d, device="cuda", generator=g).bfloat16()
+    y = swiglu_ffn(x, w1, wg, w2, r)
+    assert y is not None
+    y.backward(dy)
+    torch.cuda.synchronize()
+    assert gemm_pair_error(0) == 0
+    leaves = [x, w1, wg, w2] + ([r] if with_residual else [])
+    fl = [t.detach().float().requires_grad_() for t in leaves]
+    xf, w1f, wgf, w2f = fl[:4]
+    yf = (torch.nn.functional.silu(xf @ wgf.t()) * (xf @ w1f.t())) @ w2f.t()
+    if with_residual:
+        yf = yf + fl[4]
+    yf.backward(dy.float())
+    err = ((y.float() - yf).norm() / yf.norm()).item()
+    assert err < 2e-2, ("y", err)
+    for name, got, ref in zip(["dx", "dw1", "dwg", "dw2", "dr"], leaves, fl):
+        e = ((got.grad.float() - ref.grad).norm() / ref.grad.norm()).item()
+        assert e < 3e-2, (name, e)
