@@ -164,3 +164,73 @@ class PipelineStage(nn.Module):
         for work, _ in pending:
             work.wait()
         return torch.stack(losses).sum() if self.last else None
+
+
+def _bench(argv=None) -> None:
+    """``torchrun --nproc-per-node P -m llm_research_b200.parallel.pipeline``: time the
+    1F1B forward + backward of one step (``--micro-batches`` of ``--micro x --seq``
+    tokens) of a preset on P GPUs, one stage per GPU, with CUDA events (max over
+    ranks; the optimizer step is not part of it); rank 0 prints a JSON line."""
+    import argparse
+    import datetime
+    import json
+    import os
+
+    import torch.nn.functional as F
+
+    from genesis.model.hlrt import HLRT
+    from llm_research_b200.models.presets import build_hlrt_config
+
+    ap = argparse.ArgumentParser(description=_bench.__doc__.split("\n")[0])
+    ap.add_argument("--preset", default="genesis-1b")
+    ap.add_argument("--micro-batches", type=int, default=8)
+    ap.add_argument("--micro", type=int, default=1)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=2)
+    args = ap.parse_args(argv)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    cfg = build_hlrt_config(args.preset)
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = HLRT(cfg).to(torch.bfloat16)
+    st = PipelineStage(model)
+    g = torch.Generator().manual_seed(1)
+    mbs = [torch.randint(0, cfg.vocab_size, (args.micro, args.seq), generator=g) for _ in range(args.micro_batches)]
+
+    def loss_fn(out, ids):
+        logits = out["logits"]
+        return F.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]).float(), ids[:, 1:].reshape(-1))
+
+    def step():
+        for p in st.stage_parameters():
+            p.grad = None
+        st.train_step(mbs, loss_fn, act_shape=(args.micro, args.seq, cfg.d_model), act_dtype=torch.bfloat16)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([start.elapsed_time(end) / args.steps], device=device)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    tokens = args.micro_batches * args.micro * args.seq
+    if dist.get_rank() == 0:
+        print(json.dumps({"case": "pipeline_1f1b", "preset": args.preset, "stages": dist.get_world_size(),
+                          "micro_batches": args.micro_batches, "tokens_per_step": tokens,
+                          "ms_per_step": ms.item(), "tokens_per_s": tokens / (ms.item() / 1e3),
+                          "note": "forward + backward of one step, no optimizer"}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    _bench()
