@@ -167,3 +167,26 @@ def test_native_pack_skip_rules(tmp_path, corpus):
     (d / "a.jsonl").write_bytes(("\n".join(lines) + "\n").encode() + b"\xff\xfe bad utf8\n")
     meta = pack_corpus(str(d), str(tmp_path / "o"), vocab, block_size=8, train_ratio=0.5, eos_id=1, threads=2)
     assert meta["total_docs"] == 3 and meta["skipped_docs"] == 5
+
+
+@pytest.mark.skipif(not os.environ.get("LRB_CL100K_RANKS"),
+                    reason="set LRB_CL100K_RANKS to the cl100k_base.tiktoken rank file (not shipped; no network here)")
+def test_native_pack_with_the_cl100k_table(tmp_path):
+    """With the real cl100k_base rank table: the public token ids of a known
+    string, through the Python encoder and through the native packer's stream."""
+    from olympus.data.bpe import load_tiktoken_ranks
+
+    ranks = load_tiktoken_ranks(os.environ["LRB_CL100K_RANKS"])
+    enc = BytePairEncoder(ranks)
+    assert enc.encode_ordinary("hello world") == [15339, 1917]
+    d = tmp_path / "in"
+    d.mkdir()
+    text = "hello world " * 20  # 240 bytes: kept
+    (d / "a.jsonl").write_text(json.dumps({"text": text}) + "\n")
+    build_genesis_pack()
+    meta = pack_corpus(str(d), str(tmp_path / "o"), os.environ["LRB_CL100K_RANKS"], block_size=4, train_ratio=1.0,
+                       eos_id=100257, threads=1)
+    got = np.fromfile(tmp_path / "o" / "train_input_ids.bin", dtype="<u4")
+    want = enc.encode_ordinary(text) + [100257]
+    assert meta["total_docs"] == 1
+    np.testing.assert_array_equal(got, np.array(want[: len(want) // 4 * 4], dtype=np.uint32))
