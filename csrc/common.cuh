@@ -24,6 +24,13 @@ namespace lrb {
 
 inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
+// Makes `dev` current in this host thread with its primary context bound.  The
+// autograd engine's worker threads start with no current CUDA context, and
+// c10's device guard does not call cudaSetDevice when the device index already
+// matches; entry points that build tensor maps and launch cluster kernels from
+// a backward pass call this first.
+inline void bind_device(int dev) { LRB_CUDA_CHECK(cudaSetDevice(dev)); }
+
 // Device address of a file-scope `__device__ int` error word (one copy per
 // device, part of the module image) on device `dev`.  Looked up once per device
 // with that device current and cached in atomics: safe from any host thread

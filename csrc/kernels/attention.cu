@@ -479,6 +479,7 @@ std::tuple<at::Tensor, at::Tensor> attn_fwd(const at::Tensor& q, const at::Tenso
                                             bool causal, double scale) {
   check_qkv(q, k, v);
   c10::cuda::CUDAGuard g(q.device());
+  bind_device(q.get_device());
   const int64_t B = q.size(0), Sq = q.size(1), H = q.size(2), D = q.size(3);
   auto o = at::empty({B, Sq, H, D}, q.options());
   auto lse = at::empty({B, H, Sq}, q.options().dtype(at::kFloat));
@@ -508,6 +509,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> attn_bwd(const at::Tensor& dout, 
   check_qkv(q, k, v);
   LRB_CHECK(dout.is_contiguous() && out.is_contiguous(), "attn_bwd: dout/out must be contiguous");
   c10::cuda::CUDAGuard g(q.device());
+  bind_device(q.get_device());
   const int64_t B = q.size(0), Sq = q.size(1), H = q.size(2), D = q.size(3), Skv = k.size(1), Hkv = k.size(2);
   auto dq = at::empty({B, Sq, H, D}, q.options());
   auto dk = at::empty({B, Skv, Hkv, D}, q.options());

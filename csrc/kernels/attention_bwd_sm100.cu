@@ -853,6 +853,7 @@ void attn_bwd_sm100(const at::Tensor& dout, const at::Tensor& q, const at::Tenso
                     const at::Tensor& lse, const at::Tensor& di, at::Tensor& dq_acc, at::Tensor& dk, at::Tensor& dv,
                     bool causal, double scale) {
   c10::cuda::CUDAGuard g(q.device());
+  bind_device(q.get_device());
   const int64_t B = q.size(0), Sq = q.size(1), H = q.size(2), Skv = k.size(1), Hkv = k.size(2);
   if (B * Skv * Hkv == 0) return;
   CUtensorMap tq = bshd_map(q), tk = bshd_map(k), tv = bshd_map(v), tdo = bshd_map(dout);

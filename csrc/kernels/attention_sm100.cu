@@ -694,6 +694,7 @@ std::tuple<at::Tensor, at::Tensor> attn_fwd_sm100(const at::Tensor& q, const at:
                                                   bool causal, double scale) {
   LRB_CHECK(attn_sm100_supported(q, k, v), "attn_fwd_sm100: bf16, head_dim 128, 16-byte aligned strides required");
   c10::cuda::CUDAGuard g(q.device());
+  bind_device(q.get_device());
   const int64_t B = q.size(0), Sq = q.size(1), H = q.size(2), Skv = k.size(1), Hkv = k.size(2);
   LRB_CHECK(Hkv > 0 && H % Hkv == 0 && k.sizes() == v.sizes(), "attn_fwd_sm100: head mismatch");
   auto o = at::empty({B, Sq, H, HD}, q.options());

@@ -194,6 +194,7 @@ __global__ void rope_qkv_bwd_kernel(const T* __restrict__ dq, const T* __restric
 at::Tensor swiglu_fwd(const at::Tensor& gu) {
   LRB_CHECK(gu.is_cuda() && gu.is_contiguous() && gu.size(-1) % 2 == 0, "swiglu_fwd: bad input");
   c10::cuda::CUDAGuard g(gu.device());
+  bind_device(gu.get_device());
   const int64_t F = gu.size(-1) / 2, rows = gu.numel() / gu.size(-1);
   auto sizes = gu.sizes().vec();
   sizes.back() = F;
@@ -214,6 +215,7 @@ at::Tensor swiglu_fwd(const at::Tensor& gu) {
 
 at::Tensor swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu) {
   c10::cuda::CUDAGuard g(gu.device());
+  bind_device(gu.get_device());
   const int64_t F = gu.size(-1) / 2, rows = gu.numel() / gu.size(-1);
   auto dgu = at::empty_like(gu);
   if (rows == 0) return dgu;
@@ -240,6 +242,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> rope_qkv_fwd(const at::Tensor& qk
   LRB_CHECK(cos_t.scalar_type() == at::kFloat && cos_t.size(-1) == D, "rope tables must be fp32 (S, D)");
   LRB_CHECK(cos_t.size(0) >= offset + qkv.size(1), "rope table too short");
   c10::cuda::CUDAGuard g(qkv.device());
+  bind_device(qkv.get_device());
   const int64_t B = qkv.size(0), S = qkv.size(1);
   auto q = at::empty({B, S, H, D}, qkv.options());
   auto k = at::empty({B, S, Hkv, D}, qkv.options());
@@ -266,6 +269,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> rope_qkv_fwd(const at::Tensor& qk
 at::Tensor rope_qkv_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv, const at::Tensor& cos_t,
                         const at::Tensor& sin_t, int64_t H, int64_t Hkv, int64_t D, int64_t offset) {
   c10::cuda::CUDAGuard g(dq.device());
+  bind_device(dq.get_device());
   const int64_t B = dq.size(0), S = dq.size(1);
   auto dqkv = at::empty({B, S, (H + 2 * Hkv) * D}, dq.options());
   const int64_t n = B * S * (H + 2 * Hkv) * (D / 2);
@@ -298,6 +302,7 @@ __global__ void exp2_fma_kernel(const float* __restrict__ x, float* __restrict__
 at::Tensor exp2_fma_eval(const at::Tensor& x) {
   LRB_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous(), "exp2_fma_eval: contiguous fp32 CUDA");
   c10::cuda::CUDAGuard g(x.device());
+  bind_device(x.get_device());
   auto y = at::empty_like(x);
   const int64_t n = x.numel();
   if (n == 0) return y;

@@ -274,6 +274,7 @@ void gemm_batched(const at::Tensor& A, const at::Tensor& B, bool b_mn, const at:
   }
   LRB_CHECK(C.data_ptr() != A.data_ptr() && C.data_ptr() != B.data_ptr(), "gemm_batched: C must not alias A or B");
   c10::cuda::CUDAGuard g(A.device());
+  bind_device(A.get_device());
   if (C.numel() == 0) return;
   LRB_CHECK(K > 0, "gemm_batched: K must be positive");
   CUtensorMap ta = map3d(A, BK, BM);

@@ -252,6 +252,7 @@ at::Tensor gemm_nvfp4(const at::Tensor& A, const at::Tensor& sfa, const at::Tens
                 sfb.is_contiguous(),
             "gemm_nvfp4: scale atoms must cover ceil(rows/128) x K/64 x 512 bytes");
   c10::cuda::CUDAGuard g(A.device());
+  bind_device(A.get_device());
   auto C = at::empty({M, N}, A.options().dtype(at::kBFloat16));
   if (M == 0 || N == 0) return C;
   CUtensorMap ta = fp4_map(A.data_ptr(), M, K / 2, A.stride(0)), tb = fp4_map(B.data_ptr(), N, K / 2, B.stride(0));

@@ -881,6 +881,7 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, bool a_mn, bool b_mn, a
   LRB_CHECK(!accumulate || C.scalar_type() == at::kFloat, "gemm_pair: accumulation needs an fp32 C");
   LRB_CHECK(C.data_ptr() != A.data_ptr() && C.data_ptr() != B.data_ptr(), "gemm_pair: C must not alias A or B");
   c10::cuda::CUDAGuard g(A.device());
+  bind_device(A.get_device());
   if (M == 0 || N == 0 || a.batch == 0) return;
   if (K == 0) {
     if (!accumulate) C.zero_();
@@ -953,6 +954,7 @@ void gemm_pair_axpby(const at::Tensor& A, const at::Tensor& B, bool b_mn, at::Te
   LRB_CHECK(C.data_ptr() != A.data_ptr() && C.data_ptr() != B.data_ptr() && C.data_ptr() != D.data_ptr(),
             "gemm_pair_axpby: C must not alias A, B or D");
   c10::cuda::CUDAGuard g(A.device());
+  bind_device(A.get_device());
   if (M == 0 || N == 0 || a.batch == 0) return;
   LRB_CHECK(K > 0, "gemm_pair_axpby: K must be positive");
   const bool bf = A.scalar_type() == at::kBFloat16;
@@ -993,6 +995,7 @@ void gemm_pair_swiglu_bwd(const at::Tensor& DY, const at::Tensor& W2, const at::
             "gemm_pair_swiglu_bwd: 16-byte aligned bases and pitches required");
   LRB_CHECK(DGU.data_ptr() != GU.data_ptr(), "gemm_pair_swiglu_bwd: dgu must not alias gu");
   c10::cuda::CUDAGuard g(DY.device());
+  bind_device(DY.get_device());
   if (M == 0 || F == 0) return;
   LRB_CHECK(K > 0, "gemm_pair_swiglu_bwd: K must be positive");
   CUtensorMap ta = make_map(DY.data_ptr(), 1, M, K, dy.ld, 0, BK, BM, true);
@@ -1025,6 +1028,7 @@ void gemm_pair_swiglu(const at::Tensor& X, const at::Tensor& W1, const at::Tenso
   LRB_CHECK(tma_ok(X, x) && tma_ok(W1, w1) && tma_ok(Wg, wg) && tma_ok(GU, gu) && tma_ok(Hout, hm),
             "gemm_pair_swiglu: 16-byte aligned bases and pitches required");
   c10::cuda::CUDAGuard g(X.device());
+  bind_device(X.get_device());
   if (M == 0 || F == 0) return;
   CUtensorMap ta = make_map(X.data_ptr(), 1, M, K, x.ld, 0, BK, BM, true);
   CUtensorMap tb = make_map(W1.data_ptr(), 1, F, K, w1.ld, 0, BK, BN / 2, true);
@@ -1058,6 +1062,7 @@ void gemm_pair_rope(const at::Tensor& X, const at::Tensor& W, at::Tensor& Out, c
                 sin_t.sizes() == cos_t.sizes() && seq > 0 && pos0 >= 0 && seq + pos0 <= cos_t.size(1),
             "gemm_pair_rope: fp32 column-major (128, positions) cos / sin tables covering the positions");
   c10::cuda::CUDAGuard g(X.device());
+  bind_device(X.get_device());
   if (M == 0) return;
   CUtensorMap ta = make_map(X.data_ptr(), 1, M, K, x.ld, 0, BK, BM, true);
   CUtensorMap tb = make_map(W.data_ptr(), 1, N, K, w.ld, 0, BK, BN / 2, true);

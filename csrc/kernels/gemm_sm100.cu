@@ -274,6 +274,7 @@ at::Tensor gemm_tn(const at::Tensor& A, const at::Tensor& B, at::ScalarType out_
   check_operand(B, "B");
   LRB_CHECK(A.size(1) == B.size(1) && A.scalar_type() == B.scalar_type(), "gemm: K/dtype mismatch");
   c10::cuda::CUDAGuard g(A.device());
+  bind_device(A.get_device());
   auto C = at::empty({A.size(0), B.size(0)}, A.options().dtype(out_dtype));
   if (C.numel() == 0) return C;
   if (A.size(1) == 0) return C.zero_();
@@ -301,6 +302,7 @@ void gemm_tn_accumulate(const at::Tensor& A, const at::Tensor& B, at::Tensor& C,
                 C.size(1) == B.size(0), "gemm_accumulate: C must be fp32 (M, N)");
   LRB_CHECK((reinterpret_cast<uintptr_t>(C.data_ptr()) % 16) == 0 && C.stride(0) % 4 == 0, "gemm_accumulate: C alignment");
   c10::cuda::CUDAGuard g(A.device());
+  bind_device(A.get_device());
   if (C.numel() == 0 || A.size(1) == 0) return;
   if (A.scalar_type() == at::kBFloat16) launch<float, kAccumF32, true>(A, B, C.data_ptr(), C.stride(0), (float)alpha);
   else launch<float, kAccumF32, false>(A, B, C.data_ptr(), C.stride(0), (float)alpha);

@@ -110,6 +110,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> ce_fwd(const at::Tensor& logits, 
   LRB_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.is_contiguous(), "ce_fwd: logits must be contiguous 2-D");
   LRB_CHECK(targets.scalar_type() == at::kLong && targets.numel() == logits.size(0), "ce_fwd: bad targets");
   c10::cuda::CUDAGuard g(logits.device());
+  bind_device(logits.get_device());
   const int64_t R = logits.size(0), V = logits.size(1);
   auto f32 = logits.options().dtype(at::kFloat);
   auto lse = at::empty({R}, f32);
@@ -133,6 +134,7 @@ at::Tensor ce_bwd_impl(const at::Tensor& logits, const at::Tensor& targets, cons
   LRB_CHECK(targets.scalar_type() == at::kLong && targets.numel() == logits.size(0), "ce_bwd: bad targets");
   LRB_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == logits.size(0), "ce_bwd: lse must be fp32 per row");
   c10::cuda::CUDAGuard g(logits.device());
+  bind_device(logits.get_device());
   const int64_t R = logits.size(0), V = logits.size(1);
   auto dx = at::empty_like(logits);
   auto sc = scale.to(at::kFloat).reshape({1}).contiguous();

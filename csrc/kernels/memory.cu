@@ -103,6 +103,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> topk_softmax_gather(const at::Ten
             "topk_softmax_gather: values (N, dv)");
   LRB_CHECK(k >= 1 && k <= 32 && k <= sim.size(1), "topk_softmax_gather: 1 <= k <= min(32, N)");
   c10::cuda::CUDAGuard g(sim.device());
+  bind_device(sim.get_device());
   const int64_t Q = sim.size(0);
   const int N = (int)sim.size(1), dv = (int)values.size(1);
   auto out = at::empty({Q, dv}, sim.options());

@@ -310,6 +310,7 @@ std::tuple<at::Tensor, at::Tensor> memory_topk_candidates(const at::Tensor& q, c
   LRB_CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(keys.data_ptr()) % 16 == 0,
             "memory_topk: 16-byte aligned operands");
   c10::cuda::CUDAGuard g(q.device());
+  bind_device(q.get_device());
   const int64_t qt = (T + TQ - 1) / TQ;
   if (splits <= 0) splits = std::max<int64_t>(1, num_sms() / std::max<int64_t>(qt, 1));
   int64_t per = (N + splits - 1) / splits;
@@ -340,6 +341,7 @@ std::tuple<at::Tensor, at::Tensor> topk_gather_fwd(const at::Tensor& s, const at
   LRB_CHECK(idx.scalar_type() == at::kInt && idx.is_contiguous() && values.is_contiguous() && values.size(1) % 256 == 0,
             "topk_gather_fwd: idx int32, values (N, Dv) with Dv % 256 == 0");
   c10::cuda::CUDAGuard g(s.device());
+  bind_device(s.get_device());
   const int T = (int)s.size(0), Dv = (int)values.size(1);
   auto out = at::empty({T, Dv}, values.options());
   auto w = at::empty({T, TOPK}, s.options());

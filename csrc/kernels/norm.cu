@@ -334,6 +334,7 @@ std::tuple<at::Tensor, at::Tensor, c10::optional<at::Tensor>> rmsnorm_fwd(
   const int d = (int)x.size(1);
   LRB_CHECK(w.numel() == d && w.is_contiguous(), "rmsnorm_fwd: weight size mismatch");
   c10::cuda::CUDAGuard g(x.device());
+  bind_device(x.get_device());
   auto y = at::empty({rows, d}, x.options().dtype(out_dtype));
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
   at::Tensor s;
@@ -364,6 +365,7 @@ std::tuple<at::Tensor, at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::T
   const int64_t rows = x.size(0);
   const int d = (int)x.size(1);
   c10::cuda::CUDAGuard g(x.device());
+  bind_device(x.get_device());
   auto dx = at::empty_like(x);
   auto dw = at::zeros({d}, x.options().dtype(at::kFloat));
   if (rows == 0) return {dx, dw};

@@ -27,6 +27,7 @@ void gemm_pair_axpby(const at::Tensor& A, const at::Tensor& B, bool b_mn, at::Te
 at::Tensor newton_schulz(const at::Tensor& X0, int64_t steps, double a, double b, double c) {
   LRB_CHECK(X0.is_cuda() && X0.dim() == 3 && X0.size(1) <= X0.size(2), "newton_schulz: (B, m, n) with m <= n");
   c10::cuda::CUDAGuard g(X0.device());
+  bind_device(X0.get_device());
   const int64_t Bt = X0.size(0), m = X0.size(1), n = X0.size(2);
   const bool native_ok = X0.scalar_type() == at::kBFloat16 && m % 8 == 0 && n % 8 == 0;
   if (!native_ok) {  // fp16 / fp32 or rows that TMA cannot address: library batched GEMMs

@@ -139,16 +139,6 @@ __global__ void nvfp4_quant_kernel(const T* __restrict__ x, const float* __restr
 }
 
 
-__device__ __forceinline__ int e2m1_sr_fast(float a, float r) {
-  const int lo = (a >= 0.5f) + (a >= 1.f) + (a >= 1.5f) + (a >= 2.f) + (a >= 3.f) + (a >= 4.f) + (a >= 6.f);
-  if (lo == 7) return 7;
-  const float g = lo < 4 ? 0.5f * lo : (lo == 4 ? 2.f : (lo == 5 ? 3.f : 4.f));
-  const float w = lo < 4 ? 2.f : (lo < 6 ? 1.f : 0.5f);  // 1 / grid spacing
-  return r < (a - g) * w ? lo + 1 : lo;
-}
-
-// One 16-element NVFP4 block: e4m3 scale byte and 8 packed bytes (low nibble first).
-// ridx(i) gives the element index that seeds stochastic rounding.
 // Two fp32 values -> one byte of E2M1 codes (lo in the low nibble), round to
 // nearest even with saturation to +-6: the hardware conversion, which rounds
 // as e2m1_rne does (ties to the even code; the one-thread-per-block quantiser
@@ -192,21 +182,20 @@ __device__ __forceinline__ void quant_block16(const float* v, float st, uint32_t
     for (int i = 0; i < 16; i += 2) w[i >> 3] |= cvt_e2m1x2(v[i] * inv, v[i + 1] * inv) << (4 * (i & 7));
     packed = make_uint2(clear_negative_zero(w[0]), clear_negative_zero(w[1]));
   } else {
-    // one 32-bit draw per element pair: 16 random bits per element
+    // the hardware stochastic-rounding conversion, four values per instruction
+    // (cvt.rs: the random bits come from one 32-bit draw per group of four; the
+    // first operand lands in the highest nibble, as in cvt.rn ... e2m1x2)
     const uint32_t key = mix32(seed ^ mix32(hi + 0x9e3779b9u));
 #pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      const uint32_t h = mix32(key ^ ((idx0 + (uint32_t)i) >> 1));
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float y = v[i + j] * inv;
-        const float r = (float)((h >> (16 * j)) & 0xFFFFu) * (1.f / 65536.f);
-        int code = e2m1_sr_fast(fabsf(y), r);
-        if (y < 0.f && code > 0) code |= 8;
-        w[(i + j) >> 3] |= (uint32_t)code << (4 * ((i + j) & 7));
-      }
+    for (int i = 0; i < 16; i += 4) {
+      const uint32_t rb = mix32(key ^ ((idx0 + (uint32_t)i) >> 2));
+      uint16_t d;
+      asm("cvt.rs.satfinite.e2m1x4.f32 %0, {%1, %2, %3, %4}, %5;"
+          : "=h"(d)
+          : "f"(v[i + 3] * inv), "f"(v[i + 2] * inv), "f"(v[i + 1] * inv), "f"(v[i] * inv), "r"(rb));
+      w[i >> 3] |= (uint32_t)d << (4 * (i & 7));
     }
-    packed = make_uint2(w[0], w[1]);
+    packed = make_uint2(clear_negative_zero(w[0]), clear_negative_zero(w[1]));
   }
 }
 
@@ -294,6 +283,7 @@ __global__ void nvfp4_dequant_kernel(const uint8_t* __restrict__ packed, const _
 std::tuple<at::Tensor, at::Tensor> int4_quantize(const at::Tensor& x, int64_t G) {
   LRB_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "int4_quantize: 2-D contiguous CUDA input");
   c10::cuda::CUDAGuard g(x.device());
+  bind_device(x.get_device());
   const int64_t M = x.size(0);
   const int D = (int)x.size(1);
   const int ng = (int)((D + G - 1) / G);
@@ -310,6 +300,7 @@ std::tuple<at::Tensor, at::Tensor> int4_quantize(const at::Tensor& x, int64_t G)
 
 at::Tensor int4_dequantize(const at::Tensor& q, const at::Tensor& s, int64_t G) {
   c10::cuda::CUDAGuard g(q.device());
+  bind_device(q.get_device());
   const int64_t M = q.size(0);
   const int D = (int)q.size(1);
   auto out = at::empty({M, D}, q.options().dtype(at::kFloat));
@@ -325,6 +316,7 @@ at::Tensor int4_dequantize(const at::Tensor& q, const at::Tensor& s, int64_t G) 
 std::tuple<at::Tensor, at::Tensor, at::Tensor> nvfp4_quantize(const at::Tensor& x, bool stochastic, int64_t seed) {
   LRB_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous() && x.size(1) % 16 == 0, "nvfp4_quantize: (M, K%16==0)");
   c10::cuda::CUDAGuard g(x.device());
+  bind_device(x.get_device());
   const int64_t M = x.size(0), K = x.size(1);
   auto packed = at::empty({M, K / 2}, x.options().dtype(at::kByte));
   auto sb = at::empty({M, K / 16}, x.options().dtype(at::kFloat8_e4m3fn));
@@ -354,6 +346,7 @@ std::vector<at::Tensor> nvfp4_quantize_dual(const at::Tensor& x, const c10::opti
   LRB_CHECK(M % 128 == 0 && K % 128 == 0, "nvfp4_quantize_dual: M and K multiples of 128");
   LRB_CHECK(rowwise || colwise, "nvfp4_quantize_dual: nothing requested");
   c10::cuda::CUDAGuard g(x.device());
+  bind_device(x.get_device());
   auto u8 = x.options().dtype(at::kByte);
   at::Tensor pr, ar, pc, ac;
   if (rowwise) {
@@ -408,6 +401,7 @@ std::vector<at::Tensor> nvfp4_quantize_dual(const at::Tensor& x, const c10::opti
 at::Tensor nvfp4_dequantize(const at::Tensor& packed, const at::Tensor& sb, const at::Tensor& st,
                             at::ScalarType dtype) {
   c10::cuda::CUDAGuard g(packed.device());
+  bind_device(packed.get_device());
   const int64_t M = packed.size(0), K = packed.size(1) * 2;
   auto out = at::empty({M, K}, packed.options().dtype(dtype));
   const int64_t n = M * K;

@@ -165,6 +165,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> route_slots(const at:
   const int64_t A = idx.numel();
   LRB_CHECK(A < (1LL << 31), "route_slots: too many assignments");
   c10::cuda::CUDAGuard g(idx.device());
+  bind_device(idx.get_device());
   auto i32 = idx.options().dtype(at::kInt);
   auto dest = at::empty({A}, i32), le = at::empty({A}, i32), slot = at::empty({A}, i32);
   auto counts = at::zeros({num_experts}, i32);
@@ -185,6 +186,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> softmax_topk_fwd(const at::Tensor
   const int E = (int)logits.size(1);
   LRB_CHECK(k >= 1 && k <= 8 && k <= E, "softmax_topk supports 1 <= k <= min(8, E)");
   c10::cuda::CUDAGuard g(logits.device());
+  bind_device(logits.get_device());
   auto f32 = logits.options().dtype(at::kFloat);
   auto w = at::empty({N, k}, f32);
   auto idx = at::empty({N, k}, logits.options().dtype(at::kLong));
@@ -203,6 +205,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> softmax_topk_fwd(const at::Tensor
 at::Tensor chunk_mean_pool_fwd(const at::Tensor& x, int64_t c) {
   LRB_CHECK(x.is_cuda() && x.dim() == 3 && x.is_contiguous() && x.size(1) % c == 0, "chunk_mean_pool: bad input");
   c10::cuda::CUDAGuard g(x.device());
+  bind_device(x.get_device());
   const int64_t B = x.size(0), S = x.size(1), D = x.size(2);
   auto out = at::empty({B, S / c, D}, x.options());
   const int64_t n = B * (S / c) * D;
@@ -222,6 +225,7 @@ std::tuple<at::Tensor, at::Tensor> compact_chunks(const at::Tensor& mask) {
   LRB_CHECK(mask.is_cuda() && mask.scalar_type() == at::kBool && mask.dim() == 2 && mask.is_contiguous(),
             "compact_chunks: bool (B, C) mask");
   c10::cuda::CUDAGuard g(mask.device());
+  bind_device(mask.get_device());
   const int64_t B = mask.size(0), C = mask.size(1);
   auto ids = at::full({B, C}, C, mask.options().dtype(at::kLong));
   auto counts = at::zeros({B}, mask.options().dtype(at::kLong));

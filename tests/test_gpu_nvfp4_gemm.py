@@ -132,3 +132,31 @@ def test_nvfp4_quantize_dual_stochastic_is_unbiased():
     for acc in (acc_r, acc_c):
         bias = ((acc / n - ref).norm() / ref.norm()).item()
         assert bias < 0.035, bias
+
+
+@pytest.mark.gpu
+def test_nvfp4_stochastic_rounding_picks_a_neighbour_with_the_right_odds():
+    """Stochastic rounding onto the E2M1 grid: values with known neighbours
+    (one 16-element block with amax 6 so the block scale is 1) round only to
+    those two grid points, with the probability of the upper one equal to the
+    distance from the lower one over the spacing; element order in the packed
+    bytes checked through the grid points themselves."""
+    from llm_research_b200.ops.quant import nvfp4_quantize_dual
+
+    base = torch.tensor([6.0, 0.3, -0.3, 1.25, 2.5, 3.5, 5.0, -4.5, 0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, -6.0])
+    x = base.repeat(128, 8).to("cuda").to(torch.bfloat16)  # (128, 128): every block holds the 16 values
+    lo = torch.tensor([6.0, 0.0, -0.5, 1.0, 2.0, 3.0, 4.0, -6.0, 0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, -6.0])
+    hi = torch.tensor([6.0, 0.5, 0.0, 1.5, 3.0, 4.0, 6.0, -4.0, 0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, -6.0])
+    ups = torch.zeros(16)
+    n = 32
+    for i in range(n):
+        row, _, _ = nvfp4_quantize_dual(x, stochastic=True, seed=7 + i)
+        q = row.dequantize().float().cpu().view(128, 8, 16)  # block scale x tensor scale = 1 up to rounding
+        is_lo = torch.isclose(q, lo.expand_as(q), rtol=1e-5, atol=1e-6)
+        is_hi = torch.isclose(q, hi.expand_as(q), rtol=1e-5, atol=1e-6)
+        ok = is_lo | is_hi
+        assert bool(ok.all()), q[~ok][:8]
+        ups += is_hi.float().mean(dim=(0, 1))
+    p_up = ups / n
+    want = torch.where(hi != lo, (base - lo) / (hi - lo), torch.ones(16))
+    assert torch.allclose(p_up, want, atol=0.03), (p_up, want)
