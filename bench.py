@@ -154,7 +154,7 @@ def parse_args(argv=None):
     ap.add_argument("--preset", default="genesis-1b")
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--per-gpu-seqs", type=int, default=32)
-    ap.add_argument("--micro-batch", type=int, default=8)
+    ap.add_argument("--micro-batch", type=int, default=16)
     ap.add_argument("--ref-micro-batch", type=int, default=0,
                     help="reference micro-batch; 0 = 2 (the largest that fits its fp32 O(S^2) attention on one "
                          "B200 at seq 4096), then 1 if that runs out of memory on one GPU")
