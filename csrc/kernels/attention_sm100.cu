@@ -534,18 +534,24 @@ __global__ void __launch_bounds__(fwd2::kThreads, 1)
         tmem_ld_32x32b_x32(tS, reinterpret_cast<uint32_t*>(t));
         tmem_ld_32x32b_x32(tS + 32, reinterpret_cast<uint32_t*>(t + 32));
         tmem_ld_wait();
+        if (edge) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) pm[i & 7] = fmaxf(pm[i & 7], masked(t[i], j * TK + i));
+          for (int i = 0; i < 64; ++i) pm[i & 7] = fmaxf(pm[i & 7], masked(t[i], j * TK + i));
+        } else {  // interior tile: no masks
+#pragma unroll
+          for (int i = 0; i < 64; ++i) pm[i & 7] = fmaxf(pm[i & 7], t[i]);
+        }
       }
       float hi[64];
       tmem_ld_32x32b_x32(tS + 64, reinterpret_cast<uint32_t*>(hi));
       tmem_ld_32x32b_x32(tS + 96, reinterpret_cast<uint32_t*>(hi + 32));
       tmem_ld_wait();
+      if (edge) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        hi[i] = masked(hi[i], j * TK + 64 + i);
-        pm[i & 7] = fmaxf(pm[i & 7], hi[i]);
+        for (int i = 0; i < 64; ++i) hi[i] = masked(hi[i], j * TK + 64 + i);
       }
+#pragma unroll
+      for (int i = 0; i < 64; ++i) pm[i & 7] = fmaxf(pm[i & 7], hi[i]);
       const float mraw = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                                fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       const float mx = mraw * c;  // c > 0: the max of the scaled scores
@@ -556,39 +562,41 @@ __global__ void __launch_bounds__(fwd2::kThreads, 1)
         m_run = m_new;
       }
       const float nm = (m_run == -INFINITY) ? 0.f : -m_run;
-      float ps[8];
+      // exponentials on packed pairs: one f32x2 FMA per two scores, four f32x2
+      // partial sums (8 accumulators as before)
+      const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(nm, nm);
+      uint64_t ps2[4];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ps[e] = 0.f;
+      for (int e = 0; e < 4; ++e) ps2[e] = f2_pack(0.f, 0.f);
+      auto exp_pair = [&](float s0, float s1, uint32_t& packed, int i) {
+        const float2 y = f2_unpack(f2_fma(f2_pack(s0, s1), c2, nm2));
+        const float p0 = fast_exp2(y.x), p1 = fast_exp2(y.y);
+        ps2[i & 3] = f2_add(ps2[i & 3], f2_pack(p0, p1));
+        packed = pack_bf16(p0, p1);
+      };
 #pragma unroll 1
       for (int cc = 0; cc < 2; ++cc) {  // keys 0..63, re-read
         float lo[32];
         tmem_ld_32x32b_x32(tS + cc * 32, reinterpret_cast<uint32_t*>(lo));
         tmem_ld_wait();
+        if (edge) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) lo[i] = masked(lo[i], j * TK + cc * 32 + i);
+        }
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = fast_exp2(fmaf(masked(lo[2 * i], j * TK + cc * 32 + 2 * i), c, nm));
-          const float p1 = fast_exp2(fmaf(masked(lo[2 * i + 1], j * TK + cc * 32 + 2 * i + 1), c, nm));
-          ps[(2 * i) & 7] += p0;
-          ps[(2 * i + 1) & 7] += p1;
-          pk[i] = pack_bf16(p0, p1);
-        }
+        for (int i = 0; i < 16; ++i) exp_pair(lo[2 * i], lo[2 * i + 1], pk[i], i);
         tmem_st_32x32b_x16(tS + cc * 16, pk);
       }
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {  // keys 64..127, from registers
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = fast_exp2(fmaf(hi[cc * 32 + 2 * i], c, nm));
-          const float p1 = fast_exp2(fmaf(hi[cc * 32 + 2 * i + 1], c, nm));
-          ps[(2 * i) & 7] += p0;
-          ps[(2 * i + 1) & 7] += p1;
-          pk[i] = pack_bf16(p0, p1);
-        }
+        for (int i = 0; i < 16; ++i) exp_pair(hi[cc * 32 + 2 * i], hi[cc * 32 + 2 * i + 1], pk[i], i);
         tmem_st_32x32b_x16(tS + 32 + cc * 16, pk);
       }
-      const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      const float2 s01 = f2_unpack(f2_add(ps2[0], ps2[1])), s23 = f2_unpack(f2_add(ps2[2], ps2[3]));
+      const float sum = (s01.x + s01.y) + (s23.x + s23.y);
       l_run = l_run * alpha + sum;
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
