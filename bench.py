@@ -369,7 +369,7 @@ def run_ours(args) -> dict:
             "l2": "inputs+activations >> 126 MB L2; no flush",
             "model_tflops_per_gpu": flops * value / world / 1e12,
             "exposed_comm_ms_per_step": exposed,
-            "comm": getattr(trainer.model, "comm", "none"),
+            "comm": (getattr(trainer.model, "comm", "none") if dp_world > 1 else "none (one rank)"),
             "final_loss": final_loss,
         },
         "clocks": sampler.summary(),

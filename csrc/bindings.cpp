@@ -100,6 +100,18 @@ void diloco_push(const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_
                  int64_t, at::Tensor&, at::Tensor&);
 void diloco_reduce_nesterov(const at::Tensor&, at::Tensor&, at::Tensor&, at::Tensor&, int64_t, double, double,
                             const at::Tensor&, at::Tensor&, at::Tensor&, int64_t, at::Tensor&, at::Tensor&);
+// comm/nvls.cu
+void nvls_all_reduce(at::Tensor&, int64_t, const at::Tensor&, int64_t, int64_t, int64_t, int64_t, double, at::Tensor&,
+                     at::Tensor&);
+void nvls_rs_stage(at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int64_t,
+                   at::Tensor&, at::Tensor&);
+void nvls_rs_reduce(int64_t, at::Tensor&, double, bool, const at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t,
+                    int64_t, c10::optional<at::Tensor>, at::Tensor&, at::Tensor&);
+void nvls_ag_publish(const at::Tensor&, int64_t, const at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t,
+                     int64_t, int64_t, at::Tensor&, at::Tensor&);
+void nvls_wait(const at::Tensor&, int64_t, int64_t, at::Tensor&);
+void nvls_diloco_outer(at::Tensor&, int64_t, const at::Tensor&, int64_t, const at::Tensor&, at::Tensor&, int64_t, int64_t,
+                       int64_t, double, double, bool, at::Tensor&, at::Tensor&);
 // comm/ep.cu
 void ep_push(const at::Tensor&, const c10::optional<at::Tensor>&, bool, const at::Tensor&, int64_t, int64_t, int64_t,
              int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, const at::Tensor&, const at::Tensor&,
@@ -195,4 +207,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_a2av_pull", &lrb::p2p_a2av_pull, "all-to-all-v by P2P loads from the peers' symmetric heaps");
   m.def("diloco_push", &lrb::diloco_push);
   m.def("diloco_reduce_nesterov", &lrb::diloco_reduce_nesterov);
+  m.def("nvls_all_reduce", &lrb::nvls_all_reduce, "in-place all-reduce through NVSwitch multicast (multimem)");
+  m.def("nvls_rs_stage", &lrb::nvls_rs_stage);
+  m.def("nvls_rs_reduce", &lrb::nvls_rs_reduce);
+  m.def("nvls_ag_publish", &lrb::nvls_ag_publish);
+  m.def("nvls_wait", &lrb::nvls_wait);
+  m.def("nvls_diloco_outer", &lrb::nvls_diloco_outer);
 }

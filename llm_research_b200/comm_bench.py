@@ -15,6 +15,12 @@ Cases (M = tokens over all ranks, sequence-sharded; N x K weights):
   ep_dispatch  MoE dispatch (P2P stores into the owners' expert slots) vs NCCL all_to_all
   ep_combine   MoE combine (P2P loads fused with the top-k weighted sum) vs NCCL all_to_all + gather
                (``--ep-tokens`` per rank x d 4096, top-2 of 16 experts, random-normal router logits)
+  nvls_rs      FSDP reduce-scatter through NVSwitch multicast (bf16 staging, multimem.ld_reduce
+               summing in the switch, fused scale/norm) vs NCCL (fp32)
+  nvls_ag      once-per-step parameter broadcast (fp32 master shard -> bf16 multimem.st into every
+               rank's gathered buffer) vs NCCL all_gather of the bf16 shards
+  nvls_ar      in-place fp32 all-reduce (multimem.ld_reduce of one slice per rank, multimem.st of
+               the sum) vs NCCL all_reduce, ``--ar-elements`` per rank
   diloco_outer DiLoCo outer step over all ranks as replicas (fused pseudo-gradient exchange +
                Nesterov on symmetric memory) vs the all-reduce path, ``--diloco-elements`` fp32
                per rank
@@ -64,6 +70,8 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--ep-tokens", type=int, nargs="*", default=[1024, 8192, 65536])
+    ap.add_argument("--nvls", type=int, default=1, help="run the NVSwitch multicast cases (0: skip)")
+    ap.add_argument("--ar-elements", type=int, nargs="*", default=[16 * 1024 * 1024, 128 * 1024 * 1024])
     ap.add_argument("--diloco-elements", type=int, default=0,
                     help="per-rank fp32 elements of the DiLoCo outer-step case (0: skip)")
     args = ap.parse_args(argv)
@@ -159,12 +167,80 @@ def main(argv=None) -> None:
                           "frac_of_roofline": round(roof / ms, 3)}), flush=True)
     heap.check()
     heap.close()
+    if args.nvls:
+        _nvls_cases(args, rank, world, dev, n)
     if args.ep_tokens:
         _ep_cases(args, rank, world, dev)
     if args.diloco_elements:
         _diloco_case(args, rank, world, dev)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def _nvls_cases(args, rank: int, world: int, dev, n: int) -> None:
+    """The multicast (NVLS) collectives against NCCL; skipped without multicast."""
+    from llm_research_b200._ext import native
+    from llm_research_b200.parallel.nvls import MulticastHeap, NVLSAllReduce, NVLSUnavailable
+
+    C = native()
+    shard = n // world
+    try:
+        heap = MulticastHeap(2 * n * 2 + 4 * sum(args.ar_elements or [0]) + (1 << 22), device=dev)
+    except NVLSUnavailable as e:
+        if rank == 0:
+            print(json.dumps({"case": "nvls", "gpus": world, "skipped": str(e)}), flush=True)
+        return
+    stage_off, ag_off, flag_off = heap.alloc(n * 2), heap.alloc(n * 2), heap.alloc(16 * world)
+    stage = heap.view(stage_off, (n,), torch.bfloat16)
+    flags = heap.view(flag_off, (4 * world,), torch.int32)
+    ready, consumed, agfree, agready = (flags[i * world:(i + 1) * world] for i in range(4))
+    counters = torch.zeros(4, dtype=torch.int32, device=dev)
+    g = torch.randn(n, device=dev)
+    dst = torch.empty(shard, device=dev)
+    sumsq = torch.zeros((), device=dev)
+    master = torch.randn(shard, device=dev)
+    full = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    master_bf = master.to(torch.bfloat16)
+    st = {"rs": 0, "ag": 0}
+
+    def rs():
+        st["rs"] += 1
+        C.nvls_rs_stage(g, stage, consumed, heap.bases, flag_off, rank, world, st["rs"], counters[0:1], heap.err)
+        C.nvls_rs_reduce(heap.mc(stage_off), dst, 1.0 / world, False, ready, heap.bases, flag_off + 4 * world, rank,
+                         world, st["rs"], sumsq, counters[1:2], heap.err)
+
+    def ag():
+        st["ag"] += 1
+        C.nvls_ag_publish(master, heap.mc(ag_off), agfree, heap.bases, flag_off + 8 * world, flag_off + 12 * world,
+                          rank, world, st["ag"], counters[2:3], heap.err)
+        C.nvls_wait(agready, world, st["ag"], heap.err)
+
+    ms_rs = _time(rs, args.warmup, args.iters, dev)
+    base_rs = _time(lambda: dist.reduce_scatter_tensor(dst, g, op=dist.ReduceOp.AVG), args.warmup, args.iters, dev)
+    ms_ag = _time(ag, args.warmup, args.iters, dev)
+    base_ag = _time(lambda: dist.all_gather_into_tensor(full, master_bf), args.warmup, args.iters, dev)
+    if rank == 0:
+        roof = (world - 1) * shard * 2 / (NVLINK_GBS * 1e9) * 1e3  # bf16 bytes that must reach / leave each GPU
+        for case, ms, base, what in (("nvls_rs", ms_rs, base_rs, "nccl_fp32_ms"),
+                                     ("nvls_ag", ms_ag, base_ag, "nccl_bf16_ms")):
+            print(json.dumps({"case": case, "gpus": world, "elements": n, "ms": round(ms, 4), what: round(base, 4),
+                              "speedup_vs_nccl": round(base / ms, 3), "roofline_ms": round(roof, 4),
+                              "frac_of_roofline": round(roof / ms, 3)}), flush=True)
+    for m in args.ar_elements:
+        ar = NVLSAllReduce(m, heap=heap)
+        ar.tensor().normal_()
+        x = torch.randn(m, device=dev)
+        ms = _time(ar.run, args.warmup, args.iters, dev)
+        base = _time(lambda: dist.all_reduce(x), args.warmup, args.iters, dev)
+        if rank == 0:
+            # each GPU's data leaves once and the sum arrives once (bytes per direction)
+            roof = m * 4 * (world - 1) / world / (NVLINK_GBS * 1e9) * 1e3
+            print(json.dumps({"case": "nvls_ar", "gpus": world, "elements": m, "ms": round(ms, 4),
+                              "nccl_ms": round(base, 4), "speedup_vs_nccl": round(base / ms, 3),
+                              "busbw_gbs": round(2 * (world - 1) / world * m * 4 / ms / 1e6, 1),
+                              "roofline_ms": round(roof, 4), "frac_of_roofline": round(roof / ms, 3)}), flush=True)
+    heap.check()
+    heap.close()
 
 
 def _ep_cases(args, rank: int, world: int, dev) -> None:
@@ -224,10 +300,11 @@ def _diloco_case(args, rank: int, world: int, dev) -> None:
     n = args.diloco_elements
     shard = torch.randn(n, device=dev)
     times = {}
-    for comm in ("p2p", "collective"):
+    for comm in ("p2p", "nvls", "collective"):
         dl = DiLoCo([shard], dist.group.WORLD, list(range(world)),
                     DiLoCoConfig(comm=comm, fault_tolerance=False), tag=f"bench-{comm}")
-        times[comm] = _time(dl.outer_step, args.warmup, args.iters, dev)
+        if dl.comm == comm:
+            times[comm] = _time(dl.outer_step, args.warmup, args.iters, dev)
         dl.close()
     if rank == 0:
         # each rank sends (world-1)/world of its fp32 pseudo-gradient and receives the same of the anchor
@@ -238,6 +315,12 @@ def _diloco_case(args, rank: int, world: int, dev) -> None:
                           "speedup_vs_nccl": round(times["collective"] / times["p2p"], 3),
                           "roofline_ms": round(roof, 4), "frac_of_roofline": round(roof / times["p2p"], 3)}),
               flush=True)
+        if "nvls" in times:
+            print(json.dumps({"case": "diloco_outer_nvls", "gpus": world, "elements_per_rank": n,
+                              "ms": round(times["nvls"], 4), "collective_ms": round(times["collective"], 4),
+                              "speedup_vs_nccl": round(times["collective"] / times["nvls"], 3),
+                              "roofline_ms": round(roof, 4), "frac_of_roofline": round(roof / times["nvls"], 3)}),
+                  flush=True)
 
 
 if __name__ == "__main__":

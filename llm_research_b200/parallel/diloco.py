@@ -57,7 +57,7 @@ class DiLoCoConfig:
     quantize_bits: int = 0          # 0: exact fp32 exchange; 4: int4 absmax (group 128) pseudo-gradients
     fault_tolerance: bool = True
     max_island_failures: int = 2
-    comm: str = "auto"              # auto | p2p | collective
+    comm: str = "auto"              # auto | p2p | nvls | collective
 
 
 def make_diloco_groups(num_replicas: int) -> Tuple[Optional[dist.ProcessGroup], dist.ProcessGroup, List[int], int]:
@@ -112,17 +112,30 @@ class DiLoCo:
         if comm == "auto":
             comm = "p2p" if self._p2p_possible() else "collective"
         self.comm = comm
+        if self.comm == "nvls":
+            from llm_research_b200.parallel.nvls import NVLSUnavailable
+            from llm_research_b200.parallel.symm import single_node
+
+            try:
+                if not (self.device.type == "cuda" and len(self.members) > 1 and self.cfg.quantize_bits == 0
+                        and isinstance(self.group, dist.ProcessGroup) and single_node(self.group)):
+                    raise NVLSUnavailable("the replica group is not a single-node process group")
+                self._setup_nvls()
+            except NVLSUnavailable:
+                self.comm = "p2p" if self._p2p_possible() else "collective"
         if self.comm == "p2p":
             self._setup_p2p()
-        else:
+        elif self.comm != "nvls":
             self.momentum = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
 
     # ------------------------------------------------------------- plumbing
     def _p2p_possible(self) -> bool:
         from llm_research_b200.parallel.symm import single_node
 
+        # The fused P2P kernel implements the Nesterov form only; heavy-ball
+        # momentum (nesterov=False) takes the NVLS or collective path.
         return (self.device.type == "cuda" and len(self.members) > 1 and self.cfg.quantize_bits == 0
-                and single_node(self.group))
+                and self.cfg.nesterov and single_node(self.group))
 
     def _setup_p2p(self) -> None:
         from llm_research_b200.parallel.symm import SymmetricHeap
@@ -143,6 +156,16 @@ class DiLoCo:
         self.counters = torch.zeros(4, dtype=torch.int32, device=self.device)
         self.my = self.members.index(self.rank)
         self.momentum = torch.zeros(shard, dtype=torch.float32, device=self.device)
+
+    def _setup_nvls(self) -> None:
+        from llm_research_b200.parallel.nvls import NVLSAllReduce
+
+        R = len(self.members)
+        self.nvls = NVLSAllReduce(self.padded, dtype=torch.float32, group=self.group, device=self.device)
+        self.my = self.members.index(self.rank)
+        per = -(-(self.padded // 4) // R)  # 16-byte vectors in this rank's slice
+        self.momentum = torch.zeros(per * 4, dtype=torch.float32, device=self.device)
+        self.heap = self.nvls.heap
 
     def _flatten(self) -> None:
         o = 0
@@ -177,7 +200,9 @@ class DiLoCo:
         elif self.cfg.fault_tolerance and self.monitor is not None:
             joiners = self._update_roster()
         self._epoch += 1
-        if self.comm == "p2p" and self.members == self.initial and not joiners:
+        if self.comm == "nvls" and self.members == self.initial and not joiners:
+            self._outer_nvls()
+        elif self.comm == "p2p" and self.members == self.initial and not joiners:
             self._outer_p2p()
         else:
             self._outer_collective(len(self.members) - len(joiners))
@@ -199,6 +224,21 @@ class DiLoCo:
                                  self.outready, self._epoch, self.counters[1:2], self.heap.err)
         C.p2p_pull(self.anchor, self.heap.bases, self.out_off, self.outready_off, R, self._epoch, self.heap.err)
         self.heap.poll_error()
+
+    def _outer_nvls(self) -> None:
+        """Pseudo-gradients summed in the switch, the momentum step on this rank's
+        slice and the new anchor multicast back: one kernel (``nvls_diloco_outer``)."""
+        from llm_research_b200._ext import native
+
+        ar = self.nvls
+        buf = ar.tensor()
+        torch.sub(self.anchor, self.local, out=buf)
+        ar.epoch += 1
+        native().nvls_diloco_outer(ar.buffer, ar.heap.mc(ar.data_off), ar.heap.bases, ar.flag_off, self.anchor,
+                                   self.momentum, ar.rank, ar.world, ar.epoch, self.cfg.outer_lr,
+                                   self.cfg.outer_momentum, self.cfg.nesterov, ar.counter, ar.heap.err)
+        self.anchor.copy_(buf)
+        ar.heap.poll_error()
 
     def _outer_collective(self, contributors: int) -> None:
         R = len(self.members)

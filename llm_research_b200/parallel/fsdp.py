@@ -40,6 +40,22 @@ framework's own kernels on symmetric memory (:mod:`llm_research_b200.parallel.sy
 * all-gather = ``p2p_ag_publish`` (the optimizer's fp32 master shard is cast
   to bf16 straight into the heap) + ``p2p_pull`` (each rank reads all shards).
 
+``comm="nvls"`` (one node with NVSwitch multicast) runs the kernels of
+:mod:`llm_research_b200.parallel.nvls` on a multicast heap:
+
+* reduce-scatter = ``nvls_rs_stage`` (the fp32 accumulator is cast to bf16
+  into this rank's copy of a staging buffer and zeroed) + ``nvls_rs_reduce``
+  (the owner reads its shard with ``multimem.ld_reduce``: the switch sums the
+  ranks' copies in fp32; then scale, store and sum of squares as above);
+* all-gather = ``nvls_ag_publish`` once per optimizer step, on the
+  communication stream: every rank casts its master shard to bf16 and
+  ``multimem.st`` writes it into its slot of every rank's gathered-parameter
+  buffer, so the bf16 parameters stay resident and each gather reduces to one
+  flag wait per unit and step.  Memory per rank: 2 bytes per parameter for the
+  gathered copy plus 2 for the staging buffer (sharded fp32 master, gradient
+  shard and optimizer state as in the other modes).  The publish first
+  exchanges "released" flags so no rank overwrites weights a peer still reads.
+
 Ordering argument for reusing the heap shard: a rank republishes a unit's
 shard only after its reduce of that unit, which waited for every peer's push
 of the unit, and each peer pushes only after its backward of the unit, which
@@ -189,6 +205,17 @@ class FlatShardEngine(nn.Module):
             self.comm = "p2p" if self.world <= 4 else "nccl"
         self.heap = None
         self._sumsq: Optional[torch.Tensor] = None
+        if self.comm == "nvls":
+            from llm_research_b200.parallel.nvls import NVLSUnavailable
+            from llm_research_b200.parallel.symm import single_node
+
+            if not (self.world > 1 and self.device.type == "cuda" and single_node(self.pg)):
+                self.comm = "nccl"
+            else:
+                try:
+                    self._setup_nvls()
+                except NVLSUnavailable:
+                    self.comm = "p2p"
         if self.comm == "p2p":
             from llm_research_b200.parallel.symm import single_node
 
@@ -312,10 +339,51 @@ class FlatShardEngine(nn.Module):
         dist.barrier(group=self.pg)  # every heap is zeroed before anyone publishes
         self._publish()
 
+    def _setup_nvls(self) -> None:
+        from llm_research_b200.parallel.nvls import MulticastHeap
+
+        W = self.world
+        need = sum(2 * _round_up(u.total * 2, 256) + _round_up(16 * W, 256) for u in self.units)
+        self.heap = heap = MulticastHeap(need + (1 << 20), group=self.pg, device=self.device)
+        for u in self.units:
+            u.nv_ag_off = heap.alloc(u.total * 2)
+            u.nv_stage_off = heap.alloc(u.total * 2)
+            u.nv_flag_off = heap.alloc(16 * W)
+            u.nv_stage = heap.view(u.nv_stage_off, (u.total,), torch.bfloat16)
+            flags = heap.view(u.nv_flag_off, (4 * W,), torch.int32)
+            # ready[W] and consumed[W] of the reduce-scatter, released[W] and
+            # published[W] of the all-gather; peer r writes entry r.
+            u.nv_ready, u.nv_consumed, u.nv_agfree, u.nv_agready = (flags[i * W:(i + 1) * W] for i in range(4))
+            u.nv_seen = 0
+            # The gathered bf16 parameters live in the heap for good: the compute
+            # buffer, its writer alias and the weight views all point there.
+            u.compute = heap.view(u.nv_ag_off, (u.total,), self.compute_dtype)
+            u.writer = torch.empty(0, dtype=self.compute_dtype, device=self.device).set_(
+                u.compute.untyped_storage(), u.compute.storage_offset(), (u.total,), (1,))
+            for info in u.params:
+                u.views[info.name] = u.compute[info.offset: info.offset + info.numel].view(info.shape)
+            u.counters = torch.zeros(4, dtype=torch.int32, device=self.device)
+            u.rs_epoch = 0
+            u.gathered = False
+        self._sumsq = torch.zeros((), dtype=torch.float32, device=self.device)
+        self._ag_epoch = 0
+        self._publish()
+
     @nvtx_fn("lrb/fsdp/publish")
     def _publish(self) -> None:
         C = ops_native()
         self._ag_epoch += 1
+        if self.comm == "nvls":
+            # On the communication stream, after the optimizer step: the next
+            # forward's units wait for their own broadcast only (``_gather``), so
+            # the broadcast of later units overlaps the compute of earlier ones.
+            h, W = self.heap, self.world
+            self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.comm_stream):
+                for u in self.units:
+                    C.nvls_ag_publish(u.master, h.mc(u.nv_ag_off), u.nv_agfree, h.bases, u.nv_flag_off + 8 * W,
+                                      u.nv_flag_off + 12 * W, self.rank, W, self._ag_epoch, u.counters[2:3], h.err)
+            return
         for u in self.units:
             C.p2p_ag_publish(u.master, u.compute_shard, u.agready, self._ag_epoch, u.counters[2:3])
 
@@ -327,6 +395,8 @@ class FlatShardEngine(nn.Module):
 
     # --------------------------------------------------------------- gathers
     def _free(self, u: Unit) -> None:
+        if getattr(self, "comm", None) == "nvls":  # resident in the multicast heap
+            return
         if self.world > 1 and u.compute.untyped_storage().size() > 0:
             u.compute.untyped_storage().resize_(0)
         u.gathered = self.world == 1
@@ -341,6 +411,22 @@ class FlatShardEngine(nn.Module):
                 st.resize_(u.total * u.compute.element_size())
             dist.all_gather_into_tensor(u.writer, u.compute_shard, group=self.pg)
             u.gathered = True
+            return
+        if self.comm == "nvls":
+            # The publish after the optimizer step already broadcast the shards:
+            # wait (once per step) for every rank's flag of this unit.
+            if u.nv_seen != self._ag_epoch:
+                self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+                with torch.cuda.stream(self.comm_stream):
+                    ops_native().nvls_wait(u.nv_agready, self.world, self._ag_epoch, self.heap.err)
+                    ev = torch.cuda.Event()
+                    ev.record(self.comm_stream)
+                u.gather_event = ev
+                u.nv_seen = self._ag_epoch
+            u.gathered = True
+            if wait and u.gather_event is not None:
+                self._wait_comm(u.gather_event)
+                u.gather_event = None
             return
         if not u.gathered:
             st = u.compute.untyped_storage()
@@ -467,6 +553,19 @@ class FlatShardEngine(nn.Module):
             return
         cur = torch.cuda.current_stream(self.device)
         self.comm_stream.wait_stream(cur)
+        if self.comm == "nvls":
+            C, h, W = ops_native(), self.heap, self.world
+            u.rs_epoch += 1
+            with torch.cuda.stream(self.comm_stream):
+                C.nvls_rs_stage(u.grad_acc, u.nv_stage, u.nv_consumed, h.bases, u.nv_flag_off, self.rank, W,
+                                u.rs_epoch, u.counters[0:1], h.err)
+                C.nvls_rs_reduce(h.mc(u.nv_stage_off), u.grad_shard, 1.0 / W, False, u.nv_ready, h.bases,
+                                 u.nv_flag_off + 4 * W, self.rank, W, u.rs_epoch, self._sumsq, u.counters[1:2],
+                                 h.err)
+                ev = torch.cuda.Event()
+                ev.record(self.comm_stream)
+            u.rs_event = ev
+            return
         if self.heap is not None:
             C = ops_native()
             u.rs_epoch += 1
