@@ -94,6 +94,10 @@ void p2p_rs_push(at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int6
 void p2p_rs_reduce(const at::Tensor&, at::Tensor&, int64_t, double, bool, const at::Tensor&, at::Tensor&, int64_t,
                    c10::optional<at::Tensor>, at::Tensor&, at::Tensor&);
 void p2p_ag_publish(const at::Tensor&, at::Tensor&, at::Tensor&, int64_t, at::Tensor&);
+void p2p_rows_rs_push(const at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                      at::Tensor&, at::Tensor&);
+void p2p_rows_rs_reduce(const at::Tensor&, const c10::optional<at::Tensor>&, at::Tensor&, int64_t, const at::Tensor&,
+                        at::Tensor&, int64_t, at::Tensor&, at::Tensor&);
 void p2p_pull(at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int64_t, at::Tensor&);
 void p2p_a2av_pull(at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, at::Tensor&);
 void diloco_push(const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t, int64_t, int64_t, int64_t, int64_t,
@@ -203,6 +207,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_rs_push", &lrb::p2p_rs_push);
   m.def("p2p_rs_reduce", &lrb::p2p_rs_reduce);
   m.def("p2p_ag_publish", &lrb::p2p_ag_publish);
+  m.def("p2p_rows_rs_push", &lrb::p2p_rows_rs_push);
+  m.def("p2p_rows_rs_reduce", &lrb::p2p_rows_rs_reduce);
   m.def("p2p_pull", &lrb::p2p_pull);
   m.def("p2p_a2av_pull", &lrb::p2p_a2av_pull, "all-to-all-v by P2P loads from the peers' symmetric heaps");
   m.def("diloco_push", &lrb::diloco_push);

@@ -298,6 +298,48 @@ __global__ void diloco_reduce_nesterov_kernel(const float4* __restrict__ recv, f
   }
 }
 
+// ------------------------------------------------ bf16 row reduce-scatter
+// Tensor parallelism around GEMMs that are not fused with the collective (the
+// NVFP4 linears): the partial product (world*shard bf16, owner r holding the
+// rows [r*shard, (r+1)*shard) of the flat row-major buffer) is pushed into the
+// owners' slots, then each owner sums its world slots in fp32, adds an
+// optional residual and writes bf16.  Same flag protocol as rs_push / rs_reduce.
+__global__ void rows_rs_push_kernel(const uint4* __restrict__ src, int64_t s8, const uint64_t* __restrict__ bases,
+                                    int64_t recv_off, int64_t ready_off, int64_t consumed_off, int rank, int world,
+                                    uint32_t epoch, unsigned int* counter, int* err) {
+  const bool ok = block_wait_flags(bases, consumed_off, world, epoch - 1, err, kErrSlotWait);
+  const int64_t n8 = ok ? (int64_t)world * s8 : 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / s8);
+    const int64_t j = i - (int64_t)r * s8;
+    reinterpret_cast<uint4*>(bases[r] + recv_off)[(int64_t)rank * s8 + j] = src[i];
+  }
+  if (last_block_done(counter) && no_error(err)) {
+    __threadfence_system();
+    for (int r = 0; r < world; ++r)
+      st_release_sys(reinterpret_cast<uint32_t*>(bases[r] + ready_off) + rank, epoch);
+  }
+}
+
+__global__ void rows_rs_reduce_kernel(const uint4* __restrict__ recv, const uint4* __restrict__ residual,
+                                      uint4* __restrict__ out, int64_t s8, int world, const uint32_t* ready,
+                                      uint32_t* consumed, uint32_t epoch, unsigned int* counter, int* err) {
+  const bool ok = block_wait_local_flags(ready, world, epoch, err, kErrPeerWait);
+  const int64_t n = ok ? s8 : 0;
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (residual != nullptr) unpack8_bf16(residual[j], acc);
+    for (int p = 0; p < world; ++p) {
+      float f[8];
+      unpack8_bf16(recv[(int64_t)p * s8 + j], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += f[e];
+    }
+    out[j] = pack8_bf16(acc);
+  }
+  if (last_block_done(counter) && no_error(err)) st_release_sys(consumed, epoch);
+}
+
 inline int grid_for(int64_t work, int threads = 256) {
   const int64_t blocks = (work + threads - 1) / threads;
   return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)num_sms() * 4));
@@ -380,6 +422,39 @@ void p2p_rs_reduce(const at::Tensor& recv, at::Tensor& dst, int64_t world, doubl
       accumulate ? 1 : 0, reinterpret_cast<const uint32_t*>(ready.data_ptr<int>()),
       reinterpret_cast<uint32_t*>(consumed.data_ptr<int>()), (uint32_t)epoch,
       sumsq ? sumsq->data_ptr<float>() : nullptr, counter_ptr(counter), err.data_ptr<int>());
+  LRB_LAUNCH_CHECK();
+}
+
+// y (world*shard bf16 rows, row-major) -> owners' slots; see rows_rs_push_kernel.
+void p2p_rows_rs_push(const at::Tensor& y, const at::Tensor& bases, int64_t recv_off, int64_t ready_off,
+                      int64_t consumed_off, int64_t rank, int64_t world, int64_t epoch, at::Tensor& counter,
+                      at::Tensor& err) {
+  const int64_t n = y.numel();
+  LRB_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.is_contiguous() && n % (8 * world) == 0,
+            "p2p_rows_rs_push: y must be contiguous bf16 with numel a multiple of 8*world");
+  c10::cuda::CUDAGuard g(y.device());
+  rows_rs_push_kernel<<<grid_for(n / 8), 256, 0, stream()>>>(
+      reinterpret_cast<const uint4*>(y.data_ptr()), n / world / 8, dev_u64(bases), recv_off, ready_off, consumed_off,
+      (int)rank, (int)world, (uint32_t)epoch, counter_ptr(counter), err.data_ptr<int>());
+  LRB_LAUNCH_CHECK();
+}
+
+void p2p_rows_rs_reduce(const at::Tensor& recv, const c10::optional<at::Tensor>& residual, at::Tensor& out,
+                        int64_t world, const at::Tensor& ready, at::Tensor& consumed, int64_t epoch,
+                        at::Tensor& counter, at::Tensor& err) {
+  const int64_t shard = out.numel();
+  LRB_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.is_contiguous() && shard % 8 == 0,
+            "p2p_rows_rs_reduce: out must be contiguous bf16 with numel a multiple of 8");
+  LRB_CHECK(recv.scalar_type() == at::kBFloat16 && recv.numel() >= world * shard, "p2p_rows_rs_reduce: bad recv");
+  if (residual)
+    LRB_CHECK(residual->scalar_type() == at::kBFloat16 && residual->is_contiguous() && residual->numel() == shard,
+              "p2p_rows_rs_reduce: residual must match out");
+  c10::cuda::CUDAGuard g(out.device());
+  rows_rs_reduce_kernel<<<grid_for(shard / 8), 256, 0, stream()>>>(
+      reinterpret_cast<const uint4*>(recv.data_ptr()),
+      residual ? reinterpret_cast<const uint4*>(residual->data_ptr()) : nullptr, reinterpret_cast<uint4*>(out.data_ptr()),
+      shard / 8, (int)world, reinterpret_cast<const uint32_t*>(ready.data_ptr<int>()),
+      reinterpret_cast<uint32_t*>(consumed.data_ptr<int>()), (uint32_t)epoch, counter_ptr(counter), err.data_ptr<int>());
   LRB_LAUNCH_CHECK();
 }
 

@@ -23,8 +23,20 @@ its own ``ag_gemm(e-1)``, which waited for every peer's ``e-1`` publish, which
 each peer issued after finishing its ``ag_gemm(e-2)`` reads of that slot
 (one stream per rank).
 
-Without a heap (CPU, several nodes, or ``comm="nccl"``) the same layers run
-NCCL / gloo collectives around ``F.linear`` -- the baseline.
+Backward GEMMs: the weight gradients run on the CTA-pair kernel from the rows
+the fused forward gathered anyway (``ag_gemm`` keeps its gathered input), with
+direct fp32 accumulation into the sharding engine's gradient buffer, so no
+collective and no library GEMM runs for them.
+
+Under NVFP4 linear precision (or shapes the fused kernels do not take) a layer
+is ``project`` -- NVFP4 forward, dgrad and wgrad on the block-scaled kernel --
+composed with differentiable row all-gather / reduce-scatter functions that
+use this heap's P2P kernels (``shard_publish`` + ``p2p_pull``;
+``p2p_rows_rs_push`` + ``p2p_rows_rs_reduce`` with the residual added in the
+reduction).
+
+Without a heap (CPU, several nodes, or ``comm="nccl"``) the same composition
+runs NCCL / gloo collectives -- the baseline.
 """
 
 from __future__ import annotations
@@ -58,7 +70,7 @@ class TPComm:
         W = self.world
         # gemm_rs slots are tile-major with the width padded to whole 256-column tiles
         slot = (max_tokens // W) * (-(-max_width // 256) * 256) * 2
-        self.heap = h = SymmetricHeap(2 * W * slot + 2 * slot + 8192, group=group, device=device)
+        self.heap = h = SymmetricHeap(3 * W * slot + 2 * slot + 16384, group=group, device=device)
         # gemm_rs receive slots, two sets alternating by epoch parity (a call only waits
         # for the owners to have consumed the call before the previous one)
         self.recv_offs = [h.alloc(W * slot), h.alloc(W * slot)]
@@ -73,6 +85,17 @@ class TPComm:
         self.chunk_flags = torch.zeros(max_tokens // 128, dtype=torch.int32, device=device)
         self.rs_epoch = 0
         self.ag_epoch = 0
+        # row reduce-scatter outside the fused GEMMs: one receive region, released
+        # by each owner's consumed flag before the next push
+        self.rrs_recv_off = h.alloc(W * slot)
+        self.rrs_ready_off = h.alloc(4 * W)
+        self.rrs_consumed_off = h.alloc(4)
+        self.rrs_recv = h.view(self.rrs_recv_off, (W * slot // 2,), torch.bfloat16)
+        self.rrs_ready = h.view(self.rrs_ready_off, (W,), torch.int32)
+        self.rrs_consumed = h.view(self.rrs_consumed_off, (1,), torch.int32)
+        self.rrs_counters = torch.zeros(2, dtype=torch.int32, device=device)
+        self.rrs_epoch = 0
+        self._slot_bytes = slot
 
     @nvtx_fn("lrb/tp/gemm_rs")
     def gemm_rs(self, x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -90,24 +113,59 @@ class TPComm:
                     self.consumed, self.rs_epoch, self.counters[self.world:self.world + 1], self.heap.err)
         return out
 
-    @nvtx_fn("lrb/tp/ag_gemm")
-    def ag_gemm(self, x_shard: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        """``AllGather_rows(x_shard) @ w.T``: ``(T / world, K) x (N, K) -> (T, N)``."""
-        C = native()
+    def _publish(self, x_shard: torch.Tensor) -> int:
+        """Copy this rank's rows into the shard slot of the next gather epoch."""
         Tl, K = x_shard.shape
-        T = Tl * self.world
         self.ag_epoch += 1
         s = self.ag_epoch % 2
-        dst = self.heap.view(self.shard_off[s], (Tl, K), torch.bfloat16)
-        C.shard_publish(x_shard.contiguous(), dst, self.shard_ready[s], self.ag_epoch,
-                        self.counters[self.world + 1:self.world + 2])
-        a_full = torch.empty(T, K, dtype=x_shard.dtype, device=x_shard.device)
-        return C.ag_gemm(w, a_full, self.chunk_flags, self.heap.bases, self.shard_off[s], self.shard_ready_off[s],
-                         self.rank, self.world, self.ag_epoch, self.ncopy, self.heap.err)
+        dst = self.heap.view(self.shard_off[s], (Tl, K), x_shard.dtype)
+        native().shard_publish(x_shard.contiguous(), dst, self.shard_ready[s], self.ag_epoch,
+                               self.counters[self.world + 1:self.world + 2])
+        return s
+
+    @nvtx_fn("lrb/tp/ag_gemm")
+    def ag_gemm(self, x_shard: torch.Tensor, w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """``AllGather_rows(x_shard) @ w.T``: ``(T / world, K) x (N, K) -> (T, N)``,
+        and the gathered ``(T, K)`` rows (the weight gradient's operand)."""
+        Tl, K = x_shard.shape
+        s = self._publish(x_shard)
+        a_full = torch.empty(Tl * self.world, K, dtype=x_shard.dtype, device=x_shard.device)
+        y = native().ag_gemm(w, a_full, self.chunk_flags, self.heap.bases, self.shard_off[s], self.shard_ready_off[s],
+                             self.rank, self.world, self.ag_epoch, self.ncopy, self.heap.err)
+        return y, a_full
+
+    @nvtx_fn("lrb/tp/all_gather")
+    def all_gather(self, x_shard: torch.Tensor) -> torch.Tensor:
+        """Rows of every rank, P2P pulls from the peers' shard slots."""
+        Tl, K = x_shard.shape
+        s = self._publish(x_shard)
+        out = torch.empty(Tl * self.world, K, dtype=x_shard.dtype, device=x_shard.device)
+        native().p2p_pull(out, self.heap.bases, self.shard_off[s], self.shard_ready_off[s], self.world,
+                          self.ag_epoch, self.heap.err)
+        return out
+
+    @nvtx_fn("lrb/tp/reduce_scatter")
+    def reduce_scatter(self, y: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """This rank's rows of the sum over ranks of ``y`` (+ ``residual``)."""
+        C = native()
+        T, N = y.shape
+        self.rrs_epoch += 1
+        C.p2p_rows_rs_push(y.contiguous(), self.heap.bases, self.rrs_recv_off, self.rrs_ready_off,
+                           self.rrs_consumed_off, self.rank, self.world, self.rrs_epoch, self.rrs_counters[0:1],
+                           self.heap.err)
+        out = torch.empty(T // self.world, N, dtype=y.dtype, device=y.device)
+        C.p2p_rows_rs_reduce(self.rrs_recv, residual.contiguous() if residual is not None else None, out, self.world,
+                             self.rrs_ready, self.rrs_consumed, self.rrs_epoch, self.rrs_counters[1:2], self.heap.err)
+        return out
 
     def fits(self, tokens: int, width: int) -> bool:
         return (tokens <= self.max_tokens and width <= self.max_width and tokens % (128 * self.world) == 0
                 and width % 8 == 0)
+
+    def fits_rows(self, t: torch.Tensor, tokens: int) -> bool:
+        """``t`` (rows of a ``tokens``-row matrix) can use the P2P gather / reduce-scatter."""
+        return (t.is_cuda and t.dtype == torch.bfloat16 and t.dim() == 2 and tokens <= self.max_tokens
+                and t.shape[1] <= self.max_width and (tokens * t.shape[1]) % (8 * self.world) == 0)
 
     def close(self) -> None:
         self.heap.close()
@@ -142,55 +200,116 @@ def _fused_ok(comm: Optional[TPComm], x: torch.Tensor, tokens: int, widths) -> b
             and all(comm.fits(tokens, w) for w in widths))
 
 
+def _gather_rows(x_shard: torch.Tensor, comm: Optional[TPComm], group) -> torch.Tensor:
+    W = dist.get_world_size(group)
+    if comm is not None and comm.fits_rows(x_shard, x_shard.shape[0] * W):
+        return comm.all_gather(x_shard)
+    return _all_gather_rows(x_shard, group)
+
+
+def _scatter_rows(y: torch.Tensor, comm: Optional[TPComm], group,
+                  residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if comm is not None and comm.fits_rows(y, y.shape[0]):
+        return comm.reduce_scatter(y, residual)
+    out = _reduce_scatter_rows(y, group)
+    return out + residual if residual is not None else out
+
+
+class _AllGatherRows(torch.autograd.Function):
+    """Sequence shards -> all rows; backward reduce-scatters the gradient."""
+
+    @staticmethod
+    def forward(ctx, x_shard, comm, group):
+        ctx.comm, ctx.group = comm, group
+        return _gather_rows(x_shard, comm, group)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _scatter_rows(g.contiguous(), ctx.comm, ctx.group), None, None
+
+
+class _ReduceScatterRows(torch.autograd.Function):
+    """Partial products -> this rank's rows of their sum (+ residual); backward
+    all-gathers the gradient (the residual's gradient passes through)."""
+
+    @staticmethod
+    def forward(ctx, y, residual, comm, group):
+        ctx.comm, ctx.group, ctx.has_residual = comm, group, residual is not None
+        return _scatter_rows(y, comm, group, residual)
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous()
+        return _gather_rows(g, ctx.comm, ctx.group), (g if ctx.has_residual else None), None, None
+
+
+def _wgrad(dy: torch.Tensor, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``dy^T x`` on the pair kernel, added into the engine's fp32 accumulator when
+    the weight carries one (the returned marker tells the engine it is done)."""
+    from llm_research_b200.ops.gemm import linear_wgrad
+    from llm_research_b200.ops.linear import _acc_of, accumulated_marker
+
+    acc = _acc_of(w)
+    if acc is not None:
+        linear_wgrad(dy, x, out=acc, accumulate=True)
+        return accumulated_marker(w)
+    return linear_wgrad(dy, x).to(w.dtype)
+
+
 class _ColumnFn(torch.autograd.Function):
+    """Fused column-parallel layer: forward ``ag_gemm``; backward dX by ``gemm_rs``
+    and dW from the rows the forward gathered."""
+
     @staticmethod
     def forward(ctx, x_shard, w, comm, group):
         ctx.comm, ctx.group = comm, group
-        ctx.save_for_backward(x_shard, w)
-        T = x_shard.shape[0] * dist.get_world_size(group)
-        if _fused_ok(comm, x_shard, T, (x_shard.shape[1], w.shape[0])):
-            return comm.ag_gemm(x_shard, w)
-        return project(_all_gather_rows(x_shard, group), w)
+        y, a_full = comm.ag_gemm(x_shard, w)
+        ctx.save_for_backward(a_full, w)
+        return y
 
     @staticmethod
     def backward(ctx, dy):
-        x_shard, w = ctx.saved_tensors
+        from llm_research_b200.ops.gemm import linear_dgrad
+
+        a_full, w = ctx.saved_tensors
         comm, group = ctx.comm, ctx.group
         dy = dy.contiguous()
-        T = dy.shape[0]
-        x_full = _all_gather_rows(x_shard, group)
-        dw = dy.t().matmul(x_full) if ctx.needs_input_grad[1] else None
-        if _fused_ok(comm, dy, T, (w.shape[1], w.shape[0])):
-            dx = comm.gemm_rs(dy, w.t().contiguous())
-        else:
-            dx = _reduce_scatter_rows(dy.matmul(w), group)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            if _fused_ok(comm, dy, dy.shape[0], (w.shape[1], w.shape[0])):
+                dx = comm.gemm_rs(dy, w.t().contiguous())
+            else:
+                dx = _scatter_rows(linear_dgrad(dy, w), comm, group)
+        dw = _wgrad(dy, a_full, w) if ctx.needs_input_grad[1] else None
         return dx, dw, None, None
 
 
 class _RowFn(torch.autograd.Function):
+    """Fused row-parallel layer: forward ``gemm_rs`` (+ residual in the reduction);
+    backward dX by ``ag_gemm`` and dW from the gradient rows it gathered."""
+
     @staticmethod
     def forward(ctx, x, w, residual, comm, group):
         ctx.comm, ctx.group = comm, group
         ctx.save_for_backward(x, w)
         ctx.has_residual = residual is not None
-        T = x.shape[0]
-        if _fused_ok(comm, x, T, (w.shape[0], w.shape[1])):
-            return comm.gemm_rs(x, w, residual)
-        y = _reduce_scatter_rows(project(x, w), group)
-        return y + residual if residual is not None else y
+        return comm.gemm_rs(x, w, residual)
 
     @staticmethod
     def backward(ctx, dy):
+        from llm_research_b200.ops.gemm import linear_dgrad
+
         x, w = ctx.saved_tensors
         comm, group = ctx.comm, ctx.group
         dy = dy.contiguous()
         T = dy.shape[0] * dist.get_world_size(group)
         dres = dy if ctx.has_residual else None
         if _fused_ok(comm, dy, T, (w.shape[0], w.shape[1])):
-            dx = comm.ag_gemm(dy, w.t().contiguous())
+            dx, dy_full = comm.ag_gemm(dy, w.t().contiguous())
         else:
-            dx = _all_gather_rows(dy, group).matmul(w)
-        dw = _all_gather_rows(dy, group).t().matmul(x) if ctx.needs_input_grad[1] else None
+            dy_full = _gather_rows(dy, comm, group)
+            dx = linear_dgrad(dy_full, w)
+        dw = _wgrad(dy_full, x, w) if ctx.needs_input_grad[1] else None
         return dx, dw, dres, None, None
 
 
@@ -208,7 +327,7 @@ class ColumnParallelLinear(nn.Module):
         nn.init.normal_(self.weight, std=0.02)
 
     def forward(self, x_shard: torch.Tensor) -> torch.Tensor:
-        return _ColumnFn.apply(x_shard, self.weight, self.comm, self.group)
+        return column_parallel(x_shard, self.weight, self.group, self.comm)
 
 
 class RowParallelLinear(nn.Module):
@@ -225,7 +344,7 @@ class RowParallelLinear(nn.Module):
         nn.init.normal_(self.weight, std=0.02 / math.sqrt(2.0))
 
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
-        return _RowFn.apply(x, self.weight, residual, self.comm, self.group)
+        return row_parallel(x, self.weight, self.group, self.comm, residual)
 
 
 def shard_linear_weight(w: torch.Tensor, group: Optional[dist.ProcessGroup], dim: int) -> torch.Tensor:
@@ -350,9 +469,17 @@ def sum_grad(w: torch.Tensor, group) -> torch.Tensor:
 
 
 def column_parallel(x_shard: torch.Tensor, w: torch.Tensor, group, comm: Optional[TPComm]) -> torch.Tensor:
-    return _ColumnFn.apply(x_shard, w, comm, group)
+    """``(T/tp, in) -> (T, out/tp)``: the fused kernels in bf16, else ``project`` after
+    a differentiable row all-gather (NVFP4 GEMMs under NVFP4 precision)."""
+    T = x_shard.shape[0] * dist.get_world_size(group)
+    if _fused_ok(comm, x_shard, T, (x_shard.shape[1], w.shape[0])):
+        return _ColumnFn.apply(x_shard, w, comm, group)
+    return project(_AllGatherRows.apply(x_shard, comm, group), w)
 
 
 def row_parallel(x: torch.Tensor, w: torch.Tensor, group, comm: Optional[TPComm],
                  residual: Optional[torch.Tensor] = None) -> torch.Tensor:
-    return _RowFn.apply(x, w, residual, comm, group)
+    """``(T, in/tp) -> (T/tp, out)`` (+ residual, added in the reduction)."""
+    if _fused_ok(comm, x, x.shape[0], (w.shape[0], w.shape[1])):
+        return _RowFn.apply(x, w, residual, comm, group)
+    return _ReduceScatterRows.apply(project(x, w), residual, comm, group)

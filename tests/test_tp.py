@@ -256,3 +256,64 @@ def test_fsdp_plus_tensor_parallel_matches_single_process(fused_loss):
         for k, (v, dim) in sd.items():
             ref = single[k] if dim is None else single[k].chunk(2, dim=dim)[rank % 2]
             torch.testing.assert_close(v, ref, atol=5e-5, rtol=1e-4, msg=f"rank {rank} {k}")
+
+
+def _tp_rows_and_nvfp4_case(rank, world, use_comm):
+    """The heap's P2P row all-gather / reduce-scatter against NCCL, then an NVFP4
+    column + row layer pair (P2P collectives around the block-scaled GEMMs)."""
+    import torch.distributed as dist
+
+    from llm_research_b200.ops.linear import linear_precision
+    from llm_research_b200.parallel.tp import ColumnParallelLinear, RowParallelLinear, TPComm, shard_linear_weight
+
+    dev = torch.device("cuda", rank)
+    T, d, h = 512, 256, 512
+    comm = TPComm(None, max_tokens=T, max_width=max(d, h), device=dev) if use_comm else None
+    out = {}
+    if comm is not None:
+        g = torch.Generator(device=dev).manual_seed(10 + rank)
+        for e in range(3):  # slot and flag reuse
+            xs = torch.randn(T // world, d, device=dev, generator=g).to(torch.bfloat16)
+            ref = torch.empty(T, d, dtype=torch.bfloat16, device=dev)
+            dist.all_gather_into_tensor(ref, xs)
+            out[f"ag{e}"] = bool(torch.equal(comm.all_gather(xs), ref))
+            y = torch.randn(T, h, device=dev, generator=g).to(torch.bfloat16)
+            res = torch.randn(T // world, h, device=dev, generator=g).to(torch.bfloat16)
+            ref = torch.empty(T // world, h, device=dev)
+            dist.reduce_scatter_tensor(ref, y.float())
+            got = comm.reduce_scatter(y, res).float()
+            out[f"rs{e}"] = ((got - ref - res.float()).norm() / ref.norm()).item()
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(T, d, generator=g).to(dev, torch.bfloat16)
+    w1 = (torch.randn(h, d, generator=g) * 0.05).to(dev, torch.bfloat16)
+    w2 = (torch.randn(d, h, generator=g) * 0.05).to(dev, torch.bfloat16)
+    dy = torch.randn(T, d, generator=g).to(dev, torch.bfloat16)
+    col = ColumnParallelLinear(d, h, comm=comm, device=dev, dtype=torch.bfloat16)
+    row = RowParallelLinear(h, d, comm=comm, device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        col.weight.copy_(shard_linear_weight(w1, None, 0))
+        row.weight.copy_(shard_linear_weight(w2, None, 1))
+    xs = x.chunk(world)[rank].clone().requires_grad_()
+    with linear_precision("nvfp4"):
+        y = row(torch.relu(col(xs)), residual=x.chunk(world)[rank].clone())
+        y.backward(dy.chunk(world)[rank])
+    out.update(y=y.detach().float().cpu(), dx=xs.grad.float().cpu(), dw1=col.weight.grad.float().cpu(),
+               dw2=row.weight.grad.float().cpu())
+    if comm is not None:
+        comm.heap.check()
+        comm.close()
+    return out
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp_p2p_rows_and_nvfp4_layers_gpu():
+    a = run_ranks(_tp_rows_and_nvfp4_case, 2, True, backend="nccl")
+    b = run_ranks(_tp_rows_and_nvfp4_case, 2, False, backend="nccl")
+    for r in range(2):
+        for e in range(3):
+            assert a[r][f"ag{e}"], (r, e)
+            assert a[r][f"rs{e}"] < 1e-2, (r, e, a[r][f"rs{e}"])
+        # same NVFP4 GEMMs (and stochastic-rounding draws) around P2P or NCCL collectives
+        for k in ("y", "dx", "dw1", "dw2"):
+            torch.testing.assert_close(a[r][k], b[r][k], atol=3e-2, rtol=3e-2, msg=k)
