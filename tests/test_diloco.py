@@ -16,12 +16,14 @@ def _shards(rank, n=1000):
     return [torch.randn(n, generator=g), torch.randn(37, 3, generator=g)]
 
 
-def _outer_math(rank, world, quant):
+def _outer_math(rank, world, quant, comm="collective"):
     from llm_research_b200.parallel.diloco import DiLoCo, DiLoCoConfig, make_diloco_groups
 
     _, rg, ranks, _ = make_diloco_groups(world)
     shards = _shards(rank)
-    dl = DiLoCo(shards, rg, ranks, DiLoCoConfig(inner_steps=2, quantize_bits=quant, comm="collective"))
+    dl = DiLoCo(shards, rg, ranks, DiLoCoConfig(inner_steps=2, quantize_bits=quant, comm=comm))
+    # CPU ranks have no multicast or peer memory: "nvls" falls back to the collective path
+    assert dl.comm == "collective"
     anchor0 = dl.anchor.clone()
     for s in shards:  # "inner training": each replica drifts differently
         s.add_(0.01 * (rank + 1))
@@ -30,10 +32,10 @@ def _outer_math(rank, world, quant):
     return anchor0, torch.cat([s.reshape(-1) for s in shards]), dl.anchor[: dl.numel].clone()
 
 
-@pytest.mark.parametrize("quant", [0, 4])
-def test_diloco_nesterov_outer_step(quant):
+@pytest.mark.parametrize("quant,comm", [(0, "collective"), (4, "collective"), (0, "nvls")])
+def test_diloco_nesterov_outer_step(quant, comm):
     world = 3
-    res = run_ranks(_outer_math, world, quant)
+    res = run_ranks(_outer_math, world, quant, comm)
     anchor0 = res[0][0][: res[0][2].numel()]
     for r in range(world):
         torch.testing.assert_close(res[r][0][: res[r][2].numel()], anchor0)  # same start on every replica

@@ -106,3 +106,21 @@ def test_no_shard_replicates_and_matches_single_process():
         assert res["master_numel"] >= total  # replicated, not sharded
         for k, v in single.items():
             torch.testing.assert_close(res["params"][k], v, atol=5e-5, rtol=1e-4, msg=f"rank {r} {k}")
+
+
+def _nvls_fallback_rank_fn(rank, world):
+    import os
+
+    os.environ["LRB_FSDP_COMM"] = "nvls"  # no multicast on CPU ranks: the engine falls back
+    data = _data()
+    per = data.shape[0] // world
+    sd, orch = _train(_toy_model(), [data[rank * per:(rank + 1) * per]], engine=True)
+    return {"params": sd, "comm": orch._models["hlrt"].model.comm}
+
+
+def test_engine_nvls_request_falls_back_on_cpu_ranks():
+    single, _ = _train(_toy_model(), [_data()], engine=False)
+    for r, res in enumerate(run_ranks(_nvls_fallback_rank_fn, 2)):
+        assert res["comm"] == "nccl"  # the collective path (gloo on CPU)
+        for k, v in single.items():
+            torch.testing.assert_close(res["params"][k], v, atol=5e-5, rtol=1e-4, msg=f"rank {r} {k}")
