@@ -120,6 +120,11 @@ class DiLoCo:
                 if not (self.device.type == "cuda" and len(self.members) > 1 and self.cfg.quantize_bits == 0
                         and isinstance(self.group, dist.ProcessGroup) and single_node(self.group)):
                     raise NVLSUnavailable("the replica group is not a single-node process group")
+                # A replica that dies while its memory is bound to a multicast
+                # object can fault its peers' GPUs: with replica drop / rejoin
+                # enabled (a heartbeat monitor), the plain P2P path is used.
+                if self.cfg.fault_tolerance and self.monitor is not None:
+                    raise NVLSUnavailable("replica drop / rejoin is enabled")
                 self._setup_nvls()
             except NVLSUnavailable:
                 self.comm = "p2p" if self._p2p_possible() else "collective"
