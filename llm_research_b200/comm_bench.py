@@ -11,6 +11,8 @@ JSON line per case on rank 0 with the achieved fraction of its roofline:
 Cases (M = tokens over all ranks, sequence-sharded; N x K weights):
   ag_gemm      fused all-gather(rows) -> GEMM    vs  NCCL all_gather + cuBLAS
   gemm_rs      fused GEMM -> reduce-scatter(rows) vs  cuBLAS + NCCL reduce_scatter
+  tp_rows_*    the P2P row all-gather and reduce-scatter (+ residual) that the NVFP4 TP layers
+               run around their block-scaled GEMMs  vs  NCCL
   fsdp_rs      P2P reduce-scatter (bf16 wire, fp32 accumulate, fused norm) vs NCCL (fp32)
   ep_dispatch  MoE dispatch (P2P stores into the owners' expert slots) vs NCCL all_to_all
   ep_combine   MoE combine (P2P loads fused with the top-k weighted sum) vs NCCL all_to_all + gather
@@ -127,7 +129,22 @@ def main(argv=None) -> None:
             ms = _time(lambda: comm.gemm_rs(xk, w2), args.warmup, args.iters, dev)
             base = _time(nccl_rs, args.warmup, args.iters, dev)
             report("gemm_rs", T, N, K // world, ms, base, flops, rs_bytes)
-            del x_shard, w, full, xk, w2, out
+
+            # the row collectives the NVFP4 layers run around their block-scaled GEMMs
+            y = torch.randn(T, N, device=dev, dtype=torch.bfloat16)
+            res = torch.randn(Tl, N, device=dev, dtype=torch.bfloat16)
+            ms = _time(lambda: comm.all_gather(x_shard), args.warmup, args.iters, dev)
+            base = _time(lambda: dist.all_gather_into_tensor(full, x_shard), args.warmup, args.iters, dev)
+            report("tp_rows_all_gather", T, 0, K, ms, base, 0.0, ag_bytes)
+            ms = _time(lambda: comm.reduce_scatter(y, res), args.warmup, args.iters, dev)
+
+            def nccl_rows_rs():
+                dist.reduce_scatter_tensor(out, y)
+                return out + res
+
+            base = _time(nccl_rows_rs, args.warmup, args.iters, dev)
+            report("tp_rows_reduce_scatter_residual", T, N, 0, ms, base, 0.0, rs_bytes)
+            del x_shard, w, full, xk, w2, out, y, res
     comm.heap.check()
     comm.close()
 
